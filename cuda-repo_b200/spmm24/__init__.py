@@ -1,0 +1,227 @@
+"""Python host binding of libspmm24 (the sm_100a 2:4 SpMM library).
+
+Mirrors the reference's host interface (SpeakOutLoudly/CUDA-Repo):
+  SpMM_N2M4_Launch      src/SpMM_API.cu:61-70      -> SpMM_N2M4_Launch / launch
+  toolCompressMatrixA   test/utils.h:91-150        -> toolCompressMatrixA / compress_a
+  toolReorderMetadata   test/utils.h:155-185       -> toolReorderMetadata / reorder_metadata
+  toolPackMatrixB       test/utils.h:188-229       -> toolPackMatrixB / pack_b
+
+Everything goes through the C ABI of ``lib/libspmm24.so``; there is no
+Python or CPU fallback.  Importing this module on a machine where the
+library was not built raises ImportError.  PyTorch is used only to hand
+device pointers and streams to the library.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+
+_PKG_DIR = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(os.path.dirname(_PKG_DIR), "lib", "libspmm24.so")
+
+if not os.path.exists(_LIB_PATH):
+    raise ImportError(f"libspmm24.so not built ({_LIB_PATH}); run `make -C cuda-repo_b200`")
+
+_lib = ctypes.CDLL(_LIB_PATH)
+_u16p = ctypes.POINTER(ctypes.c_uint16)
+_vp = ctypes.c_void_p
+
+
+class SpmmConfig(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int) for n in
+                ("tile_m", "tile_n", "stage_k", "stages", "split_k", "grid_ctas", "smem_bytes")]
+
+
+_lib.spmm24_launch.argtypes = [_vp, _vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_int]
+_lib.spmm24_launch.restype = ctypes.c_int
+_lib.spmm24_compress_a.argtypes = [_u16p, ctypes.c_int, ctypes.c_int, _u16p, _u16p]
+_lib.spmm24_compress_a.restype = ctypes.c_int
+_lib.spmm24_compress_reordered.argtypes = [_u16p, ctypes.c_int, ctypes.c_int, _u16p, _u16p]
+_lib.spmm24_compress_reordered.restype = ctypes.c_int
+_lib.spmm24_reorder_metadata.argtypes = [_u16p, ctypes.c_int, ctypes.c_int, _u16p]
+_lib.spmm24_reorder_metadata.restype = ctypes.c_int
+_lib.spmm24_pack_b.argtypes = [_u16p, ctypes.c_int, ctypes.c_int, _u16p]
+_lib.spmm24_pack_b.restype = ctypes.c_int
+_lib.spmm24_prune_2of4.argtypes = [_u16p, ctypes.c_int, ctypes.c_int]
+_lib.spmm24_prune_2of4.restype = ctypes.c_int
+_lib.spmm24_workspace_bytes.argtypes = [ctypes.c_int] * 4
+_lib.spmm24_workspace_bytes.restype = ctypes.c_size_t
+_lib.spmm24_select_config.argtypes = [ctypes.c_int] * 4 + [ctypes.POINTER(SpmmConfig)]
+_lib.spmm24_select_config.restype = ctypes.c_int
+_lib.spmm24_device_status.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_uint32)]
+_lib.spmm24_device_status.restype = ctypes.c_int
+_lib.spmm24_last_error.restype = ctypes.c_char_p
+_lib.spmm24_version.restype = ctypes.c_char_p
+
+CUDA_SUCCESS = 0
+CUDA_ERROR_INVALID_VALUE = 1
+
+
+class SpmmError(RuntimeError):
+    def __init__(self, code: int, where: str):
+        msg = _lib.spmm24_last_error().decode() if code == CUDA_ERROR_INVALID_VALUE else ""
+        super().__init__(f"{where}: cudaError {code}" + (f" ({msg})" if msg else ""))
+        self.code = code
+
+
+def library_path() -> str:
+    return _LIB_PATH
+
+
+def version() -> str:
+    return _lib.spmm24_version().decode()
+
+
+def _ptr(x) -> int | None:
+    """Device pointer of a torch tensor, an int address, or None."""
+    if x is None:
+        return None
+    if isinstance(x, int):
+        return x
+    return int(x.data_ptr())
+
+
+def _stream_handle(stream) -> int | None:
+    if stream is None:
+        return None
+    if isinstance(stream, int):
+        return stream
+    return int(stream.cuda_stream)
+
+
+# -------------------------------------------------------------- launch
+def launch(stream, compressed_a, b_packed, metadata, c, M: int, N: int, K: int, split_reduction=None,
+           split_k: int = 0) -> int:
+    """spmm24_launch through the C ABI; returns the cudaError_t code."""
+    return _lib.spmm24_launch(_stream_handle(stream), _ptr(compressed_a), _ptr(b_packed), _ptr(metadata), _ptr(c),
+                              M, N, K, _ptr(split_reduction), split_k)
+
+
+def SpMM_N2M4_Launch(stream, Compressed_A, B, metadata, C, M_Global: int, N_Global: int, K_Global: int,
+                     Split_Reduction=None, Split_K: int = 1) -> int:
+    """The reference's launcher signature (src/SpMM_API.cu:61-70)."""
+    return launch(stream, Compressed_A, B, metadata, C, M_Global, N_Global, K_Global, Split_Reduction, Split_K)
+
+
+def spmm(compressed_a, metadata, b_packed, M: int, N: int, K: int, split_k: int = 0, out=None, stream=None):
+    """C = A_sparse * B for device tensors in the ABI formats; returns C (M x N fp16).
+
+    Raises SpmmError when the library rejects the call."""
+    import torch
+
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.float16, device=compressed_a.device)
+    if stream is None:
+        stream = torch.cuda.current_stream(compressed_a.device)
+    rc = launch(stream, compressed_a, b_packed, metadata, out, M, N, K, None, split_k)
+    if rc != CUDA_SUCCESS:
+        raise SpmmError(rc, "spmm24_launch")
+    return out
+
+
+def select_config(M: int, N: int, K: int, split_k: int = 0) -> dict:
+    cfg = SpmmConfig()
+    if _lib.spmm24_select_config(M, N, K, split_k, ctypes.byref(cfg)) != 0:
+        raise ValueError("unsupported shape")
+    return {n: getattr(cfg, n) for n, _ in SpmmConfig._fields_}
+
+
+def workspace_bytes(M: int, N: int, K: int, split_k: int) -> int:
+    return int(_lib.spmm24_workspace_bytes(M, N, K, split_k))
+
+
+def device_status(device: int = 0) -> int:
+    """Reads and clears the sticky status word (non-zero: a bounded wait gave up)."""
+    v = ctypes.c_uint32(0)
+    rc = _lib.spmm24_device_status(device, ctypes.byref(v))
+    if rc != CUDA_SUCCESS:
+        raise SpmmError(rc, "spmm24_device_status")
+    return int(v.value)
+
+
+# -------------------------------------------------------------- packer
+def _u16(a: np.ndarray) -> np.ndarray:
+    a = np.ascontiguousarray(a)
+    if a.dtype == np.float16:
+        a = a.view(np.uint16)
+    if a.dtype != np.uint16:
+        raise TypeError("expected fp16 data (as float16 or raw uint16 bits)")
+    return a
+
+
+def _p(a: np.ndarray):
+    return a.ctypes.data_as(_u16p)
+
+
+def compress_a(dense_a: np.ndarray, M: int, K: int):
+    """(values[M*K/2], raw metadata[M*K/16]) of a 2:4-sparse fp16 matrix."""
+    d = _u16(dense_a).reshape(-1)
+    vals = np.empty(M * K // 2, dtype=np.uint16)
+    meta = np.empty(M * K // 16, dtype=np.uint16)
+    n = _lib.spmm24_compress_a(_p(d), M, K, _p(vals), _p(meta))
+    if n == -2:
+        raise ValueError("matrix is not 2:4 sparse along K (a group of four has fewer than two zeros)")
+    if n < 0:
+        raise ValueError("compress_a: M and K must be multiples of 16")
+    return vals, meta
+
+
+def reorder_metadata(meta: np.ndarray, M: int, K: int) -> np.ndarray:
+    m = _u16(meta).reshape(-1)
+    out = np.empty_like(m)
+    if _lib.spmm24_reorder_metadata(_p(m), M, K, _p(out)) != 0:
+        raise ValueError("reorder_metadata: M % 16 and K % 64 must be 0")
+    return out
+
+
+def compress_reordered(dense_a: np.ndarray, M: int, K: int):
+    """(values, on-device metadata) in one pass."""
+    d = _u16(dense_a).reshape(-1)
+    vals = np.empty(M * K // 2, dtype=np.uint16)
+    meta = np.empty(M * K // 16, dtype=np.uint16)
+    n = _lib.spmm24_compress_reordered(_p(d), M, K, _p(vals), _p(meta))
+    if n == -2:
+        raise ValueError("matrix is not 2:4 sparse along K (a group of four has fewer than two zeros)")
+    if n < 0:
+        raise ValueError("compress_reordered: M % 16 and K % 64 must be 0")
+    return vals, meta
+
+
+def pack_b(b_rowmajor: np.ndarray, K: int, N: int) -> np.ndarray:
+    """Packed B (ceil(N/8) strips of K x 8); pad columns are zero."""
+    b = _u16(b_rowmajor).reshape(-1)
+    out = np.empty(((N + 7) // 8) * 8 * K, dtype=np.uint16)
+    if _lib.spmm24_pack_b(_p(b), K, N, _p(out)) != 0:
+        raise ValueError("pack_b: K % 64 must be 0")
+    return out
+
+
+def prune_2of4(dense_a: np.ndarray, M: int, K: int) -> np.ndarray:
+    """Magnitude 2:4 pruning along K (returns a pruned copy)."""
+    a = _u16(dense_a).reshape(-1).copy()
+    if _lib.spmm24_prune_2of4(_p(a), M, K) != 0:
+        raise ValueError("prune_2of4: K % 4 must be 0")
+    return a
+
+
+# Reference-named wrappers (Block sizes fixed as in the reference harness).
+def toolCompressMatrixA(denseMatrixA: np.ndarray, Global_M: int, Global_K: int, Block_M: int = 16,
+                        Block_K: int = 16):
+    if (Block_M, Block_K) != (16, 16):
+        raise ValueError("only 16x16 blocks are supported")
+    vals, meta = compress_a(denseMatrixA, Global_M, Global_K)
+    return vals.size, vals, meta
+
+
+def toolReorderMetadata(matadata: np.ndarray, Global_M: int, Global_K: int, Block_M: int = 16, Block_K: int = 16):
+    if (Block_M, Block_K) != (16, 16):
+        raise ValueError("only 16x16 blocks are supported")
+    return reorder_metadata(matadata, Global_M, Global_K)
+
+
+def toolPackMatrixB(MatrixB: np.ndarray, Global_K: int, Global_N: int, Block_K: int = 64, Block_N: int = 8):
+    if (Block_K, Block_N) != (64, 8):
+        raise ValueError("only 64x8 blocks are supported")
+    return pack_b(MatrixB, Global_K, Global_N)

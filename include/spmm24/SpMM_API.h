@@ -1,0 +1,138 @@
+/*
+ * SpMM_API.h -- public interface of libspmm24, the sm_100a (B200) 2:4
+ * structured-sparse fp16 SpMM library: C = A_sparse * B.
+ *
+ * Drop-in for SpeakOutLoudly/CUDA-Repo's SpMM_N2M4_Launch path.  Every entry
+ * point below names the reference interface it replaces (file:line within
+ * that project).  Two bindings are provided:
+ *
+ *   - extern "C" entry points (spmm24_*) with plain pointers and sizes, for
+ *     C, ctypes, cgo, JNI or any other FFI;
+ *   - C++ declarations with exactly the reference's names and parameter
+ *     types, so existing C++ callers link against the same mangled symbols
+ *     (e.g. _Z16SpMM_N2M4_LaunchP11CUstream_stPK6__halfS3_PKtPS1_iiiS6_i).
+ *
+ * Data formats (identical to the reference's):
+ *   compressed A   M*K/2 fp16 values in 16x8 blocks: band b (16 rows), 16-K
+ *                  block q, row r -> 8 values at ((b*(K/16)+q)*16+r)*8
+ *                  (test/utils.h:114-147)
+ *   metadata       M*K/16 uint16 words, the reference's reordered layout
+ *                  (test/utils.h:155-185): per band and 64-K group, word
+ *                  [i*8+j] holds row i+8*(j%2), 16-K block j/2; each word
+ *                  has eight 2-bit in-group indices, lowest bits first
+ *   packed B       ceil(N/8) strips, each K x 8 fp16 row-major
+ *                  (test/utils.h:188-229); for N % 8 != 0 the last strip is
+ *                  padded (pad values never reach C)
+ *   C              M x N fp16, row-major
+ * Shape rules: M % 16 == 0, K % 64 == 0, N >= 1.  A, B and metadata must be
+ * 16-byte aligned device pointers; C must be 2-byte aligned.
+ */
+#ifndef SPMM24_SPMM_API_H
+#define SPMM24_SPMM_API_H
+
+#include <stddef.h>
+#include <stdint.h>
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Launches C = A_sparse * B on `stream`, asynchronously.
+ * Replaces SpMM_N2M4_Launch (src/SpMM_API.cu:61-171).
+ *   split_k   0 lets the library choose the K split from the shape;
+ *             1..8 requests that many K slices (clamped to the number of
+ *             128-wide K stages).  Values above 8 are treated as 8.  The
+ *             result does not depend on split_k beyond fp32 summation order.
+ *   split_reduction  accepted for ABI compatibility and never touched: the
+ *             split-K reduction happens on chip, so it may be NULL.
+ * Returns cudaSuccess, cudaErrorInvalidValue (bad pointer, alignment or
+ * shape -- the reference silently did nothing for unsupported N), or the
+ * launch error. */
+cudaError_t spmm24_launch(cudaStream_t stream, const void* compressed_a, const void* b_packed,
+                          const uint16_t* metadata, void* c, int M, int N, int K, void* split_reduction,
+                          int split_k);
+
+/* Caller-allocated form of toolCompressMatrixA (test/utils.h:91-150) with
+ * its Block_M = Block_K = 16: dense row-major fp16 (as raw bits) ->
+ * compressed values (M*K/2) and raw metadata (M*K/16).  Bit-exact with the
+ * reference for every 2:4-sparse input (at least two zeros -- +0 or -0 --
+ * in each group of four along K).  Returns the value count, -1 for a bad
+ * shape (M % 16 or K % 16 nonzero) and -2 for a group with fewer than two
+ * zeros (the reference would write past its buffers). */
+int spmm24_compress_a(const uint16_t* dense_a, int M, int K, uint16_t* values_out, uint16_t* meta_out);
+
+/* Caller-allocated form of toolReorderMetadata (test/utils.h:155-185).
+ * Returns 0, or -1 when M % 16 or K % 64 is nonzero. */
+int spmm24_reorder_metadata(const uint16_t* meta_in, int M, int K, uint16_t* meta_out);
+
+/* compress + reorder in one pass: the on-device metadata directly. */
+int spmm24_compress_reordered(const uint16_t* dense_a, int M, int K, uint16_t* values_out, uint16_t* meta_out);
+
+/* Caller-allocated form of toolPackMatrixB (test/utils.h:188-229) with its
+ * Block_K = 64, Block_N = 8.  Writes ceil(N/8)*8*K values; for N % 8 != 0
+ * the pad columns are zero.  Returns 0, or -1 when K % 64 != 0. */
+int spmm24_pack_b(const uint16_t* b_rowmajor, int K, int N, uint16_t* b_packed_out);
+
+/* Magnitude 2:4 pruning along K, in place: keeps the two largest |x| of
+ * each group of four (ties prefer the lower index).  The reference only
+ * generates random masks (test/utils.h:38-66); this is the pruning step of
+ * its host prune/compress/metadata pipeline.  Returns 0, or -1 if K % 4. */
+int spmm24_prune_2of4(uint16_t* dense_a, int M, int K);
+
+/* Workspace the caller must pass as split_reduction: always 0 bytes.
+ * Replaces the Split_K*M*N halves contract of test/kernelTest.cu:136. */
+size_t spmm24_workspace_bytes(int M, int N, int K, int split_k);
+
+/* The tile / stage / split configuration spmm24_launch would use.
+ * Replaces the compile-time N switch of src/SpMM_API.cu:128-154 and
+ * N2M4TilingConfig (src/TileConfig.h:60-94).  Returns 0 or -1. */
+typedef struct spmm24_config {
+    int tile_m;      /* rows per CTA (128) */
+    int tile_n;      /* columns per CTA */
+    int stage_k;     /* logical K per pipeline stage (128) */
+    int stages;      /* pipeline depth */
+    int split_k;     /* CTAs per cluster along K */
+    int grid_ctas;   /* CTAs launched */
+    int smem_bytes;  /* dynamic shared memory per CTA */
+} spmm24_config;
+int spmm24_select_config(int M, int N, int K, int split_k, spmm24_config* out);
+
+/* Reads and clears this process's sticky device status word on `device`
+ * (0 = no kernel gave up a bounded wait).  Synchronises the device. */
+cudaError_t spmm24_device_status(int device, uint32_t* status_out);
+
+/* Human-readable reason for the last cudaErrorInvalidValue returned on the
+ * calling thread ("" if none). */
+const char* spmm24_last_error(void);
+
+const char* spmm24_version(void);
+
+#ifdef __cplusplus
+} /* extern "C" */
+
+#include <cuda_fp16.h>
+
+/* C++ drop-ins with the reference's exact names and types. */
+
+/* src/SpMM_API.cu:61-70 (the stale 7-argument declaration of
+ * build/SpMM_API.cuh:15-22 is replaced by the 9-argument definition). */
+cudaError_t SpMM_N2M4_Launch(cudaStream_t stream, const half* Compressed_A, const half* B, const uint16_t* metadata,
+                             half* C, const int M_Global, const int N_Global, const int K_Global,
+                             half* Split_Reduction, const int Split_K);
+
+/* test/utils.h:91-150; outputs are malloc'ed, the caller frees them.
+ * Only Block_M = Block_K = 16 is supported (-1 otherwise). */
+int toolCompressMatrixA(half* denseMatrixA, int Global_M, int Global_K, int Block_M, int Block_K,
+                        half** compressedMatrixA, uint16_t** matadata);
+
+/* test/utils.h:155-185; output malloc'ed (NULL on failure). */
+void toolReorderMetadata(uint16_t* matadata, int Global_M, int Global_K, int Block_M, int Block_K,
+                         uint16_t** reorderMatadata);
+
+/* test/utils.h:188-229; output malloc'ed (NULL on failure). */
+void toolPackMatrixB(half* MatrixB, int Global_K, int Global_N, int Block_K, int Block_N, half** packMatrixB);
+
+#endif /* __cplusplus */
+
+#endif /* SPMM24_SPMM_API_H */

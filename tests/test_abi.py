@@ -1,0 +1,94 @@
+"""The C-ABI boundary: the library loads, exports every entry point that
+include/spmm24/SpMM_API.h declares (plus the reference's mangled C++
+names), and rejects bad calls before touching a GPU."""
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+
+import oracle as O
+import spmm24
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(REPO, "include", "spmm24", "SpMM_API.h")
+
+# The reference's launcher as C++ code links to it (verified with nm on a
+# build of src/SpMM_API.cu), plus the packer names from test/utils.h.
+REFERENCE_MANGLED = [
+    "_Z16SpMM_N2M4_LaunchP11CUstream_stPK6__halfS3_PKtPS1_iiiS6_i",
+    "_Z19toolCompressMatrixAP6__halfiiiiPS0_PPt",
+    "_Z19toolReorderMetadataPtiiiiPS_",
+    "_Z15toolPackMatrixBP6__halfiiiiPS0_",
+]
+
+
+def declared_c_functions():
+    text = open(HEADER).read()
+    c_part = text.split("} /* extern \"C\" */")[0]
+    return sorted(set(re.findall(r"\b(spmm24_[a-z_0-9]+)\s*\(", c_part)))
+
+
+def exported_symbols(path):
+    out = subprocess.run(["nm", "-D", "--defined-only", path], capture_output=True, text=True, check=True).stdout
+    return {line.split()[-1] for line in out.splitlines() if line.strip()}
+
+
+def test_header_declares_entry_points():
+    names = declared_c_functions()
+    assert "spmm24_launch" in names and "spmm24_compress_a" in names and len(names) >= 10
+
+
+def test_library_exports_all_declared_symbols():
+    syms = exported_symbols(spmm24.library_path())
+    missing = [n for n in declared_c_functions() if n not in syms]
+    assert not missing, missing
+    for m in REFERENCE_MANGLED:
+        assert m in syms, m
+
+
+@pytest.mark.skipif(not O.ref_spmm_available(), reason="reference kernel not built (oracle/_ref)")
+def test_launcher_mangled_name_equals_reference_build():
+    ref_syms = exported_symbols(os.path.join(REPO, "oracle", "_ref", "libref_spmm.so"))
+    assert REFERENCE_MANGLED[0] in ref_syms
+
+
+def test_version_and_workspace():
+    assert "sm_100a" in spmm24.version()
+    assert spmm24.workspace_bytes(4096, 16, 4096, 4) == 0
+
+
+
+
+def _launch(a, b, e, c, M, N, K, split=1):
+    return spmm24.launch(None, a, b, e, c, M, N, K, None, split)
+
+
+def test_launch_rejects_bad_arguments_without_gpu():
+    ok = (0x10000, 0x20000, 0x30000, 0x40000)
+    assert _launch(0, *ok[1:], 256, 16, 256) == spmm24.CUDA_ERROR_INVALID_VALUE
+    assert "null" in spmm24._lib.spmm24_last_error().decode()
+    assert _launch(*ok, 250, 16, 256) == spmm24.CUDA_ERROR_INVALID_VALUE   # M % 16
+    assert _launch(*ok, 256, 16, 96) == spmm24.CUDA_ERROR_INVALID_VALUE    # K % 64
+    assert _launch(*ok, 256, 0, 256) == spmm24.CUDA_ERROR_INVALID_VALUE    # N <= 0
+    assert _launch(*ok, 256, 16, 256, split=-1) == spmm24.CUDA_ERROR_INVALID_VALUE
+    assert _launch(0x10008, *ok[1:], 256, 16, 256) == spmm24.CUDA_ERROR_INVALID_VALUE  # A misaligned
+    assert _launch(ok[0], ok[1], ok[2], 0x40001, 256, 16, 256) == spmm24.CUDA_ERROR_INVALID_VALUE  # C odd
+    assert "aligned" in spmm24._lib.spmm24_last_error().decode()
+
+
+def test_select_config_picks_tiles_and_splits():
+    c = spmm24.select_config(4096, 16, 4096)
+    assert c["tile_m"] == 128 and c["tile_n"] == 16 and c["stage_k"] == 128
+    assert 1 <= c["split_k"] <= 8 and c["grid_ctas"] == 32 * c["split_k"]
+    assert c["grid_ctas"] <= 148
+    # explicit split honoured, clamped to the number of 128-K stages
+    assert spmm24.select_config(256, 128, 256, 8)["split_k"] == 2
+    assert spmm24.select_config(256, 128, 4096, 5)["split_k"] == 5
+    assert spmm24.select_config(256, 128, 4096, 12)["split_k"] == 8
+    assert spmm24.select_config(4096, 1, 4096)["tile_n"] == 16
+    for n, t in ((17, 32), (64, 64), (65, 128), (4096, 128)):
+        assert spmm24.select_config(1024, n, 1024, 1)["tile_n"] == t
+    with pytest.raises(ValueError):
+        spmm24.select_config(100, 16, 256)

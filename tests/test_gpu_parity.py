@@ -1,0 +1,153 @@
+"""GPU parity: the sm_100a kernel through the C ABI against the CPU oracle
+(and against the reference's own kernel built for sm_100a, where it
+supports the shape).  Tolerance: see tests/problems.py (max relative error
+1e-2, mean absolute error 1e-3 against the oracle's fp32 result rounded to
+fp16); integer-valued known-answer cases must match exactly."""
+import numpy as np
+import pytest
+
+import oracle as O
+from problems import compare, make_problem, oracle_c, pack_problem, within_tolerance
+
+pytestmark = pytest.mark.gpu
+
+
+def _to_dev(torch, arr, dev):
+    return torch.from_numpy(np.ascontiguousarray(arr).view(np.int16)).to(dev)
+
+
+def run_gpu(p, split_k=0, dev=None):
+    import torch
+
+    import spmm24
+
+    A = _to_dev(torch, p.vals, dev)
+    E = _to_dev(torch, p.meta, dev)
+    B = _to_dev(torch, p.b_packed, dev)
+    C = torch.full((p.M, p.N), float("nan"), dtype=torch.float16, device=dev)
+    rc = spmm24.launch(torch.cuda.current_stream(dev), A, B, E, C, p.M, p.N, p.K, None, split_k)
+    assert rc == 0, spmm24._lib.spmm24_last_error().decode()
+    torch.cuda.synchronize(dev)
+    return C.view(torch.int16).cpu().numpy().view(np.uint16)
+
+
+def check(p, split_k, dev):
+    got = run_gpu(p, split_k, dev)
+    stats = compare(got, oracle_c(p))
+    assert within_tolerance(stats), stats
+    return got
+
+
+def test_config1_correctness_run(cuda_device):
+    """M=256, K=256, N=128, A N(0,1) seed 0 magnitude-pruned,
+    B U(-1,1) seed 1, split_K=1."""
+    p = make_problem(256, 128, 256, seed=0)
+    check(p, 1, cuda_device)
+
+
+def test_known_answer_reference_inputs(cuda_device):
+    """The reference harness's own inputs (kept values 1.0 with its glibc
+    rand() mask, B all ones): every output is exactly K/2."""
+    M, N, K = 256, 128, 256
+    a = O.ref_init_pruned(M, K)
+    b = np.full(K * N, 0x3C00, dtype=np.uint16)
+    got = run_gpu(pack_problem(M, N, K, a, b), 1, cuda_device)
+    assert np.all(got.view(np.float16) == K / 2)
+
+
+@pytest.mark.parametrize("shape", [
+    (128, 16, 128),   # one stage
+    (128, 16, 64),    # a single (odd) 64-K group
+    (256, 8, 192),    # odd group count, N below the MMA tile
+    (16, 1, 64),      # one band, one column
+    (144, 12, 320),   # ragged M tile, ragged N strip, odd groups
+    (384, 40, 512),
+    (512, 200, 1024),
+    (256, 256, 256),
+    (128, 520, 256),  # several N tiles with a ragged last tile
+])
+@pytest.mark.parametrize("split_k", [1, 2, 3, 0])
+def test_shapes_and_splits(cuda_device, shape, split_k):
+    M, N, K = shape
+    p = make_problem(M, N, K, seed=M + N + K)
+    check(p, split_k, cuda_device)
+
+
+@pytest.mark.parametrize("split_k", [1, 2, 3, 4, 5, 6, 7, 8])
+def test_llama7b_decode_split_sweep(cuda_device, split_k):
+    """BASELINE config 2 shape (M=K=4096, N=16), split_K swept over 1..8."""
+    p = make_problem(4096, 16, 4096, seed=2, a_scale=0.02, b_dist="normal")
+    check(p, split_k, cuda_device)
+
+
+@pytest.mark.parametrize("M,K", [(11008, 4096), (4096, 11008)])
+@pytest.mark.parametrize("N", [1, 8, 32])
+def test_llama7b_decode_full_size_row_sample(cuda_device, M, K, N):
+    """Full-size decode layers, checked on a seeded sample of rows."""
+    p = make_problem(M, N, K, seed=3, a_scale=0.02, b_dist="normal")
+    got = run_gpu(p, 0, cuda_device).reshape(M, N)
+    rows = np.sort(np.random.default_rng(0).choice(M, 256, replace=False))
+    stats = compare(got[rows].reshape(-1), oracle_c(p, rows))
+    assert within_tolerance(stats), stats
+
+
+def test_prefill_shape_row_sample(cuda_device):
+    """BASELINE config 3 shape (4096 x 4096, N=512), sampled rows."""
+    M, N, K = 4096, 512, 4096
+    p = make_problem(M, N, K, seed=4, a_scale=0.02, b_dist="normal")
+    got = run_gpu(p, 1, cuda_device).reshape(M, N)
+    rows = np.sort(np.random.default_rng(1).choice(M, 128, replace=False))
+    stats = compare(got[rows].reshape(-1), oracle_c(p, rows))
+    assert within_tolerance(stats), stats
+
+
+def test_random_mask_square(cuda_device):
+    """BASELINE config 5 inputs (U(-1,1) with a uniformly random 2:4 mask)."""
+    p = make_problem(1024, 1024, 1024, seed=5, a_dist="uniform", mask="random")
+    got = run_gpu(p, 0, cuda_device).reshape(1024, 1024)
+    rows = np.arange(0, 1024, 7)
+    stats = compare(got[rows].reshape(-1), oracle_c(p, rows))
+    assert within_tolerance(stats), stats
+
+
+def test_deterministic_for_fixed_split(cuda_device):
+    p = make_problem(1024, 32, 2048, seed=6)
+    a = run_gpu(p, 4, cuda_device)
+    b = run_gpu(p, 4, cuda_device)
+    assert np.array_equal(a, b)
+
+
+@pytest.mark.skipif(not O.ref_spmm_available(), reason="reference kernel not built (oracle/_ref)")
+@pytest.mark.parametrize("N", [8, 16, 32, 64, 128])
+def test_matches_reference_kernel(cuda_device, N):
+    """Same packed inputs through the reference's own SpMM_N2M4_Launch
+    (compiled for sm_100a from its sources) and through this library."""
+    import torch
+
+    M, K = 512, 1024
+    p = make_problem(M, N, K, seed=7)
+    ref = O.ref_spmm()
+    assert ref.ref_spmm_supported(M, N, K, 1)
+    A = _to_dev(torch, p.vals, cuda_device)
+    E = _to_dev(torch, p.meta, cuda_device)
+    B = _to_dev(torch, p.b_packed, cuda_device)
+    C = torch.zeros((M, N), dtype=torch.float16, device=cuda_device)
+    rc = ref.ref_spmm_launch(torch.cuda.current_stream().cuda_stream, A.data_ptr(), B.data_ptr(), E.data_ptr(),
+                             C.data_ptr(), M, N, K, None, 1)
+    assert rc == 0
+    torch.cuda.synchronize()
+    ref_bits = C.view(torch.int16).cpu().numpy().view(np.uint16)
+    ours = run_gpu(p, 1, cuda_device)
+    ref_f32 = ref_bits.view(np.float16).astype(np.float32)
+    stats = compare(ours, ref_f32)
+    assert within_tolerance(stats), stats
+    # and the reference kernel itself agrees with the oracle
+    assert within_tolerance(compare(ref_bits, oracle_c(p)))
+
+
+def test_no_bounded_wait_gave_up(cuda_device):
+    import spmm24
+
+    p = make_problem(512, 64, 1024, seed=8)
+    run_gpu(p, 2, cuda_device)
+    assert spmm24.device_status(0) == 0
