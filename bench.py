@@ -1,0 +1,573 @@
+#!/usr/bin/env python3
+"""Benchmark of the sm_100a 2:4 SpMM library on its headline workload.
+
+Workload (LLaMA-7B decode linear layers): one step runs
+the 12 SpMMs (M,K) in {(4096,4096), (11008,4096), (4096,11008)} x N in
+{1, 8, 16, 32}.  A is fp16 N(0, 0.02) magnitude-pruned 2:4 along K, B is
+fp16 N(0, 1) (synthetic, seeded).  Every call in a step reads its own copy
+of the weights (481 MB of A + metadata in total, about 4x the 126 MB L2),
+so no call finds its operands in L2.
+
+Metric: dense-equivalent TFLOPS (2*M*N*K per SpMM) of the whole job, plus
+microseconds per SpMM and the fraction of the HBM roofline (algorithmic
+bytes = M*K + M*K/8 + 2*K*N + 2*M*N per call, against the measured copy
+bandwidth in MEASURED_PEAKS.json).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                  [--workload decode|prefill|square] [--comparators]
+
+--impl reference times the reference path's CPU implementation (the
+oracle's dense GEMM on the pruned A -- the reference has no CPU GEMM of its
+own) on the host cores, on a bounded row sample of the same workload.
+Under torchrun every rank runs its own copy of the workload on its own GPU
+(weak scaling, no collective on the data path); rank 0 prints one JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(REPO, "cuda-repo_b200"))
+
+WORKLOADS = {
+    # BASELINE config 2 (the headline): LLaMA-7B decode
+    "decode": {"shapes": [(M, N, K) for (M, K) in ((4096, 4096), (11008, 4096), (4096, 11008)) for N in (1, 8, 16, 32)],
+               "a_std": 0.02, "bound": "hbm"},
+    # LLaMA-7B prefill
+    "prefill": {"shapes": [(M, N, K) for (M, K) in ((4096, 4096), (11008, 4096), (4096, 11008)) for N in (512, 2048, 4096)],
+                "a_std": 0.02, "bound": "tensor"},
+    # square sweep (up to 8192)
+    "square": {"shapes": [(s, s, s) for s in (1024, 2048, 4096, 8192)], "a_std": None, "bound": "tensor"},
+}
+
+
+def algo_bytes(M, N, K):
+    return M * K + M * K // 8 + 2 * K * N + 2 * M * N
+
+
+def flops(M, N, K):
+    return 2.0 * M * N * K
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return {"hbm_gbs": float(p["hbm_gbs"]), "bf16_tflops": float(p["bf16_tflops"]),
+                "bf16_tflops_sustained": float(p.get("bf16_tflops_sustained", p["bf16_tflops"])), "src": "measured"}
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "src": "fallback"}
+
+
+def load_traffic(workload):
+    """Per-launch DRAM traffic from the committed ncu summary, if present."""
+    path = os.path.join(REPO, "profiles", f"spmm24_{workload}_traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f)
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(prefix="clocks_", suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            time.sleep(0.25)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.15)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None or not self.path:
+            return None
+        rows = []
+        try:
+            for line in open(self.path):
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 9 and parts[1].isdigit():
+                    rows.append(parts)
+        finally:
+            os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [int(r[1]) for r in rows]
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        load = [s for s in sm if s > 0.5 * max(sm)] or sm
+        return {"sm_mhz": int(statistics.median(load)), "sm_max_mhz": int(rows[0][2]), "reasons": reasons,
+                "samples": len(rows)}
+
+
+# --------------------------------------------------------------------- data
+def make_layer(torch, spmm24, M, K, a_std, seed, mask_random=False):
+    """Pruned, compressed weights of one layer, packed by the product's own
+    host packer (spmm24_prune_2of4 / spmm24_compress_reordered)."""
+    g = torch.Generator().manual_seed(seed)
+    if a_std is None:
+        a = (torch.rand(M, K, generator=g) * 2 - 1).half()
+        if mask_random:
+            keep = torch.rand(M * K // 4, 4, generator=g).argsort(dim=1)[:, :2]
+            m = torch.zeros(M * K // 4, 4, dtype=torch.bool).scatter_(1, keep, True)
+            a = (a.reshape(-1, 4) * m).reshape(M, K).half()
+    else:
+        a = (torch.randn(M, K, generator=g) * a_std).half()
+    a_np = a.numpy().view("uint16")
+    if a_std is not None or not mask_random:
+        a_np = spmm24.prune_2of4(a_np, M, K)
+    vals, meta = spmm24.compress_reordered(a_np, M, K)
+    return a_np, vals, meta
+
+
+def make_activations(torch, spmm24, K, N, seed, uniform=False):
+    g = torch.Generator().manual_seed(seed)
+    b = ((torch.rand(K, N, generator=g) * 2 - 1) if uniform else torch.randn(K, N, generator=g)).half()
+    b_np = b.numpy().view("uint16")
+    return b_np, spmm24.pack_b(b_np, K, N)
+
+
+def to_dev(torch, arr, dev):
+    return torch.from_numpy(arr.view("int16")).to(dev)
+
+
+# ------------------------------------------------------------- our arm
+def run_ours(args, rank, world, local_rank):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import spmm24
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    wl = WORKLOADS[args.workload]
+    shapes = wl["shapes"]
+    square = args.workload == "square"
+    layers = {}
+    for i, (M, K) in enumerate(sorted({(M, K) for (M, N, K) in shapes})):
+        a_np, vals, meta = make_layer(torch, spmm24, M, K, wl["a_std"], seed=1000 * rank + i, mask_random=square)
+        layers[(M, K)] = (a_np, vals, meta)
+    acts = {}
+    for j, (K, N) in enumerate(sorted({(K, N) for (M, N, K) in shapes})):
+        acts[(K, N)] = make_activations(torch, spmm24, K, N, seed=5000 + 100 * rank + j, uniform=square)
+
+    # Device copies: every call of a step gets its own weights so that the
+    # working set of a step exceeds L2.
+    calls = []
+    for (M, N, K) in shapes:
+        _, vals, meta = layers[(M, K)]
+        b_np, bp = acts[(K, N)]
+        A = to_dev(torch, vals, dev)
+        E = to_dev(torch, meta, dev)
+        B = to_dev(torch, bp, dev)
+        C = torch.empty((M, N), dtype=torch.float16, device=dev)
+        calls.append({"M": M, "N": N, "K": K, "A": A, "E": E, "B": B, "C": C,
+                      "split": spmm24.select_config(M, N, K, 0)["split_k"]})
+    weight_bytes = sum(c["A"].numel() * 2 + c["E"].numel() * 2 for c in calls)
+    stream = torch.cuda.current_stream(dev)
+    h_stream = int(stream.cuda_stream)
+
+    flags = spmm24.STATIC_WEIGHTS if args.static_weights else 0
+
+    def launch(c):
+        rc = spmm24._lib.spmm24_launch_ex(h_stream, c["A"].data_ptr(), c["B"].data_ptr(), c["E"].data_ptr(),
+                                          c["C"].data_ptr(), c["M"], c["N"], c["K"], 0, flags)
+        if rc != 0:
+            raise RuntimeError(f"spmm24_launch failed: {rc} {spmm24._lib.spmm24_last_error().decode()}")
+
+    for _ in range(args.warmup):
+        for c in calls:
+            launch(c)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+
+    # Timed region.  A sleep kernel queued first lets the host enqueue every
+    # timed launch before the GPU reaches them, so the device-side interval
+    # measures the kernels back to back (programmatic dependent launch lets
+    # each kernel's set-up overlap the previous kernel's tail).
+    nl = len(calls) * args.steps
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        torch.cuda.synchronize(dev)
+        torch.cuda._sleep(int(2e7))
+        t0.record(stream)
+        for _ in range(args.steps):
+            for c in calls:
+                launch(c)
+        t1.record(stream)
+        torch.cuda.synchronize(dev)
+    elapsed_ms = t0.elapsed_time(t1)
+    clocks = clk.summary()
+
+    # Per-shape kernel times: an event pair around every launch (this breaks
+    # the launch overlap, so these are single-kernel durations).
+    reps = max(3, min(args.steps, 10))
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps * len(calls))]
+    torch.cuda.synchronize(dev)
+    torch.cuda._sleep(int(2e7))
+    i = 0
+    for _ in range(reps):
+        for c in calls:
+            ev[i][0].record(stream)
+            launch(c)
+            ev[i][1].record(stream)
+            i += 1
+    torch.cuda.synchronize(dev)
+    per_launch_us = [a.elapsed_time(b) * 1e3 for a, b in ev]
+    per_call = [statistics.median(per_launch_us[ci::len(calls)]) for ci in range(len(calls))]
+
+    # End to end through the public C ABI with host buffers: each call copies
+    # its packed activations from pinned host memory, launches, and reads C back.
+    host_in = [torch.from_numpy(acts[(c["K"], c["N"])][1].view("int16")).pin_memory() for c in calls]
+    host_out = [torch.empty((c["M"], c["N"]), dtype=torch.float16).pin_memory() for c in calls]
+    h2d = sum(h.numel() * 2 for h in host_in)
+    d2h = sum(h.numel() * 2 for h in host_out)
+    for _ in range(max(1, args.warmup)):
+        for c, hi, ho in zip(calls, host_in, host_out):
+            c["B"].copy_(hi, non_blocking=True)
+            launch(c)
+            ho.copy_(c["C"], non_blocking=True)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        for c, hi, ho in zip(calls, host_in, host_out):
+            c["B"].copy_(hi, non_blocking=True)
+            launch(c)
+            ho.copy_(c["C"], non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = e0.elapsed_time(e1)
+
+    if world > 1:
+        t = torch.tensor([elapsed_ms, e2e_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed_ms, e2e_ms = float(t[0]), float(t[1])
+
+    step_flops = sum(flops(c["M"], c["N"], c["K"]) for c in calls)
+    total_flops = step_flops * args.steps * world
+    value = total_flops / (elapsed_ms * 1e-3) / 1e12
+    e2e_value = total_flops / (e2e_ms * 1e-3) / 1e12
+
+    peaks = load_peaks()
+    # Average launch duration over the timed region = elapsed / launches.
+    kernel_us_total = elapsed_ms * 1e3
+    bytes_total = sum(algo_bytes(c["M"], c["N"], c["K"]) for c in calls) * args.steps
+    flops_total_rank = step_flops * args.steps
+    if wl["bound"] == "hbm":
+        achieved = bytes_total / (kernel_us_total * 1e-6) / 1e9
+        peak = peaks["hbm_gbs"]
+        unit = "GB/s"
+    else:
+        achieved = flops_total_rank / (kernel_us_total * 1e-6) / 1e12
+        peak = peaks["bf16_tflops"]
+        unit = "TFLOP/s"
+    traffic = None
+    tr = load_traffic(args.workload)
+    if tr:
+        per = [tr.get(f"{c['M']}x{c['N']}x{c['K']}") for c in calls]
+        if all(v is not None for v in per):
+            traffic = float(sum(per) / len(per))
+
+    out = {
+        "metric": "dense-equiv TFLOPS per 2:4 SpMM at LLaMA shapes (us per SpMM and % of roofline alongside)",
+        "value": round(value, 4),
+        "unit": "TFLOPS",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(elapsed_ms / args.steps, 5),
+        "us_per_spmm": round(elapsed_ms * 1e3 / args.steps / len(calls), 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f16 in, f32 accumulate, f16 out",
+        "data": "synthetic (seeded torch RNG; A N(0,0.02) magnitude-pruned 2:4, B N(0,1))" if wl["a_std"]
+                else "synthetic (U(-1,1), random 2:4 mask)",
+        "config": {"workload": f"{args.workload}: " + ", ".join(f"{M}x{N}x{K}" for (M, N, K) in shapes),
+                   "baseline_config": {"decode": 2, "prefill": 3, "square": 5}[args.workload],
+                   "spmm_per_step": len(calls), "split_k": "auto (library picker)",
+                   "l2": f"inputs larger than L2: {weight_bytes / 1e6:.0f} MB of distinct weights per step",
+                   "parallelism": f"replicas x{world} (each rank its own layers)"},
+        "per_shape_us": {f"{c['M']}x{c['N']}x{c['K']}": round(u, 3) for c, u in zip(calls, per_call)},
+        "per_shape_note": "median single-kernel duration with an event pair around each launch",
+        "launch_flags": "SPMM24_STATIC_WEIGHTS" if args.static_weights else "none",
+        "roofline": {"bound": wl["bound"], "achieved": round(achieved, 2), "peak": peak, "unit": unit,
+                     "frac": round(achieved / peak, 4), "traffic": traffic,
+                     "peak_src": f"{peaks['src']} ({'hbm_gbs copy' if unit == 'GB/s' else 'dense bf16 cuBLAS burst'})",
+                     "per_launch_us": round(kernel_us_total / nl, 3),
+                     "note": "achieved = algorithmic bytes (flops) of the timed region / its CUDA-event duration"},
+        "e2e": {"value": round(e2e_value, 4), "unit": "TFLOPS", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "ms_per_step": round(e2e_ms / args.steps, 5),
+                "path": "spmm24_launch (C ABI) with pinned-host packed B in, C out, per call"},
+        "gpu_launches": nl,
+        "clocks": clocks,
+    }
+
+    if args.comparators and rank == 0:
+        out["comparators"] = run_comparators(torch, spmm24, calls, layers, acts, dev, args)
+
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        out["cpu_baseline"] = cpu_baseline(layers, acts, shapes, budget_s=args.cpu_seconds)
+
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+
+
+def run_comparators(torch, spmm24, calls, layers, acts, dev, args):
+    """Same step through dense cuBLAS (torch.matmul fp16), cuSPARSELt
+    (torch._cslt_sparse_mm) and the reference kernel built for sm_100a
+    (oracle/_ref, only N in {8..128}).  Each is timed per call with CUDA
+    events after warm-up, with an L2 flush before each call."""
+    import numpy as np
+
+    res = {}
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+
+    def time_fn(fn, iters=10):
+        for _ in range(3):
+            fn()
+        ts = []
+        for _ in range(iters):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            torch.cuda.synchronize()
+            ts.append(a.elapsed_time(b) * 1e3)
+        return statistics.median(ts)
+
+    ours, dense, cslt = {}, {}, {}
+    for c in calls:
+        key = f"{c['M']}x{c['N']}x{c['K']}"
+        a_np = layers[(c["M"], c["K"])][0]
+        b_np = acts[(c["K"], c["N"])][0]
+        Ad = torch.from_numpy(a_np.view("int16")).to(dev).view(torch.float16).reshape(c["M"], c["K"])
+        Bd = torch.from_numpy(b_np.view("int16")).to(dev).view(torch.float16).reshape(c["K"], c["N"])
+        h = int(torch.cuda.current_stream().cuda_stream)
+        ours[key] = time_fn(lambda: spmm24._lib.spmm24_launch(h, c["A"].data_ptr(), c["B"].data_ptr(),
+                                                              c["E"].data_ptr(), c["C"].data_ptr(), c["M"], c["N"],
+                                                              c["K"], None, 0))
+        dense[key] = time_fn(lambda: torch.matmul(Ad, Bd))
+        try:
+            comp = torch._cslt_compress(Ad)
+            Np = max(c["N"], 16)
+            Bp = torch.zeros(c["K"], Np, dtype=torch.float16, device=dev)
+            Bp[:, :c["N"]] = Bd
+            cslt[key] = time_fn(lambda: torch._cslt_sparse_mm(comp, Bp))
+        except Exception as e:  # noqa: BLE001
+            cslt[key] = None
+            res["cusparselt_error"] = str(e)[:200]
+        del Ad, Bd
+    res["us_ours"] = ours
+    res["us_cublas_dense_fp16"] = dense
+    res["us_cusparselt"] = cslt
+    try:
+        sys.path.insert(0, os.path.join(REPO, "oracle"))
+        import oracle as O
+
+        if O.ref_spmm_available():
+            ref = O.ref_spmm()
+            rk = {}
+            for c in calls:
+                key = f"{c['M']}x{c['N']}x{c['K']}"
+                if ref.ref_spmm_supported(c["M"], c["N"], c["K"], 1):
+                    h = int(torch.cuda.current_stream().cuda_stream)
+                    rk[key] = time_fn(lambda: ref.ref_spmm_launch(h, c["A"].data_ptr(), c["B"].data_ptr(),
+                                                                  c["E"].data_ptr(), c["C"].data_ptr(), c["M"],
+                                                                  c["N"], c["K"], None, 1))
+            res["us_reference_kernel_sm100a_splitk1"] = rk
+    except Exception as e:  # noqa: BLE001
+        res["reference_kernel_error"] = str(e)[:200]
+    return res
+
+
+def cpu_baseline(layers, acts, shapes, budget_s=10.0):
+    """The oracle's OpenMP dense GEMM (fp16 -> fp32, fp32 accumulate) on the
+    pruned A, on a row sample of every shape of the workload."""
+    import numpy as np
+
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import oracle as O
+
+    threads = O.max_threads()
+    # estimate: 64 rows of every shape
+    probe_rows = 64
+    t = time.perf_counter()
+    for (M, N, K) in shapes:
+        a = layers[(M, K)][0][: probe_rows * K]
+        O.dense_gemm_f32(a, acts[(K, N)][0], probe_rows, N, K, threads)
+    dt = time.perf_counter() - t
+    rows = int(max(16, min(4096, probe_rows * budget_s / max(dt, 1e-3) / 1.2)))
+    fl = 0.0
+    t = time.perf_counter()
+    for (M, N, K) in shapes:
+        r = min(rows, M)
+        a = layers[(M, K)][0][: r * K]
+        O.dense_gemm_f32(a, acts[(K, N)][0], r, N, K, threads)
+        fl += flops(r, N, K)
+    dt = time.perf_counter() - t
+    return {"value": round(fl / dt / 1e12, 6), "unit": "TFLOPS", "cores": threads, "kind": "port",
+            "sample": f"first {rows} rows of each of the {len(shapes)} shapes (dense fp32 GEMM on the pruned A), "
+                      f"{dt:.1f} s"}
+
+
+# -------------------------------------------------------- reference arm
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    import numpy as np
+    import torch
+
+    import spmm24
+
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import oracle as O
+
+    wl = WORKLOADS[args.workload]
+    shapes = wl["shapes"]
+    square = args.workload == "square"
+    layers = {}
+    for i, (M, K) in enumerate(sorted({(M, K) for (M, N, K) in shapes})):
+        layers[(M, K)] = make_layer(torch, spmm24, M, K, wl["a_std"], seed=i, mask_random=square)
+    acts = {}
+    for j, (K, N) in enumerate(sorted({(K, N) for (M, N, K) in shapes})):
+        acts[(K, N)] = make_activations(torch, spmm24, K, N, seed=5000 + j, uniform=square)
+    threads = O.max_threads()
+
+    def step(rows):
+        fl = 0.0
+        for (M, N, K) in shapes:
+            r = min(rows, M)
+            O.dense_gemm_f32(layers[(M, K)][0][: r * K], acts[(K, N)][0], r, N, K, threads)
+            fl += flops(r, N, K)
+        return fl
+
+    t = time.perf_counter()
+    step(32)
+    dt = time.perf_counter() - t
+    # each step ~2 s of CPU work so that --steps 20 --warmup 5 ends in about a minute
+    rows = int(max(16, min(4096, 32 * 2.0 / max(dt, 1e-4))))
+    for _ in range(args.warmup):
+        step(rows)
+    fl = 0.0
+    t = time.perf_counter()
+    for _ in range(args.steps):
+        fl += step(rows)
+    dt = time.perf_counter() - t
+    value = fl / dt / 1e12
+    sample = f"first {rows} rows of each of the {len(shapes)} shapes per step (dense fp32 GEMM on the pruned A)"
+    print(json.dumps({
+        "impl": "reference",
+        "metric": "dense-equiv TFLOPS per 2:4 SpMM at LLaMA shapes (us per SpMM and % of roofline alongside)",
+        "value": round(value, 6), "unit": "TFLOPS", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(dt * 1e3 / args.steps, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f16 in, f32 accumulate, f16 out", "data": "synthetic",
+        "config": {"workload": f"{args.workload}: " + ", ".join(f"{M}x{N}x{K}" for (M, N, K) in shapes),
+                   "baseline_config": {"decode": 2, "prefill": 3, "square": 5}[args.workload]},
+        "cpu_baseline": {"value": round(value, 6), "unit": "TFLOPS", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(value, 6), "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference has no CPU GEMM of its own; this is the oracle's restatement of its math "
+                "(oracle/oracle.c orc_dense_gemm_f32) on all host threads",
+    }), flush=True)
+
+
+def run_single(args):
+    """One shape, `warmup` launches then 3 more: the case profiler captures
+    use (ncu -k regex:spmm24 -s <warmup> -c 3)."""
+    import torch
+
+    import spmm24
+
+    parts = [int(x) for x in args.single.split(",")]
+    M, N, K = parts[:3]
+    split = parts[3] if len(parts) > 3 else 0
+    dev = torch.device("cuda", 0)
+    _, vals, meta = make_layer(torch, spmm24, M, K, 0.02, seed=1)
+    _, bp = make_activations(torch, spmm24, K, N, seed=2)
+    A, E, B = to_dev(torch, vals, dev), to_dev(torch, meta, dev), to_dev(torch, bp, dev)
+    C = torch.empty((M, N), dtype=torch.float16, device=dev)
+    s = torch.cuda.current_stream(dev)
+    for _ in range(args.warmup + 3):
+        rc = spmm24.launch(s, A, B, E, C, M, N, K, None, split)
+        if rc != 0:
+            raise SystemExit(f"launch failed {rc}")
+    torch.cuda.synchronize(dev)
+    print(json.dumps({"single": [M, N, K], "config": spmm24.select_config(M, N, K, split),
+                      "status": spmm24.device_status(0)}))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="decode")
+    ap.add_argument("--comparators", action="store_true")
+    ap.add_argument("--no-static-weights", dest="static_weights", action="store_false",
+                    help="launch without SPMM24_STATIC_WEIGHTS (no kernel in the step writes the weights)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--single", default=None,
+                    help="M,N,K[,split]: run one shape (warm-up + 3 launches) for profiler captures")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    if args.single:
+        run_single(args)
+        return
+    run_ours(args, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    main()

@@ -184,6 +184,44 @@ __device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// ------------------------------------------------ programmatic launch
+// Waits until every grid this one depends on (the previous kernel in the
+// stream, under programmatic stream serialization) has completed and its
+// memory operations are visible.  A no-op when launched without PDL.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Allows the next kernel in the stream (if launched with PDL) to begin
+// launching; it still waits in grid_dep_wait() for this grid to finish.
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+__device__ __forceinline__ void named_barrier(uint32_t id, uint32_t nthreads) {
+    asm volatile("barrier.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// ------------------------------------------------ inter-CTA flags (global)
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_gpu(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void st_relaxed_gpu(uint32_t* p, uint32_t v) {
+    asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void nanosleep_ns(uint32_t ns) { asm volatile("nanosleep.u32 %0;" ::"r"(ns)); }
+
+// Bounded wait until *flag == 1 (acquire).  Returns false after limit_ns.
+__device__ __forceinline__ bool wait_flag_bounded(const uint32_t* flag, uint64_t limit_ns) {
+    if (ld_acquire_gpu(flag) == 1u) return true;
+    const uint64_t t0 = globaltimer();
+    while (true) {
+        nanosleep_ns(64);
+        if (ld_acquire_gpu(flag) == 1u) return true;
+        if (globaltimer() - t0 > limit_ns) return false;
+    }
+}
+
 // ------------------------------------------------------- cluster / DSMEM
 __device__ __forceinline__ uint32_t cluster_ctarank() {
     uint32_t r;

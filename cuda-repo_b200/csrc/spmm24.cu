@@ -1,12 +1,12 @@
 // spmm24.cu -- host launch API of the sm_100a 2:4 SpMM library.
 //
 // Replaces SpMM_N2M4_Launch / SpMM_N2M4_Kernel_API (SpeakOutLoudly/CUDA-Repo
-// src/SpMM_API.cu:15-171): validates the call, picks a tile / stage / split
-// configuration from the shape (the compile-time N switch of
+// src/SpMM_API.cu:15-171): validates the call, picks a kernel and a tile /
+// stage / split configuration from the shape (the compile-time N switch of
 // src/SpMM_API.cu:128-154 becomes a runtime picker), encodes the three TMA
-// tensor maps and launches one kernel (a thread-block cluster along K when
-// split-K is used; the reduction runs on chip, so the reference's second
-// SplitK_Reduction launch is gone).
+// tensor maps and launches one kernel.  The reference's second launch
+// (SplitK_Reduction) is gone: split-K partials are reduced on chip (cluster
+// path) or by the last contributing CTA (stream-K path).
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -14,7 +14,9 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <map>
 #include <mutex>
+#include <utility>
 
 #include "spmm24/SpMM_API.h"
 #include "spmm24_kernel.cuh"
@@ -58,112 +60,253 @@ bool encode(CUtensorMap* m, int rank, const void* base, const cuuint64_t* dims, 
     return r == CUDA_SUCCESS;
 }
 
-struct Plan {
-    int tile_n;
-    int stages;
-    int split;
-    int smem;
-    int m_tiles, n_tiles;
-    int stages_total;
-};
-
-template <int NT, int ST>
-struct Variant {
-    using C_ = Cfg<NT, ST>;
-    static constexpr int kTileN = NT;
-    static constexpr int kStages = ST;
-};
-
-// One configuration per N tile: the deepest ring that fits in 227 KB.
-using V16 = Variant<16, 8>;
-using V32 = Variant<32, 8>;
-using V64 = Variant<64, 6>;
-using V128 = Variant<128, 4>;
-using V256 = Variant<256, 2>;
-
-int stages_for(int tile_n) {
-    switch (tile_n) {
-        case 16: return V16::kStages;
-        case 32: return V32::kStages;
-        case 64: return V64::kStages;
-        case 128: return V128::kStages;
-        default: return V256::kStages;
-    }
-}
-int smem_for(int tile_n) {
-    switch (tile_n) {
-        case 16: return V16::C_::SMEM_ALLOC;
-        case 32: return V32::C_::SMEM_ALLOC;
-        case 64: return V64::C_::SMEM_ALLOC;
-        case 128: return V128::C_::SMEM_ALLOC;
-        default: return V256::C_::SMEM_ALLOC;
-    }
-}
-
 int env_int(const char* name, int dflt) {
     const char* v = std::getenv(name);
     return (v && *v) ? std::atoi(v) : dflt;
 }
 
-constexpr int kNumSMs = 148;
+constexpr int kMaxDevices = 64;
 constexpr int kMaxSplit = 8;
 
-Plan make_plan(int M, int N, int K, int split_k) {
+int sm_count(int dev) {
+    static std::atomic<int> cache[kMaxDevices];
+    if (dev < 0 || dev >= kMaxDevices) return 148;
+    int v = cache[dev].load(std::memory_order_relaxed);
+    if (v > 0) return v;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) v = 148;
+    cache[dev].store(v, std::memory_order_relaxed);
+    return v;
+}
+
+// ----------------------------------------------------------- configurations
+enum class Path { kCluster, kStreamK };
+
+template <int NT, int ST>
+struct ClusterVariant {
+    using C_ = ClusterCfg<NT, ST>;
+    static constexpr int kTileN = NT;
+    static constexpr int kStages = ST;
+};
+template <int NT, int ST>
+struct StreamKVariant {
+    using C_ = StreamKCfg<NT, ST>;
+    static constexpr int kTileN = NT;
+    static constexpr int kStages = ST;
+};
+
+// One configuration per N tile: the deepest ring that fits in 227 KB.
+using CV16 = ClusterVariant<16, 8>;
+using CV32 = ClusterVariant<32, 8>;
+using CV64 = ClusterVariant<64, 6>;
+using CV128 = ClusterVariant<128, 4>;
+using CV256 = ClusterVariant<256, 2>;
+using SV16 = StreamKVariant<16, 8>;
+using SV32 = StreamKVariant<32, 8>;
+// Shallow rings (about 92 KB of shared memory): two CTAs fit on one SM, so
+// consecutive launches overlap on the same SM under programmatic launch.
+using CV16s = ClusterVariant<16, 4>;
+using CV32s = ClusterVariant<32, 4>;
+using SV16s = StreamKVariant<16, 4>;
+using SV32s = StreamKVariant<32, 4>;
+
+struct Plan {
+    Path path;
+    bool shallow;  // 4-stage ring, two CTAs per SM (narrow N only)
+    int tile_n;
+    int stages;
+    int split;  // cluster path: CTAs per cluster
+    int grid;   // stream-K path: persistent CTAs
+    int smem;
+    int m_tiles, n_tiles;
+    int stages_total;  // 128-K stages per tile
+};
+
+int cluster_stages(int tn) {
+    switch (tn) {
+        case 16: return CV16::kStages;
+        case 32: return CV32::kStages;
+        case 64: return CV64::kStages;
+        case 128: return CV128::kStages;
+        default: return CV256::kStages;
+    }
+}
+int cluster_smem(int tn) {
+    switch (tn) {
+        case 16: return CV16::C_::SMEM_ALLOC;
+        case 32: return CV32::C_::SMEM_ALLOC;
+        case 64: return CV64::C_::SMEM_ALLOC;
+        case 128: return CV128::C_::SMEM_ALLOC;
+        default: return CV256::C_::SMEM_ALLOC;
+    }
+}
+
+Plan make_plan(int M, int N, int K, int split_k, int sms) {
     Plan p{};
     int tn = N <= 16 ? 16 : N <= 32 ? 32 : N <= 64 ? 64 : 128;
-    int forced = env_int("SPMM24_TILE_N", 0);  // tuning override (16/32/64/128/256)
+    const int forced = env_int("SPMM24_TILE_N", 0);  // tuning override (16/32/64/128/256)
     if (forced == 16 || forced == 32 || forced == 64 || forced == 128 || forced == 256) tn = forced;
     p.tile_n = tn;
-    p.stages = stages_for(tn);
-    p.smem = smem_for(tn);
     p.m_tiles = (M + kTileM - 1) / kTileM;
     p.n_tiles = (N + tn - 1) / tn;
     p.stages_total = (K / 64 + 1) / 2;
+    const long long tiles = (long long)p.m_tiles * p.n_tiles;
+    const long long units = tiles * p.stages_total;
+
+    // Narrow N (decode) streams weights: a 4-stage ring (about 92 KB) puts two
+    // CTAs on each SM, so consecutive launches overlap on the same SM under
+    // programmatic launch, and the K split fills both slots of every SM.
+    const int stages_env = env_int("SPMM24_STAGES", 0);  // tuning override: 4 or 8
+    p.shallow = tn <= 32 && stages_env != 8;
+
+    // Stream-K (tuning option only; the cluster path measured faster on the
+    // decode shapes): one CTA per SM streaming an equal share of the stages.
+    if (env_int("SPMM24_PATH", 0) == 2 && split_k == 0 && tn <= 32 && units >= 2) {
+        p.path = Path::kStreamK;
+        if (p.shallow) {
+            p.stages = tn == 16 ? SV16s::kStages : SV32s::kStages;
+            p.smem = tn == 16 ? SV16s::C_::SMEM_ALLOC : SV32s::C_::SMEM_ALLOC;
+        } else {
+            p.stages = tn == 16 ? SV16::kStages : SV32::kStages;
+            p.smem = tn == 16 ? SV16::C_::SMEM_ALLOC : SV32::C_::SMEM_ALLOC;
+        }
+        const int g = env_int("SPMM24_GRID", sms);
+        p.grid = (int)std::max<long long>(1, std::min<long long>(g, units));
+        p.split = 1;
+        return p;
+    }
+    p.path = Path::kCluster;
+    if (p.shallow) {
+        p.stages = tn == 16 ? CV16s::kStages : CV32s::kStages;
+        p.smem = tn == 16 ? CV16s::C_::SMEM_ALLOC : CV32s::C_::SMEM_ALLOC;
+    } else {
+        p.stages = cluster_stages(tn);
+        p.smem = cluster_smem(tn);
+    }
     int s;
     if (split_k > 0) {
         s = split_k;
     } else {
-        long tiles = (long)p.m_tiles * p.n_tiles;
-        s = (int)(kNumSMs / tiles);
+        // As many K slices as fill the resident CTA slots (two per SM with the
+        // shallow ring), keeping at least two stages per slice.
+        const long long slots = (long long)sms * (p.shallow ? 2 : 1);
+        s = (int)std::max<long long>(1, slots / tiles);
         s = std::max(1, std::min(s, p.stages_total / 2));
     }
-    s = std::max(1, std::min(std::min(s, kMaxSplit), p.stages_total));
-    p.split = s;
+    p.split = std::max(1, std::min(std::min(s, kMaxSplit), p.stages_total));
+    p.grid = p.split * p.n_tiles * p.m_tiles;
     return p;
 }
 
-std::atomic<uint64_t> g_attr_done[5];  // per variant: bit per device (devices < 64)
+// ------------------------------------------------------------- workspace
+// Stream-K partial tiles and per-CTA flags, one buffer per (device, stream)
+// so that calls on different streams never share it.  Layout:
+// [flags: counter_cap u32][partials: partial_cap bytes].  The flags sit at
+// a fixed offset whatever the shape, are zeroed when the buffer is
+// (re)allocated, and every launch leaves the ones it used at zero again.
+struct Workspace {
+    void* ptr = nullptr;
+    size_t counter_cap = 0;  // number of u32 counters
+    size_t partial_cap = 0;  // bytes
+};
+std::mutex g_ws_mu;
+std::map<std::pair<int, uintptr_t>, Workspace>* g_ws = new std::map<std::pair<int, uintptr_t>, Workspace>();
 
-template <class V>
-cudaError_t launch_variant(const Plan& pl, cudaStream_t stream, const CUtensorMap& ta, const CUtensorMap& tb,
-                           const CUtensorMap& te, const KernelParams& kp, int variant_idx) {
-    auto kern = spmm24_sm100_kernel<V::kTileN, V::kStages>;
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return e;
-    const uint64_t bit = 1ull << (dev & 63);
-    if (!(g_attr_done[variant_idx].load(std::memory_order_acquire) & bit)) {
-        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, V::C_::SMEM_ALLOC);
+cudaError_t get_workspace(int dev, cudaStream_t stream, size_t counters, size_t partial_bytes, uint32_t** ctr,
+                          float** partials) {
+    std::lock_guard<std::mutex> lk(g_ws_mu);
+    Workspace& w = (*g_ws)[{dev, reinterpret_cast<uintptr_t>(stream)}];
+    if (w.ptr == nullptr || w.counter_cap < counters || w.partial_cap < partial_bytes) {
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        cudaError_t e = cudaStreamIsCapturing(stream, &cs);
         if (e != cudaSuccess) return e;
-        g_attr_done[variant_idx].fetch_or(bit, std::memory_order_acq_rel);
+        if (cs != cudaStreamCaptureStatusNone) return cudaErrorStreamCaptureUnsupported;
+        size_t ncap = std::max<size_t>(std::max(counters, w.counter_cap), 16384);
+        size_t pcap = std::max<size_t>(std::max(partial_bytes, w.partial_cap), (size_t)4 << 20);
+        if (w.ptr) {
+            // The old buffer may still be in use by work queued on this stream.
+            if ((e = cudaStreamSynchronize(stream)) != cudaSuccess) return e;
+            cudaFree(w.ptr);
+            w = Workspace{};
+        }
+        const size_t cbytes = (ncap * sizeof(uint32_t) + 255) & ~(size_t)255;
+        void* p = nullptr;
+        if ((e = cudaMalloc(&p, cbytes + pcap)) != cudaSuccess) return e;
+        if ((e = cudaMemsetAsync(p, 0, cbytes, stream)) != cudaSuccess) {
+            cudaFree(p);
+            return e;
+        }
+        w.ptr = p;
+        w.counter_cap = ncap;
+        w.partial_cap = pcap;
     }
+    const size_t cbytes = (w.counter_cap * sizeof(uint32_t) + 255) & ~(size_t)255;
+    *ctr = static_cast<uint32_t*>(w.ptr);
+    *partials = reinterpret_cast<float*>(static_cast<uint8_t*>(w.ptr) + cbytes);
+    return cudaSuccess;
+}
+
+std::atomic<uint64_t> g_attr_done[16];  // per kernel variant: one bit per device
+
+template <class Kern>
+cudaError_t prepare(Kern kern, int smem, int dev, int idx) {
+    const uint64_t bit = 1ull << (dev & 63);
+    if (g_attr_done[idx].load(std::memory_order_acquire) & bit) return cudaSuccess;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    g_attr_done[idx].fetch_or(bit, std::memory_order_acq_rel);
+    return cudaSuccess;
+}
+
+template <class Kern, class Params>
+cudaError_t launch_kernel(Kern kern, dim3 grid, int smem, cudaStream_t stream, unsigned cluster_x, bool pdl,
+                          const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& te, const Params& kp) {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)pl.split, (unsigned)pl.n_tiles, (unsigned)pl.m_tiles);
+    cfg.gridDim = grid;
     cfg.blockDim = dim3(kThreads, 1, 1);
-    cfg.dynamicSmemBytes = V::C_::SMEM_ALLOC;
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = (unsigned)pl.split;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
+    cudaLaunchAttribute attr[2];
+    int n = 0;
+    if (cluster_x > 1) {
+        attr[n].id = cudaLaunchAttributeClusterDimension;
+        attr[n].val.clusterDim.x = cluster_x;
+        attr[n].val.clusterDim.y = 1;
+        attr[n].val.clusterDim.z = 1;
+        ++n;
+    }
+    if (pdl) {
+        attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[n].val.programmaticStreamSerializationAllowed = 1;
+        ++n;
+    }
     cfg.attrs = attr;
-    cfg.numAttrs = pl.split > 1 ? 1 : 0;
+    cfg.numAttrs = n;
     return cudaLaunchKernelEx(&cfg, kern, ta, tb, te, kp);
 }
 
+template <class V>
+cudaError_t launch_cluster(const Plan& pl, cudaStream_t stream, int dev, bool pdl, const CUtensorMap& ta,
+                           const CUtensorMap& tb, const CUtensorMap& te, const ClusterParams& kp, int idx) {
+    auto kern = spmm24_cluster_kernel<V::kTileN, V::kStages>;
+    cudaError_t e = prepare(kern, V::C_::SMEM_ALLOC, dev, idx);
+    if (e != cudaSuccess) return e;
+    return launch_kernel(kern, dim3((unsigned)pl.split, (unsigned)pl.n_tiles, (unsigned)pl.m_tiles),
+                         V::C_::SMEM_ALLOC, stream, (unsigned)pl.split, pdl, ta, tb, te, kp);
+}
+
+template <class V>
+cudaError_t launch_streamk(const Plan& pl, cudaStream_t stream, int dev, bool pdl, const CUtensorMap& ta,
+                           const CUtensorMap& tb, const CUtensorMap& te, const StreamKParams& kp, int idx) {
+    auto kern = spmm24_streamk_kernel<V::kTileN, V::kStages>;
+    cudaError_t e = prepare(kern, V::C_::SMEM_ALLOC, dev, idx);
+    if (e != cudaSuccess) return e;
+    return launch_kernel(kern, dim3((unsigned)pl.grid, 1, 1), V::C_::SMEM_ALLOC, stream, 1u, pdl, ta, tb, te, kp);
+}
+
+size_t streamk_partial_bytes(const Plan& pl) { return (size_t)pl.grid * kTileM * pl.tile_n * sizeof(float); }
+
 cudaError_t launch_impl(cudaStream_t stream, const void* A, const void* B, const uint16_t* E, void* C, int M, int N,
-                        int K, int split_k) {
+                        int K, int split_k, unsigned flags) {
     g_last_error[0] = '\0';
     if (!A || !B || !E || !C) return invalid("null pointer");
     if (M <= 0 || N <= 0 || K <= 0) return invalid("M, N and K must be positive");
@@ -173,8 +316,33 @@ cudaError_t launch_impl(cudaStream_t stream, const void* A, const void* B, const
     if (((uintptr_t)A | (uintptr_t)B | (uintptr_t)E) & 15u) return invalid("A, B and metadata must be 16-byte aligned");
     if ((uintptr_t)C & 1u) return invalid("C must be 2-byte aligned");
     if ((long)M / kTileM >= 65535) return invalid("M too large");
+    if (flags & ~(unsigned)(SPMM24_STATIC_WEIGHTS | SPMM24_NO_PDL)) return invalid("unknown flag");
 
-    const Plan pl = make_plan(M, N, K, split_k);
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    Plan pl = make_plan(M, N, K, split_k, sm_count(dev));
+
+    uint32_t* ws_counters = nullptr;
+    float* ws_partials = nullptr;
+    if (pl.path == Path::kStreamK) {
+        e = get_workspace(dev, stream, (size_t)pl.grid, streamk_partial_bytes(pl), &ws_counters, &ws_partials);
+        if (e == cudaErrorStreamCaptureUnsupported) {
+            // First use of this stream under graph capture: no allocation is
+            // allowed, so fall back to the workspace-free cluster path.
+            cudaGetLastError();
+            pl = make_plan(M, N, K, 0, sm_count(dev));
+            pl.path = Path::kCluster;
+            pl.shallow = false;
+            pl.stages = cluster_stages(pl.tile_n);
+            pl.smem = cluster_smem(pl.tile_n);
+            int s = std::max(1, std::min((int)(sm_count(dev) / ((long long)pl.m_tiles * pl.n_tiles)),
+                                         pl.stages_total / 2));
+            pl.split = std::max(1, std::min(std::min(s, kMaxSplit), pl.stages_total));
+        } else if (e != cudaSuccess) {
+            return e;
+        }
+    }
 
     // A: (128 halves of one 16x8 block, bands, 16-K blocks); box 8 bands x 8 blocks.
     CUtensorMap ta, tb, te;
@@ -200,7 +368,31 @@ cudaError_t launch_impl(cudaStream_t stream, const void* A, const void* B, const
         if (!encode(&te, 2, E, dims, str, box)) return invalid("TMA descriptor for metadata could not be encoded");
     }
 
-    KernelParams kp;
+    const bool pdl = !(flags & SPMM24_NO_PDL);
+    const int wstatic = (flags & SPMM24_STATIC_WEIGHTS) ? 1 : 0;
+    if (pl.path == Path::kStreamK) {
+        StreamKParams kp;
+        kp.C = static_cast<__half*>(C);
+        kp.ws = ws_partials;
+        kp.flags = ws_counters;
+        kp.M = M;
+        kp.N = N;
+        kp.K = K;
+        kp.groups = K / 64;
+        kp.stages_per_tile = pl.stages_total;
+        kp.m_tiles = pl.m_tiles;
+        kp.n_tiles = pl.n_tiles;
+        kp.units = (long long)pl.m_tiles * pl.n_tiles * pl.stages_total;
+        kp.grid = pl.grid;
+        kp.weights_static = wstatic;
+        if (pl.shallow) {
+            if (pl.tile_n == 16) return launch_streamk<SV16s>(pl, stream, dev, pdl, ta, tb, te, kp, 7);
+            return launch_streamk<SV32s>(pl, stream, dev, pdl, ta, tb, te, kp, 8);
+        }
+        if (pl.tile_n == 16) return launch_streamk<SV16>(pl, stream, dev, pdl, ta, tb, te, kp, 5);
+        return launch_streamk<SV32>(pl, stream, dev, pdl, ta, tb, te, kp, 6);
+    }
+    ClusterParams kp;
     kp.C = static_cast<__half*>(C);
     kp.M = M;
     kp.N = N;
@@ -208,13 +400,17 @@ cudaError_t launch_impl(cudaStream_t stream, const void* A, const void* B, const
     kp.groups = K / 64;
     kp.stages_total = pl.stages_total;
     kp.split = pl.split;
-
+    kp.weights_static = wstatic;
+    if (pl.shallow) {
+        if (pl.tile_n == 16) return launch_cluster<CV16s>(pl, stream, dev, pdl, ta, tb, te, kp, 9);
+        return launch_cluster<CV32s>(pl, stream, dev, pdl, ta, tb, te, kp, 10);
+    }
     switch (pl.tile_n) {
-        case 16: return launch_variant<V16>(pl, stream, ta, tb, te, kp, 0);
-        case 32: return launch_variant<V32>(pl, stream, ta, tb, te, kp, 1);
-        case 64: return launch_variant<V64>(pl, stream, ta, tb, te, kp, 2);
-        case 128: return launch_variant<V128>(pl, stream, ta, tb, te, kp, 3);
-        default: return launch_variant<V256>(pl, stream, ta, tb, te, kp, 4);
+        case 16: return launch_cluster<CV16>(pl, stream, dev, pdl, ta, tb, te, kp, 0);
+        case 32: return launch_cluster<CV32>(pl, stream, dev, pdl, ta, tb, te, kp, 1);
+        case 64: return launch_cluster<CV64>(pl, stream, dev, pdl, ta, tb, te, kp, 2);
+        case 128: return launch_cluster<CV128>(pl, stream, dev, pdl, ta, tb, te, kp, 3);
+        default: return launch_cluster<CV256>(pl, stream, dev, pdl, ta, tb, te, kp, 4);
     }
 }
 
@@ -226,21 +422,32 @@ extern "C" cudaError_t spmm24_launch(cudaStream_t stream, const void* compressed
                                      const uint16_t* metadata, void* c, int M, int N, int K, void* split_reduction,
                                      int split_k) {
     (void)split_reduction;
-    return spmm24::launch_impl(stream, compressed_a, b_packed, metadata, c, M, N, K, split_k);
+    return spmm24::launch_impl(stream, compressed_a, b_packed, metadata, c, M, N, K, split_k, 0u);
+}
+
+extern "C" cudaError_t spmm24_launch_ex(cudaStream_t stream, const void* compressed_a, const void* b_packed,
+                                        const uint16_t* metadata, void* c, int M, int N, int K, int split_k,
+                                        unsigned flags) {
+    return spmm24::launch_impl(stream, compressed_a, b_packed, metadata, c, M, N, K, split_k, flags);
 }
 
 extern "C" size_t spmm24_workspace_bytes(int, int, int, int) { return 0; }
 
 extern "C" int spmm24_select_config(int M, int N, int K, int split_k, spmm24_config* out) {
     if (!out || M <= 0 || N <= 0 || K <= 0 || M % 16 || K % 64 || split_k < 0) return -1;
-    const spmm24::Plan pl = spmm24::make_plan(M, N, K, split_k);
+    int dev = 0;
+    int sms = (cudaGetDevice(&dev) == cudaSuccess) ? spmm24::sm_count(dev) : 148;
+    if (sms <= 0) sms = 148;
+    cudaGetLastError();
+    const spmm24::Plan pl = spmm24::make_plan(M, N, K, split_k, sms);
     out->tile_m = spmm24::kTileM;
     out->tile_n = pl.tile_n;
     out->stage_k = 128;
     out->stages = pl.stages;
-    out->split_k = pl.split;
-    out->grid_ctas = pl.split * pl.n_tiles * pl.m_tiles;
+    out->split_k = pl.path == spmm24::Path::kStreamK ? 0 : pl.split;
+    out->grid_ctas = pl.grid;
     out->smem_bytes = pl.smem;
+    out->stream_k = pl.path == spmm24::Path::kStreamK ? 1 : 0;
     return 0;
 }
 
@@ -261,11 +468,19 @@ extern "C" cudaError_t spmm24_device_status(int device, uint32_t* status_out) {
 
 extern "C" const char* spmm24_last_error(void) { return spmm24::g_last_error; }
 
-extern "C" const char* spmm24_version(void) { return "spmm24 0.1.0 (sm_100a tcgen05.mma.sp)"; }
+#ifdef SPMM24_TRACE
+// Trace builds only: where the kernels write their per-CTA timeline.
+extern "C" cudaError_t spmm24_set_trace(void* buf) {
+    return cudaMemcpyToSymbol(spmm24::g_spmm24_trace, &buf, sizeof(buf));
+}
+#endif
+
+extern "C" const char* spmm24_version(void) { return "spmm24 0.2.0 (sm_100a tcgen05.mma.sp)"; }
 
 // ------------------------------------------------------- C++ drop-in
 cudaError_t SpMM_N2M4_Launch(cudaStream_t stream, const half* Compressed_A, const half* B, const uint16_t* metadata,
                              half* C, const int M_Global, const int N_Global, const int K_Global,
                              half* Split_Reduction, const int Split_K) {
-    return spmm24::launch_impl(stream, Compressed_A, B, metadata, C, M_Global, N_Global, K_Global, Split_K);
+    (void)Split_Reduction;
+    return spmm24::launch_impl(stream, Compressed_A, B, metadata, C, M_Global, N_Global, K_Global, Split_K, 0u);
 }

@@ -1,0 +1,158 @@
+// spmm24_common.cuh -- pieces shared by the sm_100a 2:4 SpMM kernels: the
+// shared-memory stage layout, the TMA loads of one 128-K stage, the sparse
+// MMAs of one stage, and the metadata fix-up for an odd final 64-K group.
+//
+// Input formats are the reference ABI's, unchanged (SpeakOutLoudly/CUDA-Repo
+// test/utils.h:91-229):
+//   A  compressed fp16 values, 16x8 blocks band-major: band b (16 rows),
+//      16-K block q, row r -> 8 halves at ((b*K/16+q)*16+r)*8
+//   E  reordered 2-bit metadata: per band and 64-K group g, 8 rows of 16
+//      bytes; row i holds four u32 words (row i, block t) | (row i+8, block t)<<16
+//   B  packed: ceil(N/8) strips of K x 8 row-major halves
+//   C  row-major M x N fp16
+//
+// Mapping onto tcgen05.mma.sp (kind::f16, M=128, K=32 logical per MMA):
+//   One pipeline stage covers two 64-K groups g0, g0+1 (128 logical K).
+//   A single tcgen05.cp.128x128b moves the stage's metadata straight from
+//   the reference layout into TMEM: smem row l = 16*band + 8*h + i (h picks
+//   the group) lands in TMEM lane l, its four words in four columns.  The
+//   sparse MMA reads lane m0 + 8*k1 + 16*band for rows (m0, m0+8) of a band
+//   and the k1-th 16-K half of its 32-K step, so MMA j of the stage consumes
+//   the K-slices {group g0 block j, group g0+1 block j}.  A and B are laid
+//   out in shared memory with the same permutation of 16-K blocks -- the TMA
+//   boxes do it -- which leaves the sum over K unchanged.
+#pragma once
+#include <cuda_fp16.h>
+#include <cstdint>
+#include "ptx_sm100.cuh"
+
+namespace spmm24 {
+
+constexpr int kTileM = 128;                        // rows of C per tile (one M=128 MMA)
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s bound on any wait
+
+// Status bits written to the device status word when a bounded wait gives up.
+constexpr uint32_t kStatusProducerTimeout = 1u;
+constexpr uint32_t kStatusMmaTimeout = 2u;
+constexpr uint32_t kStatusEpilogueTimeout = 4u;
+
+// Sticky device status word (per device, per process).  Bounded waits that
+// give up OR their bit in; the host reads and clears it through
+// spmm24_device_status().
+static __device__ uint32_t g_spmm24_status;
+
+// Optional per-CTA timeline for performance work: builds that define
+// SPMM24_TRACE record %globaltimer and clock64 stamps into g_spmm24_trace
+// (16 words per CTA, linear CTA index).  The product build compiles the
+// stamps away.
+#ifdef SPMM24_TRACE
+__device__ unsigned long long* g_spmm24_trace;
+__device__ __forceinline__ void trace_stamp(int slot) {
+    if (g_spmm24_trace) {
+        const size_t cta = blockIdx.x + (size_t)gridDim.x * (blockIdx.y + (size_t)gridDim.y * blockIdx.z);
+        unsigned long long t, c;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        c = clock64();
+        g_spmm24_trace[cta * 16 + 2 * slot] = t;
+        g_spmm24_trace[cta * 16 + 2 * slot + 1] = c;
+    }
+}
+#define SPMM24_STAMP(slot) ::spmm24::trace_stamp(slot)
+#else
+#define SPMM24_STAMP(slot) \
+    do {                   \
+    } while (0)
+#endif
+
+template <int N_TILE, int STAGES, int ACC_BUFS>
+struct Cfg {
+    static_assert(N_TILE % 16 == 0 && N_TILE >= 16 && N_TILE <= 256, "M=128 sparse MMA needs N % 16 == 0");
+    static constexpr int A_BYTES = 8 * 8 * 256;          // 8 16-K blocks x 8 bands x (16 rows x 16 B)
+    static constexpr int B_BYTES = (N_TILE / 8) * 2048;  // strips x (4 blocks x 2 groups x 256 B)
+    static constexpr int E_BYTES = 16 * 128;             // 16 core matrices of 8 x 16 B
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + E_BYTES;
+    static constexpr int RING_BYTES = STAGES * STAGE_BYTES;
+    static constexpr int META_COL = ACC_BUFS * N_TILE;  // TMEM column of the metadata ring
+    static constexpr int TMEM_NEED = META_COL + 4 * STAGES;
+    static constexpr int TMEM_COLS = TMEM_NEED <= 32 ? 32 : TMEM_NEED <= 64 ? 64 : TMEM_NEED <= 128 ? 128
+                                                          : TMEM_NEED <= 256 ? 256 : 512;
+    static_assert(TMEM_NEED <= 512, "TMEM overflow");
+};
+
+// Shared-memory matrix descriptor, canonical no-swizzle layout (version 1).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+    return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+           ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
+}
+
+// Instruction descriptor: sparse, D=f32, A=B=f16, A K-major, B MN-major.
+template <int N_TILE>
+__host__ __device__ constexpr uint32_t make_idesc() {
+    return (1u << 2) | (1u << 4) | (0u << 7) | (0u << 10) | (0u << 15) | (1u << 16) |
+           ((uint32_t)(N_TILE >> 3) << 17) | ((uint32_t)(kTileM >> 4) << 24);
+}
+
+// The weight (A + metadata) half of one stage's loads.
+template <class C_>
+__device__ __forceinline__ void load_stage_weights(uint8_t* st, uint64_t* bar, const CUtensorMap* tmA,
+                                                   const CUtensorMap* tmE, int band0, int g0, uint64_t pol) {
+    // A: box (128 halves, 8 bands, 8 blocks) -> smem [block][band][256 B]
+    ptx::tma_load_3d(st, tmA, bar, 0, band0, 4 * g0, pol);
+    // E: box (128 words, 8 bands) -> smem [band][group][128 B]
+    ptx::tma_load_2d(st + C_::A_BYTES + C_::B_BYTES, tmE, bar, 64 * g0, band0, pol);
+}
+
+// The activation (B) half of one stage's loads.
+template <class C_>
+__device__ __forceinline__ void load_stage_acts(uint8_t* st, uint64_t* bar, const CUtensorMap* tmB, int strip0, int g0,
+                                                uint64_t pol) {
+    // B: box (128 halves, 2 groups, 4 blocks, strips) -> smem [strip][block][group][256 B]
+    ptx::tma_load_4d(st + C_::A_BYTES, tmB, bar, 0, g0, 0, strip0, pol);
+}
+
+// Final stage of an odd number of 64-K groups: the second group lies past K,
+// so TMA filled its A, B and metadata with zeros.  Give those metadata rows
+// a valid ordered index pattern (kept positions 0 and 1 of every group of
+// four); the zero A values keep the contribution at zero.  Whole warp.
+template <class C_>
+__device__ __forceinline__ void patch_tail_metadata(uint8_t* st, int lane) {
+    uint8_t* e = st + C_::A_BYTES + C_::B_BYTES;
+    const uint4 pat = make_uint4(0x44444444u, 0x44444444u, 0x44444444u, 0x44444444u);
+    for (int c = lane; c < 64; c += 32) {
+        const int cm = c >> 3;  // which of the 8 second-group core matrices
+        *reinterpret_cast<uint4*>(e + (2 * cm + 1) * 128 + (c & 7) * 16) = pat;
+    }
+    ptx::fence_proxy_async_smem();
+    __syncwarp();
+}
+
+// Metadata copy + the four sparse MMAs of one stage (single thread).
+template <class C_, int N_TILE>
+__device__ __forceinline__ void mma_stage(uint32_t st_addr, uint32_t meta_col, uint32_t d_tmem, uint32_t& accumulate) {
+    constexpr uint32_t idesc = make_idesc<N_TILE>();
+    const uint32_t stB = st_addr + C_::A_BYTES;
+    const uint32_t stE = stB + C_::B_BYTES;
+    ptx::tmem_cp_128x128b(meta_col, smem_desc(stE, 0, 128));
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const uint64_t adesc = smem_desc(st_addr + j * 2048, 4 * 2048, 128);
+        const uint64_t bdesc = smem_desc(stB + j * 512, 128, 2048);
+        ptx::mma_sp_f16(d_tmem, adesc, bdesc, meta_col + (j & 2), idesc | (uint32_t)(j & 1), accumulate);
+        accumulate = 1;
+    }
+}
+
+// Round 8 fp32 values to fp16 and store them at `out` (16-byte store when
+// allowed, else element by element up to `lim`).
+__device__ __forceinline__ void store_h8(__half* out, const float* v, bool vec, int lim) {
+    if (vec) {
+        __align__(16) __half h[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) h[e] = __float2half_rn(v[e]);
+        *reinterpret_cast<uint4*>(out) = *reinterpret_cast<const uint4*>(h);
+    } else {
+        for (int e = 0; e < lim && e < 8; ++e) out[e] = __float2half_rn(v[e]);
+    }
+}
+
+}  // namespace spmm24

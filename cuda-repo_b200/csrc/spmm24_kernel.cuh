@@ -1,106 +1,86 @@
-// spmm24_kernel.cuh -- the sm_100a 2:4 sparse SpMM kernel, C = A_sparse * B.
+// spmm24_kernel.cuh -- the sm_100a 2:4 sparse SpMM kernels, C = A_sparse * B.
 //
-// Replaces SpMM_N2M4_Kernel (SpeakOutLoudly/CUDA-Repo src/SpMM_Kernel.cuh:301)
+// Replace SpMM_N2M4_Kernel (SpeakOutLoudly/CUDA-Repo src/SpMM_Kernel.cuh:301)
 // and the separate split-K pass SplitK_Reduction (src/reduce_Kernel.cuh:27).
+// Formats and the tcgen05 mapping are described in spmm24_common.cuh.
 //
-// Input formats are the reference ABI's, unchanged:
-//   A  compressed fp16 values, 16x8 blocks band-major (test/utils.h:114-147):
-//      band b (16 rows), 16-K block q, row r -> 8 halves at ((b*K/16+q)*16+r)*8
-//   E  reordered 2-bit metadata (test/utils.h:155-185): per band and 64-K
-//      group g, 8 rows of 16 bytes; row i holds four u32 words
-//      (row i, block t) | (row i+8, block t) << 16 for t = 0..3
-//   B  packed: N/8 strips of K x 8 row-major halves (test/utils.h:188-229)
-//   C  row-major M x N fp16
+// Two kernels share the stage layout and the MMA issue:
 //
-// Mapping onto tcgen05.mma.sp (kind::f16, M=128, K=32 logical per MMA):
-//   One pipeline stage covers two 64-K groups g0, g0+1 (128 logical K).
-//   A single tcgen05.cp.128x128b moves the stage's metadata straight from
-//   the reference layout into TMEM: smem row l = 16*band + 8*h + i (h picks
-//   the group) lands in TMEM lane l, its four words in four columns.  The
-//   sparse MMA reads lane m0 + 8*k1 + 16*band for rows (m0, m0+8) of a band
-//   and the k1-th 16-K half of its 32-K step, so MMA j of the stage consumes
-//   the K-slices {group g0 block j, group g0+1 block j}.  A and B are laid
-//   out in shared memory with the same permutation of 16-K blocks, which is
-//   free (the TMA boxes do it) and leaves the sum over K unchanged.
+//   spmm24_cluster_kernel  one 128 x N_TILE tile per CTA; a split-K request
+//       of S becomes a thread-block cluster of S CTAs along K whose fp32
+//       partial tiles are reduce-scattered through distributed shared memory
+//       (no global workspace, no second launch, fixed summation order).
+//
+//   spmm24_streamk_kernel  a persistent grid (one CTA per SM) in which every
+//       CTA takes an equal share of the (tile, 128-K stage) units, walked
+//       tile-major.  A tile shared by several CTAs is finished by the CTA
+//       that holds its first unit; every other contributor starts its range
+//       inside that tile, so it processes its share first and publishes the
+//       fp32 partial (global workspace slot + release flag) early.  The
+//       finisher's epilogue warps collect the published partials while its
+//       own last segment is still streaming, so the end of the kernel only
+//       adds the accumulator and stores.  Summation order is fixed.
 //
 // Roles (192 threads):
-//   warp 0     TMA producer (one elected lane)
-//   warp 1     TMEM allocator, tcgen05.cp + tcgen05.mma issuer (one lane)
-//   warps 2-5  epilogue: TMEM -> registers -> shared -> coalesced fp16 stores
-// Split-K runs as a thread-block cluster of S CTAs along K; the partial
-// fp32 tiles are reduce-scattered through distributed shared memory (no
-// global workspace, no second launch, fixed summation order).
+//   warp 0     TMA producer (lane 0)
+//   warp 1     TMEM allocator, tcgen05.cp + tcgen05.mma issuer (lane 0)
+//   warps 2-5  epilogue: TMEM -> registers -> fp16 stores
+// Every wait is bounded; the producer starts before TMEM is allocated; the
+// kernels take part in programmatic dependent launch (they wait for the
+// previous grid before touching global memory it may write, and let the
+// next grid start launching early).
 #pragma once
-#include <cuda_fp16.h>
-#include <cstdint>
-#include "ptx_sm100.cuh"
+#include "spmm24_common.cuh"
 
 namespace spmm24 {
 
-constexpr int kTileM = 128;          // rows of C per CTA (one M=128 MMA)
-constexpr int kThreads = 192;        // 6 warps
-constexpr int kEpiThreads = 128;     // warps 2..5
-constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s bound on any wait
+constexpr int kThreads = 192;     // 6 warps
+constexpr int kEpiThreads = 128;  // warps 2..5
+constexpr uint32_t kBarEpi = 1;   // named barrier: epilogue warps
+constexpr uint32_t kBarTmem = 2;  // named barrier: warps 1..5 after TMEM allocation
 
-// Status bits written to the device status word when a bounded wait gives up.
-constexpr uint32_t kStatusProducerTimeout = 1u;
-constexpr uint32_t kStatusMmaTimeout = 2u;
-constexpr uint32_t kStatusEpilogueTimeout = 4u;
-
-// Sticky device status word (per device, per process).  Bounded waits that
-// give up OR their bit in; the host reads and clears it through
-// spmm24_device_status().
-static __device__ uint32_t g_spmm24_status;
-
-struct KernelParams {
+struct ClusterParams {
     __half* C;
     int M, N, K;
     int groups;        // K / 64
     int stages_total;  // ceil(groups / 2)
     int split;         // CTAs per cluster along K
+    int weights_static;
 };
 
+struct StreamKParams {
+    __half* C;
+    float* ws;        // one partial tile (128 x N_TILE fp32) per CTA
+    uint32_t* flags;  // one per CTA: 1 = its partial is published; zero between launches
+    int M, N, K;
+    int groups;           // K / 64
+    int stages_per_tile;  // ceil(groups / 2)
+    int m_tiles, n_tiles;
+    long long units;      // tiles * stages_per_tile
+    int grid;
+    int weights_static;
+};
+
+// -------------------------------------------------------------------------
 template <int N_TILE, int STAGES>
-struct Cfg {
-    static_assert(N_TILE % 16 == 0 && N_TILE >= 16 && N_TILE <= 256, "M=128 sparse MMA needs N % 16 == 0");
-    static constexpr int A_BYTES = 8 * 8 * 256;          // 8 16-K blocks x 8 bands x (16 rows x 16 B)
-    static constexpr int B_BYTES = (N_TILE / 8) * 2048;  // strips x (4 blocks x 2 groups x 256 B)
-    static constexpr int E_BYTES = 16 * 128;             // 16 core matrices of 8 x 16 B
-    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + E_BYTES;
-    static constexpr int BAR_OFFSET = STAGES * STAGE_BYTES;
+struct ClusterCfg : Cfg<N_TILE, STAGES, 1> {
+    using B_ = Cfg<N_TILE, STAGES, 1>;
+    static constexpr int BAR_OFFSET = B_::RING_BYTES;
     static constexpr int NUM_BARS = 2 * STAGES + 1;
     static constexpr int HOLDER_OFFSET = BAR_OFFSET + NUM_BARS * 8;
     static constexpr int SMEM_BYTES = HOLDER_OFFSET + 16;
     static constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;  // slack to align the base to 1024 B
-    static constexpr int META_COL = N_TILE;               // TMEM column of the metadata ring
-    static constexpr int TMEM_NEED = N_TILE + 4 * STAGES;
-    static constexpr int TMEM_COLS = TMEM_NEED <= 32 ? 32 : TMEM_NEED <= 64 ? 64 : TMEM_NEED <= 128 ? 128
-                                                          : TMEM_NEED <= 256 ? 256 : 512;
-    static constexpr int RED_PITCH = N_TILE + 4;  // floats per row of the reduction buffer
-    static_assert(TMEM_NEED <= 512, "TMEM overflow");
+    static constexpr int RED_PITCH = N_TILE + 4;         // floats per row of the reduction buffer
     static_assert(SMEM_ALLOC <= 232448, "shared memory overflow");
     // The reduction buffer reuses the stage ring: S sources x ceil(128/S) rows.
-    static_assert((kTileM + 7) * RED_PITCH * 4 <= STAGES * STAGE_BYTES, "reduction buffer does not fit");
+    static_assert((kTileM + 7) * RED_PITCH * 4 <= B_::RING_BYTES, "reduction buffer does not fit");
 };
-
-// Shared-memory matrix descriptor, canonical no-swizzle layout (version 1).
-__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
-    return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
-           ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
-}
-
-// Instruction descriptor: sparse, D=f32, A=B=f16, A K-major, B MN-major.
-template <int N_TILE>
-__host__ __device__ constexpr uint32_t make_idesc() {
-    return (1u << 2) | (1u << 4) | (0u << 7) | (0u << 10) | (0u << 15) | (1u << 16) |
-           ((uint32_t)(N_TILE >> 3) << 17) | ((uint32_t)(kTileM >> 4) << 24);
-}
 
 template <int N_TILE, int STAGES>
 __global__ void __launch_bounds__(kThreads, 1)
-spmm24_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                    const __grid_constant__ CUtensorMap tmE, const KernelParams p) {
-    using C_ = Cfg<N_TILE, STAGES>;
+spmm24_cluster_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                      const __grid_constant__ CUtensorMap tmE, const ClusterParams p) {
+    using C_ = ClusterCfg<N_TILE, STAGES>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + C_::BAR_OFFSET);
@@ -123,33 +103,37 @@ spmm24_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     const int st_count = st_base + (rank < st_rem ? 1 : 0);
 
     if (threadIdx.x == 0) {
+        SPMM24_STAMP(0);
         for (int s = 0; s < STAGES; ++s) {
             ptx::mbar_init(&full[s], 1);
             ptx::mbar_init(&empty[s], 1);
         }
         ptx::mbar_init(acc_full, 1);
         ptx::fence_mbarrier_init();
-        ptx::fence_proxy_async_smem();
         ptx::prefetch_tmap(&tmA);
         ptx::prefetch_tmap(&tmB);
         ptx::prefetch_tmap(&tmE);
     }
-    if (warp == 1) {
-        ptx::tmem_alloc(tmem_holder, C_::TMEM_COLS);
-        ptx::tmem_relinquish();
-    }
-    ptx::tc_fence_before();
     __syncthreads();
-    ptx::tc_fence_after();
-    const uint32_t tmem_base = *tmem_holder;
-    const uint32_t smem_base = ptx::smem_u32(smem);
+    if (threadIdx.x == 0) ptx::grid_dep_launch();
 
+    uint32_t tmem_base = 0;
     if (warp == 0) {
         // ---------------------------------------------------- TMA producer
         if (lane == 0) {
             const uint64_t pol_stream = ptx::policy_evict_first();  // A, E: read once
             const uint64_t pol_keep = ptx::policy_evict_last();     // B: re-read by every M tile
-            for (int it = 0; it < st_count; ++it) {
+            const int pre = p.weights_static ? min(STAGES, st_count) : 0;
+            for (int it = 0; it < pre; ++it) {  // weights of the first stages before the previous grid ends
+                uint8_t* st = smem + it * C_::STAGE_BYTES;
+                ptx::mbar_arrive_expect_tx(&full[it], C_::STAGE_BYTES);
+                load_stage_weights<C_>(st, &full[it], &tmA, &tmE, band0, 2 * (st_begin + it), pol_stream);
+            }
+            ptx::grid_dep_wait();
+            SPMM24_STAMP(1);
+            for (int it = 0; it < pre; ++it)
+                load_stage_acts<C_>(smem + it * C_::STAGE_BYTES, &full[it], &tmB, strip0, 2 * (st_begin + it), pol_keep);
+            for (int it = pre; it < st_count; ++it) {
                 const int s = it % STAGES;
                 const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
                 if (!ptx::mbar_wait_bounded(&empty[s], ph ^ 1u, kWaitLimitNs)) {
@@ -157,19 +141,27 @@ spmm24_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                     break;
                 }
                 uint8_t* st = smem + s * C_::STAGE_BYTES;
-                ptx::mbar_arrive_expect_tx(&full[s], C_::STAGE_BYTES);
                 const int g0 = 2 * (st_begin + it);
-                // A: box (128 halves, 8 bands, 8 blocks) -> smem [block][band][256 B]
-                ptx::tma_load_3d(st, &tmA, &full[s], 0, band0, 4 * g0, pol_stream);
-                // B: box (128 halves, 2 groups, 4 blocks, strips) -> smem [strip][block][group][256 B]
-                ptx::tma_load_4d(st + C_::A_BYTES, &tmB, &full[s], 0, g0, 0, strip0, pol_keep);
-                // E: box (128 words, 8 bands) -> smem [band][group][128 B]
-                ptx::tma_load_2d(st + C_::A_BYTES + C_::B_BYTES, &tmE, &full[s], 64 * g0, band0, pol_stream);
+                ptx::mbar_arrive_expect_tx(&full[s], C_::STAGE_BYTES);
+                load_stage_weights<C_>(st, &full[s], &tmA, &tmE, band0, g0, pol_stream);
+                load_stage_acts<C_>(st, &full[s], &tmB, strip0, g0, pol_keep);
             }
         }
-    } else if (warp == 1) {
+        __syncwarp();
+    } else {
+        if (warp == 1) {
+            ptx::tmem_alloc(tmem_holder, C_::TMEM_COLS);
+            ptx::tmem_relinquish();
+        }
+        ptx::tc_fence_before();
+        ptx::named_barrier(kBarTmem, kThreads - 32);
+        ptx::tc_fence_after();
+        tmem_base = *tmem_holder;
+    }
+
+    if (warp == 1) {
         // ------------------------------------------------------ MMA issuer
-        constexpr uint32_t idesc = make_idesc<N_TILE>();
+        const uint32_t smem_base = ptx::smem_u32(smem);
         uint32_t accumulate = 0;
         for (int it = 0; it < st_count; ++it) {
             const int s = it % STAGES;
@@ -178,36 +170,13 @@ spmm24_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                 if (lane == 0) atomicOr(&g_spmm24_status, kStatusMmaTimeout);
                 break;
             }
+            if (lane == 0 && it == 0) SPMM24_STAMP(2);
+            if (lane == 0 && it == st_count - 1) SPMM24_STAMP(3);
             ptx::tc_fence_after();
-            const uint32_t st = smem_base + s * C_::STAGE_BYTES;
-            const uint32_t stB = st + C_::A_BYTES;
-            const uint32_t stE = stB + C_::B_BYTES;
-            if (2 * (st_begin + it) + 1 >= p.groups) {
-                // Final stage of an odd number of 64-K groups: the second
-                // group is past K, so TMA filled its A, B and metadata with
-                // zeros.  Give those metadata rows a valid ordered index
-                // pattern (kept positions 0,1 in every group of four); the
-                // zero A values keep their contribution at zero.
-                uint8_t* e = smem + s * C_::STAGE_BYTES + C_::A_BYTES + C_::B_BYTES;
-                const uint4 pat = make_uint4(0x44444444u, 0x44444444u, 0x44444444u, 0x44444444u);
-                for (int c = lane; c < 64; c += 32) {
-                    const int cm = c >> 3;  // which of the 8 second-group core matrices
-                    *reinterpret_cast<uint4*>(e + (2 * cm + 1) * 128 + (c & 7) * 16) = pat;
-                }
-                ptx::fence_proxy_async_smem();
-                __syncwarp();
-            }
+            if (2 * (st_begin + it) + 1 >= p.groups) patch_tail_metadata<C_>(smem + s * C_::STAGE_BYTES, lane);
             if (lane == 0) {
-                const uint32_t meta_col = tmem_base + C_::META_COL + 4 * s;
-                ptx::tmem_cp_128x128b(meta_col, smem_desc(stE, 0, 128));
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const uint64_t adesc = smem_desc(st + j * 2048, 4 * 2048, 128);
-                    const uint64_t bdesc = smem_desc(stB + j * 512, 128, 2048);
-                    ptx::mma_sp_f16(tmem_base, adesc, bdesc, meta_col + (j & 2), idesc | (uint32_t)(j & 1),
-                                    accumulate);
-                    accumulate = 1;
-                }
+                mma_stage<C_, N_TILE>(smem_base + s * C_::STAGE_BYTES, tmem_base + C_::META_COL + 4 * s, tmem_base,
+                                      accumulate);
                 ptx::tc_commit(&empty[s]);
             }
             __syncwarp();
@@ -223,6 +192,7 @@ spmm24_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     const bool epi = warp >= 2;
     if (epi) {
         if (!ptx::mbar_wait_bounded(acc_full, 0, kWaitLimitNs)) atomicOr(&g_spmm24_status, kStatusEpilogueTimeout);
+        if (threadIdx.x == 64) SPMM24_STAMP(4);
         ptx::tc_fence_after();
     }
     __syncwarp();
@@ -243,10 +213,10 @@ spmm24_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             ptx::tmem_wait_ld();
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-                const uint32_t a = dst + (uint32_t)((c * 16 + q * 4) * 4);
                 if (S > 1) {
-                    ptx::st_cluster_v4(a, __uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
-                                       __uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3]));
+                    ptx::st_cluster_v4(dst + (uint32_t)((c * 16 + q * 4) * 4), __uint_as_float(v[4 * q]),
+                                       __uint_as_float(v[4 * q + 1]), __uint_as_float(v[4 * q + 2]),
+                                       __uint_as_float(v[4 * q + 3]));
                 } else {
                     *reinterpret_cast<float4*>(dst_row + c * 16 + q * 4) =
                         make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
@@ -260,9 +230,10 @@ spmm24_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     if (S > 1) {
         ptx::cluster_sync();  // all partial rows delivered to their owners
     } else if (epi) {
-        asm volatile("barrier.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
+        ptx::named_barrier(kBarEpi, kEpiThreads);
     }
     if (epi) {
+        ptx::grid_dep_wait();  // C may be read or written by the previous grid
         // Owner side: sum the S partial copies of this CTA's rows in a fixed
         // order, round to fp16 and store with 16-byte coalesced writes.
         const int my_start = (kTileM * rank + S - 1) / S;
@@ -288,25 +259,260 @@ spmm24_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             const int gm = m0 + my_start + lr;
             const int gn = n0 + ch * 8;
             if (gm >= p.M || gn >= p.N) continue;
-            __half* out = p.C + (size_t)gm * p.N + gn;
-            if (vec_ok) {
-                __align__(16) __half h[8];
-#pragma unroll
-                for (int e = 0; e < 8; ++e) h[e] = __float2half_rn(acc[e]);
-                *reinterpret_cast<uint4*>(out) = *reinterpret_cast<const uint4*>(h);
-            } else {
-                const int lim = min(8, p.N - gn);
-                for (int e = 0; e < lim; ++e) out[e] = __float2half_rn(acc[e]);
-            }
+            store_h8(p.C + (size_t)gm * p.N + gn, acc, vec_ok, p.N - gn);
         }
     }
 
+    if (threadIdx.x == 64) SPMM24_STAMP(5);
     ptx::tc_fence_before();
     __syncthreads();
     if (warp == 1) {
         ptx::tc_fence_after();
         ptx::tmem_dealloc(tmem_base, C_::TMEM_COLS);
     }
+    if (threadIdx.x == 0) SPMM24_STAMP(6);
+}
+
+// -------------------------------------------------------------------------
+template <int N_TILE, int STAGES>
+struct StreamKCfg : Cfg<N_TILE, STAGES, 2> {
+    using B_ = Cfg<N_TILE, STAGES, 2>;
+    static constexpr int BAR_OFFSET = B_::RING_BYTES;
+    static constexpr int NUM_BARS = 2 * STAGES + 4;  // full, empty, acc_full[2], acc_empty[2]
+    static constexpr int HOLDER_OFFSET = BAR_OFFSET + NUM_BARS * 8;
+    static constexpr int SMEM_BYTES = HOLDER_OFFSET + 16;
+    static constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;
+    static_assert(N_TILE <= 64, "stream-K keeps one accumulator row in registers");
+    static_assert(SMEM_ALLOC <= 232448, "shared memory overflow");
+};
+
+__host__ __device__ __forceinline__ long long sk_unit_begin(long long c, long long units, long long grid) {
+    return c * units / grid;
+}
+// CTA whose unit range contains unit u.
+__host__ __device__ __forceinline__ int sk_cta_of(long long u, long long units, long long grid) {
+    return (int)(((u + 1) * grid - 1) / units);
+}
+
+template <int N_TILE, int STAGES>
+__global__ void __launch_bounds__(kThreads, 1)
+spmm24_streamk_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                      const __grid_constant__ CUtensorMap tmE, const StreamKParams p) {
+    using C_ = StreamKCfg<N_TILE, STAGES>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C_::BAR_OFFSET);
+    uint64_t* empty = full + STAGES;
+    uint64_t* acc_full = empty + STAGES;  // [2]
+    uint64_t* acc_empty = acc_full + 2;   // [2]
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + C_::HOLDER_OFFSET);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int cta = blockIdx.x;
+    const long long U = p.units;
+    const int SPT = p.stages_per_tile;
+    const long long u_begin = sk_unit_begin(cta, U, p.grid);
+    const long long u_end = sk_unit_begin(cta + 1, U, p.grid);
+
+    if (threadIdx.x == 0) {
+        SPMM24_STAMP(0);
+        for (int s = 0; s < STAGES; ++s) {
+            ptx::mbar_init(&full[s], 1);
+            ptx::mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            ptx::mbar_init(&acc_full[b], 1);
+            ptx::mbar_init(&acc_empty[b], kEpiThreads / 32);
+        }
+        ptx::fence_mbarrier_init();
+        ptx::prefetch_tmap(&tmA);
+        ptx::prefetch_tmap(&tmB);
+        ptx::prefetch_tmap(&tmE);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) ptx::grid_dep_launch();
+
+    uint32_t tmem_base = 0;
+    if (warp == 0) {
+        // ---------------------------------------------------- TMA producer
+        if (lane == 0) {
+            const uint64_t pol_stream = ptx::policy_evict_first();
+            const uint64_t pol_keep = ptx::policy_evict_last();
+            const int count = (int)(u_end - u_begin);
+            const int pre = p.weights_static ? min(STAGES, count) : 0;
+            for (int it = 0; it < pre; ++it) {
+                const long long u = u_begin + it;
+                const int tile = (int)(u / SPT), g0 = 2 * (int)(u % SPT);
+                ptx::mbar_arrive_expect_tx(&full[it], C_::STAGE_BYTES);
+                load_stage_weights<C_>(smem + it * C_::STAGE_BYTES, &full[it], &tmA, &tmE, (tile / p.n_tiles) * 8, g0,
+                                       pol_stream);
+            }
+            ptx::grid_dep_wait();
+            SPMM24_STAMP(1);
+            for (int it = 0; it < pre; ++it) {
+                const long long u = u_begin + it;
+                const int tile = (int)(u / SPT), g0 = 2 * (int)(u % SPT);
+                load_stage_acts<C_>(smem + it * C_::STAGE_BYTES, &full[it], &tmB, (tile % p.n_tiles) * (N_TILE / 8), g0,
+                                    pol_keep);
+            }
+            for (int it = pre; it < count; ++it) {
+                const int s = it % STAGES;
+                const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
+                if (!ptx::mbar_wait_bounded(&empty[s], ph ^ 1u, kWaitLimitNs)) {
+                    atomicOr(&g_spmm24_status, kStatusProducerTimeout);
+                    break;
+                }
+                const long long u = u_begin + it;
+                const int tile = (int)(u / SPT), g0 = 2 * (int)(u % SPT);
+                uint8_t* st = smem + s * C_::STAGE_BYTES;
+                ptx::mbar_arrive_expect_tx(&full[s], C_::STAGE_BYTES);
+                load_stage_weights<C_>(st, &full[s], &tmA, &tmE, (tile / p.n_tiles) * 8, g0, pol_stream);
+                load_stage_acts<C_>(st, &full[s], &tmB, (tile % p.n_tiles) * (N_TILE / 8), g0, pol_keep);
+            }
+        }
+        __syncwarp();
+    } else {
+        if (warp == 1) {
+            ptx::tmem_alloc(tmem_holder, C_::TMEM_COLS);
+            ptx::tmem_relinquish();
+        }
+        ptx::tc_fence_before();
+        ptx::named_barrier(kBarTmem, kThreads - 32);
+        ptx::tc_fence_after();
+        tmem_base = *tmem_holder;
+    }
+
+    if (warp == 1) {
+        // ------------------------------------------------------ MMA issuer
+        const uint32_t smem_base = ptx::smem_u32(smem);
+        int it = 0;
+        int seg = 0;
+        bool ok = true;
+        for (long long u = u_begin; u < u_end && ok; ++seg) {
+            const long long tile = u / SPT;
+            const long long seg_end = min(u_end, (tile + 1) * SPT);
+            const int b = seg & 1;
+            if (!ptx::mbar_wait_bounded(&acc_empty[b], (uint32_t)((seg >> 1) & 1) ^ 1u, kWaitLimitNs)) {
+                if (lane == 0) atomicOr(&g_spmm24_status, kStatusMmaTimeout);
+                break;
+            }
+            ptx::tc_fence_after();
+            uint32_t accumulate = 0;
+            for (; u < seg_end; ++u, ++it) {
+                const int s = it % STAGES;
+                const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
+                if (!ptx::mbar_wait_bounded(&full[s], ph, kWaitLimitNs)) {
+                    if (lane == 0) atomicOr(&g_spmm24_status, kStatusMmaTimeout);
+                    ok = false;
+                    break;
+                }
+                if (lane == 0 && u == u_begin) SPMM24_STAMP(2);
+                if (lane == 0 && u == u_end - 1) SPMM24_STAMP(3);
+                ptx::tc_fence_after();
+                if (2 * (int)(u % SPT) + 1 >= p.groups) patch_tail_metadata<C_>(smem + s * C_::STAGE_BYTES, lane);
+                if (lane == 0) {
+                    mma_stage<C_, N_TILE>(smem_base + s * C_::STAGE_BYTES, tmem_base + C_::META_COL + 4 * s,
+                                          tmem_base + (uint32_t)(b * N_TILE), accumulate);
+                    ptx::tc_commit(&empty[s]);
+                }
+                __syncwarp();
+            }
+            if (lane == 0) ptx::tc_commit(&acc_full[b]);
+            __syncwarp();
+        }
+    } else if (warp >= 2) {
+        // ----------------------------------------------------------- epilogue
+        const int quad = warp & 3;
+        const int row = quad * 32 + lane;
+        const int etid = threadIdx.x - 64;
+        const bool vec_ok = (p.N % 8 == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15u) == 0);
+        ptx::grid_dep_wait();  // C and the workspace may be in use by the previous grid
+        int seg = 0;
+        for (long long u = u_begin; u < u_end; ++seg) {
+            const long long tile = u / SPT;
+            const long long tile_begin = tile * SPT, tile_end = tile_begin + SPT;
+            const long long seg_end = min(u_end, tile_end);
+            const int b = seg & 1;
+            const bool publish = u != tile_begin;  // range starts inside the tile: someone else finishes it
+            float acc[N_TILE];
+#pragma unroll
+            for (int e = 0; e < N_TILE; ++e) acc[e] = 0.f;
+            if (!publish && seg_end != tile_end) {
+                // Finisher of a shared tile: the partners (the CTAs after this
+                // one up to the tile's last unit) published their shares at
+                // the start of their ranges.  Collect them now, while this
+                // segment is still streaming.
+                const int c_last = sk_cta_of(tile_end - 1, U, p.grid);
+                if (etid == 0) {
+                    for (int pc = cta + 1; pc <= c_last; ++pc)
+                        if (!ptx::wait_flag_bounded(p.flags + pc, kWaitLimitNs))
+                            atomicOr(&g_spmm24_status, kStatusEpilogueTimeout);
+                }
+                ptx::named_barrier(kBarEpi, kEpiThreads);
+                for (int pc = cta + 1; pc <= c_last; ++pc) {
+                    const float* src = p.ws + ((size_t)pc * kTileM + row) * N_TILE;
+#pragma unroll
+                    for (int e = 0; e < N_TILE; e += 4) {
+                        const float4 x = __ldcg(reinterpret_cast<const float4*>(src + e));
+                        acc[e] += x.x; acc[e + 1] += x.y; acc[e + 2] += x.z; acc[e + 3] += x.w;
+                    }
+                }
+                ptx::named_barrier(kBarEpi, kEpiThreads);
+                if (etid == 0)
+                    for (int pc = cta + 1; pc <= c_last; ++pc) ptx::st_relaxed_gpu(p.flags + pc, 0u);  // ready for the next launch
+            }
+            if (!ptx::mbar_wait_bounded(&acc_full[b], (uint32_t)((seg >> 1) & 1), kWaitLimitNs))
+                atomicOr(&g_spmm24_status, kStatusEpilogueTimeout);
+            if (etid == 0) SPMM24_STAMP(4);
+            ptx::tc_fence_after();
+            __syncwarp();
+            float v[N_TILE];
+#pragma unroll
+            for (int c = 0; c < N_TILE / 16; ++c) {
+                uint32_t r[16];
+                ptx::tmem_ld_32x32b_x16(tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(b * N_TILE + c * 16), r);
+                ptx::tmem_wait_ld();
+#pragma unroll
+                for (int e = 0; e < 16; ++e) v[c * 16 + e] = __uint_as_float(r[e]);
+            }
+            ptx::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) ptx::mbar_arrive(&acc_empty[b]);  // accumulator buffer b may be reused
+
+            if (publish) {
+                float* slot = p.ws + ((size_t)cta * kTileM + row) * N_TILE;
+#pragma unroll
+                for (int e = 0; e < N_TILE; e += 4)
+                    __stcg(reinterpret_cast<float4*>(slot + e), make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]));
+                __threadfence();
+                ptx::named_barrier(kBarEpi, kEpiThreads);
+                if (etid == 0) ptx::st_release_gpu(p.flags + cta, 1u);
+            } else {
+                const int m_tile = (int)(tile / p.n_tiles), n_tile = (int)(tile % p.n_tiles);
+                const int gm = m_tile * kTileM + row;
+                const int n0 = n_tile * N_TILE;
+                if (gm < p.M) {
+#pragma unroll
+                    for (int e = 0; e < N_TILE; ++e) v[e] += acc[e];
+                    __half* out = p.C + (size_t)gm * p.N + n0;
+#pragma unroll
+                    for (int e = 0; e < N_TILE; e += 8)
+                        if (n0 + e < p.N) store_h8(out + e, v + e, vec_ok, p.N - n0 - e);
+                }
+            }
+            u = seg_end;
+        }
+    }
+
+    if (threadIdx.x == 64) SPMM24_STAMP(5);
+    ptx::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        ptx::tc_fence_after();
+        ptx::tmem_dealloc(tmem_base, C_::TMEM_COLS);
+    }
+    if (threadIdx.x == 0) SPMM24_STAMP(6);
 }
 
 }  // namespace spmm24

@@ -31,11 +31,14 @@ _vp = ctypes.c_void_p
 
 class SpmmConfig(ctypes.Structure):
     _fields_ = [(n, ctypes.c_int) for n in
-                ("tile_m", "tile_n", "stage_k", "stages", "split_k", "grid_ctas", "smem_bytes")]
+                ("tile_m", "tile_n", "stage_k", "stages", "split_k", "grid_ctas", "smem_bytes", "stream_k")]
 
 
 _lib.spmm24_launch.argtypes = [_vp, _vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_int]
 _lib.spmm24_launch.restype = ctypes.c_int
+_lib.spmm24_launch_ex.argtypes = [_vp, _vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                  ctypes.c_uint]
+_lib.spmm24_launch_ex.restype = ctypes.c_int
 _lib.spmm24_compress_a.argtypes = [_u16p, ctypes.c_int, ctypes.c_int, _u16p, _u16p]
 _lib.spmm24_compress_a.restype = ctypes.c_int
 _lib.spmm24_compress_reordered.argtypes = [_u16p, ctypes.c_int, ctypes.c_int, _u16p, _u16p]
@@ -57,6 +60,8 @@ _lib.spmm24_version.restype = ctypes.c_char_p
 
 CUDA_SUCCESS = 0
 CUDA_ERROR_INVALID_VALUE = 1
+STATIC_WEIGHTS = 1  # SPMM24_STATIC_WEIGHTS
+NO_PDL = 2          # SPMM24_NO_PDL
 
 
 class SpmmError(RuntimeError):
@@ -97,6 +102,13 @@ def launch(stream, compressed_a, b_packed, metadata, c, M: int, N: int, K: int, 
     """spmm24_launch through the C ABI; returns the cudaError_t code."""
     return _lib.spmm24_launch(_stream_handle(stream), _ptr(compressed_a), _ptr(b_packed), _ptr(metadata), _ptr(c),
                               M, N, K, _ptr(split_reduction), split_k)
+
+
+def launch_ex(stream, compressed_a, b_packed, metadata, c, M: int, N: int, K: int, split_k: int = 0,
+              flags: int = 0) -> int:
+    """spmm24_launch_ex through the C ABI; returns the cudaError_t code."""
+    return _lib.spmm24_launch_ex(_stream_handle(stream), _ptr(compressed_a), _ptr(b_packed), _ptr(metadata), _ptr(c),
+                                 M, N, K, split_k, flags)
 
 
 def SpMM_N2M4_Launch(stream, Compressed_A, B, metadata, C, M_Global: int, N_Global: int, K_Global: int,

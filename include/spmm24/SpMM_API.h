@@ -40,18 +40,43 @@ extern "C" {
 
 /* Launches C = A_sparse * B on `stream`, asynchronously.
  * Replaces SpMM_N2M4_Launch (src/SpMM_API.cu:61-171).
- *   split_k   0 lets the library choose the K split from the shape;
+ *   split_k   0 lets the library choose the decomposition from the shape;
  *             1..8 requests that many K slices (clamped to the number of
- *             128-wide K stages).  Values above 8 are treated as 8.  The
- *             result does not depend on split_k beyond fp32 summation order.
- *   split_reduction  accepted for ABI compatibility and never touched: the
- *             split-K reduction happens on chip, so it may be NULL.
+ *             128-wide K stages).  Values above 8 are treated as 8.  The K
+ *             slices of a tile run as one thread-block cluster and their fp32
+ *             partial sums are reduced on chip.  The result does not depend
+ *             on split_k beyond fp32 summation order, and is bitwise
+ *             reproducible for a fixed split_k on a fixed GPU.
+ *   split_reduction  accepted for ABI compatibility and never touched, so it
+ *             may be NULL.
+ * Memory: this call allocates nothing.  (Only the stream-K tuning path,
+ * selected with the environment variable SPMM24_PATH=2, keeps a workspace of
+ * a few MB per device and stream, allocated on its first use; during CUDA
+ * graph capture it falls back to the default path instead of allocating.)
+ * The kernel is launched with programmatic stream serialization: it may
+ * start its set-up while the previous kernel in the stream finishes, and
+ * waits for that kernel before touching global memory.
  * Returns cudaSuccess, cudaErrorInvalidValue (bad pointer, alignment or
  * shape -- the reference silently did nothing for unsupported N), or the
- * launch error. */
+ * CUDA error of the allocation or launch. */
 cudaError_t spmm24_launch(cudaStream_t stream, const void* compressed_a, const void* b_packed,
                           const uint16_t* metadata, void* c, int M, int N, int K, void* split_reduction,
                           int split_k);
+
+/* Flags of spmm24_launch_ex. */
+enum {
+    /* Nothing earlier in the stream writes A or the metadata: the kernel may
+     * start streaming the weights before the previous kernel has finished
+     * (the activations B are still read only after it). */
+    SPMM24_STATIC_WEIGHTS = 1u,
+    /* Launch without programmatic stream serialization. */
+    SPMM24_NO_PDL = 2u
+};
+
+/* spmm24_launch with flags (no split_reduction argument).  Same contract
+ * otherwise; unknown flag bits give cudaErrorInvalidValue. */
+cudaError_t spmm24_launch_ex(cudaStream_t stream, const void* compressed_a, const void* b_packed,
+                             const uint16_t* metadata, void* c, int M, int N, int K, int split_k, unsigned flags);
 
 /* Caller-allocated form of toolCompressMatrixA (test/utils.h:91-150) with
  * its Block_M = Block_K = 16: dense row-major fp16 (as raw bits) ->
@@ -80,7 +105,8 @@ int spmm24_pack_b(const uint16_t* b_rowmajor, int K, int N, uint16_t* b_packed_o
  * its host prune/compress/metadata pipeline.  Returns 0, or -1 if K % 4. */
 int spmm24_prune_2of4(uint16_t* dense_a, int M, int K);
 
-/* Workspace the caller must pass as split_reduction: always 0 bytes.
+/* Workspace the caller must pass as split_reduction: always 0 bytes (any
+ * workspace is owned by the library, see spmm24_launch).
  * Replaces the Split_K*M*N halves contract of test/kernelTest.cu:136. */
 size_t spmm24_workspace_bytes(int M, int N, int K, int split_k);
 
@@ -92,9 +118,10 @@ typedef struct spmm24_config {
     int tile_n;      /* columns per CTA */
     int stage_k;     /* logical K per pipeline stage (128) */
     int stages;      /* pipeline depth */
-    int split_k;     /* CTAs per cluster along K */
+    int split_k;     /* CTAs per cluster along K (0 on the stream-K path) */
     int grid_ctas;   /* CTAs launched */
     int smem_bytes;  /* dynamic shared memory per CTA */
+    int stream_k;    /* 1: persistent stream-K kernel, 0: cluster kernel */
 } spmm24_config;
 int spmm24_select_config(int M, int N, int K, int split_k, spmm24_config* out);
 

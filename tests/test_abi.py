@@ -81,10 +81,20 @@ def test_launch_rejects_bad_arguments_without_gpu():
 def test_select_config_picks_tiles_and_splits():
     c = spmm24.select_config(4096, 16, 4096)
     assert c["tile_m"] == 128 and c["tile_n"] == 16 and c["stage_k"] == 128
-    assert 1 <= c["split_k"] <= 8 and c["grid_ctas"] == 32 * c["split_k"]
-    assert c["grid_ctas"] <= 148
+    # narrow N with an automatic split: shallow ring (two CTAs per SM) and a
+    # K split that fills both slots of every SM
+    assert c["stream_k"] == 0 and c["stages"] == 4 and c["split_k"] == 8 and c["grid_ctas"] == 256
+    assert spmm24.select_config(11008, 16, 4096)["split_k"] == 3
+    assert spmm24.select_config(256, 16, 128)["split_k"] == 1  # at least two stages per slice
+    # an explicit split is honoured
+    c = spmm24.select_config(4096, 16, 4096, 4)
+    assert c["stream_k"] == 0 and c["split_k"] == 4 and c["grid_ctas"] == 128
+    # wide N keeps the deep ring, one CTA per SM
+    c = spmm24.select_config(4096, 512, 4096)
+    assert c["tile_n"] == 128 and c["stages"] == 4 and c["split_k"] == 1
     # explicit split honoured, clamped to the number of 128-K stages
     assert spmm24.select_config(256, 128, 256, 8)["split_k"] == 2
+    assert spmm24.select_config(256, 16, 4096)["stages"] == 4
     assert spmm24.select_config(256, 128, 4096, 5)["split_k"] == 5
     assert spmm24.select_config(256, 128, 4096, 12)["split_k"] == 8
     assert spmm24.select_config(4096, 1, 4096)["tile_n"] == 16

@@ -16,7 +16,7 @@ def _to_dev(torch, arr, dev):
     return torch.from_numpy(np.ascontiguousarray(arr).view(np.int16)).to(dev)
 
 
-def run_gpu(p, split_k=0, dev=None):
+def run_gpu(p, split_k=0, dev=None, flags=None, stream=None):
     import torch
 
     import spmm24
@@ -25,7 +25,11 @@ def run_gpu(p, split_k=0, dev=None):
     E = _to_dev(torch, p.meta, dev)
     B = _to_dev(torch, p.b_packed, dev)
     C = torch.full((p.M, p.N), float("nan"), dtype=torch.float16, device=dev)
-    rc = spmm24.launch(torch.cuda.current_stream(dev), A, B, E, C, p.M, p.N, p.K, None, split_k)
+    s = stream if stream is not None else torch.cuda.current_stream(dev)
+    if flags is None:
+        rc = spmm24.launch(s, A, B, E, C, p.M, p.N, p.K, None, split_k)
+    else:
+        rc = spmm24.launch_ex(s, A, B, E, C, p.M, p.N, p.K, split_k, flags)
     assert rc == 0, spmm24._lib.spmm24_last_error().decode()
     torch.cuda.synchronize(dev)
     return C.view(torch.int16).cpu().numpy().view(np.uint16)
@@ -71,6 +75,81 @@ def test_shapes_and_splits(cuda_device, shape, split_k):
     M, N, K = shape
     p = make_problem(M, N, K, seed=M + N + K)
     check(p, split_k, cuda_device)
+
+
+@pytest.mark.parametrize("grid", [1, 2, 3, 7, 33, 100, 148, 500])
+@pytest.mark.parametrize("shape", [(256, 16, 1024), (1152, 8, 704), (144, 12, 320), (4096, 32, 4096), (128, 1, 320)])
+def test_stream_k_grids(cuda_device, shape, grid, monkeypatch):
+    """The stream-K path (split_k = 0, narrow N) with forced grid sizes: tiles
+    split across one, two or many CTAs, single-unit tiles, ragged M and N,
+    odd 64-K group counts, and more CTAs requested than units exist."""
+    import spmm24
+
+    M, N, K = shape
+    monkeypatch.setenv("SPMM24_PATH", "2")
+    monkeypatch.setenv("SPMM24_GRID", str(grid))
+    monkeypatch.setenv("SPMM24_STAGES", "8" if grid % 2 else "4")
+    assert spmm24.select_config(M, N, K)["stream_k"] == 1
+    p = make_problem(M, N, K, seed=grid + M)
+    first = check(p, 0, cuda_device)
+    # counters reset themselves: a second launch on the same workspace agrees bitwise
+    assert np.array_equal(first, run_gpu(p, 0, cuda_device))
+
+
+@pytest.mark.parametrize("stages", ["4", "8"])
+@pytest.mark.parametrize("path", ["1", "2"])
+def test_flags_and_streams(cuda_device, monkeypatch, path, stages):
+    """Static-weight prefetch, launches without PDL, and two streams (each gets
+    its own stream-K workspace) all give the same bits, on both kernels."""
+    import torch
+
+    import spmm24
+
+    monkeypatch.setenv("SPMM24_PATH", path)
+    monkeypatch.setenv("SPMM24_STAGES", stages)
+    p = make_problem(2048, 16, 2048, seed=12, a_scale=0.02, b_dist="normal")
+    ref = check(p, 0, cuda_device)
+    assert np.array_equal(ref, run_gpu(p, 0, cuda_device, flags=spmm24.STATIC_WEIGHTS))
+    assert np.array_equal(ref, run_gpu(p, 0, cuda_device, flags=spmm24.NO_PDL))
+    s2 = torch.cuda.Stream(cuda_device)
+    assert np.array_equal(ref, run_gpu(p, 0, cuda_device, stream=s2))
+    assert within_tolerance(compare(run_gpu(p, 4, cuda_device, flags=spmm24.STATIC_WEIGHTS), oracle_c(p)))
+    rc = spmm24.launch_ex(None, 16, 16, 16, 16, 256, 16, 256, 0, 8)
+    assert rc == spmm24.CUDA_ERROR_INVALID_VALUE
+
+
+def test_back_to_back_calls_pdl(cuda_device):
+    """A chain of dependent calls on one stream (each call's output is the
+    next call's activation), launched with programmatic dependent launch."""
+    import torch
+
+    import spmm24
+
+    M = K = 1024
+    N = 16
+    p = make_problem(M, N, K, seed=13, a_scale=0.03, b_dist="normal")
+    A = _to_dev(torch, p.vals, cuda_device)
+    E = _to_dev(torch, p.meta, cuda_device)
+    x = torch.from_numpy(p.b_rowmajor.view(np.float16).reshape(K, N).copy()).to(cuda_device)
+    xs_host = [p.b_rowmajor.copy()]
+    s = torch.cuda.current_stream(cuda_device)
+    bufs = []
+    for step in range(4):
+        Bp = x.reshape(K, N // 8, 8).permute(1, 0, 2).contiguous()  # pack on device (strips of 8 columns)
+        C = torch.empty((M, N), dtype=torch.float16, device=cuda_device)
+        rc = spmm24.launch_ex(s, A, Bp, E, C, M, N, K, 0, spmm24.STATIC_WEIGHTS)
+        assert rc == 0
+        bufs.append((Bp, C))
+        x = C
+    torch.cuda.synchronize(cuda_device)
+    # replay the chain on the CPU oracle
+    b = p.b_rowmajor
+    for step in range(4):
+        ref = O.dense_gemm_f32(p.a_dense, b, M, N, K)
+        got = bufs[step][1].view(torch.int16).cpu().numpy().view(np.uint16).reshape(-1)
+        assert within_tolerance(compare(got, ref)), step
+        b = got  # feed the GPU's fp16 output forward, as the chain did
+        xs_host.append(b)
 
 
 @pytest.mark.parametrize("split_k", [1, 2, 3, 4, 5, 6, 7, 8])
