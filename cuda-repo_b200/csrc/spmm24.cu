@@ -414,6 +414,116 @@ cudaError_t launch_impl(cudaStream_t stream, const void* A, const void* B, const
     }
 }
 
+// ------------------------------------------------ allocation-free variant
+// Scratch for spmm24_launch_noalloc, owned by the library as a file-scope
+// device array instead of a cudaMalloc'ed buffer: 256 flag words followed by
+// room for 256 partial tiles of 128 x 32 fp32 (4 MB + 1 KB in total, held by
+// every GPU that loads the library until the process exits).
+constexpr int kNoAllocMaxCtas = 256;
+constexpr int kNoAllocMaxTileN = 32;
+constexpr size_t kNoAllocFlagBytes = (size_t)kNoAllocMaxCtas * sizeof(uint32_t);  // 1 KB, keeps the partials 256-B aligned
+constexpr size_t kNoAllocPartialBytes = (size_t)kNoAllocMaxCtas * kTileM * kNoAllocMaxTileN * sizeof(float);
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocFlagBytes + kNoAllocPartialBytes];
+
+// Device address of g_noalloc_scratch per device.  In host code the array's
+// name is only a host-side stand-in, so the address is looked up with
+// cudaGetSymbolAddress, once per device, with that device current.
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[kMaxDevices] = {};
+
+cudaError_t noalloc_scratch(int dev, void** out) {
+    if (dev < 0 || dev >= kMaxDevices) return invalid("device index out of range");
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_addr[dev]) {
+        void* p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) return e;
+        if (!p) return cudaErrorInvalidSymbol;
+        g_noalloc_addr[dev] = p;
+    }
+    *out = g_noalloc_addr[dev];
+    return cudaSuccess;
+}
+
+cudaError_t launch_noalloc_impl(cudaStream_t stream, const void* A, const void* B, const uint16_t* E, void* C, int M,
+                                int N, int K) {
+    g_last_error[0] = '\0';
+    if (!A || !B || !E || !C) return invalid("null pointer");
+    if (M <= 0 || N <= 0 || K <= 0) return invalid("M, N and K must be positive");
+    if (M % 16) return invalid("M must be a multiple of 16");
+    if (K % 64) return invalid("K must be a multiple of 64");
+    if (N > kNoAllocMaxTileN)
+        return invalid("spmm24_launch_noalloc supports N <= 32: its fixed scratch holds 256 partial tiles of "
+                       "128 x 32 fp32 (4 MB); use spmm24_launch for wider N");
+    if (((uintptr_t)A | (uintptr_t)B | (uintptr_t)E) & 15u) return invalid("A, B and metadata must be 16-byte aligned");
+    if ((uintptr_t)C & 1u) return invalid("C must be 2-byte aligned");
+    if ((long)M / kTileM >= 65535) return invalid("M too large");
+
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    void* scratch = nullptr;
+    if ((e = noalloc_scratch(dev, &scratch)) != cudaSuccess) return e;
+
+    Plan pl{};
+    pl.path = Path::kStreamK;
+    pl.shallow = false;
+    pl.tile_n = N <= 16 ? 16 : 32;
+    pl.stages = pl.tile_n == 16 ? SV16::kStages : SV32::kStages;
+    pl.smem = pl.tile_n == 16 ? SV16::C_::SMEM_ALLOC : SV32::C_::SMEM_ALLOC;
+    pl.m_tiles = (M + kTileM - 1) / kTileM;
+    pl.n_tiles = 1;
+    pl.stages_total = (K / 64 + 1) / 2;
+    pl.split = 1;
+    const long long units = (long long)pl.m_tiles * pl.stages_total;
+    pl.grid = (int)std::max<long long>(1, std::min<long long>(std::min(sm_count(dev), kNoAllocMaxCtas), units));
+    if ((size_t)pl.grid * kTileM * pl.tile_n * sizeof(float) > kNoAllocPartialBytes ||
+        (size_t)pl.grid * sizeof(uint32_t) > kNoAllocFlagBytes)
+        return invalid("problem needs more scratch than spmm24_launch_noalloc holds");
+
+    uint32_t* flags = static_cast<uint32_t*>(scratch);
+    float* partials = reinterpret_cast<float*>(static_cast<unsigned char*>(scratch) + kNoAllocFlagBytes);
+    // The scratch keeps whatever the previous call left; the flags must start
+    // at zero, so clear the ones this call uses (a memset node, no allocation).
+    if ((e = cudaMemsetAsync(flags, 0, (size_t)pl.grid * sizeof(uint32_t), stream)) != cudaSuccess) return e;
+
+    CUtensorMap ta, tb, te;
+    {
+        cuuint64_t dims[3] = {128, (cuuint64_t)(M / 16), (cuuint64_t)(K / 16)};
+        cuuint64_t str[2] = {(cuuint64_t)16 * K, 256};
+        cuuint32_t box[3] = {128, 8, 8};
+        if (!encode(&ta, 3, A, dims, str, box)) return invalid("TMA descriptor for A could not be encoded");
+    }
+    {
+        cuuint64_t dims[4] = {128, (cuuint64_t)(K / 64), 4, (cuuint64_t)((N + 7) / 8)};
+        cuuint64_t str[3] = {1024, 256, (cuuint64_t)16 * K};
+        cuuint32_t box[4] = {128, 2, 4, (cuuint32_t)(pl.tile_n / 8)};
+        if (!encode(&tb, 4, B, dims, str, box)) return invalid("TMA descriptor for B could not be encoded");
+    }
+    {
+        cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)(M / 16)};
+        cuuint64_t str[1] = {(cuuint64_t)2 * K};
+        cuuint32_t box[2] = {128, 8};
+        if (!encode(&te, 2, E, dims, str, box)) return invalid("TMA descriptor for metadata could not be encoded");
+    }
+    StreamKParams kp;
+    kp.C = static_cast<__half*>(C);
+    kp.ws = partials;
+    kp.flags = flags;
+    kp.M = M;
+    kp.N = N;
+    kp.K = K;
+    kp.groups = K / 64;
+    kp.stages_per_tile = pl.stages_total;
+    kp.m_tiles = pl.m_tiles;
+    kp.n_tiles = pl.n_tiles;
+    kp.units = units;
+    kp.grid = pl.grid;
+    kp.weights_static = 0;
+    if (pl.tile_n == 16) return launch_streamk<SV16>(pl, stream, dev, true, ta, tb, te, kp, 5);
+    return launch_streamk<SV32>(pl, stream, dev, true, ta, tb, te, kp, 6);
+}
+
 }  // namespace
 }  // namespace spmm24
 
@@ -429,6 +539,11 @@ extern "C" cudaError_t spmm24_launch_ex(cudaStream_t stream, const void* compres
                                         const uint16_t* metadata, void* c, int M, int N, int K, int split_k,
                                         unsigned flags) {
     return spmm24::launch_impl(stream, compressed_a, b_packed, metadata, c, M, N, K, split_k, flags);
+}
+
+extern "C" cudaError_t spmm24_launch_noalloc(cudaStream_t stream, const void* compressed_a, const void* b_packed,
+                                             const uint16_t* metadata, void* c, int M, int N, int K) {
+    return spmm24::launch_noalloc_impl(stream, compressed_a, b_packed, metadata, c, M, N, K);
 }
 
 extern "C" size_t spmm24_workspace_bytes(int, int, int, int) { return 0; }

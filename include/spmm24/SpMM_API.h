@@ -78,6 +78,29 @@ enum {
 cudaError_t spmm24_launch_ex(cudaStream_t stream, const void* compressed_a, const void* b_packed,
                              const uint16_t* metadata, void* c, int M, int N, int K, int split_k, unsigned flags);
 
+/* Allocation-free launch (no counterpart in the reference).  For callers
+ * that cannot let a library call cudaMalloc: applications whose device
+ * memory is owned by their own pool or arena (a framework allocator, a
+ * pre-planned serving engine), and latency-critical loops where an
+ * allocation, which can synchronise the device, is not acceptable.
+ * Computes the same C = A_sparse * B as spmm24_launch (same formats and
+ * shape rules, fp32 summation order may differ) with the stream-K kernel,
+ * whose scratch is a fixed array inside the library: 4 MB + 1 KB of device
+ * memory held by every GPU that loads the library, until process exit.
+ *   Limit: N <= 32 (the scratch holds up to 256 partial tiles of 128 x 32
+ *   fp32); wider N returns cudaErrorInvalidValue with the reason in
+ *   spmm24_last_error().
+ *   The first call on a device looks up the scratch array's device address
+ *   (cudaGetSymbolAddress, with that device current); make that first call
+ *   before any stream capture.
+ *   All calls share the one scratch array and every call starts by clearing
+ *   the flag words it uses: calls that overlap on the GPU (different
+ *   streams, or different host threads) race and must be serialised by the
+ *   caller.
+ * Calls no cudaMalloc, cudaFree or allocating library routine. */
+cudaError_t spmm24_launch_noalloc(cudaStream_t stream, const void* compressed_a, const void* b_packed,
+                                  const uint16_t* metadata, void* c, int M, int N, int K);
+
 /* Caller-allocated form of toolCompressMatrixA (test/utils.h:91-150) with
  * its Block_M = Block_K = 16: dense row-major fp16 (as raw bits) ->
  * compressed values (M*K/2) and raw metadata (M*K/16).  Bit-exact with the
