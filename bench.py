@@ -297,8 +297,11 @@ def run_ours(args, rank, world, local_rank):
         peak = peaks["hbm_gbs"]
         unit = "GB/s"
     else:
+        # Dense-equivalent rate against the 2:4 sparse tensor-core ceiling:
+        # the sparse MMA does the same dense-equivalent work at twice the
+        # dense rate, so the ceiling is 2x the measured dense bf16 burst.
         achieved = flops_total_rank / (kernel_us_total * 1e-6) / 1e12
-        peak = peaks["bf16_tflops"]
+        peak = 2.0 * peaks["bf16_tflops"]
         unit = "TFLOP/s"
     traffic = None
     tr = load_traffic(args.workload)
@@ -332,7 +335,7 @@ def run_ours(args, rank, world, local_rank):
         "launch_flags": "SPMM24_STATIC_WEIGHTS" if args.static_weights else "none",
         "roofline": {"bound": wl["bound"], "achieved": round(achieved, 2), "peak": peak, "unit": unit,
                      "frac": round(achieved / peak, 4), "traffic": traffic,
-                     "peak_src": f"{peaks['src']} ({'hbm_gbs copy' if unit == 'GB/s' else 'dense bf16 cuBLAS burst'})",
+                     "peak_src": f"{peaks['src']} ({'hbm_gbs copy' if unit == 'GB/s' else '2 x dense bf16 cuBLAS burst (2:4 sparse rate)'})",
                      "per_launch_us": round(kernel_us_total / nl, 3),
                      "note": "achieved = algorithmic bytes (flops) of the timed region / its CUDA-event duration"},
         "e2e": {"value": round(e2e_value, 4), "unit": "TFLOPS", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,

@@ -79,7 +79,7 @@ int sm_count(int dev) {
 }
 
 // ----------------------------------------------------------- configurations
-enum class Path { kCluster, kStreamK };
+enum class Path { kCluster, kStreamK, kPair };
 
 template <int NT, int ST>
 struct ClusterVariant {
@@ -100,6 +100,8 @@ using CV32 = ClusterVariant<32, 8>;
 using CV64 = ClusterVariant<64, 6>;
 using CV128 = ClusterVariant<128, 4>;
 using CV256 = ClusterVariant<256, 2>;
+constexpr int kPairStages = 4;
+using PairC = PairCfg<kPairStages>;
 using SV16 = StreamKVariant<16, 8>;
 using SV32 = StreamKVariant<32, 8>;
 // Shallow rings (about 92 KB of shared memory): two CTAs fit on one SM, so
@@ -172,6 +174,22 @@ Plan make_plan(int M, int N, int K, int split_k, int sms) {
         const int g = env_int("SPMM24_GRID", sms);
         p.grid = (int)std::max<long long>(1, std::min<long long>(g, units));
         p.split = 1;
+        return p;
+    }
+    // Wide N with K % 128 == 0: a CTA pair per 256 x 256 tile (cta_group::2),
+    // so each SM feeds the tensor core half of B.
+    const int pair_env = env_int("SPMM24_PAIR", -1);  // tuning override: 0 = never, 1 = whenever legal
+    const bool pair_ok = (K % 128 == 0) && (split_k <= 1);
+    if (pair_ok && (pair_env == 1 || (pair_env != 0 && N > 128))) {
+        p.path = Path::kPair;
+        p.shallow = false;
+        p.tile_n = PairC::TILE_N;
+        p.stages = kPairStages;
+        p.smem = PairC::SMEM_ALLOC;
+        p.m_tiles = (M + PairC::TILE_M - 1) / PairC::TILE_M;
+        p.n_tiles = (N + PairC::TILE_N - 1) / PairC::TILE_N;
+        p.split = 1;
+        p.grid = 2 * p.m_tiles * p.n_tiles;
         return p;
     }
     p.path = Path::kCluster;
@@ -303,6 +321,15 @@ cudaError_t launch_streamk(const Plan& pl, cudaStream_t stream, int dev, bool pd
     return launch_kernel(kern, dim3((unsigned)pl.grid, 1, 1), V::C_::SMEM_ALLOC, stream, 1u, pdl, ta, tb, te, kp);
 }
 
+cudaError_t launch_pair(const Plan& pl, cudaStream_t stream, int dev, bool pdl, const CUtensorMap& ta,
+                        const CUtensorMap& tb, const CUtensorMap& te, const PairParams& kp) {
+    auto kern = spmm24_pair_kernel<kPairStages>;
+    cudaError_t e = prepare(kern, PairC::SMEM_ALLOC, dev, 11);
+    if (e != cudaSuccess) return e;
+    return launch_kernel(kern, dim3(2u, (unsigned)pl.n_tiles, (unsigned)pl.m_tiles), PairC::SMEM_ALLOC, stream, 2u, pdl,
+                         ta, tb, te, kp);
+}
+
 size_t streamk_partial_bytes(const Plan& pl) { return (size_t)pl.grid * kTileM * pl.tile_n * sizeof(float); }
 
 cudaError_t launch_impl(cudaStream_t stream, const void* A, const void* B, const uint16_t* E, void* C, int M, int N,
@@ -357,7 +384,8 @@ cudaError_t launch_impl(cudaStream_t stream, const void* A, const void* B, const
     {
         cuuint64_t dims[4] = {128, (cuuint64_t)(K / 64), 4, (cuuint64_t)((N + 7) / 8)};
         cuuint64_t str[3] = {1024, 256, (cuuint64_t)16 * K};
-        cuuint32_t box[4] = {128, 2, 4, (cuuint32_t)(pl.tile_n / 8)};
+        const int cta_n = pl.path == Path::kPair ? PairC::HALF_N : pl.tile_n;  // columns one CTA loads
+        cuuint32_t box[4] = {128, 2, 4, (cuuint32_t)(cta_n / 8)};
         if (!encode(&tb, 4, B, dims, str, box)) return invalid("TMA descriptor for B could not be encoded");
     }
     // E: (K words per band, bands); box two 64-K groups x 8 bands.
@@ -370,6 +398,16 @@ cudaError_t launch_impl(cudaStream_t stream, const void* A, const void* B, const
 
     const bool pdl = !(flags & SPMM24_NO_PDL);
     const int wstatic = (flags & SPMM24_STATIC_WEIGHTS) ? 1 : 0;
+    if (pl.path == Path::kPair) {
+        PairParams kp;
+        kp.C = static_cast<__half*>(C);
+        kp.M = M;
+        kp.N = N;
+        kp.K = K;
+        kp.stages_total = K / 128;
+        kp.weights_static = wstatic;
+        return launch_pair(pl, stream, dev, pdl, ta, tb, te, kp);
+    }
     if (pl.path == Path::kStreamK) {
         StreamKParams kp;
         kp.C = static_cast<__half*>(C);
@@ -555,7 +593,7 @@ extern "C" int spmm24_select_config(int M, int N, int K, int split_k, spmm24_con
     if (sms <= 0) sms = 148;
     cudaGetLastError();
     const spmm24::Plan pl = spmm24::make_plan(M, N, K, split_k, sms);
-    out->tile_m = spmm24::kTileM;
+    out->tile_m = pl.path == spmm24::Path::kPair ? spmm24::PairC::TILE_M : spmm24::kTileM;
     out->tile_n = pl.tile_n;
     out->stage_k = 128;
     out->stages = pl.stages;
@@ -563,6 +601,7 @@ extern "C" int spmm24_select_config(int M, int N, int K, int split_k, spmm24_con
     out->grid_ctas = pl.grid;
     out->smem_bytes = pl.smem;
     out->stream_k = pl.path == spmm24::Path::kStreamK ? 1 : 0;
+    out->cta_pair = pl.path == spmm24::Path::kPair ? 1 : 0;
     return 0;
 }
 

@@ -11,6 +11,11 @@
 //       partial tiles are reduce-scattered through distributed shared memory
 //       (no global workspace, no second launch, fixed summation order).
 //
+//   spmm24_pair_kernel  a CTA pair (cluster of 2) computing one 256 x 256
+//       tile with tcgen05.mma.sp.cta_group::2: each CTA holds 128 rows of A
+//       and 128 columns of B, so each SM feeds the tensor core only half of
+//       B -- the prefill (compute-bound) path.
+//
 //   spmm24_streamk_kernel  a persistent grid (one CTA per SM) in which every
 //       CTA takes an equal share of the (tile, 128-K stage) units, walked
 //       tile-major.  A tile shared by several CTAs is finished by the CTA
@@ -45,6 +50,13 @@ struct ClusterParams {
     int groups;        // K / 64
     int stages_total;  // ceil(groups / 2)
     int split;         // CTAs per cluster along K
+    int weights_static;
+};
+
+struct PairParams {
+    __half* C;
+    int M, N, K;
+    int stages_total;  // K / 128 (the pair kernel requires K % 128 == 0)
     int weights_static;
 };
 
@@ -269,6 +281,203 @@ spmm24_cluster_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_cons
     if (warp == 1) {
         ptx::tc_fence_after();
         ptx::tmem_dealloc(tmem_base, C_::TMEM_COLS);
+    }
+    if (threadIdx.x == 0) SPMM24_STAMP(6);
+}
+
+// -------------------------------------------------------------------------
+template <int STAGES>
+struct PairCfg {
+    static constexpr int HALF_N = 128;                   // columns of B / C per CTA
+    static constexpr int TILE_N = 256;                   // columns per pair
+    static constexpr int TILE_M = 2 * kTileM;            // rows per pair
+    static constexpr int A_BYTES = 8 * 8 * 256;          // this CTA's 128 rows x 128 logical K
+    static constexpr int B_BYTES = (HALF_N / 8) * 2048;  // this CTA's 128 columns x 128 K
+    static constexpr int E_BYTES = 16 * 128;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + E_BYTES;
+    static constexpr int RING_BYTES = STAGES * STAGE_BYTES;
+    static constexpr int BAR_OFFSET = RING_BYTES;
+    static constexpr int NUM_BARS = 2 * STAGES + 1;
+    static constexpr int HOLDER_OFFSET = BAR_OFFSET + NUM_BARS * 8;
+    static constexpr int SMEM_BYTES = HOLDER_OFFSET + 16;
+    static constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;
+    static constexpr int META_COL = TILE_N;  // accumulator: 256 fp32 columns
+    static constexpr int TMEM_COLS = 512;
+    static constexpr int C_PITCH = TILE_N + 8;  // halves per staged output row (bank-shifted)
+    static_assert(META_COL + 4 * STAGES <= TMEM_COLS, "TMEM overflow");
+    static_assert(SMEM_ALLOC <= 232448, "shared memory overflow");
+    static_assert(kTileM * C_PITCH * 2 <= RING_BYTES, "output staging does not fit");
+};
+
+// Instruction descriptor of the pair MMA: sparse, D=f32, A=B=f16, A K-major,
+// B MN-major, M=256, N=256.
+__host__ __device__ constexpr uint32_t pair_idesc() {
+    return (1u << 2) | (1u << 4) | (1u << 16) | ((uint32_t)(256 >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
+}
+
+template <int STAGES>
+__global__ void __launch_bounds__(kThreads, 1)
+spmm24_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmE, const PairParams p) {
+    using C_ = PairCfg<STAGES>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C_::BAR_OFFSET);  // used in the leader only
+    uint64_t* empty = full + STAGES;
+    uint64_t* acc_full = empty + STAGES;
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + C_::HOLDER_OFFSET);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = ptx::cluster_ctarank();  // 0 = leader (issues the MMAs), 1 = peer
+    const bool leader = rank == 0;
+    const int n_tile = blockIdx.y;
+    const int m_tile = blockIdx.z;
+    const int band0 = (m_tile * C_::TILE_M + (int)rank * kTileM) / 16;
+    const int strip0 = (n_tile * C_::TILE_N + (int)rank * C_::HALF_N) / 8;
+    const int st_count = p.stages_total;
+
+    if (threadIdx.x == 0) {
+        SPMM24_STAMP(0);
+        for (int s = 0; s < STAGES; ++s) {
+            ptx::mbar_init(&full[s], 1);
+            ptx::mbar_init(&empty[s], 1);
+        }
+        ptx::mbar_init(acc_full, 1);
+        ptx::fence_mbarrier_init();
+        ptx::prefetch_tmap(&tmA);
+        ptx::prefetch_tmap(&tmB);
+        ptx::prefetch_tmap(&tmE);
+    }
+    if (warp == 1) {
+        ptx::tmem_alloc_pair(tmem_holder, C_::TMEM_COLS);
+        ptx::tmem_relinquish_pair();
+    }
+    ptx::tc_fence_before();
+    ptx::cluster_sync();  // both CTAs: barriers initialised, TMEM allocated
+    ptx::tc_fence_after();
+    const uint32_t tmem_base = *tmem_holder;
+    if (threadIdx.x == 0) ptx::grid_dep_launch();
+
+    if (warp == 0) {
+        // ---------------------------------------------------- TMA producer
+        if (lane == 0) {
+            const uint64_t pol = ptx::policy_evict_last();  // A is re-read by every N tile, B by every M tile
+            // Both CTAs' loads complete on the leader's full barrier.
+            const uint32_t full0 = ptx::mapa_shared(ptx::smem_u32(&full[0]), 0u);
+            const int pre = p.weights_static ? min(STAGES, st_count) : 0;
+            for (int it = 0; it < pre; ++it) {
+                uint8_t* st = smem + it * C_::STAGE_BYTES;
+                if (leader) ptx::mbar_arrive_expect_tx(&full[it], 2 * C_::STAGE_BYTES);
+                ptx::tma_load_3d_pair(st, &tmA, full0 + 8u * it, 0, band0, 8 * it, pol);
+                ptx::tma_load_2d_pair(st + C_::A_BYTES + C_::B_BYTES, &tmE, full0 + 8u * it, 128 * it, band0, pol);
+            }
+            ptx::grid_dep_wait();
+            SPMM24_STAMP(1);
+            for (int it = 0; it < pre; ++it)
+                ptx::tma_load_4d_pair(smem + it * C_::STAGE_BYTES + C_::A_BYTES, &tmB, full0 + 8u * it, 0, 2 * it, 0,
+                                      strip0, pol);
+            for (int it = pre; it < st_count; ++it) {
+                const int s = it % STAGES;
+                const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
+                if (!ptx::mbar_wait_bounded(&empty[s], ph ^ 1u, kWaitLimitNs)) {
+                    atomicOr(&g_spmm24_status, kStatusProducerTimeout);
+                    break;
+                }
+                uint8_t* st = smem + s * C_::STAGE_BYTES;
+                const uint32_t bar = full0 + 8u * s;
+                if (leader) ptx::mbar_arrive_expect_tx(&full[s], 2 * C_::STAGE_BYTES);
+                ptx::tma_load_3d_pair(st, &tmA, bar, 0, band0, 8 * it, pol);
+                ptx::tma_load_2d_pair(st + C_::A_BYTES + C_::B_BYTES, &tmE, bar, 128 * it, band0, pol);
+                ptx::tma_load_4d_pair(st + C_::A_BYTES, &tmB, bar, 0, 2 * it, 0, strip0, pol);
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1 && leader) {
+        // ---------------------------------- MMA issuer (leader CTA only)
+        constexpr uint32_t idesc = pair_idesc();
+        const uint32_t smem_base = ptx::smem_u32(smem);
+        uint32_t accumulate = 0;
+        for (int it = 0; it < st_count; ++it) {
+            const int s = it % STAGES;
+            const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
+            if (!ptx::mbar_wait_bounded(&full[s], ph, kWaitLimitNs)) {
+                if (lane == 0) atomicOr(&g_spmm24_status, kStatusMmaTimeout);
+                break;
+            }
+            if (lane == 0 && it == 0) SPMM24_STAMP(2);
+            if (lane == 0 && it == st_count - 1) SPMM24_STAMP(3);
+            ptx::tc_fence_after();
+            if (lane == 0) {
+                const uint32_t st = smem_base + s * C_::STAGE_BYTES;
+                const uint32_t stB = st + C_::A_BYTES;
+                const uint32_t meta_col = tmem_base + C_::META_COL + 4 * s;
+                ptx::tmem_cp_128x128b_pair(meta_col, smem_desc(stB + C_::B_BYTES, 0, 128));
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const uint64_t adesc = smem_desc(st + j * 2048, 4 * 2048, 128);
+                    const uint64_t bdesc = smem_desc(stB + j * 512, 128, 2048);
+                    ptx::mma_sp_f16_pair(tmem_base, adesc, bdesc, meta_col + (j & 2), idesc | (uint32_t)(j & 1),
+                                         accumulate);
+                    accumulate = 1;
+                }
+                ptx::tc_commit_pair_mc(&empty[s], 0x3);  // frees ring slot s in both CTAs
+            }
+            __syncwarp();
+        }
+        if (lane == 0) ptx::tc_commit_pair_mc(acc_full, 0x3);
+        __syncwarp();
+    } else if (warp >= 2) {
+        // ------------------------------------------- epilogue (both CTAs)
+        if (!ptx::mbar_wait_bounded(acc_full, 0, kWaitLimitNs)) atomicOr(&g_spmm24_status, kStatusEpilogueTimeout);
+        if (threadIdx.x == 64) SPMM24_STAMP(4);
+        ptx::tc_fence_after();
+        __syncwarp();
+        const int quad = warp & 3;
+        const int row = quad * 32 + lane;
+        // Stage the fp16 tile in the (now idle) ring: rows are bank-shifted
+        // by 16 bytes so the per-row writes do not collide.
+        __half* cst = reinterpret_cast<__half*>(smem);
+#pragma unroll 1
+        for (int c = 0; c < C_::TILE_N / 16; ++c) {
+            uint32_t v[16];
+            ptx::tmem_ld_32x32b_x16(tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(c * 16), v);
+            ptx::tmem_wait_ld();
+            __align__(16) __half h[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) h[e] = __float2half_rn(__uint_as_float(v[e]));
+            uint4* dst = reinterpret_cast<uint4*>(cst + (size_t)row * C_::C_PITCH + c * 16);
+            dst[0] = reinterpret_cast<const uint4*>(h)[0];
+            dst[1] = reinterpret_cast<const uint4*>(h)[1];
+        }
+        ptx::tc_fence_before();
+        ptx::named_barrier(kBarEpi, kEpiThreads);
+        ptx::grid_dep_wait();  // C may be in use by the previous grid
+        const int etid = threadIdx.x - 64;
+        const int gm0 = m_tile * C_::TILE_M + (int)rank * kTileM;
+        const int gn = n_tile * C_::TILE_N + lane * 8;
+        const bool vec_ok = (p.N % 8 == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15u) == 0);
+        for (int r = etid >> 5; r < kTileM; r += kEpiThreads / 32) {
+            const int gm = gm0 + r;
+            if (gm >= p.M || gn >= p.N) continue;
+            const __half* src = cst + (size_t)r * C_::C_PITCH + lane * 8;
+            __half* out = p.C + (size_t)gm * p.N + gn;
+            if (vec_ok) {
+                *reinterpret_cast<uint4*>(out) = *reinterpret_cast<const uint4*>(src);
+            } else {
+                const int lim = min(8, p.N - gn);
+                for (int e = 0; e < lim; ++e) out[e] = src[e];
+            }
+        }
+    }
+
+    if (threadIdx.x == 64) SPMM24_STAMP(5);
+    ptx::tc_fence_before();
+    __syncthreads();
+    ptx::cluster_sync();  // neither CTA may leave while the pair still shares shared memory / TMEM
+    if (warp == 1) {
+        ptx::tc_fence_after();
+        ptx::tmem_dealloc_pair(tmem_base, C_::TMEM_COLS);
     }
     if (threadIdx.x == 0) SPMM24_STAMP(6);
 }

@@ -31,7 +31,7 @@ _vp = ctypes.c_void_p
 
 class SpmmConfig(ctypes.Structure):
     _fields_ = [(n, ctypes.c_int) for n in
-                ("tile_m", "tile_n", "stage_k", "stages", "split_k", "grid_ctas", "smem_bytes", "stream_k")]
+                ("tile_m", "tile_n", "stage_k", "stages", "split_k", "grid_ctas", "smem_bytes", "stream_k", "cta_pair")]
 
 
 _lib.spmm24_launch.argtypes = [_vp, _vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_int]

@@ -137,14 +137,15 @@ size_t spmm24_workspace_bytes(int M, int N, int K, int split_k);
  * Replaces the compile-time N switch of src/SpMM_API.cu:128-154 and
  * N2M4TilingConfig (src/TileConfig.h:60-94).  Returns 0 or -1. */
 typedef struct spmm24_config {
-    int tile_m;      /* rows per CTA (128) */
-    int tile_n;      /* columns per CTA */
+    int tile_m;      /* rows per tile (128; 256 for a CTA pair) */
+    int tile_n;      /* columns per tile */
     int stage_k;     /* logical K per pipeline stage (128) */
     int stages;      /* pipeline depth */
     int split_k;     /* CTAs per cluster along K (0 on the stream-K path) */
     int grid_ctas;   /* CTAs launched */
     int smem_bytes;  /* dynamic shared memory per CTA */
     int stream_k;    /* 1: persistent stream-K kernel, 0: cluster kernel */
+    int cta_pair;    /* 1: 256 x 256 tiles on CTA pairs (cta_group::2 MMAs) */
 } spmm24_config;
 int spmm24_select_config(int M, int N, int K, int split_k, spmm24_config* out);
 

@@ -89,16 +89,21 @@ def test_select_config_picks_tiles_and_splits():
     # an explicit split is honoured
     c = spmm24.select_config(4096, 16, 4096, 4)
     assert c["stream_k"] == 0 and c["split_k"] == 4 and c["grid_ctas"] == 128
-    # wide N keeps the deep ring, one CTA per SM
+    # mid N: one CTA per 128 x 128 tile with the deep ring
+    c = spmm24.select_config(4096, 128, 4096)
+    assert c["tile_n"] == 128 and c["stages"] == 4 and c["cta_pair"] == 0
+    # wide N with K % 128 == 0: 256 x 256 tiles on CTA pairs
     c = spmm24.select_config(4096, 512, 4096)
-    assert c["tile_n"] == 128 and c["stages"] == 4 and c["split_k"] == 1
+    assert c["cta_pair"] == 1 and c["tile_m"] == 256 and c["tile_n"] == 256 and c["grid_ctas"] == 64
+    assert spmm24.select_config(4096, 512, 4160)["cta_pair"] == 0  # K % 128 != 0
+    assert spmm24.select_config(4096, 512, 4096, 2)["cta_pair"] == 0  # explicit split-K
     # explicit split honoured, clamped to the number of 128-K stages
     assert spmm24.select_config(256, 128, 256, 8)["split_k"] == 2
     assert spmm24.select_config(256, 16, 4096)["stages"] == 4
     assert spmm24.select_config(256, 128, 4096, 5)["split_k"] == 5
     assert spmm24.select_config(256, 128, 4096, 12)["split_k"] == 8
     assert spmm24.select_config(4096, 1, 4096)["tile_n"] == 16
-    for n, t in ((17, 32), (64, 64), (65, 128), (4096, 128)):
+    for n, t in ((17, 32), (64, 64), (65, 128), (128, 128), (4096, 256)):
         assert spmm24.select_config(1024, n, 1024, 1)["tile_n"] == t
     with pytest.raises(ValueError):
         spmm24.select_config(100, 16, 256)

@@ -152,6 +152,32 @@ def test_back_to_back_calls_pdl(cuda_device):
         xs_host.append(b)
 
 
+@pytest.mark.parametrize("shape", [
+    (256, 256, 128),     # one pair, one stage
+    (512, 512, 512),
+    (272, 264, 384),     # ragged M (one band past a pair tile) and ragged N
+    (4096, 520, 1024),   # several pairs, ragged last N tile
+    (768, 1000, 256),    # N not a multiple of 8: scalar stores
+])
+def test_cta_pair_kernel(cuda_device, shape):
+    """The cta_group::2 pair kernel (256 x 256 tiles, K % 128 == 0)."""
+    import spmm24
+
+    M, N, K = shape
+    assert spmm24.select_config(M, N, K)["cta_pair"] == 1
+    p = make_problem(M, N, K, seed=3 * M + N)
+    check(p, 0, cuda_device)
+
+
+def test_cta_pair_forced_small_n(cuda_device, monkeypatch):
+    """The pair kernel forced on N below its tile (most of B is zero-filled)."""
+    import spmm24
+
+    monkeypatch.setenv("SPMM24_PAIR", "1")
+    assert spmm24.select_config(384, 40, 512)["cta_pair"] == 1
+    check(make_problem(384, 40, 512, seed=9), 0, cuda_device)
+
+
 @pytest.mark.parametrize("split_k", [1, 2, 3, 4, 5, 6, 7, 8])
 def test_llama7b_decode_split_sweep(cuda_device, split_k):
     """BASELINE config 2 shape (M=K=4096, N=16), split_K swept over 1..8."""
