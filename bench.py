@@ -43,6 +43,10 @@ WORKLOADS = {
     # LLaMA-7B prefill
     "prefill": {"shapes": [(M, N, K) for (M, K) in ((4096, 4096), (11008, 4096), (4096, 11008)) for N in (512, 2048, 4096)],
                 "a_std": 0.02, "bound": "tensor"},
+    # LLaMA-70B layers, each layer split along M across the
+    # ranks (strong scaling; no reduction; optional all-gather of C)
+    "70b": {"shapes": [(M, N, K) for (M, K) in ((8192, 8192), (28672, 8192), (8192, 28672)) for N in (16, 256, 4096)],
+            "a_std": 0.01, "bound": "tensor", "shard": True},
     # square sweep (up to 8192)
     "square": {"shapes": [(s, s, s) for s in (1024, 2048, 4096, 8192)], "a_std": None, "bound": "tensor"},
 }
@@ -178,9 +182,14 @@ def run_ours(args, rank, world, local_rank):
     wl = WORKLOADS[args.workload]
     shapes = wl["shapes"]
     square = args.workload == "square"
+    shard = bool(wl.get("shard"))
+    # With sharding every rank holds rows [r0, r1) of each layer (generated
+    # for that range directly); otherwise every rank runs whole layers.
+    rows = {M: (spmm24.shard_rows(M, world, rank, 128) if shard else (0, M)) for (M, N, K) in shapes}
     layers = {}
     for i, (M, K) in enumerate(sorted({(M, K) for (M, N, K) in shapes})):
-        a_np, vals, meta = make_layer(torch, spmm24, M, K, wl["a_std"], seed=1000 * rank + i, mask_random=square)
+        r0, r1 = rows[M]
+        a_np, vals, meta = make_layer(torch, spmm24, r1 - r0, K, wl["a_std"], seed=1000 * rank + i, mask_random=square)
         layers[(M, K)] = (a_np, vals, meta)
     acts = {}
     for j, (K, N) in enumerate(sorted({(K, N) for (M, N, K) in shapes})):
@@ -195,9 +204,10 @@ def run_ours(args, rank, world, local_rank):
         A = to_dev(torch, vals, dev)
         E = to_dev(torch, meta, dev)
         B = to_dev(torch, bp, dev)
-        C = torch.empty((M, N), dtype=torch.float16, device=dev)
-        calls.append({"M": M, "N": N, "K": K, "A": A, "E": E, "B": B, "C": C,
-                      "split": spmm24.select_config(M, N, K, 0)["split_k"]})
+        r0, r1 = rows[M]
+        C = torch.empty((r1 - r0, N), dtype=torch.float16, device=dev)
+        calls.append({"M": r1 - r0, "N": N, "K": K, "A": A, "E": E, "B": B, "C": C, "M_full": M,
+                      "split": spmm24.select_config(max(16, r1 - r0), N, K, 0)["split_k"]})
     weight_bytes = sum(c["A"].numel() * 2 + c["E"].numel() * 2 for c in calls)
     stream = torch.cuda.current_stream(dev)
     h_stream = int(stream.cuda_stream)
@@ -283,7 +293,11 @@ def run_ours(args, rank, world, local_rank):
         elapsed_ms, e2e_ms = float(t[0]), float(t[1])
 
     step_flops = sum(flops(c["M"], c["N"], c["K"]) for c in calls)
-    total_flops = step_flops * args.steps * world
+    if shard:
+        # strong scaling: the job is the unsharded layers, whatever the ranks
+        total_flops = sum(flops(c["M_full"], c["N"], c["K"]) for c in calls) * args.steps
+    else:
+        total_flops = step_flops * args.steps * world
     value = total_flops / (elapsed_ms * 1e-3) / 1e12
     e2e_value = total_flops / (e2e_ms * 1e-3) / 1e12
 
@@ -320,16 +334,17 @@ def run_ours(args, rank, world, local_rank):
         "ms_per_step": round(elapsed_ms / args.steps, 5),
         "us_per_spmm": round(elapsed_ms * 1e3 / args.steps / len(calls), 3),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if shard else "weak",
         "vs_baseline": None,
         "dtype": "f16 in, f32 accumulate, f16 out",
-        "data": "synthetic (seeded torch RNG; A N(0,0.02) magnitude-pruned 2:4, B N(0,1))" if wl["a_std"]
+        "data": f"synthetic (seeded torch RNG; A N(0,{wl['a_std']}) magnitude-pruned 2:4, B N(0,1))" if wl["a_std"]
                 else "synthetic (U(-1,1), random 2:4 mask)",
         "config": {"workload": f"{args.workload}: " + ", ".join(f"{M}x{N}x{K}" for (M, N, K) in shapes),
-                   "baseline_config": {"decode": 2, "prefill": 3, "square": 5}[args.workload],
+                   "baseline_config": {"decode": 2, "prefill": 3, "70b": 4, "square": 5}[args.workload],
                    "spmm_per_step": len(calls), "split_k": "auto (library picker)",
                    "l2": f"inputs larger than L2: {weight_bytes / 1e6:.0f} MB of distinct weights per step",
-                   "parallelism": f"replicas x{world} (each rank its own layers)"},
+                   "parallelism": (f"M-sharded x{world} (rows split by spmm24_shard_rows, no reduction)" if shard
+                                   else f"replicas x{world} (each rank its own layers)")},
         "per_shape_us": {f"{c['M']}x{c['N']}x{c['K']}": round(u, 3) for c, u in zip(calls, per_call)},
         "per_shape_note": "median single-kernel duration with an event pair around each launch",
         "launch_flags": "SPMM24_STATIC_WEIGHTS" if args.static_weights else "none",
@@ -344,6 +359,36 @@ def run_ours(args, rank, world, local_rank):
         "gpu_launches": nl,
         "clocks": clocks,
     }
+
+    if shard and args.allgather and world > 1:
+        # NCCL all-gather of the C shards (contiguous row ranges) into the full
+        # C on every rank, timed on its own, max over ranks.
+        fulls = [torch.empty((c["M_full"], c["N"]), dtype=torch.float16, device=dev) for c in calls]
+        equal = all(c["M_full"] % world == 0 and c["M"] * world == c["M_full"] for c in calls)
+        def gather():
+            for c, f in zip(calls, fulls):
+                if equal:
+                    dist.all_gather_into_tensor(f, c["C"])
+                else:
+                    dist.all_gather(list(f.split([spmm24.shard_rows(c["M_full"], world, i, 128)[1] -
+                                                  spmm24.shard_rows(c["M_full"], world, i, 128)[0]
+                                                  for i in range(world)])), c["C"])
+        for _ in range(args.warmup):
+            gather()
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record(stream)
+        for _ in range(args.steps):
+            gather()
+        g1.record(stream)
+        torch.cuda.synchronize(dev)
+        gt = torch.tensor([g0.elapsed_time(g1)], device=dev, dtype=torch.float64)
+        dist.all_reduce(gt, op=dist.ReduceOp.MAX)
+        gbytes = sum(2 * c["M_full"] * c["N"] for c in calls)
+        out["allgather"] = {"us_per_step": round(float(gt[0]) * 1e3 / args.steps, 2), "bytes_per_step": gbytes,
+                            "busbw_GBps": round(gbytes * (world - 1) / world / (float(gt[0]) * 1e-3 / args.steps) / 1e9, 1),
+                            "op": "NCCL all_gather_into_tensor of the C shards"}
 
     if args.comparators and rank == 0:
         out["comparators"] = run_comparators(torch, spmm24, calls, layers, acts, dev, args)
@@ -427,6 +472,15 @@ def run_comparators(torch, spmm24, calls, layers, acts, dev, args):
     return res
 
 
+def host_threads():
+    """All host cores this process may run on (torchrun sets OMP_NUM_THREADS=1,
+    which must not throttle the CPU baseline)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
 def cpu_baseline(layers, acts, shapes, budget_s=10.0):
     """The oracle's OpenMP dense GEMM (fp16 -> fp32, fp32 accumulate) on the
     pruned A, on a row sample of every shape of the workload."""
@@ -435,7 +489,7 @@ def cpu_baseline(layers, acts, shapes, budget_s=10.0):
     sys.path.insert(0, os.path.join(REPO, "oracle"))
     import oracle as O
 
-    threads = O.max_threads()
+    threads = host_threads()
     # estimate: 64 rows of every shape
     probe_rows = 64
     t = time.perf_counter()
@@ -478,7 +532,7 @@ def run_reference(args, rank, world):
     acts = {}
     for j, (K, N) in enumerate(sorted({(K, N) for (M, N, K) in shapes})):
         acts[(K, N)] = make_activations(torch, spmm24, K, N, seed=5000 + j, uniform=square)
-    threads = O.max_threads()
+    threads = host_threads()
 
     def step(rows):
         fl = 0.0
@@ -509,7 +563,7 @@ def run_reference(args, rank, world):
         "ms_per_step": round(dt * 1e3 / args.steps, 3), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f16 in, f32 accumulate, f16 out", "data": "synthetic",
         "config": {"workload": f"{args.workload}: " + ", ".join(f"{M}x{N}x{K}" for (M, N, K) in shapes),
-                   "baseline_config": {"decode": 2, "prefill": 3, "square": 5}[args.workload]},
+                   "baseline_config": {"decode": 2, "prefill": 3, "70b": 4, "square": 5}[args.workload]},
         "cpu_baseline": {"value": round(value, 6), "unit": "TFLOPS", "cores": threads, "kind": "port",
                          "sample": sample},
         "e2e": {"value": round(value, 6), "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -551,6 +605,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="decode")
     ap.add_argument("--comparators", action="store_true")
+    ap.add_argument("--allgather", action="store_true", help="70b workload: also time the NCCL all-gather of C")
     ap.add_argument("--no-static-weights", dest="static_weights", action="store_false",
                     help="launch without SPMM24_STATIC_WEIGHTS (no kernel in the step writes the weights)")
     ap.add_argument("--no-cpu-baseline", action="store_true")

@@ -202,3 +202,20 @@ void toolPackMatrixB(half* MatrixB, int Global_K, int Global_N, int Block_K, int
     spmm24_pack_b(reinterpret_cast<const uint16_t*>(MatrixB), Global_K, Global_N, o);
     *packMatrixB = reinterpret_cast<half*>(o);
 }
+
+extern "C" int spmm24_shard_rows(int M, int parts, int index, int align, int* row_begin, int* row_end) {
+    if (!row_begin || !row_end || M <= 0 || M % 16 || parts <= 0 || index < 0 || index >= parts || align <= 0 ||
+        align % 16)
+        return -1;
+    // Whole `align`-row units, spread as evenly as possible.  The final unit
+    // may be partial (M need only be a multiple of 16), so the shards that
+    // take one unit more are the last ones, the partial unit among them.
+    const long long units = ((long long)M + align - 1) / align;
+    const long long base = units / parts, rem = units % parts;
+    const long long first_big = parts - rem;  // shards [first_big, parts) get base + 1 units
+    const long long u0 = index * base + std::max<long long>(0, index - first_big);
+    const long long u1 = u0 + base + (index >= first_big ? 1 : 0);
+    *row_begin = (int)std::min<long long>(u0 * align, M);
+    *row_end = (int)std::min<long long>(u1 * align, M);
+    return 0;
+}

@@ -309,6 +309,8 @@ struct PairCfg {
     static_assert(kTileM * C_PITCH * 2 <= RING_BYTES, "output staging does not fit");
 };
 
+constexpr int kPairGroupM = 8;  // tile rows per rasterisation group
+
 // Instruction descriptor of the pair MMA: sparse, D=f32, A=B=f16, A K-major,
 // B MN-major, M=256, N=256.
 __host__ __device__ constexpr uint32_t pair_idesc() {
@@ -331,8 +333,20 @@ spmm24_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
     const int lane = threadIdx.x & 31;
     const uint32_t rank = ptx::cluster_ctarank();  // 0 = leader (issues the MMAs), 1 = peer
     const bool leader = rank == 0;
-    const int n_tile = blockIdx.y;
-    const int m_tile = blockIdx.z;
+    // Grouped rasterisation: consecutive pairs walk down a group of
+    // kPairGroupM tile rows before moving to the next tile column, so the A
+    // and B panels of one wave of pairs stay in L2.
+    int m_tile, n_tile;
+    {
+        const int pid = blockIdx.y + gridDim.y * blockIdx.z;  // pairs in launch order
+        const int n_tiles = gridDim.y, m_tiles = gridDim.z;
+        const int per_group = kPairGroupM * n_tiles;
+        const int first_m = (pid / per_group) * kPairGroupM;
+        const int group_m = min(m_tiles - first_m, kPairGroupM);
+        const int in_group = pid % per_group;
+        m_tile = first_m + in_group % group_m;
+        n_tile = in_group / group_m;
+    }
     const int band0 = (m_tile * C_::TILE_M + (int)rank * kTileM) / 16;
     const int strip0 = (n_tile * C_::TILE_N + (int)rank * C_::HALF_N) / 8;
     const int st_count = p.stages_total;

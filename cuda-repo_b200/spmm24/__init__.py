@@ -55,6 +55,8 @@ _lib.spmm24_select_config.argtypes = [ctypes.c_int] * 4 + [ctypes.POINTER(SpmmCo
 _lib.spmm24_select_config.restype = ctypes.c_int
 _lib.spmm24_device_status.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_uint32)]
 _lib.spmm24_device_status.restype = ctypes.c_int
+_lib.spmm24_shard_rows.argtypes = [ctypes.c_int] * 4 + [ctypes.POINTER(ctypes.c_int)] * 2
+_lib.spmm24_shard_rows.restype = ctypes.c_int
 _lib.spmm24_last_error.restype = ctypes.c_char_p
 _lib.spmm24_version.restype = ctypes.c_char_p
 
@@ -151,6 +153,25 @@ def device_status(device: int = 0) -> int:
     if rc != CUDA_SUCCESS:
         raise SpmmError(rc, "spmm24_device_status")
     return int(v.value)
+
+
+# ---------------------------------------------------------- sharding
+def shard_rows(M: int, parts: int, index: int, align: int = 128) -> tuple[int, int]:
+    """[row_begin, row_end) of shard `index` of `parts` (split along M)."""
+    b, e = ctypes.c_int(), ctypes.c_int()
+    if _lib.spmm24_shard_rows(M, parts, index, align, ctypes.byref(b), ctypes.byref(e)) != 0:
+        raise ValueError("shard_rows: bad arguments")
+    return b.value, e.value
+
+
+def shard_views(compressed_a, metadata, M: int, K: int, row_begin: int, row_end: int):
+    """The contiguous slices of compressed A and metadata holding rows
+    [row_begin, row_end) -- works for numpy arrays and torch tensors."""
+    if row_begin % 16 or row_end % 16 or not 0 <= row_begin <= row_end <= M:
+        raise ValueError("shard rows must be multiples of 16 inside [0, M]")
+    a = compressed_a.reshape(-1)[row_begin * K // 2: row_end * K // 2]
+    e = metadata.reshape(-1)[row_begin * K // 16: row_end * K // 16]
+    return a, e
 
 
 # -------------------------------------------------------------- packer

@@ -149,6 +149,17 @@ typedef struct spmm24_config {
 } spmm24_config;
 int spmm24_select_config(int M, int N, int K, int split_k, spmm24_config* out);
 
+/* Row range of shard `index` of `parts` when an M x K layer is split along
+ * M across devices (no reduction needed: each shard is a contiguous slice
+ * of the compressed A, of the metadata and of the rows of C).  Boundaries
+ * are multiples of `align` rows (align a positive multiple of 16; 128
+ * keeps whole 128-row tiles on one device); the last shard takes the
+ * remainder.  Element offsets of the shard: compressed A row_begin*K/2,
+ * metadata row_begin*K/16, C row_begin*N.  The reference runs on one GPU
+ * only (test/build/kernelTest.sh:37); this is the partition its multi-GPU
+ * use needs.  Returns 0, or -1 for bad arguments. */
+int spmm24_shard_rows(int M, int parts, int index, int align, int* row_begin, int* row_end);
+
 /* Reads and clears this process's sticky device status word on `device`
  * (0 = no kernel gave up a bounded wait).  Synchronises the device. */
 cudaError_t spmm24_device_status(int device, uint32_t* status_out);

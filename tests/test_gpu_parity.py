@@ -178,6 +178,28 @@ def test_cta_pair_forced_small_n(cuda_device, monkeypatch):
     check(make_problem(384, 40, 512, seed=9), 0, cuda_device)
 
 
+@pytest.mark.parametrize("parts", [2, 4, 8])
+def test_m_shards_reproduce_full_launch(cuda_device, parts):
+    """Launching every M-shard (shard views of A / metadata, rows of C) gives
+    the unsharded result bit for bit -- the multi-GPU partition, on one GPU."""
+    import torch
+
+    import spmm24
+
+    M, N, K = 2048, 32, 1024
+    p = make_problem(M, N, K, seed=parts)
+    A, E, B = _to_dev(torch, p.vals, cuda_device), _to_dev(torch, p.meta, cuda_device), _to_dev(torch, p.b_packed, cuda_device)
+    full = torch.empty((M, N), dtype=torch.float16, device=cuda_device)
+    assert spmm24.launch(None, A, B, E, full, M, N, K, None, 1) == 0
+    sharded = torch.full((M, N), float("nan"), dtype=torch.float16, device=cuda_device)
+    for i in range(parts):
+        r0, r1 = spmm24.shard_rows(M, parts, i, 128)
+        a, e = spmm24.shard_views(A, E, M, K, r0, r1)
+        assert spmm24.launch(None, a, B, e, sharded[r0:r1], r1 - r0, N, K, None, 1) == 0
+    torch.cuda.synchronize(cuda_device)
+    assert torch.equal(full.view(torch.int16), sharded.view(torch.int16))
+
+
 @pytest.mark.parametrize("split_k", [1, 2, 3, 4, 5, 6, 7, 8])
 def test_llama7b_decode_split_sweep(cuda_device, split_k):
     """BASELINE config 2 shape (M=K=4096, N=16), split_K swept over 1..8."""
