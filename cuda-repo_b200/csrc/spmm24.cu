@@ -562,6 +562,29 @@ cudaError_t launch_noalloc_impl(cudaStream_t stream, const void* A, const void* 
     return launch_streamk<SV32>(pl, stream, dev, true, ta, tb, te, kp, 6);
 }
 
+// ------------------------------------------------------ bounded-wait self test
+// A flag and an mbarrier that nothing ever completes: the self test waits on
+// one of them with a short limit and must come back with a timeout status,
+// leaving the context usable.  Failure detection is thereby tested without
+// faulting, trapping or hanging the GPU.
+static __device__ uint32_t g_selftest_flag;  // stays 0
+static __device__ uint32_t g_selftest_result;
+
+__global__ void spmm24_selftest_kernel(int which, unsigned long long limit_ns) {
+    __shared__ uint64_t bar;
+    uint32_t status = 0;
+    if (threadIdx.x == 0) {
+        if (which == 0) {
+            ptx::mbar_init(&bar, 1);  // expects one arrival that never comes
+            ptx::fence_mbarrier_init();
+            if (!ptx::mbar_wait_bounded(&bar, 0, limit_ns)) status = kStatusMmaTimeout;
+        } else {
+            if (!ptx::wait_flag_bounded(&g_selftest_flag, limit_ns)) status = kStatusEpilogueTimeout;
+        }
+        g_selftest_result = status;
+    }
+}
+
 }  // namespace
 }  // namespace spmm24
 
@@ -616,6 +639,18 @@ extern "C" cudaError_t spmm24_device_status(int device, uint32_t* status_out) {
     if (e == cudaSuccess) e = cudaMemcpyFromSymbol(&v, spmm24::g_spmm24_status, sizeof(v));
     if (e == cudaSuccess) e = cudaMemcpyToSymbol(spmm24::g_spmm24_status, &zero, sizeof(zero));
     cudaSetDevice(prev);
+    *status_out = v;
+    return e;
+}
+
+extern "C" cudaError_t spmm24_selftest_bounded_wait(int which, unsigned limit_us, uint32_t* status_out) {
+    if (!status_out || (which != 0 && which != 1) || limit_us == 0 || limit_us > 10000000u)
+        return cudaErrorInvalidValue;
+    spmm24::spmm24_selftest_kernel<<<1, 32>>>(which, (unsigned long long)limit_us * 1000ull);
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    uint32_t v = 0;
+    if (e == cudaSuccess) e = cudaMemcpyFromSymbol(&v, spmm24::g_selftest_result, sizeof(v));
     *status_out = v;
     return e;
 }

@@ -164,6 +164,15 @@ int spmm24_shard_rows(int M, int parts, int index, int align, int* row_begin, in
  * (0 = no kernel gave up a bounded wait).  Synchronises the device. */
 cudaError_t spmm24_device_status(int device, uint32_t* status_out);
 
+/* Self test of the failure detection: runs a one-block kernel that waits,
+ * with the library's bounded wait and a limit of `limit_us` microseconds,
+ * on an mbarrier (which = 0) or a global flag (which = 1) that nothing ever
+ * completes, then reports the status the kernel recorded (non-zero: the wait
+ * gave up as designed) and whether the device is still usable.  Nothing
+ * faults, traps or hangs.  The reference has no failure detection
+ * (checkLastCudaError, test/utils.h:21-28, only exits the process). */
+cudaError_t spmm24_selftest_bounded_wait(int which, unsigned limit_us, uint32_t* status_out);
+
 /* Human-readable reason for the last cudaErrorInvalidValue returned on the
  * calling thread ("" if none). */
 const char* spmm24_last_error(void);
