@@ -312,6 +312,16 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t local_smem_addr, uint32
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_smem_addr), "r"(rank));
     return r;
 }
+// Asynchronous 16-byte store into another CTA's shared memory; completion is
+// counted (16 bytes of complete_tx) on the mbarrier `mbar_cluster` of that CTA.
+__device__ __forceinline__ void st_async_v4(uint32_t cluster_addr, float a, float b, float c, float d,
+                                            uint32_t mbar_cluster) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+                     cluster_addr),
+                 "f"(a), "f"(b), "f"(c), "f"(d), "r"(mbar_cluster)
+                 : "memory");
+}
+
 __device__ __forceinline__ void st_cluster_v4(uint32_t cluster_addr, float a, float b, float c, float d) {
     asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(cluster_addr), "f"(a), "f"(b), "f"(c),
                  "f"(d)

@@ -96,7 +96,7 @@ struct StreamKVariant {
 
 // One configuration per N tile: the deepest ring that fits in 227 KB.
 using CV16 = ClusterVariant<16, 8>;
-using CV32 = ClusterVariant<32, 8>;
+using CV32 = ClusterVariant<32, 7>;
 using CV64 = ClusterVariant<64, 6>;
 using CV128 = ClusterVariant<128, 4>;
 using CV256 = ClusterVariant<256, 2>;
@@ -107,7 +107,7 @@ using SV32 = StreamKVariant<32, 8>;
 // Shallow rings (about 92 KB of shared memory): two CTAs fit on one SM, so
 // consecutive launches overlap on the same SM under programmatic launch.
 using CV16s = ClusterVariant<16, 4>;
-using CV32s = ClusterVariant<32, 4>;
+using CV32s = ClusterVariant<32, 3>;
 using SV16s = StreamKVariant<16, 4>;
 using SV32s = StreamKVariant<32, 4>;
 

@@ -77,15 +77,21 @@ struct StreamKParams {
 template <int N_TILE, int STAGES>
 struct ClusterCfg : Cfg<N_TILE, STAGES, 1> {
     using B_ = Cfg<N_TILE, STAGES, 1>;
-    static constexpr int BAR_OFFSET = B_::RING_BYTES;
-    static constexpr int NUM_BARS = 2 * STAGES + 1;
+    static constexpr int RED_PITCH = N_TILE + 4;  // floats per row of the reduction buffer
+    static constexpr int RED_ROWS = 136;          // >= S * ceil(128 / S) for every S <= 8
+    // Narrow tiles get a dedicated receive buffer, so partial rows can be
+    // pushed to their owner with st.async as soon as the sender is done; wide
+    // tiles reuse the idle stage ring behind two cluster barriers.
+    static constexpr bool RECV_BUF = N_TILE <= 32;
+    static constexpr int RECV_OFFSET = B_::RING_BYTES;
+    static constexpr int RECV_BYTES = RECV_BUF ? RED_ROWS * RED_PITCH * 4 : 0;
+    static constexpr int BAR_OFFSET = RECV_OFFSET + RECV_BYTES;
+    static constexpr int NUM_BARS = 2 * STAGES + 2;  // full, empty, acc_full, recv
     static constexpr int HOLDER_OFFSET = BAR_OFFSET + NUM_BARS * 8;
     static constexpr int SMEM_BYTES = HOLDER_OFFSET + 16;
     static constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;  // slack to align the base to 1024 B
-    static constexpr int RED_PITCH = N_TILE + 4;         // floats per row of the reduction buffer
     static_assert(SMEM_ALLOC <= 232448, "shared memory overflow");
-    // The reduction buffer reuses the stage ring: S sources x ceil(128/S) rows.
-    static_assert((kTileM + 7) * RED_PITCH * 4 <= B_::RING_BYTES, "reduction buffer does not fit");
+    static_assert(RECV_BUF || RED_ROWS * RED_PITCH * 4 <= B_::RING_BYTES, "reduction buffer does not fit");
 };
 
 template <int N_TILE, int STAGES>
@@ -98,12 +104,16 @@ spmm24_cluster_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_cons
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + C_::BAR_OFFSET);
     uint64_t* empty = full + STAGES;
     uint64_t* acc_full = empty + STAGES;
+    uint64_t* recv_bar = acc_full + 1;
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + C_::HOLDER_OFFSET);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int S = p.split;
     const int rank = (S > 1) ? (int)ptx::cluster_ctarank() : 0;
+    const int rows_per = (kTileM + S - 1) / S;
+    const int my_start = (kTileM * rank + S - 1) / S;
+    const int my_end = (kTileM * (rank + 1) + S - 1) / S;
     const int n_tile = blockIdx.y;
     const int m_tile = blockIdx.z;
     const int band0 = m_tile * (kTileM / 16);
@@ -121,12 +131,20 @@ spmm24_cluster_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_cons
             ptx::mbar_init(&empty[s], 1);
         }
         ptx::mbar_init(acc_full, 1);
+        ptx::mbar_init(recv_bar, 1);
+        if (C_::RECV_BUF && S > 1)  // the other S-1 CTAs' partial rows of this CTA's slice
+            ptx::mbar_arrive_expect_tx(recv_bar, (uint32_t)((S - 1) * (my_end - my_start) * N_TILE * 4));
         ptx::fence_mbarrier_init();
         ptx::prefetch_tmap(&tmA);
         ptx::prefetch_tmap(&tmB);
         ptx::prefetch_tmap(&tmE);
     }
     __syncthreads();
+    // With a receive buffer, partial rows may arrive from the other CTAs of
+    // the cluster at any time from here on, so every CTA's barriers must be
+    // initialised first (the CTAs of a cluster start together: this costs one
+    // barrier round trip, spent while the previous grid is still finishing).
+    if (C_::RECV_BUF && S > 1) ptx::cluster_sync();
     if (threadIdx.x == 0) ptx::grid_dep_launch();
 
     uint32_t tmem_base = 0;
@@ -198,17 +216,18 @@ spmm24_cluster_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_cons
     }
 
     // ----------------------------------------------------------- epilogue
-    // Reduction buffer red[src][row][RED_PITCH] (fp32) reuses the stage ring.
-    const int rows_per = (kTileM + S - 1) / S;
-    float* red = reinterpret_cast<float*>(smem);
+    // Reduction buffer red[src][row][RED_PITCH] (fp32): the dedicated receive
+    // buffer for narrow tiles, else the stage ring once it is idle.
+    float* red = reinterpret_cast<float*>(smem + (C_::RECV_BUF ? C_::RECV_OFFSET : 0));
     const bool epi = warp >= 2;
+    const bool push = C_::RECV_BUF && S > 1;  // st.async to the owners, no cluster barriers
     if (epi) {
         if (!ptx::mbar_wait_bounded(acc_full, 0, kWaitLimitNs)) atomicOr(&g_spmm24_status, kStatusEpilogueTimeout);
         if (threadIdx.x == 64) SPMM24_STAMP(4);
         ptx::tc_fence_after();
     }
     __syncwarp();
-    if (S > 1) ptx::cluster_sync();  // every CTA's accumulator is final and its ring is idle
+    if (S > 1 && !push) ptx::cluster_sync();  // every CTA's accumulator is final and its ring is idle
     if (epi) {
         const int quad = warp & 3;  // TMEM lane quadrant this warp may access
         const int row = quad * 32 + lane;
@@ -217,7 +236,9 @@ spmm24_cluster_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_cons
         const int lr = row - owner_start;
         float* dst_row = red + ((size_t)rank * rows_per + lr) * C_::RED_PITCH;
         const uint32_t dst_local = ptx::smem_u32(dst_row);
-        const uint32_t dst = (S > 1) ? ptx::mapa_shared(dst_local, (uint32_t)owner) : dst_local;
+        const bool remote = S > 1 && owner != rank;
+        const uint32_t dst = remote ? ptx::mapa_shared(dst_local, (uint32_t)owner) : dst_local;
+        const uint32_t dst_bar = remote ? ptx::mapa_shared(ptx::smem_u32(recv_bar), (uint32_t)owner) : 0u;
 #pragma unroll 1
         for (int c = 0; c < N_TILE / 16; ++c) {
             uint32_t v[16];
@@ -225,31 +246,31 @@ spmm24_cluster_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_cons
             ptx::tmem_wait_ld();
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-                if (S > 1) {
-                    ptx::st_cluster_v4(dst + (uint32_t)((c * 16 + q * 4) * 4), __uint_as_float(v[4 * q]),
-                                       __uint_as_float(v[4 * q + 1]), __uint_as_float(v[4 * q + 2]),
-                                       __uint_as_float(v[4 * q + 3]));
+                const float a = __uint_as_float(v[4 * q]), b = __uint_as_float(v[4 * q + 1]);
+                const float cc = __uint_as_float(v[4 * q + 2]), d = __uint_as_float(v[4 * q + 3]);
+                if (remote && push) {
+                    ptx::st_async_v4(dst + (uint32_t)((c * 16 + q * 4) * 4), a, b, cc, d, dst_bar);
+                } else if (remote) {
+                    ptx::st_cluster_v4(dst + (uint32_t)((c * 16 + q * 4) * 4), a, b, cc, d);
                 } else {
-                    *reinterpret_cast<float4*>(dst_row + c * 16 + q * 4) =
-                        make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
-                                    __uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3]));
+                    *reinterpret_cast<float4*>(dst_row + c * 16 + q * 4) = make_float4(a, b, cc, d);
                 }
             }
         }
         ptx::tc_fence_before();
     }
     __syncwarp();
-    if (S > 1) {
+    if (S > 1 && !push) {
         ptx::cluster_sync();  // all partial rows delivered to their owners
     } else if (epi) {
-        ptx::named_barrier(kBarEpi, kEpiThreads);
+        ptx::named_barrier(kBarEpi, kEpiThreads);  // this CTA's own rows are in the buffer
+        if (push && !ptx::mbar_wait_bounded(recv_bar, 0, kWaitLimitNs))  // and every other CTA's
+            atomicOr(&g_spmm24_status, kStatusEpilogueTimeout);
     }
     if (epi) {
         ptx::grid_dep_wait();  // C may be read or written by the previous grid
         // Owner side: sum the S partial copies of this CTA's rows in a fixed
         // order, round to fp16 and store with 16-byte coalesced writes.
-        const int my_start = (kTileM * rank + S - 1) / S;
-        const int my_end = (kTileM * (rank + 1) + S - 1) / S;
         const int nrows = my_end - my_start;
         constexpr int CHUNKS = N_TILE / 8;
         const int m0 = m_tile * kTileM;
