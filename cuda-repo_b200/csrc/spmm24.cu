@@ -100,8 +100,10 @@ using CV32 = ClusterVariant<32, 7>;
 using CV64 = ClusterVariant<64, 6>;
 using CV128 = ClusterVariant<128, 4>;
 using CV256 = ClusterVariant<256, 2>;
-constexpr int kPairStages = 4;
-using PairC = PairCfg<kPairStages>;
+// Pair tiles: 256 x 256 with a 4-stage ring (one CTA per SM) or 256 x 128
+// with a 3-stage ring (two CTAs per SM).
+using PairWide = PairCfg<128, 4>;
+using PairNarrow = PairCfg<64, 3>;
 using SV16 = StreamKVariant<16, 8>;
 using SV32 = StreamKVariant<32, 8>;
 // Shallow rings (about 92 KB of shared memory): two CTAs fit on one SM, so
@@ -113,7 +115,8 @@ using SV32s = StreamKVariant<32, 4>;
 
 struct Plan {
     Path path;
-    bool shallow;  // 4-stage ring, two CTAs per SM (narrow N only)
+    bool shallow;      // 4-stage ring, two CTAs per SM (narrow N only)
+    bool split_issue;  // pair path: A/metadata and B loads issued by two warps
     int tile_n;
     int stages;
     int split;  // cluster path: CTAs per cluster
@@ -183,11 +186,13 @@ Plan make_plan(int M, int N, int K, int split_k, int sms) {
     if (pair_ok && (pair_env == 1 || (pair_env != 0 && N > 128))) {
         p.path = Path::kPair;
         p.shallow = false;
-        p.tile_n = PairC::TILE_N;
-        p.stages = kPairStages;
-        p.smem = PairC::SMEM_ALLOC;
-        p.m_tiles = (M + PairC::TILE_M - 1) / PairC::TILE_M;
-        p.n_tiles = (N + PairC::TILE_N - 1) / PairC::TILE_N;
+        const bool narrow = env_int("SPMM24_PAIR_N", 256) == 128;  // tuning override
+        p.split_issue = env_int("SPMM24_PAIR_ISSUE", 1) == 2;      // tuning override
+        p.tile_n = narrow ? PairNarrow::TILE_N : PairWide::TILE_N;
+        p.stages = narrow ? 3 : 4;
+        p.smem = narrow ? PairNarrow::SMEM_ALLOC : PairWide::SMEM_ALLOC;
+        p.m_tiles = (M + 2 * kTileM - 1) / (2 * kTileM);
+        p.n_tiles = (N + p.tile_n - 1) / p.tile_n;
         p.split = 1;
         p.grid = 2 * p.m_tiles * p.n_tiles;
         return p;
@@ -205,10 +210,14 @@ Plan make_plan(int M, int N, int K, int split_k, int sms) {
         s = split_k;
     } else {
         // As many K slices as fill the resident CTA slots (two per SM with the
-        // shallow ring), keeping at least two stages per slice.
+        // shallow ring), keeping at least two stages per slice -- five for
+        // long K: measured on the 4096 x 4096 decode shapes, six slices of 5-6
+        // stages beat eight of 4 (fewer CTAs leave SM slots to the next
+        // launch's early CTAs).
         const long long slots = (long long)sms * (p.shallow ? 2 : 1);
+        const int min_stages = p.stages_total >= 24 ? 5 : 2;
         s = (int)std::max<long long>(1, slots / tiles);
-        s = std::max(1, std::min(s, p.stages_total / 2));
+        s = std::max(1, std::min(s, p.stages_total / min_stages));
     }
     p.split = std::max(1, std::min(std::min(s, kMaxSplit), p.stages_total));
     p.grid = p.split * p.n_tiles * p.m_tiles;
@@ -263,7 +272,10 @@ cudaError_t get_workspace(int dev, cudaStream_t stream, size_t counters, size_t 
     return cudaSuccess;
 }
 
-std::atomic<uint64_t> g_attr_done[16];  // per kernel variant: one bit per device
+std::atomic<uint64_t> g_attr_done[32];
+#ifdef SPMM24_TRACE
+std::atomic<long long> g_trace_next{0};  // next free CTA record in the trace buffer
+#endif  // per kernel variant: one bit per device
 
 template <class Kern>
 cudaError_t prepare(Kern kern, int smem, int dev, int idx) {
@@ -299,7 +311,13 @@ cudaError_t launch_kernel(Kern kern, dim3 grid, int smem, cudaStream_t stream, u
     }
     cfg.attrs = attr;
     cfg.numAttrs = n;
+#ifdef SPMM24_TRACE
+    Params kt = kp;
+    kt.trace_base = g_trace_next.fetch_add((long long)grid.x * grid.y * grid.z);
+    return cudaLaunchKernelEx(&cfg, kern, ta, tb, te, kt);
+#else
     return cudaLaunchKernelEx(&cfg, kern, ta, tb, te, kp);
+#endif
 }
 
 template <class V>
@@ -321,13 +339,24 @@ cudaError_t launch_streamk(const Plan& pl, cudaStream_t stream, int dev, bool pd
     return launch_kernel(kern, dim3((unsigned)pl.grid, 1, 1), V::C_::SMEM_ALLOC, stream, 1u, pdl, ta, tb, te, kp);
 }
 
+template <int HALF_N, int STAGES, bool SPLIT>
+cudaError_t launch_pair_v(const Plan& pl, cudaStream_t stream, int dev, bool pdl, const CUtensorMap& ta,
+                          const CUtensorMap& tb, const CUtensorMap& te, const PairParams& kp, int idx) {
+    using C_ = PairCfg<HALF_N, STAGES>;
+    auto kern = spmm24_pair_kernel<HALF_N, STAGES, SPLIT>;
+    cudaError_t e = prepare(kern, C_::SMEM_ALLOC, dev, idx);
+    if (e != cudaSuccess) return e;
+    return launch_kernel(kern, dim3(2u, (unsigned)pl.n_tiles, (unsigned)pl.m_tiles), C_::SMEM_ALLOC, stream, 2u, pdl,
+                         ta, tb, te, kp);
+}
+
 cudaError_t launch_pair(const Plan& pl, cudaStream_t stream, int dev, bool pdl, const CUtensorMap& ta,
                         const CUtensorMap& tb, const CUtensorMap& te, const PairParams& kp) {
-    auto kern = spmm24_pair_kernel<kPairStages>;
-    cudaError_t e = prepare(kern, PairC::SMEM_ALLOC, dev, 11);
-    if (e != cudaSuccess) return e;
-    return launch_kernel(kern, dim3(2u, (unsigned)pl.n_tiles, (unsigned)pl.m_tiles), PairC::SMEM_ALLOC, stream, 2u, pdl,
-                         ta, tb, te, kp);
+    if (pl.tile_n == PairNarrow::TILE_N)
+        return pl.split_issue ? launch_pair_v<64, 3, true>(pl, stream, dev, pdl, ta, tb, te, kp, 14)
+                              : launch_pair_v<64, 3, false>(pl, stream, dev, pdl, ta, tb, te, kp, 13);
+    return pl.split_issue ? launch_pair_v<128, 4, true>(pl, stream, dev, pdl, ta, tb, te, kp, 12)
+                          : launch_pair_v<128, 4, false>(pl, stream, dev, pdl, ta, tb, te, kp, 11);
 }
 
 size_t streamk_partial_bytes(const Plan& pl) { return (size_t)pl.grid * kTileM * pl.tile_n * sizeof(float); }
@@ -384,7 +413,7 @@ cudaError_t launch_impl(cudaStream_t stream, const void* A, const void* B, const
     {
         cuuint64_t dims[4] = {128, (cuuint64_t)(K / 64), 4, (cuuint64_t)((N + 7) / 8)};
         cuuint64_t str[3] = {1024, 256, (cuuint64_t)16 * K};
-        const int cta_n = pl.path == Path::kPair ? PairC::HALF_N : pl.tile_n;  // columns one CTA loads
+        const int cta_n = pl.path == Path::kPair ? pl.tile_n / 2 : pl.tile_n;  // columns one CTA loads
         cuuint32_t box[4] = {128, 2, 4, (cuuint32_t)(cta_n / 8)};
         if (!encode(&tb, 4, B, dims, str, box)) return invalid("TMA descriptor for B could not be encoded");
     }
@@ -616,7 +645,7 @@ extern "C" int spmm24_select_config(int M, int N, int K, int split_k, spmm24_con
     if (sms <= 0) sms = 148;
     cudaGetLastError();
     const spmm24::Plan pl = spmm24::make_plan(M, N, K, split_k, sms);
-    out->tile_m = pl.path == spmm24::Path::kPair ? spmm24::PairC::TILE_M : spmm24::kTileM;
+    out->tile_m = pl.path == spmm24::Path::kPair ? 2 * spmm24::kTileM : spmm24::kTileM;
     out->tile_n = pl.tile_n;
     out->stage_k = 128;
     out->stages = pl.stages;
@@ -660,6 +689,7 @@ extern "C" const char* spmm24_last_error(void) { return spmm24::g_last_error; }
 #ifdef SPMM24_TRACE
 // Trace builds only: where the kernels write their per-CTA timeline.
 extern "C" cudaError_t spmm24_set_trace(void* buf) {
+    spmm24::g_trace_next = 0;
     return cudaMemcpyToSymbol(spmm24::g_spmm24_trace, &buf, sizeof(buf));
 }
 #endif

@@ -43,13 +43,14 @@ static __device__ uint32_t g_spmm24_status;
 
 // Optional per-CTA timeline for performance work: builds that define
 // SPMM24_TRACE record %globaltimer and clock64 stamps into g_spmm24_trace
-// (16 words per CTA, linear CTA index).  The product build compiles the
-// stamps away.
+// (16 words per CTA; each launch writes its own records starting at the
+// trace_base its parameters carry).  The product build compiles the stamps
+// away.
 #ifdef SPMM24_TRACE
 __device__ unsigned long long* g_spmm24_trace;
-__device__ __forceinline__ void trace_stamp(int slot) {
+__device__ __forceinline__ void trace_stamp(long long base, int slot) {
     if (g_spmm24_trace) {
-        const size_t cta = blockIdx.x + (size_t)gridDim.x * (blockIdx.y + (size_t)gridDim.y * blockIdx.z);
+        const size_t cta = (size_t)base + blockIdx.x + (size_t)gridDim.x * (blockIdx.y + (size_t)gridDim.y * blockIdx.z);
         unsigned long long t, c;
         asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
         c = clock64();
@@ -57,11 +58,13 @@ __device__ __forceinline__ void trace_stamp(int slot) {
         g_spmm24_trace[cta * 16 + 2 * slot + 1] = c;
     }
 }
-#define SPMM24_STAMP(slot) ::spmm24::trace_stamp(slot)
+#define SPMM24_STAMP(slot) ::spmm24::trace_stamp(p.trace_base, slot)
+#define SPMM24_TRACE_FIELD long long trace_base;
 #else
 #define SPMM24_STAMP(slot) \
     do {                   \
     } while (0)
+#define SPMM24_TRACE_FIELD
 #endif
 
 template <int N_TILE, int STAGES, int ACC_BUFS>

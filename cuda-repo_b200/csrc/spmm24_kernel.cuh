@@ -12,9 +12,9 @@
 //       (no global workspace, no second launch, fixed summation order).
 //
 //   spmm24_pair_kernel  a CTA pair (cluster of 2) computing one 256 x 256
-//       tile with tcgen05.mma.sp.cta_group::2: each CTA holds 128 rows of A
-//       and 128 columns of B, so each SM feeds the tensor core only half of
-//       B -- the prefill (compute-bound) path.
+//       or 256 x 128 tile with tcgen05.mma.sp.cta_group::2: each CTA holds
+//       128 rows of A and half of the tile's columns of B, so each SM feeds
+//       the tensor core only half of B -- the prefill (compute-bound) path.
 //
 //   spmm24_streamk_kernel  a persistent grid (one CTA per SM) in which every
 //       CTA takes an equal share of the (tile, 128-K stage) units, walked
@@ -51,6 +51,7 @@ struct ClusterParams {
     int stages_total;  // ceil(groups / 2)
     int split;         // CTAs per cluster along K
     int weights_static;
+    SPMM24_TRACE_FIELD
 };
 
 struct PairParams {
@@ -58,6 +59,7 @@ struct PairParams {
     int M, N, K;
     int stages_total;  // K / 128 (the pair kernel requires K % 128 == 0)
     int weights_static;
+    SPMM24_TRACE_FIELD
 };
 
 struct StreamKParams {
@@ -71,6 +73,7 @@ struct StreamKParams {
     long long units;      // tiles * stages_per_tile
     int grid;
     int weights_static;
+    SPMM24_TRACE_FIELD
 };
 
 // -------------------------------------------------------------------------
@@ -90,12 +93,15 @@ struct ClusterCfg : Cfg<N_TILE, STAGES, 1> {
     static constexpr int HOLDER_OFFSET = BAR_OFFSET + NUM_BARS * 8;
     static constexpr int SMEM_BYTES = HOLDER_OFFSET + 16;
     static constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;  // slack to align the base to 1024 B
+    // CTAs that fit on one SM (228 KB, 1 KB reserved per CTA), at most 4.
+    static constexpr int CTAS_PER_SM = 233472 / (SMEM_ALLOC + 1024) < 4 ? 233472 / (SMEM_ALLOC + 1024) : 4;
     static_assert(SMEM_ALLOC <= 232448, "shared memory overflow");
     static_assert(RECV_BUF || RED_ROWS * RED_PITCH * 4 <= B_::RING_BYTES, "reduction buffer does not fit");
+    static_assert(CTAS_PER_SM * B_::TMEM_COLS <= 512, "co-resident CTAs must fit in TMEM together");
 };
 
 template <int N_TILE, int STAGES>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, ClusterCfg<N_TILE, STAGES>::CTAS_PER_SM)
 spmm24_cluster_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const __grid_constant__ CUtensorMap tmE, const ClusterParams p) {
     using C_ = ClusterCfg<N_TILE, STAGES>;
@@ -307,13 +313,18 @@ spmm24_cluster_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_cons
 }
 
 // -------------------------------------------------------------------------
-template <int STAGES>
+// A CTA pair computes a 256 x (2 * HALF_N) tile; each CTA holds 128 rows of A
+// and HALF_N columns of B.  HALF_N = 128 (256-wide tiles, 4-stage ring, one
+// CTA per SM) or 64 (128-wide tiles, 3-stage ring of 102 KB, two CTAs per
+// SM: TMA streams into shared memory at a bounded rate per CTA, so two
+// resident CTAs feed an SM about twice as fast as one).
+template <int HALF_N_, int STAGES>
 struct PairCfg {
-    static constexpr int HALF_N = 128;                   // columns of B / C per CTA
-    static constexpr int TILE_N = 256;                   // columns per pair
+    static constexpr int HALF_N = HALF_N_;               // columns of B / C per CTA
+    static constexpr int TILE_N = 2 * HALF_N;            // columns per pair
     static constexpr int TILE_M = 2 * kTileM;            // rows per pair
     static constexpr int A_BYTES = 8 * 8 * 256;          // this CTA's 128 rows x 128 logical K
-    static constexpr int B_BYTES = (HALF_N / 8) * 2048;  // this CTA's 128 columns x 128 K
+    static constexpr int B_BYTES = (HALF_N / 8) * 2048;  // this CTA's HALF_N columns x 128 K
     static constexpr int E_BYTES = 16 * 128;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + E_BYTES;
     static constexpr int RING_BYTES = STAGES * STAGE_BYTES;
@@ -322,10 +333,15 @@ struct PairCfg {
     static constexpr int HOLDER_OFFSET = BAR_OFFSET + NUM_BARS * 8;
     static constexpr int SMEM_BYTES = HOLDER_OFFSET + 16;
     static constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;
-    static constexpr int META_COL = TILE_N;  // accumulator: 256 fp32 columns
-    static constexpr int TMEM_COLS = 512;
+    static constexpr int META_COL = TILE_N;  // accumulator: TILE_N fp32 columns
+    static constexpr int TMEM_NEED = META_COL + 4 * STAGES;
+    static constexpr int TMEM_COLS = TMEM_NEED <= 128 ? 128 : TMEM_NEED <= 256 ? 256 : 512;
+    // Two CTAs per SM when both rings fit in the SM's 228 KB (1 KB reserved per CTA).
+    static constexpr int CTAS_PER_SM = 2 * (SMEM_ALLOC + 1024) <= 233472 ? 2 : 1;
     static constexpr int C_PITCH = TILE_N + 8;  // halves per staged output row (bank-shifted)
-    static_assert(META_COL + 4 * STAGES <= TMEM_COLS, "TMEM overflow");
+    static_assert(HALF_N == 64 || HALF_N == 128, "pair tiles are 128 or 256 columns wide");
+    static_assert(TMEM_NEED <= 512, "TMEM overflow");
+    static_assert(CTAS_PER_SM * TMEM_COLS <= 512, "co-resident CTAs must fit in TMEM together");
     static_assert(SMEM_ALLOC <= 232448, "shared memory overflow");
     static_assert(kTileM * C_PITCH * 2 <= RING_BYTES, "output staging does not fit");
 };
@@ -333,16 +349,19 @@ struct PairCfg {
 constexpr int kPairGroupM = 8;  // tile rows per rasterisation group
 
 // Instruction descriptor of the pair MMA: sparse, D=f32, A=B=f16, A K-major,
-// B MN-major, M=256, N=256.
+// B MN-major, M=256, N=TILE_N.
+template <int TILE_N>
 __host__ __device__ constexpr uint32_t pair_idesc() {
-    return (1u << 2) | (1u << 4) | (1u << 16) | ((uint32_t)(256 >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
+    return (1u << 2) | (1u << 4) | (1u << 16) | ((uint32_t)(TILE_N >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
 }
 
-template <int STAGES>
-__global__ void __launch_bounds__(kThreads, 1)
+// SPLIT_ISSUE: warp 0 issues the A and metadata loads and warp 2 the B loads
+// (before it joins the epilogue), so two threads of the CTA keep TMA busy.
+template <int HALF_N, int STAGES, bool SPLIT_ISSUE>
+__global__ void __launch_bounds__(kThreads, PairCfg<HALF_N, STAGES>::CTAS_PER_SM)
 spmm24_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmE, const PairParams p) {
-    using C_ = PairCfg<STAGES>;
+    using C_ = PairCfg<HALF_N, STAGES>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + C_::BAR_OFFSET);  // used in the leader only
@@ -394,13 +413,14 @@ spmm24_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
     const uint32_t tmem_base = *tmem_holder;
     if (threadIdx.x == 0) ptx::grid_dep_launch();
 
+    // Both CTAs' loads complete on the leader's full barrier; the leader arms
+    // it once per stage with both CTAs' bytes.
+    const uint64_t pol = ptx::policy_evict_last();  // A is re-read by every N tile, B by every M tile
+    const uint32_t full0 = ptx::mapa_shared(ptx::smem_u32(&full[0]), 0u);
+    const int pre = p.weights_static ? min(STAGES, st_count) : 0;
     if (warp == 0) {
-        // ---------------------------------------------------- TMA producer
+        // ------------------------------------- TMA producer: A + metadata (+ B)
         if (lane == 0) {
-            const uint64_t pol = ptx::policy_evict_last();  // A is re-read by every N tile, B by every M tile
-            // Both CTAs' loads complete on the leader's full barrier.
-            const uint32_t full0 = ptx::mapa_shared(ptx::smem_u32(&full[0]), 0u);
-            const int pre = p.weights_static ? min(STAGES, st_count) : 0;
             for (int it = 0; it < pre; ++it) {
                 uint8_t* st = smem + it * C_::STAGE_BYTES;
                 if (leader) ptx::mbar_arrive_expect_tx(&full[it], 2 * C_::STAGE_BYTES);
@@ -409,9 +429,10 @@ spmm24_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
             }
             ptx::grid_dep_wait();
             SPMM24_STAMP(1);
-            for (int it = 0; it < pre; ++it)
-                ptx::tma_load_4d_pair(smem + it * C_::STAGE_BYTES + C_::A_BYTES, &tmB, full0 + 8u * it, 0, 2 * it, 0,
-                                      strip0, pol);
+            if (!SPLIT_ISSUE)
+                for (int it = 0; it < pre; ++it)
+                    ptx::tma_load_4d_pair(smem + it * C_::STAGE_BYTES + C_::A_BYTES, &tmB, full0 + 8u * it, 0, 2 * it,
+                                          0, strip0, pol);
             for (int it = pre; it < st_count; ++it) {
                 const int s = it % STAGES;
                 const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
@@ -424,13 +445,13 @@ spmm24_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                 if (leader) ptx::mbar_arrive_expect_tx(&full[s], 2 * C_::STAGE_BYTES);
                 ptx::tma_load_3d_pair(st, &tmA, bar, 0, band0, 8 * it, pol);
                 ptx::tma_load_2d_pair(st + C_::A_BYTES + C_::B_BYTES, &tmE, bar, 128 * it, band0, pol);
-                ptx::tma_load_4d_pair(st + C_::A_BYTES, &tmB, bar, 0, 2 * it, 0, strip0, pol);
+                if (!SPLIT_ISSUE) ptx::tma_load_4d_pair(st + C_::A_BYTES, &tmB, bar, 0, 2 * it, 0, strip0, pol);
             }
         }
         __syncwarp();
     } else if (warp == 1 && leader) {
         // ---------------------------------- MMA issuer (leader CTA only)
-        constexpr uint32_t idesc = pair_idesc();
+        constexpr uint32_t idesc = pair_idesc<C_::TILE_N>();
         const uint32_t smem_base = ptx::smem_u32(smem);
         uint32_t accumulate = 0;
         for (int it = 0; it < st_count; ++it) {
@@ -462,7 +483,25 @@ spmm24_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
         }
         if (lane == 0) ptx::tc_commit_pair_mc(acc_full, 0x3);
         __syncwarp();
-    } else if (warp >= 2) {
+    }
+    if (SPLIT_ISSUE && warp == 2) {
+        // --------------------- second TMA producer: B, then the epilogue
+        if (lane == 0) {
+            ptx::grid_dep_wait();
+            for (int it = 0; it < st_count; ++it) {
+                const int s = it % STAGES;
+                const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
+                if (it >= STAGES && !ptx::mbar_wait_bounded(&empty[s], ph ^ 1u, kWaitLimitNs)) {
+                    atomicOr(&g_spmm24_status, kStatusProducerTimeout);
+                    break;
+                }
+                ptx::tma_load_4d_pair(smem + s * C_::STAGE_BYTES + C_::A_BYTES, &tmB, full0 + 8u * s, 0, 2 * it, 0,
+                                      strip0, pol);
+            }
+        }
+        __syncwarp();
+    }
+    if (warp >= 2) {
         // ------------------------------------------- epilogue (both CTAs)
         if (!ptx::mbar_wait_bounded(acc_full, 0, kWaitLimitNs)) atomicOr(&g_spmm24_status, kStatusEpilogueTimeout);
         if (threadIdx.x == 64) SPMM24_STAMP(4);
@@ -488,14 +527,18 @@ spmm24_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
         ptx::tc_fence_before();
         ptx::named_barrier(kBarEpi, kEpiThreads);
         ptx::grid_dep_wait();  // C may be in use by the previous grid
+        // Coalesced copy-out: LPR threads cover one row with 16-byte chunks.
+        constexpr int LPR = C_::TILE_N / 8;
+        constexpr int RPP = kEpiThreads / LPR;  // rows per pass
         const int etid = threadIdx.x - 64;
+        const int chunk = etid % LPR;
         const int gm0 = m_tile * C_::TILE_M + (int)rank * kTileM;
-        const int gn = n_tile * C_::TILE_N + lane * 8;
+        const int gn = n_tile * C_::TILE_N + chunk * 8;
         const bool vec_ok = (p.N % 8 == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15u) == 0);
-        for (int r = etid >> 5; r < kTileM; r += kEpiThreads / 32) {
+        for (int r = etid / LPR; r < kTileM; r += RPP) {
             const int gm = gm0 + r;
             if (gm >= p.M || gn >= p.N) continue;
-            const __half* src = cst + (size_t)r * C_::C_PITCH + lane * 8;
+            const __half* src = cst + (size_t)r * C_::C_PITCH + chunk * 8;
             __half* out = p.C + (size_t)gm * p.N + gn;
             if (vec_ok) {
                 *reinterpret_cast<uint4*>(out) = *reinterpret_cast<const uint4*>(src);

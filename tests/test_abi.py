@@ -81,10 +81,12 @@ def test_launch_rejects_bad_arguments_without_gpu():
 def test_select_config_picks_tiles_and_splits():
     c = spmm24.select_config(4096, 16, 4096)
     assert c["tile_m"] == 128 and c["tile_n"] == 16 and c["stage_k"] == 128
-    # narrow N with an automatic split: shallow ring (two CTAs per SM) and a
-    # K split that fills both slots of every SM
-    assert c["stream_k"] == 0 and c["stages"] == 4 and c["split_k"] == 8 and c["grid_ctas"] == 256
+    # narrow N with an automatic split: shallow ring (two CTAs per SM), a K
+    # split towards two slots per SM, at least five stages per slice for long K
+    assert c["stream_k"] == 0 and c["stages"] == 4 and c["split_k"] == 6 and c["grid_ctas"] == 192
     assert spmm24.select_config(11008, 16, 4096)["split_k"] == 3
+    assert spmm24.select_config(4096, 16, 11008)["split_k"] == 8
+    assert spmm24.select_config(4096, 16, 1024)["split_k"] == 4  # short K: two stages per slice
     assert spmm24.select_config(256, 16, 128)["split_k"] == 1  # at least two stages per slice
     # an explicit split is honoured
     c = spmm24.select_config(4096, 16, 4096, 4)

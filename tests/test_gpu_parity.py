@@ -159,12 +159,17 @@ def test_back_to_back_calls_pdl(cuda_device):
     (4096, 520, 1024),   # several pairs, ragged last N tile
     (768, 1000, 256),    # N not a multiple of 8: scalar stores
 ])
-def test_cta_pair_kernel(cuda_device, shape):
-    """The cta_group::2 pair kernel (256 x 256 tiles, K % 128 == 0)."""
+@pytest.mark.parametrize("tile_n,issue", [(256, 1), (256, 2), (128, 1), (128, 2)])
+def test_cta_pair_kernel(cuda_device, monkeypatch, shape, tile_n, issue):
+    """The cta_group::2 pair kernel (256 x 256 or 256 x 128 tiles, K % 128 ==
+    0), with the loads issued by one or by two warps."""
     import spmm24
 
+    monkeypatch.setenv("SPMM24_PAIR_N", str(tile_n))
+    monkeypatch.setenv("SPMM24_PAIR_ISSUE", str(issue))
     M, N, K = shape
-    assert spmm24.select_config(M, N, K)["cta_pair"] == 1
+    cfg = spmm24.select_config(M, N, K)
+    assert cfg["cta_pair"] == 1 and cfg["tile_n"] == tile_n
     p = make_problem(M, N, K, seed=3 * M + N)
     check(p, 0, cuda_device)
 
