@@ -52,6 +52,18 @@ WORKLOADS = {
 }
 
 
+# --workload pack: the on-device packer over the LLaMA-7B layer weights of
+# config 2 (dense fp16 N(0, 0.02), magnitude-pruned and compressed in one
+# kernel per layer).
+PACK_LAYERS = [(4096, 4096), (11008, 4096), (4096, 11008)]
+
+
+def pack_bytes(M, K):
+    """Algorithmic bytes of one spmm24_pack_a_device call: the dense fp16
+    read, the compressed values and the metadata written."""
+    return 2 * M * K + M * K + M * K // 8
+
+
 def algo_bytes(M, N, K):
     return M * K + M * K // 8 + 2 * K * N + 2 * M * N
 
@@ -537,9 +549,219 @@ def cpu_baseline(layers, acts, shapes, budget_s=10.0):
                       f"{dt:.1f} s"}
 
 
+# ------------------------------------------------- on-device packer
+def host_pack_baseline(dense_np, budget_s=10.0):
+    """The reference's own host packer (toolCompressMatrixA +
+    toolReorderMetadata built from its sources into oracle/_ref), else the
+    oracle's restatement of it, on a row sample of each layer; single
+    threaded as the reference is.  Returns (GB/s, kind, sample)."""
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import oracle as O
+
+    use_ref = O.ref_packer_available()
+
+    def pack(a, M, K):
+        # the reference has no pruning step (its inputs are generated 2:4):
+        # the oracle's prune runs first, inside the timed work
+        a = O.prune_magnitude_2of4(a, M, K)
+        if use_ref:
+            _, _, meta = O.ref_compress_a(a, M, K)
+            O.ref_reorder_metadata(meta, M, K)
+        else:
+            _, meta = O.compress_a(a, M, K)
+            O.reorder_metadata(meta, M, K)
+
+    probe = 64
+    t = time.perf_counter()
+    for (M, K), a in zip(PACK_LAYERS, dense_np):
+        pack(a[: probe * K], probe, K)
+    dt = time.perf_counter() - t
+    rows = int(max(16, min(4096, probe * budget_s / max(dt, 1e-3) / 1.2))) // 16 * 16
+    nbytes = 0
+    t = time.perf_counter()
+    for (M, K), a in zip(PACK_LAYERS, dense_np):
+        r = min(rows, M)
+        pack(a[: r * K], r, K)
+        nbytes += pack_bytes(r, K)
+    dt = time.perf_counter() - t
+    kind = "reference" if use_ref else "port"
+    return nbytes / dt / 1e9, kind, (f"first {rows} rows of each of the {len(PACK_LAYERS)} layers through "
+                                     f"{'oracle prune, then toolCompressMatrixA + toolReorderMetadata (oracle/_ref)' if use_ref else 'oracle prune + orc_compress_a + orc_reorder_metadata'}, "
+                                     f"1 thread, {dt:.1f} s")
+
+
+def run_pack(args, rank, world, local_rank):
+    """Times spmm24_pack_a_device (magnitude prune + compress + reordered
+    metadata in one kernel) over the three LLaMA-7B layer shapes, weights
+    resident in HBM (214 MB of dense weights per step, more than L2)."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import spmm24
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    g = torch.Generator(device=dev).manual_seed(7 + rank)
+    dense = [(torch.randn(M, K, generator=g, device=dev) * 0.02).half() for (M, K) in PACK_LAYERS]
+    vals = [torch.empty(M * K // 2, dtype=torch.int16, device=dev) for (M, K) in PACK_LAYERS]
+    meta = [torch.empty(M * K // 16, dtype=torch.int16, device=dev) for (M, K) in PACK_LAYERS]
+    bad = torch.zeros(len(PACK_LAYERS), dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    hs = int(stream.cuda_stream)
+    L = spmm24._lib
+
+    def step():
+        for i, (M, K) in enumerate(PACK_LAYERS):
+            rc = L.spmm24_pack_a_device(hs, dense[i].data_ptr(), M, K, 1, vals[i].data_ptr(), meta[i].data_ptr(),
+                                        bad.data_ptr() + 4 * i)
+            if rc != 0:
+                raise RuntimeError(f"spmm24_pack_a_device failed: {rc} {L.spmm24_last_error().decode()}")
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        torch.cuda._sleep(int(2e7))
+        t0.record(stream)
+        for _ in range(args.steps):
+            step()
+        t1.record(stream)
+        torch.cuda.synchronize(dev)
+    elapsed_ms = t0.elapsed_time(t1)
+    clocks = clk.summary()
+    # the timed work is checked: no bad rows, and the smallest layer equals the host packer bit for bit
+    assert int(bad.sum()) == 0
+    d0 = dense[0].view(torch.int16).cpu().numpy().view(np.uint16)
+    hv, hm = spmm24.compress_reordered(spmm24.prune_2of4(d0, *PACK_LAYERS[0]), *PACK_LAYERS[0])
+    assert np.array_equal(vals[0].cpu().numpy().view(np.uint16), hv)
+    assert np.array_equal(meta[0].cpu().numpy().view(np.uint16), hm)
+
+    # per-layer kernel durations (event pair around each launch)
+    per = {}
+    for i, (M, K) in enumerate(PACK_LAYERS):
+        ts = []
+        for _ in range(5):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            L.spmm24_pack_a_device(hs, dense[i].data_ptr(), M, K, 1, vals[i].data_ptr(), meta[i].data_ptr(), None)
+            b.record(stream)
+            torch.cuda.synchronize(dev)
+            ts.append(a.elapsed_time(b) * 1e3)
+        per[f"{M}x{K}"] = round(statistics.median(ts), 3)
+
+    # end to end: dense weights from pinned host memory, pack, compressed
+    # values + metadata back to pinned host memory, every step
+    host_dense = [d.cpu().pin_memory() for d in dense]
+    host_vals = [torch.empty(v.shape, dtype=v.dtype).pin_memory() for v in vals]
+    host_meta = [torch.empty(m.shape, dtype=m.dtype).pin_memory() for m in meta]
+
+    def e2e_step():
+        for i in range(len(PACK_LAYERS)):
+            dense[i].copy_(host_dense[i], non_blocking=True)
+        step()
+        for i in range(len(PACK_LAYERS)):
+            host_vals[i].copy_(vals[i], non_blocking=True)
+            host_meta[i].copy_(meta[i], non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([elapsed_ms, e2e_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed_ms, e2e_ms = float(t[0]), float(t[1])
+
+    step_bytes = sum(pack_bytes(M, K) for (M, K) in PACK_LAYERS)
+    value = step_bytes * args.steps * world / (elapsed_ms * 1e-3) / 1e9
+    achieved = step_bytes * args.steps / (elapsed_ms * 1e-3) / 1e9
+    peaks = load_peaks()
+    out = {
+        "metric": "GB/s of the on-device 2:4 packer (magnitude prune + compress + reordered metadata) "
+                  "on the LLaMA-7B layer weights",
+        "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(elapsed_ms / args.steps, 5), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "u16 (fp16 bit patterns; integer/byte work)",
+        "data": "synthetic (seeded torch RNG on the device; dense fp16 N(0,0.02))",
+        "config": {"workload": "pack: " + ", ".join(f"{M}x{K}" for (M, K) in PACK_LAYERS),
+                   "baseline_config": 2, "calls_per_step": len(PACK_LAYERS),
+                   "l2": f"inputs larger than L2: {sum(2 * M * K for (M, K) in PACK_LAYERS) / 1e6:.0f} MB of "
+                         "dense weights per step",
+                   "parallelism": f"replicas x{world}"},
+        "per_layer_us": per,
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None,
+                     "peak_src": f"{peaks['src']} (hbm_gbs copy)",
+                     "note": "bytes = dense read 2MK + values MK + metadata MK/8 per layer"},
+        "e2e": {"value": round(step_bytes * args.steps * world / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                "h2d_bytes_per_step": sum(2 * M * K for (M, K) in PACK_LAYERS),
+                "d2h_bytes_per_step": sum(M * K + M * K // 8 for (M, K) in PACK_LAYERS),
+                "ms_per_step": round(e2e_ms / args.steps, 4),
+                "path": "per step: H2D of the dense weights (pinned), spmm24_pack_a_device per layer, "
+                        "D2H of values + metadata"},
+        "gpu_launches": len(PACK_LAYERS) * args.steps,
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        dn = [d.view(torch.int16).cpu().numpy().view(np.uint16).reshape(-1) for d in dense]
+        gbs, kind, sample = host_pack_baseline(dn, args.cpu_seconds)
+        out["cpu_baseline"] = {"value": round(gbs, 4), "unit": "GB/s", "cores": 1, "kind": kind, "sample": sample}
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+
+
 # -------------------------------------------------------- reference arm
+def run_reference_pack(args):
+    """--impl reference --workload pack: the reference's host packer on row
+    samples of the same layers, one step = one sample of each layer."""
+    import numpy as np
+    import torch
+
+    g = torch.Generator().manual_seed(7)
+    dense = [(torch.randn(M, K, generator=g) * 0.02).half().numpy().view(np.uint16).reshape(-1)
+             for (M, K) in PACK_LAYERS]
+    vals = []
+    for _ in range(args.warmup):
+        host_pack_baseline(dense, 0.2)
+    for _ in range(args.steps):
+        vals.append(host_pack_baseline(dense, 1.0))
+    gbs = statistics.median(v[0] for v in vals)
+    kind, sample = vals[-1][1], vals[-1][2]
+    print(json.dumps({
+        "impl": "reference",
+        "metric": "GB/s of the on-device 2:4 packer (magnitude prune + compress + reordered metadata) "
+                  "on the LLaMA-7B layer weights",
+        "value": round(gbs, 4), "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "u16 (fp16 bit patterns; integer/byte work)", "data": "synthetic",
+        "config": {"workload": "pack: " + ", ".join(f"{M}x{K}" for (M, K) in PACK_LAYERS), "baseline_config": 2},
+        "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": 1, "kind": kind, "sample": sample},
+        "e2e": {"value": round(gbs, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference packs on the host only; it has no prune, so the oracle's prune runs before its "
+                "compress + reorder",
+    }), flush=True)
+
+
 def run_reference(args, rank, world):
     if rank != 0:
+        return
+    if args.workload == "pack":
+        run_reference_pack(args)
         return
     import numpy as np
     import torch
@@ -629,7 +851,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="decode")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["pack"], default="decode")
     ap.add_argument("--comparators", action="store_true")
     ap.add_argument("--allgather", action="store_true", help="70b workload: also time the NCCL all-gather of C")
     ap.add_argument("--no-static-weights", dest="static_weights", action="store_false",
@@ -649,6 +871,9 @@ def main():
         return
     if args.single:
         run_single(args)
+        return
+    if args.workload == "pack":
+        run_pack(args, rank, world, local_rank)
         return
     run_ours(args, rank, world, local_rank)
 

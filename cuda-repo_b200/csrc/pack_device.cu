@@ -1,0 +1,270 @@
+// pack_device.cu -- the host packer (packer.cpp) as sm_100a kernels, so
+// weights and activations can be brought into the SpMM's formats without a
+// round trip through host memory:
+//
+//   spmm24_pack_a_device     optional magnitude 2:4 prune, then compress to
+//                            16x8 value blocks and write the reordered
+//                            metadata, in one pass over the dense weights
+//                            (toolCompressMatrixA + toolReorderMetadata,
+//                            SpeakOutLoudly/CUDA-Repo test/utils.h:91-185)
+//   spmm24_prune_2of4_device the prune alone, in place
+//   spmm24_pack_b_device     row-major K x N -> 8-column strips
+//                            (toolPackMatrixB, test/utils.h:188-229)
+//
+// All three are bit-exact with packer.cpp on every input the host functions
+// accept.  They are HBM-bound copies: each CTA stages a tile in shared
+// memory so that both the reads and the writes are coalesced.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "spmm24/SpMM_API.h"
+#include "spmm24_host.h"
+
+namespace spmm24 {
+namespace {
+
+constexpr int kPackThreads = 256;
+constexpr int kTileBlocks = 16;                      // 16-K blocks per A tile (256 columns)
+constexpr int kTileCols = kTileBlocks * 16;          // halves per A tile row
+constexpr int kTilePitch = kTileCols + 8;            // padded row pitch (halves): 16-byte bank shift per row
+constexpr int kBTileRows = 64, kBTileCols = 64;      // B tile: 64 K rows x 8 strips
+constexpr int kBTilePitch = kBTileCols + 8;
+
+// The kernels work on a group of four halves held in two 32-bit words
+// (x = h0 | h1 << 16, y = h2 | h3 << 16) with integer operations only.
+//
+// Magnitudes: for fp16 bit patterns, |x| orders like the 15-bit integer
+// h & 0x7fff, except that a NaN (above 0x7c00) compares false with
+// everything -- the host's float comparisons, reproduced exactly.
+
+// Magnitude 2:4 prune of one group (packer.cpp spmm24_prune_2of4): keep the
+// largest |x| (first on ties), then the largest of the other three (first on
+// ties), replace the other two by +0.
+//
+// Sequential form, exact for NaN (a NaN never wins or loses a comparison).
+__device__ __forceinline__ uint32_t prune_keep_sequential(uint32_t ax, uint32_t ay) {
+    const uint32_t m0 = ax & 0xffffu, m1 = ax >> 16, m2 = ay & 0xffffu, m3 = ay >> 16;
+    const bool v0 = m0 <= 0x7c00u, v1 = m1 <= 0x7c00u, v2 = m2 <= 0x7c00u, v3 = m3 <= 0x7c00u;
+    uint32_t k0 = 0, mk = m0;
+    bool c = v0 && v1 && m1 > mk;
+    k0 = c ? 1u : k0;
+    mk = c ? m1 : mk;
+    c = v0 && v2 && m2 > mk;
+    k0 = c ? 2u : k0;
+    mk = c ? m2 : mk;
+    c = v0 && v3 && m3 > mk;
+    k0 = c ? 3u : k0;
+    uint32_t k1 = k0 == 0 ? 1u : 0u;
+    uint32_t mk1 = k0 == 0 ? m1 : m0;
+    const bool vk1 = k0 == 0 ? v1 : v0;
+    c = k0 >= 2 && vk1 && v1 && m1 > mk1;
+    k1 = c ? 1u : k1;
+    mk1 = c ? m1 : mk1;
+    c = k0 != 2 && vk1 && v2 && m2 > mk1;
+    k1 = c ? 2u : k1;
+    mk1 = c ? m2 : mk1;
+    c = k0 != 3 && vk1 && v3 && m3 > mk1;
+    k1 = c ? 3u : k1;
+    return (1u << k0) | (1u << k1);
+}
+
+__device__ __forceinline__ void prune_group(uint32_t& x, uint32_t& y) {
+    const uint32_t ax = x & 0x7fff7fffu, ay = y & 0x7fff7fffu;
+    const uint32_t mx = __vmaxu2(ax, ay);
+    uint32_t keep;
+    if (max(mx & 0xffffu, mx >> 16) <= 0x7c00u) {
+        // No NaN: the sequential scan keeps the two largest of the unique keys
+        // |x| << 2 | (3 - position) (equal magnitudes: the lower position wins).
+        const uint32_t a0 = ((ax << 2) & 0x3fffcu) | 3u, a1 = ((ax >> 14) & 0x3fffcu) | 2u;
+        const uint32_t a2 = ((ay << 2) & 0x3fffcu) | 1u, a3 = (ay >> 14) & 0x3fffcu;
+        const uint32_t hi01 = max(a0, a1), lo01 = min(a0, a1), hi23 = max(a2, a3), lo23 = min(a2, a3);
+        const uint32_t top = max(hi01, hi23), second = max(min(hi01, hi23), max(lo01, lo23));
+        keep = (8u >> (top & 3u)) | (8u >> (second & 3u));
+    } else {
+        keep = prune_keep_sequential(ax, ay);
+    }
+    x &= (keep & 1u) * 0xffffu + (keep & 2u) * 0x7fff8000u;
+    y &= ((keep >> 2) & 1u) * 0xffffu + ((keep >> 2) & 2u) * 0x7fff8000u;
+}
+
+// Compress one group (test/utils.h:124-146): the first two zeros (+0 or -0)
+// are dropped and the rest is kept.  With z the 4-bit mask of zero
+// positions, a 16-entry nibble table gives the two kept positions (ia | ib
+// << 2, the lower first); fewer than two zeros (z in {0, 1, 2, 4, 8}) keep
+// more than two values and make the group invalid.  Returns the kept halves
+// (the lower position in the low 16 bits) and the positions in *idx.
+__device__ __forceinline__ bool compress_group(uint32_t x, uint32_t y, uint32_t* halves, uint32_t* idx) {
+    const uint32_t ax = x & 0x7fff7fffu, ay = y & 0x7fff7fffu;
+    const uint32_t z = ((ax & 0xffffu) == 0 ? 1u : 0u) | (ax < 0x10000u ? 2u : 0u) |
+                       ((ay & 0xffffu) == 0 ? 4u : 0u) | (ay < 0x10000u ? 8u : 0u);
+    const uint32_t id = (uint32_t)(0xECD4E894ECD4E444ull >> (4 * z)) & 0xfu;
+    const uint32_t ia = id & 3u, ib = id >> 2;
+    *halves = __byte_perm(x, y, ia * 0x22u + ib * 0x2200u + 0x1010u);
+    *idx = id;
+    return ((0x0117u >> z) & 1u) == 0;
+}
+
+// One CTA: kPackBands 16-row bands x 16 blocks of 16 K.  All of the tile's
+// loads are issued before any is used (8 x 16 bytes per thread), so each SM
+// keeps about 200 KB of reads in flight.  Thread t then handles row t % 16
+// of block t / 16 in every band; per band the value writes (block-major,
+// then row) are one contiguous 4 KB run.
+constexpr int kPackBands = 4;
+constexpr int kLoadsPerThread = kPackBands * 16 * (kTileCols / 8) / kPackThreads;
+
+__global__ void __launch_bounds__(kPackThreads) pack_a_kernel(const uint16_t* __restrict__ dense, int M, int K,
+                                                              int prune, uint16_t* __restrict__ vals,
+                                                              uint16_t* __restrict__ meta, int* bad_blocks) {
+    __shared__ __align__(16) uint16_t tile[kPackBands * 16 * kTilePitch];
+    const int band0 = blockIdx.y * kPackBands;
+    const int nb = min(kPackBands, M / 16 - band0);
+    const int nbc = K / 16;
+    const int q0 = blockIdx.x * kTileBlocks;
+    const int nq = min(kTileBlocks, nbc - q0);  // a multiple of 4 (K % 64 == 0)
+    const int chunks_per_row = nq * 2;          // 16-byte chunks
+    const int total = nb * 16 * chunks_per_row;
+    const uint16_t* base = dense + (size_t)band0 * 16 * K + (size_t)q0 * 16;
+    uint4 v[kLoadsPerThread];
+#pragma unroll
+    for (int i = 0; i < kLoadsPerThread; ++i) {
+        const int c = threadIdx.x + i * kPackThreads;
+        if (c < total) {
+            const int r = c / chunks_per_row, x = c % chunks_per_row;
+            v[i] = *reinterpret_cast<const uint4*>(base + (size_t)r * K + x * 8);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < kLoadsPerThread; ++i) {
+        const int c = threadIdx.x + i * kPackThreads;
+        if (c < total) {
+            const int r = c / chunks_per_row, x = c % chunks_per_row;
+            *reinterpret_cast<uint4*>(tile + r * kTilePitch + x * 8) = v[i];
+        }
+    }
+    __syncthreads();
+    const int q = threadIdx.x / 16, r = threadIdx.x % 16;
+    if (q >= nq) return;
+    const int qg = q0 + q;
+    int bad = 0;
+    for (int b = 0; b < nb; ++b) {
+        const uint16_t* row = tile + (b * 16 + r) * kTilePitch + q * 16;
+        const uint4 lo = *reinterpret_cast<const uint4*>(row);
+        const uint4 hi = *reinterpret_cast<const uint4*>(row + 8);
+        uint32_t wx[4] = {lo.x, lo.z, hi.x, hi.z}, wy[4] = {lo.y, lo.w, hi.y, hi.w};
+        uint32_t w[4], md = 0;
+        bool ok = true;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            if (prune) prune_group(wx[k], wy[k]);
+            uint32_t idx;
+            ok &= compress_group(wx[k], wy[k], &w[k], &idx);
+            md |= idx << (4 * k);
+        }
+        bad += ok ? 0 : 1;
+        const int band = band0 + b;
+        *reinterpret_cast<uint4*>(vals + (((size_t)band * nbc + qg) * 16 + r) * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+        // Reordered metadata (test/utils.h:179-180): per band and 64-K group,
+        // word i*8 + j holds (row (j%2)*8 + i, block j/2 of the group).
+        const size_t grp = (size_t)band * (K / 64) + qg / 4;
+        meta[grp * 64 + (r % 8) * 8 + 2 * (qg % 4) + r / 8] = (uint16_t)md;
+    }
+    if (bad && bad_blocks) atomicAdd(bad_blocks, bad);
+}
+
+// In-place magnitude prune, one group of four per thread.
+__global__ void __launch_bounds__(kPackThreads) prune_kernel(uint16_t* __restrict__ a, long long groups) {
+    for (long long g = blockIdx.x * (long long)kPackThreads + threadIdx.x; g < groups;
+         g += (long long)gridDim.x * kPackThreads) {
+        uint2 w = *reinterpret_cast<uint2*>(a + 4 * g);
+        prune_group(w.x, w.y);
+        *reinterpret_cast<uint2*>(a + 4 * g) = w;
+    }
+}
+
+// One CTA: 64 K rows x 64 columns (8 strips).  Reads row segments of 128
+// bytes, writes each strip's 64 rows as one contiguous 1 KB run.
+__global__ void __launch_bounds__(kPackThreads) pack_b_kernel(const uint16_t* __restrict__ b, int K, int N,
+                                                              uint16_t* __restrict__ out) {
+    __shared__ __align__(16) uint16_t tile[kBTileRows * kBTilePitch];
+    const int k0 = blockIdx.y * kBTileRows;
+    const int n0 = blockIdx.x * kBTileCols;
+    const bool vec = (N % 8 == 0) && ((reinterpret_cast<uintptr_t>(b) & 15u) == 0);
+    for (int c = threadIdx.x; c < kBTileRows * (kBTileCols / 8); c += kPackThreads) {
+        const int r = c / (kBTileCols / 8), x = c % (kBTileCols / 8);
+        const int n = n0 + x * 8;
+        const uint16_t* src = b + (size_t)(k0 + r) * N + n;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (vec) {
+            if (n < N) v = *reinterpret_cast<const uint4*>(src);
+        } else {
+            __align__(16) uint16_t h[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) h[e] = (n + e < N) ? src[e] : (uint16_t)0;
+            v = *reinterpret_cast<const uint4*>(h);
+        }
+        *reinterpret_cast<uint4*>(tile + r * kBTilePitch + x * 8) = v;
+    }
+    __syncthreads();
+    const int strips = (N + 7) / 8;
+    for (int c = threadIdx.x; c < kBTileRows * (kBTileCols / 8); c += kPackThreads) {
+        const int s = c / kBTileRows, r = c % kBTileRows;
+        const int strip = n0 / 8 + s;
+        if (strip >= strips) continue;
+        *reinterpret_cast<uint4*>(out + ((size_t)strip * K + k0 + r) * 8) =
+            *reinterpret_cast<const uint4*>(tile + r * kBTilePitch + s * 8);
+    }
+}
+
+bool misaligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) != 0; }
+
+}  // namespace
+}  // namespace spmm24
+
+extern "C" cudaError_t spmm24_pack_a_device(cudaStream_t stream, const void* dense_a, int M, int K, int prune,
+                                            void* values_out, uint16_t* meta_out, int* bad_blocks) {
+    using namespace spmm24;
+    clear_last_error();
+    if (!dense_a || !values_out || !meta_out) return record_invalid("null pointer");
+    if (M <= 0 || K <= 0 || M % 16 || K % 64) return record_invalid("M must be a multiple of 16 and K of 64");
+    if (misaligned16(dense_a) || misaligned16(values_out)) return record_invalid("dense A and values must be 16-byte aligned");
+    if ((reinterpret_cast<uintptr_t>(meta_out) & 1u) || (reinterpret_cast<uintptr_t>(bad_blocks) & 3u))
+        return record_invalid("metadata must be 2-byte and bad_blocks 4-byte aligned");
+    const int nbc = K / 16;
+    dim3 grid((unsigned)((nbc + kTileBlocks - 1) / kTileBlocks), (unsigned)((M / 16 + kPackBands - 1) / kPackBands));
+    if (grid.y > 65535) return record_invalid("M too large");
+    pack_a_kernel<<<grid, kPackThreads, 0, stream>>>(static_cast<const uint16_t*>(dense_a), M, K, prune ? 1 : 0,
+                                                     static_cast<uint16_t*>(values_out), meta_out, bad_blocks);
+    return cudaGetLastError();
+}
+
+extern "C" cudaError_t spmm24_prune_2of4_device(cudaStream_t stream, void* dense_a, int M, int K) {
+    using namespace spmm24;
+    clear_last_error();
+    if (!dense_a) return record_invalid("null pointer");
+    if (M <= 0 || K <= 0 || K % 4) return record_invalid("M must be positive and K a multiple of 4");
+    if (reinterpret_cast<uintptr_t>(dense_a) & 7u) return record_invalid("dense A must be 8-byte aligned");
+    const long long groups = (long long)M * K / 4;
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const long long want = (groups + kPackThreads - 1) / kPackThreads;
+    const unsigned blocks = (unsigned)(want < (long long)sms * 16 ? want : (long long)sms * 16);
+    prune_kernel<<<blocks, kPackThreads, 0, stream>>>(static_cast<uint16_t*>(dense_a), groups);
+    return cudaGetLastError();
+}
+
+extern "C" cudaError_t spmm24_pack_b_device(cudaStream_t stream, const void* b_rowmajor, int K, int N,
+                                            void* b_packed_out) {
+    using namespace spmm24;
+    clear_last_error();
+    if (!b_rowmajor || !b_packed_out) return record_invalid("null pointer");
+    if (K <= 0 || N <= 0 || K % 64) return record_invalid("K must be a positive multiple of 64");
+    if (misaligned16(b_packed_out)) return record_invalid("packed B must be 16-byte aligned");
+    if (reinterpret_cast<uintptr_t>(b_rowmajor) & 1u) return record_invalid("B must be 2-byte aligned");
+    if (K / kBTileRows > 65535) return record_invalid("K too large");
+    dim3 grid((unsigned)((N + kBTileCols - 1) / kBTileCols), (unsigned)(K / kBTileRows));
+    pack_b_kernel<<<grid, kPackThreads, 0, stream>>>(static_cast<const uint16_t*>(b_rowmajor), K, N,
+                                                     static_cast<uint16_t*>(b_packed_out));
+    return cudaGetLastError();
+}

@@ -19,17 +19,22 @@
 #include <utility>
 
 #include "spmm24/SpMM_API.h"
+#include "spmm24_host.h"
 #include "spmm24_kernel.cuh"
 
 namespace spmm24 {
-namespace {
 
 thread_local char g_last_error[256] = "";
 
-cudaError_t invalid(const char* why) {
+cudaError_t record_invalid(const char* why) {
     std::snprintf(g_last_error, sizeof(g_last_error), "%s", why);
     return cudaErrorInvalidValue;
 }
+void clear_last_error() { g_last_error[0] = '\0'; }
+
+namespace {
+
+cudaError_t invalid(const char* why) { return record_invalid(why); }
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,

@@ -49,6 +49,12 @@ _lib.spmm24_pack_b.argtypes = [_u16p, ctypes.c_int, ctypes.c_int, _u16p]
 _lib.spmm24_pack_b.restype = ctypes.c_int
 _lib.spmm24_prune_2of4.argtypes = [_u16p, ctypes.c_int, ctypes.c_int]
 _lib.spmm24_prune_2of4.restype = ctypes.c_int
+_lib.spmm24_pack_a_device.argtypes = [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp, _vp, _vp]
+_lib.spmm24_pack_a_device.restype = ctypes.c_int
+_lib.spmm24_prune_2of4_device.argtypes = [_vp, _vp, ctypes.c_int, ctypes.c_int]
+_lib.spmm24_prune_2of4_device.restype = ctypes.c_int
+_lib.spmm24_pack_b_device.argtypes = [_vp, _vp, ctypes.c_int, ctypes.c_int, _vp]
+_lib.spmm24_pack_b_device.restype = ctypes.c_int
 _lib.spmm24_workspace_bytes.argtypes = [ctypes.c_int] * 4
 _lib.spmm24_workspace_bytes.restype = ctypes.c_size_t
 _lib.spmm24_select_config.argtypes = [ctypes.c_int] * 4 + [ctypes.POINTER(SpmmConfig)]
@@ -153,6 +159,55 @@ def device_status(device: int = 0) -> int:
     if rc != CUDA_SUCCESS:
         raise SpmmError(rc, "spmm24_device_status")
     return int(v.value)
+
+
+# ------------------------------------------------------ device packer
+def pack_a_device(dense, M: int, K: int, prune: bool = False, values=None, meta=None, stream=None):
+    """spmm24_pack_a_device on a device tensor holding the dense M x K fp16
+    weights: optional magnitude 2:4 prune, compress and reordered metadata in
+    one kernel.  Returns (values (M*K/2 fp16 as int16 bits), metadata (M*K/16
+    u16 as int16), bad_rows (int)); synchronises the stream to read bad_rows."""
+    import torch
+
+    dev = dense.device
+    if values is None:
+        values = torch.empty(M * K // 2, dtype=torch.int16, device=dev)
+    if meta is None:
+        meta = torch.empty(M * K // 16, dtype=torch.int16, device=dev)
+    bad = torch.zeros(1, dtype=torch.int32, device=dev)
+    if stream is None:
+        stream = torch.cuda.current_stream(dev)
+    rc = _lib.spmm24_pack_a_device(_stream_handle(stream), _ptr(dense), M, K, 1 if prune else 0, _ptr(values),
+                                   _ptr(meta), _ptr(bad))
+    if rc != CUDA_SUCCESS:
+        raise SpmmError(rc, "spmm24_pack_a_device")
+    return values, meta, int(bad.item())
+
+
+def prune_2of4_device(dense, M: int, K: int, stream=None) -> None:
+    """spmm24_prune_2of4_device: in-place magnitude 2:4 prune of a device matrix."""
+    import torch
+
+    if stream is None:
+        stream = torch.cuda.current_stream(dense.device)
+    rc = _lib.spmm24_prune_2of4_device(_stream_handle(stream), _ptr(dense), M, K)
+    if rc != CUDA_SUCCESS:
+        raise SpmmError(rc, "spmm24_prune_2of4_device")
+
+
+def pack_b_device(b, K: int, N: int, out=None, stream=None):
+    """spmm24_pack_b_device: row-major K x N device fp16 -> packed strips
+    (ceil(N/8)*8*K halves, returned as int16 bits unless `out` is given)."""
+    import torch
+
+    if out is None:
+        out = torch.empty(((N + 7) // 8) * 8 * K, dtype=torch.int16, device=b.device)
+    if stream is None:
+        stream = torch.cuda.current_stream(b.device)
+    rc = _lib.spmm24_pack_b_device(_stream_handle(stream), _ptr(b), K, N, _ptr(out))
+    if rc != CUDA_SUCCESS:
+        raise SpmmError(rc, "spmm24_pack_b_device")
+    return out
 
 
 # ---------------------------------------------------------- sharding

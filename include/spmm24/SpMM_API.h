@@ -128,6 +128,30 @@ int spmm24_pack_b(const uint16_t* b_rowmajor, int K, int N, uint16_t* b_packed_o
  * its host prune/compress/metadata pipeline.  Returns 0, or -1 if K % 4. */
 int spmm24_prune_2of4(uint16_t* dense_a, int M, int K);
 
+/* On-device packer (no counterpart in the reference, whose packer runs on
+ * the host only): one pass over a dense row-major M x K fp16 matrix in
+ * device memory that optionally applies the magnitude 2:4 prune of
+ * spmm24_prune_2of4 (prune != 0), then writes the compressed values
+ * (M*K/2 halves) and the REORDERED metadata (M*K/16 u16) -- bit-exact with
+ * spmm24_prune_2of4 + spmm24_compress_reordered.  M % 16 == 0, K % 64 == 0;
+ * dense and values 16-byte aligned.  If bad_blocks (device int, optional)
+ * is given, the kernel adds 1 for every row of a 16x16 block holding a
+ * group of four with fewer than two zeros (the outputs of those rows are
+ * unspecified); the caller zeroes it first.  Asynchronous on `stream`. */
+cudaError_t spmm24_pack_a_device(cudaStream_t stream, const void* dense_a, int M, int K, int prune,
+                                 void* values_out, uint16_t* meta_out, int* bad_blocks);
+
+/* spmm24_prune_2of4 on a device matrix, in place (K % 4 == 0, 8-byte
+ * aligned).  Asynchronous on `stream`. */
+cudaError_t spmm24_prune_2of4_device(cudaStream_t stream, void* dense_a, int M, int K);
+
+/* spmm24_pack_b on the device: row-major K x N fp16 -> ceil(N/8) strips of
+ * K x 8 (pad columns zero), bit-exact with the host form; the producer of a
+ * layer's activations can pack them in place of toolPackMatrixB
+ * (test/utils.h:188-229).  K % 64 == 0, output 16-byte aligned.
+ * Asynchronous on `stream`. */
+cudaError_t spmm24_pack_b_device(cudaStream_t stream, const void* b_rowmajor, int K, int N, void* b_packed_out);
+
 /* Workspace the caller must pass as split_reduction: always 0 bytes (any
  * workspace is owned by the library, see spmm24_launch).
  * Replaces the Split_K*M*N halves contract of test/kernelTest.cu:136. */

@@ -78,6 +78,22 @@ def test_launch_rejects_bad_arguments_without_gpu():
     assert "aligned" in spmm24._lib.spmm24_last_error().decode()
 
 
+def test_device_packer_rejects_bad_arguments_without_gpu():
+    L = spmm24._lib
+    ok = 0x10000
+    assert L.spmm24_pack_a_device(None, 0, 256, 256, 1, ok, ok, None) == spmm24.CUDA_ERROR_INVALID_VALUE
+    assert "null" in L.spmm24_last_error().decode()
+    assert L.spmm24_pack_a_device(None, ok, 250, 256, 1, ok, ok, None) == spmm24.CUDA_ERROR_INVALID_VALUE  # M % 16
+    assert L.spmm24_pack_a_device(None, ok, 256, 96, 1, ok, ok, None) == spmm24.CUDA_ERROR_INVALID_VALUE   # K % 64
+    assert L.spmm24_pack_a_device(None, ok + 8, 256, 256, 1, ok, ok, None) == spmm24.CUDA_ERROR_INVALID_VALUE
+    assert "aligned" in L.spmm24_last_error().decode()
+    assert L.spmm24_prune_2of4_device(None, ok, 16, 6) == spmm24.CUDA_ERROR_INVALID_VALUE  # K % 4
+    assert L.spmm24_prune_2of4_device(None, ok + 4, 16, 8) == spmm24.CUDA_ERROR_INVALID_VALUE  # 8-byte alignment
+    assert L.spmm24_pack_b_device(None, ok, 96, 16, ok) == spmm24.CUDA_ERROR_INVALID_VALUE  # K % 64
+    assert L.spmm24_pack_b_device(None, ok, 64, 16, ok + 2) == spmm24.CUDA_ERROR_INVALID_VALUE  # output alignment
+    assert L.spmm24_pack_b_device(None, ok + 1, 64, 16, ok) == spmm24.CUDA_ERROR_INVALID_VALUE  # odd source
+
+
 def test_select_config_picks_tiles_and_splits():
     c = spmm24.select_config(4096, 16, 4096)
     assert c["tile_m"] == 128 and c["tile_n"] == 16 and c["stage_k"] == 128
