@@ -35,18 +35,19 @@ constexpr int kBTilePitch = kBTileCols + 8;
 // The kernels work on a group of four halves held in two 32-bit words
 // (x = h0 | h1 << 16, y = h2 | h3 << 16) with integer operations only.
 //
-// Magnitudes: for fp16 bit patterns, |x| orders like the 15-bit integer
-// h & 0x7fff, except that a NaN (above 0x7c00) compares false with
-// everything -- the host's float comparisons, reproduced exactly.
+// Magnitudes: for fp16 and bf16 bit patterns alike, |x| orders like the
+// 15-bit integer h & 0x7fff, except that a NaN (above the infinity pattern:
+// 0x7c00 for fp16, 0x7f80 for bf16) compares false with everything -- the
+// host's float comparisons, reproduced exactly.
 
 // Magnitude 2:4 prune of one group (packer.cpp spmm24_prune_2of4): keep the
 // largest |x| (first on ties), then the largest of the other three (first on
 // ties), replace the other two by +0.
 //
 // Sequential form, exact for NaN (a NaN never wins or loses a comparison).
-__device__ __forceinline__ uint32_t prune_keep_sequential(uint32_t ax, uint32_t ay) {
+__device__ __forceinline__ uint32_t prune_keep_sequential(uint32_t ax, uint32_t ay, uint32_t inf) {
     const uint32_t m0 = ax & 0xffffu, m1 = ax >> 16, m2 = ay & 0xffffu, m3 = ay >> 16;
-    const bool v0 = m0 <= 0x7c00u, v1 = m1 <= 0x7c00u, v2 = m2 <= 0x7c00u, v3 = m3 <= 0x7c00u;
+    const bool v0 = m0 <= inf, v1 = m1 <= inf, v2 = m2 <= inf, v3 = m3 <= inf;
     uint32_t k0 = 0, mk = m0;
     bool c = v0 && v1 && m1 > mk;
     k0 = c ? 1u : k0;
@@ -70,11 +71,12 @@ __device__ __forceinline__ uint32_t prune_keep_sequential(uint32_t ax, uint32_t 
     return (1u << k0) | (1u << k1);
 }
 
-__device__ __forceinline__ void prune_group(uint32_t& x, uint32_t& y) {
+// `inf`: the infinity bit pattern of the element type (0x7c00 fp16, 0x7f80 bf16).
+__device__ __forceinline__ void prune_group(uint32_t& x, uint32_t& y, uint32_t inf) {
     const uint32_t ax = x & 0x7fff7fffu, ay = y & 0x7fff7fffu;
     const uint32_t mx = __vmaxu2(ax, ay);
     uint32_t keep;
-    if (max(mx & 0xffffu, mx >> 16) <= 0x7c00u) {
+    if (max(mx & 0xffffu, mx >> 16) <= inf) {
         // No NaN: the sequential scan keeps the two largest of the unique keys
         // |x| << 2 | (3 - position) (equal magnitudes: the lower position wins).
         const uint32_t a0 = ((ax << 2) & 0x3fffcu) | 3u, a1 = ((ax >> 14) & 0x3fffcu) | 2u;
@@ -83,7 +85,7 @@ __device__ __forceinline__ void prune_group(uint32_t& x, uint32_t& y) {
         const uint32_t top = max(hi01, hi23), second = max(min(hi01, hi23), max(lo01, lo23));
         keep = (8u >> (top & 3u)) | (8u >> (second & 3u));
     } else {
-        keep = prune_keep_sequential(ax, ay);
+        keep = prune_keep_sequential(ax, ay, inf);
     }
     x &= (keep & 1u) * 0xffffu + (keep & 2u) * 0x7fff8000u;
     y &= ((keep >> 2) & 1u) * 0xffffu + ((keep >> 2) & 2u) * 0x7fff8000u;
@@ -157,7 +159,7 @@ __global__ void __launch_bounds__(kPackThreads) pack_a_kernel(const uint16_t* __
         bool ok = true;
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-            if (prune) prune_group(wx[k], wy[k]);
+            if (prune) prune_group(wx[k], wy[k], prune == 2 ? 0x7f80u : 0x7c00u);
             uint32_t idx;
             ok &= compress_group(wx[k], wy[k], &w[k], &idx);
             md |= idx << (4 * k);
@@ -174,11 +176,11 @@ __global__ void __launch_bounds__(kPackThreads) pack_a_kernel(const uint16_t* __
 }
 
 // In-place magnitude prune, one group of four per thread.
-__global__ void __launch_bounds__(kPackThreads) prune_kernel(uint16_t* __restrict__ a, long long groups) {
+__global__ void __launch_bounds__(kPackThreads) prune_kernel(uint16_t* __restrict__ a, long long groups, uint32_t inf) {
     for (long long g = blockIdx.x * (long long)kPackThreads + threadIdx.x; g < groups;
          g += (long long)gridDim.x * kPackThreads) {
         uint2 w = *reinterpret_cast<uint2*>(a + 4 * g);
-        prune_group(w.x, w.y);
+        prune_group(w.x, w.y, inf);
         *reinterpret_cast<uint2*>(a + 4 * g) = w;
     }
 }
@@ -234,13 +236,15 @@ extern "C" cudaError_t spmm24_pack_a_device(cudaStream_t stream, const void* den
     const int nbc = K / 16;
     dim3 grid((unsigned)((nbc + kTileBlocks - 1) / kTileBlocks), (unsigned)((M / 16 + kPackBands - 1) / kPackBands));
     if (grid.y > 65535) return record_invalid("M too large");
-    pack_a_kernel<<<grid, kPackThreads, 0, stream>>>(static_cast<const uint16_t*>(dense_a), M, K, prune ? 1 : 0,
+    if (prune < SPMM24_PRUNE_NONE || prune > SPMM24_PRUNE_BF16) return record_invalid("unknown prune mode");
+    pack_a_kernel<<<grid, kPackThreads, 0, stream>>>(static_cast<const uint16_t*>(dense_a), M, K, prune,
                                                      static_cast<uint16_t*>(values_out), meta_out, bad_blocks);
     return cudaGetLastError();
 }
 
-extern "C" cudaError_t spmm24_prune_2of4_device(cudaStream_t stream, void* dense_a, int M, int K) {
-    using namespace spmm24;
+namespace spmm24 {
+namespace {
+cudaError_t prune_device(cudaStream_t stream, void* dense_a, int M, int K, uint32_t inf) {
     clear_last_error();
     if (!dense_a) return record_invalid("null pointer");
     if (M <= 0 || K <= 0 || K % 4) return record_invalid("M must be positive and K a multiple of 4");
@@ -250,8 +254,18 @@ extern "C" cudaError_t spmm24_prune_2of4_device(cudaStream_t stream, void* dense
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const long long want = (groups + kPackThreads - 1) / kPackThreads;
     const unsigned blocks = (unsigned)(want < (long long)sms * 16 ? want : (long long)sms * 16);
-    prune_kernel<<<blocks, kPackThreads, 0, stream>>>(static_cast<uint16_t*>(dense_a), groups);
+    prune_kernel<<<blocks, kPackThreads, 0, stream>>>(static_cast<uint16_t*>(dense_a), groups, inf);
     return cudaGetLastError();
+}
+}  // namespace
+}  // namespace spmm24
+
+extern "C" cudaError_t spmm24_prune_2of4_device(cudaStream_t stream, void* dense_a, int M, int K) {
+    return spmm24::prune_device(stream, dense_a, M, K, 0x7c00u);
+}
+
+extern "C" cudaError_t spmm24_prune_2of4_bf16_device(cudaStream_t stream, void* dense_a, int M, int K) {
+    return spmm24::prune_device(stream, dense_a, M, K, 0x7f80u);
 }
 
 extern "C" cudaError_t spmm24_pack_b_device(cudaStream_t stream, const void* b_rowmajor, int K, int N,

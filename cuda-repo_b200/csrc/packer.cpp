@@ -132,14 +132,24 @@ extern "C" int spmm24_pack_b(const uint16_t* b, int K, int N, uint16_t* out) {
     return 0;
 }
 
-extern "C" int spmm24_prune_2of4(uint16_t* a, int M, int K) {
+namespace {
+
+inline float bf2f(uint16_t h) {
+    uint32_t u = (uint32_t)h << 16;
+    float f;
+    std::memcpy(&f, &u, 4);
+    return f;
+}
+
+template <float (*Decode)(uint16_t)>
+int prune_rows(uint16_t* a, int M, int K) {
     if (!a || M <= 0 || K <= 0 || K % 4) return -1;
     parallel_for(M, K, [&](int m0, int m1) {
         for (int m = m0; m < m1; ++m) {
             uint16_t* row = a + (size_t)m * K;
             for (int g = 0; g < K; g += 4) {
                 float v[4];
-                for (int i = 0; i < 4; ++i) v[i] = std::fabs(h2f(row[g + i]));
+                for (int i = 0; i < 4; ++i) v[i] = std::fabs(Decode(row[g + i]));
                 int k0 = 0;
                 for (int i = 1; i < 4; ++i)
                     if (v[i] > v[k0]) k0 = i;
@@ -155,6 +165,12 @@ extern "C" int spmm24_prune_2of4(uint16_t* a, int M, int K) {
     });
     return 0;
 }
+
+}  // namespace
+
+extern "C" int spmm24_prune_2of4(uint16_t* a, int M, int K) { return prune_rows<h2f>(a, M, K); }
+
+extern "C" int spmm24_prune_2of4_bf16(uint16_t* a, int M, int K) { return prune_rows<bf2f>(a, M, K); }
 
 // ------------------------------------------------- C++ reference drop-ins
 int toolCompressMatrixA(half* denseMatrixA, int Global_M, int Global_K, int Block_M, int Block_K,

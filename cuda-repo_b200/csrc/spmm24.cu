@@ -11,6 +11,7 @@
 #include <cuda_runtime.h>
 
 #include <atomic>
+#include <cmath>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -150,7 +151,7 @@ int cluster_smem(int tn) {
     }
 }
 
-Plan make_plan(int M, int N, int K, int split_k, int sms) {
+Plan make_plan(int M, int N, int K, int split_k, int sms, bool plain = true) {
     Plan p{};
     int tn = N <= 16 ? 16 : N <= 32 ? 32 : N <= 64 ? 64 : 128;
     const int forced = env_int("SPMM24_TILE_N", 0);  // tuning override (16/32/64/128/256)
@@ -170,7 +171,7 @@ Plan make_plan(int M, int N, int K, int split_k, int sms) {
 
     // Stream-K (tuning option only; the cluster path measured faster on the
     // decode shapes): one CTA per SM streaming an equal share of the stages.
-    if (env_int("SPMM24_PATH", 0) == 2 && split_k == 0 && tn <= 32 && units >= 2) {
+    if (plain && env_int("SPMM24_PATH", 0) == 2 && split_k == 0 && tn <= 32 && units >= 2) {
         p.path = Path::kStreamK;
         if (p.shallow) {
             p.stages = tn == 16 ? SV16s::kStages : SV32s::kStages;
@@ -277,10 +278,15 @@ cudaError_t get_workspace(int dev, cudaStream_t stream, size_t counters, size_t 
     return cudaSuccess;
 }
 
-std::atomic<uint64_t> g_attr_done[32];
+std::atomic<uint64_t> g_attr_done[64];  // per kernel variant: one bit per device
+
+// The plain SpMM: fp16, row-major C, no epilogue work.
+bool epilogue_plain_fp16(const Epilogue& e) {
+    return e.bias == nullptr && e.residual == nullptr && e.act == kActNone && e.alpha == 1.f && !e.packed && !e.bf16;
+}
 #ifdef SPMM24_TRACE
 std::atomic<long long> g_trace_next{0};  // next free CTA record in the trace buffer
-#endif  // per kernel variant: one bit per device
+#endif
 
 template <class Kern>
 cudaError_t prepare(Kern kern, int smem, int dev, int idx) {
@@ -325,11 +331,17 @@ cudaError_t launch_kernel(Kern kern, dim3 grid, int smem, cudaStream_t stream, u
 #endif
 }
 
+// Attribute-cache slots: variant index, plus kEpiSlot for the general-epilogue
+// instantiation of the same variant.
+constexpr int kEpiSlot = 32;
+
 template <class V>
 cudaError_t launch_cluster(const Plan& pl, cudaStream_t stream, int dev, bool pdl, const CUtensorMap& ta,
                            const CUtensorMap& tb, const CUtensorMap& te, const ClusterParams& kp, int idx) {
-    auto kern = spmm24_cluster_kernel<V::kTileN, V::kStages>;
-    cudaError_t e = prepare(kern, V::C_::SMEM_ALLOC, dev, idx);
+    const bool general = !epilogue_plain_fp16(kp.epi);
+    auto kern = general ? spmm24_cluster_kernel<V::kTileN, V::kStages, true>
+                        : spmm24_cluster_kernel<V::kTileN, V::kStages, false>;
+    cudaError_t e = prepare(kern, V::C_::SMEM_ALLOC, dev, idx + (general ? kEpiSlot : 0));
     if (e != cudaSuccess) return e;
     return launch_kernel(kern, dim3((unsigned)pl.split, (unsigned)pl.n_tiles, (unsigned)pl.m_tiles),
                          V::C_::SMEM_ALLOC, stream, (unsigned)pl.split, pdl, ta, tb, te, kp);
@@ -348,8 +360,9 @@ template <int HALF_N, int STAGES, bool SPLIT>
 cudaError_t launch_pair_v(const Plan& pl, cudaStream_t stream, int dev, bool pdl, const CUtensorMap& ta,
                           const CUtensorMap& tb, const CUtensorMap& te, const PairParams& kp, int idx) {
     using C_ = PairCfg<HALF_N, STAGES>;
-    auto kern = spmm24_pair_kernel<HALF_N, STAGES, SPLIT>;
-    cudaError_t e = prepare(kern, C_::SMEM_ALLOC, dev, idx);
+    const bool general = !epilogue_plain_fp16(kp.epi);
+    auto kern = general ? spmm24_pair_kernel<HALF_N, STAGES, SPLIT, true> : spmm24_pair_kernel<HALF_N, STAGES, SPLIT, false>;
+    cudaError_t e = prepare(kern, C_::SMEM_ALLOC, dev, idx + (general ? kEpiSlot : 0));
     if (e != cudaSuccess) return e;
     return launch_kernel(kern, dim3(2u, (unsigned)pl.n_tiles, (unsigned)pl.m_tiles), C_::SMEM_ALLOC, stream, 2u, pdl,
                          ta, tb, te, kp);
@@ -367,7 +380,7 @@ cudaError_t launch_pair(const Plan& pl, cudaStream_t stream, int dev, bool pdl, 
 size_t streamk_partial_bytes(const Plan& pl) { return (size_t)pl.grid * kTileM * pl.tile_n * sizeof(float); }
 
 cudaError_t launch_impl(cudaStream_t stream, const void* A, const void* B, const uint16_t* E, void* C, int M, int N,
-                        int K, int split_k, unsigned flags) {
+                        int K, int split_k, unsigned flags, const spmm24_epilogue* user_epi = nullptr) {
     g_last_error[0] = '\0';
     if (!A || !B || !E || !C) return invalid("null pointer");
     if (M <= 0 || N <= 0 || K <= 0) return invalid("M, N and K must be positive");
@@ -377,12 +390,31 @@ cudaError_t launch_impl(cudaStream_t stream, const void* A, const void* B, const
     if (((uintptr_t)A | (uintptr_t)B | (uintptr_t)E) & 15u) return invalid("A, B and metadata must be 16-byte aligned");
     if ((uintptr_t)C & 1u) return invalid("C must be 2-byte aligned");
     if ((long)M / kTileM >= 65535) return invalid("M too large");
-    if (flags & ~(unsigned)(SPMM24_STATIC_WEIGHTS | SPMM24_NO_PDL)) return invalid("unknown flag");
+    if (flags & ~(unsigned)(SPMM24_STATIC_WEIGHTS | SPMM24_NO_PDL | SPMM24_BF16)) return invalid("unknown flag");
+    Epilogue epi{nullptr, nullptr, 1.f, kActNone, 0, (flags & SPMM24_BF16) ? 1 : 0};
+    if (user_epi) {
+        if (user_epi->activation < SPMM24_ACT_NONE || user_epi->activation > SPMM24_ACT_GELU)
+            return invalid("unknown epilogue activation");
+        if (user_epi->out_layout != SPMM24_OUT_ROW_MAJOR && user_epi->out_layout != SPMM24_OUT_PACKED_B)
+            return invalid("unknown output layout");
+        if (!std::isfinite(user_epi->alpha)) return invalid("epilogue alpha must be finite");
+        epi.bias = static_cast<const uint16_t*>(user_epi->bias);
+        epi.residual = static_cast<const uint16_t*>(user_epi->residual);
+        epi.alpha = user_epi->alpha;
+        epi.act = user_epi->activation;
+        epi.packed = user_epi->out_layout == SPMM24_OUT_PACKED_B ? 1 : 0;
+        if ((uintptr_t)epi.bias & 1u) return invalid("bias must be 2-byte aligned");
+        if ((uintptr_t)epi.residual & 1u) return invalid("residual must be 2-byte aligned");
+        if (epi.packed && (((uintptr_t)C | (uintptr_t)epi.residual) & 15u))
+            return invalid("a packed C (and its residual) must be 16-byte aligned");
+    }
+    const bool plain = epi.bias == nullptr && epi.residual == nullptr && epi.act == kActNone && epi.alpha == 1.f &&
+                       !epi.packed && !epi.bf16;
 
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    Plan pl = make_plan(M, N, K, split_k, sm_count(dev));
+    Plan pl = make_plan(M, N, K, split_k, sm_count(dev), plain);
 
     uint32_t* ws_counters = nullptr;
     float* ws_partials = nullptr;
@@ -434,7 +466,8 @@ cudaError_t launch_impl(cudaStream_t stream, const void* A, const void* B, const
     const int wstatic = (flags & SPMM24_STATIC_WEIGHTS) ? 1 : 0;
     if (pl.path == Path::kPair) {
         PairParams kp;
-        kp.C = static_cast<__half*>(C);
+        kp.C = static_cast<uint16_t*>(C);
+        kp.epi = epi;
         kp.M = M;
         kp.N = N;
         kp.K = K;
@@ -465,7 +498,8 @@ cudaError_t launch_impl(cudaStream_t stream, const void* A, const void* B, const
         return launch_streamk<SV32>(pl, stream, dev, pdl, ta, tb, te, kp, 6);
     }
     ClusterParams kp;
-    kp.C = static_cast<__half*>(C);
+    kp.C = static_cast<uint16_t*>(C);
+    kp.epi = epi;
     kp.M = M;
     kp.N = N;
     kp.K = K;
@@ -639,6 +673,12 @@ extern "C" cudaError_t spmm24_launch_ex(cudaStream_t stream, const void* compres
 extern "C" cudaError_t spmm24_launch_noalloc(cudaStream_t stream, const void* compressed_a, const void* b_packed,
                                              const uint16_t* metadata, void* c, int M, int N, int K) {
     return spmm24::launch_noalloc_impl(stream, compressed_a, b_packed, metadata, c, M, N, K);
+}
+
+extern "C" cudaError_t spmm24_launch_fused(cudaStream_t stream, const void* compressed_a, const void* b_packed,
+                                           const uint16_t* metadata, void* c, int M, int N, int K, int split_k,
+                                           unsigned flags, const spmm24_epilogue* epilogue) {
+    return spmm24::launch_impl(stream, compressed_a, b_packed, metadata, c, M, N, K, split_k, flags, epilogue);
 }
 
 extern "C" size_t spmm24_workspace_bytes(int, int, int, int) { return 0; }

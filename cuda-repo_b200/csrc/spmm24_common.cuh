@@ -22,6 +22,7 @@
 //   out in shared memory with the same permutation of 16-K blocks -- the TMA
 //   boxes do it -- which leaves the sum over K unchanged.
 #pragma once
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cstdint>
 #include "ptx_sm100.cuh"
@@ -94,6 +95,8 @@ __host__ __device__ constexpr uint32_t make_idesc() {
     return (1u << 2) | (1u << 4) | (0u << 7) | (0u << 10) | (0u << 15) | (1u << 16) |
            ((uint32_t)(N_TILE >> 3) << 17) | ((uint32_t)(kTileM >> 4) << 24);
 }
+// Operand-format bits that turn an f16 descriptor into a bf16 one (A and B).
+constexpr uint32_t kIdescBf16 = (1u << 7) | (1u << 10);
 
 // The weight (A + metadata) half of one stage's loads.
 template <class C_>
@@ -130,9 +133,11 @@ __device__ __forceinline__ void patch_tail_metadata(uint8_t* st, int lane) {
 }
 
 // Metadata copy + the four sparse MMAs of one stage (single thread).
+// `fmt` is 0 (f16 operands) or kIdescBf16.
 template <class C_, int N_TILE>
-__device__ __forceinline__ void mma_stage(uint32_t st_addr, uint32_t meta_col, uint32_t d_tmem, uint32_t& accumulate) {
-    constexpr uint32_t idesc = make_idesc<N_TILE>();
+__device__ __forceinline__ void mma_stage(uint32_t st_addr, uint32_t meta_col, uint32_t d_tmem, uint32_t& accumulate,
+                                          uint32_t fmt) {
+    const uint32_t idesc = make_idesc<N_TILE>() | fmt;
     const uint32_t stB = st_addr + C_::A_BYTES;
     const uint32_t stE = stB + C_::B_BYTES;
     ptx::tmem_cp_128x128b(meta_col, smem_desc(stE, 0, 128));
@@ -142,6 +147,136 @@ __device__ __forceinline__ void mma_stage(uint32_t st_addr, uint32_t meta_col, u
         const uint64_t bdesc = smem_desc(stB + j * 512, 128, 2048);
         ptx::mma_sp_f16(d_tmem, adesc, bdesc, meta_col + (j & 2), idesc | (uint32_t)(j & 1), accumulate);
         accumulate = 1;
+    }
+}
+
+// ------------------------------------------------------------ epilogue
+// Applied after the split-K reduction, before the output is rounded:
+//   y = act(alpha * acc + bias[m]) + residual[m, n]
+// stored in C's element type and layout.  Row-major C is M x N; the packed
+// layout is the next layer's packed B: ceil(N/8) strips of M x 8 (element
+// (m, n) at ((n / 8) * M + m) * 8 + n % 8, pad columns zero).
+constexpr int kActNone = 0, kActRelu = 1, kActSilu = 2, kActGelu = 3;
+
+struct Epilogue {
+    const uint16_t* bias;      // M values in C's type, or null
+    const uint16_t* residual;  // same type and layout as C, or null
+    float alpha;               // accumulator scale
+    int act;                   // kAct*
+    int packed;                // 1: C (and residual) in packed-B strips
+    int bf16;                  // 1: A, B, C, bias and residual are bf16; 0: fp16
+};
+
+__device__ __forceinline__ float elem_to_f32(uint16_t h, int bf16) {
+    if (bf16) return __uint_as_float((uint32_t)h << 16);
+    __half_raw r;
+    r.x = h;
+    return __half2float(__half(r));
+}
+
+__device__ __forceinline__ uint16_t f32_to_elem(float v, int bf16) {
+    if (bf16) {
+        const __nv_bfloat16 b = __float2bfloat16_rn(v);
+        return static_cast<__nv_bfloat16_raw>(b).x;
+    }
+    const __half h = __float2half_rn(v);
+    return static_cast<__half_raw>(h).x;
+}
+
+// ReLU; SiLU y * sigmoid(y); GELU in its tanh form (Hendrycks & Gimpel,
+// 2016): 0.5 y (1 + tanh(sqrt(2 / pi) (y + 0.044715 y^3))).
+__device__ __forceinline__ float activate(float y, int act) {
+    if (act == kActRelu) return fmaxf(y, 0.f);
+    if (act == kActSilu) return y / (1.f + expf(-y));
+    if (act == kActGelu) return 0.5f * y * (1.f + tanhf(0.7978845608028654f * (y + 0.044715f * y * y * y)));
+    return y;
+}
+
+// Element offset of (m, n) in C's layout.
+__device__ __forceinline__ size_t c_offset(const Epilogue& e, int m, int n, int M, int N) {
+    return e.packed ? ((((size_t)(n >> 3) * M + m) << 3) + (n & 7)) : ((size_t)m * N + n);
+}
+
+// True when the epilogue only rounds (the plain SpMM): the kernels then take
+// a short path with no per-element epilogue work.
+__device__ __forceinline__ bool epilogue_is_plain(const Epilogue& e) {
+    return e.bias == nullptr && e.residual == nullptr && e.act == kActNone && e.alpha == 1.f;
+}
+
+// Rounds 8 values to C's type; columns at or past N (lim) become zero.
+__device__ __forceinline__ void round8(const float* y, int lim, int bf16, uint32_t* w) {
+    if (bf16) {
+#pragma unroll
+        for (int i = 0; i < 8; i += 2)
+            w[i >> 1] = (i < lim ? (uint32_t)f32_to_elem(y[i], 1) : 0u) |
+                        ((i + 1 < lim ? (uint32_t)f32_to_elem(y[i + 1], 1) : 0u) << 16);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; i += 2)
+            w[i >> 1] = (i < lim ? (uint32_t)f32_to_elem(y[i], 0) : 0u) |
+                        ((i + 1 < lim ? (uint32_t)f32_to_elem(y[i + 1], 0) : 0u) << 16);
+    }
+}
+
+// Epilogue of 8 consecutive columns gn..gn+7 (gn % 8 == 0) of row gm < M:
+// returns the 8 output elements packed in four words (columns at or past N
+// are zero).  `vec_rowmajor`: 16-byte accesses allowed for a row-major
+// residual (N % 8 == 0 and 16-byte aligned); a packed residual is always
+// read as whole 16-byte strip rows.  Each optional stage sits behind one
+// uniform branch, so an unused stage costs nothing.
+__device__ __forceinline__ void epilogue8(const float* v, const Epilogue& e, int gm, int gn, int M, int N,
+                                          bool vec_rowmajor, uint32_t* w) {
+    const int lim = min(8, N - gn);
+    float y[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) y[i] = v[i];
+    if (e.alpha != 1.f) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) y[i] *= e.alpha;
+    }
+    if (e.bias) {
+        const float b = elem_to_f32(e.bias[gm], e.bf16);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) y[i] += b;
+    }
+    if (e.act == kActRelu) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) y[i] = fmaxf(y[i], 0.f);
+    } else if (e.act == kActSilu) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) y[i] = activate(y[i], kActSilu);
+    } else if (e.act == kActGelu) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) y[i] = activate(y[i], kActGelu);
+    }
+    if (e.residual) {
+        const size_t base = c_offset(e, gm, gn, M, N);
+        if (e.packed || vec_rowmajor) {
+            const uint4 q = *reinterpret_cast<const uint4*>(e.residual + base);
+            const uint32_t x[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+            for (int i = 0; i < 8; ++i) y[i] += elem_to_f32((uint16_t)(x[i >> 1] >> (16 * (i & 1))), e.bf16);
+        } else {
+            for (int i = 0; i < lim; ++i) y[i] += elem_to_f32(e.residual[base + i], e.bf16);
+        }
+    }
+    round8(y, lim, e.bf16, w);
+}
+
+// Epilogue + the store into C of 8 columns of row gm < M (gn < N).  A packed
+// C is always written as whole 16-byte strip rows.  `plain`: the caller's
+// epilogue_is_plain(e), evaluated once per kernel.
+__device__ __forceinline__ void epilogue_store8(uint16_t* C, const float* v, const Epilogue& e, int gm, int gn, int M,
+                                                int N, bool vec_rowmajor, bool plain) {
+    const int lim = min(8, N - gn);
+    uint32_t w[4];
+    if (plain) round8(v, lim, e.bf16, w);
+    else epilogue8(v, e, gm, gn, M, N, vec_rowmajor, w);
+    const size_t base = c_offset(e, gm, gn, M, N);
+    if (e.packed || vec_rowmajor) {
+        *reinterpret_cast<uint4*>(C + base) = make_uint4(w[0], w[1], w[2], w[3]);
+    } else {
+        for (int i = 0; i < lim; ++i) C[base + i] = (uint16_t)(w[i >> 1] >> (16 * (i & 1)));
     }
 }
 

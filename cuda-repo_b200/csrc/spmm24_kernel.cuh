@@ -45,20 +45,22 @@ constexpr uint32_t kBarEpi = 1;   // named barrier: epilogue warps
 constexpr uint32_t kBarTmem = 2;  // named barrier: warps 1..5 after TMEM allocation
 
 struct ClusterParams {
-    __half* C;
+    uint16_t* C;  // fp16 or bf16 elements (epi.bf16), row-major or packed (epi.packed)
     int M, N, K;
     int groups;        // K / 64
     int stages_total;  // ceil(groups / 2)
     int split;         // CTAs per cluster along K
     int weights_static;
+    Epilogue epi;
     SPMM24_TRACE_FIELD
 };
 
 struct PairParams {
-    __half* C;
+    uint16_t* C;  // fp16 or bf16 elements (epi.bf16), row-major or packed (epi.packed)
     int M, N, K;
     int stages_total;  // K / 128 (the pair kernel requires K % 128 == 0)
     int weights_static;
+    Epilogue epi;
     SPMM24_TRACE_FIELD
 };
 
@@ -100,7 +102,11 @@ struct ClusterCfg : Cfg<N_TILE, STAGES, 1> {
     static_assert(CTAS_PER_SM * B_::TMEM_COLS <= 512, "co-resident CTAs must fit in TMEM together");
 };
 
-template <int N_TILE, int STAGES>
+// EPI: the general epilogue (bias, activation, residual, alpha, bf16, packed
+// output).  The plain fp16 row-major SpMM is a separate instantiation
+// without it: the epilogue runs on the critical path at the end of every
+// tile, and its extra code measurably slows the plain kernel.
+template <int N_TILE, int STAGES, bool EPI>
 __global__ void __launch_bounds__(kThreads, ClusterCfg<N_TILE, STAGES>::CTAS_PER_SM)
 spmm24_cluster_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const __grid_constant__ CUtensorMap tmE, const ClusterParams p) {
@@ -212,7 +218,7 @@ spmm24_cluster_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_cons
             if (2 * (st_begin + it) + 1 >= p.groups) patch_tail_metadata<C_>(smem + s * C_::STAGE_BYTES, lane);
             if (lane == 0) {
                 mma_stage<C_, N_TILE>(smem_base + s * C_::STAGE_BYTES, tmem_base + C_::META_COL + 4 * s, tmem_base,
-                                      accumulate);
+                                      accumulate, (EPI && p.epi.bf16) ? kIdescBf16 : 0u);
                 ptx::tc_commit(&empty[s]);
             }
             __syncwarp();
@@ -276,15 +282,18 @@ spmm24_cluster_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_cons
     if (epi) {
         ptx::grid_dep_wait();  // C may be read or written by the previous grid
         // Owner side: sum the S partial copies of this CTA's rows in a fixed
-        // order, round to fp16 and store with 16-byte coalesced writes.
+        // order, apply the epilogue, round and store with 16-byte coalesced
+        // writes (row-major C: consecutive threads take consecutive column
+        // chunks of a row; packed C: consecutive rows of a strip).
         const int nrows = my_end - my_start;
         constexpr int CHUNKS = N_TILE / 8;
         const int m0 = m_tile * kTileM;
         const int n0 = n_tile * N_TILE;
         const bool vec_ok = (p.N % 8 == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15u) == 0);
+        const bool packed = EPI && p.epi.packed;
         for (int w = threadIdx.x - 64; w < nrows * CHUNKS; w += kEpiThreads) {
-            const int lr = w / CHUNKS;
-            const int ch = w % CHUNKS;
+            const int lr = packed ? w % nrows : w / CHUNKS;
+            const int ch = packed ? w / nrows : w % CHUNKS;
             float acc[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) acc[e] = 0.f;
@@ -298,7 +307,10 @@ spmm24_cluster_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_cons
             const int gm = m0 + my_start + lr;
             const int gn = n0 + ch * 8;
             if (gm >= p.M || gn >= p.N) continue;
-            store_h8(p.C + (size_t)gm * p.N + gn, acc, vec_ok, p.N - gn);
+            if constexpr (EPI)
+                epilogue_store8(p.C, acc, p.epi, gm, gn, p.M, p.N, vec_ok, epilogue_is_plain(p.epi));
+            else
+                store_h8(reinterpret_cast<__half*>(p.C) + (size_t)gm * p.N + gn, acc, vec_ok, p.N - gn);
         }
     }
 
@@ -357,7 +369,8 @@ __host__ __device__ constexpr uint32_t pair_idesc() {
 
 // SPLIT_ISSUE: warp 0 issues the A and metadata loads and warp 2 the B loads
 // (before it joins the epilogue), so two threads of the CTA keep TMA busy.
-template <int HALF_N, int STAGES, bool SPLIT_ISSUE>
+// EPI: the general epilogue, as for spmm24_cluster_kernel.
+template <int HALF_N, int STAGES, bool SPLIT_ISSUE, bool EPI>
 __global__ void __launch_bounds__(kThreads, PairCfg<HALF_N, STAGES>::CTAS_PER_SM)
 spmm24_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmE, const PairParams p) {
@@ -451,7 +464,7 @@ spmm24_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
         __syncwarp();
     } else if (warp == 1 && leader) {
         // ---------------------------------- MMA issuer (leader CTA only)
-        constexpr uint32_t idesc = pair_idesc<C_::TILE_N>();
+        const uint32_t idesc = pair_idesc<C_::TILE_N>() | ((EPI && p.epi.bf16) ? kIdescBf16 : 0u);
         const uint32_t smem_base = ptx::smem_u32(smem);
         uint32_t accumulate = 0;
         for (int it = 0; it < st_count; ++it) {
@@ -509,42 +522,113 @@ spmm24_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
         __syncwarp();
         const int quad = warp & 3;
         const int row = quad * 32 + lane;
-        // Stage the fp16 tile in the (now idle) ring: rows are bank-shifted
-        // by 16 bytes so the per-row writes do not collide.
-        __half* cst = reinterpret_cast<__half*>(smem);
+        if constexpr (!EPI) {
+            // Plain fp16 row-major: stage the rounded tile in the (now idle)
+            // ring -- rows bank-shifted by 16 bytes so the per-row writes do
+            // not collide -- then copy it out with coalesced 16-byte stores.
+            __half* cst = reinterpret_cast<__half*>(smem);
 #pragma unroll 1
-        for (int c = 0; c < C_::TILE_N / 16; ++c) {
-            uint32_t v[16];
-            ptx::tmem_ld_32x32b_x16(tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(c * 16), v);
-            ptx::tmem_wait_ld();
-            __align__(16) __half h[16];
+            for (int c = 0; c < C_::TILE_N / 16; ++c) {
+                uint32_t v[16];
+                ptx::tmem_ld_32x32b_x16(tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(c * 16), v);
+                ptx::tmem_wait_ld();
+                __align__(16) __half h[16];
 #pragma unroll
-            for (int e = 0; e < 16; ++e) h[e] = __float2half_rn(__uint_as_float(v[e]));
-            uint4* dst = reinterpret_cast<uint4*>(cst + (size_t)row * C_::C_PITCH + c * 16);
-            dst[0] = reinterpret_cast<const uint4*>(h)[0];
-            dst[1] = reinterpret_cast<const uint4*>(h)[1];
-        }
-        ptx::tc_fence_before();
-        ptx::named_barrier(kBarEpi, kEpiThreads);
-        ptx::grid_dep_wait();  // C may be in use by the previous grid
-        // Coalesced copy-out: LPR threads cover one row with 16-byte chunks.
-        constexpr int LPR = C_::TILE_N / 8;
-        constexpr int RPP = kEpiThreads / LPR;  // rows per pass
-        const int etid = threadIdx.x - 64;
-        const int chunk = etid % LPR;
-        const int gm0 = m_tile * C_::TILE_M + (int)rank * kTileM;
-        const int gn = n_tile * C_::TILE_N + chunk * 8;
-        const bool vec_ok = (p.N % 8 == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15u) == 0);
-        for (int r = etid / LPR; r < kTileM; r += RPP) {
-            const int gm = gm0 + r;
-            if (gm >= p.M || gn >= p.N) continue;
-            const __half* src = cst + (size_t)r * C_::C_PITCH + chunk * 8;
-            __half* out = p.C + (size_t)gm * p.N + gn;
-            if (vec_ok) {
-                *reinterpret_cast<uint4*>(out) = *reinterpret_cast<const uint4*>(src);
+                for (int e = 0; e < 16; ++e) h[e] = __float2half_rn(__uint_as_float(v[e]));
+                uint4* dst = reinterpret_cast<uint4*>(cst + (size_t)row * C_::C_PITCH + c * 16);
+                dst[0] = reinterpret_cast<const uint4*>(h)[0];
+                dst[1] = reinterpret_cast<const uint4*>(h)[1];
+            }
+            ptx::tc_fence_before();
+            ptx::named_barrier(kBarEpi, kEpiThreads);
+            ptx::grid_dep_wait();  // C may be in use by the previous grid
+            constexpr int LPR = C_::TILE_N / 8;     // threads per row (16-byte chunks)
+            constexpr int RPP = kEpiThreads / LPR;  // rows per pass
+            const int etid = threadIdx.x - 64;
+            const int chunk = etid % LPR;
+            const int gm0 = m_tile * C_::TILE_M + (int)rank * kTileM;
+            const int gn = n_tile * C_::TILE_N + chunk * 8;
+            const bool vec_ok = (p.N % 8 == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15u) == 0);
+            for (int r = etid / LPR; r < kTileM; r += RPP) {
+                const int gm = gm0 + r;
+                if (gm >= p.M || gn >= p.N) continue;
+                const __half* src = cst + (size_t)r * C_::C_PITCH + chunk * 8;
+                __half* out = reinterpret_cast<__half*>(p.C) + (size_t)gm * p.N + gn;
+                if (vec_ok) {
+                    *reinterpret_cast<uint4*>(out) = *reinterpret_cast<const uint4*>(src);
+                } else {
+                    const int lim = min(8, p.N - gn);
+                    for (int e = 0; e < lim; ++e) out[e] = src[e];
+                }
+            }
+        } else {
+            const int gm0 = m_tile * C_::TILE_M + (int)rank * kTileM;
+            const int gn0 = n_tile * C_::TILE_N;
+            const bool vec_ok = (p.N % 8 == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15u) == 0);
+            const bool vec_res = (p.N % 8 == 0) && ((reinterpret_cast<uintptr_t>(p.epi.residual) & 15u) == 0);
+            const bool plain = epilogue_is_plain(p.epi);
+            // The bias and the residual may be written by the previous grid.
+            if (!plain) ptx::grid_dep_wait();
+            // Stage the output tile (C's element type) in the (now idle) ring,
+            // after the epilogue: rows are bank-shifted by 16 bytes so the
+            // per-row writes do not collide.
+            uint16_t* cst = reinterpret_cast<uint16_t*>(smem);
+    #pragma unroll 1
+            for (int c = 0; c < C_::TILE_N / 16; ++c) {
+                uint32_t v[16];
+                ptx::tmem_ld_32x32b_x16(tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(c * 16), v);
+                ptx::tmem_wait_ld();
+                uint32_t h[8];
+                const int gm = gm0 + row, gn = gn0 + c * 16;
+                float f[16];
+    #pragma unroll
+                for (int e = 0; e < 16; ++e) f[e] = __uint_as_float(v[e]);
+                if (plain || gm >= p.M || gn >= p.N) {
+                    // columns at or past N become zero (pad columns of a packed C)
+                    round8(f, max(0, min(8, p.N - gn)), p.epi.bf16, h);
+                    round8(f + 8, max(0, min(8, p.N - gn - 8)), p.epi.bf16, h + 4);
+                } else {
+                    epilogue8(f, p.epi, gm, gn, p.M, p.N, vec_res, h);
+                    if (gn + 8 < p.N) epilogue8(f + 8, p.epi, gm, gn + 8, p.M, p.N, vec_res, h + 4);
+                    else h[4] = h[5] = h[6] = h[7] = 0u;
+                }
+                uint4* dst = reinterpret_cast<uint4*>(cst + (size_t)row * C_::C_PITCH + c * 16);
+                dst[0] = make_uint4(h[0], h[1], h[2], h[3]);
+                dst[1] = make_uint4(h[4], h[5], h[6], h[7]);
+            }
+            ptx::tc_fence_before();
+            ptx::named_barrier(kBarEpi, kEpiThreads);
+            ptx::grid_dep_wait();  // C may be in use by the previous grid
+            const int etid = threadIdx.x - 64;
+            if (p.epi.packed) {
+                // One 16-byte strip row per thread; consecutive threads take
+                // consecutive rows of a strip (contiguous in the packed layout).
+                const int strips = (p.N + 7) / 8;
+                for (int idx = etid; idx < kTileM * (C_::TILE_N / 8); idx += kEpiThreads) {
+                    const int ch = idx / kTileM, r = idx % kTileM;
+                    const int gm = gm0 + r, strip = gn0 / 8 + ch;
+                    if (gm >= p.M || strip >= strips) continue;
+                    *reinterpret_cast<uint4*>(p.C + ((size_t)strip * p.M + gm) * 8) =
+                        *reinterpret_cast<const uint4*>(cst + (size_t)r * C_::C_PITCH + ch * 8);
+                }
             } else {
-                const int lim = min(8, p.N - gn);
-                for (int e = 0; e < lim; ++e) out[e] = src[e];
+                // Coalesced copy-out: LPR threads cover one row with 16-byte chunks.
+                constexpr int LPR = C_::TILE_N / 8;
+                constexpr int RPP = kEpiThreads / LPR;  // rows per pass
+                const int chunk = etid % LPR;
+                const int gn = gn0 + chunk * 8;
+                for (int r = etid / LPR; r < kTileM; r += RPP) {
+                    const int gm = gm0 + r;
+                    if (gm >= p.M || gn >= p.N) continue;
+                    const uint16_t* src = cst + (size_t)r * C_::C_PITCH + chunk * 8;
+                    uint16_t* out = p.C + (size_t)gm * p.N + gn;
+                    if (vec_ok) {
+                        *reinterpret_cast<uint4*>(out) = *reinterpret_cast<const uint4*>(src);
+                    } else {
+                        const int lim = min(8, p.N - gn);
+                        for (int e = 0; e < lim; ++e) out[e] = src[e];
+                    }
+                }
             }
         }
     }
@@ -700,7 +784,7 @@ spmm24_streamk_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_cons
                 if (2 * (int)(u % SPT) + 1 >= p.groups) patch_tail_metadata<C_>(smem + s * C_::STAGE_BYTES, lane);
                 if (lane == 0) {
                     mma_stage<C_, N_TILE>(smem_base + s * C_::STAGE_BYTES, tmem_base + C_::META_COL + 4 * s,
-                                          tmem_base + (uint32_t)(b * N_TILE), accumulate);
+                                          tmem_base + (uint32_t)(b * N_TILE), accumulate, 0u);
                     ptx::tc_commit(&empty[s]);
                 }
                 __syncwarp();

@@ -49,6 +49,19 @@ _lib.spmm24_pack_b.argtypes = [_u16p, ctypes.c_int, ctypes.c_int, _u16p]
 _lib.spmm24_pack_b.restype = ctypes.c_int
 _lib.spmm24_prune_2of4.argtypes = [_u16p, ctypes.c_int, ctypes.c_int]
 _lib.spmm24_prune_2of4.restype = ctypes.c_int
+class Epilogue(ctypes.Structure):
+    """spmm24_epilogue (include/spmm24/SpMM_API.h)."""
+    _fields_ = [("bias", ctypes.c_void_p), ("residual", ctypes.c_void_p), ("alpha", ctypes.c_float),
+                ("activation", ctypes.c_int), ("out_layout", ctypes.c_int)]
+
+
+_lib.spmm24_launch_fused.argtypes = [_vp, _vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                     ctypes.c_uint, ctypes.POINTER(Epilogue)]
+_lib.spmm24_launch_fused.restype = ctypes.c_int
+_lib.spmm24_prune_2of4_bf16.argtypes = [_u16p, ctypes.c_int, ctypes.c_int]
+_lib.spmm24_prune_2of4_bf16.restype = ctypes.c_int
+_lib.spmm24_prune_2of4_bf16_device.argtypes = [_vp, _vp, ctypes.c_int, ctypes.c_int]
+_lib.spmm24_prune_2of4_bf16_device.restype = ctypes.c_int
 _lib.spmm24_pack_a_device.argtypes = [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp, _vp, _vp]
 _lib.spmm24_pack_a_device.restype = ctypes.c_int
 _lib.spmm24_prune_2of4_device.argtypes = [_vp, _vp, ctypes.c_int, ctypes.c_int]
@@ -70,6 +83,10 @@ CUDA_SUCCESS = 0
 CUDA_ERROR_INVALID_VALUE = 1
 STATIC_WEIGHTS = 1  # SPMM24_STATIC_WEIGHTS
 NO_PDL = 2          # SPMM24_NO_PDL
+BF16 = 4            # SPMM24_BF16
+ACT_NONE, ACT_RELU, ACT_SILU, ACT_GELU = 0, 1, 2, 3   # SPMM24_ACT_*
+OUT_ROW_MAJOR, OUT_PACKED_B = 0, 1                    # SPMM24_OUT_*
+PRUNE_NONE, PRUNE_F16, PRUNE_BF16 = 0, 1, 2           # SPMM24_PRUNE_*
 
 
 class SpmmError(RuntimeError):
@@ -119,6 +136,17 @@ def launch_ex(stream, compressed_a, b_packed, metadata, c, M: int, N: int, K: in
                                  M, N, K, split_k, flags)
 
 
+def launch_fused(stream, compressed_a, b_packed, metadata, c, M: int, N: int, K: int, split_k: int = 0,
+                 flags: int = 0, bias=None, residual=None, alpha: float = 1.0, activation: int = ACT_NONE,
+                 out_layout: int = OUT_ROW_MAJOR) -> int:
+    """spmm24_launch_fused: C = act(alpha * A_sparse B + bias) + residual, in
+    C's layout (row-major or the next layer's packed B); returns the
+    cudaError_t code."""
+    epi = Epilogue(_ptr(bias), _ptr(residual), float(alpha), int(activation), int(out_layout))
+    return _lib.spmm24_launch_fused(_stream_handle(stream), _ptr(compressed_a), _ptr(b_packed), _ptr(metadata),
+                                    _ptr(c), M, N, K, split_k, flags, ctypes.byref(epi))
+
+
 def SpMM_N2M4_Launch(stream, Compressed_A, B, metadata, C, M_Global: int, N_Global: int, K_Global: int,
                      Split_Reduction=None, Split_K: int = 1) -> int:
     """The reference's launcher signature (src/SpMM_API.cu:61-70)."""
@@ -162,10 +190,10 @@ def device_status(device: int = 0) -> int:
 
 
 # ------------------------------------------------------ device packer
-def pack_a_device(dense, M: int, K: int, prune: bool = False, values=None, meta=None, stream=None):
+def pack_a_device(dense, M: int, K: int, prune=False, values=None, meta=None, stream=None):
     """spmm24_pack_a_device on a device tensor holding the dense M x K fp16
-    weights: optional magnitude 2:4 prune, compress and reordered metadata in
-    one kernel.  Returns (values (M*K/2 fp16 as int16 bits), metadata (M*K/16
+    (or bf16) weights: optional magnitude 2:4 prune (True / PRUNE_F16, or
+    PRUNE_BF16), compress and reordered metadata in one kernel.  Returns (values (M*K/2 fp16 as int16 bits), metadata (M*K/16
     u16 as int16), bad_rows (int)); synchronises the stream to read bad_rows."""
     import torch
 
@@ -177,20 +205,23 @@ def pack_a_device(dense, M: int, K: int, prune: bool = False, values=None, meta=
     bad = torch.zeros(1, dtype=torch.int32, device=dev)
     if stream is None:
         stream = torch.cuda.current_stream(dev)
-    rc = _lib.spmm24_pack_a_device(_stream_handle(stream), _ptr(dense), M, K, 1 if prune else 0, _ptr(values),
+    mode = int(prune) if not isinstance(prune, bool) else (PRUNE_F16 if prune else PRUNE_NONE)
+    rc = _lib.spmm24_pack_a_device(_stream_handle(stream), _ptr(dense), M, K, mode, _ptr(values),
                                    _ptr(meta), _ptr(bad))
     if rc != CUDA_SUCCESS:
         raise SpmmError(rc, "spmm24_pack_a_device")
     return values, meta, int(bad.item())
 
 
-def prune_2of4_device(dense, M: int, K: int, stream=None) -> None:
-    """spmm24_prune_2of4_device: in-place magnitude 2:4 prune of a device matrix."""
+def prune_2of4_device(dense, M: int, K: int, stream=None, bf16: bool = False) -> None:
+    """spmm24_prune_2of4_device (bf16: spmm24_prune_2of4_bf16_device):
+    in-place magnitude 2:4 prune of a device matrix."""
     import torch
 
     if stream is None:
         stream = torch.cuda.current_stream(dense.device)
-    rc = _lib.spmm24_prune_2of4_device(_stream_handle(stream), _ptr(dense), M, K)
+    fn = _lib.spmm24_prune_2of4_bf16_device if bf16 else _lib.spmm24_prune_2of4_device
+    rc = fn(_stream_handle(stream), _ptr(dense), M, K)
     if rc != CUDA_SUCCESS:
         raise SpmmError(rc, "spmm24_prune_2of4_device")
 
@@ -291,6 +322,14 @@ def prune_2of4(dense_a: np.ndarray, M: int, K: int) -> np.ndarray:
     a = _u16(dense_a).reshape(-1).copy()
     if _lib.spmm24_prune_2of4(_p(a), M, K) != 0:
         raise ValueError("prune_2of4: K % 4 must be 0")
+    return a
+
+
+def prune_2of4_bf16(dense_a: np.ndarray, M: int, K: int) -> np.ndarray:
+    """Magnitude 2:4 pruning along K of bf16 bit patterns (returns a pruned copy)."""
+    a = _u16(dense_a).reshape(-1).copy()
+    if _lib.spmm24_prune_2of4_bf16(_p(a), M, K) != 0:
+        raise ValueError("prune_2of4_bf16: K % 4 must be 0")
     return a
 
 

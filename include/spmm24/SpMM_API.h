@@ -70,13 +70,52 @@ enum {
      * (the activations B are still read only after it). */
     SPMM24_STATIC_WEIGHTS = 1u,
     /* Launch without programmatic stream serialization. */
-    SPMM24_NO_PDL = 2u
+    SPMM24_NO_PDL = 2u,
+    /* A, B and C (and the epilogue's bias and residual) hold bf16 instead of
+     * fp16; same layouts (the packer's formats are type-agnostic, prune with
+     * spmm24_prune_2of4_bf16 or SPMM24_PRUNE_BF16).  fp32 accumulation. */
+    SPMM24_BF16 = 4u
 };
 
 /* spmm24_launch with flags (no split_reduction argument).  Same contract
  * otherwise; unknown flag bits give cudaErrorInvalidValue. */
 cudaError_t spmm24_launch_ex(cudaStream_t stream, const void* compressed_a, const void* b_packed,
                              const uint16_t* metadata, void* c, int M, int N, int K, int split_k, unsigned flags);
+
+/* Epilogue of spmm24_launch_fused (no counterpart in the reference, whose
+ * epilogue only rounds to fp16, src/LoadAndStore.cuh:385-429).  Applied
+ * after the split-K reduction, before the output is rounded:
+ *     C[m, n] = act(alpha * acc[m, n] + bias[m]) + residual[m, n]
+ * bias: M elements of C's type (per output row = per output feature of the
+ * layer), or NULL.  residual: C's type and layout, or NULL (it may be C
+ * itself: each element is read before it is written).  */
+enum {
+    SPMM24_ACT_NONE = 0,
+    SPMM24_ACT_RELU = 1,
+    SPMM24_ACT_SILU = 2, /* y * sigmoid(y) */
+    SPMM24_ACT_GELU = 3  /* tanh form: 0.5 y (1 + tanh(sqrt(2/pi) (y + 0.044715 y^3))) */
+};
+enum {
+    SPMM24_OUT_ROW_MAJOR = 0, /* C is M x N row-major */
+    /* C is written as the next layer's packed B (toolPackMatrixB's layout,
+     * test/utils.h:188-229, with K' = M): ceil(N/8) strips of M x 8, element
+     * (m, n) at ((n / 8) * M + m) * 8 + n % 8, pad columns zero; C must be
+     * 16-byte aligned and hold ceil(N/8) * 8 * M elements. */
+    SPMM24_OUT_PACKED_B = 1
+};
+typedef struct spmm24_epilogue {
+    const void* bias;
+    const void* residual;
+    float alpha;    /* 1.0f for none */
+    int activation; /* SPMM24_ACT_* */
+    int out_layout; /* SPMM24_OUT_* */
+} spmm24_epilogue;
+
+/* spmm24_launch_ex with a fused epilogue; epilogue == NULL is the plain
+ * launch.  flags as for spmm24_launch_ex (SPMM24_BF16 included). */
+cudaError_t spmm24_launch_fused(cudaStream_t stream, const void* compressed_a, const void* b_packed,
+                                const uint16_t* metadata, void* c, int M, int N, int K, int split_k, unsigned flags,
+                                const spmm24_epilogue* epilogue);
 
 /* Allocation-free launch (no counterpart in the reference).  For callers
  * that cannot let a library call cudaMalloc: applications whose device
@@ -128,22 +167,29 @@ int spmm24_pack_b(const uint16_t* b_rowmajor, int K, int N, uint16_t* b_packed_o
  * its host prune/compress/metadata pipeline.  Returns 0, or -1 if K % 4. */
 int spmm24_prune_2of4(uint16_t* dense_a, int M, int K);
 
+/* The same prune on bf16 bit patterns (for SPMM24_BF16 weights). */
+int spmm24_prune_2of4_bf16(uint16_t* dense_a, int M, int K);
+
 /* On-device packer (no counterpart in the reference, whose packer runs on
- * the host only): one pass over a dense row-major M x K fp16 matrix in
- * device memory that optionally applies the magnitude 2:4 prune of
- * spmm24_prune_2of4 (prune != 0), then writes the compressed values
- * (M*K/2 halves) and the REORDERED metadata (M*K/16 u16) -- bit-exact with
- * spmm24_prune_2of4 + spmm24_compress_reordered.  M % 16 == 0, K % 64 == 0;
+ * the host only): one pass over a dense row-major M x K 16-bit matrix in
+ * device memory that optionally applies a magnitude 2:4 prune (prune =
+ * SPMM24_PRUNE_F16: spmm24_prune_2of4; SPMM24_PRUNE_BF16:
+ * spmm24_prune_2of4_bf16; SPMM24_PRUNE_NONE: none), then writes the
+ * compressed values (M*K/2 elements) and the REORDERED metadata (M*K/16
+ * u16) -- bit-exact with the prune + spmm24_compress_reordered.  M % 16 == 0, K % 64 == 0;
  * dense and values 16-byte aligned.  If bad_blocks (device int, optional)
  * is given, the kernel adds 1 for every row of a 16x16 block holding a
  * group of four with fewer than two zeros (the outputs of those rows are
  * unspecified); the caller zeroes it first.  Asynchronous on `stream`. */
+enum { SPMM24_PRUNE_NONE = 0, SPMM24_PRUNE_F16 = 1, SPMM24_PRUNE_BF16 = 2 };
 cudaError_t spmm24_pack_a_device(cudaStream_t stream, const void* dense_a, int M, int K, int prune,
                                  void* values_out, uint16_t* meta_out, int* bad_blocks);
 
 /* spmm24_prune_2of4 on a device matrix, in place (K % 4 == 0, 8-byte
  * aligned).  Asynchronous on `stream`. */
 cudaError_t spmm24_prune_2of4_device(cudaStream_t stream, void* dense_a, int M, int K);
+/* spmm24_prune_2of4_bf16 on a device matrix, in place. */
+cudaError_t spmm24_prune_2of4_bf16_device(cudaStream_t stream, void* dense_a, int M, int K);
 
 /* spmm24_pack_b on the device: row-major K x N fp16 -> ceil(N/8) strips of
  * K x 8 (pad columns zero), bit-exact with the host form; the producer of a

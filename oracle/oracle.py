@@ -61,6 +61,10 @@ def lib() -> ctypes.CDLL:
         L.orc_spmm_from_abi_f32.argtypes = [_u16p, _u16p, _u16p, _f32p] + [ctypes.c_int] * 4
         L.orc_spmm_from_abi_f32.restype = ctypes.c_int
         L.orc_f32_to_f16.argtypes = [_f32p, _u16p, ctypes.c_size_t]
+        L.orc_f32_to_bf16.argtypes = [_f32p, _u16p, ctypes.c_size_t]
+        L.orc_prune_magnitude_2of4_bf16.argtypes = [_u16p, ctypes.c_int, ctypes.c_int]
+        L.orc_dense_gemm_bf16_f32.argtypes = [_u16p, _u16p, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                              ctypes.c_int]
         L.orc_fnv1a64.argtypes = [ctypes.c_void_p, ctypes.c_size_t]
         L.orc_fnv1a64.restype = ctypes.c_uint64
         L.orc_max_threads.restype = ctypes.c_int
@@ -152,6 +156,27 @@ def spmm_from_abi_f32(vals, meta_reordered, b_packed, M: int, N: int, K: int, th
     if rc != 0:
         raise ValueError(f"spmm_from_abi_f32 failed ({rc})")
     return c
+
+
+def prune_magnitude_2of4_bf16(a: np.ndarray, M: int, K: int) -> np.ndarray:
+    a = np.ascontiguousarray(a, dtype=np.uint16).copy()
+    lib().orc_prune_magnitude_2of4_bf16(_p16(a), M, K)
+    return a
+
+
+def dense_gemm_bf16_f32(a: np.ndarray, b_rowmajor: np.ndarray, M: int, N: int, K: int, threads: int = 0) -> np.ndarray:
+    a = np.ascontiguousarray(a, dtype=np.uint16)
+    b = np.ascontiguousarray(b_rowmajor, dtype=np.uint16)
+    c = np.empty(M * N, dtype=np.float32)
+    lib().orc_dense_gemm_bf16_f32(_p16(a), _p16(b), _pf(c), M, N, K, threads)
+    return c
+
+
+def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty(x.size, dtype=np.uint16)
+    lib().orc_f32_to_bf16(_pf(x), _p16(out), x.size)
+    return out
 
 
 def f32_to_f16_bits(x: np.ndarray) -> np.ndarray:

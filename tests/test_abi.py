@@ -6,6 +6,7 @@ import os
 import re
 import subprocess
 
+import numpy as np
 import pytest
 
 import oracle as O
@@ -76,6 +77,33 @@ def test_launch_rejects_bad_arguments_without_gpu():
     assert _launch(0x10008, *ok[1:], 256, 16, 256) == spmm24.CUDA_ERROR_INVALID_VALUE  # A misaligned
     assert _launch(ok[0], ok[1], ok[2], 0x40001, 256, 16, 256) == spmm24.CUDA_ERROR_INVALID_VALUE  # C odd
     assert "aligned" in spmm24._lib.spmm24_last_error().decode()
+
+
+def test_fused_launch_rejects_bad_epilogues_without_gpu():
+    ok = (0x10000, 0x20000, 0x30000, 0x40000)
+    L = spmm24._lib
+
+    def fused(c=ok[3], flags=0, **kw):
+        e = spmm24.Epilogue(kw.get("bias"), kw.get("residual"), kw.get("alpha", 1.0), kw.get("act", 0),
+                            kw.get("layout", 0))
+        return L.spmm24_launch_fused(None, ok[0], ok[1], ok[2], c, 256, 16, 256, 0, flags, ctypes.byref(e))
+
+    assert fused(act=7) == spmm24.CUDA_ERROR_INVALID_VALUE
+    assert "activation" in L.spmm24_last_error().decode()
+    assert fused(layout=2) == spmm24.CUDA_ERROR_INVALID_VALUE
+    assert fused(alpha=float("nan")) == spmm24.CUDA_ERROR_INVALID_VALUE
+    assert fused(bias=0x50001) == spmm24.CUDA_ERROR_INVALID_VALUE
+    assert fused(c=0x40008, layout=1) == spmm24.CUDA_ERROR_INVALID_VALUE  # packed C must be 16-byte aligned
+    assert fused(flags=8) == spmm24.CUDA_ERROR_INVALID_VALUE               # unknown flag
+    assert L.spmm24_pack_a_device(None, ok[0], 256, 256, 3, ok[1], ok[2], None) == spmm24.CUDA_ERROR_INVALID_VALUE
+
+
+def test_host_bf16_prune_matches_oracle():
+    rng = np.random.default_rng(4)
+    a = (rng.standard_normal(64 * 128).astype(np.float32).view(np.uint32) >> 16).astype(np.uint16)
+    a[rng.random(a.size) < 0.2] = 0x8000
+    a[rng.random(a.size) < 0.05] = 0x7FC0  # NaN
+    assert np.array_equal(spmm24.prune_2of4_bf16(a, 64, 128), O.prune_magnitude_2of4_bf16(a, 64, 128))
 
 
 def test_device_packer_rejects_bad_arguments_without_gpu():
