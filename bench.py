@@ -147,29 +147,31 @@ class ClockSampler:
 
 
 # --------------------------------------------------------------------- data
-def make_layer(torch, spmm24, M, K, a_std, seed, mask_random=False):
+def make_layer(torch, spmm24, M, K, a_std, seed, mask_random=False, bf16=False):
     """Pruned, compressed weights of one layer, packed by the product's own
-    host packer (spmm24_prune_2of4 / spmm24_compress_reordered)."""
+    host packer (spmm24_prune_2of4[_bf16] / spmm24_compress_reordered)."""
     g = torch.Generator().manual_seed(seed)
+    dt = torch.bfloat16 if bf16 else torch.float16
     if a_std is None:
-        a = (torch.rand(M, K, generator=g) * 2 - 1).half()
+        a = (torch.rand(M, K, generator=g) * 2 - 1).to(dt)
         if mask_random:
             keep = torch.rand(M * K // 4, 4, generator=g).argsort(dim=1)[:, :2]
             m = torch.zeros(M * K // 4, 4, dtype=torch.bool).scatter_(1, keep, True)
-            a = (a.reshape(-1, 4) * m).reshape(M, K).half()
+            a = (a.reshape(-1, 4) * m).reshape(M, K).to(dt)
     else:
-        a = (torch.randn(M, K, generator=g) * a_std).half()
-    a_np = a.numpy().view("uint16")
+        a = (torch.randn(M, K, generator=g) * a_std).to(dt)
+    a_np = a.view(torch.int16).numpy().view("uint16")
     if a_std is not None or not mask_random:
-        a_np = spmm24.prune_2of4(a_np, M, K)
+        a_np = spmm24.prune_2of4_bf16(a_np, M, K) if bf16 else spmm24.prune_2of4(a_np, M, K)
     vals, meta = spmm24.compress_reordered(a_np, M, K)
     return a_np, vals, meta
 
 
-def make_activations(torch, spmm24, K, N, seed, uniform=False):
+def make_activations(torch, spmm24, K, N, seed, uniform=False, bf16=False):
     g = torch.Generator().manual_seed(seed)
-    b = ((torch.rand(K, N, generator=g) * 2 - 1) if uniform else torch.randn(K, N, generator=g)).half()
-    b_np = b.numpy().view("uint16")
+    dt = torch.bfloat16 if bf16 else torch.float16
+    b = ((torch.rand(K, N, generator=g) * 2 - 1) if uniform else torch.randn(K, N, generator=g)).to(dt)
+    b_np = b.view(torch.int16).numpy().view("uint16")
     return b_np, spmm24.pack_b(b_np, K, N)
 
 
@@ -195,13 +197,15 @@ def run_ours(args, rank, world, local_rank):
     shapes = wl["shapes"]
     square = args.workload == "square"
     shard = bool(wl.get("shard"))
+    bf16 = args.dtype == "bf16"
     # With sharding every rank holds rows [r0, r1) of each layer (generated
     # for that range directly); otherwise every rank runs whole layers.
     rows = {M: (spmm24.shard_rows(M, world, rank, 128) if shard else (0, M)) for (M, N, K) in shapes}
     layers = {}
     for i, (M, K) in enumerate(sorted({(M, K) for (M, N, K) in shapes})):
         r0, r1 = rows[M]
-        a_np, vals, meta = make_layer(torch, spmm24, r1 - r0, K, wl["a_std"], seed=1000 * rank + i, mask_random=square)
+        a_np, vals, meta = make_layer(torch, spmm24, r1 - r0, K, wl["a_std"], seed=1000 * rank + i, mask_random=square,
+                                      bf16=bf16)
         layers[(M, K)] = (a_np, vals, meta)
     acts = {}
     for j, (K, N) in enumerate(sorted({(K, N) for (M, N, K) in shapes})):
@@ -234,11 +238,30 @@ def run_ours(args, rank, world, local_rank):
     stream = torch.cuda.current_stream(dev)
     h_stream = int(stream.cuda_stream)
 
-    flags = spmm24.STATIC_WEIGHTS if args.static_weights else 0
+    flags = (spmm24.STATIC_WEIGHTS if args.static_weights else 0) | (spmm24.BF16 if bf16 else 0)
+    # Optional fused epilogue (spmm24_launch_fused): per-row bias + SiLU, or
+    # per-row bias + residual add (the residual is another M x N tensor).
+    fused = args.epilogue != "none" or bf16
+    if fused:
+        import ctypes
+
+        edt = torch.bfloat16 if bf16 else torch.float16
+        for c in calls:
+            c["bias"] = (torch.randn(c["M"], device=dev) * 0.1).to(edt)
+            c["res"] = torch.randn(c["M"], c["N"], device=dev).to(edt) if args.epilogue == "bias_residual" else None
+            c["epi"] = spmm24.Epilogue(c["bias"].data_ptr() if args.epilogue != "none" else None,
+                                       c["res"].data_ptr() if c["res"] is not None else None, 1.0,
+                                       spmm24.ACT_SILU if args.epilogue == "bias_silu" else spmm24.ACT_NONE,
+                                       spmm24.OUT_ROW_MAJOR)
 
     def launch(c, hs=None):
-        rc = spmm24._lib.spmm24_launch_ex(h_stream if hs is None else hs, c["A"].data_ptr(), c["B"].data_ptr(),
-                                          c["E"].data_ptr(), c["C"].data_ptr(), c["M"], c["N"], c["K"], 0, flags)
+        if fused:
+            rc = spmm24._lib.spmm24_launch_fused(h_stream if hs is None else hs, c["A"].data_ptr(), c["B"].data_ptr(),
+                                                 c["E"].data_ptr(), c["C"].data_ptr(), c["M"], c["N"], c["K"], 0,
+                                                 flags, ctypes.byref(c["epi"]))
+        else:
+            rc = spmm24._lib.spmm24_launch_ex(h_stream if hs is None else hs, c["A"].data_ptr(), c["B"].data_ptr(),
+                                              c["E"].data_ptr(), c["C"].data_ptr(), c["M"], c["N"], c["K"], 0, flags)
         if rc != 0:
             raise RuntimeError(f"spmm24_launch failed: {rc} {spmm24._lib.spmm24_last_error().decode()}")
 
@@ -372,7 +395,7 @@ def run_ours(args, rank, world, local_rank):
         "higher_is_better": True,
         "scaling": "strong" if shard else "weak",
         "vs_baseline": None,
-        "dtype": "f16 in, f32 accumulate, f16 out",
+        "dtype": f"{args.dtype} in, f32 accumulate, {args.dtype} out",
         "data": f"synthetic (seeded torch RNG; A N(0,{wl['a_std']}) magnitude-pruned 2:4, B N(0,1))" if wl["a_std"]
                 else "synthetic (U(-1,1), random 2:4 mask)",
         "config": {"workload": f"{args.workload}: " + ", ".join(f"{M}x{N}x{K}" for (M, N, K) in shapes),
@@ -383,7 +406,9 @@ def run_ours(args, rank, world, local_rank):
                                    else f"replicas x{world} (each rank its own layers)")},
         "per_shape_us": {f"{c['M']}x{c['N']}x{c['K']}": round(u, 3) for c, u in zip(calls, per_call)},
         "per_shape_note": "median single-kernel duration with an event pair around each launch",
-        "launch_flags": "SPMM24_STATIC_WEIGHTS" if args.static_weights else "none",
+        "launch_flags": " | ".join(f for f, on in (("SPMM24_STATIC_WEIGHTS", args.static_weights), ("SPMM24_BF16", bf16))
+                                   if on) or "none",
+        "epilogue": args.epilogue,
         "roofline": {"bound": wl["bound"], "achieved": round(achieved, 2), "peak": peak, "unit": unit,
                      "frac": round(achieved / peak, 4), "traffic": traffic,
                      "peak_src": f"{peaks['src']} ({'hbm_gbs copy' if unit == 'GB/s' else '2 x dense bf16 cuBLAS burst (2:4 sparse rate)'})",
@@ -428,11 +453,11 @@ def run_ours(args, rank, world, local_rank):
                             "busbw_GBps": round(gbytes * (world - 1) / world / (float(gt[0]) * 1e-3 / args.steps) / 1e9, 1),
                             "op": "NCCL all_gather_into_tensor of the C shards"}
 
-    if args.comparators and rank == 0:
+    if args.comparators and rank == 0 and not bf16:
         out["comparators"] = run_comparators(torch, spmm24, calls, layers, acts, dev, args)
 
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        out["cpu_baseline"] = cpu_baseline(layers, acts, shapes, budget_s=args.cpu_seconds)
+        out["cpu_baseline"] = cpu_baseline(layers, acts, shapes, budget_s=args.cpu_seconds, bf16=bf16)
 
     if world > 1:
         dist.barrier()
@@ -519,13 +544,15 @@ def host_threads():
         return os.cpu_count() or 1
 
 
-def cpu_baseline(layers, acts, shapes, budget_s=10.0):
-    """The oracle's OpenMP dense GEMM (fp16 -> fp32, fp32 accumulate) on the
-    pruned A, on a row sample of every shape of the workload."""
+def cpu_baseline(layers, acts, shapes, budget_s=10.0, bf16=False):
+    """The oracle's OpenMP dense GEMM (fp16 or bf16 -> fp32, fp32 accumulate)
+    on the pruned A, on a row sample of every shape of the workload."""
     import numpy as np
 
     sys.path.insert(0, os.path.join(REPO, "oracle"))
     import oracle as O
+
+    gemm = O.dense_gemm_bf16_f32 if bf16 else O.dense_gemm_f32
 
     threads = host_threads()
     # estimate: 64 rows of every shape
@@ -533,7 +560,7 @@ def cpu_baseline(layers, acts, shapes, budget_s=10.0):
     t = time.perf_counter()
     for (M, N, K) in shapes:
         a = layers[(M, K)][0][: probe_rows * K]
-        O.dense_gemm_f32(a, acts[(K, N)][0], probe_rows, N, K, threads)
+        gemm(a, acts[(K, N)][0], probe_rows, N, K, threads)
     dt = time.perf_counter() - t
     rows = int(max(16, min(4096, probe_rows * budget_s / max(dt, 1e-3) / 1.2)))
     fl = 0.0
@@ -541,7 +568,7 @@ def cpu_baseline(layers, acts, shapes, budget_s=10.0):
     for (M, N, K) in shapes:
         r = min(rows, M)
         a = layers[(M, K)][0][: r * K]
-        O.dense_gemm_f32(a, acts[(K, N)][0], r, N, K, threads)
+        gemm(a, acts[(K, N)][0], r, N, K, threads)
         fl += flops(r, N, K)
     dt = time.perf_counter() - t
     return {"value": round(fl / dt / 1e12, 6), "unit": "TFLOPS", "cores": threads, "kind": "port",
@@ -857,6 +884,9 @@ def main():
     ap.add_argument("--no-static-weights", dest="static_weights", action="store_false",
                     help="launch without SPMM24_STATIC_WEIGHTS (no kernel in the step writes the weights)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--dtype", choices=["f16", "bf16"], default="f16", help="operand and output type (SPMM24_BF16)")
+    ap.add_argument("--epilogue", choices=["none", "bias_silu", "bias_residual"], default="none",
+                    help="fused epilogue through spmm24_launch_fused")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--single", default=None,
                     help="M,N,K[,split]: run one shape (warm-up + 3 launches) for profiler captures")

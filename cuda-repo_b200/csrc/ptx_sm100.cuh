@@ -110,6 +110,14 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* m, uin
         : "memory");
 }
 
+// 16-byte asynchronous global -> shared copy (LDGSTS), grouped and waited
+// for with cp.async.commit_group / wait_group.
+__device__ __forceinline__ void cp_async16(void* dst_smem, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst_smem)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
 // Loads for a CTA pair running cta_group::2 MMAs: the bytes are counted on
 // the mbarrier at `bar_cluster` (a shared::cluster address, normally the
 // leader CTA's barrier), not on the executing CTA's.

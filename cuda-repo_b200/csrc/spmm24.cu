@@ -300,10 +300,11 @@ cudaError_t prepare(Kern kern, int smem, int dev, int idx) {
 
 template <class Kern, class Params>
 cudaError_t launch_kernel(Kern kern, dim3 grid, int smem, cudaStream_t stream, unsigned cluster_x, bool pdl,
-                          const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& te, const Params& kp) {
+                          const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& te, const Params& kp,
+                          int threads = kThreads) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
-    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.blockDim = dim3((unsigned)threads, 1, 1);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[2];
@@ -365,7 +366,7 @@ cudaError_t launch_pair_v(const Plan& pl, cudaStream_t stream, int dev, bool pdl
     cudaError_t e = prepare(kern, C_::SMEM_ALLOC, dev, idx + (general ? kEpiSlot : 0));
     if (e != cudaSuccess) return e;
     return launch_kernel(kern, dim3(2u, (unsigned)pl.n_tiles, (unsigned)pl.m_tiles), C_::SMEM_ALLOC, stream, 2u, pdl,
-                         ta, tb, te, kp);
+                         ta, tb, te, kp, kPairThreads);
 }
 
 cudaError_t launch_pair(const Plan& pl, cudaStream_t stream, int dev, bool pdl, const CUtensorMap& ta,

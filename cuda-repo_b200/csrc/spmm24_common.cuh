@@ -183,13 +183,32 @@ __device__ __forceinline__ uint16_t f32_to_elem(float v, int bf16) {
     return static_cast<__half_raw>(h).x;
 }
 
-// ReLU; SiLU y * sigmoid(y); GELU in its tanh form (Hendrycks & Gimpel,
-// 2016): 0.5 y (1 + tanh(sqrt(2 / pi) (y + 0.044715 y^3))).
+// Hardware tanh approximation (tanh.approx.f32: relative error about 2^-11,
+// far below an fp16 / bf16 output ulp).
+__device__ __forceinline__ float tanh_fast(float x) {
+    float y;
+    asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// ReLU; SiLU y * sigmoid(y), with sigmoid(y) = 0.5 + 0.5 tanh(y / 2); GELU
+// in its tanh form (Hendrycks & Gimpel, 2016): 0.5 y (1 + tanh(sqrt(2 / pi)
+// (y + 0.044715 y^3))).  One hardware tanh per element.
 __device__ __forceinline__ float activate(float y, int act) {
     if (act == kActRelu) return fmaxf(y, 0.f);
-    if (act == kActSilu) return y / (1.f + expf(-y));
-    if (act == kActGelu) return 0.5f * y * (1.f + tanhf(0.7978845608028654f * (y + 0.044715f * y * y * y)));
+    if (act == kActSilu) return y * fmaf(0.5f, tanh_fast(0.5f * y), 0.5f);
+    if (act == kActGelu) return 0.5f * y * (1.f + tanh_fast(0.7978845608028654f * (y + 0.044715f * y * y * y)));
     return y;
+}
+
+// Two values rounded to C's type, packed low-first in one word.
+__device__ __forceinline__ uint32_t pack2(float a, float b, int bf16) {
+    if (bf16) {
+        const __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+        return *reinterpret_cast<const uint32_t*>(&v);
+    }
+    const __half2 v = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&v);
 }
 
 // Element offset of (m, n) in C's layout.
@@ -203,19 +222,34 @@ __device__ __forceinline__ bool epilogue_is_plain(const Epilogue& e) {
     return e.bias == nullptr && e.residual == nullptr && e.act == kActNone && e.alpha == 1.f;
 }
 
+// alpha, bias and activation on n values of row gm (no residual).
+template <int n>
+__device__ __forceinline__ void epilogue_pre(float* y, const Epilogue& e, int gm) {
+    if (e.alpha != 1.f) {
+#pragma unroll
+        for (int i = 0; i < n; ++i) y[i] *= e.alpha;
+    }
+    if (e.bias) {
+        const float b = elem_to_f32(e.bias[gm], e.bf16);
+#pragma unroll
+        for (int i = 0; i < n; ++i) y[i] += b;
+    }
+    if (e.act == kActRelu) {
+#pragma unroll
+        for (int i = 0; i < n; ++i) y[i] = fmaxf(y[i], 0.f);
+    } else if (e.act == kActSilu) {
+#pragma unroll
+        for (int i = 0; i < n; ++i) y[i] = activate(y[i], kActSilu);
+    } else if (e.act == kActGelu) {
+#pragma unroll
+        for (int i = 0; i < n; ++i) y[i] = activate(y[i], kActGelu);
+    }
+}
+
 // Rounds 8 values to C's type; columns at or past N (lim) become zero.
 __device__ __forceinline__ void round8(const float* y, int lim, int bf16, uint32_t* w) {
-    if (bf16) {
 #pragma unroll
-        for (int i = 0; i < 8; i += 2)
-            w[i >> 1] = (i < lim ? (uint32_t)f32_to_elem(y[i], 1) : 0u) |
-                        ((i + 1 < lim ? (uint32_t)f32_to_elem(y[i + 1], 1) : 0u) << 16);
-    } else {
-#pragma unroll
-        for (int i = 0; i < 8; i += 2)
-            w[i >> 1] = (i < lim ? (uint32_t)f32_to_elem(y[i], 0) : 0u) |
-                        ((i + 1 < lim ? (uint32_t)f32_to_elem(y[i + 1], 0) : 0u) << 16);
-    }
+    for (int i = 0; i < 8; i += 2) w[i >> 1] = pack2(i < lim ? y[i] : 0.f, i + 1 < lim ? y[i + 1] : 0.f, bf16);
 }
 
 // Epilogue of 8 consecutive columns gn..gn+7 (gn % 8 == 0) of row gm < M:
@@ -230,25 +264,7 @@ __device__ __forceinline__ void epilogue8(const float* v, const Epilogue& e, int
     float y[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) y[i] = v[i];
-    if (e.alpha != 1.f) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) y[i] *= e.alpha;
-    }
-    if (e.bias) {
-        const float b = elem_to_f32(e.bias[gm], e.bf16);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) y[i] += b;
-    }
-    if (e.act == kActRelu) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) y[i] = fmaxf(y[i], 0.f);
-    } else if (e.act == kActSilu) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) y[i] = activate(y[i], kActSilu);
-    } else if (e.act == kActGelu) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) y[i] = activate(y[i], kActGelu);
-    }
+    epilogue_pre<8>(y, e, gm);
     if (e.residual) {
         const size_t base = c_offset(e, gm, gn, M, N);
         if (e.packed || vec_rowmajor) {

@@ -41,6 +41,11 @@ namespace spmm24 {
 
 constexpr int kThreads = 192;     // 6 warps
 constexpr int kEpiThreads = 128;  // warps 2..5
+// The pair kernel runs 8 warps: after the main loop every warp joins the
+// epilogue, two warps per TMEM lane quadrant (each takes half the columns),
+// because the epilogue -- on the critical path of every tile -- is bound by
+// instruction latency, not bandwidth.
+constexpr int kPairThreads = 256;
 constexpr uint32_t kBarEpi = 1;   // named barrier: epilogue warps
 constexpr uint32_t kBarTmem = 2;  // named barrier: warps 1..5 after TMEM allocation
 
@@ -351,11 +356,14 @@ struct PairCfg {
     // Two CTAs per SM when both rings fit in the SM's 228 KB (1 KB reserved per CTA).
     static constexpr int CTAS_PER_SM = 2 * (SMEM_ALLOC + 1024) <= 233472 ? 2 : 1;
     static constexpr int C_PITCH = TILE_N + 8;  // halves per staged output row (bank-shifted)
+    static constexpr int F_PITCH = TILE_N + 4;  // floats per staged fp32 row (epilogue with a residual)
+    static constexpr int RES_OFFSET = kTileM * F_PITCH * 4;  // residual tile after the fp32 staging
     static_assert(HALF_N == 64 || HALF_N == 128, "pair tiles are 128 or 256 columns wide");
     static_assert(TMEM_NEED <= 512, "TMEM overflow");
     static_assert(CTAS_PER_SM * TMEM_COLS <= 512, "co-resident CTAs must fit in TMEM together");
     static_assert(SMEM_ALLOC <= 232448, "shared memory overflow");
     static_assert(kTileM * C_PITCH * 2 <= RING_BYTES, "output staging does not fit");
+    static_assert(RES_OFFSET + kTileM * TILE_N * 2 <= RING_BYTES, "fp32 staging + residual tile do not fit");
 };
 
 constexpr int kPairGroupM = 8;  // tile rows per rasterisation group
@@ -371,7 +379,7 @@ __host__ __device__ constexpr uint32_t pair_idesc() {
 // (before it joins the epilogue), so two threads of the CTA keep TMA busy.
 // EPI: the general epilogue, as for spmm24_cluster_kernel.
 template <int HALF_N, int STAGES, bool SPLIT_ISSUE, bool EPI>
-__global__ void __launch_bounds__(kThreads, PairCfg<HALF_N, STAGES>::CTAS_PER_SM)
+__global__ void __launch_bounds__(kPairThreads, PairCfg<HALF_N, STAGES>::CTAS_PER_SM)
 spmm24_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmE, const PairParams p) {
     using C_ = PairCfg<HALF_N, STAGES>;
@@ -514,21 +522,25 @@ spmm24_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
         }
         __syncwarp();
     }
-    if (warp >= 2) {
-        // ------------------------------------------- epilogue (both CTAs)
+    {
+        // ---------------------------------- epilogue (every warp, both CTAs)
         if (!ptx::mbar_wait_bounded(acc_full, 0, kWaitLimitNs)) atomicOr(&g_spmm24_status, kStatusEpilogueTimeout);
         if (threadIdx.x == 64) SPMM24_STAMP(4);
         ptx::tc_fence_after();
         __syncwarp();
-        const int quad = warp & 3;
+        const int quad = warp & 3;  // TMEM lane quadrant this warp may access
         const int row = quad * 32 + lane;
+        constexpr int NCH16 = C_::TILE_N / 16;           // 16-column chunks per row
+        const int c_begin = (warp >> 2) * (NCH16 / 2);  // this warp's half of the columns
+        const int c_end = c_begin + NCH16 / 2;
+        const int etid = threadIdx.x;
         if constexpr (!EPI) {
             // Plain fp16 row-major: stage the rounded tile in the (now idle)
             // ring -- rows bank-shifted by 16 bytes so the per-row writes do
             // not collide -- then copy it out with coalesced 16-byte stores.
             __half* cst = reinterpret_cast<__half*>(smem);
 #pragma unroll 1
-            for (int c = 0; c < C_::TILE_N / 16; ++c) {
+            for (int c = c_begin; c < c_end; ++c) {
                 uint32_t v[16];
                 ptx::tmem_ld_32x32b_x16(tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(c * 16), v);
                 ptx::tmem_wait_ld();
@@ -540,11 +552,10 @@ spmm24_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                 dst[1] = reinterpret_cast<const uint4*>(h)[1];
             }
             ptx::tc_fence_before();
-            ptx::named_barrier(kBarEpi, kEpiThreads);
+            ptx::named_barrier(kBarEpi, kPairThreads);
             ptx::grid_dep_wait();  // C may be in use by the previous grid
-            constexpr int LPR = C_::TILE_N / 8;     // threads per row (16-byte chunks)
-            constexpr int RPP = kEpiThreads / LPR;  // rows per pass
-            const int etid = threadIdx.x - 64;
+            constexpr int LPR = C_::TILE_N / 8;      // threads per row (16-byte chunks)
+            constexpr int RPP = kPairThreads / LPR;  // rows per pass
             const int chunk = etid % LPR;
             const int gm0 = m_tile * C_::TILE_M + (int)rank * kTileM;
             const int gn = n_tile * C_::TILE_N + chunk * 8;
@@ -562,71 +573,136 @@ spmm24_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                 }
             }
         } else {
+            // General epilogue.  alpha * acc + bias, activated, is computed
+            // from TMEM per row.  Without a residual it is rounded and staged
+            // as 16-bit values; with one it is staged as fp32 while the
+            // residual tile streams into the rest of the idle ring (cp.async,
+            // coalesced, all of it in flight at once), and the copy-out adds
+            // the residual before rounding once.  Each case has its own short
+            // loop: the epilogue is bound by instruction latency.  Stores are
+            // coalesced, row-major or packed.
             const int gm0 = m_tile * C_::TILE_M + (int)rank * kTileM;
             const int gn0 = n_tile * C_::TILE_N;
             const bool vec_ok = (p.N % 8 == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15u) == 0);
-            const bool vec_res = (p.N % 8 == 0) && ((reinterpret_cast<uintptr_t>(p.epi.residual) & 15u) == 0);
-            const bool plain = epilogue_is_plain(p.epi);
-            // The bias and the residual may be written by the previous grid.
-            if (!plain) ptx::grid_dep_wait();
-            // Stage the output tile (C's element type) in the (now idle) ring,
-            // after the epilogue: rows are bank-shifted by 16 bytes so the
-            // per-row writes do not collide.
-            uint16_t* cst = reinterpret_cast<uint16_t*>(smem);
-    #pragma unroll 1
-            for (int c = 0; c < C_::TILE_N / 16; ++c) {
-                uint32_t v[16];
-                ptx::tmem_ld_32x32b_x16(tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(c * 16), v);
-                ptx::tmem_wait_ld();
-                uint32_t h[8];
-                const int gm = gm0 + row, gn = gn0 + c * 16;
-                float f[16];
-    #pragma unroll
-                for (int e = 0; e < 16; ++e) f[e] = __uint_as_float(v[e]);
-                if (plain || gm >= p.M || gn >= p.N) {
-                    // columns at or past N become zero (pad columns of a packed C)
-                    round8(f, max(0, min(8, p.N - gn)), p.epi.bf16, h);
-                    round8(f + 8, max(0, min(8, p.N - gn - 8)), p.epi.bf16, h + 4);
-                } else {
-                    epilogue8(f, p.epi, gm, gn, p.M, p.N, vec_res, h);
-                    if (gn + 8 < p.N) epilogue8(f + 8, p.epi, gm, gn + 8, p.M, p.N, vec_res, h + 4);
-                    else h[4] = h[5] = h[6] = h[7] = 0u;
+            const bool has_res = p.epi.residual != nullptr;
+            const bool vec_res = p.epi.packed ||
+                                 ((p.N % 8 == 0) && ((reinterpret_cast<uintptr_t>(p.epi.residual) & 15u) == 0));
+            const int strips = (p.N + 7) / 8;
+            constexpr int CH = C_::TILE_N / 8;  // 8-column chunks per row
+            constexpr int ITEMS = kTileM * CH;   // (row, chunk) items of this CTA
+            if (p.epi.bias || has_res) ptx::grid_dep_wait();  // they may be written by the previous grid
+            uint4* rst = reinterpret_cast<uint4*>(smem + C_::RES_OFFSET);  // residual tile [row][chunk]
+            if (has_res && vec_res) {
+                // packed C: consecutive threads take consecutive rows of a
+                // strip; row-major C: consecutive chunks of a row
+                for (int idx = etid; idx < ITEMS; idx += kPairThreads) {
+                    const int r = p.epi.packed ? idx % kTileM : idx / CH;
+                    const int c = p.epi.packed ? idx / kTileM : idx % CH;
+                    const int gm = gm0 + r, gn = gn0 + c * 8;
+                    if (gm < p.M && gn < p.N)
+                        ptx::cp_async16(rst + r * CH + c, p.epi.residual + c_offset(p.epi, gm, gn, p.M, p.N));
                 }
-                uint4* dst = reinterpret_cast<uint4*>(cst + (size_t)row * C_::C_PITCH + c * 16);
-                dst[0] = make_uint4(h[0], h[1], h[2], h[3]);
-                dst[1] = make_uint4(h[4], h[5], h[6], h[7]);
+                ptx::cp_async_commit();
             }
-            ptx::tc_fence_before();
-            ptx::named_barrier(kBarEpi, kEpiThreads);
-            ptx::grid_dep_wait();  // C may be in use by the previous grid
-            const int etid = threadIdx.x - 64;
-            if (p.epi.packed) {
-                // One 16-byte strip row per thread; consecutive threads take
-                // consecutive rows of a strip (contiguous in the packed layout).
-                const int strips = (p.N + 7) / 8;
-                for (int idx = etid; idx < kTileM * (C_::TILE_N / 8); idx += kEpiThreads) {
-                    const int ch = idx / kTileM, r = idx % kTileM;
-                    const int gm = gm0 + r, strip = gn0 / 8 + ch;
-                    if (gm >= p.M || strip >= strips) continue;
-                    *reinterpret_cast<uint4*>(p.C + ((size_t)strip * p.M + gm) * 8) =
-                        *reinterpret_cast<const uint4*>(cst + (size_t)r * C_::C_PITCH + ch * 8);
+            float* fst = reinterpret_cast<float*>(smem);
+            uint16_t* hst = reinterpret_cast<uint16_t*>(smem);
+            const int gm = gm0 + row;
+            if (has_res) {
+#pragma unroll 1
+                for (int c = c_begin; c < c_end; ++c) {
+                    uint32_t v[16];
+                    ptx::tmem_ld_32x32b_x16(tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(c * 16), v);
+                    ptx::tmem_wait_ld();
+                    float f[16];
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) f[e] = __uint_as_float(v[e]);
+                    if (gm < p.M) epilogue_pre<16>(f, p.epi, gm);
+                    float4* dst = reinterpret_cast<float4*>(fst + (size_t)row * C_::F_PITCH + c * 16);
+#pragma unroll
+                    for (int q = 0; q < 4; ++q)
+                        dst[q] = make_float4(f[4 * q], f[4 * q + 1], f[4 * q + 2], f[4 * q + 3]);
                 }
             } else {
-                // Coalesced copy-out: LPR threads cover one row with 16-byte chunks.
-                constexpr int LPR = C_::TILE_N / 8;
-                constexpr int RPP = kEpiThreads / LPR;  // rows per pass
-                const int chunk = etid % LPR;
-                const int gn = gn0 + chunk * 8;
-                for (int r = etid / LPR; r < kTileM; r += RPP) {
-                    const int gm = gm0 + r;
-                    if (gm >= p.M || gn >= p.N) continue;
-                    const uint16_t* src = cst + (size_t)r * C_::C_PITCH + chunk * 8;
-                    uint16_t* out = p.C + (size_t)gm * p.N + gn;
-                    if (vec_ok) {
-                        *reinterpret_cast<uint4*>(out) = *reinterpret_cast<const uint4*>(src);
+#pragma unroll 1
+                for (int c = c_begin; c < c_end; ++c) {
+                    uint32_t v[16];
+                    ptx::tmem_ld_32x32b_x16(tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(c * 16), v);
+                    ptx::tmem_wait_ld();
+                    float f[16];
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) f[e] = __uint_as_float(v[e]);
+                    if (gm < p.M) epilogue_pre<16>(f, p.epi, gm);
+                    const int gn = gn0 + c * 16;
+                    uint32_t h[8];
+                    if (gn + 16 <= p.N) {
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) h[e] = pack2(f[2 * e], f[2 * e + 1], p.epi.bf16);
+                    } else {  // the last strip: columns at or past N become zero
+                        round8(f, max(0, min(8, p.N - gn)), p.epi.bf16, h);
+                        round8(f + 8, max(0, min(8, p.N - gn - 8)), p.epi.bf16, h + 4);
+                    }
+                    uint4* dst = reinterpret_cast<uint4*>(hst + (size_t)row * C_::C_PITCH + c * 16);
+                    dst[0] = make_uint4(h[0], h[1], h[2], h[3]);
+                    dst[1] = make_uint4(h[4], h[5], h[6], h[7]);
+                }
+            }
+            if (has_res && vec_res) ptx::cp_async_wait_all();
+            ptx::tc_fence_before();
+            ptx::named_barrier(kBarEpi, kPairThreads);
+            ptx::grid_dep_wait();  // C may be in use by the previous grid
+            // The output chunk (row r, 8-column chunk c) as four words.
+            auto chunk_out = [&](int r, int c, int gmr, int gn, uint4& out) {
+                if (has_res) {
+                    const float* src = fst + (size_t)r * C_::F_PITCH + c * 8;
+                    const float4 y0 = *reinterpret_cast<const float4*>(src);
+                    const float4 y1 = *reinterpret_cast<const float4*>(src + 4);
+                    float y[8] = {y0.x, y0.y, y0.z, y0.w, y1.x, y1.y, y1.z, y1.w};
+                    if (vec_res) {
+                        const uint4 q = rst[r * CH + c];
+                        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                        for (int e = 0; e < 8; ++e)
+                            y[e] += elem_to_f32((uint16_t)(w[e >> 1] >> (16 * (e & 1))), p.epi.bf16);
                     } else {
-                        const int lim = min(8, p.N - gn);
-                        for (int e = 0; e < lim; ++e) out[e] = src[e];
+                        const size_t off = c_offset(p.epi, gmr, gn, p.M, p.N);
+#pragma unroll
+                        for (int e = 0; e < 8; ++e)
+                            if (gn + e < p.N) y[e] += elem_to_f32(p.epi.residual[off + e], p.epi.bf16);
+                    }
+                    uint32_t h[4];
+                    round8(y, min(8, p.N - gn), p.epi.bf16, h);
+                    out = make_uint4(h[0], h[1], h[2], h[3]);
+                } else {
+                    out = *reinterpret_cast<const uint4*>(hst + (size_t)r * C_::C_PITCH + c * 8);
+                }
+            };
+            if (p.epi.packed) {
+                // consecutive threads take consecutive rows of a strip
+                for (int idx = etid; idx < ITEMS; idx += kPairThreads) {
+                    const int r = idx % kTileM, c = idx / kTileM;
+                    const int gmr = gm0 + r, gn = gn0 + c * 8;
+                    if (gmr >= p.M || (gn >> 3) >= strips) continue;
+                    uint4 out;
+                    chunk_out(r, c, gmr, gn, out);
+                    *reinterpret_cast<uint4*>(p.C + (((size_t)(gn >> 3) * p.M + gmr) << 3)) = out;
+                }
+            } else {
+                // consecutive threads take consecutive chunks of a row
+                constexpr int RPP = kPairThreads / CH;  // rows per pass
+                const int c = etid % CH;
+                const int gn = gn0 + c * 8;
+                for (int r = etid / CH; r < kTileM; r += RPP) {
+                    const int gmr = gm0 + r;
+                    if (gmr >= p.M || gn >= p.N) continue;
+                    uint4 out;
+                    chunk_out(r, c, gmr, gn, out);
+                    if (vec_ok) {
+                        *reinterpret_cast<uint4*>(p.C + (size_t)gmr * p.N + gn) = out;
+                    } else {
+                        const uint32_t w[4] = {out.x, out.y, out.z, out.w};
+#pragma unroll
+                        for (int e = 0; e < 8; ++e)
+                            if (gn + e < p.N) p.C[(size_t)gmr * p.N + gn + e] = (uint16_t)(w[e >> 1] >> (16 * (e & 1)));
                     }
                 }
             }
