@@ -49,6 +49,21 @@ _lib.spmm24_pack_b.argtypes = [_u16p, ctypes.c_int, ctypes.c_int, _u16p]
 _lib.spmm24_pack_b.restype = ctypes.c_int
 _lib.spmm24_prune_2of4.argtypes = [_u16p, ctypes.c_int, ctypes.c_int]
 _lib.spmm24_prune_2of4.restype = ctypes.c_int
+class PackedHeader(ctypes.Structure):
+    """spmm24_packed_header (include/spmm24/SpMM_API.h)."""
+    _fields_ = [("version", ctypes.c_uint32), ("dtype", ctypes.c_uint32), ("M", ctypes.c_uint32),
+                ("K", ctypes.c_uint32), ("values_bytes", ctypes.c_uint64), ("meta_bytes", ctypes.c_uint64),
+                ("checksum", ctypes.c_uint64)]
+
+
+_lib.spmm24_save_packed.argtypes = [ctypes.c_char_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp, _vp]
+_lib.spmm24_save_packed.restype = ctypes.c_int
+_lib.spmm24_load_packed_header.argtypes = [ctypes.c_char_p, ctypes.POINTER(PackedHeader)]
+_lib.spmm24_load_packed_header.restype = ctypes.c_int
+_lib.spmm24_load_packed.argtypes = [ctypes.c_char_p, _vp, _vp]
+_lib.spmm24_load_packed.restype = ctypes.c_int
+
+
 class Epilogue(ctypes.Structure):
     """spmm24_epilogue (include/spmm24/SpMM_API.h)."""
     _fields_ = [("bias", ctypes.c_void_p), ("residual", ctypes.c_void_p), ("alpha", ctypes.c_float),
@@ -331,6 +346,36 @@ def prune_2of4_bf16(dense_a: np.ndarray, M: int, K: int) -> np.ndarray:
     if _lib.spmm24_prune_2of4_bf16(_p(a), M, K) != 0:
         raise ValueError("prune_2of4_bf16: K % 4 must be 0")
     return a
+
+
+# ------------------------------------------------- packed-weight files
+PACKED_ERRORS = {-1: "bad argument or shape", -2: "I/O error or short file",
+                 -3: "not a packed-weight file (magic, version or size)", -4: "checksum mismatch"}
+
+
+def save_packed(path: str, values: np.ndarray, meta: np.ndarray, M: int, K: int, bf16: bool = False) -> None:
+    """spmm24_save_packed: write compressed values + reordered metadata (host arrays)."""
+    v = _u16(values).reshape(-1)
+    m = _u16(meta).reshape(-1)
+    if v.size != M * K // 2 or m.size != M * K // 16:
+        raise ValueError("values / metadata sizes do not match M x K")
+    rc = _lib.spmm24_save_packed(os.fsencode(path), 1 if bf16 else 0, M, K, v.ctypes.data, m.ctypes.data)
+    if rc != 0:
+        raise OSError(f"spmm24_save_packed: {PACKED_ERRORS.get(rc, rc)}")
+
+
+def load_packed(path: str):
+    """spmm24_load_packed: returns (values, metadata, M, K, bf16) as host arrays."""
+    h = PackedHeader()
+    rc = _lib.spmm24_load_packed_header(os.fsencode(path), ctypes.byref(h))
+    if rc != 0:
+        raise OSError(f"spmm24_load_packed_header: {PACKED_ERRORS.get(rc, rc)}")
+    v = np.empty(h.values_bytes // 2, dtype=np.uint16)
+    m = np.empty(h.meta_bytes // 2, dtype=np.uint16)
+    rc = _lib.spmm24_load_packed(os.fsencode(path), v.ctypes.data, m.ctypes.data)
+    if rc != 0:
+        raise OSError(f"spmm24_load_packed: {PACKED_ERRORS.get(rc, rc)}")
+    return v, m, int(h.M), int(h.K), bool(h.dtype == 1)
 
 
 # Reference-named wrappers (Block sizes fixed as in the reference harness).

@@ -198,6 +198,26 @@ cudaError_t spmm24_prune_2of4_bf16_device(cudaStream_t stream, void* dense_a, in
  * Asynchronous on `stream`. */
 cudaError_t spmm24_pack_b_device(cudaStream_t stream, const void* b_rowmajor, int K, int N, void* b_packed_out);
 
+/* Packed-weight files (no counterpart in the reference): a 64-byte header
+ * (magic "SPMM24W", version 1, dtype 0 = fp16 / 1 = bf16, M, K, payload
+ * sizes, FNV-1a-64 checksum of the payload), then the compressed values and
+ * the reordered metadata exactly as spmm24_launch consumes them.  Host
+ * buffers.  Return 0 or a negative SPMM24_PACKED_E* code. */
+enum {
+    SPMM24_PACKED_EARG = -1,     /* bad argument or shape (M % 16, K % 64) */
+    SPMM24_PACKED_EIO = -2,      /* open / read / write failed, or short file */
+    SPMM24_PACKED_EFORMAT = -3,  /* not a packed-weight file, unknown version, or trailing bytes */
+    SPMM24_PACKED_ECHECKSUM = -4 /* payload does not match its checksum */
+};
+typedef struct spmm24_packed_header {
+    uint32_t version, dtype, M, K;
+    uint64_t values_bytes, meta_bytes, checksum;
+} spmm24_packed_header;
+int spmm24_save_packed(const char* path, int dtype, int M, int K, const void* values, const uint16_t* meta);
+int spmm24_load_packed_header(const char* path, spmm24_packed_header* out);
+/* values: values_bytes, meta: meta_bytes (from the header). */
+int spmm24_load_packed(const char* path, void* values, uint16_t* meta);
+
 /* Workspace the caller must pass as split_reduction: always 0 bytes (any
  * workspace is owned by the library, see spmm24_launch).
  * Replaces the Split_K*M*N halves contract of test/kernelTest.cu:136. */

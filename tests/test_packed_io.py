@@ -1,0 +1,60 @@
+"""Packed-weight files (spmm24_save_packed / spmm24_load_packed): round trip
+of the exact bytes spmm24_launch consumes, and every corruption detected."""
+import numpy as np
+import pytest
+
+import spmm24
+
+
+def _packed(M, K, seed):
+    rng = np.random.default_rng(seed)
+    a = rng.standard_normal((M, K)).astype(np.float16).view(np.uint16)
+    return spmm24.compress_reordered(spmm24.prune_2of4(a, M, K), M, K)
+
+
+@pytest.mark.parametrize("M,K,bf16", [(16, 64, False), (256, 512, True), (4096, 1024, False)])
+def test_round_trip(tmp_path, M, K, bf16):
+    v, m = _packed(M, K, M + K)
+    p = tmp_path / "w.spmm24"
+    spmm24.save_packed(str(p), v, m, M, K, bf16=bf16)
+    assert p.stat().st_size == 64 + M * K + M * K // 8
+    v2, m2, M2, K2, b2 = spmm24.load_packed(str(p))
+    assert (M2, K2, b2) == (M, K, bf16)
+    assert np.array_equal(v, v2) and np.array_equal(m, m2)
+
+
+def test_corruption_is_detected(tmp_path):
+    M, K = 64, 256
+    v, m = _packed(M, K, 1)
+    p = tmp_path / "w.spmm24"
+    spmm24.save_packed(str(p), v, m, M, K)
+    raw = bytearray(p.read_bytes())
+    cases = {
+        "payload": (lambda b: b.__setitem__(200, b[200] ^ 0x10), "checksum"),
+        "magic": (lambda b: b.__setitem__(0, ord("X")), "not a packed-weight file"),
+        "version": (lambda b: b.__setitem__(8, 2), "not a packed-weight file"),
+        "size": (lambda b: b.__setitem__(16, 17), "not a packed-weight file"),   # M not a multiple of 16
+    }
+    for name, (mutate, msg) in cases.items():
+        b = bytearray(raw)
+        mutate(b)
+        q = tmp_path / f"{name}.spmm24"
+        q.write_bytes(bytes(b))
+        with pytest.raises(OSError, match=msg):
+            spmm24.load_packed(str(q))
+    q = tmp_path / "short.spmm24"
+    q.write_bytes(bytes(raw[:-1]))
+    with pytest.raises(OSError, match="short file"):
+        spmm24.load_packed(str(q))
+    q = tmp_path / "long.spmm24"
+    q.write_bytes(bytes(raw) + b"\0")
+    with pytest.raises(OSError, match="not a packed-weight file"):
+        spmm24.load_packed(str(q))
+    with pytest.raises(OSError):
+        spmm24.load_packed(str(tmp_path / "missing.spmm24"))
+
+
+def test_bad_arguments():
+    assert spmm24._lib.spmm24_save_packed(b"/dev/null", 0, 250, 64, 1, 1) == -1   # M % 16
+    assert spmm24._lib.spmm24_save_packed(b"/dev/null", 2, 256, 64, 1, 1) == -1   # dtype
+    assert spmm24._lib.spmm24_save_packed(b"/dev/null", 0, 256, 64, None, 1) == -1
