@@ -453,6 +453,9 @@ def run_ours(args, rank, world, local_rank):
                             "busbw_GBps": round(gbytes * (world - 1) / world / (float(gt[0]) * 1e-3 / args.steps) / 1e9, 1),
                             "op": "NCCL all_gather_into_tensor of the C shards"}
 
+    if shard and args.gather and world > 1:
+        out["gather"] = time_gather(torch, dist, spmm24, calls, stream, dev, rank, world, args, flags)
+
     if args.comparators and rank == 0 and not bf16:
         out["comparators"] = run_comparators(torch, spmm24, calls, layers, acts, dev, args)
 
@@ -464,6 +467,88 @@ def run_ours(args, rank, world, local_rank):
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(out), flush=True)
+
+
+def time_gather(torch, dist, spmm24, calls, stream, dev, rank, world, args, flags):
+    """The sharded layers with their C shards gathered into a full C on every
+    rank, two ways, each timed on the device (max over ranks):
+      fused -- spmm24_launch_gather (the epilogue writes every row into all
+               ranks' full C over NVLink) + spmm24_gather_barrier, per layer;
+      nccl  -- spmm24_launch_ex into the local shard + NCCL
+               all_gather_into_tensor, per layer."""
+    fulls = [torch.empty((c["M_full"], c["N"]), dtype=torch.float16, device=dev) for c in calls]
+    flag_buf = torch.zeros(world, dtype=torch.int32, device=dev)
+    torch.cuda.synchronize(dev)
+    mine = [spmm24.ipc_export(f) for f in fulls] + [spmm24.ipc_export(flag_buf)]
+    handles = [None] * world
+    dist.all_gather_object(handles, mine)
+    ptrs = [[None] * world for _ in range(len(calls) + 1)]
+    imported = []
+    for r in range(world):
+        for i in range(len(calls) + 1):
+            if r == rank:
+                ptrs[i][r] = (fulls[i] if i < len(calls) else flag_buf).data_ptr()
+            else:
+                ptrs[i][r] = spmm24.ipc_import(handles[r][i])
+                imported.append(ptrs[i][r])
+    dist.barrier()
+    rows = [spmm24.shard_rows(c["M_full"], world, rank, 128) for c in calls]
+    epoch = [0]
+
+    def fused():
+        for i, c in enumerate(calls):
+            rc = spmm24.launch_gather(stream, c["A"], c["B"], c["E"], c["M"], c["N"], c["K"], ptrs[i], rows[i][0],
+                                      c["M_full"], 0, flags)
+            if rc != 0:
+                raise RuntimeError(f"spmm24_launch_gather: {rc} {spmm24._lib.spmm24_last_error().decode()}")
+            epoch[0] += 1
+            if spmm24.gather_barrier(stream, ptrs[-1], rank, epoch[0]) != 0:
+                raise RuntimeError("spmm24_gather_barrier failed")
+
+    equal = all(c["M_full"] % world == 0 and c["M"] * world == c["M_full"] for c in calls)
+
+    def nccl():
+        for i, c in enumerate(calls):
+            rc = spmm24._lib.spmm24_launch_ex(int(stream.cuda_stream), c["A"].data_ptr(), c["B"].data_ptr(),
+                                              c["E"].data_ptr(), c["C"].data_ptr(), c["M"], c["N"], c["K"], 0, flags)
+            if rc != 0:
+                raise RuntimeError("spmm24_launch_ex failed")
+            if equal:
+                dist.all_gather_into_tensor(fulls[i], c["C"])
+            else:
+                dist.all_gather(list(fulls[i].split([spmm24.shard_rows(c["M_full"], world, r, 128)[1] -
+                                                     spmm24.shard_rows(c["M_full"], world, r, 128)[0]
+                                                     for r in range(world)])), c["C"])
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        t = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t[0]) * 1e3 / args.steps
+
+    us_fused = timed(fused)
+    status = spmm24.device_status(dev.index)
+    us_nccl = timed(nccl)
+    dist.barrier()
+    for p in imported:
+        spmm24.ipc_close(p)
+    dist.barrier()
+    fl = sum(flops(c["M_full"], c["N"], c["K"]) for c in calls)
+    return {"fused_us_per_step": round(us_fused, 2), "nccl_us_per_step": round(us_nccl, 2),
+            "fused_tflops": round(fl / (us_fused * 1e-6) / 1e12, 2),
+            "nccl_tflops": round(fl / (us_nccl * 1e-6) / 1e12, 2),
+            "gathered_bytes_per_step": sum(2 * c["M_full"] * c["N"] for c in calls), "status": status,
+            "op": "fused: spmm24_launch_gather + spmm24_gather_barrier per layer (peer stores over NVLink); "
+                  "nccl: spmm24_launch_ex + all_gather_into_tensor per layer"}
 
 
 def run_comparators(torch, spmm24, calls, layers, acts, dev, args):
@@ -881,6 +966,8 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["pack"], default="decode")
     ap.add_argument("--comparators", action="store_true")
     ap.add_argument("--allgather", action="store_true", help="70b workload: also time the NCCL all-gather of C")
+    ap.add_argument("--gather", action="store_true",
+                    help="70b workload: time the fused SpMM + NVLink all-gather against SpMM + NCCL all-gather")
     ap.add_argument("--no-static-weights", dest="static_weights", action="store_false",
                     help="launch without SPMM24_STATIC_WEIGHTS (no kernel in the step writes the weights)")
     ap.add_argument("--no-cpu-baseline", action="store_true")

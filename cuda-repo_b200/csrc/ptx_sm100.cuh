@@ -118,6 +118,18 @@ __device__ __forceinline__ void cp_async16(void* dst_smem, const void* src) {
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
+// Bulk copy shared -> global (any GPU's memory of the node): asynchronous,
+// completion tracked per thread in bulk groups.  wait_read returns once
+// the shared-memory source may be reused; the writes themselves complete
+// later.  Addresses 16-byte aligned, size a multiple of 16.
+__device__ __forceinline__ void bulk_store(void* dst_global, const void* src_smem, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst_global),
+                 "r"(smem_u32(src_smem)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+
 // Loads for a CTA pair running cta_group::2 MMAs: the bytes are counted on
 // the mbarrier at `bar_cluster` (a shared::cluster address, normally the
 // leader CTA's barrier), not on the executing CTA's.
@@ -281,6 +293,15 @@ __device__ __forceinline__ void st_relaxed_gpu(uint32_t* p, uint32_t v) {
     asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 __device__ __forceinline__ void nanosleep_ns(uint32_t ns) { asm volatile("nanosleep.u32 %0;" ::"r"(ns)); }
+// System scope (other GPUs): flags of the cross-GPU barrier.
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 
 // Bounded wait until *flag == 1 (acquire).  Returns false after limit_ns.
 __device__ __forceinline__ bool wait_flag_bounded(const uint32_t* flag, uint64_t limit_ns) {

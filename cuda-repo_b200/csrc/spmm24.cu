@@ -282,7 +282,8 @@ std::atomic<uint64_t> g_attr_done[64];  // per kernel variant: one bit per devic
 
 // The plain SpMM: fp16, row-major C, no epilogue work.
 bool epilogue_plain_fp16(const Epilogue& e) {
-    return e.bias == nullptr && e.residual == nullptr && e.act == kActNone && e.alpha == 1.f && !e.packed && !e.bf16;
+    return e.bias == nullptr && e.residual == nullptr && e.act == kActNone && e.alpha == 1.f && !e.packed && !e.bf16 &&
+           e.gather_n == 0;
 }
 #ifdef SPMM24_TRACE
 std::atomic<long long> g_trace_next{0};  // next free CTA record in the trace buffer
@@ -381,7 +382,8 @@ cudaError_t launch_pair(const Plan& pl, cudaStream_t stream, int dev, bool pdl, 
 size_t streamk_partial_bytes(const Plan& pl) { return (size_t)pl.grid * kTileM * pl.tile_n * sizeof(float); }
 
 cudaError_t launch_impl(cudaStream_t stream, const void* A, const void* B, const uint16_t* E, void* C, int M, int N,
-                        int K, int split_k, unsigned flags, const spmm24_epilogue* user_epi = nullptr) {
+                        int K, int split_k, unsigned flags, const spmm24_epilogue* user_epi = nullptr,
+                        const spmm24_gather* gather = nullptr) {
     g_last_error[0] = '\0';
     if (!A || !B || !E || !C) return invalid("null pointer");
     if (M <= 0 || N <= 0 || K <= 0) return invalid("M, N and K must be positive");
@@ -409,8 +411,22 @@ cudaError_t launch_impl(cudaStream_t stream, const void* A, const void* B, const
         if (epi.packed && (((uintptr_t)C | (uintptr_t)epi.residual) & 15u))
             return invalid("a packed C (and its residual) must be 16-byte aligned");
     }
+    if (gather) {
+        if (gather->n_ranks < 1 || gather->n_ranks > SPMM24_MAX_GATHER_RANKS)
+            return invalid("gather: n_ranks must be 1..8");
+        if (gather->row_offset < 0 || gather->m_full < M || gather->row_offset > gather->m_full - M)
+            return invalid("gather: the shard's rows must lie inside the full C");
+        if (epi.packed) return invalid("gather: the full C is row-major");
+        for (int r = 0; r < gather->n_ranks; ++r) {
+            if (!gather->c_full[r]) return invalid("gather: null full-C pointer");
+            if ((uintptr_t)gather->c_full[r] & 15u) return invalid("gather: full-C buffers must be 16-byte aligned");
+            epi.gather_dst[r] = static_cast<uint16_t*>(gather->c_full[r]);
+        }
+        epi.gather_n = gather->n_ranks;
+        epi.gather_row0 = gather->row_offset;
+    }
     const bool plain = epi.bias == nullptr && epi.residual == nullptr && epi.act == kActNone && epi.alpha == 1.f &&
-                       !epi.packed && !epi.bf16;
+                       !epi.packed && !epi.bf16 && epi.gather_n == 0;
 
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -654,6 +670,55 @@ __global__ void spmm24_selftest_kernel(int which, unsigned long long limit_ns) {
     }
 }
 
+// Cross-GPU barrier after a fused all-gather launch: rank `rank` publishes
+// `epoch` in its slot of every rank's flag array (system-scope release,
+// after a system fence: the previous kernel's peer stores are complete at
+// the kernel boundary and ordered before the flag), then waits -- bounded --
+// until every rank's slot in its own array has reached `epoch`.
+struct BarrierArgs {
+    uint32_t* flags[SPMM24_MAX_GATHER_RANKS];  // rank r's flag array (own one included)
+    int n, rank;
+    uint32_t epoch;
+    unsigned long long limit_ns;
+};
+
+__global__ void spmm24_gather_barrier_kernel(BarrierArgs a) {
+    const int t = threadIdx.x;
+    ptx::grid_dep_wait();
+    __threadfence_system();
+    if (t < a.n) ptx::st_release_sys(a.flags[t] + a.rank, a.epoch);
+    if (t < a.n) {
+        const uint32_t* f = a.flags[a.rank] + t;
+        const uint64_t t0 = ptx::globaltimer();
+        while ((int)(ptx::ld_acquire_sys(f) - a.epoch) < 0) {
+            ptx::nanosleep_ns(100);
+            if (ptx::globaltimer() - t0 > a.limit_ns) {
+                atomicOr(&g_spmm24_status, kStatusBarrierTimeout);
+                break;
+            }
+        }
+    }
+}
+
+using GetAddressRangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+
+GetAddressRangeFn address_range_fn() {
+    static GetAddressRangeFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<GetAddressRangeFn>(p);
+    });
+    return fn;
+}
+
+// Pointers returned by spmm24_ipc_import -> the base address of the mapping.
+std::mutex g_ipc_mu;
+std::map<uintptr_t, void*>* g_ipc_bases = new std::map<uintptr_t, void*>();
+
 }  // namespace
 }  // namespace spmm24
 
@@ -680,6 +745,94 @@ extern "C" cudaError_t spmm24_launch_fused(cudaStream_t stream, const void* comp
                                            const uint16_t* metadata, void* c, int M, int N, int K, int split_k,
                                            unsigned flags, const spmm24_epilogue* epilogue) {
     return spmm24::launch_impl(stream, compressed_a, b_packed, metadata, c, M, N, K, split_k, flags, epilogue);
+}
+
+extern "C" cudaError_t spmm24_launch_gather(cudaStream_t stream, const void* compressed_a, const void* b_packed,
+                                            const uint16_t* metadata, int M, int N, int K, int split_k, unsigned flags,
+                                            const spmm24_gather* gather) {
+    if (!gather) return spmm24::record_invalid("gather: null descriptor");
+    if (gather->n_ranks < 1 || gather->n_ranks > SPMM24_MAX_GATHER_RANKS || !gather->c_full[0])
+        return spmm24::record_invalid("gather: n_ranks must be 1..8 with non-null buffers");
+    // C is only used for the alignment test of the 16-byte stores: the
+    // shard's rows in the first rank's buffer.
+    void* c = static_cast<uint16_t*>(gather->c_full[0]) + (size_t)(gather->row_offset > 0 ? gather->row_offset : 0) * N;
+    return spmm24::launch_impl(stream, compressed_a, b_packed, metadata, c, M, N, K, split_k, flags, nullptr, gather);
+}
+
+extern "C" cudaError_t spmm24_gather_barrier(cudaStream_t stream, uint32_t* const* flag_arrays, int n_ranks, int rank,
+                                             uint32_t epoch, unsigned limit_us) {
+    spmm24::clear_last_error();
+    if (!flag_arrays || n_ranks < 1 || n_ranks > SPMM24_MAX_GATHER_RANKS || rank < 0 || rank >= n_ranks)
+        return spmm24::record_invalid("barrier: bad rank or rank count");
+    if (limit_us == 0 || limit_us > 60000000u) return spmm24::record_invalid("barrier: limit_us must be 1..60e6");
+    spmm24::BarrierArgs a{};
+    for (int r = 0; r < n_ranks; ++r) {
+        if (!flag_arrays[r] || ((uintptr_t)flag_arrays[r] & 3u)) return spmm24::record_invalid("barrier: bad flag array");
+        a.flags[r] = flag_arrays[r];
+    }
+    a.n = n_ranks;
+    a.rank = rank;
+    a.epoch = epoch;
+    a.limit_ns = (unsigned long long)limit_us * 1000ull;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(32);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 0;  // plain stream order: the gather kernel has completed
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, spmm24::spmm24_gather_barrier_kernel, a);
+}
+
+extern "C" cudaError_t spmm24_ipc_export(const void* dev_ptr, spmm24_ipc_handle* out) {
+    spmm24::clear_last_error();
+    if (!dev_ptr || !out) return spmm24::record_invalid("ipc: null pointer");
+    auto fn = spmm24::address_range_fn();
+    if (!fn) return spmm24::record_invalid("ipc: cuMemGetAddressRange unavailable");
+    CUdeviceptr base = 0;
+    size_t size = 0;
+    if (fn(&base, &size, reinterpret_cast<CUdeviceptr>(dev_ptr)) != CUDA_SUCCESS)
+        return spmm24::record_invalid("ipc: not a device allocation");
+    cudaIpcMemHandle_t h;
+    cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+    if (e != cudaSuccess) return e;
+    static_assert(sizeof(h) <= sizeof(out->handle), "IPC handle size");
+    std::memset(out, 0, sizeof(*out));
+    std::memcpy(out->handle, &h, sizeof(h));
+    out->offset = (uint64_t)(reinterpret_cast<CUdeviceptr>(dev_ptr) - base);
+    return cudaSuccess;
+}
+
+extern "C" cudaError_t spmm24_ipc_import(const spmm24_ipc_handle* handle, void** dev_ptr) {
+    spmm24::clear_last_error();
+    if (!handle || !dev_ptr) return spmm24::record_invalid("ipc: null pointer");
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle->handle, sizeof(h));
+    void* base = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return e;
+    void* p = static_cast<uint8_t*>(base) + handle->offset;
+    {
+        std::lock_guard<std::mutex> lk(spmm24::g_ipc_mu);
+        (*spmm24::g_ipc_bases)[reinterpret_cast<uintptr_t>(p)] = base;
+    }
+    *dev_ptr = p;
+    return cudaSuccess;
+}
+
+extern "C" cudaError_t spmm24_ipc_close(void* dev_ptr) {
+    spmm24::clear_last_error();
+    void* base = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(spmm24::g_ipc_mu);
+        auto it = spmm24::g_ipc_bases->find(reinterpret_cast<uintptr_t>(dev_ptr));
+        if (it == spmm24::g_ipc_bases->end()) return spmm24::record_invalid("ipc: not an imported pointer");
+        base = it->second;
+        spmm24::g_ipc_bases->erase(it);
+    }
+    return cudaIpcCloseMemHandle(base);
 }
 
 extern "C" size_t spmm24_workspace_bytes(int, int, int, int) { return 0; }

@@ -36,6 +36,7 @@ constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s bound on any wait
 constexpr uint32_t kStatusProducerTimeout = 1u;
 constexpr uint32_t kStatusMmaTimeout = 2u;
 constexpr uint32_t kStatusEpilogueTimeout = 4u;
+constexpr uint32_t kStatusBarrierTimeout = 8u;  // cross-GPU barrier of the fused all-gather
 
 // Sticky device status word (per device, per process).  Bounded waits that
 // give up OR their bit in; the host reads and clears it through
@@ -158,6 +159,8 @@ __device__ __forceinline__ void mma_stage(uint32_t st_addr, uint32_t meta_col, u
 // (m, n) at ((n / 8) * M + m) * 8 + n % 8, pad columns zero).
 constexpr int kActNone = 0, kActRelu = 1, kActSilu = 2, kActGelu = 3;
 
+constexpr int kMaxGatherRanks = 8;
+
 struct Epilogue {
     const uint16_t* bias;      // M values in C's type, or null
     const uint16_t* residual;  // same type and layout as C, or null
@@ -165,7 +168,35 @@ struct Epilogue {
     int act;                   // kAct*
     int packed;                // 1: C (and residual) in packed-B strips
     int bf16;                  // 1: A, B, C, bias and residual are bf16; 0: fp16
+    // Fused all-gather of an M-shard: each output row gm is written to row
+    // gather_row0 + gm of every rank's full row-major C (peer pointers
+    // reached over NVLink), instead of to C.  gather_n == 0: off.
+    int gather_n;
+    int gather_row0;
+    uint16_t* gather_dst[kMaxGatherRanks];
 };
+
+// Stores 16 bytes of row-major output (row gm of the shard, columns gn..) to
+// C, or to every rank's full C when the epilogue gathers.
+__device__ __forceinline__ void store_row16(uint16_t* C, const Epilogue& e, int gm, int gn, int N, uint4 v) {
+    if (e.gather_n) {
+        const size_t off = (size_t)(e.gather_row0 + gm) * N + gn;
+        for (int d = 0; d < e.gather_n; ++d) *reinterpret_cast<uint4*>(e.gather_dst[d] + off) = v;
+    } else {
+        *reinterpret_cast<uint4*>(C + (size_t)gm * N + gn) = v;
+    }
+}
+// The element-wise form (N % 8 != 0 or a misaligned C).
+__device__ __forceinline__ void store_row_elems(uint16_t* C, const Epilogue& e, int gm, int gn, int N, const uint32_t* w,
+                                                int lim) {
+    if (e.gather_n) {
+        const size_t off = (size_t)(e.gather_row0 + gm) * N + gn;
+        for (int d = 0; d < e.gather_n; ++d)
+            for (int i = 0; i < lim; ++i) e.gather_dst[d][off + i] = (uint16_t)(w[i >> 1] >> (16 * (i & 1)));
+    } else {
+        for (int i = 0; i < lim; ++i) C[(size_t)gm * N + gn + i] = (uint16_t)(w[i >> 1] >> (16 * (i & 1)));
+    }
+}
 
 __device__ __forceinline__ float elem_to_f32(uint16_t h, int bf16) {
     if (bf16) return __uint_as_float((uint32_t)h << 16);
@@ -288,11 +319,12 @@ __device__ __forceinline__ void epilogue_store8(uint16_t* C, const float* v, con
     uint32_t w[4];
     if (plain) round8(v, lim, e.bf16, w);
     else epilogue8(v, e, gm, gn, M, N, vec_rowmajor, w);
-    const size_t base = c_offset(e, gm, gn, M, N);
-    if (e.packed || vec_rowmajor) {
-        *reinterpret_cast<uint4*>(C + base) = make_uint4(w[0], w[1], w[2], w[3]);
+    if (e.packed) {
+        *reinterpret_cast<uint4*>(C + c_offset(e, gm, gn, M, N)) = make_uint4(w[0], w[1], w[2], w[3]);
+    } else if (vec_rowmajor) {
+        store_row16(C, e, gm, gn, N, make_uint4(w[0], w[1], w[2], w[3]));
     } else {
-        for (int i = 0; i < lim; ++i) C[base + i] = (uint16_t)(w[i >> 1] >> (16 * (i & 1)));
+        store_row_elems(C, e, gm, gn, N, w, lim);
     }
 }
 

@@ -676,7 +676,23 @@ spmm24_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                     out = *reinterpret_cast<const uint4*>(hst + (size_t)r * C_::C_PITCH + c * 8);
                 }
             };
-            if (p.epi.packed) {
+            if (p.epi.gather_n && !has_res && vec_ok) {
+                // Gathered output: every staged row goes to every rank's full C
+                // as one bulk copy, spread over the threads; a CTA waits only
+                // until its shared memory has been read, so the NVLink writes
+                // drain while the next tile computes.
+                ptx::fence_proxy_async_smem();  // the staged rows, written by other threads, to the async proxy
+                const int ncols = min(C_::TILE_N, p.N - gn0);
+                for (int idx = etid; idx < kTileM * p.epi.gather_n; idx += kPairThreads) {
+                    const int r = idx % kTileM, d = idx / kTileM;
+                    const int gmr = gm0 + r;
+                    if (gmr >= p.M) continue;
+                    ptx::bulk_store(p.epi.gather_dst[d] + (size_t)(p.epi.gather_row0 + gmr) * p.N + gn0,
+                                    hst + (size_t)r * C_::C_PITCH, (uint32_t)ncols * 2u);
+                }
+                ptx::bulk_commit();
+                ptx::bulk_wait_read_all();
+            } else if (p.epi.packed) {
                 // consecutive threads take consecutive rows of a strip
                 for (int idx = etid; idx < ITEMS; idx += kPairThreads) {
                     const int r = idx % kTileM, c = idx / kTileM;
@@ -697,12 +713,10 @@ spmm24_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                     uint4 out;
                     chunk_out(r, c, gmr, gn, out);
                     if (vec_ok) {
-                        *reinterpret_cast<uint4*>(p.C + (size_t)gmr * p.N + gn) = out;
+                        store_row16(p.C, p.epi, gmr, gn, p.N, out);
                     } else {
                         const uint32_t w[4] = {out.x, out.y, out.z, out.w};
-#pragma unroll
-                        for (int e = 0; e < 8; ++e)
-                            if (gn + e < p.N) p.C[(size_t)gmr * p.N + gn + e] = (uint16_t)(w[e >> 1] >> (16 * (e & 1)));
+                        store_row_elems(p.C, p.epi, gmr, gn, p.N, w, min(8, p.N - gn));
                     }
                 }
             }

@@ -64,6 +64,31 @@ _lib.spmm24_load_packed.argtypes = [ctypes.c_char_p, _vp, _vp]
 _lib.spmm24_load_packed.restype = ctypes.c_int
 
 
+class Gather(ctypes.Structure):
+    """spmm24_gather (include/spmm24/SpMM_API.h)."""
+    _fields_ = [("c_full", ctypes.c_void_p * 8), ("n_ranks", ctypes.c_int), ("row_offset", ctypes.c_int),
+                ("m_full", ctypes.c_int)]
+
+
+class IpcHandle(ctypes.Structure):
+    """spmm24_ipc_handle (include/spmm24/SpMM_API.h)."""
+    _fields_ = [("handle", ctypes.c_ubyte * 64), ("offset", ctypes.c_uint64)]
+
+
+_lib.spmm24_launch_gather.argtypes = [_vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                      ctypes.c_uint, ctypes.POINTER(Gather)]
+_lib.spmm24_launch_gather.restype = ctypes.c_int
+_lib.spmm24_gather_barrier.argtypes = [_vp, ctypes.POINTER(ctypes.c_void_p), ctypes.c_int, ctypes.c_int,
+                                       ctypes.c_uint32, ctypes.c_uint]
+_lib.spmm24_gather_barrier.restype = ctypes.c_int
+_lib.spmm24_ipc_export.argtypes = [_vp, ctypes.POINTER(IpcHandle)]
+_lib.spmm24_ipc_export.restype = ctypes.c_int
+_lib.spmm24_ipc_import.argtypes = [ctypes.POINTER(IpcHandle), ctypes.POINTER(ctypes.c_void_p)]
+_lib.spmm24_ipc_import.restype = ctypes.c_int
+_lib.spmm24_ipc_close.argtypes = [_vp]
+_lib.spmm24_ipc_close.restype = ctypes.c_int
+
+
 class Epilogue(ctypes.Structure):
     """spmm24_epilogue (include/spmm24/SpMM_API.h)."""
     _fields_ = [("bias", ctypes.c_void_p), ("residual", ctypes.c_void_p), ("alpha", ctypes.c_float),
@@ -257,6 +282,53 @@ def pack_b_device(b, K: int, N: int, out=None, stream=None):
 
 
 # ---------------------------------------------------------- sharding
+# ---------------------------------------- fused all-gather across GPUs
+def ipc_export(tensor) -> bytes:
+    """spmm24_ipc_export: a 72-byte description of a device tensor's memory
+    that another process of the node can map with ipc_import."""
+    h = IpcHandle()
+    rc = _lib.spmm24_ipc_export(_ptr(tensor), ctypes.byref(h))
+    if rc != CUDA_SUCCESS:
+        raise SpmmError(rc, "spmm24_ipc_export")
+    return bytes(h)
+
+
+def ipc_import(handle: bytes) -> int:
+    """spmm24_ipc_import: maps a peer's exported memory; returns the device address."""
+    h = IpcHandle.from_buffer_copy(handle)
+    out = ctypes.c_void_p()
+    rc = _lib.spmm24_ipc_import(ctypes.byref(h), ctypes.byref(out))
+    if rc != CUDA_SUCCESS:
+        raise SpmmError(rc, "spmm24_ipc_import")
+    return int(out.value)
+
+
+def ipc_close(ptr: int) -> None:
+    rc = _lib.spmm24_ipc_close(ptr)
+    if rc != CUDA_SUCCESS:
+        raise SpmmError(rc, "spmm24_ipc_close")
+
+
+def launch_gather(stream, compressed_a, b_packed, metadata, M: int, N: int, K: int, c_full_ptrs, row_offset: int,
+                  m_full: int, split_k: int = 0, flags: int = 0) -> int:
+    """spmm24_launch_gather: this rank's M-shard, written into every rank's
+    full C (c_full_ptrs in rank order, own buffer included)."""
+    if len(c_full_ptrs) > 8:
+        raise ValueError("at most 8 ranks (SPMM24_MAX_GATHER_RANKS)")
+    g = Gather()
+    for i, p in enumerate(c_full_ptrs):
+        g.c_full[i] = _ptr(p)
+    g.n_ranks, g.row_offset, g.m_full = len(c_full_ptrs), row_offset, m_full
+    return _lib.spmm24_launch_gather(_stream_handle(stream), _ptr(compressed_a), _ptr(b_packed), _ptr(metadata), M, N,
+                                     K, split_k, flags, ctypes.byref(g))
+
+
+def gather_barrier(stream, flag_ptrs, rank: int, epoch: int, limit_us: int = 2_000_000) -> int:
+    """spmm24_gather_barrier over the ranks' flag arrays (rank order)."""
+    arr = (ctypes.c_void_p * len(flag_ptrs))(*[_ptr(p) for p in flag_ptrs])
+    return _lib.spmm24_gather_barrier(_stream_handle(stream), arr, len(flag_ptrs), rank, epoch, limit_us)
+
+
 def shard_rows(M: int, parts: int, index: int, align: int = 128) -> tuple[int, int]:
     """[row_begin, row_end) of shard `index` of `parts` (split along M)."""
     b, e = ctypes.c_int(), ctypes.c_int()

@@ -117,6 +117,50 @@ cudaError_t spmm24_launch_fused(cudaStream_t stream, const void* compressed_a, c
                                 const uint16_t* metadata, void* c, int M, int N, int K, int split_k, unsigned flags,
                                 const spmm24_epilogue* epilogue);
 
+/* Fused SpMM + all-gather across the GPUs of one node (no counterpart in
+ * the reference, which runs on one GPU).  For an M-sharded layer each rank
+ * launches its shard (compressed_a / metadata = the shard's rows, M = the
+ * shard's row count) and the epilogue writes every output row straight into
+ * row row_offset + m of every rank's full C (row-major, m_full x N) over
+ * NVLink -- no separate collective.  c_full[r] is rank r's buffer as seen
+ * from this process (this rank's own buffer, and the peers' buffers opened
+ * with spmm24_ipc_import); all 16-byte aligned.  flags: as for
+ * spmm24_launch_ex.  The peers' rows are complete only after
+ * spmm24_gather_barrier on every rank. */
+#define SPMM24_MAX_GATHER_RANKS 8
+typedef struct spmm24_gather {
+    void* c_full[SPMM24_MAX_GATHER_RANKS];
+    int n_ranks;
+    int row_offset;
+    int m_full;
+} spmm24_gather;
+cudaError_t spmm24_launch_gather(cudaStream_t stream, const void* compressed_a, const void* b_packed,
+                                 const uint16_t* metadata, int M, int N, int K, int split_k, unsigned flags,
+                                 const spmm24_gather* gather);
+
+/* Cross-GPU barrier on `stream` after spmm24_launch_gather: rank `rank`
+ * writes `epoch` into slot `rank` of every rank's flag array
+ * (flag_arrays[r]: n_ranks u32 of rank r, peers' opened with
+ * spmm24_ipc_import, zero-initialised once), then waits until all n_ranks
+ * slots of its own array have reached `epoch` (use a counter that grows by
+ * one per call).  The wait is bounded by limit_us; a barrier that gives up
+ * sets bit 8 of the device status word (spmm24_device_status) instead of
+ * hanging. */
+cudaError_t spmm24_gather_barrier(cudaStream_t stream, uint32_t* const* flag_arrays, int n_ranks, int rank,
+                                  uint32_t epoch, unsigned limit_us);
+
+/* CUDA IPC for the peer buffers: spmm24_ipc_export describes a device
+ * pointer (any address inside an allocation, e.g. a tensor of a caching
+ * allocator) for another process of the node; spmm24_ipc_import maps it
+ * there (peer access over NVLink) and spmm24_ipc_close unmaps it. */
+typedef struct spmm24_ipc_handle {
+    unsigned char handle[64];
+    uint64_t offset;
+} spmm24_ipc_handle;
+cudaError_t spmm24_ipc_export(const void* dev_ptr, spmm24_ipc_handle* out);
+cudaError_t spmm24_ipc_import(const spmm24_ipc_handle* handle, void** dev_ptr);
+cudaError_t spmm24_ipc_close(void* dev_ptr);
+
 /* Allocation-free launch (no counterpart in the reference).  For callers
  * that cannot let a library call cudaMalloc: applications whose device
  * memory is owned by their own pool or arena (a framework allocator, a

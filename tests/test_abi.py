@@ -106,6 +106,31 @@ def test_host_bf16_prune_matches_oracle():
     assert np.array_equal(spmm24.prune_2of4_bf16(a, 64, 128), O.prune_magnitude_2of4_bf16(a, 64, 128))
 
 
+def test_gather_rejects_bad_arguments_without_gpu():
+    L = spmm24._lib
+    A, B, E = 0x10000, 0x20000, 0x30000
+    ok = [0x40000, 0x50000]
+
+    def gather(ptrs, row_offset=0, m_full=512, M=256):
+        return spmm24.launch_gather(None, A, B, E, M, 16, 256, ptrs, row_offset, m_full)
+
+    assert gather([]) == spmm24.CUDA_ERROR_INVALID_VALUE
+    g = spmm24.Gather()
+    g.c_full[0], g.n_ranks, g.row_offset, g.m_full = ok[0], 9, 0, 512        # more than 8 ranks
+    assert L.spmm24_launch_gather(None, A, B, E, 256, 16, 256, 0, 0, ctypes.byref(g)) == spmm24.CUDA_ERROR_INVALID_VALUE
+    with pytest.raises(ValueError):
+        gather(ok * 5)
+    assert gather(ok, row_offset=300) == spmm24.CUDA_ERROR_INVALID_VALUE      # shard past the full C
+    assert gather(ok, m_full=128) == spmm24.CUDA_ERROR_INVALID_VALUE
+    assert gather([0x40000, 0x50008]) == spmm24.CUDA_ERROR_INVALID_VALUE       # misaligned peer buffer
+    assert "aligned" in L.spmm24_last_error().decode()
+    assert spmm24.gather_barrier(None, [0x60000, 0x70000], 2, 1) == spmm24.CUDA_ERROR_INVALID_VALUE  # rank >= n
+    assert spmm24.gather_barrier(None, [0x60000, 0x70002], 0, 1) == spmm24.CUDA_ERROR_INVALID_VALUE  # misaligned
+    assert spmm24.gather_barrier(None, [0x60000], 0, 1, limit_us=0) == spmm24.CUDA_ERROR_INVALID_VALUE
+    assert L.spmm24_ipc_export(None, None) == spmm24.CUDA_ERROR_INVALID_VALUE
+    assert L.spmm24_ipc_close(0x1234) == spmm24.CUDA_ERROR_INVALID_VALUE      # never imported
+
+
 def test_device_packer_rejects_bad_arguments_without_gpu():
     L = spmm24._lib
     ok = 0x10000

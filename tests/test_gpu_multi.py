@@ -1,0 +1,96 @@
+"""The fused SpMM + all-gather across two GPUs (spmm24_launch_gather +
+spmm24_gather_barrier over CUDA IPC peer buffers), run as two processes, one
+per GPU.  Skipped where fewer than two GPUs are visible.  Each rank's full C
+must equal, bit for bit, the shards every rank computes locally with the
+plain launch."""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, shapes):
+    import sys
+    from datetime import timedelta
+
+    sys.path.insert(0, os.path.join(REPO, "cuda-repo_b200"))
+    import torch
+    import torch.distributed as dist
+
+    import spmm24
+
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=60))
+    flags = torch.zeros(world, dtype=torch.int32, device=dev)
+    epoch = 0
+    for (M, N, K, split) in shapes:
+        rng = np.random.default_rng(M + N + K)   # same weights and activations on every rank
+        a = rng.standard_normal((M, K)).astype(np.float16).view(np.uint16)
+        vals, meta = spmm24.compress_reordered(spmm24.prune_2of4(a, M, K), M, K)
+        b = rng.uniform(-1, 1, (K, N)).astype(np.float16).view(np.uint16)
+        bp = torch.from_numpy(spmm24.pack_b(b, K, N).view(np.int16)).to(dev)
+        A = torch.from_numpy(vals.view(np.int16)).to(dev)
+        E = torch.from_numpy(meta.view(np.int16)).to(dev)
+        # expected: every shard with the plain launch, on this GPU
+        expect = torch.empty((M, N), dtype=torch.float16, device=dev)
+        rows = [spmm24.shard_rows(M, world, r, 128) for r in range(world)]
+        for (r0, r1) in rows:
+            Av, Ev = spmm24.shard_views(A, E, M, K, r0, r1)
+            assert spmm24.launch(None, Av, bp, Ev, expect[r0:r1], r1 - r0, N, K, None, split) == 0
+        # the gathered C: this rank's buffer + the peers' through IPC
+        c_full = torch.full((M, N), float("nan"), dtype=torch.float16, device=dev)
+        torch.cuda.synchronize(dev)
+        handles = [None] * world
+        dist.all_gather_object(handles, (spmm24.ipc_export(c_full), spmm24.ipc_export(flags)))
+        peers_c, peers_f = [], []
+        for r in range(world):
+            if r == rank:
+                peers_c.append(c_full.data_ptr())
+                peers_f.append(flags.data_ptr())
+            else:
+                peers_c.append(spmm24.ipc_import(handles[r][0]))
+                peers_f.append(spmm24.ipc_import(handles[r][1]))
+        dist.barrier()
+        r0, r1 = rows[rank]
+        Av, Ev = spmm24.shard_views(A, E, M, K, r0, r1)
+        epoch += 1
+        s = torch.cuda.current_stream(dev)
+        assert spmm24.launch_gather(s, Av, bp, Ev, r1 - r0, N, K, peers_c, r0, M, split, spmm24.STATIC_WEIGHTS) == 0, \
+            spmm24._lib.spmm24_last_error().decode()
+        assert spmm24.gather_barrier(s, peers_f, rank, epoch) == 0
+        torch.cuda.synchronize(dev)
+        assert spmm24.device_status(rank) == 0
+        assert torch.equal(c_full, expect), (rank, M, N, K)
+        dist.barrier()  # every rank is done with the peers' buffers before they go away
+        for r in range(world):
+            if r != rank:
+                spmm24.ipc_close(peers_c[r])
+                spmm24.ipc_close(peers_f[r])
+        dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_fused_allgather_two_gpus():
+    import torch
+    import torch.multiprocessing as mp
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    if not torch.cuda.can_device_access_peer(0, 1):
+        pytest.skip("no peer access between GPU 0 and GPU 1")
+    # decode (cluster kernel, split-K 4 and auto), mid N, prefill (pair kernel), ragged N
+    shapes = [(1024, 16, 1024, 4), (2048, 32, 2048, 0), (1024, 64, 512, 0), (1024, 512, 1024, 0), (512, 40, 512, 0)]
+    mp.spawn(_worker, args=(2, _free_port(), shapes), nprocs=2, join=True)
