@@ -106,10 +106,9 @@ using CV32 = ClusterVariant<32, 7>;
 using CV64 = ClusterVariant<64, 6>;
 using CV128 = ClusterVariant<128, 4>;
 using CV256 = ClusterVariant<256, 2>;
-// Pair tiles: 256 x 256 with a 4-stage ring (one CTA per SM) or 256 x 128
-// with a 3-stage ring (two CTAs per SM).
-using PairWide = PairCfg<128, 4>;
-using PairNarrow = PairCfg<64, 3>;
+// Pair tiles: 256 x 256 with a 4-stage ring (one CTA per SM).
+constexpr int kPairStages = 4;
+using PairC = PairCfg<kPairStages>;
 using SV16 = StreamKVariant<16, 8>;
 using SV32 = StreamKVariant<32, 8>;
 // Shallow rings (about 92 KB of shared memory): two CTAs fit on one SM, so
@@ -122,7 +121,6 @@ using SV32s = StreamKVariant<32, 4>;
 struct Plan {
     Path path;
     bool shallow;      // 4-stage ring, two CTAs per SM (narrow N only)
-    bool split_issue;  // pair path: A/metadata and B loads issued by two warps
     int tile_n;
     int stages;
     int split;  // cluster path: CTAs per cluster
@@ -192,15 +190,26 @@ Plan make_plan(int M, int N, int K, int split_k, int sms, bool plain = true) {
     if (pair_ok && (pair_env == 1 || (pair_env != 0 && N > 128))) {
         p.path = Path::kPair;
         p.shallow = false;
-        const bool narrow = env_int("SPMM24_PAIR_N", 256) == 128;  // tuning override
-        p.split_issue = env_int("SPMM24_PAIR_ISSUE", 1) == 2;      // tuning override
-        p.tile_n = narrow ? PairNarrow::TILE_N : PairWide::TILE_N;
-        p.stages = narrow ? 3 : 4;
-        p.smem = narrow ? PairNarrow::SMEM_ALLOC : PairWide::SMEM_ALLOC;
+        p.tile_n = PairC::TILE_N;
+        p.stages = kPairStages;
+        p.smem = PairC::SMEM_ALLOC;
         p.m_tiles = (M + 2 * kTileM - 1) / (2 * kTileM);
         p.n_tiles = (N + p.tile_n - 1) / p.tile_n;
-        p.split = 1;
-        p.grid = 2 * p.m_tiles * p.n_tiles;
+        // Few tiles and long K (at most half a wave of pairs, at least 48
+        // stages): two pairs per tile, each taking half of K (a cluster of 4
+        // with an on-chip reduction).  Measured: 4096 x 512 x 11008 -10%
+        // time; shorter K or more tiles lose (clusters of 4 leave SMs of
+        // every GPC idle, and the 128 KB exchange costs a few us per tile).
+        const long long ptiles = (long long)p.m_tiles * p.n_tiles;
+        const int pair_split_env = env_int("SPMM24_PAIR_SPLIT", 0);  // tuning override: 1 or 2
+        int ps = 1;
+        if (pair_split_env == 1 || pair_split_env == 2)
+            ps = pair_split_env;
+        else if (split_k == 0 && 2 * ptiles <= (long long)(sms / 2) && p.stages_total >= 48)
+            ps = 2;
+        if (p.stages_total < 2) ps = 1;
+        p.split = ps;
+        p.grid = 2 * ps * (int)ptiles;
         return p;
     }
     p.path = Path::kCluster;
@@ -358,25 +367,22 @@ cudaError_t launch_streamk(const Plan& pl, cudaStream_t stream, int dev, bool pd
     return launch_kernel(kern, dim3((unsigned)pl.grid, 1, 1), V::C_::SMEM_ALLOC, stream, 1u, pdl, ta, tb, te, kp);
 }
 
-template <int HALF_N, int STAGES, bool SPLIT>
+template <bool KSPLIT>
 cudaError_t launch_pair_v(const Plan& pl, cudaStream_t stream, int dev, bool pdl, const CUtensorMap& ta,
                           const CUtensorMap& tb, const CUtensorMap& te, const PairParams& kp, int idx) {
-    using C_ = PairCfg<HALF_N, STAGES>;
     const bool general = !epilogue_plain_fp16(kp.epi);
-    auto kern = general ? spmm24_pair_kernel<HALF_N, STAGES, SPLIT, true> : spmm24_pair_kernel<HALF_N, STAGES, SPLIT, false>;
-    cudaError_t e = prepare(kern, C_::SMEM_ALLOC, dev, idx + (general ? kEpiSlot : 0));
+    auto kern = general ? spmm24_pair_kernel<kPairStages, true, KSPLIT> : spmm24_pair_kernel<kPairStages, false, KSPLIT>;
+    cudaError_t e = prepare(kern, PairC::SMEM_ALLOC, dev, idx + (general ? kEpiSlot : 0));
     if (e != cudaSuccess) return e;
-    return launch_kernel(kern, dim3(2u, (unsigned)pl.n_tiles, (unsigned)pl.m_tiles), C_::SMEM_ALLOC, stream, 2u, pdl,
-                         ta, tb, te, kp, kPairThreads);
+    const unsigned cl = KSPLIT ? 4u : 2u;
+    return launch_kernel(kern, dim3(cl, (unsigned)pl.n_tiles, (unsigned)pl.m_tiles), PairC::SMEM_ALLOC, stream, cl,
+                         pdl, ta, tb, te, kp, kPairThreads);
 }
 
 cudaError_t launch_pair(const Plan& pl, cudaStream_t stream, int dev, bool pdl, const CUtensorMap& ta,
                         const CUtensorMap& tb, const CUtensorMap& te, const PairParams& kp) {
-    if (pl.tile_n == PairNarrow::TILE_N)
-        return pl.split_issue ? launch_pair_v<64, 3, true>(pl, stream, dev, pdl, ta, tb, te, kp, 14)
-                              : launch_pair_v<64, 3, false>(pl, stream, dev, pdl, ta, tb, te, kp, 13);
-    return pl.split_issue ? launch_pair_v<128, 4, true>(pl, stream, dev, pdl, ta, tb, te, kp, 12)
-                          : launch_pair_v<128, 4, false>(pl, stream, dev, pdl, ta, tb, te, kp, 11);
+    return pl.split == 2 ? launch_pair_v<true>(pl, stream, dev, pdl, ta, tb, te, kp, 12)
+                         : launch_pair_v<false>(pl, stream, dev, pdl, ta, tb, te, kp, 11);
 }
 
 size_t streamk_partial_bytes(const Plan& pl) { return (size_t)pl.grid * kTileM * pl.tile_n * sizeof(float); }
@@ -467,7 +473,7 @@ cudaError_t launch_impl(cudaStream_t stream, const void* A, const void* B, const
     {
         cuuint64_t dims[4] = {128, (cuuint64_t)(K / 64), 4, (cuuint64_t)((N + 7) / 8)};
         cuuint64_t str[3] = {1024, 256, (cuuint64_t)16 * K};
-        const int cta_n = pl.path == Path::kPair ? pl.tile_n / 2 : pl.tile_n;  // columns one CTA loads
+        const int cta_n = pl.path == Path::kPair ? PairC::HALF_N : pl.tile_n;  // columns one CTA loads
         cuuint32_t box[4] = {128, 2, 4, (cuuint32_t)(cta_n / 8)};
         if (!encode(&tb, 4, B, dims, str, box)) return invalid("TMA descriptor for B could not be encoded");
     }
@@ -482,6 +488,10 @@ cudaError_t launch_impl(cudaStream_t stream, const void* A, const void* B, const
     const bool pdl = !(flags & SPMM24_NO_PDL);
     const int wstatic = (flags & SPMM24_STATIC_WEIGHTS) ? 1 : 0;
     if (pl.path == Path::kPair) {
+        if (epi.residual && pl.split != 1) {  // the partner partial would overlap the residual's staging
+            pl.split = 1;
+            pl.grid = 2 * pl.m_tiles * pl.n_tiles;
+        }
         PairParams kp;
         kp.C = static_cast<uint16_t*>(C);
         kp.epi = epi;
@@ -490,6 +500,7 @@ cudaError_t launch_impl(cudaStream_t stream, const void* A, const void* B, const
         kp.K = K;
         kp.stages_total = K / 128;
         kp.weights_static = wstatic;
+        kp.split = pl.split;
         return launch_pair(pl, stream, dev, pdl, ta, tb, te, kp);
     }
     if (pl.path == Path::kStreamK) {

@@ -65,6 +65,7 @@ struct PairParams {
     int M, N, K;
     int stages_total;  // K / 128 (the pair kernel requires K % 128 == 0)
     int weights_static;
+    int split;         // pairs per cluster along K (1 or 2)
     Epilogue epi;
     SPMM24_TRACE_FIELD
 };
@@ -335,9 +336,13 @@ spmm24_cluster_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_cons
 // CTA per SM) or 64 (128-wide tiles, 3-stage ring of 102 KB, two CTAs per
 // SM: TMA streams into shared memory at a bounded rate per CTA, so two
 // resident CTAs feed an SM about twice as fast as one).
-template <int HALF_N_, int STAGES>
+// A CTA pair computes a 256 x 256 tile; each CTA holds 128 rows of A and 128
+// columns of B.  With a K split, a cluster of two pairs computes the tile:
+// pair 1 sends its fp32 partial accumulator to pair 0 through distributed
+// shared memory, and pair 0 adds it before the epilogue.
+template <int STAGES>
 struct PairCfg {
-    static constexpr int HALF_N = HALF_N_;               // columns of B / C per CTA
+    static constexpr int HALF_N = 128;                   // columns of B / C per CTA
     static constexpr int TILE_N = 2 * HALF_N;            // columns per pair
     static constexpr int TILE_M = 2 * kTileM;            // rows per pair
     static constexpr int A_BYTES = 8 * 8 * 256;          // this CTA's 128 rows x 128 logical K
@@ -346,24 +351,25 @@ struct PairCfg {
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + E_BYTES;
     static constexpr int RING_BYTES = STAGES * STAGE_BYTES;
     static constexpr int BAR_OFFSET = RING_BYTES;
-    static constexpr int NUM_BARS = 2 * STAGES + 1;
+    static constexpr int NUM_BARS = 2 * STAGES + 3;  // full, empty, acc_full, recv (pair 0), free (pair 1)
     static constexpr int HOLDER_OFFSET = BAR_OFFSET + NUM_BARS * 8;
     static constexpr int SMEM_BYTES = HOLDER_OFFSET + 16;
     static constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;
     static constexpr int META_COL = TILE_N;  // accumulator: TILE_N fp32 columns
     static constexpr int TMEM_NEED = META_COL + 4 * STAGES;
     static constexpr int TMEM_COLS = TMEM_NEED <= 128 ? 128 : TMEM_NEED <= 256 ? 256 : 512;
-    // Two CTAs per SM when both rings fit in the SM's 228 KB (1 KB reserved per CTA).
-    static constexpr int CTAS_PER_SM = 2 * (SMEM_ALLOC + 1024) <= 233472 ? 2 : 1;
     static constexpr int C_PITCH = TILE_N + 8;  // halves per staged output row (bank-shifted)
     static constexpr int F_PITCH = TILE_N + 4;  // floats per staged fp32 row (epilogue with a residual)
     static constexpr int RES_OFFSET = kTileM * F_PITCH * 4;  // residual tile after the fp32 staging
-    static_assert(HALF_N == 64 || HALF_N == 128, "pair tiles are 128 or 256 columns wide");
+    // K split: the partner pair's partial accumulator, fp32 rows of F_PITCH,
+    // after the 16-bit output staging.
+    static constexpr int RECV_OFFSET = ((kTileM * C_PITCH * 2 + 1023) / 1024) * 1024;
+    static constexpr uint32_t RECV_BYTES = (uint32_t)kTileM * TILE_N * 4;  // bytes the partner sends
     static_assert(TMEM_NEED <= 512, "TMEM overflow");
-    static_assert(CTAS_PER_SM * TMEM_COLS <= 512, "co-resident CTAs must fit in TMEM together");
     static_assert(SMEM_ALLOC <= 232448, "shared memory overflow");
     static_assert(kTileM * C_PITCH * 2 <= RING_BYTES, "output staging does not fit");
     static_assert(RES_OFFSET + kTileM * TILE_N * 2 <= RING_BYTES, "fp32 staging + residual tile do not fit");
+    static_assert(RECV_OFFSET + kTileM * F_PITCH * 4 <= RING_BYTES, "16-bit staging + partner partial do not fit");
 };
 
 constexpr int kPairGroupM = 8;  // tile rows per rasterisation group
@@ -375,24 +381,30 @@ __host__ __device__ constexpr uint32_t pair_idesc() {
     return (1u << 2) | (1u << 4) | (1u << 16) | ((uint32_t)(TILE_N >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
 }
 
-// SPLIT_ISSUE: warp 0 issues the A and metadata loads and warp 2 the B loads
-// (before it joins the epilogue), so two threads of the CTA keep TMA busy.
-// EPI: the general epilogue, as for spmm24_cluster_kernel.
-template <int HALF_N, int STAGES, bool SPLIT_ISSUE, bool EPI>
-__global__ void __launch_bounds__(kPairThreads, PairCfg<HALF_N, STAGES>::CTAS_PER_SM)
+// EPI: the general epilogue, as for spmm24_cluster_kernel.  KSPLIT: a
+// cluster of two pairs, each taking half of the 128-K stages (p.split == 2;
+// not with a residual, whose staging the partner partial would overlap).
+template <int STAGES, bool EPI, bool KSPLIT>
+__global__ void __launch_bounds__(kPairThreads, 1)
 spmm24_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmE, const PairParams p) {
-    using C_ = PairCfg<HALF_N, STAGES>;
+    using C_ = PairCfg<STAGES>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + C_::BAR_OFFSET);  // used in the leader only
     uint64_t* empty = full + STAGES;
     uint64_t* acc_full = empty + STAGES;
+    uint64_t* recv_bar = acc_full + 1;  // pair 0 of a K split: the partner's partial has arrived
+    uint64_t* free_bar = acc_full + 2;  // pair 1 of a K split: pair 0 is ready to receive
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + C_::HOLDER_OFFSET);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const uint32_t rank = ptx::cluster_ctarank();  // 0 = leader (issues the MMAs), 1 = peer
+    const uint32_t crank = ptx::cluster_ctarank();
+    const uint32_t rank = crank & 1u;         // within the pair: 0 = leader (issues the MMAs), 1 = peer
+    const uint32_t lead_rank = crank & ~1u;   // the pair's leader in the cluster
+    const int kpart = KSPLIT ? (int)(crank >> 1) : 0;  // which half of K this pair computes
+    const uint16_t pair_mask = (uint16_t)(0x3u << (2 * kpart));
     const bool leader = rank == 0;
     // Grouped rasterisation: consecutive pairs walk down a group of
     // kPairGroupM tile rows before moving to the next tile column, so the A
@@ -410,7 +422,11 @@ spmm24_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
     }
     const int band0 = (m_tile * C_::TILE_M + (int)rank * kTileM) / 16;
     const int strip0 = (n_tile * C_::TILE_N + (int)rank * C_::HALF_N) / 8;
-    const int st_count = p.stages_total;
+    // This pair's 128-K stages: all of them, or its half under a K split.
+    const int nsplit = KSPLIT ? 2 : 1;
+    const int st_base = p.stages_total / nsplit, st_rem = p.stages_total % nsplit;
+    const int st_begin = kpart * st_base + min(kpart, st_rem);
+    const int st_count = st_base + (kpart < st_rem ? 1 : 0);
 
     if (threadIdx.x == 0) {
         SPMM24_STAMP(0);
@@ -419,6 +435,8 @@ spmm24_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
             ptx::mbar_init(&empty[s], 1);
         }
         ptx::mbar_init(acc_full, 1);
+        ptx::mbar_init(recv_bar, 1);
+        ptx::mbar_init(free_bar, 1);
         ptx::fence_mbarrier_init();
         ptx::prefetch_tmap(&tmA);
         ptx::prefetch_tmap(&tmB);
@@ -429,33 +447,34 @@ spmm24_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
         ptx::tmem_relinquish_pair();
     }
     ptx::tc_fence_before();
-    ptx::cluster_sync();  // both CTAs: barriers initialised, TMEM allocated
+    ptx::cluster_sync();  // every CTA of the cluster: barriers initialised, TMEM allocated
     ptx::tc_fence_after();
     const uint32_t tmem_base = *tmem_holder;
     if (threadIdx.x == 0) ptx::grid_dep_launch();
 
-    // Both CTAs' loads complete on the leader's full barrier; the leader arms
-    // it once per stage with both CTAs' bytes.
+    // Both CTAs' loads complete on the pair leader's full barrier; the leader
+    // arms it once per stage with both CTAs' bytes.
     const uint64_t pol = ptx::policy_evict_last();  // A is re-read by every N tile, B by every M tile
-    const uint32_t full0 = ptx::mapa_shared(ptx::smem_u32(&full[0]), 0u);
+    const uint32_t full0 = ptx::mapa_shared(ptx::smem_u32(&full[0]), lead_rank);
     const int pre = p.weights_static ? min(STAGES, st_count) : 0;
     if (warp == 0) {
-        // ------------------------------------- TMA producer: A + metadata (+ B)
+        // ------------------------------------------------- TMA producer
         if (lane == 0) {
             for (int it = 0; it < pre; ++it) {
+                const int g = st_begin + it;
                 uint8_t* st = smem + it * C_::STAGE_BYTES;
                 if (leader) ptx::mbar_arrive_expect_tx(&full[it], 2 * C_::STAGE_BYTES);
-                ptx::tma_load_3d_pair(st, &tmA, full0 + 8u * it, 0, band0, 8 * it, pol);
-                ptx::tma_load_2d_pair(st + C_::A_BYTES + C_::B_BYTES, &tmE, full0 + 8u * it, 128 * it, band0, pol);
+                ptx::tma_load_3d_pair(st, &tmA, full0 + 8u * it, 0, band0, 8 * g, pol);
+                ptx::tma_load_2d_pair(st + C_::A_BYTES + C_::B_BYTES, &tmE, full0 + 8u * it, 128 * g, band0, pol);
             }
             ptx::grid_dep_wait();
             SPMM24_STAMP(1);
-            if (!SPLIT_ISSUE)
-                for (int it = 0; it < pre; ++it)
-                    ptx::tma_load_4d_pair(smem + it * C_::STAGE_BYTES + C_::A_BYTES, &tmB, full0 + 8u * it, 0, 2 * it,
-                                          0, strip0, pol);
+            for (int it = 0; it < pre; ++it)
+                ptx::tma_load_4d_pair(smem + it * C_::STAGE_BYTES + C_::A_BYTES, &tmB, full0 + 8u * it, 0,
+                                      2 * (st_begin + it), 0, strip0, pol);
             for (int it = pre; it < st_count; ++it) {
                 const int s = it % STAGES;
+                const int g = st_begin + it;
                 const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
                 if (!ptx::mbar_wait_bounded(&empty[s], ph ^ 1u, kWaitLimitNs)) {
                     atomicOr(&g_spmm24_status, kStatusProducerTimeout);
@@ -464,9 +483,9 @@ spmm24_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                 uint8_t* st = smem + s * C_::STAGE_BYTES;
                 const uint32_t bar = full0 + 8u * s;
                 if (leader) ptx::mbar_arrive_expect_tx(&full[s], 2 * C_::STAGE_BYTES);
-                ptx::tma_load_3d_pair(st, &tmA, bar, 0, band0, 8 * it, pol);
-                ptx::tma_load_2d_pair(st + C_::A_BYTES + C_::B_BYTES, &tmE, bar, 128 * it, band0, pol);
-                if (!SPLIT_ISSUE) ptx::tma_load_4d_pair(st + C_::A_BYTES, &tmB, bar, 0, 2 * it, 0, strip0, pol);
+                ptx::tma_load_3d_pair(st, &tmA, bar, 0, band0, 8 * g, pol);
+                ptx::tma_load_2d_pair(st + C_::A_BYTES + C_::B_BYTES, &tmE, bar, 128 * g, band0, pol);
+                ptx::tma_load_4d_pair(st + C_::A_BYTES, &tmB, bar, 0, 2 * g, 0, strip0, pol);
             }
         }
         __syncwarp();
@@ -498,28 +517,11 @@ spmm24_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                                          accumulate);
                     accumulate = 1;
                 }
-                ptx::tc_commit_pair_mc(&empty[s], 0x3);  // frees ring slot s in both CTAs
+                ptx::tc_commit_pair_mc(&empty[s], pair_mask);  // frees ring slot s in both CTAs of the pair
             }
             __syncwarp();
         }
-        if (lane == 0) ptx::tc_commit_pair_mc(acc_full, 0x3);
-        __syncwarp();
-    }
-    if (SPLIT_ISSUE && warp == 2) {
-        // --------------------- second TMA producer: B, then the epilogue
-        if (lane == 0) {
-            ptx::grid_dep_wait();
-            for (int it = 0; it < st_count; ++it) {
-                const int s = it % STAGES;
-                const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
-                if (it >= STAGES && !ptx::mbar_wait_bounded(&empty[s], ph ^ 1u, kWaitLimitNs)) {
-                    atomicOr(&g_spmm24_status, kStatusProducerTimeout);
-                    break;
-                }
-                ptx::tma_load_4d_pair(smem + s * C_::STAGE_BYTES + C_::A_BYTES, &tmB, full0 + 8u * s, 0, 2 * it, 0,
-                                      strip0, pol);
-            }
-        }
+        if (lane == 0) ptx::tc_commit_pair_mc(acc_full, pair_mask);
         __syncwarp();
     }
     {
@@ -534,7 +536,57 @@ spmm24_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
         const int c_begin = (warp >> 2) * (NCH16 / 2);  // this warp's half of the columns
         const int c_end = c_begin + NCH16 / 2;
         const int etid = threadIdx.x;
-        if constexpr (!EPI) {
+        // K split: pair 1 sends its fp32 partial to the matching CTA of pair 0
+        // (st.async into its idle ring, counted on its receive barrier) once
+        // pair 0 is ready; pair 0 adds it to its own accumulator row by row.
+        const float* part = reinterpret_cast<const float*>(smem + C_::RECV_OFFSET);
+        bool produce = true;
+        if constexpr (KSPLIT) {
+            if (kpart == 0) {
+                if (threadIdx.x == 0) {
+                    ptx::mbar_arrive_expect_tx(recv_bar, C_::RECV_BYTES);
+                    ptx::mbar_arrive_cluster(ptx::mapa_shared(ptx::smem_u32(free_bar), crank + 2u));
+                }
+                if (!ptx::mbar_wait_bounded(recv_bar, 0, kWaitLimitNs))
+                    atomicOr(&g_spmm24_status, kStatusEpilogueTimeout);
+            } else {
+                produce = false;
+                if (!ptx::mbar_wait_bounded(free_bar, 0, kWaitLimitNs)) {
+                    atomicOr(&g_spmm24_status, kStatusEpilogueTimeout);
+                } else {
+                    const uint32_t dst0 = ptx::mapa_shared(ptx::smem_u32(smem + C_::RECV_OFFSET), crank - 2u);
+                    const uint32_t dbar = ptx::mapa_shared(ptx::smem_u32(recv_bar), crank - 2u);
+#pragma unroll 1
+                    for (int c = c_begin; c < c_end; ++c) {
+                        uint32_t v[16];
+                        ptx::tmem_ld_32x32b_x16(tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(c * 16), v);
+                        ptx::tmem_wait_ld();
+                        const uint32_t dst = dst0 + (uint32_t)((row * C_::F_PITCH + c * 16) * 4);
+#pragma unroll
+                        for (int q = 0; q < 4; ++q)
+                            ptx::st_async_v4(dst + 16u * q, __uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
+                                             __uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3]), dbar);
+                    }
+                }
+            }
+        }
+        // the partner partial of (this thread's row, 16-column chunk c), added to v
+        auto add_partial = [&](uint32_t* v, int c) {
+            if constexpr (KSPLIT) {
+                const float4* pp = reinterpret_cast<const float4*>(part + (size_t)row * C_::F_PITCH + c * 16);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const float4 x = pp[q];
+                    v[4 * q] = __float_as_uint(__uint_as_float(v[4 * q]) + x.x);
+                    v[4 * q + 1] = __float_as_uint(__uint_as_float(v[4 * q + 1]) + x.y);
+                    v[4 * q + 2] = __float_as_uint(__uint_as_float(v[4 * q + 2]) + x.z);
+                    v[4 * q + 3] = __float_as_uint(__uint_as_float(v[4 * q + 3]) + x.w);
+                }
+            }
+        };
+        if (!produce) {
+            // pair 1 of a K split: its partial has been sent
+        } else if constexpr (!EPI) {
             // Plain fp16 row-major: stage the rounded tile in the (now idle)
             // ring -- rows bank-shifted by 16 bytes so the per-row writes do
             // not collide -- then copy it out with coalesced 16-byte stores.
@@ -544,6 +596,7 @@ spmm24_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                 uint32_t v[16];
                 ptx::tmem_ld_32x32b_x16(tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(c * 16), v);
                 ptx::tmem_wait_ld();
+                add_partial(v, c);
                 __align__(16) __half h[16];
 #pragma unroll
                 for (int e = 0; e < 16; ++e) h[e] = __float2half_rn(__uint_as_float(v[e]));
@@ -613,6 +666,7 @@ spmm24_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                     uint32_t v[16];
                     ptx::tmem_ld_32x32b_x16(tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(c * 16), v);
                     ptx::tmem_wait_ld();
+                    add_partial(v, c);
                     float f[16];
 #pragma unroll
                     for (int e = 0; e < 16; ++e) f[e] = __uint_as_float(v[e]);
@@ -628,6 +682,7 @@ spmm24_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                     uint32_t v[16];
                     ptx::tmem_ld_32x32b_x16(tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(c * 16), v);
                     ptx::tmem_wait_ld();
+                    add_partial(v, c);
                     float f[16];
 #pragma unroll
                     for (int e = 0; e < 16; ++e) f[e] = __uint_as_float(v[e]);

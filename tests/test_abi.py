@@ -165,7 +165,13 @@ def test_select_config_picks_tiles_and_splits():
     assert c["tile_n"] == 128 and c["stages"] == 4 and c["cta_pair"] == 0
     # wide N with K % 128 == 0: 256 x 256 tiles on CTA pairs
     c = spmm24.select_config(4096, 512, 4096)
-    assert c["cta_pair"] == 1 and c["tile_m"] == 256 and c["tile_n"] == 256 and c["grid_ctas"] == 64
+    assert c["cta_pair"] == 1 and c["tile_m"] == 256 and c["tile_n"] == 256 and c["split_k"] == 1
+    assert c["grid_ctas"] == 64
+    # 32 pair tiles (0.4 waves) and 86 stages: two pairs per tile, each with half of K
+    c = spmm24.select_config(4096, 512, 11008)
+    assert c["cta_pair"] == 1 and c["split_k"] == 2 and c["grid_ctas"] == 128
+    assert spmm24.select_config(8192, 256, 28672)["split_k"] == 2
+    assert spmm24.select_config(11008, 512, 4096)["split_k"] == 1   # 86 tiles: more than half a wave
     assert spmm24.select_config(4096, 512, 4160)["cta_pair"] == 0  # K % 128 != 0
     assert spmm24.select_config(4096, 512, 4096, 2)["cta_pair"] == 0  # explicit split-K
     # explicit split honoured, clamped to the number of 128-K stages

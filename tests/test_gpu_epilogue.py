@@ -120,7 +120,7 @@ def _run(cuda_device, M, N, K, *, bf16=False, bias=False, residual=False, alpha=
 # (M, N, K, split): narrow N with K splits of 1, 3 and 8 (cluster kernel with
 # the push reduction), mid N (deep ring), wide N (CTA pair), ragged shapes
 SHAPES = [(256, 16, 1024, 1), (384, 16, 2048, 3), (512, 32, 4096, 8), (272, 40, 512, 0), (256, 128, 1024, 0),
-          (512, 512, 1024, 0), (272, 264, 384, 0)]
+          (512, 512, 1024, 0), (272, 264, 384, 0), (1024, 512, 6144, 0)]   # the last: pair kernel with a K split
 
 
 @pytest.mark.parametrize("shape", SHAPES)

@@ -91,6 +91,8 @@ def test_fused_allgather_two_gpus():
         pytest.skip("needs two GPUs")
     if not torch.cuda.can_device_access_peer(0, 1):
         pytest.skip("no peer access between GPU 0 and GPU 1")
-    # decode (cluster kernel, split-K 4 and auto), mid N, prefill (pair kernel), ragged N
-    shapes = [(1024, 16, 1024, 4), (2048, 32, 2048, 0), (1024, 64, 512, 0), (1024, 512, 1024, 0), (512, 40, 512, 0)]
+    # decode (cluster kernel, split-K 4 and auto), mid N, prefill (pair kernel, with and without
+    # the K split), ragged N
+    shapes = [(1024, 16, 1024, 4), (2048, 32, 2048, 0), (1024, 64, 512, 0), (1024, 512, 1024, 0), (512, 40, 512, 0),
+              (1024, 512, 6144, 0)]   # the last: pair kernel with a K split
     mp.spawn(_worker, args=(2, _free_port(), shapes), nprocs=2, join=True)

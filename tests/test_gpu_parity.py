@@ -158,18 +158,20 @@ def test_back_to_back_calls_pdl(cuda_device):
     (272, 264, 384),     # ragged M (one band past a pair tile) and ragged N
     (4096, 520, 1024),   # several pairs, ragged last N tile
     (768, 1000, 256),    # N not a multiple of 8: scalar stores
+    (1024, 512, 4096),   # few tiles, long K: the automatic K split
+    (768, 520, 3200),    # odd stage count split unevenly, ragged N
 ])
-@pytest.mark.parametrize("tile_n,issue", [(256, 1), (256, 2), (128, 1), (128, 2)])
-def test_cta_pair_kernel(cuda_device, monkeypatch, shape, tile_n, issue):
-    """The cta_group::2 pair kernel (256 x 256 or 256 x 128 tiles, K % 128 ==
-    0), with the loads issued by one or by two warps."""
+@pytest.mark.parametrize("split", [1, 2])
+def test_cta_pair_kernel(cuda_device, monkeypatch, shape, split):
+    """The cta_group::2 pair kernel (256 x 256 tiles, K % 128 == 0), one pair
+    per tile or two pairs along K reducing through distributed shared
+    memory."""
     import spmm24
 
-    monkeypatch.setenv("SPMM24_PAIR_N", str(tile_n))
-    monkeypatch.setenv("SPMM24_PAIR_ISSUE", str(issue))
+    monkeypatch.setenv("SPMM24_PAIR_SPLIT", str(split))
     M, N, K = shape
     cfg = spmm24.select_config(M, N, K)
-    assert cfg["cta_pair"] == 1 and cfg["tile_n"] == tile_n
+    assert cfg["cta_pair"] == 1 and cfg["tile_n"] == 256 and cfg["split_k"] == (split if K >= 256 else 1)
     p = make_problem(M, N, K, seed=3 * M + N)
     check(p, 0, cuda_device)
 
