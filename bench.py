@@ -578,13 +578,57 @@ def time_gather(torch, dist, spmm24, calls, stream, dev, rank, world, args, flag
     for p in imported:
         spmm24.ipc_close(p)
     dist.barrier()
+
+    # The same with every output chunk stored once through an NVLink
+    # multicast address (symmetric-memory buffers bound to all ranks).
+    us_mc = None
+    try:
+        import torch.distributed._symmetric_memory as symm_mem
+
+        group = dist.group.WORLD
+        mfulls = [symm_mem.empty((c["M_full"], c["N"]), dtype=torch.float16, device=dev) for c in calls]
+        mhandles = [symm_mem.rendezvous(t, group) for t in mfulls]
+        mflags = symm_mem.empty((world,), dtype=torch.int32, device=dev)
+        mflags.zero_()
+        fh = symm_mem.rendezvous(mflags, group)
+        if all(h.multicast_ptr for h in mhandles) and all(c["N"] % 8 == 0 for c in calls):
+            foff = mflags.data_ptr() - fh.buffer_ptrs[rank]
+            fptrs = [fh.buffer_ptrs[r] + foff for r in range(world)]
+            mc = []
+            for t, h in zip(mfulls, mhandles):
+                off = t.data_ptr() - h.buffer_ptrs[rank]
+                mc.append(([h.buffer_ptrs[r] + off for r in range(world)], h.multicast_ptr + off))
+            mepoch = [0]
+
+            def fused_mc():
+                for i, c in enumerate(calls):
+                    rc = spmm24.launch_gather(stream, c["A"], c["B"], c["E"], c["M"], c["N"], c["K"], mc[i][0],
+                                              rows[i][0], c["M_full"], 0, flags, c_multicast=mc[i][1])
+                    if rc != 0:
+                        raise RuntimeError(f"spmm24_launch_gather: {rc} {spmm24._lib.spmm24_last_error().decode()}")
+                    mepoch[0] += 1
+                    if spmm24.gather_barrier(stream, fptrs, rank, mepoch[0]) != 0:
+                        raise RuntimeError("spmm24_gather_barrier failed")
+
+            us_mc = timed(fused_mc)
+            status |= spmm24.device_status(dev.index)
+        dist.barrier()
+    except Exception as e:  # noqa: BLE001 -- report, keep the other numbers
+        us_mc = f"unavailable: {str(e)[:120]}"
     fl = sum(flops(c["M_full"], c["N"], c["K"]) for c in calls)
-    return {"fused_us_per_step": round(us_fused, 2), "nccl_us_per_step": round(us_nccl, 2),
-            "fused_tflops": round(fl / (us_fused * 1e-6) / 1e12, 2),
-            "nccl_tflops": round(fl / (us_nccl * 1e-6) / 1e12, 2),
-            "gathered_bytes_per_step": sum(2 * c["M_full"] * c["N"] for c in calls), "status": status,
-            "op": "fused: spmm24_launch_gather + spmm24_gather_barrier per layer (peer stores over NVLink); "
-                  "nccl: spmm24_launch_ex + all_gather_into_tensor per layer"}
+    out = {"fused_us_per_step": round(us_fused, 2), "nccl_us_per_step": round(us_nccl, 2),
+           "fused_tflops": round(fl / (us_fused * 1e-6) / 1e12, 2),
+           "nccl_tflops": round(fl / (us_nccl * 1e-6) / 1e12, 2),
+           "gathered_bytes_per_step": sum(2 * c["M_full"] * c["N"] for c in calls), "status": status,
+           "op": "fused: spmm24_launch_gather + spmm24_gather_barrier per layer (peer stores over NVLink); "
+                 "fused_multicast: the same, each chunk stored once through an NVLink multicast address "
+                 "(multimem.st); nccl: spmm24_launch_ex + all_gather_into_tensor per layer"}
+    if isinstance(us_mc, float):
+        out["fused_multicast_us_per_step"] = round(us_mc, 2)
+        out["fused_multicast_tflops"] = round(fl / (us_mc * 1e-6) / 1e12, 2)
+    elif us_mc is not None:
+        out["fused_multicast"] = us_mc
+    return out
 
 
 def run_comparators(torch, spmm24, calls, layers, acts, dev, args):

@@ -135,6 +135,16 @@ __device__ __forceinline__ void bulk_store(void* dst_global, const void* src_sme
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 
+// 16-byte store to an NVLink multicast address: the switch replicates it
+// into the memory of every GPU bound to the multicast object.  The bits are
+// moved as four 32-bit words.
+__device__ __forceinline__ void multimem_st_v4(void* mc_addr, uint4 v) {
+    asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc_addr),
+                 "f"(__uint_as_float(v.x)), "f"(__uint_as_float(v.y)), "f"(__uint_as_float(v.z)),
+                 "f"(__uint_as_float(v.w))
+                 : "memory");
+}
+
 // Loads for a CTA pair running cta_group::2 MMAs: the bytes are counted on
 // the mbarrier at `bar_cluster` (a shared::cluster address, normally the
 // leader CTA's barrier), not on the executing CTA's.

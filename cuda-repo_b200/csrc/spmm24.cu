@@ -430,6 +430,11 @@ cudaError_t launch_impl(cudaStream_t stream, const void* A, const void* B, const
         }
         epi.gather_n = gather->n_ranks;
         epi.gather_row0 = gather->row_offset;
+        if (gather->c_multicast) {
+            if (N % 8) return invalid("gather: a multicast C needs N % 8 == 0");
+            if ((uintptr_t)gather->c_multicast & 15u) return invalid("gather: the multicast C must be 16-byte aligned");
+            epi.gather_mc = static_cast<uint16_t*>(gather->c_multicast);
+        }
     }
     const bool plain = epi.bias == nullptr && epi.residual == nullptr && epi.act == kActNone && epi.alpha == 1.f &&
                        !epi.packed && !epi.bf16 && epi.gather_n == 0;

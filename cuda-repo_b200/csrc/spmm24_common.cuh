@@ -174,6 +174,9 @@ struct Epilogue {
     int gather_n;
     int gather_row0;
     uint16_t* gather_dst[kMaxGatherRanks];
+    // Multicast address of the full C (NVSwitch replicates each store into
+    // every rank's buffer), or null: one unicast store per rank instead.
+    uint16_t* gather_mc;
 };
 
 // Stores 16 bytes of row-major output (row gm of the shard, columns gn..) to
@@ -181,7 +184,11 @@ struct Epilogue {
 __device__ __forceinline__ void store_row16(uint16_t* C, const Epilogue& e, int gm, int gn, int N, uint4 v) {
     if (e.gather_n) {
         const size_t off = (size_t)(e.gather_row0 + gm) * N + gn;
-        for (int d = 0; d < e.gather_n; ++d) *reinterpret_cast<uint4*>(e.gather_dst[d] + off) = v;
+        if (e.gather_mc) {
+            ptx::multimem_st_v4(e.gather_mc + off, v);
+        } else {
+            for (int d = 0; d < e.gather_n; ++d) *reinterpret_cast<uint4*>(e.gather_dst[d] + off) = v;
+        }
     } else {
         *reinterpret_cast<uint4*>(C + (size_t)gm * N + gn) = v;
     }

@@ -731,7 +731,7 @@ spmm24_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                     out = *reinterpret_cast<const uint4*>(hst + (size_t)r * C_::C_PITCH + c * 8);
                 }
             };
-            if (p.epi.gather_n && !has_res && vec_ok) {
+            if (p.epi.gather_n && !p.epi.gather_mc && !has_res && vec_ok) {
                 // Gathered output: every staged row goes to every rank's full C
                 // as one bulk copy, spread over the threads; a CTA waits only
                 // until its shared memory has been read, so the NVLink writes

@@ -67,7 +67,7 @@ _lib.spmm24_load_packed.restype = ctypes.c_int
 class Gather(ctypes.Structure):
     """spmm24_gather (include/spmm24/SpMM_API.h)."""
     _fields_ = [("c_full", ctypes.c_void_p * 8), ("n_ranks", ctypes.c_int), ("row_offset", ctypes.c_int),
-                ("m_full", ctypes.c_int)]
+                ("m_full", ctypes.c_int), ("c_multicast", ctypes.c_void_p)]
 
 
 class IpcHandle(ctypes.Structure):
@@ -310,15 +310,17 @@ def ipc_close(ptr: int) -> None:
 
 
 def launch_gather(stream, compressed_a, b_packed, metadata, M: int, N: int, K: int, c_full_ptrs, row_offset: int,
-                  m_full: int, split_k: int = 0, flags: int = 0) -> int:
+                  m_full: int, split_k: int = 0, flags: int = 0, c_multicast=None) -> int:
     """spmm24_launch_gather: this rank's M-shard, written into every rank's
-    full C (c_full_ptrs in rank order, own buffer included)."""
+    full C (c_full_ptrs in rank order, own buffer included; or, with
+    c_multicast, once through the full C's NVLink multicast address)."""
     if len(c_full_ptrs) > 8:
         raise ValueError("at most 8 ranks (SPMM24_MAX_GATHER_RANKS)")
     g = Gather()
     for i, p in enumerate(c_full_ptrs):
         g.c_full[i] = _ptr(p)
     g.n_ranks, g.row_offset, g.m_full = len(c_full_ptrs), row_offset, m_full
+    g.c_multicast = _ptr(c_multicast)
     return _lib.spmm24_launch_gather(_stream_handle(stream), _ptr(compressed_a), _ptr(b_packed), _ptr(metadata), M, N,
                                      K, split_k, flags, ctypes.byref(g))
 

@@ -133,6 +133,12 @@ typedef struct spmm24_gather {
     int n_ranks;
     int row_offset;
     int m_full;
+    /* Optional: the full C's NVLink multicast address (a multicast object
+     * bound to every rank's c_full, e.g. a symmetric-memory buffer's
+     * multicast pointer).  Each output chunk is then stored once with
+     * multimem.st and replicated by the switch, instead of once per rank.
+     * Requires N % 8 == 0.  NULL: unicast stores to c_full[]. */
+    void* c_multicast;
 } spmm24_gather;
 cudaError_t spmm24_launch_gather(cudaStream_t stream, const void* compressed_a, const void* b_packed,
                                  const uint16_t* metadata, int M, int N, int K, int split_k, unsigned flags,

@@ -96,3 +96,83 @@ def test_fused_allgather_two_gpus():
     shapes = [(1024, 16, 1024, 4), (2048, 32, 2048, 0), (1024, 64, 512, 0), (1024, 512, 1024, 0), (512, 40, 512, 0),
               (1024, 512, 6144, 0)]   # the last: pair kernel with a K split
     mp.spawn(_worker, args=(2, _free_port(), shapes), nprocs=2, join=True)
+
+
+def _worker_multicast(rank, world, port, shapes, result_dir):
+    import sys
+    from datetime import timedelta
+
+    sys.path.insert(0, os.path.join(REPO, "cuda-repo_b200"))
+    import torch
+    import torch.distributed as dist
+    import torch.distributed._symmetric_memory as symm_mem
+
+    import spmm24
+
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=60), device_id=dev)
+    group = dist.group.WORLD
+    flags = symm_mem.empty((world,), dtype=torch.int32, device=dev)
+    flags.zero_()
+    fh = symm_mem.rendezvous(flags, group)
+    flag_ptrs = [fh.buffer_ptrs[r] + (flags.data_ptr() - fh.buffer_ptrs[rank]) for r in range(world)]
+    epoch = 0
+    supported = True
+    for (M, N, K, split) in shapes:
+        rng = np.random.default_rng(M + N + K)
+        a = rng.standard_normal((M, K)).astype(np.float16).view(np.uint16)
+        vals, meta = spmm24.compress_reordered(spmm24.prune_2of4(a, M, K), M, K)
+        b = rng.uniform(-1, 1, (K, N)).astype(np.float16).view(np.uint16)
+        bp = torch.from_numpy(spmm24.pack_b(b, K, N).view(np.int16)).to(dev)
+        A = torch.from_numpy(vals.view(np.int16)).to(dev)
+        E = torch.from_numpy(meta.view(np.int16)).to(dev)
+        expect = torch.empty((M, N), dtype=torch.float16, device=dev)
+        rows = [spmm24.shard_rows(M, world, r, 128) for r in range(world)]
+        for (r0, r1) in rows:
+            Av, Ev = spmm24.shard_views(A, E, M, K, r0, r1)
+            assert spmm24.launch(None, Av, bp, Ev, expect[r0:r1], r1 - r0, N, K, None, split) == 0
+        c_full = symm_mem.empty((M, N), dtype=torch.float16, device=dev)
+        c_full.fill_(float("nan"))
+        h = symm_mem.rendezvous(c_full, group)
+        if not h.multicast_ptr:  # no multicast object behind this buffer
+            supported = False
+            break
+        off = c_full.data_ptr() - h.buffer_ptrs[rank]
+        ptrs = [h.buffer_ptrs[r] + off for r in range(world)]
+        mc = h.multicast_ptr + off
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        r0, r1 = rows[rank]
+        Av, Ev = spmm24.shard_views(A, E, M, K, r0, r1)
+        epoch += 1
+        s = torch.cuda.current_stream(dev)
+        assert spmm24.launch_gather(s, Av, bp, Ev, r1 - r0, N, K, ptrs, r0, M, split, spmm24.STATIC_WEIGHTS,
+                                    c_multicast=mc) == 0, spmm24._lib.spmm24_last_error().decode()
+        assert spmm24.gather_barrier(s, flag_ptrs, rank, epoch) == 0
+        torch.cuda.synchronize(dev)
+        assert spmm24.device_status(rank) == 0
+        assert torch.equal(c_full, expect), (rank, M, N, K)
+        dist.barrier()
+    with open(os.path.join(result_dir, f"rank{rank}"), "w") as f:
+        f.write("ok" if supported else "unsupported")
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_fused_allgather_multicast_two_gpus(tmp_path):
+    """The same gather with each output chunk stored once through the full
+    C's NVLink multicast address (multimem.st; a symmetric-memory buffer
+    bound to both GPUs)."""
+    import torch
+    import torch.multiprocessing as mp
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    shapes = [(1024, 16, 1024, 4), (2048, 32, 2048, 0), (1024, 512, 1024, 0), (1024, 512, 6144, 0)]
+    mp.spawn(_worker_multicast, args=(2, _free_port(), shapes, str(tmp_path)), nprocs=2, join=True)
+    results = {(tmp_path / f"rank{r}").read_text() for r in range(2)}
+    if results == {"unsupported"}:
+        pytest.skip("no NVLink multicast between GPU 0 and GPU 1")
+    assert results == {"ok"}
