@@ -40,6 +40,14 @@ constexpr int kBTilePitch = kBTileCols + 8;
 // 0x7c00 for fp16, 0x7f80 for bf16) compares false with everything -- the
 // host's float comparisons, reproduced exactly.
 
+// True when none of the four magnitudes (ax, ay: two 15-bit halves each)
+// is above `inf`: adding 0x7fff - inf to each half carries into its bit 15
+// exactly when it is above (no half overflows its 16 bits).
+__device__ __forceinline__ bool no_nan(uint32_t ax, uint32_t ay, uint32_t inf) {
+    const uint32_t add = (0x7fffu - inf) * 0x10001u;
+    return (((ax + add) | (ay + add)) & 0x80008000u) == 0u;
+}
+
 // Magnitude 2:4 prune of one group (packer.cpp spmm24_prune_2of4): keep the
 // largest |x| (first on ties), then the largest of the other three (first on
 // ties), replace the other two by +0.
@@ -74,9 +82,8 @@ __device__ __forceinline__ uint32_t prune_keep_sequential(uint32_t ax, uint32_t 
 // `inf`: the infinity bit pattern of the element type (0x7c00 fp16, 0x7f80 bf16).
 __device__ __forceinline__ void prune_group(uint32_t& x, uint32_t& y, uint32_t inf) {
     const uint32_t ax = x & 0x7fff7fffu, ay = y & 0x7fff7fffu;
-    const uint32_t mx = __vmaxu2(ax, ay);
     uint32_t keep;
-    if (max(mx & 0xffffu, mx >> 16) <= inf) {
+    if (no_nan(ax, ay, inf)) {
         // No NaN: the sequential scan keeps the two largest of the unique keys
         // |x| << 2 | (3 - position) (equal magnitudes: the lower position wins).
         const uint32_t a0 = ((ax << 2) & 0x3fffcu) | 3u, a1 = ((ax >> 14) & 0x3fffcu) | 2u;
@@ -106,6 +113,31 @@ __device__ __forceinline__ bool compress_group(uint32_t x, uint32_t y, uint32_t*
     *halves = __byte_perm(x, y, ia * 0x22u + ib * 0x2200u + 0x1010u);
     *idx = id;
     return ((0x0117u >> z) & 1u) == 0;
+}
+
+// Prune + compress of one group in one step.  Common case (no NaN, both
+// kept magnitudes non-zero): the kept positions are the top-2 of the unique
+// keys, the two pruned positions are exactly the zeros the compress drops,
+// so positions and values come straight from the selection.  Otherwise the
+// two steps run as written above.  Same results bit for bit.
+__device__ __forceinline__ bool prune_compress_group(uint32_t x, uint32_t y, uint32_t inf, uint32_t* halves,
+                                                     uint32_t* idx) {
+    const uint32_t ax = x & 0x7fff7fffu, ay = y & 0x7fff7fffu;
+    if (no_nan(ax, ay, inf)) {
+        const uint32_t a0 = ((ax << 2) & 0x3fffcu) | 3u, a1 = ((ax >> 14) & 0x3fffcu) | 2u;
+        const uint32_t a2 = ((ay << 2) & 0x3fffcu) | 1u, a3 = (ay >> 14) & 0x3fffcu;
+        const uint32_t hi01 = max(a0, a1), lo01 = min(a0, a1), hi23 = max(a2, a3), lo23 = min(a2, a3);
+        const uint32_t top = max(hi01, hi23), second = max(min(hi01, hi23), max(lo01, lo23));
+        if (second >= 4u) {  // both kept magnitudes non-zero
+            const uint32_t k0 = 3u - (top & 3u), k1 = 3u - (second & 3u);
+            const uint32_t ia = min(k0, k1), ib = max(k0, k1);
+            *halves = __byte_perm(x, y, ia * 0x22u + ib * 0x2200u + 0x1010u);
+            *idx = ia | (ib << 2);
+            return true;
+        }
+    }
+    prune_group(x, y, inf);
+    return compress_group(x, y, halves, idx);
 }
 
 // One CTA: kPackBands 16-row bands x 16 blocks of 16 K.  All of the tile's
@@ -157,12 +189,21 @@ __global__ void __launch_bounds__(kPackThreads) pack_a_kernel(const uint16_t* __
         uint32_t wx[4] = {lo.x, lo.z, hi.x, hi.z}, wy[4] = {lo.y, lo.w, hi.y, hi.w};
         uint32_t w[4], md = 0;
         bool ok = true;
+        if (prune) {
+            const uint32_t inf = prune == 2 ? 0x7f80u : 0x7c00u;
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            if (prune) prune_group(wx[k], wy[k], prune == 2 ? 0x7f80u : 0x7c00u);
-            uint32_t idx;
-            ok &= compress_group(wx[k], wy[k], &w[k], &idx);
-            md |= idx << (4 * k);
+            for (int k = 0; k < 4; ++k) {
+                uint32_t idx;
+                ok &= prune_compress_group(wx[k], wy[k], inf, &w[k], &idx);
+                md |= idx << (4 * k);
+            }
+        } else {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                uint32_t idx;
+                ok &= compress_group(wx[k], wy[k], &w[k], &idx);
+                md |= idx << (4 * k);
+            }
         }
         bad += ok ? 0 : 1;
         const int band = band0 + b;
