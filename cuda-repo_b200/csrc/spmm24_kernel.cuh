@@ -4,7 +4,7 @@
 // and the separate split-K pass SplitK_Reduction (src/reduce_Kernel.cuh:27).
 // Formats and the tcgen05 mapping are described in spmm24_common.cuh.
 //
-// Two kernels share the stage layout and the MMA issue:
+// Three kernels share the stage layout and the MMA issue:
 //
 //   spmm24_cluster_kernel  one 128 x N_TILE tile per CTA; a split-K request
 //       of S becomes a thread-block cluster of S CTAs along K whose fp32
@@ -12,9 +12,12 @@
 //       (no global workspace, no second launch, fixed summation order).
 //
 //   spmm24_pair_kernel  a CTA pair (cluster of 2) computing one 256 x 256
-//       or 256 x 128 tile with tcgen05.mma.sp.cta_group::2: each CTA holds
-//       128 rows of A and half of the tile's columns of B, so each SM feeds
-//       the tensor core only half of B -- the prefill (compute-bound) path.
+//       tile with tcgen05.mma.sp.cta_group::2: each CTA holds 128 rows of A
+//       and half of the tile's columns of B, so each SM feeds the tensor
+//       core only half of B -- the prefill (compute-bound) path.  With a K
+//       split, a cluster of two pairs takes the two halves of K and pair 1
+//       sends its partial accumulator to pair 0 through distributed shared
+//       memory.
 //
 //   spmm24_streamk_kernel  a persistent grid (one CTA per SM) in which every
 //       CTA takes an equal share of the (tile, 128-K stage) units, walked
@@ -26,10 +29,16 @@
 //       own last segment is still streaming, so the end of the kernel only
 //       adds the accumulator and stores.  Summation order is fixed.
 //
-// Roles (192 threads):
+// The cluster and pair kernels come in two instantiations: the plain fp16
+// row-major SpMM, and EPI (alpha, bias, activation, residual, bf16, packed
+// output, fused all-gather), kept apart because the epilogue of every tile
+// is on the critical path.
+//
+// Roles (192 threads; the pair kernel 256):
 //   warp 0     TMA producer (lane 0)
 //   warp 1     TMEM allocator, tcgen05.cp + tcgen05.mma issuer (lane 0)
-//   warps 2-5  epilogue: TMEM -> registers -> fp16 stores
+//   warps 2-5  epilogue: TMEM -> registers -> stores (in the pair kernel
+//              every warp joins the epilogue once its role is done)
 // Every wait is bounded; the producer starts before TMEM is allocated; the
 // kernels take part in programmatic dependent launch (they wait for the
 // previous grid before touching global memory it may write, and let the
