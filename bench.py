@@ -64,7 +64,9 @@ def pack_bytes(M, K):
     return 2 * M * K + M * K + M * K // 8
 
 
-def algo_bytes(M, N, K):
+def algo_bytes(M, N, K, fp8=False):
+    if fp8:  # fp8 values M*K/2, metadata M*K/8, B N*K bytes, fp16 C
+        return M * K // 2 + M * K // 8 + K * N + 2 * M * N
     return M * K + M * K // 8 + 2 * K * N + 2 * M * N
 
 
@@ -175,7 +177,27 @@ def make_activations(torch, spmm24, K, N, seed, uniform=False, bf16=False):
     return b_np, spmm24.pack_b(b_np, K, N)
 
 
+def make_layer_fp8(torch, spmm24, M, K, seed):
+    """fp8 (E4M3) weights of one layer: N(0,1) quantised by torch's float8
+    cast (the dequantisation scale goes into the epilogue's alpha), pruned
+    and compressed by the product's host packer."""
+    g = torch.Generator().manual_seed(seed)
+    a = torch.randn(M, K, generator=g).to(torch.float8_e4m3fn).view(torch.uint8).numpy().reshape(-1)
+    a = spmm24.prune_2of4_fp8(a, M, K, spmm24.FP8_E4M3)
+    vals, meta = spmm24.compress_a_fp8(a, M, K)
+    return a, vals, meta
+
+
+def make_activations_fp8(torch, K, N, seed):
+    """fp8 (E4M3) activations, N x K row-major (the fp8 path's B layout)."""
+    g = torch.Generator().manual_seed(seed)
+    b = torch.randn(N, K, generator=g).to(torch.float8_e4m3fn).view(torch.uint8).numpy().reshape(-1)
+    return b, b
+
+
 def to_dev(torch, arr, dev):
+    if arr.dtype.itemsize == 1:
+        return torch.from_numpy(arr.view("uint8")).to(dev)
     return torch.from_numpy(arr.view("int16")).to(dev)
 
 
@@ -198,17 +220,24 @@ def run_ours(args, rank, world, local_rank):
     square = args.workload == "square"
     shard = bool(wl.get("shard"))
     bf16 = args.dtype == "bf16"
+    fp8 = args.dtype == "fp8"
     # With sharding every rank holds rows [r0, r1) of each layer (generated
     # for that range directly); otherwise every rank runs whole layers.
     rows = {M: (spmm24.shard_rows(M, world, rank, 128) if shard else (0, M)) for (M, N, K) in shapes}
     layers = {}
     for i, (M, K) in enumerate(sorted({(M, K) for (M, N, K) in shapes})):
         r0, r1 = rows[M]
+        if fp8:
+            layers[(M, K)] = make_layer_fp8(torch, spmm24, r1 - r0, K, seed=1000 * rank + i)
+            continue
         a_np, vals, meta = make_layer(torch, spmm24, r1 - r0, K, wl["a_std"], seed=1000 * rank + i, mask_random=square,
                                       bf16=bf16)
         layers[(M, K)] = (a_np, vals, meta)
     acts = {}
     for j, (K, N) in enumerate(sorted({(K, N) for (M, N, K) in shapes})):
+        if fp8:
+            acts[(K, N)] = make_activations_fp8(torch, K, N, seed=5000 + 100 * rank + j)
+            continue
         acts[(K, N)] = make_activations(torch, spmm24, K, N, seed=5000 + 100 * rank + j, uniform=square)
 
     # Device copies: every call of a step gets its own weights so that the
@@ -217,9 +246,10 @@ def run_ours(args, rank, world, local_rank):
     # host<->device in one copy each.
     b_sizes = [acts[(K, N)][1].size for (M, N, K) in shapes]
     c_sizes = [(rows[M][1] - rows[M][0]) * N for (M, N, K) in shapes]
-    B_all = torch.empty(sum(b_sizes), dtype=torch.int16, device=dev)
+    bdt, bview = (torch.uint8, "uint8") if fp8 else (torch.int16, "int16")
+    B_all = torch.empty(sum(b_sizes), dtype=bdt, device=dev)
     C_all = torch.empty(sum(c_sizes), dtype=torch.float16, device=dev)
-    host_in = torch.from_numpy(np.concatenate([acts[(K, N)][1].view("int16") for (M, N, K) in shapes])).pin_memory()
+    host_in = torch.from_numpy(np.concatenate([acts[(K, N)][1].view(bview) for (M, N, K) in shapes])).pin_memory()
     B_all.copy_(host_in)
     calls = []
     boff = coff = 0
@@ -234,29 +264,35 @@ def run_ours(args, rank, world, local_rank):
         coff += cs
         calls.append({"M": r1 - r0, "N": N, "K": K, "A": A, "E": E, "B": B, "C": C, "M_full": M,
                       "boff": boff - bs, "coff": coff - cs,
-                      "split": spmm24.select_config(max(16, r1 - r0), N, K, 0)["split_k"]})
-    weight_bytes = sum(c["A"].numel() * 2 + c["E"].numel() * 2 for c in calls)
+                      "split": spmm24.select_config(max(16, r1 - r0), N, K // 2 if fp8 else K, 0)["split_k"]})
+    weight_bytes = sum(c["A"].numel() * c["A"].element_size() + c["E"].numel() * c["E"].element_size() for c in calls)
     stream = torch.cuda.current_stream(dev)
     h_stream = int(stream.cuda_stream)
 
     flags = (spmm24.STATIC_WEIGHTS if args.static_weights else 0) | (spmm24.BF16 if bf16 else 0)
     # Optional fused epilogue (spmm24_launch_fused): per-row bias + SiLU, or
     # per-row bias + residual add (the residual is another M x N tensor).
-    fused = args.epilogue != "none" or bf16
+    # fp8: always through spmm24_launch_fp8, alpha = the weights' dequantisation scale.
+    fused = args.epilogue != "none" or bf16 or fp8
     if fused:
         import ctypes
 
         edt = torch.bfloat16 if bf16 else torch.float16
+        alpha = float(wl["a_std"] or 1.0) if fp8 else 1.0
         for c in calls:
             c["bias"] = (torch.randn(c["M"], device=dev) * 0.1).to(edt)
             c["res"] = torch.randn(c["M"], c["N"], device=dev).to(edt) if args.epilogue == "bias_residual" else None
             c["epi"] = spmm24.Epilogue(c["bias"].data_ptr() if args.epilogue != "none" else None,
-                                       c["res"].data_ptr() if c["res"] is not None else None, 1.0,
+                                       c["res"].data_ptr() if c["res"] is not None else None, alpha,
                                        spmm24.ACT_SILU if args.epilogue == "bias_silu" else spmm24.ACT_NONE,
                                        spmm24.OUT_ROW_MAJOR)
 
     def launch(c, hs=None):
-        if fused:
+        if fp8:
+            rc = spmm24._lib.spmm24_launch_fp8(h_stream if hs is None else hs, c["A"].data_ptr(), c["B"].data_ptr(),
+                                               c["E"].data_ptr(), c["C"].data_ptr(), c["M"], c["N"], c["K"], 0,
+                                               flags, ctypes.addressof(c["epi"]))
+        elif fused:
             rc = spmm24._lib.spmm24_launch_fused(h_stream if hs is None else hs, c["A"].data_ptr(), c["B"].data_ptr(),
                                                  c["E"].data_ptr(), c["C"].data_ptr(), c["M"], c["N"], c["K"], 0,
                                                  flags, ctypes.byref(c["epi"]))
@@ -316,7 +352,7 @@ def run_ours(args, rank, world, local_rank):
     # overlaps step i-1's kernels and step i-1's download (another stream)
     # overlaps step i's; events order every reuse of a buffer.
     host_out = [torch.empty(C_all.shape, dtype=torch.float16).pin_memory() for _ in range(2)]
-    h2d = host_in.numel() * 2
+    h2d = host_in.numel() * host_in.element_size()
     d2h = host_out[0].numel() * 2
     B_set = [B_all, torch.empty_like(B_all)]
     C_set = [C_all, torch.empty_like(C_all)]
@@ -398,7 +434,7 @@ def run_ours(args, rank, world, local_rank):
     peaks = load_peaks()
     # Average launch duration over the timed region = elapsed / launches.
     kernel_us_total = elapsed_ms * 1e3
-    bytes_total = sum(algo_bytes(c["M"], c["N"], c["K"]) for c in calls) * args.steps
+    bytes_total = sum(algo_bytes(c["M"], c["N"], c["K"], fp8) for c in calls) * args.steps
     flops_total_rank = step_flops * args.steps
     if wl["bound"] == "hbm":
         achieved = bytes_total / (kernel_us_total * 1e-6) / 1e9
@@ -430,9 +466,12 @@ def run_ours(args, rank, world, local_rank):
         "higher_is_better": True,
         "scaling": "strong" if shard else "weak",
         "vs_baseline": None,
-        "dtype": f"{args.dtype} in, f32 accumulate, {args.dtype} out",
-        "data": f"synthetic (seeded torch RNG; A N(0,{wl['a_std']}) magnitude-pruned 2:4, B N(0,1))" if wl["a_std"]
-                else "synthetic (U(-1,1), random 2:4 mask)",
+        "dtype": ("fp8 e4m3 in, f32 accumulate, f16 out" if fp8
+                  else f"{args.dtype} in, f32 accumulate, {args.dtype} out"),
+        "data": ("synthetic (seeded torch RNG; A N(0,1) in E4M3, magnitude-pruned 2:4, dequantised by alpha = "
+                 f"{wl['a_std']}; B N(0,1) in E4M3, N x K)" if fp8 else
+                 f"synthetic (seeded torch RNG; A N(0,{wl['a_std']}) magnitude-pruned 2:4, B N(0,1))" if wl["a_std"]
+                 else "synthetic (U(-1,1), random 2:4 mask)"),
         "config": {"workload": f"{args.workload}: " + ", ".join(f"{M}x{N}x{K}" for (M, N, K) in shapes),
                    "baseline_config": {"decode": 2, "prefill": 3, "70b": 4, "square": 5}[args.workload],
                    "spmm_per_step": len(calls), "split_k": "auto (library picker)",
@@ -441,8 +480,8 @@ def run_ours(args, rank, world, local_rank):
                                    else f"replicas x{world} (each rank its own layers)")},
         "per_shape_us": {f"{c['M']}x{c['N']}x{c['K']}": round(u, 3) for c, u in zip(calls, per_call)},
         "per_shape_note": "median single-kernel duration with an event pair around each launch",
-        "launch_flags": " | ".join(f for f, on in (("SPMM24_STATIC_WEIGHTS", args.static_weights), ("SPMM24_BF16", bf16))
-                                   if on) or "none",
+        "launch_flags": " | ".join(f for f, on in (("SPMM24_STATIC_WEIGHTS", args.static_weights), ("SPMM24_BF16", bf16),
+                                                   ("spmm24_launch_fp8", fp8)) if on) or "none",
         "epilogue": args.epilogue,
         "roofline": {"bound": wl["bound"], "achieved": round(achieved, 2), "peak": peak, "unit": unit,
                      "frac": round(achieved / peak, 4), "traffic": traffic,
@@ -492,11 +531,11 @@ def run_ours(args, rank, world, local_rank):
     if shard and args.gather and world > 1:
         out["gather"] = time_gather(torch, dist, spmm24, calls, stream, dev, rank, world, args, flags)
 
-    if args.comparators and rank == 0 and not bf16:
+    if args.comparators and rank == 0 and not bf16 and not fp8:
         out["comparators"] = run_comparators(torch, spmm24, calls, layers, acts, dev, args)
 
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        out["cpu_baseline"] = cpu_baseline(layers, acts, shapes, budget_s=args.cpu_seconds, bf16=bf16)
+        out["cpu_baseline"] = cpu_baseline(layers, acts, shapes, budget_s=args.cpu_seconds, bf16=bf16, fp8=fp8)
 
     if world > 1:
         dist.barrier()
@@ -709,36 +748,41 @@ def host_threads():
         return os.cpu_count() or 1
 
 
-def cpu_baseline(layers, acts, shapes, budget_s=10.0, bf16=False):
+def cpu_baseline(layers, acts, shapes, budget_s=10.0, bf16=False, fp8=False):
     """The oracle's OpenMP dense GEMM (fp16 or bf16 -> fp32, fp32 accumulate)
-    on the pruned A, on a row sample of every shape of the workload."""
-    import numpy as np
-
+    on the pruned A, on a row sample of every shape of the workload (fp8:
+    the oracle's fp8 SpMM -- decode of the first bands' values and metadata,
+    then the fp32 GEMM)."""
     sys.path.insert(0, os.path.join(REPO, "oracle"))
     import oracle as O
 
-    gemm = O.dense_gemm_bf16_f32 if bf16 else O.dense_gemm_f32
-
     threads = host_threads()
+
+    def run(M, N, K, r):
+        if fp8:
+            _, vals, meta = layers[(M, K)]
+            O.spmm_fp8_f32(vals[: r * K // 2], meta[: r * K // 8], acts[(K, N)][0], r, N, K, 0, 0, threads)
+        else:
+            gemm = O.dense_gemm_bf16_f32 if bf16 else O.dense_gemm_f32
+            gemm(layers[(M, K)][0][: r * K], acts[(K, N)][0], r, N, K, threads)
+
     # estimate: 64 rows of every shape
     probe_rows = 64
     t = time.perf_counter()
     for (M, N, K) in shapes:
-        a = layers[(M, K)][0][: probe_rows * K]
-        gemm(a, acts[(K, N)][0], probe_rows, N, K, threads)
+        run(M, N, K, probe_rows)
     dt = time.perf_counter() - t
-    rows = int(max(16, min(4096, probe_rows * budget_s / max(dt, 1e-3) / 1.2)))
+    rows = int(max(16, min(4096, probe_rows * budget_s / max(dt, 1e-3) / 1.2))) // 16 * 16
     fl = 0.0
     t = time.perf_counter()
     for (M, N, K) in shapes:
         r = min(rows, M)
-        a = layers[(M, K)][0][: r * K]
-        gemm(a, acts[(K, N)][0], r, N, K, threads)
+        run(M, N, K, r)
         fl += flops(r, N, K)
     dt = time.perf_counter() - t
+    what = "fp8 decode + fp32 GEMM" if fp8 else "dense fp32 GEMM on the pruned A"
     return {"value": round(fl / dt / 1e12, 6), "unit": "TFLOPS", "cores": threads, "kind": "port",
-            "sample": f"first {rows} rows of each of the {len(shapes)} shapes (dense fp32 GEMM on the pruned A), "
-                      f"{dt:.1f} s"}
+            "sample": f"first {rows} rows of each of the {len(shapes)} shapes ({what}), {dt:.1f} s"}
 
 
 # ------------------------------------------------- on-device packer
@@ -1051,7 +1095,8 @@ def main():
     ap.add_argument("--no-static-weights", dest="static_weights", action="store_false",
                     help="launch without SPMM24_STATIC_WEIGHTS (no kernel in the step writes the weights)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--dtype", choices=["f16", "bf16"], default="f16", help="operand and output type (SPMM24_BF16)")
+    ap.add_argument("--dtype", choices=["f16", "bf16", "fp8"], default="f16",
+                    help="operand and output type (SPMM24_BF16; fp8: E4M3 operands through spmm24_launch_fp8, fp16 out)")
     ap.add_argument("--epilogue", choices=["none", "bias_silu", "bias_residual"], default="none",
                     help="fused epilogue through spmm24_launch_fused")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)

@@ -172,6 +172,89 @@ extern "C" int spmm24_prune_2of4(uint16_t* a, int M, int K) { return prune_rows<
 
 extern "C" int spmm24_prune_2of4_bf16(uint16_t* a, int M, int K) { return prune_rows<bf2f>(a, M, K); }
 
+// ------------------------------------------------------------------- fp8
+// OCP fp8 bytes (E4M3: fmt 0, E5M2: fmt 1).  For both, |x| of a non-NaN
+// byte orders like the 7-bit integer b & 0x7f; NaN is every magnitude above
+// the largest non-NaN pattern (0x7e for E4M3, whose only NaN is 0x7f; the
+// infinity 0x7c for E5M2) and compares false with everything, as the float
+// comparisons of the 16-bit prune do.
+namespace {
+
+inline bool fp8_gt(uint32_t a, uint32_t b, uint32_t top) { return a <= top && b <= top && a > b; }
+
+int prune_rows_fp8(uint8_t* a, int M, int K, int fmt) {
+    if (!a || M <= 0 || K <= 0 || K % 4 || (fmt != 0 && fmt != 1)) return -1;
+    const uint32_t top = fmt == 0 ? 0x7eu : 0x7cu;
+    parallel_for(M, K, [&](int m0, int m1) {
+        for (int m = m0; m < m1; ++m) {
+            uint8_t* row = a + (size_t)m * K;
+            for (int g = 0; g < K; g += 4) {
+                uint32_t v[4];
+                for (int i = 0; i < 4; ++i) v[i] = row[g + i] & 0x7fu;
+                int k0 = 0;
+                for (int i = 1; i < 4; ++i)
+                    if (fp8_gt(v[i], v[k0], top)) k0 = i;
+                int k1 = -1;
+                for (int i = 0; i < 4; ++i) {
+                    if (i == k0) continue;
+                    if (k1 < 0 || fp8_gt(v[i], v[k1], top)) k1 = i;
+                }
+                for (int i = 0; i < 4; ++i)
+                    if (i != k0 && i != k1) row[g + i] = 0;
+            }
+        }
+    });
+    return 0;
+}
+
+}  // namespace
+
+extern "C" int spmm24_prune_2of4_fp8(uint8_t* a, int M, int K, int fmt) { return prune_rows_fp8(a, M, K, fmt); }
+
+// Values: band b, 32-K block q, row r -> 16 bytes at ((b*K/32 + q)*16 + r)*16.
+// Metadata: band b, 128-K group g, row r -> 16 bytes at ((b*K/128 + g)*16 +
+// r)*16, nibble c = group of four at K 128g + 4c (i0 | i1 << 2, i0 < i1).
+// Compress rule of the 16-bit packer (test/utils.h:124-146) on bytes.
+extern "C" int spmm24_compress_a_fp8(const uint8_t* dense, int M, int K, uint8_t* vals, uint8_t* meta) {
+    if (!dense || !vals || !meta || M <= 0 || K <= 0 || M % 16 || K % 128) return -1;
+    const int blocks = K / 32, groups = K / 128;
+    std::vector<char> bad((size_t)(M / 16), 0);
+    parallel_for(M / 16, (long)16 * K, [&](int b0, int b1) {
+        for (int band = b0; band < b1 && !bad[band]; ++band)
+            for (int r = 0; r < 16; ++r) {
+                const uint8_t* src = dense + (size_t)(band * 16 + r) * K;
+                for (int g = 0; g < groups; ++g) {
+                    uint8_t md[16] = {};
+                    for (int c = 0; c < 32; ++c) {
+                        const int k = g * 128 + 4 * c;
+                        int zeros = 0, kept = 0;
+                        uint32_t nib = 0;
+                        uint8_t* dst = vals + (((size_t)band * blocks + k / 32) * 16 + r) * 16 + (k % 32) / 2;
+                        for (int o = 0; o < 4; ++o) {
+                            const uint8_t x = src[k + o];
+                            if (zeros < 2 && (x & 0x7fu) == 0) {
+                                ++zeros;
+                                continue;
+                            }
+                            if (kept == 2) {
+                                bad[band] = 1;
+                                return;
+                            }
+                            dst[kept] = x;
+                            nib |= (uint32_t)o << (2 * kept);
+                            ++kept;
+                        }
+                        md[c / 2] |= (uint8_t)(nib << (4 * (c & 1)));
+                    }
+                    std::memcpy(meta + (((size_t)band * groups + g) * 16 + r) * 16, md, 16);
+                }
+            }
+    });
+    for (char b : bad)
+        if (b) return -2;
+    return (int)((size_t)M * K / 2);
+}
+
 // ------------------------------------------------- C++ reference drop-ins
 int toolCompressMatrixA(half* denseMatrixA, int Global_M, int Global_K, int Block_M, int Block_K,
                         half** compressedMatrixA, uint16_t** matadata) {

@@ -221,6 +221,17 @@ __device__ __forceinline__ void mma_sp_f16(uint32_t d_tmem, uint64_t a_desc, uin
         : "memory");
 }
 
+// The fp8 form (kind::f8f6f4; formats in the instruction descriptor).
+__device__ __forceinline__ void mma_sp_f8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t meta_tmem,
+                                          uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %5, 0;\n\t"
+        "tcgen05.mma.sp.cta_group::1.kind::f8f6f4 [%0], %1, %2, [%3], %4, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(meta_tmem), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 // 128 lanes x 128 bits from shared memory (canonical no-swizzle K-major
 // layout: 8-row core matrices of 16-byte rows) into TMEM lanes 0..127,
 // four consecutive 32-bit columns.

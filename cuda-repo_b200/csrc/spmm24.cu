@@ -54,15 +54,16 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-// All three operands are moved as raw 16-bit words (no conversion in TMA).
+// Operands are moved as raw 16-bit words (the fp8 B as bytes): no conversion
+// in TMA.
 bool encode(CUtensorMap* m, int rank, const void* base, const cuuint64_t* dims, const cuuint64_t* strides_bytes,
-            const cuuint32_t* box) {
+            const cuuint32_t* box, CUtensorMapDataType type = CU_TENSOR_MAP_DATA_TYPE_UINT16) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return false;
     cuuint32_t estr[5] = {1, 1, 1, 1, 1};
-    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, (cuuint32_t)rank, const_cast<void*>(base), dims, strides_bytes,
-                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    CUresult r = fn(m, type, (cuuint32_t)rank, const_cast<void*>(base), dims, strides_bytes, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
 }
 
@@ -149,7 +150,9 @@ int cluster_smem(int tn) {
     }
 }
 
-Plan make_plan(int M, int N, int K, int split_k, int sms, bool plain = true) {
+// plain: the plain fp16 launch (the only one the stream-K option serves).
+// allow_pair: the CTA-pair path may be chosen (not for fp8).
+Plan make_plan(int M, int N, int K, int split_k, int sms, bool plain = true, bool allow_pair = true) {
     Plan p{};
     int tn = N <= 16 ? 16 : N <= 32 ? 32 : N <= 64 ? 64 : 128;
     const int forced = env_int("SPMM24_TILE_N", 0);  // tuning override (16/32/64/128/256)
@@ -186,7 +189,7 @@ Plan make_plan(int M, int N, int K, int split_k, int sms, bool plain = true) {
     // Wide N with K % 128 == 0: a CTA pair per 256 x 256 tile (cta_group::2),
     // so each SM feeds the tensor core half of B.
     const int pair_env = env_int("SPMM24_PAIR", -1);  // tuning override: 0 = never, 1 = whenever legal
-    const bool pair_ok = (K % 128 == 0) && (split_k <= 1);
+    const bool pair_ok = allow_pair && (K % 128 == 0) && (split_k <= 1);
     if (pair_ok && (pair_env == 1 || (pair_env != 0 && N > 128))) {
         p.path = Path::kPair;
         p.shallow = false;
@@ -358,6 +361,20 @@ cudaError_t launch_cluster(const Plan& pl, cudaStream_t stream, int dev, bool pd
                          V::C_::SMEM_ALLOC, stream, (unsigned)pl.split, pdl, ta, tb, te, kp);
 }
 
+// The fp8 instantiation (general epilogue always); attribute slots kFp8Slot + idx.
+constexpr int kFp8Slot = 48;
+
+template <class V>
+cudaError_t launch_cluster_fp8(const Plan& pl, cudaStream_t stream, int dev, bool pdl, const CUtensorMap& ta,
+                               const CUtensorMap& tb, const CUtensorMap& te, const ClusterParams& kp, int idx) {
+    using C8 = ClusterCfg<V::kTileN, V::kStages, true>;
+    auto kern = spmm24_cluster_kernel<V::kTileN, V::kStages, true, true>;
+    cudaError_t e = prepare(kern, C8::SMEM_ALLOC, dev, kFp8Slot + idx);
+    if (e != cudaSuccess) return e;
+    return launch_kernel(kern, dim3((unsigned)pl.split, (unsigned)pl.n_tiles, (unsigned)pl.m_tiles), C8::SMEM_ALLOC,
+                         stream, (unsigned)pl.split, pdl, ta, tb, te, kp);
+}
+
 template <class V>
 cudaError_t launch_streamk(const Plan& pl, cudaStream_t stream, int dev, bool pdl, const CUtensorMap& ta,
                            const CUtensorMap& tb, const CUtensorMap& te, const StreamKParams& kp, int idx) {
@@ -385,21 +402,9 @@ cudaError_t launch_pair(const Plan& pl, cudaStream_t stream, int dev, bool pdl, 
                          : launch_pair_v<false>(pl, stream, dev, pdl, ta, tb, te, kp, 11);
 }
 
-size_t streamk_partial_bytes(const Plan& pl) { return (size_t)pl.grid * kTileM * pl.tile_n * sizeof(float); }
-
-cudaError_t launch_impl(cudaStream_t stream, const void* A, const void* B, const uint16_t* E, void* C, int M, int N,
-                        int K, int split_k, unsigned flags, const spmm24_epilogue* user_epi = nullptr,
-                        const spmm24_gather* gather = nullptr) {
-    g_last_error[0] = '\0';
-    if (!A || !B || !E || !C) return invalid("null pointer");
-    if (M <= 0 || N <= 0 || K <= 0) return invalid("M, N and K must be positive");
-    if (M % 16) return invalid("M must be a multiple of 16");
-    if (K % 64) return invalid("K must be a multiple of 64");
-    if (split_k < 0) return invalid("split_k must be >= 0");
-    if (((uintptr_t)A | (uintptr_t)B | (uintptr_t)E) & 15u) return invalid("A, B and metadata must be 16-byte aligned");
-    if ((uintptr_t)C & 1u) return invalid("C must be 2-byte aligned");
-    if ((long)M / kTileM >= 65535) return invalid("M too large");
-    if (flags & ~(unsigned)(SPMM24_STATIC_WEIGHTS | SPMM24_NO_PDL | SPMM24_BF16)) return invalid("unknown flag");
+// Validates a caller's epilogue and turns it into the kernels' form
+// (SPMM24_BF16 in flags: 16-bit outputs are bf16).
+cudaError_t make_epilogue(const spmm24_epilogue* user_epi, unsigned flags, const void* C, Epilogue* out) {
     Epilogue epi{nullptr, nullptr, 1.f, kActNone, 0, (flags & SPMM24_BF16) ? 1 : 0};
     if (user_epi) {
         if (user_epi->activation < SPMM24_ACT_NONE || user_epi->activation > SPMM24_ACT_GELU)
@@ -417,6 +422,28 @@ cudaError_t launch_impl(cudaStream_t stream, const void* A, const void* B, const
         if (epi.packed && (((uintptr_t)C | (uintptr_t)epi.residual) & 15u))
             return invalid("a packed C (and its residual) must be 16-byte aligned");
     }
+    *out = epi;
+    return cudaSuccess;
+}
+
+size_t streamk_partial_bytes(const Plan& pl) { return (size_t)pl.grid * kTileM * pl.tile_n * sizeof(float); }
+
+cudaError_t launch_impl(cudaStream_t stream, const void* A, const void* B, const uint16_t* E, void* C, int M, int N,
+                        int K, int split_k, unsigned flags, const spmm24_epilogue* user_epi = nullptr,
+                        const spmm24_gather* gather = nullptr) {
+    g_last_error[0] = '\0';
+    if (!A || !B || !E || !C) return invalid("null pointer");
+    if (M <= 0 || N <= 0 || K <= 0) return invalid("M, N and K must be positive");
+    if (M % 16) return invalid("M must be a multiple of 16");
+    if (K % 64) return invalid("K must be a multiple of 64");
+    if (split_k < 0) return invalid("split_k must be >= 0");
+    if (((uintptr_t)A | (uintptr_t)B | (uintptr_t)E) & 15u) return invalid("A, B and metadata must be 16-byte aligned");
+    if ((uintptr_t)C & 1u) return invalid("C must be 2-byte aligned");
+    if ((long)M / kTileM >= 65535) return invalid("M too large");
+    if (flags & ~(unsigned)(SPMM24_STATIC_WEIGHTS | SPMM24_NO_PDL | SPMM24_BF16)) return invalid("unknown flag");
+    Epilogue epi;
+    cudaError_t e = make_epilogue(user_epi, flags, C, &epi);
+    if (e != cudaSuccess) return e;
     if (gather) {
         if (gather->n_ranks < 1 || gather->n_ranks > SPMM24_MAX_GATHER_RANKS)
             return invalid("gather: n_ranks must be 1..8");
@@ -440,7 +467,7 @@ cudaError_t launch_impl(cudaStream_t stream, const void* A, const void* B, const
                        !epi.packed && !epi.bf16 && epi.gather_n == 0;
 
     int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
+    e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     Plan pl = make_plan(M, N, K, split_k, sm_count(dev), plain);
 
@@ -540,6 +567,7 @@ cudaError_t launch_impl(cudaStream_t stream, const void* A, const void* B, const
     kp.stages_total = pl.stages_total;
     kp.split = pl.split;
     kp.weights_static = wstatic;
+    kp.mma_fmt = 0;
     if (pl.shallow) {
         if (pl.tile_n == 16) return launch_cluster<CV16s>(pl, stream, dev, pdl, ta, tb, te, kp, 9);
         return launch_cluster<CV32s>(pl, stream, dev, pdl, ta, tb, te, kp, 10);
@@ -550,6 +578,82 @@ cudaError_t launch_impl(cudaStream_t stream, const void* A, const void* B, const
         case 64: return launch_cluster<CV64>(pl, stream, dev, pdl, ta, tb, te, kp, 2);
         case 128: return launch_cluster<CV128>(pl, stream, dev, pdl, ta, tb, te, kp, 3);
         default: return launch_cluster<CV256>(pl, stream, dev, pdl, ta, tb, te, kp, 4);
+    }
+}
+
+// ------------------------------------------------------------------- fp8
+// The fp8 SpMM runs the cluster kernel with a stage of 256 logical K; its A
+// values occupy the bytes of a 16-bit A with K/2, so the plan and the A
+// descriptor are those of K/2.
+cudaError_t launch_fp8_impl(cudaStream_t stream, const void* A, const void* B, const void* E, void* C, int M, int N,
+                            int K, int split_k, unsigned flags, const spmm24_epilogue* user_epi) {
+    g_last_error[0] = '\0';
+    if (!A || !B || !E || !C) return invalid("null pointer");
+    if (M <= 0 || N <= 0 || K <= 0) return invalid("M, N and K must be positive");
+    if (M % 16) return invalid("M must be a multiple of 16");
+    if (K % 128) return invalid("fp8: K must be a multiple of 128");
+    if (split_k < 0) return invalid("split_k must be >= 0");
+    if (((uintptr_t)A | (uintptr_t)B | (uintptr_t)E) & 15u) return invalid("A, B and metadata must be 16-byte aligned");
+    if ((uintptr_t)C & 1u) return invalid("C must be 2-byte aligned");
+    if ((long)M / kTileM >= 65535) return invalid("M too large");
+    if (flags & ~(unsigned)(SPMM24_STATIC_WEIGHTS | SPMM24_NO_PDL | SPMM24_BF16 | SPMM24_FP8_A_E5M2 |
+                            SPMM24_FP8_B_E5M2))
+        return invalid("unknown flag");
+    Epilogue epi;
+    cudaError_t e = make_epilogue(user_epi, flags, C, &epi);
+    if (e != cudaSuccess) return e;
+    int dev = 0;
+    e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const int Kh = K / 2;  // the 16-bit-equivalent K of the A bytes
+    Plan pl = make_plan(M, N, Kh, split_k, sm_count(dev), false, false);
+
+    CUtensorMap ta, tb, te;
+    {
+        cuuint64_t dims[3] = {128, (cuuint64_t)(M / 16), (cuuint64_t)(Kh / 16)};
+        cuuint64_t str[2] = {(cuuint64_t)16 * Kh, 256};
+        cuuint32_t box[3] = {128, 8, 8};
+        if (!encode(&ta, 3, A, dims, str, box)) return invalid("TMA descriptor for A could not be encoded");
+    }
+    // B (N x K bytes): (16 bytes of K, rows, 16-byte chunks of K); box
+    // tile_n rows x 16 chunks (256 K) -> smem [chunk][row][16 B].
+    {
+        cuuint64_t dims[3] = {16, (cuuint64_t)N, (cuuint64_t)(K / 16)};
+        cuuint64_t str[2] = {(cuuint64_t)K, 16};
+        cuuint32_t box[3] = {16, (cuuint32_t)pl.tile_n, 16};
+        if (!encode(&tb, 3, B, dims, str, box, CU_TENSOR_MAP_DATA_TYPE_UINT8))
+            return invalid("TMA descriptor for B could not be encoded");
+    }
+    // E: (256 bytes of one band and 128-K group, bands, groups); box 8 bands
+    // x 2 groups -> smem [group][band][256 B].
+    {
+        cuuint64_t dims[3] = {128, (cuuint64_t)(M / 16), (cuuint64_t)(K / 128)};
+        cuuint64_t str[2] = {(cuuint64_t)(K / 128) * 256, 256};
+        cuuint32_t box[3] = {128, 8, 2};
+        if (!encode(&te, 3, E, dims, str, box)) return invalid("TMA descriptor for metadata could not be encoded");
+    }
+    ClusterParams kp;
+    kp.C = static_cast<uint16_t*>(C);
+    kp.epi = epi;
+    kp.M = M;
+    kp.N = N;
+    kp.K = K;
+    kp.groups = K / 128;
+    kp.stages_total = pl.stages_total;
+    kp.split = pl.split;
+    kp.weights_static = (flags & SPMM24_STATIC_WEIGHTS) ? 1 : 0;
+    kp.mma_fmt = ((flags & SPMM24_FP8_A_E5M2) ? kIdescFp8AE5M2 : 0u) | ((flags & SPMM24_FP8_B_E5M2) ? kIdescFp8BE5M2 : 0u);
+    const bool pdl = !(flags & SPMM24_NO_PDL);
+    if (pl.shallow) {
+        if (pl.tile_n == 16) return launch_cluster_fp8<CV16s>(pl, stream, dev, pdl, ta, tb, te, kp, 9);
+        return launch_cluster_fp8<CV32s>(pl, stream, dev, pdl, ta, tb, te, kp, 10);
+    }
+    switch (pl.tile_n) {
+        case 16: return launch_cluster_fp8<CV16>(pl, stream, dev, pdl, ta, tb, te, kp, 0);
+        case 32: return launch_cluster_fp8<CV32>(pl, stream, dev, pdl, ta, tb, te, kp, 1);
+        case 64: return launch_cluster_fp8<CV64>(pl, stream, dev, pdl, ta, tb, te, kp, 2);
+        case 128: return launch_cluster_fp8<CV128>(pl, stream, dev, pdl, ta, tb, te, kp, 3);
+        default: return launch_cluster_fp8<CV256>(pl, stream, dev, pdl, ta, tb, te, kp, 4);
     }
 }
 
@@ -761,6 +865,12 @@ extern "C" cudaError_t spmm24_launch_fused(cudaStream_t stream, const void* comp
                                            const uint16_t* metadata, void* c, int M, int N, int K, int split_k,
                                            unsigned flags, const spmm24_epilogue* epilogue) {
     return spmm24::launch_impl(stream, compressed_a, b_packed, metadata, c, M, N, K, split_k, flags, epilogue);
+}
+
+extern "C" cudaError_t spmm24_launch_fp8(cudaStream_t stream, const void* values, const void* b_nk, const void* metadata,
+                                         void* c, int M, int N, int K, int split_k, unsigned flags,
+                                         const spmm24_epilogue* epilogue) {
+    return spmm24::launch_fp8_impl(stream, values, b_nk, metadata, c, M, N, K, split_k, flags, epilogue);
 }
 
 extern "C" cudaError_t spmm24_launch_gather(cudaStream_t stream, const void* compressed_a, const void* b_packed,

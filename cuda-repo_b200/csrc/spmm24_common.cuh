@@ -69,16 +69,21 @@ __device__ __forceinline__ void trace_stamp(long long base, int slot) {
 #define SPMM24_TRACE_FIELD
 #endif
 
-template <int N_TILE, int STAGES, int ACC_BUFS>
+// FP8: a stage covers 256 logical K of fp8 operands in the same A and B
+// bytes (A: 8 blocks of 32 K; B: 16 chunks of 16 K x N_TILE rows) and twice
+// the metadata (two 128-K groups, 8 TMEM columns).
+template <int N_TILE, int STAGES, int ACC_BUFS, bool FP8 = false>
 struct Cfg {
     static_assert(N_TILE % 16 == 0 && N_TILE >= 16 && N_TILE <= 256, "M=128 sparse MMA needs N % 16 == 0");
+    static constexpr bool kFp8 = FP8;
     static constexpr int A_BYTES = 8 * 8 * 256;          // 8 16-K blocks x 8 bands x (16 rows x 16 B)
     static constexpr int B_BYTES = (N_TILE / 8) * 2048;  // strips x (4 blocks x 2 groups x 256 B)
-    static constexpr int E_BYTES = 16 * 128;             // 16 core matrices of 8 x 16 B
+    static constexpr int E_BYTES = (FP8 ? 2 : 1) * 16 * 128;  // 16 core matrices of 8 x 16 B per copy
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + E_BYTES;
     static constexpr int RING_BYTES = STAGES * STAGE_BYTES;
     static constexpr int META_COL = ACC_BUFS * N_TILE;  // TMEM column of the metadata ring
-    static constexpr int TMEM_NEED = META_COL + 4 * STAGES;
+    static constexpr int META_STRIDE = FP8 ? 8 : 4;     // metadata columns per stage
+    static constexpr int TMEM_NEED = META_COL + META_STRIDE * STAGES;
     static constexpr int TMEM_COLS = TMEM_NEED <= 32 ? 32 : TMEM_NEED <= 64 ? 64 : TMEM_NEED <= 128 ? 128
                                                           : TMEM_NEED <= 256 ? 256 : 512;
     static_assert(TMEM_NEED <= 512, "TMEM overflow");
@@ -99,22 +104,34 @@ __host__ __device__ constexpr uint32_t make_idesc() {
 // Operand-format bits that turn an f16 descriptor into a bf16 one (A and B).
 constexpr uint32_t kIdescBf16 = (1u << 7) | (1u << 10);
 
-// The weight (A + metadata) half of one stage's loads.
+// The weight (A + metadata) half of one stage's loads.  g0: the stage's
+// first 64-K group (fp8: its first 128-K metadata group).
 template <class C_>
 __device__ __forceinline__ void load_stage_weights(uint8_t* st, uint64_t* bar, const CUtensorMap* tmA,
                                                    const CUtensorMap* tmE, int band0, int g0, uint64_t pol) {
     // A: box (128 halves, 8 bands, 8 blocks) -> smem [block][band][256 B]
+    // (fp8: the same bytes, blocks of 32 K)
     ptx::tma_load_3d(st, tmA, bar, 0, band0, 4 * g0, pol);
-    // E: box (128 words, 8 bands) -> smem [band][group][128 B]
-    ptx::tma_load_2d(st + C_::A_BYTES + C_::B_BYTES, tmE, bar, 64 * g0, band0, pol);
+    if constexpr (C_::kFp8) {
+        // E: box (256 B of one band and group, 8 bands, 2 groups) -> smem [group][band][256 B]
+        ptx::tma_load_3d(st + C_::A_BYTES + C_::B_BYTES, tmE, bar, 0, band0, g0, pol);
+    } else {
+        // E: box (128 words, 8 bands) -> smem [band][group][128 B]
+        ptx::tma_load_2d(st + C_::A_BYTES + C_::B_BYTES, tmE, bar, 64 * g0, band0, pol);
+    }
 }
 
 // The activation (B) half of one stage's loads.
 template <class C_>
 __device__ __forceinline__ void load_stage_acts(uint8_t* st, uint64_t* bar, const CUtensorMap* tmB, int strip0, int g0,
                                                 uint64_t pol) {
-    // B: box (128 halves, 2 groups, 4 blocks, strips) -> smem [strip][block][group][256 B]
-    ptx::tma_load_4d(st + C_::A_BYTES, tmB, bar, 0, g0, 0, strip0, pol);
+    if constexpr (C_::kFp8) {
+        // B (N x K bytes): box (16 B of K, N_TILE rows, 16 chunks) -> smem [chunk][row][16 B]
+        ptx::tma_load_3d(st + C_::A_BYTES, tmB, bar, 0, 8 * strip0, 8 * g0, pol);
+    } else {
+        // B: box (128 halves, 2 groups, 4 blocks, strips) -> smem [strip][block][group][256 B]
+        ptx::tma_load_4d(st + C_::A_BYTES, tmB, bar, 0, g0, 0, strip0, pol);
+    }
 }
 
 // Final stage of an odd number of 64-K groups: the second group lies past K,
@@ -125,9 +142,14 @@ template <class C_>
 __device__ __forceinline__ void patch_tail_metadata(uint8_t* st, int lane) {
     uint8_t* e = st + C_::A_BYTES + C_::B_BYTES;
     const uint4 pat = make_uint4(0x44444444u, 0x44444444u, 0x44444444u, 0x44444444u);
-    for (int c = lane; c < 64; c += 32) {
-        const int cm = c >> 3;  // which of the 8 second-group core matrices
-        *reinterpret_cast<uint4*>(e + (2 * cm + 1) * 128 + (c & 7) * 16) = pat;
+    if constexpr (C_::kFp8) {
+        for (int c = lane; c < 128; c += 32)  // the second group: smem [1][band][256 B]
+            *reinterpret_cast<uint4*>(e + 2048 + c * 16) = pat;
+    } else {
+        for (int c = lane; c < 64; c += 32) {
+            const int cm = c >> 3;  // which of the 8 second-group core matrices
+            *reinterpret_cast<uint4*>(e + (2 * cm + 1) * 128 + (c & 7) * 16) = pat;
+        }
     }
     ptx::fence_proxy_async_smem();
     __syncwarp();
@@ -147,6 +169,39 @@ __device__ __forceinline__ void mma_stage(uint32_t st_addr, uint32_t meta_col, u
         const uint64_t adesc = smem_desc(st_addr + j * 2048, 4 * 2048, 128);
         const uint64_t bdesc = smem_desc(stB + j * 512, 128, 2048);
         ptx::mma_sp_f16(d_tmem, adesc, bdesc, meta_col + (j & 2), idesc | (uint32_t)(j & 1), accumulate);
+        accumulate = 1;
+    }
+}
+
+// fp8 (kind::f8f6f4, sparse K = 64 logical per MMA).  Instruction
+// descriptor: sparse, D=f32, A and B K-major, format bits from the caller
+// (A: bit 7 = E5M2, B: bit 10 = E5M2; zero = E4M3).
+template <int N_TILE>
+__host__ __device__ constexpr uint32_t make_idesc_fp8() {
+    return (1u << 2) | (1u << 4) | ((uint32_t)(N_TILE >> 3) << 17) | ((uint32_t)(kTileM >> 4) << 24);
+}
+constexpr uint32_t kIdescFp8AE5M2 = 1u << 7;
+constexpr uint32_t kIdescFp8BE5M2 = 1u << 10;
+
+// Metadata copies + the four fp8 sparse MMAs of one stage (single thread).
+// Metadata: each 128-K group is 128 rows x 16 bytes, one tcgen05.cp into
+// four TMEM columns (lane = row); MMA j reads columns 2j, 2j+1.  A: MMA j
+// takes 32-K blocks 2j, 2j+1 (K-major core matrices, 2048 B apart along K,
+// 128 B apart along M).  B: MMA j takes 16-K chunks 4j..4j+3 of the
+// [chunk][row][16 B] tile (N_TILE*16 B apart along K, 128 B along N).
+template <class C_, int N_TILE>
+__device__ __forceinline__ void mma_stage_fp8(uint32_t st_addr, uint32_t meta_col, uint32_t d_tmem,
+                                              uint32_t& accumulate, uint32_t fmt) {
+    const uint32_t idesc = make_idesc_fp8<N_TILE>() | fmt;
+    const uint32_t stB = st_addr + C_::A_BYTES;
+    const uint32_t stE = stB + C_::B_BYTES;
+    ptx::tmem_cp_128x128b(meta_col, smem_desc(stE, 0, 128));
+    ptx::tmem_cp_128x128b(meta_col + 4, smem_desc(stE + 2048, 0, 128));
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const uint64_t adesc = smem_desc(st_addr + j * 4096, 2048, 128);
+        const uint64_t bdesc = smem_desc(stB + j * (N_TILE * 64), N_TILE * 16, 128);
+        ptx::mma_sp_f8(d_tmem, adesc, bdesc, meta_col + 2 * j, idesc, accumulate);
         accumulate = 1;
     }
 }

@@ -61,10 +61,11 @@ constexpr uint32_t kBarTmem = 2;  // named barrier: warps 1..5 after TMEM alloca
 struct ClusterParams {
     uint16_t* C;  // fp16 or bf16 elements (epi.bf16), row-major or packed (epi.packed)
     int M, N, K;
-    int groups;        // K / 64
+    int groups;        // K / 64 (fp8: K / 128, the metadata groups)
     int stages_total;  // ceil(groups / 2)
     int split;         // CTAs per cluster along K
     int weights_static;
+    uint32_t mma_fmt;  // fp8 kernel: operand-format bits of the instruction descriptor
     Epilogue epi;
     SPMM24_TRACE_FIELD
 };
@@ -94,9 +95,9 @@ struct StreamKParams {
 };
 
 // -------------------------------------------------------------------------
-template <int N_TILE, int STAGES>
-struct ClusterCfg : Cfg<N_TILE, STAGES, 1> {
-    using B_ = Cfg<N_TILE, STAGES, 1>;
+template <int N_TILE, int STAGES, bool FP8 = false>
+struct ClusterCfg : Cfg<N_TILE, STAGES, 1, FP8> {
+    using B_ = Cfg<N_TILE, STAGES, 1, FP8>;
     static constexpr int RED_PITCH = N_TILE + 4;  // floats per row of the reduction buffer
     static constexpr int RED_ROWS = 136;          // >= S * ceil(128 / S) for every S <= 8
     // Narrow tiles get a dedicated receive buffer, so partial rows can be
@@ -121,11 +122,13 @@ struct ClusterCfg : Cfg<N_TILE, STAGES, 1> {
 // output).  The plain fp16 row-major SpMM is a separate instantiation
 // without it: the epilogue runs on the critical path at the end of every
 // tile, and its extra code measurably slows the plain kernel.
-template <int N_TILE, int STAGES, bool EPI>
-__global__ void __launch_bounds__(kThreads, ClusterCfg<N_TILE, STAGES>::CTAS_PER_SM)
+// FP8: the fp8 operand formats and kind::f8f6f4 MMAs (always with EPI).
+template <int N_TILE, int STAGES, bool EPI, bool FP8 = false>
+__global__ void __launch_bounds__(kThreads, ClusterCfg<N_TILE, STAGES, FP8>::CTAS_PER_SM)
 spmm24_cluster_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const __grid_constant__ CUtensorMap tmE, const ClusterParams p) {
-    using C_ = ClusterCfg<N_TILE, STAGES>;
+    static_assert(EPI || !FP8, "the fp8 kernel always runs the general epilogue");
+    using C_ = ClusterCfg<N_TILE, STAGES, FP8>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + C_::BAR_OFFSET);
@@ -232,8 +235,13 @@ spmm24_cluster_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_cons
             ptx::tc_fence_after();
             if (2 * (st_begin + it) + 1 >= p.groups) patch_tail_metadata<C_>(smem + s * C_::STAGE_BYTES, lane);
             if (lane == 0) {
-                mma_stage<C_, N_TILE>(smem_base + s * C_::STAGE_BYTES, tmem_base + C_::META_COL + 4 * s, tmem_base,
-                                      accumulate, (EPI && p.epi.bf16) ? kIdescBf16 : 0u);
+                if constexpr (FP8)
+                    mma_stage_fp8<C_, N_TILE>(smem_base + s * C_::STAGE_BYTES,
+                                              tmem_base + C_::META_COL + C_::META_STRIDE * s, tmem_base, accumulate,
+                                              p.mma_fmt);
+                else
+                    mma_stage<C_, N_TILE>(smem_base + s * C_::STAGE_BYTES, tmem_base + C_::META_COL + 4 * s,
+                                          tmem_base, accumulate, (EPI && p.epi.bf16) ? kIdescBf16 : 0u);
                 ptx::tc_commit(&empty[s]);
             }
             __syncwarp();
@@ -340,11 +348,6 @@ spmm24_cluster_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_cons
 }
 
 // -------------------------------------------------------------------------
-// A CTA pair computes a 256 x (2 * HALF_N) tile; each CTA holds 128 rows of A
-// and HALF_N columns of B.  HALF_N = 128 (256-wide tiles, 4-stage ring, one
-// CTA per SM) or 64 (128-wide tiles, 3-stage ring of 102 KB, two CTAs per
-// SM: TMA streams into shared memory at a bounded rate per CTA, so two
-// resident CTAs feed an SM about twice as fast as one).
 // A CTA pair computes a 256 x 256 tile; each CTA holds 128 rows of A and 128
 // columns of B.  With a K split, a cluster of two pairs computes the tile:
 // pair 1 sends its fp32 partial accumulator to pair 0 through distributed

@@ -108,6 +108,14 @@ _lib.spmm24_prune_2of4_device.argtypes = [_vp, _vp, ctypes.c_int, ctypes.c_int]
 _lib.spmm24_prune_2of4_device.restype = ctypes.c_int
 _lib.spmm24_pack_b_device.argtypes = [_vp, _vp, ctypes.c_int, ctypes.c_int, _vp]
 _lib.spmm24_pack_b_device.restype = ctypes.c_int
+_u8p = ctypes.POINTER(ctypes.c_uint8)
+_lib.spmm24_prune_2of4_fp8.argtypes = [_u8p, ctypes.c_int, ctypes.c_int, ctypes.c_int]
+_lib.spmm24_prune_2of4_fp8.restype = ctypes.c_int
+_lib.spmm24_compress_a_fp8.argtypes = [_u8p, ctypes.c_int, ctypes.c_int, _u8p, _u8p]
+_lib.spmm24_compress_a_fp8.restype = ctypes.c_int
+_lib.spmm24_launch_fp8.argtypes = [_vp, _vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                   ctypes.c_uint, ctypes.c_void_p]
+_lib.spmm24_launch_fp8.restype = ctypes.c_int
 _lib.spmm24_workspace_bytes.argtypes = [ctypes.c_int] * 4
 _lib.spmm24_workspace_bytes.restype = ctypes.c_size_t
 _lib.spmm24_select_config.argtypes = [ctypes.c_int] * 4 + [ctypes.POINTER(SpmmConfig)]
@@ -127,6 +135,8 @@ BF16 = 4            # SPMM24_BF16
 ACT_NONE, ACT_RELU, ACT_SILU, ACT_GELU = 0, 1, 2, 3   # SPMM24_ACT_*
 OUT_ROW_MAJOR, OUT_PACKED_B = 0, 1                    # SPMM24_OUT_*
 PRUNE_NONE, PRUNE_F16, PRUNE_BF16 = 0, 1, 2           # SPMM24_PRUNE_*
+FP8_E4M3, FP8_E5M2 = 0, 1                             # SPMM24_FP8_E4M3 / E5M2
+FP8_A_E5M2, FP8_B_E5M2 = 8, 16                        # spmm24_launch_fp8 flags
 
 
 class SpmmError(RuntimeError):
@@ -185,6 +195,17 @@ def launch_fused(stream, compressed_a, b_packed, metadata, c, M: int, N: int, K:
     epi = Epilogue(_ptr(bias), _ptr(residual), float(alpha), int(activation), int(out_layout))
     return _lib.spmm24_launch_fused(_stream_handle(stream), _ptr(compressed_a), _ptr(b_packed), _ptr(metadata),
                                     _ptr(c), M, N, K, split_k, flags, ctypes.byref(epi))
+
+
+def launch_fp8(stream, values, b_nk, metadata, c, M: int, N: int, K: int, split_k: int = 0, flags: int = 0,
+               bias=None, residual=None, alpha: float = 1.0, activation: int = ACT_NONE,
+               out_layout: int = OUT_ROW_MAJOR) -> int:
+    """spmm24_launch_fp8: C = act(alpha * A_sparse B + bias) + residual with fp8
+    A (values + metadata in the fp8 formats) and B as N x K fp8 bytes; C fp16
+    (bf16 with BF16 in flags).  Returns the cudaError_t code."""
+    epi = Epilogue(_ptr(bias), _ptr(residual), float(alpha), int(activation), int(out_layout))
+    return _lib.spmm24_launch_fp8(_stream_handle(stream), _ptr(values), _ptr(b_nk), _ptr(metadata), _ptr(c), M, N, K,
+                                  split_k, flags, ctypes.addressof(epi))
 
 
 def SpMM_N2M4_Launch(stream, Compressed_A, B, metadata, C, M_Global: int, N_Global: int, K_Global: int,
@@ -420,6 +441,34 @@ def prune_2of4_bf16(dense_a: np.ndarray, M: int, K: int) -> np.ndarray:
     if _lib.spmm24_prune_2of4_bf16(_p(a), M, K) != 0:
         raise ValueError("prune_2of4_bf16: K % 4 must be 0")
     return a
+
+
+def _u8(a: np.ndarray) -> np.ndarray:
+    a = np.ascontiguousarray(a)
+    if a.dtype != np.uint8:
+        raise TypeError("fp8 arrays are passed as uint8 bit patterns")
+    return a
+
+
+def prune_2of4_fp8(dense_a: np.ndarray, M: int, K: int, fmt: int = FP8_E4M3) -> np.ndarray:
+    """Magnitude 2:4 pruning along K of fp8 bytes (returns a pruned copy)."""
+    a = _u8(dense_a).reshape(-1).copy()
+    if _lib.spmm24_prune_2of4_fp8(a.ctypes.data_as(_u8p), M, K, fmt) != 0:
+        raise ValueError("prune_2of4_fp8: K % 4 must be 0 and fmt 0 or 1")
+    return a
+
+
+def compress_a_fp8(dense_a: np.ndarray, M: int, K: int):
+    """(values, metadata) of a 2:4-sparse fp8 matrix in the fp8 SpMM's formats."""
+    d = _u8(dense_a).reshape(-1)
+    vals = np.empty(M * K // 2, dtype=np.uint8)
+    meta = np.empty(M * K // 8, dtype=np.uint8)
+    n = _lib.spmm24_compress_a_fp8(d.ctypes.data_as(_u8p), M, K, vals.ctypes.data_as(_u8p), meta.ctypes.data_as(_u8p))
+    if n == -2:
+        raise ValueError("matrix is not 2:4 sparse along K (a group of four has fewer than two zeros)")
+    if n < 0:
+        raise ValueError("compress_a_fp8: M % 16 and K % 128 must be 0")
+    return vals, meta
 
 
 # ------------------------------------------------- packed-weight files

@@ -248,6 +248,45 @@ cudaError_t spmm24_prune_2of4_bf16_device(cudaStream_t stream, void* dense_a, in
  * Asynchronous on `stream`. */
 cudaError_t spmm24_pack_b_device(cudaStream_t stream, const void* b_rowmajor, int K, int N, void* b_packed_out);
 
+/* ---------------------------------------------------------------- fp8
+ * fp8 extension (no counterpart in the reference, which is fp16 only):
+ * A and B hold OCP 8-bit floats, E4M3 (no infinities) or E5M2, and the
+ * tensor cores run tcgen05.mma.sp kind::f8f6f4 with fp32 accumulation; C,
+ * bias and residual are fp16 (bf16 with SPMM24_BF16).  Half the weight
+ * bytes of the 16-bit path.  Formats (K % 128 == 0, M % 16 == 0):
+ *   values   M*K/2 bytes: band b (16 rows), 32-K block q, row r -> the 16
+ *            kept bytes of that row's eight groups of four, in K order, at
+ *            ((b*K/32 + q)*16 + r)*16 -- the 16-bit layout's 16x8 blocks
+ *            with bytes in place of halves
+ *   metadata M*K/8 bytes: band b, 128-K group g, row r -> 16 bytes at
+ *            ((b*K/128 + g)*16 + r)*16; nibble c (bits 4c..4c+3 of the
+ *            little-endian 128-bit row) describes the group of four at
+ *            K = 128g + 4c: i0 | i1 << 2, i0 < i1 the kept positions
+ *   B        N x K row-major (the activations as a layer produces them: no
+ *            B packing step)
+ * The compress rule is the 16-bit one (test/utils.h:124-146) on bytes: the
+ * first two zeros (+0 or -0) of each group are dropped. */
+enum { SPMM24_FP8_E4M3 = 0, SPMM24_FP8_E5M2 = 1 };
+enum {
+    SPMM24_FP8_A_E5M2 = 8u,  /* spmm24_launch_fp8 flag: A holds E5M2 (default E4M3) */
+    SPMM24_FP8_B_E5M2 = 16u  /* B holds E5M2 (default E4M3) */
+};
+/* Magnitude 2:4 prune of a row-major M x K fp8 matrix in place (the
+ * selection of spmm24_prune_2of4; NaN compares false).  fmt: SPMM24_FP8_*.
+ * Returns 0 or -1. */
+int spmm24_prune_2of4_fp8(uint8_t* dense_a, int M, int K, int fmt);
+/* Dense M x K fp8 (host) -> values (M*K/2 bytes) + metadata (M*K/8 bytes).
+ * Returns M*K/2, -1 for bad arguments, -2 when a group of four holds more
+ * than two non-zeros. */
+int spmm24_compress_a_fp8(const uint8_t* dense_a, int M, int K, uint8_t* values_out, uint8_t* meta_out);
+/* C = A_sparse * B^T-layout B, with the same split_k, flags
+ * (SPMM24_STATIC_WEIGHTS, SPMM24_NO_PDL, SPMM24_BF16 for the output type,
+ * SPMM24_FP8_A_E5M2, SPMM24_FP8_B_E5M2) and epilogue (alpha doubles as the
+ * product of the per-tensor dequantisation scales) as spmm24_launch_fused.
+ * values, b_nk and metadata 16-byte aligned.  Asynchronous on `stream`. */
+cudaError_t spmm24_launch_fp8(cudaStream_t stream, const void* values, const void* b_nk, const void* metadata, void* c,
+                              int M, int N, int K, int split_k, unsigned flags, const spmm24_epilogue* epilogue);
+
 /* Packed-weight files (no counterpart in the reference): a 64-byte header
  * (magic "SPMM24W", version 1, dtype 0 = fp16 / 1 = bf16, M, K, payload
  * sizes, FNV-1a-64 checksum of the payload), then the compressed values and

@@ -12,6 +12,8 @@ Reference anchors (SpeakOutLoudly/CUDA-Repo):
   init_host_matrices_pruned test/utils.h:38-66 -> ref_init_pruned
   SpMM_N2M4_Kernel + SplitK_Reduction math (src/SpMM_Kernel.cuh:301-492,
   src/reduce_Kernel.cuh:27-53) -> dense_gemm_f32 / spmm_from_abi_f32
+  The fp8 extension (no reference counterpart): the same prune, compress rule
+  (test/utils.h:124-146) and GEMM on OCP E4M3 / E5M2 bytes -> *_fp8
 """
 from __future__ import annotations
 
@@ -27,6 +29,7 @@ _REF_PACKER = os.path.join(_HERE, "_ref", "libref_packer.so")
 _REF_SPMM = os.path.join(_HERE, "_ref", "libref_spmm.so")
 
 _u16p = ctypes.POINTER(ctypes.c_uint16)
+_u8p = ctypes.POINTER(ctypes.c_uint8)
 _f32p = ctypes.POINTER(ctypes.c_float)
 
 
@@ -65,6 +68,13 @@ def lib() -> ctypes.CDLL:
         L.orc_prune_magnitude_2of4_bf16.argtypes = [_u16p, ctypes.c_int, ctypes.c_int]
         L.orc_dense_gemm_bf16_f32.argtypes = [_u16p, _u16p, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                               ctypes.c_int]
+        L.orc_fp8_to_f32_array.argtypes = [_u8p, _f32p, ctypes.c_size_t, ctypes.c_int]
+        L.orc_f32_to_fp8_array.argtypes = [_f32p, _u8p, ctypes.c_size_t, ctypes.c_int]
+        L.orc_prune_magnitude_2of4_fp8.argtypes = [_u8p, ctypes.c_int, ctypes.c_int, ctypes.c_int]
+        L.orc_compress_a_fp8.argtypes = [_u8p, ctypes.c_int, ctypes.c_int, _u8p, _u8p]
+        L.orc_compress_a_fp8.restype = ctypes.c_int
+        L.orc_spmm_fp8_f32.argtypes = [_u8p, _u8p, _u8p, _f32p] + [ctypes.c_int] * 6
+        L.orc_spmm_fp8_f32.restype = ctypes.c_int
         L.orc_fnv1a64.argtypes = [ctypes.c_void_p, ctypes.c_size_t]
         L.orc_fnv1a64.restype = ctypes.c_uint64
         L.orc_max_threads.restype = ctypes.c_int
@@ -184,6 +194,52 @@ def f32_to_f16_bits(x: np.ndarray) -> np.ndarray:
     out = np.empty(x.size, dtype=np.uint16)
     lib().orc_f32_to_f16(_pf(x), _p16(out), x.size)
     return out
+
+
+# ------------------------------------------------------------------ fp8
+# fmt 0 = OCP E4M3 (no infinities), 1 = OCP E5M2.
+def _p8(a: np.ndarray):
+    assert a.dtype == np.uint8 and a.flags["C_CONTIGUOUS"]
+    return a.ctypes.data_as(_u8p)
+
+
+def fp8_to_f32(x: np.ndarray, fmt: int) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.uint8)
+    out = np.empty(x.size, dtype=np.float32)
+    lib().orc_fp8_to_f32_array(_p8(x), _pf(out), x.size, fmt)
+    return out
+
+
+def f32_to_fp8(x: np.ndarray, fmt: int) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty(x.size, dtype=np.uint8)
+    lib().orc_f32_to_fp8_array(_pf(x), _p8(out), x.size, fmt)
+    return out
+
+
+def prune_magnitude_2of4_fp8(a: np.ndarray, M: int, K: int, fmt: int) -> np.ndarray:
+    a = np.ascontiguousarray(a, dtype=np.uint8).copy()
+    lib().orc_prune_magnitude_2of4_fp8(_p8(a), M, K, fmt)
+    return a
+
+
+def compress_a_fp8(dense: np.ndarray, M: int, K: int):
+    dense = np.ascontiguousarray(dense, dtype=np.uint8)
+    vals = np.zeros(M * K // 2, dtype=np.uint8)
+    meta = np.zeros(M * K // 8, dtype=np.uint8)
+    n = lib().orc_compress_a_fp8(_p8(dense), M, K, _p8(vals), _p8(meta))
+    return n, vals, meta
+
+
+def spmm_fp8_f32(vals, meta, b_nk, M: int, N: int, K: int, fmt_a: int = 0, fmt_b: int = 0,
+                 threads: int = 0) -> np.ndarray:
+    c = np.empty(M * N, dtype=np.float32)
+    rc = lib().orc_spmm_fp8_f32(_p8(np.ascontiguousarray(vals, dtype=np.uint8)),
+                                _p8(np.ascontiguousarray(meta, dtype=np.uint8)),
+                                _p8(np.ascontiguousarray(b_nk, dtype=np.uint8)), _pf(c), M, N, K, fmt_a, fmt_b, threads)
+    if rc != 0:
+        raise ValueError(f"spmm_fp8_f32 failed ({rc})")
+    return c
 
 
 def fnv1a64(buf: np.ndarray) -> int:

@@ -1,0 +1,188 @@
+"""spmm24_launch_fp8 (OCP E4M3 / E5M2 operands, kind::f8f6f4 sparse MMAs)
+against the oracle: fp8 decode -> fp32 GEMM in increasing k, epilogue in
+float64, rounded to C's type.
+
+Tolerance: fp8 products are exact in fp32; the GPU and the oracle differ
+only in the order (and the tensor core's internal precision) of the fp32
+sums, so |got - ref| <= 2^-10 |ref| + 2^-12 S, S = sum_k |a_mk b_nk|,
+plus the final rounding to C's type, is a bound a wrong metadata index or
+operand layout cannot meet.  Integer-valued cases are exact."""
+import numpy as np
+import pytest
+
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+from test_gpu_epilogue import _act, _bits_to_f32, _round  # noqa: E402
+
+
+def _u8dev(a, device):
+    import torch
+
+    return torch.from_numpy(np.ascontiguousarray(a, dtype=np.uint8)).to(device)
+
+
+def _i16dev(a, device):
+    import torch
+
+    return torch.from_numpy(np.ascontiguousarray(a, dtype=np.uint16).view(np.int16)).to(device)
+
+
+def _dense_f32(bits, fmt, shape):
+    return O.fp8_to_f32(bits.reshape(-1), fmt).reshape(shape).astype(np.float64)
+
+
+def _problem(M, N, K, fmt_a, fmt_b, seed, integer=False):
+    import spmm24
+
+    rng = np.random.default_rng(seed)
+    if integer:
+        a = rng.integers(-4, 5, (M, K)).astype(np.float32)
+        b = rng.integers(-3, 4, (N, K)).astype(np.float32)
+    else:
+        a = rng.standard_normal((M, K)).astype(np.float32)
+        b = rng.standard_normal((N, K)).astype(np.float32)
+    a_bits = spmm24.prune_2of4_fp8(O.f32_to_fp8(a.reshape(-1), fmt_a), M, K, fmt_a)
+    b_bits = O.f32_to_fp8(b.reshape(-1), fmt_b)
+    vals, meta = spmm24.compress_a_fp8(a_bits, M, K)
+    acc = O.spmm_fp8_f32(vals, meta, b_bits, M, N, K, fmt_a, fmt_b).reshape(M, N).astype(np.float64)
+    A = _dense_f32(a_bits, fmt_a, (M, K))
+    B = _dense_f32(b_bits, fmt_b, (N, K))
+    S = np.abs(A) @ np.abs(B).T
+    return vals, meta, b_bits, acc, S
+
+
+def _run(dev, M, N, K, *, fmt_a=0, fmt_b=0, split=0, bf16=False, bias=False, residual=False, alpha=1.0, act=0,
+         packed=False, seed=0, integer=False, tile_env=None, monkeypatch=None):
+    import torch
+
+    import spmm24
+
+    if tile_env is not None:
+        monkeypatch.setenv("SPMM24_TILE_N", str(tile_env))
+    vals, meta, b_bits, acc, S = _problem(M, N, K, fmt_a, fmt_b, seed, integer)
+    rng = np.random.default_rng(seed + 7)
+    bias_bits = _round(rng.standard_normal(M), bf16) if bias else None
+    res_bits = _round(rng.standard_normal((M, N)), bf16).reshape(M, N) if residual else None
+    strips = (N + 7) // 8
+    c = torch.zeros(strips * 8 * M if packed else M * N, dtype=torch.int16, device=dev)
+    res_dev = None
+    if residual:
+        if packed:
+            pad = np.zeros((M, strips * 8), dtype=np.uint16)
+            pad[:, :N] = res_bits
+            res_layout = pad.reshape(M, strips, 8).transpose(1, 0, 2).reshape(-1)
+        else:
+            res_layout = res_bits.reshape(-1)
+        res_dev = _i16dev(res_layout, dev)
+    flags = (spmm24.FP8_A_E5M2 if fmt_a else 0) | (spmm24.FP8_B_E5M2 if fmt_b else 0) | (spmm24.BF16 if bf16 else 0)
+    rc = spmm24.launch_fp8(None, _u8dev(vals, dev), _u8dev(b_bits, dev), _u8dev(meta, dev), c, M, N, K, split, flags,
+                           bias=_i16dev(bias_bits, dev) if bias else None, residual=res_dev, alpha=alpha,
+                           activation=act, out_layout=spmm24.OUT_PACKED_B if packed else spmm24.OUT_ROW_MAJOR)
+    assert rc == 0, spmm24._lib.spmm24_last_error().decode()
+    torch.cuda.synchronize(dev)
+    got_bits = c.cpu().numpy().view(np.uint16)
+    if packed:
+        full = got_bits.reshape(strips, M, 8).transpose(1, 0, 2).reshape(M, strips * 8)
+        assert not full[:, N:].any(), "pad columns of a packed C must be zero"
+        got_bits = full[:, :N]
+    got_bits = got_bits.reshape(M, N)
+    assert spmm24.device_status(dev.index or 0) == 0
+
+    y = alpha * acc
+    if bias:
+        y = y + _bits_to_f32(bias_bits, bf16).astype(np.float64)[:, None]
+    y = _act(y, act)
+    if residual:
+        y = y + _bits_to_f32(res_bits, bf16).astype(np.float64).reshape(M, N)
+    ref_bits = _round(y.astype(np.float32), bf16).reshape(M, N)
+    if integer and not (bias or residual or act or alpha != 1.0):
+        assert np.array_equal(got_bits, ref_bits), int((got_bits != ref_bits).sum())
+        return
+    got = _bits_to_f32(got_bits, bf16).reshape(M, N).astype(np.float64)
+    ref = _bits_to_f32(ref_bits, bf16).reshape(M, N).astype(np.float64)
+    assert np.isfinite(got).all()
+    ulp = 2.0 ** (-7 if bf16 else -10)
+    # the epilogue's slope (<= 1.1 for the activations) scales the sum error
+    tol = ulp * np.abs(ref) + 1.2 * abs(alpha) * 2.0 ** -12 * S + 1e-6
+    bad = np.abs(got - ref) > tol
+    assert not bad.any(), (int(bad.sum()), float(np.abs(got - ref).max()))
+
+
+# (M, N, K, split): one half-filled stage (odd metadata groups: the tail
+# patch), decode shapes with cluster K splits, every N tile (16, 32, 64,
+# 128), ragged N, N = 1.
+SHAPES = [
+    (128, 16, 128, 0),
+    (256, 16, 384, 0),
+    (4096, 16, 4096, 0),
+    (2048, 32, 2048, 3),
+    (1024, 64, 1024, 0),
+    (512, 128, 512, 0),
+    (256, 200, 768, 0),
+    (512, 8, 4096, 0),
+    (1024, 1, 2048, 0),
+    (384, 24, 1152, 8),
+]
+
+
+@pytest.mark.parametrize("shape", SHAPES, ids=lambda s: "x".join(map(str, s)))
+def test_fp8_e4m3_matches_oracle(cuda_device, shape):
+    M, N, K, split = shape
+    _run(cuda_device, M, N, K, split=split, seed=M + N + K)
+
+
+@pytest.mark.parametrize("fmts", [(0, 0), (1, 0), (0, 1), (1, 1)], ids=["e4m3xe4m3", "e5m2xe4m3", "e4m3xe5m2",
+                                                                      "e5m2xe5m2"])
+def test_fp8_formats(cuda_device, fmts):
+    _run(cuda_device, 512, 16, 1024, fmt_a=fmts[0], fmt_b=fmts[1], seed=11)
+    _run(cuda_device, 256, 64, 640, fmt_a=fmts[0], fmt_b=fmts[1], seed=12)
+
+
+@pytest.mark.parametrize("shape", [(256, 16, 512), (128, 32, 1024), (512, 48, 384)], ids=lambda s: "x".join(map(str, s)))
+def test_fp8_integer_exact(cuda_device, shape):
+    """Small integers are exact in fp8 and in every partial sum: C must equal
+    the rounded exact product bit for bit (any metadata or layout slip shows)."""
+    M, N, K = shape
+    _run(cuda_device, M, N, K, integer=True, seed=5)
+    _run(cuda_device, M, N, K, integer=True, fmt_a=1, fmt_b=1, seed=6)
+
+
+@pytest.mark.parametrize("split", [1, 2, 4, 5, 8])
+def test_fp8_split_k(cuda_device, split):
+    _run(cuda_device, 1024, 16, 2560, split=split, seed=split)
+
+
+def test_fp8_epilogue_bf16_out(cuda_device):
+    _run(cuda_device, 512, 32, 1024, bf16=True, bias=True, residual=True, alpha=0.25, act=2, seed=21)
+    _run(cuda_device, 768, 16, 2048, bias=True, act=3, alpha=0.5, seed=22)
+    _run(cuda_device, 256, 40, 512, residual=True, packed=True, act=1, seed=23)
+
+
+def test_fp8_wide_tile(cuda_device, monkeypatch):
+    """The 256-column tile (a tuning override for fp8)."""
+    _run(cuda_device, 256, 256, 1024, seed=31, tile_env=256, monkeypatch=monkeypatch)
+
+
+def test_fp8_cuda_graph(cuda_device):
+    """fp8 launches captured in a CUDA graph give the eager results."""
+    import torch
+
+    import spmm24
+
+    M, N, K = 1024, 16, 2048
+    vals, meta, b_bits, _, _ = _problem(M, N, K, 0, 0, 41)
+    A, E, B = _u8dev(vals, cuda_device), _u8dev(meta, cuda_device), _u8dev(b_bits, cuda_device)
+    c1 = torch.empty(M * N, dtype=torch.int16, device=cuda_device)
+    c2 = torch.empty_like(c1)
+    assert spmm24.launch_fp8(torch.cuda.current_stream(cuda_device), A, B, E, c1, M, N, K, 0,
+                             spmm24.STATIC_WEIGHTS) == 0
+    torch.cuda.synchronize(cuda_device)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        assert spmm24.launch_fp8(torch.cuda.current_stream(cuda_device), A, B, E, c2, M, N, K, 0,
+                                 spmm24.STATIC_WEIGHTS) == 0
+    g.replay()
+    torch.cuda.synchronize(cuda_device)
+    assert torch.equal(c1, c2)
