@@ -1067,17 +1067,26 @@ def run_single(args):
     M, N, K = parts[:3]
     split = parts[3] if len(parts) > 3 else 0
     dev = torch.device("cuda", 0)
-    _, vals, meta = make_layer(torch, spmm24, M, K, 0.02, seed=1)
-    _, bp = make_activations(torch, spmm24, K, N, seed=2)
+    fp8 = args.dtype == "fp8"
+    if fp8:
+        _, vals, meta = make_layer_fp8(torch, spmm24, M, K, seed=1)
+        _, bp = make_activations_fp8(torch, K, N, seed=2)
+    else:
+        _, vals, meta = make_layer(torch, spmm24, M, K, 0.02, seed=1)
+        _, bp = make_activations(torch, spmm24, K, N, seed=2)
     A, E, B = to_dev(torch, vals, dev), to_dev(torch, meta, dev), to_dev(torch, bp, dev)
     C = torch.empty((M, N), dtype=torch.float16, device=dev)
     s = torch.cuda.current_stream(dev)
     for _ in range(args.warmup + 3):
-        rc = spmm24.launch(s, A, B, E, C, M, N, K, None, split)
+        if fp8:
+            rc = spmm24.launch_fp8(s, A, B, E, C, M, N, K, split, 0, alpha=0.02)
+        else:
+            rc = spmm24.launch(s, A, B, E, C, M, N, K, None, split)
         if rc != 0:
             raise SystemExit(f"launch failed {rc}")
     torch.cuda.synchronize(dev)
-    print(json.dumps({"single": [M, N, K], "config": spmm24.select_config(M, N, K, split),
+    print(json.dumps({"single": [M, N, K], "dtype": args.dtype,
+                      "config": spmm24.select_config(M, N, K // 2 if fp8 else K, split),
                       "status": spmm24.device_status(0)}))
 
 

@@ -70,8 +70,9 @@ __device__ __forceinline__ void trace_stamp(long long base, int slot) {
 #endif
 
 // FP8: a stage covers 256 logical K of fp8 operands in the same A and B
-// bytes (A: 8 blocks of 32 K; B: 16 chunks of 16 K x N_TILE rows) and twice
-// the metadata (two 128-K groups, 8 TMEM columns).
+// bytes (A: 8 blocks of 32 K; B: two 128-byte-swizzled halves of N_TILE
+// rows x 128 K, each a multiple of 1024 bytes) and twice the metadata (two
+// 128-K groups, 8 TMEM columns).
 template <int N_TILE, int STAGES, int ACC_BUFS, bool FP8 = false>
 struct Cfg {
     static_assert(N_TILE % 16 == 0 && N_TILE >= 16 && N_TILE <= 256, "M=128 sparse MMA needs N % 16 == 0");
@@ -87,12 +88,23 @@ struct Cfg {
     static constexpr int TMEM_COLS = TMEM_NEED <= 32 ? 32 : TMEM_NEED <= 64 ? 64 : TMEM_NEED <= 128 ? 128
                                                           : TMEM_NEED <= 256 ? 256 : 512;
     static_assert(TMEM_NEED <= 512, "TMEM overflow");
+    static_assert(!FP8 || (A_BYTES % 1024 == 0 && (B_BYTES / 2) % 1024 == 0 && STAGE_BYTES % 1024 == 0),
+                  "fp8 B halves must start on 1024-byte boundaries (128-byte swizzle atoms)");
 };
 
 // Shared-memory matrix descriptor, canonical no-swizzle layout (version 1).
 __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
     return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
            ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
+}
+// K-major operand in the 128-byte swizzled layout: rows of 128 bytes, 8-row
+// atoms of 1024 bytes (1024-byte aligned), 16-byte chunk c of row r stored
+// at chunk c ^ (r % 8) -- what TMA writes with SWIZZLE_128B.  addr may
+// point inside the first row (a K offset within the 128 bytes); the leading
+// offset is unused for this layout.
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
+    return (uint64_t)((addr >> 4) & 0x3FFFu) | (1ull << 16) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) |
+           (2ull << 61);
 }
 
 // Instruction descriptor: sparse, D=f32, A=B=f16, A K-major, B MN-major.
@@ -126,8 +138,10 @@ template <class C_>
 __device__ __forceinline__ void load_stage_acts(uint8_t* st, uint64_t* bar, const CUtensorMap* tmB, int strip0, int g0,
                                                 uint64_t pol) {
     if constexpr (C_::kFp8) {
-        // B (N x K bytes): box (16 B of K, N_TILE rows, 16 chunks) -> smem [chunk][row][16 B]
-        ptx::tma_load_3d(st + C_::A_BYTES, tmB, bar, 0, 8 * strip0, 8 * g0, pol);
+        // B (N x K bytes): two boxes of (128 bytes of K, N_TILE rows), 128-byte
+        // swizzle -> smem [half][row][128 B]
+        ptx::tma_load_2d(st + C_::A_BYTES, tmB, bar, 128 * g0, 8 * strip0, pol);
+        ptx::tma_load_2d(st + C_::A_BYTES + C_::B_BYTES / 2, tmB, bar, 128 * g0 + 128, 8 * strip0, pol);
     } else {
         // B: box (128 halves, 2 groups, 4 blocks, strips) -> smem [strip][block][group][256 B]
         ptx::tma_load_4d(st + C_::A_BYTES, tmB, bar, 0, g0, 0, strip0, pol);
@@ -187,8 +201,8 @@ constexpr uint32_t kIdescFp8BE5M2 = 1u << 10;
 // Metadata: each 128-K group is 128 rows x 16 bytes, one tcgen05.cp into
 // four TMEM columns (lane = row); MMA j reads columns 2j, 2j+1.  A: MMA j
 // takes 32-K blocks 2j, 2j+1 (K-major core matrices, 2048 B apart along K,
-// 128 B apart along M).  B: MMA j takes 16-K chunks 4j..4j+3 of the
-// [chunk][row][16 B] tile (N_TILE*16 B apart along K, 128 B along N).
+// 128 B apart along M).  B: MMA j takes bytes 64 (j % 2) .. + 63 of every
+// row of the 128-byte swizzled half j / 2 (N_TILE rows of 128 B).
 template <class C_, int N_TILE>
 __device__ __forceinline__ void mma_stage_fp8(uint32_t st_addr, uint32_t meta_col, uint32_t d_tmem,
                                               uint32_t& accumulate, uint32_t fmt) {
@@ -200,7 +214,7 @@ __device__ __forceinline__ void mma_stage_fp8(uint32_t st_addr, uint32_t meta_co
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         const uint64_t adesc = smem_desc(st_addr + j * 4096, 2048, 128);
-        const uint64_t bdesc = smem_desc(stB + j * (N_TILE * 64), N_TILE * 16, 128);
+        const uint64_t bdesc = smem_desc_sw128(stB + (j >> 1) * (C_::B_BYTES / 2) + (j & 1) * 64);
         ptx::mma_sp_f8(d_tmem, adesc, bdesc, meta_col + 2 * j, idesc, accumulate);
         accumulate = 1;
     }
