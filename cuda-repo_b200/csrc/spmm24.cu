@@ -111,6 +111,7 @@ using CV256 = ClusterVariant<256, 2>;
 // Pair tiles: 256 x 256 with a 4-stage ring (one CTA per SM).
 constexpr int kPairStages = 4;
 using PairC = PairCfg<kPairStages>;
+using PairC8 = PairCfg<kPairStages, true>;
 using SV16 = StreamKVariant<16, 8>;
 using SV32 = StreamKVariant<32, 8>;
 // Shallow rings (about 92 KB of shared memory): two CTAs fit on one SM, so
@@ -399,6 +400,17 @@ cudaError_t launch_pair_v(const Plan& pl, cudaStream_t stream, int dev, bool pdl
                          pdl, ta, tb, te, kp, kPairThreads);
 }
 
+template <bool KSPLIT>
+cudaError_t launch_pair_fp8(const Plan& pl, cudaStream_t stream, int dev, bool pdl, const CUtensorMap& ta,
+                            const CUtensorMap& tb, const CUtensorMap& te, const PairParams& kp) {
+    auto kern = spmm24_pair_kernel<kPairStages, true, KSPLIT, true>;
+    cudaError_t e = prepare(kern, PairC8::SMEM_ALLOC, dev, kFp8Slot + (KSPLIT ? 12 : 11));
+    if (e != cudaSuccess) return e;
+    const unsigned cl = KSPLIT ? 4u : 2u;
+    return launch_kernel(kern, dim3(cl, (unsigned)pl.n_tiles, (unsigned)pl.m_tiles), PairC8::SMEM_ALLOC, stream, cl,
+                         pdl, ta, tb, te, kp, kPairThreads);
+}
+
 cudaError_t launch_pair(const Plan& pl, cudaStream_t stream, int dev, bool pdl, const CUtensorMap& ta,
                         const CUtensorMap& tb, const CUtensorMap& te, const PairParams& kp) {
     return pl.split == 2 ? launch_pair_v<true>(pl, stream, dev, pdl, ta, tb, te, kp, 12)
@@ -536,6 +548,7 @@ cudaError_t launch_impl(cudaStream_t stream, const void* A, const void* B, const
         kp.stages_total = K / 128;
         kp.weights_static = wstatic;
         kp.split = pl.split;
+        kp.mma_fmt = 0;
         return launch_pair(pl, stream, dev, pdl, ta, tb, te, kp);
     }
     if (pl.path == Path::kStreamK) {
@@ -612,8 +625,10 @@ cudaError_t launch_fp8_impl(cudaStream_t stream, const void* A, const void* B, c
     // Automatic splits stop at 5: measured on the decode chain (M = 4096,
     // K = 4096 and 11008, N <= 32), five K slices beat eight by 4-8% per call
     // (a cheaper cluster reduction and more SM slots left to the next
-    // launch's early CTAs), and 11008-row layers pick 3 either way.
-    Plan pl = make_plan(M, N, Kh, split_k, sm_count(dev), false, false, 5);
+    // launch's early CTAs), and 11008-row layers pick 3 either way.  Wide N
+    // takes the CTA pair as for 16-bit operands (its stage is 256 K: K % 256).
+    Plan pl = make_plan(M, N, Kh, split_k, sm_count(dev), false, Kh % 128 == 0, 5);
+    const bool pair = pl.path == Path::kPair;
 
     CUtensorMap ta, tb, te;
     {
@@ -627,7 +642,7 @@ cudaError_t launch_fp8_impl(cudaStream_t stream, const void* A, const void* B, c
     {
         cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)N};
         cuuint64_t str[1] = {(cuuint64_t)K};
-        cuuint32_t box[2] = {128, (cuuint32_t)pl.tile_n};
+        cuuint32_t box[2] = {128, (cuuint32_t)(pair ? PairC8::HALF_N : pl.tile_n)};
         if (!encode(&tb, 2, B, dims, str, box, CU_TENSOR_MAP_DATA_TYPE_UINT8, CU_TENSOR_MAP_SWIZZLE_128B))
             return invalid("TMA descriptor for B could not be encoded");
     }
@@ -639,6 +654,27 @@ cudaError_t launch_fp8_impl(cudaStream_t stream, const void* A, const void* B, c
         cuuint32_t box[3] = {128, 8, 2};
         if (!encode(&te, 3, E, dims, str, box)) return invalid("TMA descriptor for metadata could not be encoded");
     }
+    const uint32_t mma_fmt =
+        ((flags & SPMM24_FP8_A_E5M2) ? kIdescFp8AE5M2 : 0u) | ((flags & SPMM24_FP8_B_E5M2) ? kIdescFp8BE5M2 : 0u);
+    const bool pdl = !(flags & SPMM24_NO_PDL);
+    if (pair) {
+        if (epi.residual && pl.split != 1) {  // the partner partial would overlap the residual's staging
+            pl.split = 1;
+            pl.grid = 2 * pl.m_tiles * pl.n_tiles;
+        }
+        PairParams kp;
+        kp.C = static_cast<uint16_t*>(C);
+        kp.epi = epi;
+        kp.M = M;
+        kp.N = N;
+        kp.K = K;
+        kp.stages_total = K / 256;
+        kp.weights_static = (flags & SPMM24_STATIC_WEIGHTS) ? 1 : 0;
+        kp.split = pl.split;
+        kp.mma_fmt = mma_fmt;
+        return pl.split == 2 ? launch_pair_fp8<true>(pl, stream, dev, pdl, ta, tb, te, kp)
+                             : launch_pair_fp8<false>(pl, stream, dev, pdl, ta, tb, te, kp);
+    }
     ClusterParams kp;
     kp.C = static_cast<uint16_t*>(C);
     kp.epi = epi;
@@ -649,8 +685,7 @@ cudaError_t launch_fp8_impl(cudaStream_t stream, const void* A, const void* B, c
     kp.stages_total = pl.stages_total;
     kp.split = pl.split;
     kp.weights_static = (flags & SPMM24_STATIC_WEIGHTS) ? 1 : 0;
-    kp.mma_fmt = ((flags & SPMM24_FP8_A_E5M2) ? kIdescFp8AE5M2 : 0u) | ((flags & SPMM24_FP8_B_E5M2) ? kIdescFp8BE5M2 : 0u);
-    const bool pdl = !(flags & SPMM24_NO_PDL);
+    kp.mma_fmt = mma_fmt;
     if (pl.shallow) {
         if (pl.tile_n == 16) return launch_cluster_fp8<CV16s>(pl, stream, dev, pdl, ta, tb, te, kp, 9);
         return launch_cluster_fp8<CV32s>(pl, stream, dev, pdl, ta, tb, te, kp, 10);

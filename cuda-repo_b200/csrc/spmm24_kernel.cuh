@@ -76,6 +76,7 @@ struct PairParams {
     int stages_total;  // K / 128 (the pair kernel requires K % 128 == 0)
     int weights_static;
     int split;         // pairs per cluster along K (1 or 2)
+    uint32_t mma_fmt;  // fp8 kernel: operand-format bits of the instruction descriptor
     Epilogue epi;
     SPMM24_TRACE_FIELD
 };
@@ -352,14 +353,18 @@ spmm24_cluster_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_cons
 // columns of B.  With a K split, a cluster of two pairs computes the tile:
 // pair 1 sends its fp32 partial accumulator to pair 0 through distributed
 // shared memory, and pair 0 adds it before the epilogue.
-template <int STAGES>
+// FP8: a stage covers 256 logical K of fp8 operands in the same A and B bytes
+// (B: two 128-byte-swizzled halves of HALF_N rows x 128 K) and two 128-K
+// metadata groups.
+template <int STAGES, bool FP8 = false>
 struct PairCfg {
+    static constexpr bool kFp8 = FP8;
     static constexpr int HALF_N = 128;                   // columns of B / C per CTA
     static constexpr int TILE_N = 2 * HALF_N;            // columns per pair
     static constexpr int TILE_M = 2 * kTileM;            // rows per pair
     static constexpr int A_BYTES = 8 * 8 * 256;          // this CTA's 128 rows x 128 logical K
     static constexpr int B_BYTES = (HALF_N / 8) * 2048;  // this CTA's HALF_N columns x 128 K
-    static constexpr int E_BYTES = 16 * 128;
+    static constexpr int E_BYTES = (FP8 ? 2 : 1) * 16 * 128;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + E_BYTES;
     static constexpr int RING_BYTES = STAGES * STAGE_BYTES;
     static constexpr int BAR_OFFSET = RING_BYTES;
@@ -368,7 +373,8 @@ struct PairCfg {
     static constexpr int SMEM_BYTES = HOLDER_OFFSET + 16;
     static constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;
     static constexpr int META_COL = TILE_N;  // accumulator: TILE_N fp32 columns
-    static constexpr int TMEM_NEED = META_COL + 4 * STAGES;
+    static constexpr int META_STRIDE = FP8 ? 8 : 4;
+    static constexpr int TMEM_NEED = META_COL + META_STRIDE * STAGES;
     static constexpr int TMEM_COLS = TMEM_NEED <= 128 ? 128 : TMEM_NEED <= 256 ? 256 : 512;
     static constexpr int C_PITCH = TILE_N + 8;  // halves per staged output row (bank-shifted)
     static constexpr int F_PITCH = TILE_N + 4;  // floats per staged fp32 row (epilogue with a residual)
@@ -382,7 +388,31 @@ struct PairCfg {
     static_assert(kTileM * C_PITCH * 2 <= RING_BYTES, "output staging does not fit");
     static_assert(RES_OFFSET + kTileM * TILE_N * 2 <= RING_BYTES, "fp32 staging + residual tile do not fit");
     static_assert(RECV_OFFSET + kTileM * F_PITCH * 4 <= RING_BYTES, "16-bit staging + partner partial do not fit");
+    static_assert(!FP8 || (A_BYTES % 1024 == 0 && (B_BYTES / 2) % 1024 == 0 && STAGE_BYTES % 1024 == 0),
+                  "fp8 B halves must start on 1024-byte boundaries (128-byte swizzle atoms)");
 };
+
+// One stage's loads for one CTA of a pair (both CTAs' loads complete on the
+// leader's barrier `bar`).  g: the stage index (128 logical K; fp8: 256).
+template <class C_>
+__device__ __forceinline__ void pair_load_weights(uint8_t* st, const CUtensorMap* tmA, const CUtensorMap* tmE,
+                                                  uint32_t bar, int band0, int g, uint64_t pol) {
+    ptx::tma_load_3d_pair(st, tmA, bar, 0, band0, 8 * g, pol);
+    if constexpr (C_::kFp8)
+        ptx::tma_load_3d_pair(st + C_::A_BYTES + C_::B_BYTES, tmE, bar, 0, band0, 2 * g, pol);
+    else
+        ptx::tma_load_2d_pair(st + C_::A_BYTES + C_::B_BYTES, tmE, bar, 128 * g, band0, pol);
+}
+template <class C_>
+__device__ __forceinline__ void pair_load_acts(uint8_t* st, const CUtensorMap* tmB, uint32_t bar, int strip0, int g,
+                                               uint64_t pol) {
+    if constexpr (C_::kFp8) {
+        ptx::tma_load_2d_pair(st + C_::A_BYTES, tmB, bar, 256 * g, 8 * strip0, pol);
+        ptx::tma_load_2d_pair(st + C_::A_BYTES + C_::B_BYTES / 2, tmB, bar, 256 * g + 128, 8 * strip0, pol);
+    } else {
+        ptx::tma_load_4d_pair(st + C_::A_BYTES, tmB, bar, 0, 2 * g, 0, strip0, pol);
+    }
+}
 
 constexpr int kPairGroupM = 8;  // tile rows per rasterisation group
 
@@ -392,15 +422,23 @@ template <int TILE_N>
 __host__ __device__ constexpr uint32_t pair_idesc() {
     return (1u << 2) | (1u << 4) | (1u << 16) | ((uint32_t)(TILE_N >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
 }
+// The fp8 pair MMA (kind::f8f6f4): sparse, D=f32, A and B K-major, M=256,
+// N=TILE_N; operand-format bits from the caller.
+template <int TILE_N>
+__host__ __device__ constexpr uint32_t pair_idesc_fp8() {
+    return (1u << 2) | (1u << 4) | ((uint32_t)(TILE_N >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
+}
 
 // EPI: the general epilogue, as for spmm24_cluster_kernel.  KSPLIT: a
 // cluster of two pairs, each taking half of the 128-K stages (p.split == 2;
 // not with a residual, whose staging the partner partial would overlap).
-template <int STAGES, bool EPI, bool KSPLIT>
+// FP8: fp8 operand formats and kind::f8f6f4 MMAs (always with EPI).
+template <int STAGES, bool EPI, bool KSPLIT, bool FP8 = false>
 __global__ void __launch_bounds__(kPairThreads, 1)
 spmm24_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmE, const PairParams p) {
-    using C_ = PairCfg<STAGES>;
+    static_assert(EPI || !FP8, "the fp8 kernel always runs the general epilogue");
+    using C_ = PairCfg<STAGES, FP8>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + C_::BAR_OFFSET);  // used in the leader only
@@ -476,14 +514,12 @@ spmm24_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                 const int g = st_begin + it;
                 uint8_t* st = smem + it * C_::STAGE_BYTES;
                 if (leader) ptx::mbar_arrive_expect_tx(&full[it], 2 * C_::STAGE_BYTES);
-                ptx::tma_load_3d_pair(st, &tmA, full0 + 8u * it, 0, band0, 8 * g, pol);
-                ptx::tma_load_2d_pair(st + C_::A_BYTES + C_::B_BYTES, &tmE, full0 + 8u * it, 128 * g, band0, pol);
+                pair_load_weights<C_>(st, &tmA, &tmE, full0 + 8u * it, band0, g, pol);
             }
             ptx::grid_dep_wait();
             SPMM24_STAMP(1);
             for (int it = 0; it < pre; ++it)
-                ptx::tma_load_4d_pair(smem + it * C_::STAGE_BYTES + C_::A_BYTES, &tmB, full0 + 8u * it, 0,
-                                      2 * (st_begin + it), 0, strip0, pol);
+                pair_load_acts<C_>(smem + it * C_::STAGE_BYTES, &tmB, full0 + 8u * it, strip0, st_begin + it, pol);
             for (int it = pre; it < st_count; ++it) {
                 const int s = it % STAGES;
                 const int g = st_begin + it;
@@ -495,15 +531,15 @@ spmm24_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                 uint8_t* st = smem + s * C_::STAGE_BYTES;
                 const uint32_t bar = full0 + 8u * s;
                 if (leader) ptx::mbar_arrive_expect_tx(&full[s], 2 * C_::STAGE_BYTES);
-                ptx::tma_load_3d_pair(st, &tmA, bar, 0, band0, 8 * g, pol);
-                ptx::tma_load_2d_pair(st + C_::A_BYTES + C_::B_BYTES, &tmE, bar, 128 * g, band0, pol);
-                ptx::tma_load_4d_pair(st + C_::A_BYTES, &tmB, bar, 0, 2 * g, 0, strip0, pol);
+                pair_load_weights<C_>(st, &tmA, &tmE, bar, band0, g, pol);
+                pair_load_acts<C_>(st, &tmB, bar, strip0, g, pol);
             }
         }
         __syncwarp();
     } else if (warp == 1 && leader) {
         // ---------------------------------- MMA issuer (leader CTA only)
-        const uint32_t idesc = pair_idesc<C_::TILE_N>() | ((EPI && p.epi.bf16) ? kIdescBf16 : 0u);
+        const uint32_t idesc = FP8 ? pair_idesc_fp8<C_::TILE_N>() | p.mma_fmt
+                                   : pair_idesc<C_::TILE_N>() | ((EPI && p.epi.bf16) ? kIdescBf16 : 0u);
         const uint32_t smem_base = ptx::smem_u32(smem);
         uint32_t accumulate = 0;
         for (int it = 0; it < st_count; ++it) {
@@ -519,15 +555,28 @@ spmm24_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
             if (lane == 0) {
                 const uint32_t st = smem_base + s * C_::STAGE_BYTES;
                 const uint32_t stB = st + C_::A_BYTES;
-                const uint32_t meta_col = tmem_base + C_::META_COL + 4 * s;
-                ptx::tmem_cp_128x128b_pair(meta_col, smem_desc(stB + C_::B_BYTES, 0, 128));
+                const uint32_t meta_col = tmem_base + C_::META_COL + C_::META_STRIDE * s;
+                if constexpr (FP8) {
+                    // as mma_stage_fp8, on both CTAs of the pair
+                    ptx::tmem_cp_128x128b_pair(meta_col, smem_desc(stB + C_::B_BYTES, 0, 128));
+                    ptx::tmem_cp_128x128b_pair(meta_col + 4, smem_desc(stB + C_::B_BYTES + 2048, 0, 128));
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const uint64_t adesc = smem_desc(st + j * 2048, 4 * 2048, 128);
-                    const uint64_t bdesc = smem_desc(stB + j * 512, 128, 2048);
-                    ptx::mma_sp_f16_pair(tmem_base, adesc, bdesc, meta_col + (j & 2), idesc | (uint32_t)(j & 1),
-                                         accumulate);
-                    accumulate = 1;
+                    for (int j = 0; j < 4; ++j) {
+                        const uint64_t adesc = smem_desc(st + j * 4096, 2048, 128);
+                        const uint64_t bdesc = smem_desc_sw128(stB + (j >> 1) * (C_::B_BYTES / 2) + (j & 1) * 64);
+                        ptx::mma_sp_f8_pair(tmem_base, adesc, bdesc, meta_col + 2 * j, idesc, accumulate);
+                        accumulate = 1;
+                    }
+                } else {
+                    ptx::tmem_cp_128x128b_pair(meta_col, smem_desc(stB + C_::B_BYTES, 0, 128));
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const uint64_t adesc = smem_desc(st + j * 2048, 4 * 2048, 128);
+                        const uint64_t bdesc = smem_desc(stB + j * 512, 128, 2048);
+                        ptx::mma_sp_f16_pair(tmem_base, adesc, bdesc, meta_col + (j & 2), idesc | (uint32_t)(j & 1),
+                                             accumulate);
+                        accumulate = 1;
+                    }
                 }
                 ptx::tc_commit_pair_mc(&empty[s], pair_mask);  // frees ring slot s in both CTAs of the pair
             }

@@ -161,8 +161,49 @@ def test_fp8_epilogue_bf16_out(cuda_device):
 
 
 def test_fp8_wide_tile(cuda_device, monkeypatch):
-    """The 256-column tile (a tuning override for fp8)."""
+    """The cluster kernel's 256-column tile (a tuning override; wide N
+    otherwise takes the CTA pair)."""
+    monkeypatch.setenv("SPMM24_PAIR", "0")
     _run(cuda_device, 256, 256, 1024, seed=31, tile_env=256, monkeypatch=monkeypatch)
+
+
+# CTA-pair kernel (N > 128, K % 256 == 0): 256 x 256 tiles, M and N ragged.
+PAIR_SHAPES = [
+    (512, 256, 1024),
+    (768, 520, 2048),
+    (256, 1024, 512),
+    (1024, 384, 4096),
+    (384, 136, 256),
+]
+
+
+@pytest.mark.parametrize("shape", PAIR_SHAPES, ids=lambda s: "x".join(map(str, s)))
+def test_fp8_pair_matches_oracle(cuda_device, shape):
+    import spmm24
+
+    M, N, K = shape
+    assert spmm24.select_config(M, N, K // 2)["cta_pair"] == 1
+    _run(cuda_device, M, N, K, seed=M + 3 * N + K)
+
+
+def test_fp8_pair_integer_exact_and_formats(cuda_device):
+    _run(cuda_device, 512, 256, 1024, integer=True, seed=51)
+    _run(cuda_device, 256, 512, 512, integer=True, fmt_a=1, fmt_b=0, seed=52)
+    _run(cuda_device, 512, 264, 768, fmt_a=0, fmt_b=1, seed=53)
+    _run(cuda_device, 256, 256, 1280, fmt_a=1, fmt_b=1, seed=54)
+
+
+def test_fp8_pair_k_split(cuda_device, monkeypatch):
+    """Two pairs per tile, each half of K, partial exchanged on chip."""
+    monkeypatch.setenv("SPMM24_PAIR_SPLIT", "2")
+    _run(cuda_device, 512, 512, 4096, seed=61)
+    _run(cuda_device, 256, 256, 2816, seed=62)  # odd number of 256-K stages
+    _run(cuda_device, 512, 256, 2048, bias=True, act=3, alpha=0.5, seed=63)
+
+
+def test_fp8_pair_epilogue(cuda_device):
+    _run(cuda_device, 512, 256, 1024, bf16=True, bias=True, residual=True, alpha=0.25, act=2, seed=71)
+    _run(cuda_device, 256, 264, 512, residual=True, packed=True, act=1, seed=72)
 
 
 def test_fp8_cuda_graph(cuda_device):
