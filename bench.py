@@ -58,9 +58,12 @@ WORKLOADS = {
 PACK_LAYERS = [(4096, 4096), (11008, 4096), (4096, 11008)]
 
 
-def pack_bytes(M, K):
+def pack_bytes(M, K, fp8=False):
     """Algorithmic bytes of one spmm24_pack_a_device call: the dense fp16
-    read, the compressed values and the metadata written."""
+    read, the compressed values and the metadata written (fp8: the dense
+    bytes, M*K/2 values, M*K/8 metadata)."""
+    if fp8:
+        return M * K + M * K // 2 + M * K // 8
     return 2 * M * K + M * K + M * K // 8
 
 
@@ -790,17 +793,21 @@ def cpu_baseline(layers, acts, shapes, budget_s=10.0, bf16=False, fp8=False):
 
 
 # ------------------------------------------------- on-device packer
-def host_pack_baseline(dense_np, budget_s=10.0):
+def host_pack_baseline(dense_np, budget_s=10.0, fp8=False):
     """The reference's own host packer (toolCompressMatrixA +
     toolReorderMetadata built from its sources into oracle/_ref), else the
     oracle's restatement of it, on a row sample of each layer; single
-    threaded as the reference is.  Returns (GB/s, kind, sample)."""
+    threaded as the reference is (fp8, which the reference lacks: the
+    oracle's fp8 prune + compress).  Returns (GB/s, kind, sample)."""
     sys.path.insert(0, os.path.join(REPO, "oracle"))
     import oracle as O
 
-    use_ref = O.ref_packer_available()
+    use_ref = O.ref_packer_available() and not fp8
 
     def pack(a, M, K):
+        if fp8:
+            O.compress_a_fp8(O.prune_magnitude_2of4_fp8(a, M, K, 0), M, K)
+            return
         # the reference has no pruning step (its inputs are generated 2:4):
         # the oracle's prune runs first, inside the timed work
         a = O.prune_magnitude_2of4(a, M, K)
@@ -822,11 +829,11 @@ def host_pack_baseline(dense_np, budget_s=10.0):
     for (M, K), a in zip(PACK_LAYERS, dense_np):
         r = min(rows, M)
         pack(a[: r * K], r, K)
-        nbytes += pack_bytes(r, K)
+        nbytes += pack_bytes(r, K, fp8)
     dt = time.perf_counter() - t
     kind = "reference" if use_ref else "port"
     return nbytes / dt / 1e9, kind, (f"first {rows} rows of each of the {len(PACK_LAYERS)} layers through "
-                                     f"{'oracle prune, then toolCompressMatrixA + toolReorderMetadata (oracle/_ref)' if use_ref else 'oracle prune + orc_compress_a + orc_reorder_metadata'}, "
+                                     f"{'oracle prune, then toolCompressMatrixA + toolReorderMetadata (oracle/_ref)' if use_ref else 'orc_prune_magnitude_2of4_fp8 + orc_compress_a_fp8' if fp8 else 'oracle prune + orc_compress_a + orc_reorder_metadata'}, "
                                      f"1 thread, {dt:.1f} s")
 
 
@@ -845,21 +852,30 @@ def run_pack(args, rank, world, local_rank):
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    # fp8: spmm24_pack_a_fp8_device on E4M3 weights (N(0,1) through torch's float8 cast)
+    fp8 = args.dtype == "fp8"
     g = torch.Generator(device=dev).manual_seed(7 + rank)
-    dense = [(torch.randn(M, K, generator=g, device=dev) * 0.02).half() for (M, K) in PACK_LAYERS]
-    vals = [torch.empty(M * K // 2, dtype=torch.int16, device=dev) for (M, K) in PACK_LAYERS]
-    meta = [torch.empty(M * K // 16, dtype=torch.int16, device=dev) for (M, K) in PACK_LAYERS]
+    if fp8:
+        dense = [torch.randn(M, K, generator=g, device=dev).to(torch.float8_e4m3fn).view(torch.uint8)
+                 for (M, K) in PACK_LAYERS]
+        vals = [torch.empty(M * K // 2, dtype=torch.uint8, device=dev) for (M, K) in PACK_LAYERS]
+        meta = [torch.empty(M * K // 8, dtype=torch.uint8, device=dev) for (M, K) in PACK_LAYERS]
+    else:
+        dense = [(torch.randn(M, K, generator=g, device=dev) * 0.02).half() for (M, K) in PACK_LAYERS]
+        vals = [torch.empty(M * K // 2, dtype=torch.int16, device=dev) for (M, K) in PACK_LAYERS]
+        meta = [torch.empty(M * K // 16, dtype=torch.int16, device=dev) for (M, K) in PACK_LAYERS]
     bad = torch.zeros(len(PACK_LAYERS), dtype=torch.int32, device=dev)
     stream = torch.cuda.current_stream(dev)
     hs = int(stream.cuda_stream)
     L = spmm24._lib
+    pack_fn = L.spmm24_pack_a_fp8_device if fp8 else L.spmm24_pack_a_device
 
     def step():
         for i, (M, K) in enumerate(PACK_LAYERS):
-            rc = L.spmm24_pack_a_device(hs, dense[i].data_ptr(), M, K, 1, vals[i].data_ptr(), meta[i].data_ptr(),
-                                        bad.data_ptr() + 4 * i)
+            rc = pack_fn(hs, dense[i].data_ptr(), M, K, 1, vals[i].data_ptr(), meta[i].data_ptr(),
+                         bad.data_ptr() + 4 * i)
             if rc != 0:
-                raise RuntimeError(f"spmm24_pack_a_device failed: {rc} {L.spmm24_last_error().decode()}")
+                raise RuntimeError(f"device packer failed: {rc} {L.spmm24_last_error().decode()}")
 
     for _ in range(args.warmup):
         step()
@@ -878,10 +894,15 @@ def run_pack(args, rank, world, local_rank):
     clocks = clk.summary()
     # the timed work is checked: no bad rows, and the smallest layer equals the host packer bit for bit
     assert int(bad.sum()) == 0
-    d0 = dense[0].view(torch.int16).cpu().numpy().view(np.uint16)
-    hv, hm = spmm24.compress_reordered(spmm24.prune_2of4(d0, *PACK_LAYERS[0]), *PACK_LAYERS[0])
-    assert np.array_equal(vals[0].cpu().numpy().view(np.uint16), hv)
-    assert np.array_equal(meta[0].cpu().numpy().view(np.uint16), hm)
+    if fp8:
+        d0 = dense[0].cpu().numpy().reshape(-1)
+        hv, hm = spmm24.compress_a_fp8(spmm24.prune_2of4_fp8(d0, *PACK_LAYERS[0], spmm24.FP8_E4M3), *PACK_LAYERS[0])
+        assert np.array_equal(vals[0].cpu().numpy(), hv) and np.array_equal(meta[0].cpu().numpy(), hm)
+    else:
+        d0 = dense[0].view(torch.int16).cpu().numpy().view(np.uint16)
+        hv, hm = spmm24.compress_reordered(spmm24.prune_2of4(d0, *PACK_LAYERS[0]), *PACK_LAYERS[0])
+        assert np.array_equal(vals[0].cpu().numpy().view(np.uint16), hv)
+        assert np.array_equal(meta[0].cpu().numpy().view(np.uint16), hm)
 
     # per-layer kernel durations (event pair around each launch)
     per = {}
@@ -890,7 +911,7 @@ def run_pack(args, rank, world, local_rank):
         for _ in range(5):
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record(stream)
-            L.spmm24_pack_a_device(hs, dense[i].data_ptr(), M, K, 1, vals[i].data_ptr(), meta[i].data_ptr(), None)
+            pack_fn(hs, dense[i].data_ptr(), M, K, 1, vals[i].data_ptr(), meta[i].data_ptr(), None)
             b.record(stream)
             torch.cuda.synchronize(dev)
             ts.append(a.elapsed_time(b) * 1e3)
@@ -924,39 +945,49 @@ def run_pack(args, rank, world, local_rank):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         elapsed_ms, e2e_ms = float(t[0]), float(t[1])
 
-    step_bytes = sum(pack_bytes(M, K) for (M, K) in PACK_LAYERS)
+    step_bytes = sum(pack_bytes(M, K, fp8) for (M, K) in PACK_LAYERS)
+    dense_bytes = sum(M * K * (1 if fp8 else 2) for (M, K) in PACK_LAYERS)
     value = step_bytes * args.steps * world / (elapsed_ms * 1e-3) / 1e9
     achieved = step_bytes * args.steps / (elapsed_ms * 1e-3) / 1e9
     peaks = load_peaks()
     out = {
-        "metric": "GB/s of the on-device 2:4 packer (magnitude prune + compress + reordered metadata) "
-                  "on the LLaMA-7B layer weights",
+        "metric": ("GB/s of the on-device fp8 2:4 packer (magnitude prune + compress + metadata) "
+                   "on the LLaMA-7B layer weights" if fp8 else
+                   "GB/s of the on-device 2:4 packer (magnitude prune + compress + reordered metadata) "
+                   "on the LLaMA-7B layer weights"),
         "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(elapsed_ms / args.steps, 5), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "u16 (fp16 bit patterns; integer/byte work)",
-        "data": "synthetic (seeded torch RNG on the device; dense fp16 N(0,0.02))",
+        "vs_baseline": None,
+        "dtype": "u8 (fp8 E4M3 bit patterns; integer/byte work)" if fp8 else "u16 (fp16 bit patterns; integer/byte work)",
+        "data": ("synthetic (seeded torch RNG on the device; dense E4M3 from N(0,1))" if fp8
+                 else "synthetic (seeded torch RNG on the device; dense fp16 N(0,0.02))"),
         "config": {"workload": "pack: " + ", ".join(f"{M}x{K}" for (M, K) in PACK_LAYERS),
                    "baseline_config": 2, "calls_per_step": len(PACK_LAYERS),
-                   "l2": f"inputs larger than L2: {sum(2 * M * K for (M, K) in PACK_LAYERS) / 1e6:.0f} MB of "
-                         "dense weights per step",
+                   "l2": f"inputs larger than L2: {dense_bytes / 1e6:.0f} MB of dense weights per step",
                    "parallelism": f"replicas x{world}"},
         "per_layer_us": per,
         "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None,
                      "peak_src": f"{peaks['src']} (hbm_gbs copy)",
-                     "note": "bytes = dense read 2MK + values MK + metadata MK/8 per layer"},
+                     "note": ("bytes = dense read MK + values MK/2 + metadata MK/8 per layer" if fp8 else
+                              "bytes = dense read 2MK + values MK + metadata MK/8 per layer")},
         "e2e": {"value": round(step_bytes * args.steps * world / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
-                "h2d_bytes_per_step": sum(2 * M * K for (M, K) in PACK_LAYERS),
-                "d2h_bytes_per_step": sum(M * K + M * K // 8 for (M, K) in PACK_LAYERS),
+                "h2d_bytes_per_step": dense_bytes,
+                "d2h_bytes_per_step": sum(v.numel() * v.element_size() + m.numel() * m.element_size()
+                                          for v, m in zip(vals, meta)),
                 "ms_per_step": round(e2e_ms / args.steps, 4),
-                "path": "per step: H2D of the dense weights (pinned), spmm24_pack_a_device per layer, "
+                "path": f"per step: H2D of the dense weights (pinned), "
+                        f"{'spmm24_pack_a_fp8_device' if fp8 else 'spmm24_pack_a_device'} per layer, "
                         "D2H of values + metadata"},
         "gpu_launches": len(PACK_LAYERS) * args.steps,
         "clocks": clocks,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        dn = [d.view(torch.int16).cpu().numpy().view(np.uint16).reshape(-1) for d in dense]
-        gbs, kind, sample = host_pack_baseline(dn, args.cpu_seconds)
+        if fp8:
+            dn = [d.cpu().numpy().reshape(-1) for d in dense]
+        else:
+            dn = [d.view(torch.int16).cpu().numpy().view(np.uint16).reshape(-1) for d in dense]
+        gbs, kind, sample = host_pack_baseline(dn, args.cpu_seconds, fp8=fp8)
         out["cpu_baseline"] = {"value": round(gbs, 4), "unit": "GB/s", "cores": 1, "kind": kind, "sample": sample}
     if world > 1:
         dist.barrier()

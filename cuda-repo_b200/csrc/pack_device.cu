@@ -216,6 +216,147 @@ __global__ void __launch_bounds__(kPackThreads) pack_a_kernel(const uint16_t* __
     if (bad && bad_blocks) atomicAdd(bad_blocks, bad);
 }
 
+// ------------------------------------------------------------------- fp8
+// The same steps on a group of four fp8 bytes held in one 32-bit word (byte
+// i = position i).  Magnitudes are b & 0x7f; NaN is every magnitude above
+// `top` (0x7e for E4M3, 0x7c for E5M2) and compares false with everything.
+
+// True when none of the four magnitudes is above `top`: adding 0x7f - top
+// to each byte carries into its bit 7 exactly when it is above.
+__device__ __forceinline__ bool no_nan8(uint32_t a, uint32_t top) {
+    return ((a + (0x7fu - top) * 0x01010101u) & 0x80808080u) == 0u;
+}
+
+// Kept positions (bit mask) of the sequential prune with NaN rules.
+__device__ __forceinline__ uint32_t prune_keep_sequential8(uint32_t a, uint32_t top) {
+    uint32_t m[4];
+    bool v[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        m[i] = (a >> (8 * i)) & 0xffu;
+        v[i] = m[i] <= top;
+    }
+    uint32_t k0 = 0, mk = m[0];
+#pragma unroll
+    for (int i = 1; i < 4; ++i) {
+        const bool c = v[0] && v[i] && m[i] > mk;  // a NaN at position 0 keeps position 0
+        k0 = c ? (uint32_t)i : k0;
+        mk = c ? m[i] : mk;
+    }
+    // k0 is 0 whenever position 0 is NaN; otherwise the comparisons above
+    // chained through the current best, which is never NaN.
+    uint32_t k1 = k0 == 0 ? 1u : 0u;
+    uint32_t mk1 = k0 == 0 ? m[1] : m[0];
+    const bool vk1 = k0 == 0 ? v[1] : v[0];
+#pragma unroll
+    for (int i = 1; i < 4; ++i) {
+        const bool c = (uint32_t)i != k0 && (uint32_t)i > k1 && vk1 && v[i] && m[i] > mk1;
+        k1 = c ? (uint32_t)i : k1;
+        mk1 = c ? m[i] : mk1;
+    }
+    return (1u << k0) | (1u << k1);
+}
+
+// Prune + compress of one group: the two kept bytes (lower position first)
+// in the low 16 bits of *pair, positions i0 | i1 << 2 in *idx; false when
+// the group keeps more than two values.  prune_top: 0 = no prune.
+__device__ __forceinline__ bool pack_group8(uint32_t w, uint32_t prune_top, uint32_t* pair, uint32_t* idx) {
+    const uint32_t a = w & 0x7f7f7f7fu;
+    if (prune_top) {
+        uint32_t keep;
+        if (no_nan8(a, prune_top)) {
+            const uint32_t a0 = ((a << 2) & 0x1fcu) | 3u, a1 = ((a >> 6) & 0x1fcu) | 2u;
+            const uint32_t a2 = ((a >> 14) & 0x1fcu) | 1u, a3 = (a >> 22) & 0x1fcu;
+            const uint32_t hi01 = max(a0, a1), lo01 = min(a0, a1), hi23 = max(a2, a3), lo23 = min(a2, a3);
+            const uint32_t top = max(hi01, hi23), second = max(min(hi01, hi23), max(lo01, lo23));
+            if (second >= 4u) {  // both kept magnitudes non-zero: they are the compress's output
+                const uint32_t k0 = 3u - (top & 3u), k1 = 3u - (second & 3u);
+                const uint32_t ia = min(k0, k1), ib = max(k0, k1);
+                *pair = __byte_perm(w, 0, ia | (ib << 4) | 0x4400u);  // bytes 2, 3 from the zero operand
+                *idx = ia | (ib << 2);
+                return true;
+            }
+            keep = (8u >> (top & 3u)) | (8u >> (second & 3u));
+        } else {
+            keep = prune_keep_sequential8(a, prune_top);
+        }
+        const uint32_t bytes = (keep & 1u) * 0xffu | (keep & 2u) * 0x7f80u | (keep & 4u) * 0x3fc000u |
+                               (keep & 8u) * 0x1fe00000u;
+        w &= bytes;
+    }
+    const uint32_t z = ((w & 0x7fu) == 0 ? 1u : 0u) | ((w & 0x7f00u) == 0 ? 2u : 0u) |
+                       ((w & 0x7f0000u) == 0 ? 4u : 0u) | ((w & 0x7f000000u) == 0 ? 8u : 0u);
+    const uint32_t id = (uint32_t)(0xECD4E894ECD4E444ull >> (4 * z)) & 0xfu;
+    *pair = __byte_perm(w, 0, (id & 3u) | ((id >> 2) << 4) | 0x4400u);
+    *idx = id;
+    return ((0x0117u >> z) & 1u) == 0;
+}
+
+// One CTA: kPackBands 16-row bands x 512 bytes of K (16 blocks of 32 K), the
+// 16-bit kernel's tile geometry in bytes.  Thread t handles row t % 16 of
+// block t / 16 in every band: 32 bytes in, 16 value bytes and 4 metadata
+// bytes out.
+__global__ void __launch_bounds__(kPackThreads) pack_a_fp8_kernel(const uint8_t* __restrict__ dense, int M, int K,
+                                                                  uint32_t prune_top, uint8_t* __restrict__ vals,
+                                                                  uint8_t* __restrict__ meta, int* bad_blocks) {
+    __shared__ __align__(16) uint8_t tile[kPackBands * 16 * kTilePitch * 2];
+    constexpr int kPitch = kTilePitch * 2;  // bytes per staged row (512 + 16)
+    const int band0 = blockIdx.y * kPackBands;
+    const int nb = min(kPackBands, M / 16 - band0);
+    const int nbc = K / 32;                     // 32-K blocks per row
+    const int q0 = blockIdx.x * kTileBlocks;
+    const int nq = min(kTileBlocks, nbc - q0);  // a multiple of 4 (K % 128 == 0)
+    const uint8_t* base = dense + (size_t)band0 * 16 * K + (size_t)q0 * 32;
+    uint4 v[kLoadsPerThread];
+    if (nq == kTileBlocks && nb == kPackBands) {  // full tile: 32 chunks of 16 bytes per row
+#pragma unroll
+        for (int i = 0; i < kLoadsPerThread; ++i) {
+            const int c = threadIdx.x + i * kPackThreads;
+            v[i] = *reinterpret_cast<const uint4*>(base + (size_t)(c >> 5) * K + (c & 31) * 16);
+        }
+#pragma unroll
+        for (int i = 0; i < kLoadsPerThread; ++i) {
+            const int c = threadIdx.x + i * kPackThreads;
+            *reinterpret_cast<uint4*>(tile + (c >> 5) * kPitch + (c & 31) * 16) = v[i];
+        }
+    } else {
+        const int chunks_per_row = nq * 2;
+        const int total = nb * 16 * chunks_per_row;
+        for (int c = threadIdx.x; c < total; c += kPackThreads) {
+            const int r = c / chunks_per_row, x = c % chunks_per_row;
+            *reinterpret_cast<uint4*>(tile + r * kPitch + x * 16) =
+                *reinterpret_cast<const uint4*>(base + (size_t)r * K + x * 16);
+        }
+    }
+    __syncthreads();
+    const int q = threadIdx.x / 16, r = threadIdx.x % 16;
+    if (q >= nq) return;
+    const int qg = q0 + q;
+    int bad = 0;
+    for (int b = 0; b < nb; ++b) {
+        const uint8_t* row = tile + (b * 16 + r) * kPitch + q * 32;
+        const uint4 lo = *reinterpret_cast<const uint4*>(row);
+        const uint4 hi = *reinterpret_cast<const uint4*>(row + 16);
+        const uint32_t w[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+        uint32_t pr[8], md = 0;
+        bool ok = true;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            uint32_t idx;
+            ok &= pack_group8(w[k], prune_top, &pr[k], &idx);
+            md |= idx << (4 * k);
+        }
+        bad += ok ? 0 : 1;
+        const int band = band0 + b;
+        const uint4 out = make_uint4(pr[0] | (pr[1] << 16), pr[2] | (pr[3] << 16), pr[4] | (pr[5] << 16),
+                                     pr[6] | (pr[7] << 16));
+        *reinterpret_cast<uint4*>(vals + (((size_t)band * nbc + qg) * 16 + r) * 16) = out;
+        // metadata row (band, 128-K group qg / 4, row r): this block's 32 bits
+        *reinterpret_cast<uint32_t*>(meta + (((size_t)band * (K / 128) + qg / 4) * 16 + r) * 16 + (qg % 4) * 4) = md;
+    }
+    if (bad && bad_blocks) atomicAdd(bad_blocks, bad);
+}
+
 // In-place magnitude prune, one group of four per thread.
 __global__ void __launch_bounds__(kPackThreads) prune_kernel(uint16_t* __restrict__ a, long long groups, uint32_t inf) {
     for (long long g = blockIdx.x * (long long)kPackThreads + threadIdx.x; g < groups;
@@ -280,6 +421,26 @@ extern "C" cudaError_t spmm24_pack_a_device(cudaStream_t stream, const void* den
     if (prune < SPMM24_PRUNE_NONE || prune > SPMM24_PRUNE_BF16) return record_invalid("unknown prune mode");
     pack_a_kernel<<<grid, kPackThreads, 0, stream>>>(static_cast<const uint16_t*>(dense_a), M, K, prune,
                                                      static_cast<uint16_t*>(values_out), meta_out, bad_blocks);
+    return cudaGetLastError();
+}
+
+extern "C" cudaError_t spmm24_pack_a_fp8_device(cudaStream_t stream, const void* dense_a, int M, int K, int prune,
+                                                void* values_out, void* meta_out, int* bad_blocks) {
+    using namespace spmm24;
+    clear_last_error();
+    if (!dense_a || !values_out || !meta_out) return record_invalid("null pointer");
+    if (M <= 0 || K <= 0 || M % 16 || K % 128) return record_invalid("M must be a multiple of 16 and K of 128");
+    if (misaligned16(dense_a) || misaligned16(values_out) || misaligned16(meta_out))
+        return record_invalid("dense A, values and metadata must be 16-byte aligned");
+    if (reinterpret_cast<uintptr_t>(bad_blocks) & 3u) return record_invalid("bad_blocks must be 4-byte aligned");
+    if (prune < 0 || prune > 2) return record_invalid("prune: 0 none, 1 E4M3, 2 E5M2");
+    const int nbc = K / 32;
+    dim3 grid((unsigned)((nbc + kTileBlocks - 1) / kTileBlocks), (unsigned)((M / 16 + kPackBands - 1) / kPackBands));
+    if (grid.y > 65535) return record_invalid("M too large");
+    const uint32_t top = prune == 1 ? 0x7eu : prune == 2 ? 0x7cu : 0u;
+    pack_a_fp8_kernel<<<grid, kPackThreads, 0, stream>>>(static_cast<const uint8_t*>(dense_a), M, K, top,
+                                                         static_cast<uint8_t*>(values_out),
+                                                         static_cast<uint8_t*>(meta_out), bad_blocks);
     return cudaGetLastError();
 }
 

@@ -116,6 +116,8 @@ _lib.spmm24_compress_a_fp8.restype = ctypes.c_int
 _lib.spmm24_launch_fp8.argtypes = [_vp, _vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                    ctypes.c_uint, ctypes.c_void_p]
 _lib.spmm24_launch_fp8.restype = ctypes.c_int
+_lib.spmm24_pack_a_fp8_device.argtypes = [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp, _vp, _vp]
+_lib.spmm24_pack_a_fp8_device.restype = ctypes.c_int
 _lib.spmm24_workspace_bytes.argtypes = [ctypes.c_int] * 4
 _lib.spmm24_workspace_bytes.restype = ctypes.c_size_t
 _lib.spmm24_select_config.argtypes = [ctypes.c_int] * 4 + [ctypes.POINTER(SpmmConfig)]
@@ -469,6 +471,24 @@ def compress_a_fp8(dense_a: np.ndarray, M: int, K: int):
     if n < 0:
         raise ValueError("compress_a_fp8: M % 16 and K % 128 must be 0")
     return vals, meta
+
+
+def pack_a_fp8_device(dense, M: int, K: int, prune: int = 0, values=None, meta=None, bad_blocks=None, stream=None):
+    """spmm24_pack_a_fp8_device on uint8 device tensors; returns (values, meta).
+    prune: 0 none, 1 E4M3, 2 E5M2."""
+    import torch
+
+    if values is None:
+        values = torch.empty(M * K // 2, dtype=torch.uint8, device=dense.device)
+    if meta is None:
+        meta = torch.empty(M * K // 8, dtype=torch.uint8, device=dense.device)
+    if stream is None:
+        stream = torch.cuda.current_stream(dense.device)
+    rc = _lib.spmm24_pack_a_fp8_device(_stream_handle(stream), _ptr(dense), M, K, int(prune), _ptr(values), _ptr(meta),
+                                       _ptr(bad_blocks))
+    if rc != CUDA_SUCCESS:
+        raise SpmmError(rc, "spmm24_pack_a_fp8_device")
+    return values, meta
 
 
 # ------------------------------------------------- packed-weight files

@@ -279,6 +279,15 @@ int spmm24_prune_2of4_fp8(uint8_t* dense_a, int M, int K, int fmt);
  * Returns M*K/2, -1 for bad arguments, -2 when a group of four holds more
  * than two non-zeros. */
 int spmm24_compress_a_fp8(const uint8_t* dense_a, int M, int K, uint8_t* values_out, uint8_t* meta_out);
+/* spmm24_compress_a_fp8 (after an optional spmm24_prune_2of4_fp8: prune 0 =
+ * none, 1 = E4M3, 2 = E5M2) on a dense M x K fp8 matrix in device memory,
+ * bit-exact with the host functions.  dense, values and metadata 16-byte
+ * aligned.  If bad_blocks (device int, optional; the caller zeroes it) is
+ * given, the kernel adds 1 for every row of a 16 x 32 block holding a group
+ * of four with more than two non-zeros (those outputs are unspecified).
+ * Asynchronous on `stream`. */
+cudaError_t spmm24_pack_a_fp8_device(cudaStream_t stream, const void* dense_a, int M, int K, int prune,
+                                     void* values_out, void* meta_out, int* bad_blocks);
 /* C = A_sparse * B^T-layout B, with the same split_k, flags
  * (SPMM24_STATIC_WEIGHTS, SPMM24_NO_PDL, SPMM24_BF16 for the output type,
  * SPMM24_FP8_A_E5M2, SPMM24_FP8_B_E5M2) and epilogue (alpha doubles as the

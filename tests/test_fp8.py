@@ -130,8 +130,21 @@ def test_launch_fp8_argument_checks():
     assert _launch(epi=ctypes.addressof(epi)) == INVALID
 
 
+def test_fp8_device_packer_argument_checks():
+    import spmm24
+
+    INVALID = spmm24.CUDA_ERROR_INVALID_VALUE
+    f = spmm24._lib.spmm24_pack_a_fp8_device
+    assert f(None, None, 64, 256, 1, 0x2000, 0x3000, None) == INVALID
+    assert f(None, 0x1000, 64, 192, 1, 0x2000, 0x3000, None) == INVALID   # K % 128
+    assert f(None, 0x1000, 60, 256, 1, 0x2000, 0x3000, None) == INVALID   # M % 16
+    assert f(None, 0x1008, 64, 256, 1, 0x2000, 0x3000, None) == INVALID   # alignment
+    assert f(None, 0x1000, 64, 256, 1, 0x2000, 0x3004, None) == INVALID
+    assert f(None, 0x1000, 64, 256, 3, 0x2000, 0x3000, None) == INVALID   # prune mode
+
+
 def test_fp8_symbols_exported():
     import spmm24
 
-    for name in ("spmm24_launch_fp8", "spmm24_compress_a_fp8", "spmm24_prune_2of4_fp8"):
+    for name in ("spmm24_launch_fp8", "spmm24_compress_a_fp8", "spmm24_prune_2of4_fp8", "spmm24_pack_a_fp8_device"):
         assert hasattr(spmm24._lib, name)

@@ -227,3 +227,78 @@ def test_fp8_cuda_graph(cuda_device):
     g.replay()
     torch.cuda.synchronize(cuda_device)
     assert torch.equal(c1, c2)
+
+
+# ---------------------------------------------------------- device packer
+def _fp8_specials(M, K, fmt, seed):
+    rng = np.random.default_rng(seed)
+    a = O.f32_to_fp8(rng.standard_normal(M * K).astype(np.float32), fmt)
+    codes = np.array([0x00, 0x80, 0x01, 0x81, 0x7E, 0xFE, 0x7F, 0xFF, 0x7C, 0xFC, 0x7D], dtype=np.uint8)
+    pick = rng.random(M * K) < 0.15
+    a[pick] = rng.choice(codes, int(pick.sum()))
+    # magnitude ties inside groups
+    a[::53] = a[1::53][: a[::53].size]
+    return a
+
+
+@pytest.mark.parametrize("fmt", [0, 1], ids=["e4m3", "e5m2"])
+@pytest.mark.parametrize("shape", [(96, 1280), (256, 4096), (16, 128)], ids=lambda s: "x".join(map(str, s)))
+def test_fp8_device_packer_matches_host(cuda_device, fmt, shape):
+    """spmm24_pack_a_fp8_device (prune + compress in one pass) equals the host
+    prune + compress bit for bit, including signed zeros, NaN / inf codes and
+    magnitude ties; without the prune it equals the host compress of a
+    pruned matrix."""
+    import torch
+
+    import spmm24
+
+    M, K = shape
+    a = _fp8_specials(M, K, fmt, 7 + fmt)
+    pruned = spmm24.prune_2of4_fp8(a, M, K, fmt)
+    v_ref, m_ref = spmm24.compress_a_fp8(pruned, M, K)
+    bad = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    v, m = spmm24.pack_a_fp8_device(_u8dev(a, cuda_device), M, K, prune=1 + fmt, bad_blocks=bad)
+    torch.cuda.synchronize(cuda_device)
+    assert int(bad.item()) == 0
+    assert np.array_equal(v.cpu().numpy(), v_ref) and np.array_equal(m.cpu().numpy(), m_ref)
+    v2, m2 = spmm24.pack_a_fp8_device(_u8dev(pruned, cuda_device), M, K, prune=0, bad_blocks=bad)
+    torch.cuda.synchronize(cuda_device)
+    assert int(bad.item()) == 0
+    assert np.array_equal(v2.cpu().numpy(), v_ref) and np.array_equal(m2.cpu().numpy(), m_ref)
+
+
+def test_fp8_device_packer_counts_dense_rows(cuda_device):
+    import torch
+
+    import spmm24
+
+    M, K = 64, 512
+    a = O.prune_magnitude_2of4_fp8(_fp8_specials(M, K, 0, 3), M, K, 0)
+    a = a.reshape(M, K)
+    a[5, 40:44] = 0x38        # row 5, block 1: a dense group
+    a[33, 300:304] = 0x40     # row 33, block 9
+    a[33, 301] = 0x00         # three non-zeros
+    bad = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    spmm24.pack_a_fp8_device(_u8dev(a.reshape(-1), cuda_device), M, K, prune=0, bad_blocks=bad)
+    torch.cuda.synchronize(cuda_device)
+    assert int(bad.item()) == 2
+
+
+def test_fp8_device_packed_operands_drive_the_spmm(cuda_device):
+    """Weights packed on the device give the same C as host-packed ones."""
+    import torch
+
+    import spmm24
+
+    M, N, K = 1024, 16, 2048
+    rng = np.random.default_rng(17)
+    a = O.f32_to_fp8(rng.standard_normal(M * K).astype(np.float32), 0)
+    b = _u8dev(O.f32_to_fp8(rng.standard_normal(N * K).astype(np.float32), 0), cuda_device)
+    v_h, m_h = spmm24.compress_a_fp8(spmm24.prune_2of4_fp8(a, M, K, 0), M, K)
+    v_d, m_d = spmm24.pack_a_fp8_device(_u8dev(a, cuda_device), M, K, prune=1)
+    c1 = torch.empty(M * N, dtype=torch.float16, device=cuda_device)
+    c2 = torch.empty_like(c1)
+    assert spmm24.launch_fp8(None, _u8dev(v_h, cuda_device), b, _u8dev(m_h, cuda_device), c1, M, N, K) == 0
+    assert spmm24.launch_fp8(None, v_d, b, m_d, c2, M, N, K) == 0
+    torch.cuda.synchronize(cuda_device)
+    assert torch.equal(c1, c2)
