@@ -157,24 +157,26 @@ __global__ void __launch_bounds__(kPackThreads) pack_a_kernel(const uint16_t* __
     const int nbc = K / 16;
     const int q0 = blockIdx.x * kTileBlocks;
     const int nq = min(kTileBlocks, nbc - q0);  // a multiple of 4 (K % 64 == 0)
-    const int chunks_per_row = nq * 2;          // 16-byte chunks
-    const int total = nb * 16 * chunks_per_row;
     const uint16_t* base = dense + (size_t)band0 * 16 * K + (size_t)q0 * 16;
-    uint4 v[kLoadsPerThread];
+    if (nq == kTileBlocks && nb == kPackBands) {  // full tile: 32 chunks of 16 bytes per row
+        uint4 v[kLoadsPerThread];
 #pragma unroll
-    for (int i = 0; i < kLoadsPerThread; ++i) {
-        const int c = threadIdx.x + i * kPackThreads;
-        if (c < total) {
-            const int r = c / chunks_per_row, x = c % chunks_per_row;
-            v[i] = *reinterpret_cast<const uint4*>(base + (size_t)r * K + x * 8);
+        for (int i = 0; i < kLoadsPerThread; ++i) {
+            const int c = threadIdx.x + i * kPackThreads;
+            v[i] = *reinterpret_cast<const uint4*>(base + (size_t)(c >> 5) * K + (c & 31) * 8);
         }
-    }
 #pragma unroll
-    for (int i = 0; i < kLoadsPerThread; ++i) {
-        const int c = threadIdx.x + i * kPackThreads;
-        if (c < total) {
+        for (int i = 0; i < kLoadsPerThread; ++i) {
+            const int c = threadIdx.x + i * kPackThreads;
+            *reinterpret_cast<uint4*>(tile + (c >> 5) * kTilePitch + (c & 31) * 8) = v[i];
+        }
+    } else {  // ragged tile (last K tile or last bands)
+        const int chunks_per_row = nq * 2;
+        const int total = nb * 16 * chunks_per_row;
+        for (int c = threadIdx.x; c < total; c += kPackThreads) {
             const int r = c / chunks_per_row, x = c % chunks_per_row;
-            *reinterpret_cast<uint4*>(tile + r * kTilePitch + x * 8) = v[i];
+            *reinterpret_cast<uint4*>(tile + r * kTilePitch + x * 8) =
+                *reinterpret_cast<const uint4*>(base + (size_t)r * K + x * 8);
         }
     }
     __syncthreads();
