@@ -4,14 +4,15 @@
 // Layout (little-endian, 64-byte header, then the payload):
 //   0  char[8]  magic "SPMM24W" + NUL
 //   8  u32      version (1)
-//  12  u32      dtype (0 fp16, 1 bf16)
+//  12  u32      dtype (0 fp16, 1 bf16, 2 fp8 E4M3, 3 fp8 E5M2)
 //  16  u32      M
 //  20  u32      K
-//  24  u64      values_bytes  (M*K/2 elements * 2 bytes = M*K)
-//  32  u64      meta_bytes    (M*K/16 u16 * 2 bytes = M*K/8)
+//  24  u64      values_bytes  (16-bit: M*K/2 elements * 2 bytes = M*K; fp8: M*K/2)
+//  32  u64      meta_bytes    (M*K/8 for every dtype)
 //  40  u64      checksum      (FNV-1a 64 over values then metadata)
 //  48  u8[16]   reserved (zero)
-//  64  values (compressed, 16x8 blocks, band-major), then metadata (reordered)
+//  64  values (compressed, 16x8 blocks, band-major), then metadata (reordered;
+//      fp8: the fp8 SpMM's value and metadata formats)
 // The reference has no file format (its packer runs per process,
 // test/utils.h:91-185).
 #include <cstdint>
@@ -56,8 +57,14 @@ uint64_t get64(const uint8_t* p) {
     return v;
 }
 
-bool shape_ok(int dtype, long long M, long long K) {
-    return (dtype == 0 || dtype == 1) && M > 0 && K > 0 && M % 16 == 0 && K % 64 == 0;
+bool is_fp8(long long dtype) { return dtype == 2 || dtype == 3; }
+
+bool shape_ok(long long dtype, long long M, long long K) {
+    return dtype >= 0 && dtype <= 3 && M > 0 && K > 0 && M % 16 == 0 && K % (is_fp8(dtype) ? 128 : 64) == 0;
+}
+
+uint64_t values_bytes(long long dtype, long long M, long long K) {
+    return is_fp8(dtype) ? (uint64_t)M * K / 2 : (uint64_t)M * K;
 }
 
 int read_header(FILE* f, spmm24_packed_header* h) {
@@ -72,17 +79,16 @@ int read_header(FILE* f, spmm24_packed_header* h) {
     h->meta_bytes = get64(b + 32);
     h->checksum = get64(b + 40);
     if (h->version != kVersion || !shape_ok((int)h->dtype, h->M, h->K)) return SPMM24_PACKED_EFORMAT;
-    if (h->values_bytes != (uint64_t)h->M * h->K || h->meta_bytes != (uint64_t)h->M * h->K / 8)
+    if (h->values_bytes != values_bytes(h->dtype, h->M, h->K) || h->meta_bytes != (uint64_t)h->M * h->K / 8)
         return SPMM24_PACKED_EFORMAT;
     return 0;
 }
 
 }  // namespace
 
-extern "C" int spmm24_save_packed(const char* path, int dtype, int M, int K, const void* values,
-                                  const uint16_t* meta) {
+extern "C" int spmm24_save_packed(const char* path, int dtype, int M, int K, const void* values, const void* meta) {
     if (!path || !values || !meta || !shape_ok(dtype, M, K)) return SPMM24_PACKED_EARG;
-    const uint64_t vb = (uint64_t)M * K, mb = (uint64_t)M * K / 8;
+    const uint64_t vb = values_bytes(dtype, M, K), mb = (uint64_t)M * K / 8;
     uint64_t sum = fnv1a64(kFnvBasis, values, vb);
     sum = fnv1a64(sum, meta, mb);
     uint8_t b[kHeaderBytes] = {};
@@ -111,7 +117,7 @@ extern "C" int spmm24_load_packed_header(const char* path, spmm24_packed_header*
     return rc;
 }
 
-extern "C" int spmm24_load_packed(const char* path, void* values, uint16_t* meta) {
+extern "C" int spmm24_load_packed(const char* path, void* values, void* meta) {
     if (!path || !values || !meta) return SPMM24_PACKED_EARG;
     FILE* f = std::fopen(path, "rb");
     if (!f) return SPMM24_PACKED_EIO;

@@ -513,12 +513,41 @@ def load_packed(path: str):
     rc = _lib.spmm24_load_packed_header(os.fsencode(path), ctypes.byref(h))
     if rc != 0:
         raise OSError(f"spmm24_load_packed_header: {PACKED_ERRORS.get(rc, rc)}")
+    if h.dtype not in (0, 1):
+        raise ValueError("an fp8 packed-weight file: use load_packed_fp8")
     v = np.empty(h.values_bytes // 2, dtype=np.uint16)
     m = np.empty(h.meta_bytes // 2, dtype=np.uint16)
     rc = _lib.spmm24_load_packed(os.fsencode(path), v.ctypes.data, m.ctypes.data)
     if rc != 0:
         raise OSError(f"spmm24_load_packed: {PACKED_ERRORS.get(rc, rc)}")
     return v, m, int(h.M), int(h.K), bool(h.dtype == 1)
+
+
+def save_packed_fp8(path: str, values: np.ndarray, meta: np.ndarray, M: int, K: int, fmt: int = FP8_E4M3) -> None:
+    """spmm24_save_packed with dtype 2 (E4M3) or 3 (E5M2): the fp8 SpMM's values and metadata."""
+    v = _u8(values).reshape(-1)
+    m = _u8(meta).reshape(-1)
+    if v.size != M * K // 2 or m.size != M * K // 8:
+        raise ValueError("values / metadata sizes do not match M x K")
+    rc = _lib.spmm24_save_packed(os.fsencode(path), 2 + int(fmt), M, K, v.ctypes.data, m.ctypes.data)
+    if rc != 0:
+        raise OSError(f"spmm24_save_packed: {PACKED_ERRORS.get(rc, rc)}")
+
+
+def load_packed_fp8(path: str):
+    """Returns (values, metadata, M, K, fmt) of an fp8 packed-weight file (uint8 host arrays)."""
+    h = PackedHeader()
+    rc = _lib.spmm24_load_packed_header(os.fsencode(path), ctypes.byref(h))
+    if rc != 0:
+        raise OSError(f"spmm24_load_packed_header: {PACKED_ERRORS.get(rc, rc)}")
+    if h.dtype not in (2, 3):
+        raise ValueError("a 16-bit packed-weight file: use load_packed")
+    v = np.empty(h.values_bytes, dtype=np.uint8)
+    m = np.empty(h.meta_bytes, dtype=np.uint8)
+    rc = _lib.spmm24_load_packed(os.fsencode(path), v.ctypes.data, m.ctypes.data)
+    if rc != 0:
+        raise OSError(f"spmm24_load_packed: {PACKED_ERRORS.get(rc, rc)}")
+    return v, m, int(h.M), int(h.K), int(h.dtype) - 2
 
 
 # Reference-named wrappers (Block sizes fixed as in the reference harness).

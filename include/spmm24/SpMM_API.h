@@ -297,10 +297,13 @@ cudaError_t spmm24_launch_fp8(cudaStream_t stream, const void* values, const voi
                               int M, int N, int K, int split_k, unsigned flags, const spmm24_epilogue* epilogue);
 
 /* Packed-weight files (no counterpart in the reference): a 64-byte header
- * (magic "SPMM24W", version 1, dtype 0 = fp16 / 1 = bf16, M, K, payload
- * sizes, FNV-1a-64 checksum of the payload), then the compressed values and
- * the reordered metadata exactly as spmm24_launch consumes them.  Host
- * buffers.  Return 0 or a negative SPMM24_PACKED_E* code. */
+ * (magic "SPMM24W", version 1, dtype 0 = fp16 / 1 = bf16 / 2 = fp8 E4M3 /
+ * 3 = fp8 E5M2, M, K, payload sizes, FNV-1a-64 checksum of the payload),
+ * then the compressed values and the metadata exactly as spmm24_launch
+ * (16-bit: M*K bytes of values, reordered metadata, K % 64 == 0) or
+ * spmm24_launch_fp8 (M*K/2 bytes of values, fp8 metadata, K % 128 == 0)
+ * consumes them; M*K/8 bytes of metadata either way.  Host buffers.
+ * Return 0 or a negative SPMM24_PACKED_E* code. */
 enum {
     SPMM24_PACKED_EARG = -1,     /* bad argument or shape (M % 16, K % 64) */
     SPMM24_PACKED_EIO = -2,      /* open / read / write failed, or short file */
@@ -311,10 +314,10 @@ typedef struct spmm24_packed_header {
     uint32_t version, dtype, M, K;
     uint64_t values_bytes, meta_bytes, checksum;
 } spmm24_packed_header;
-int spmm24_save_packed(const char* path, int dtype, int M, int K, const void* values, const uint16_t* meta);
+int spmm24_save_packed(const char* path, int dtype, int M, int K, const void* values, const void* meta);
 int spmm24_load_packed_header(const char* path, spmm24_packed_header* out);
 /* values: values_bytes, meta: meta_bytes (from the header). */
-int spmm24_load_packed(const char* path, void* values, uint16_t* meta);
+int spmm24_load_packed(const char* path, void* values, void* meta);
 
 /* Workspace the caller must pass as split_reduction: always 0 bytes (any
  * workspace is owned by the library, see spmm24_launch).

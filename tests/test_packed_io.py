@@ -56,5 +56,29 @@ def test_corruption_is_detected(tmp_path):
 
 def test_bad_arguments():
     assert spmm24._lib.spmm24_save_packed(b"/dev/null", 0, 250, 64, 1, 1) == -1   # M % 16
-    assert spmm24._lib.spmm24_save_packed(b"/dev/null", 2, 256, 64, 1, 1) == -1   # dtype
+    assert spmm24._lib.spmm24_save_packed(b"/dev/null", 4, 256, 128, 1, 1) == -1  # dtype
+    assert spmm24._lib.spmm24_save_packed(b"/dev/null", 2, 256, 64, 1, 1) == -1   # fp8 needs K % 128
     assert spmm24._lib.spmm24_save_packed(b"/dev/null", 0, 256, 64, None, 1) == -1
+
+
+@pytest.mark.parametrize("fmt", [0, 1], ids=["e4m3", "e5m2"])
+def test_fp8_round_trip(tmp_path, fmt):
+    """dtype 2 / 3: the fp8 SpMM's values (M*K/2 bytes) and metadata (M*K/8)."""
+    M, K = 128, 512
+    rng = np.random.default_rng(fmt)
+    a = rng.integers(0, 256, M * K, dtype=np.uint8)
+    a[(a & 0x7F) == 0x7F] = 0x38
+    v, m = spmm24.compress_a_fp8(spmm24.prune_2of4_fp8(a, M, K, fmt), M, K)
+    p = tmp_path / "w8.spmm24"
+    spmm24.save_packed_fp8(str(p), v, m, M, K, fmt)
+    assert p.stat().st_size == 64 + M * K // 2 + M * K // 8
+    v2, m2, M2, K2, f2 = spmm24.load_packed_fp8(str(p))
+    assert (M2, K2, f2) == (M, K, fmt)
+    assert np.array_equal(v, v2) and np.array_equal(m, m2)
+    with pytest.raises(ValueError):
+        spmm24.load_packed(str(p))
+    raw = bytearray(p.read_bytes())
+    raw[100] ^= 1
+    p.write_bytes(bytes(raw))
+    with pytest.raises(OSError, match="checksum"):
+        spmm24.load_packed_fp8(str(p))
