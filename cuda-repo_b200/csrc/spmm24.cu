@@ -294,7 +294,7 @@ cudaError_t get_workspace(int dev, cudaStream_t stream, size_t counters, size_t 
     return cudaSuccess;
 }
 
-std::atomic<uint64_t> g_attr_done[64];  // per kernel variant: one bit per device
+std::atomic<uint64_t> g_attr_done[96];  // per kernel variant: one bit per device
 
 // The plain SpMM: fp16, row-major C, no epilogue work.
 bool epilogue_plain_fp16(const Epilogue& e) {
@@ -365,15 +365,20 @@ cudaError_t launch_cluster(const Plan& pl, cudaStream_t stream, int dev, bool pd
                          V::C_::SMEM_ALLOC, stream, (unsigned)pl.split, pdl, ta, tb, te, kp);
 }
 
-// The fp8 instantiation (general epilogue always); attribute slots kFp8Slot + idx.
+// The fp8 instantiations: the general epilogue (attribute slots kFp8Slot +
+// idx), and alpha-only fp16 row-major output (kFp8PlainSlot + idx).
 constexpr int kFp8Slot = 48;
+constexpr int kFp8PlainSlot = 64;
 
 template <class V>
 cudaError_t launch_cluster_fp8(const Plan& pl, cudaStream_t stream, int dev, bool pdl, const CUtensorMap& ta,
                                const CUtensorMap& tb, const CUtensorMap& te, const ClusterParams& kp, int idx) {
     using C8 = ClusterCfg<V::kTileN, V::kStages, true>;
-    auto kern = spmm24_cluster_kernel<V::kTileN, V::kStages, true, true>;
-    cudaError_t e = prepare(kern, C8::SMEM_ALLOC, dev, kFp8Slot + idx);
+    const Epilogue& ep = kp.epi;
+    const bool general = ep.bias || ep.residual || ep.act != kActNone || ep.packed || ep.bf16 || ep.gather_n;
+    auto kern = general ? spmm24_cluster_kernel<V::kTileN, V::kStages, true, true>
+                        : spmm24_cluster_kernel<V::kTileN, V::kStages, false, true>;
+    cudaError_t e = prepare(kern, C8::SMEM_ALLOC, dev, (general ? kFp8Slot : kFp8PlainSlot) + idx);
     if (e != cudaSuccess) return e;
     return launch_kernel(kern, dim3((unsigned)pl.split, (unsigned)pl.n_tiles, (unsigned)pl.m_tiles), C8::SMEM_ALLOC,
                          stream, (unsigned)pl.split, pdl, ta, tb, te, kp);

@@ -123,12 +123,13 @@ struct ClusterCfg : Cfg<N_TILE, STAGES, 1, FP8> {
 // output).  The plain fp16 row-major SpMM is a separate instantiation
 // without it: the epilogue runs on the critical path at the end of every
 // tile, and its extra code measurably slows the plain kernel.
-// FP8: the fp8 operand formats and kind::f8f6f4 MMAs (always with EPI).
+// FP8: the fp8 operand formats and kind::f8f6f4 MMAs; without EPI the
+// output is alpha * acc rounded to fp16, row-major (the dequantisation
+// scale alone).
 template <int N_TILE, int STAGES, bool EPI, bool FP8 = false>
 __global__ void __launch_bounds__(kThreads, ClusterCfg<N_TILE, STAGES, FP8>::CTAS_PER_SM)
 spmm24_cluster_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const __grid_constant__ CUtensorMap tmE, const ClusterParams p) {
-    static_assert(EPI || !FP8, "the fp8 kernel always runs the general epilogue");
     using C_ = ClusterCfg<N_TILE, STAGES, FP8>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -331,10 +332,15 @@ spmm24_cluster_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_cons
             const int gm = m0 + my_start + lr;
             const int gn = n0 + ch * 8;
             if (gm >= p.M || gn >= p.N) continue;
-            if constexpr (EPI)
+            if constexpr (EPI) {
                 epilogue_store8(p.C, acc, p.epi, gm, gn, p.M, p.N, vec_ok, epilogue_is_plain(p.epi));
-            else
+            } else {
+                if constexpr (FP8) {
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) acc[e] *= p.epi.alpha;
+                }
                 store_h8(reinterpret_cast<__half*>(p.C) + (size_t)gm * p.N + gn, acc, vec_ok, p.N - gn);
+            }
         }
     }
 

@@ -302,3 +302,29 @@ def test_fp8_device_packed_operands_drive_the_spmm(cuda_device):
     assert spmm24.launch_fp8(None, v_d, b, m_d, c2, M, N, K) == 0
     torch.cuda.synchronize(cuda_device)
     assert torch.equal(c1, c2)
+
+
+def _fp8_cases(n, seed):
+    rng = np.random.default_rng(seed)
+    out = []
+    for _ in range(n):
+        M = int(rng.integers(1, 40)) * 16
+        K = int(rng.choice([128, 256, 384, 640, 1024, 2048, 4096]))
+        N = int(rng.choice([1, 5, 8, 16, 24, 32, 48, 64, 100, 128, 136, 256, 300]))
+        split = int(rng.choice([0, 0, 0, 1, 2, 3, 6]))
+        flag = lambda: bool(rng.random() < 0.3)  # noqa: E731
+        out.append((M, N, K, split, int(rng.integers(0, 2)), int(rng.integers(0, 2)), flag(),
+                    int(rng.integers(1, 4)) if flag() else 0, flag(), flag(), flag(),
+                    float(rng.choice([1.0, 0.02, -0.5]))))
+    return out
+
+
+@pytest.mark.parametrize("case", _fp8_cases(32, 77), ids=lambda c: "M{}N{}K{}s{}a{}b{}o{}x{}r{}p{}bias{}al{}".format(
+    c[0], c[1], c[2], c[3], c[4], c[5], "bf" if c[6] else "h", c[7], int(c[8]), int(c[9]), int(c[10]), c[11]))
+def test_fp8_random_case(cuda_device, case):
+    """Seeded sweep: shapes (both kernels), K splits, operand formats, output
+    type, activation, residual, packed output, bias, alpha (the alpha-only
+    fp16 instantiation whenever nothing else is set)."""
+    M, N, K, split, fa, fb, bf16, act, res, packed, bias, alpha = case
+    _run(cuda_device, M, N, K, fmt_a=fa, fmt_b=fb, split=split, bf16=bf16, act=act, residual=res, packed=packed,
+         bias=bias, alpha=alpha, seed=M * 5 + N * 3 + K)
