@@ -19,9 +19,6 @@
 
 #include <cstdint>
 
-#include <atomic>
-
-#include "ptx_sm100.cuh"
 #include "spmm24/SpMM_API.h"
 #include "spmm24_host.h"
 
@@ -143,124 +140,84 @@ __device__ __forceinline__ bool prune_compress_group(uint32_t x, uint32_t y, uin
     return compress_group(x, y, halves, idx);
 }
 
-// Tiles of kPackBands 16-row bands x 512 bytes of K (16 blocks of 16 K for
-// 16-bit elements, of 32 K for fp8).  A persistent grid walks the tiles
-// (K fastest); each CTA double-buffers them in shared memory: the next
-// tile's cp.async loads (16 bytes each, no registers) are in flight while
-// the current tile is processed.  Thread t handles row t % 16 of block
-// t / 16 in every band of a tile.
+// One CTA: kPackBands 16-row bands x 16 blocks of 16 K.  All of the tile's
+// loads are issued before any is used (8 x 16 bytes per thread), so each SM
+// keeps about 200 KB of reads in flight.  Thread t then handles row t % 16
+// of block t / 16 in every band; per band the value writes (block-major,
+// then row) are one contiguous 4 KB run.
 constexpr int kPackBands = 4;
-constexpr int kPitchBytes = kTilePitch * 2;                          // 512 + 16 bytes per staged row
-constexpr int kTileBytes = kPackBands * 16 * kPitchBytes;            // one buffer
-constexpr int kPackSmem = 2 * kTileBytes;                            // double buffer (67.5 KB)
-constexpr int kLoadsPerThread = kPackBands * 16 * 32 / kPackThreads;  // 16-byte chunks per thread (full tile)
-
-struct PackTile {
-    int band0, nb;  // first band, bands in the tile
-    int q0, nq;     // first block, blocks in the tile (a multiple of 4)
-};
-
-__device__ __forceinline__ PackTile pack_tile(int t, int tiles_x, int nbc, int bands) {
-    PackTile pt;
-    pt.band0 = (t / tiles_x) * kPackBands;
-    pt.nb = min(kPackBands, bands - pt.band0);
-    pt.q0 = (t % tiles_x) * kTileBlocks;
-    pt.nq = min(kTileBlocks, nbc - pt.q0);
-    return pt;
-}
-
-// Issues the cp.async loads of one tile (row_bytes: bytes per dense row) and
-// commits them as one group.
-__device__ __forceinline__ void stage_tile(uint8_t* buf, const uint8_t* dense, size_t row_bytes, const PackTile& pt) {
-    const uint8_t* base = dense + (size_t)pt.band0 * 16 * row_bytes + (size_t)pt.q0 * 32;
-    if (pt.nb == kPackBands && pt.nq == kTileBlocks) {  // full tile: 32 chunks of 16 bytes per row
-#pragma unroll
-        for (int i = 0; i < kLoadsPerThread; ++i) {
-            const int c = threadIdx.x + i * kPackThreads;
-            ptx::cp_async16(buf + (c >> 5) * kPitchBytes + (c & 31) * 16, base + (size_t)(c >> 5) * row_bytes + (c & 31) * 16);
-        }
-    } else {
-        const int chunks = pt.nq * 2, total = pt.nb * 16 * chunks;
-        for (int c = threadIdx.x; c < total; c += kPackThreads) {
-            const int r = c / chunks, x = c % chunks;
-            ptx::cp_async16(buf + r * kPitchBytes + x * 16, base + (size_t)r * row_bytes + x * 16);
-        }
-    }
-    ptx::cp_async_commit();
-}
-
-// The persistent tile loop shared by the 16-bit and the fp8 packer:
-// process(buf, tile) handles one staged tile and returns its bad rows.
-template <class Process>
-__device__ __forceinline__ void pack_tiles(const uint8_t* dense, size_t row_bytes, int bands, int nbc,
-                                           int* bad_blocks, Process process) {
-    extern __shared__ __align__(16) uint8_t pack_smem[];
-    const int tiles_x = (nbc + kTileBlocks - 1) / kTileBlocks;
-    const int n_tiles = tiles_x * ((bands + kPackBands - 1) / kPackBands);
-    int t = blockIdx.x;
-    if (t >= n_tiles) return;
-    stage_tile(pack_smem, dense, row_bytes, pack_tile(t, tiles_x, nbc, bands));
-    int bad = 0;
-    for (int i = 0; t < n_tiles; ++i, t += gridDim.x) {
-        const int tn = t + gridDim.x;
-        if (tn < n_tiles) {
-            stage_tile(pack_smem + ((i + 1) & 1) * kTileBytes, dense, row_bytes, pack_tile(tn, tiles_x, nbc, bands));
-            ptx::cp_async_wait_group1();  // this tile's group has landed, the next one may be in flight
-        } else {
-            ptx::cp_async_wait_all();
-        }
-        __syncthreads();
-        bad += process(pack_smem + (i & 1) * kTileBytes, pack_tile(t, tiles_x, nbc, bands));
-        __syncthreads();  // the buffer is free for the tile after next
-    }
-    if (bad && bad_blocks) atomicAdd(bad_blocks, bad);
-}
+constexpr int kLoadsPerThread = kPackBands * 16 * (kTileCols / 8) / kPackThreads;
 
 __global__ void __launch_bounds__(kPackThreads) pack_a_kernel(const uint16_t* __restrict__ dense, int M, int K,
                                                               int prune, uint16_t* __restrict__ vals,
                                                               uint16_t* __restrict__ meta, int* bad_blocks) {
+    __shared__ __align__(16) uint16_t tile[kPackBands * 16 * kTilePitch];
+    const int band0 = blockIdx.y * kPackBands;
+    const int nb = min(kPackBands, M / 16 - band0);
     const int nbc = K / 16;
-    const uint32_t inf = prune == 2 ? 0x7f80u : 0x7c00u;
-    const int q = threadIdx.x / 16, r = threadIdx.x % 16;
-    pack_tiles(reinterpret_cast<const uint8_t*>(dense), (size_t)K * 2, M / 16, nbc, bad_blocks,
-               [&](const uint8_t* buf, const PackTile& pt) -> int {
-        if (q >= pt.nq) return 0;
-        const int qg = pt.q0 + q;
-        int bad = 0;
-        for (int b = 0; b < pt.nb; ++b) {
-            const uint8_t* row = buf + (b * 16 + r) * kPitchBytes + q * 32;
-            const uint4 lo = *reinterpret_cast<const uint4*>(row);
-            const uint4 hi = *reinterpret_cast<const uint4*>(row + 16);
-            uint32_t wx[4] = {lo.x, lo.z, hi.x, hi.z}, wy[4] = {lo.y, lo.w, hi.y, hi.w};
-            uint32_t w[4], md = 0;
-            bool ok = true;
-            if (prune) {
+    const int q0 = blockIdx.x * kTileBlocks;
+    const int nq = min(kTileBlocks, nbc - q0);  // a multiple of 4 (K % 64 == 0)
+    const uint16_t* base = dense + (size_t)band0 * 16 * K + (size_t)q0 * 16;
+    if (nq == kTileBlocks && nb == kPackBands) {  // full tile: 32 chunks of 16 bytes per row
+        uint4 v[kLoadsPerThread];
 #pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    uint32_t idx;
-                    ok &= prune_compress_group(wx[k], wy[k], inf, &w[k], &idx);
-                    md |= idx << (4 * k);
-                }
-            } else {
-#pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    uint32_t idx;
-                    ok &= compress_group(wx[k], wy[k], &w[k], &idx);
-                    md |= idx << (4 * k);
-                }
-            }
-            bad += ok ? 0 : 1;
-            const int band = pt.band0 + b;
-            *reinterpret_cast<uint4*>(vals + (((size_t)band * nbc + qg) * 16 + r) * 8) =
-                make_uint4(w[0], w[1], w[2], w[3]);
-            // Reordered metadata (test/utils.h:179-180): per band and 64-K group,
-            // word i*8 + j holds (row (j%2)*8 + i, block j/2 of the group).
-            const size_t grp = (size_t)band * (K / 64) + qg / 4;
-            meta[grp * 64 + (r % 8) * 8 + 2 * (qg % 4) + r / 8] = (uint16_t)md;
+        for (int i = 0; i < kLoadsPerThread; ++i) {
+            const int c = threadIdx.x + i * kPackThreads;
+            v[i] = *reinterpret_cast<const uint4*>(base + (size_t)(c >> 5) * K + (c & 31) * 8);
         }
-        return bad;
-    });
+#pragma unroll
+        for (int i = 0; i < kLoadsPerThread; ++i) {
+            const int c = threadIdx.x + i * kPackThreads;
+            *reinterpret_cast<uint4*>(tile + (c >> 5) * kTilePitch + (c & 31) * 8) = v[i];
+        }
+    } else {  // ragged tile (last K tile or last bands)
+        const int chunks_per_row = nq * 2;
+        const int total = nb * 16 * chunks_per_row;
+        for (int c = threadIdx.x; c < total; c += kPackThreads) {
+            const int r = c / chunks_per_row, x = c % chunks_per_row;
+            *reinterpret_cast<uint4*>(tile + r * kTilePitch + x * 8) =
+                *reinterpret_cast<const uint4*>(base + (size_t)r * K + x * 8);
+        }
+    }
+    __syncthreads();
+    const int q = threadIdx.x / 16, r = threadIdx.x % 16;
+    if (q >= nq) return;
+    const int qg = q0 + q;
+    int bad = 0;
+    for (int b = 0; b < nb; ++b) {
+        const uint16_t* row = tile + (b * 16 + r) * kTilePitch + q * 16;
+        const uint4 lo = *reinterpret_cast<const uint4*>(row);
+        const uint4 hi = *reinterpret_cast<const uint4*>(row + 8);
+        uint32_t wx[4] = {lo.x, lo.z, hi.x, hi.z}, wy[4] = {lo.y, lo.w, hi.y, hi.w};
+        uint32_t w[4], md = 0;
+        bool ok = true;
+        if (prune) {
+            const uint32_t inf = prune == 2 ? 0x7f80u : 0x7c00u;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                uint32_t idx;
+                ok &= prune_compress_group(wx[k], wy[k], inf, &w[k], &idx);
+                md |= idx << (4 * k);
+            }
+        } else {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                uint32_t idx;
+                ok &= compress_group(wx[k], wy[k], &w[k], &idx);
+                md |= idx << (4 * k);
+            }
+        }
+        bad += ok ? 0 : 1;
+        const int band = band0 + b;
+        *reinterpret_cast<uint4*>(vals + (((size_t)band * nbc + qg) * 16 + r) * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+        // Reordered metadata (test/utils.h:179-180): per band and 64-K group,
+        // word i*8 + j holds (row (j%2)*8 + i, block j/2 of the group).
+        const size_t grp = (size_t)band * (K / 64) + qg / 4;
+        meta[grp * 64 + (r % 8) * 8 + 2 * (qg % 4) + r / 8] = (uint16_t)md;
+    }
+    if (bad && bad_blocks) atomicAdd(bad_blocks, bad);
 }
+
 // ------------------------------------------------------------------- fp8
 // The same steps on a group of four fp8 bytes held in one 32-bit word (byte
 // i = position i).  Magnitudes are b & 0x7f; NaN is every magnitude above
@@ -337,42 +294,71 @@ __device__ __forceinline__ bool pack_group8(uint32_t w, uint32_t prune_top, uint
     return ((0x0117u >> z) & 1u) == 0;
 }
 
-// The fp8 packer: the same persistent tile loop; per row of a 32-K block,
-// 32 bytes in, 16 value bytes and 4 metadata bytes out.
+// One CTA: kPackBands 16-row bands x 512 bytes of K (16 blocks of 32 K), the
+// 16-bit kernel's tile geometry in bytes.  Thread t handles row t % 16 of
+// block t / 16 in every band: 32 bytes in, 16 value bytes and 4 metadata
+// bytes out.
 __global__ void __launch_bounds__(kPackThreads) pack_a_fp8_kernel(const uint8_t* __restrict__ dense, int M, int K,
                                                                   uint32_t prune_top, uint8_t* __restrict__ vals,
                                                                   uint8_t* __restrict__ meta, int* bad_blocks) {
-    const int nbc = K / 32;  // 32-K blocks per row
-    const int q = threadIdx.x / 16, r = threadIdx.x % 16;
-    pack_tiles(dense, (size_t)K, M / 16, nbc, bad_blocks, [&](const uint8_t* buf, const PackTile& pt) -> int {
-        if (q >= pt.nq) return 0;
-        const int qg = pt.q0 + q;
-        int bad = 0;
-        for (int b = 0; b < pt.nb; ++b) {
-            const uint8_t* row = buf + (b * 16 + r) * kPitchBytes + q * 32;
-            const uint4 lo = *reinterpret_cast<const uint4*>(row);
-            const uint4 hi = *reinterpret_cast<const uint4*>(row + 16);
-            const uint32_t w[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
-            uint32_t pr[8], md = 0;
-            bool ok = true;
+    __shared__ __align__(16) uint8_t tile[kPackBands * 16 * kTilePitch * 2];
+    constexpr int kPitch = kTilePitch * 2;  // bytes per staged row (512 + 16)
+    const int band0 = blockIdx.y * kPackBands;
+    const int nb = min(kPackBands, M / 16 - band0);
+    const int nbc = K / 32;                     // 32-K blocks per row
+    const int q0 = blockIdx.x * kTileBlocks;
+    const int nq = min(kTileBlocks, nbc - q0);  // a multiple of 4 (K % 128 == 0)
+    const uint8_t* base = dense + (size_t)band0 * 16 * K + (size_t)q0 * 32;
+    uint4 v[kLoadsPerThread];
+    if (nq == kTileBlocks && nb == kPackBands) {  // full tile: 32 chunks of 16 bytes per row
 #pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                uint32_t idx;
-                ok &= pack_group8(w[k], prune_top, &pr[k], &idx);
-                md |= idx << (4 * k);
-            }
-            bad += ok ? 0 : 1;
-            const int band = pt.band0 + b;
-            const uint4 out = make_uint4(pr[0] | (pr[1] << 16), pr[2] | (pr[3] << 16), pr[4] | (pr[5] << 16),
-                                         pr[6] | (pr[7] << 16));
-            *reinterpret_cast<uint4*>(vals + (((size_t)band * nbc + qg) * 16 + r) * 16) = out;
-            // metadata row (band, 128-K group qg / 4, row r): this block's 32 bits
-            *reinterpret_cast<uint32_t*>(meta + (((size_t)band * (K / 128) + qg / 4) * 16 + r) * 16 +
-                                         (qg % 4) * 4) = md;
+        for (int i = 0; i < kLoadsPerThread; ++i) {
+            const int c = threadIdx.x + i * kPackThreads;
+            v[i] = *reinterpret_cast<const uint4*>(base + (size_t)(c >> 5) * K + (c & 31) * 16);
         }
-        return bad;
-    });
+#pragma unroll
+        for (int i = 0; i < kLoadsPerThread; ++i) {
+            const int c = threadIdx.x + i * kPackThreads;
+            *reinterpret_cast<uint4*>(tile + (c >> 5) * kPitch + (c & 31) * 16) = v[i];
+        }
+    } else {
+        const int chunks_per_row = nq * 2;
+        const int total = nb * 16 * chunks_per_row;
+        for (int c = threadIdx.x; c < total; c += kPackThreads) {
+            const int r = c / chunks_per_row, x = c % chunks_per_row;
+            *reinterpret_cast<uint4*>(tile + r * kPitch + x * 16) =
+                *reinterpret_cast<const uint4*>(base + (size_t)r * K + x * 16);
+        }
+    }
+    __syncthreads();
+    const int q = threadIdx.x / 16, r = threadIdx.x % 16;
+    if (q >= nq) return;
+    const int qg = q0 + q;
+    int bad = 0;
+    for (int b = 0; b < nb; ++b) {
+        const uint8_t* row = tile + (b * 16 + r) * kPitch + q * 32;
+        const uint4 lo = *reinterpret_cast<const uint4*>(row);
+        const uint4 hi = *reinterpret_cast<const uint4*>(row + 16);
+        const uint32_t w[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+        uint32_t pr[8], md = 0;
+        bool ok = true;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            uint32_t idx;
+            ok &= pack_group8(w[k], prune_top, &pr[k], &idx);
+            md |= idx << (4 * k);
+        }
+        bad += ok ? 0 : 1;
+        const int band = band0 + b;
+        const uint4 out = make_uint4(pr[0] | (pr[1] << 16), pr[2] | (pr[3] << 16), pr[4] | (pr[5] << 16),
+                                     pr[6] | (pr[7] << 16));
+        *reinterpret_cast<uint4*>(vals + (((size_t)band * nbc + qg) * 16 + r) * 16) = out;
+        // metadata row (band, 128-K group qg / 4, row r): this block's 32 bits
+        *reinterpret_cast<uint32_t*>(meta + (((size_t)band * (K / 128) + qg / 4) * 16 + r) * 16 + (qg % 4) * 4) = md;
+    }
+    if (bad && bad_blocks) atomicAdd(bad_blocks, bad);
 }
+
 // In-place magnitude prune, one group of four per thread.
 __global__ void __launch_bounds__(kPackThreads) prune_kernel(uint16_t* __restrict__ a, long long groups, uint32_t inf) {
     for (long long g = blockIdx.x * (long long)kPackThreads + threadIdx.x; g < groups;
@@ -419,34 +405,6 @@ __global__ void __launch_bounds__(kPackThreads) pack_b_kernel(const uint16_t* __
 
 bool misaligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) != 0; }
 
-// Launches a persistent packer: three CTAs per SM (67.5 KB of shared memory
-// each), never more CTAs than tiles.  The dynamic shared-memory limit is
-// raised once per kernel and device.
-template <class Kern, class... Args>
-cudaError_t launch_packer(Kern kern, std::atomic<uint64_t>& attr_done, int n_tiles, cudaStream_t stream,
-                          Args... args) {
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return e;
-    const uint64_t bit = 1ull << (dev & 63);
-    if (!(attr_done.load(std::memory_order_acquire) & bit)) {
-        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kPackSmem);
-        if (e != cudaSuccess) return e;
-        attr_done.fetch_or(bit, std::memory_order_acq_rel);
-    }
-    int sms = 148;
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const int grid = n_tiles < 3 * sms ? n_tiles : 3 * sms;
-    kern<<<grid, kPackThreads, kPackSmem, stream>>>(args...);
-    return cudaGetLastError();
-}
-
-std::atomic<uint64_t> g_pack16_attr{0}, g_pack8_attr{0};
-
-int pack_tile_count(int M, int nbc) {
-    return ((nbc + kTileBlocks - 1) / kTileBlocks) * ((M / 16 + kPackBands - 1) / kPackBands);
-}
-
 }  // namespace
 }  // namespace spmm24
 
@@ -459,11 +417,13 @@ extern "C" cudaError_t spmm24_pack_a_device(cudaStream_t stream, const void* den
     if (misaligned16(dense_a) || misaligned16(values_out)) return record_invalid("dense A and values must be 16-byte aligned");
     if ((reinterpret_cast<uintptr_t>(meta_out) & 1u) || (reinterpret_cast<uintptr_t>(bad_blocks) & 3u))
         return record_invalid("metadata must be 2-byte and bad_blocks 4-byte aligned");
+    const int nbc = K / 16;
+    dim3 grid((unsigned)((nbc + kTileBlocks - 1) / kTileBlocks), (unsigned)((M / 16 + kPackBands - 1) / kPackBands));
+    if (grid.y > 65535) return record_invalid("M too large");
     if (prune < SPMM24_PRUNE_NONE || prune > SPMM24_PRUNE_BF16) return record_invalid("unknown prune mode");
-    if ((long long)M / 16 * (K / 16) > (1ll << 30)) return record_invalid("matrix too large");
-    return launch_packer(pack_a_kernel, g_pack16_attr, pack_tile_count(M, K / 16), stream,
-                         static_cast<const uint16_t*>(dense_a), M, K, prune, static_cast<uint16_t*>(values_out),
-                         meta_out, bad_blocks);
+    pack_a_kernel<<<grid, kPackThreads, 0, stream>>>(static_cast<const uint16_t*>(dense_a), M, K, prune,
+                                                     static_cast<uint16_t*>(values_out), meta_out, bad_blocks);
+    return cudaGetLastError();
 }
 
 extern "C" cudaError_t spmm24_pack_a_fp8_device(cudaStream_t stream, const void* dense_a, int M, int K, int prune,
@@ -476,11 +436,14 @@ extern "C" cudaError_t spmm24_pack_a_fp8_device(cudaStream_t stream, const void*
         return record_invalid("dense A, values and metadata must be 16-byte aligned");
     if (reinterpret_cast<uintptr_t>(bad_blocks) & 3u) return record_invalid("bad_blocks must be 4-byte aligned");
     if (prune < 0 || prune > 2) return record_invalid("prune: 0 none, 1 E4M3, 2 E5M2");
-    if ((long long)M / 16 * (K / 32) > (1ll << 30)) return record_invalid("matrix too large");
+    const int nbc = K / 32;
+    dim3 grid((unsigned)((nbc + kTileBlocks - 1) / kTileBlocks), (unsigned)((M / 16 + kPackBands - 1) / kPackBands));
+    if (grid.y > 65535) return record_invalid("M too large");
     const uint32_t top = prune == 1 ? 0x7eu : prune == 2 ? 0x7cu : 0u;
-    return launch_packer(pack_a_fp8_kernel, g_pack8_attr, pack_tile_count(M, K / 32), stream,
-                         static_cast<const uint8_t*>(dense_a), M, K, top, static_cast<uint8_t*>(values_out),
-                         static_cast<uint8_t*>(meta_out), bad_blocks);
+    pack_a_fp8_kernel<<<grid, kPackThreads, 0, stream>>>(static_cast<const uint8_t*>(dense_a), M, K, top,
+                                                         static_cast<uint8_t*>(values_out),
+                                                         static_cast<uint8_t*>(meta_out), bad_blocks);
+    return cudaGetLastError();
 }
 
 namespace spmm24 {

@@ -122,8 +122,6 @@ __device__ __forceinline__ void cp_async16(void* dst_smem, const void* src) {
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
-// All but the most recent committed group have completed.
-__device__ __forceinline__ void cp_async_wait_group1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 
 // Bulk copy shared -> global (any GPU's memory of the node): asynchronous,
 // completion tracked per thread in bulk groups.  wait_read returns once
