@@ -111,6 +111,9 @@ using CV256 = ClusterVariant<256, 2>;
 // Pair tiles: 256 x 256 with a 4-stage ring (one CTA per SM).
 constexpr int kPairStages = 4;
 using PairC = PairCfg<kPairStages>;
+// Two M halves per pair (512 x 240 tiles, 3-stage ring of 66 KB stages).
+constexpr int kPair2Stages = 3;
+using Pair2C = Pair2Cfg<kPair2Stages>;
 using PairC8 = PairCfg<kPairStages, true>;
 using SV16 = StreamKVariant<16, 8>;
 using SV32 = StreamKVariant<32, 8>;
@@ -123,6 +126,7 @@ using SV32s = StreamKVariant<32, 4>;
 
 struct Plan {
     Path path;
+    bool pair2;        // pair path with two M halves per pair (512 x 240 tiles)
     bool shallow;      // 4-stage ring, two CTAs per SM (narrow N only)
     int tile_n;
     int stages;
@@ -217,6 +221,26 @@ Plan make_plan(int M, int N, int K, int split_k, int sms, bool plain = true, boo
         if (p.stages_total < 2) ps = 1;
         p.split = ps;
         p.grid = 2 * ps * (int)ptiles;
+        // Two M halves per pair share each B tile (plain fp16 output only):
+        // 512 x 240 tiles, 1.6x the time of a 256 x 256 tile for 1.875x its
+        // area (measured, 4096^3).  Taken when its waves of pairs cost less:
+        // e.g. 4096 x 4096 x 4096 (2 waves against 4: -19%), 11008 x 512 x
+        // 4096 (1 against 2), not 4096 x 512 x 4096 (1 wave either way).
+        const int pair2_env = env_int("SPMM24_PAIR2", -1);  // tuning override: 0 = never, 1 = whenever legal
+        const long long slots = std::max(1, sms / 2);
+        const long long p2tiles = (long long)((M + Pair2C::TILE_M - 1) / Pair2C::TILE_M) *
+                                  ((N + Pair2C::TILE_N - 1) / Pair2C::TILE_N);
+        const long long base_waves = (ptiles + slots - 1) / slots, p2_waves = (p2tiles + slots - 1) / slots;
+        const bool pair2_wins = 16 * p2_waves < 10 * base_waves;
+        if (plain && ps == 1 && split_k <= 1 && pair2_env != 0 && (pair2_env == 1 || pair2_wins)) {
+            p.pair2 = true;
+            p.tile_n = Pair2C::TILE_N;
+            p.stages = kPair2Stages;
+            p.smem = Pair2C::SMEM_ALLOC;
+            p.m_tiles = (M + Pair2C::TILE_M - 1) / Pair2C::TILE_M;
+            p.n_tiles = (N + Pair2C::TILE_N - 1) / Pair2C::TILE_N;
+            p.grid = 2 * p.m_tiles * p.n_tiles;
+        }
         return p;
     }
     p.path = Path::kCluster;
@@ -416,6 +440,15 @@ cudaError_t launch_pair_fp8(const Plan& pl, cudaStream_t stream, int dev, bool p
                          pdl, ta, tb, te, kp, kPairThreads);
 }
 
+cudaError_t launch_pair2(const Plan& pl, cudaStream_t stream, int dev, bool pdl, const CUtensorMap& ta,
+                         const CUtensorMap& tb, const CUtensorMap& te, const PairParams& kp) {
+    auto kern = spmm24_pair2_kernel<kPair2Stages>;
+    cudaError_t e = prepare(kern, Pair2C::SMEM_ALLOC, dev, 13);
+    if (e != cudaSuccess) return e;
+    return launch_kernel(kern, dim3(2u, (unsigned)pl.n_tiles, (unsigned)pl.m_tiles), Pair2C::SMEM_ALLOC, stream, 2u,
+                         pdl, ta, tb, te, kp, kPairThreads);
+}
+
 cudaError_t launch_pair(const Plan& pl, cudaStream_t stream, int dev, bool pdl, const CUtensorMap& ta,
                         const CUtensorMap& tb, const CUtensorMap& te, const PairParams& kp) {
     return pl.split == 2 ? launch_pair_v<true>(pl, stream, dev, pdl, ta, tb, te, kp, 12)
@@ -525,7 +558,7 @@ cudaError_t launch_impl(cudaStream_t stream, const void* A, const void* B, const
     {
         cuuint64_t dims[4] = {128, (cuuint64_t)(K / 64), 4, (cuuint64_t)((N + 7) / 8)};
         cuuint64_t str[3] = {1024, 256, (cuuint64_t)16 * K};
-        const int cta_n = pl.path == Path::kPair ? PairC::HALF_N : pl.tile_n;  // columns one CTA loads
+        const int cta_n = pl.path != Path::kPair ? pl.tile_n : pl.pair2 ? Pair2C::HALF_N : PairC::HALF_N;  // columns one CTA loads
         cuuint32_t box[4] = {128, 2, 4, (cuuint32_t)(cta_n / 8)};
         if (!encode(&tb, 4, B, dims, str, box)) return invalid("TMA descriptor for B could not be encoded");
     }
@@ -554,6 +587,7 @@ cudaError_t launch_impl(cudaStream_t stream, const void* A, const void* B, const
         kp.weights_static = wstatic;
         kp.split = pl.split;
         kp.mma_fmt = 0;
+        if (pl.pair2) return launch_pair2(pl, stream, dev, pdl, ta, tb, te, kp);
         return launch_pair(pl, stream, dev, pdl, ta, tb, te, kp);
     }
     if (pl.path == Path::kStreamK) {
@@ -1017,7 +1051,7 @@ extern "C" int spmm24_select_config(int M, int N, int K, int split_k, spmm24_con
     if (sms <= 0) sms = 148;
     cudaGetLastError();
     const spmm24::Plan pl = spmm24::make_plan(M, N, K, split_k, sms);
-    out->tile_m = pl.path == spmm24::Path::kPair ? 2 * spmm24::kTileM : spmm24::kTileM;
+    out->tile_m = pl.path == spmm24::Path::kPair ? (pl.pair2 ? 4 : 2) * spmm24::kTileM : spmm24::kTileM;
     out->tile_n = pl.tile_n;
     out->stage_k = 128;
     out->stages = pl.stages;

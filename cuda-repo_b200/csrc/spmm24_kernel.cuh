@@ -857,6 +857,239 @@ spmm24_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
 }
 
 // -------------------------------------------------------------------------
+// Two M halves per pair: a 512 x 240 tile.  Each CTA holds two 128-row
+// halves of A (rows m0 + 256h + 128 rank, h = 0, 1) and 120 columns of B;
+// per K step the leader issues two M=256 MMAs that share the B tile, into
+// two TMEM accumulators (columns 0 and 256).  Every stage moves 66 KB per
+// CTA for 15.7 MFLOP (dense-equivalent) instead of 50 KB for 8.4 MFLOP,
+// so the same shared-memory bytes in flight feed the tensor core 1.4x
+// longer.  Plain fp16 row-major output; no K split.
+template <int STAGES>
+struct Pair2Cfg {
+    static constexpr int HALF_N = 120;                   // columns of B / C per CTA (15 strips)
+    static constexpr int TILE_N = 2 * HALF_N;            // columns per pair
+    static constexpr int TILE_M = 4 * kTileM;            // rows per pair
+    static constexpr int A_HALF = 8 * 8 * 256;           // 128 rows x 128 logical K
+    static constexpr int A_BYTES = 2 * A_HALF;
+    static constexpr int B_BYTES = (HALF_N / 8) * 2048;  // 15 strips x 128 K
+    static constexpr int E_HALF = 16 * 128;
+    static constexpr int E_BYTES = 2 * E_HALF;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + E_BYTES;
+    static constexpr int RING_BYTES = STAGES * STAGE_BYTES;
+    static constexpr int BAR_OFFSET = RING_BYTES;
+    static constexpr int NUM_BARS = 2 * STAGES + 1;  // full, empty, acc_full
+    static constexpr int HOLDER_OFFSET = BAR_OFFSET + NUM_BARS * 8;
+    static constexpr int SMEM_BYTES = HOLDER_OFFSET + 16;
+    static constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;
+    static constexpr int ACC1_COL = 256;                  // second accumulator
+    static constexpr int META0_COL = TILE_N;              // metadata rings after each accumulator
+    static constexpr int META1_COL = ACC1_COL + TILE_N;
+    static constexpr int TMEM_COLS = 512;
+    static constexpr int C_PITCH = TILE_N + 8;  // halves per staged output row (bank-shifted)
+    static_assert(META0_COL + 4 * STAGES <= ACC1_COL && META1_COL + 4 * STAGES <= TMEM_COLS, "TMEM overflow");
+    static_assert(2 * kTileM * C_PITCH * 2 <= RING_BYTES, "output staging does not fit");
+    static_assert(SMEM_ALLOC <= 232448, "shared memory overflow");
+};
+
+template <int STAGES>
+__global__ void __launch_bounds__(kPairThreads, 1)
+spmm24_pair2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const __grid_constant__ CUtensorMap tmE, const PairParams p) {
+    using C_ = Pair2Cfg<STAGES>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C_::BAR_OFFSET);  // used in the leader only
+    uint64_t* empty = full + STAGES;
+    uint64_t* acc_full = empty + STAGES;
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + C_::HOLDER_OFFSET);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = ptx::cluster_ctarank();  // 0 = leader (issues the MMAs), 1 = peer
+    const bool leader = rank == 0;
+    int m_tile, n_tile;
+    {
+        const int pid = blockIdx.y + gridDim.y * blockIdx.z;
+        const int n_tiles = gridDim.y, m_tiles = gridDim.z;
+        const int per_group = kPairGroupM * n_tiles;
+        const int first_m = (pid / per_group) * kPairGroupM;
+        const int group_m = min(m_tiles - first_m, kPairGroupM);
+        const int in_group = pid % per_group;
+        m_tile = first_m + in_group % group_m;
+        n_tile = in_group / group_m;
+    }
+    // this CTA's 128-row halves: rows m0 + 256 h + 128 rank
+    const int band_h0 = (m_tile * C_::TILE_M + (int)rank * kTileM) / 16;
+    const int band_h1 = band_h0 + 2 * kTileM / 16;
+    const int strip0 = (n_tile * C_::TILE_N + (int)rank * C_::HALF_N) / 8;
+    const int st_count = p.stages_total;
+
+    if (threadIdx.x == 0) {
+        SPMM24_STAMP(0);
+        for (int s = 0; s < STAGES; ++s) {
+            ptx::mbar_init(&full[s], 1);
+            ptx::mbar_init(&empty[s], 1);
+        }
+        ptx::mbar_init(acc_full, 1);
+        ptx::fence_mbarrier_init();
+        ptx::prefetch_tmap(&tmA);
+        ptx::prefetch_tmap(&tmB);
+        ptx::prefetch_tmap(&tmE);
+    }
+    if (warp == 1) {
+        ptx::tmem_alloc_pair(tmem_holder, C_::TMEM_COLS);
+        ptx::tmem_relinquish_pair();
+    }
+    ptx::tc_fence_before();
+    ptx::cluster_sync();  // both CTAs: barriers initialised, TMEM allocated
+    ptx::tc_fence_after();
+    const uint32_t tmem_base = *tmem_holder;
+    if (threadIdx.x == 0) ptx::grid_dep_launch();
+
+    const uint64_t pol = ptx::policy_evict_last();
+    const uint32_t full0 = ptx::mapa_shared(ptx::smem_u32(&full[0]), 0u);
+    const int pre = p.weights_static ? min(STAGES, st_count) : 0;
+    auto load_weights = [&](uint8_t* st, uint32_t bar, int g) {
+        ptx::tma_load_3d_pair(st, &tmA, bar, 0, band_h0, 8 * g, pol);
+        ptx::tma_load_3d_pair(st + C_::A_HALF, &tmA, bar, 0, band_h1, 8 * g, pol);
+        ptx::tma_load_2d_pair(st + C_::A_BYTES + C_::B_BYTES, &tmE, bar, 128 * g, band_h0, pol);
+        ptx::tma_load_2d_pair(st + C_::A_BYTES + C_::B_BYTES + C_::E_HALF, &tmE, bar, 128 * g, band_h1, pol);
+    };
+    if (warp == 0) {
+        // ------------------------------------------------- TMA producer
+        if (lane == 0) {
+            for (int it = 0; it < pre; ++it) {
+                if (leader) ptx::mbar_arrive_expect_tx(&full[it], 2 * C_::STAGE_BYTES);
+                load_weights(smem + it * C_::STAGE_BYTES, full0 + 8u * it, it);
+            }
+            ptx::grid_dep_wait();
+            SPMM24_STAMP(1);
+            for (int it = 0; it < pre; ++it)
+                ptx::tma_load_4d_pair(smem + it * C_::STAGE_BYTES + C_::A_BYTES, &tmB, full0 + 8u * it, 0, 2 * it, 0,
+                                      strip0, pol);
+            for (int it = pre; it < st_count; ++it) {
+                const int s = it % STAGES;
+                const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
+                if (!ptx::mbar_wait_bounded(&empty[s], ph ^ 1u, kWaitLimitNs)) {
+                    atomicOr(&g_spmm24_status, kStatusProducerTimeout);
+                    break;
+                }
+                uint8_t* st = smem + s * C_::STAGE_BYTES;
+                const uint32_t bar = full0 + 8u * s;
+                if (leader) ptx::mbar_arrive_expect_tx(&full[s], 2 * C_::STAGE_BYTES);
+                load_weights(st, bar, it);
+                ptx::tma_load_4d_pair(st + C_::A_BYTES, &tmB, bar, 0, 2 * it, 0, strip0, pol);
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1 && leader) {
+        // ---------------------------------- MMA issuer (leader CTA only)
+        const uint32_t idesc = pair_idesc<C_::TILE_N>();
+        const uint32_t smem_base = ptx::smem_u32(smem);
+        uint32_t accumulate = 0;
+        for (int it = 0; it < st_count; ++it) {
+            const int s = it % STAGES;
+            const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
+            if (!ptx::mbar_wait_bounded(&full[s], ph, kWaitLimitNs)) {
+                if (lane == 0) atomicOr(&g_spmm24_status, kStatusMmaTimeout);
+                break;
+            }
+            if (lane == 0 && it == 0) SPMM24_STAMP(2);
+            if (lane == 0 && it == st_count - 1) SPMM24_STAMP(3);
+            ptx::tc_fence_after();
+            if (lane == 0) {
+                const uint32_t st = smem_base + s * C_::STAGE_BYTES;
+                const uint32_t stB = st + C_::A_BYTES;
+                const uint32_t stE = stB + C_::B_BYTES;
+                const uint32_t meta0 = tmem_base + C_::META0_COL + 4 * s;
+                const uint32_t meta1 = tmem_base + C_::META1_COL + 4 * s;
+                ptx::tmem_cp_128x128b_pair(meta0, smem_desc(stE, 0, 128));
+                ptx::tmem_cp_128x128b_pair(meta1, smem_desc(stE + C_::E_HALF, 0, 128));
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const uint64_t bdesc = smem_desc(stB + j * 512, 128, 2048);
+                    const uint32_t id = idesc | (uint32_t)(j & 1);
+                    ptx::mma_sp_f16_pair(tmem_base, smem_desc(st + j * 2048, 4 * 2048, 128), bdesc, meta0 + (j & 2),
+                                         id, accumulate);
+                    ptx::mma_sp_f16_pair(tmem_base + C_::ACC1_COL, smem_desc(st + C_::A_HALF + j * 2048, 4 * 2048, 128),
+                                         bdesc, meta1 + (j & 2), id, accumulate);
+                    accumulate = 1;
+                }
+                ptx::tc_commit_pair_mc(&empty[s], (uint16_t)0x3);  // frees ring slot s in both CTAs
+            }
+            __syncwarp();
+        }
+        if (lane == 0) ptx::tc_commit_pair_mc(acc_full, (uint16_t)0x3);
+        __syncwarp();
+    }
+    {
+        // ------------------------------- epilogue (every warp, both CTAs)
+        // TMEM -> fp16 -> staged rows (two halves of 128 rows, bank-shifted)
+        // -> coalesced 16-byte stores.
+        if (!ptx::mbar_wait_bounded(acc_full, 0, kWaitLimitNs)) atomicOr(&g_spmm24_status, kStatusEpilogueTimeout);
+        if (threadIdx.x == 64) SPMM24_STAMP(4);
+        ptx::tc_fence_after();
+        __syncwarp();
+        const int quad = warp & 3;
+        const int row = quad * 32 + lane;
+        constexpr int NCH16 = C_::TILE_N / 16;          // 15 chunks of 16 columns per row
+        const int c_begin = (warp >> 2) ? (NCH16 + 1) / 2 : 0;  // warps 0-3: chunks 0-7, warps 4-7: 8-14
+        const int c_end = (warp >> 2) ? NCH16 : (NCH16 + 1) / 2;
+        __half* cst = reinterpret_cast<__half*>(smem);
+#pragma unroll 1
+        for (int h = 0; h < 2; ++h) {
+#pragma unroll 1
+            for (int c = c_begin; c < c_end; ++c) {
+                uint32_t v[16];
+                ptx::tmem_ld_32x32b_x16(tmem_base + (uint32_t)(h * C_::ACC1_COL) + ((uint32_t)(quad * 32) << 16) +
+                                            (uint32_t)(c * 16),
+                                        v);
+                ptx::tmem_wait_ld();
+                __align__(16) __half hv[16];
+#pragma unroll
+                for (int e = 0; e < 16; ++e) hv[e] = __float2half_rn(__uint_as_float(v[e]));
+                uint4* dst = reinterpret_cast<uint4*>(cst + (size_t)(h * kTileM + row) * C_::C_PITCH + c * 16);
+                dst[0] = reinterpret_cast<const uint4*>(hv)[0];
+                dst[1] = reinterpret_cast<const uint4*>(hv)[1];
+            }
+        }
+        ptx::tc_fence_before();
+        ptx::named_barrier(kBarEpi, kPairThreads);
+        ptx::grid_dep_wait();  // C may be in use by the previous grid
+        constexpr int LPR = C_::TILE_N / 8;  // 30 threads per row
+        constexpr int RPP = kPairThreads / LPR;  // 8 rows per pass (240 threads)
+        const int etid = threadIdx.x;
+        if (etid < LPR * RPP) {
+            const int chunk = etid % LPR;
+            const int gn = n_tile * C_::TILE_N + chunk * 8;
+            const bool vec_ok = (p.N % 8 == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15u) == 0);
+            for (int r = etid / LPR; r < 2 * kTileM; r += RPP) {
+                const int gm = m_tile * C_::TILE_M + (r / kTileM) * 2 * kTileM + (int)rank * kTileM + r % kTileM;
+                if (gm >= p.M || gn >= p.N) continue;
+                const __half* src = cst + (size_t)r * C_::C_PITCH + chunk * 8;
+                __half* out = reinterpret_cast<__half*>(p.C) + (size_t)gm * p.N + gn;
+                if (vec_ok) {
+                    *reinterpret_cast<uint4*>(out) = *reinterpret_cast<const uint4*>(src);
+                } else {
+                    const int lim = min(8, p.N - gn);
+                    for (int e = 0; e < lim; ++e) out[e] = src[e];
+                }
+            }
+        }
+    }
+
+    if (threadIdx.x == 64) SPMM24_STAMP(5);
+    ptx::tc_fence_before();
+    __syncthreads();
+    ptx::cluster_sync();  // neither CTA may leave while the pair still shares shared memory / TMEM
+    if (warp == 1) {
+        ptx::tc_fence_after();
+        ptx::tmem_dealloc_pair(tmem_base, C_::TMEM_COLS);
+    }
+    if (threadIdx.x == 0) SPMM24_STAMP(6);
+}
+
+// -------------------------------------------------------------------------
 template <int N_TILE, int STAGES>
 struct StreamKCfg : Cfg<N_TILE, STAGES, 2> {
     using B_ = Cfg<N_TILE, STAGES, 2>;

@@ -172,6 +172,12 @@ def test_select_config_picks_tiles_and_splits():
     assert c["cta_pair"] == 1 and c["split_k"] == 2 and c["grid_ctas"] == 128
     assert spmm24.select_config(8192, 256, 28672)["split_k"] == 2
     assert spmm24.select_config(11008, 512, 4096)["split_k"] == 1   # 86 tiles: more than half a wave
+    # two M halves per pair (512 x 240) when its waves of pairs cost less
+    c = spmm24.select_config(4096, 4096, 4096)
+    assert (c["tile_m"], c["tile_n"], c["stages"], c["grid_ctas"]) == (512, 240, 3, 2 * 8 * 18)
+    assert spmm24.select_config(11008, 512, 4096)["tile_m"] == 512    # 1 wave against 2
+    assert spmm24.select_config(4096, 512, 4096)["tile_m"] == 256     # 1 wave either way
+    assert spmm24.select_config(2048, 2048, 2048)["tile_m"] == 256
     assert spmm24.select_config(4096, 512, 4160)["cta_pair"] == 0  # K % 128 != 0
     assert spmm24.select_config(4096, 512, 4096, 2)["cta_pair"] == 0  # explicit split-K
     # explicit split honoured, clamped to the number of 128-K stages

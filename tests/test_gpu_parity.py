@@ -169,11 +169,32 @@ def test_cta_pair_kernel(cuda_device, monkeypatch, shape, split):
     import spmm24
 
     monkeypatch.setenv("SPMM24_PAIR_SPLIT", str(split))
+    monkeypatch.setenv("SPMM24_PAIR2", "0")
     M, N, K = shape
     cfg = spmm24.select_config(M, N, K)
     assert cfg["cta_pair"] == 1 and cfg["tile_n"] == 256 and cfg["split_k"] == (split if K >= 256 else 1)
     p = make_problem(M, N, K, seed=3 * M + N)
     check(p, 0, cuda_device)
+
+
+@pytest.mark.parametrize("shape", [
+    (512, 240, 128),     # one pair tile, one stage
+    (1024, 480, 512),
+    (592, 500, 384),     # ragged M (second half of a pair partly past M) and ragged N
+    (4096, 1004, 1024),  # N not a multiple of 8: scalar stores
+    (2048, 2048, 1024),
+    (1536, 4096, 640),   # odd stage count
+])
+def test_cta_pair_two_m_halves(cuda_device, monkeypatch, shape):
+    """The pair kernel with two M halves per pair (512 x 240 tiles: two
+    M=256 MMAs share each B tile, two TMEM accumulators)."""
+    import spmm24
+
+    monkeypatch.setenv("SPMM24_PAIR2", "1")
+    M, N, K = shape
+    cfg = spmm24.select_config(M, N, K)
+    assert cfg["cta_pair"] == 1 and cfg["tile_m"] == 512 and cfg["tile_n"] == 240
+    check(make_problem(M, N, K, seed=5 * M + N), 0, cuda_device)
 
 
 def test_cta_pair_forced_small_n(cuda_device, monkeypatch):
