@@ -157,10 +157,11 @@ int cluster_smem(int tn) {
 }
 
 // plain: the plain fp16 launch (the only one the stream-K option serves).
-// allow_pair: the CTA-pair path may be chosen (not for fp8).  max_split:
-// the largest automatic K split.
+// allow_pair: the CTA-pair path may be chosen.  max_split: the largest
+// automatic K split.  pair2_ok: the two-M-half pair kernel may be chosen
+// (16-bit operands, no residual, row-major output, no gather).
 Plan make_plan(int M, int N, int K, int split_k, int sms, bool plain = true, bool allow_pair = true,
-               int max_split = kMaxSplit) {
+               int max_split = kMaxSplit, bool pair2_ok = true) {
     Plan p{};
     int tn = N <= 16 ? 16 : N <= 32 ? 32 : N <= 64 ? 64 : 128;
     const int forced = env_int("SPMM24_TILE_N", 0);  // tuning override (16/32/64/128/256)
@@ -232,7 +233,7 @@ Plan make_plan(int M, int N, int K, int split_k, int sms, bool plain = true, boo
                                   ((N + Pair2C::TILE_N - 1) / Pair2C::TILE_N);
         const long long base_waves = (ptiles + slots - 1) / slots, p2_waves = (p2tiles + slots - 1) / slots;
         const bool pair2_wins = 16 * p2_waves < 10 * base_waves;
-        if (plain && ps == 1 && split_k <= 1 && pair2_env != 0 && (pair2_env == 1 || pair2_wins)) {
+        if (pair2_ok && ps == 1 && split_k <= 1 && pair2_env != 0 && (pair2_env == 1 || pair2_wins)) {
             p.pair2 = true;
             p.tile_n = Pair2C::TILE_N;
             p.stages = kPair2Stages;
@@ -442,8 +443,9 @@ cudaError_t launch_pair_fp8(const Plan& pl, cudaStream_t stream, int dev, bool p
 
 cudaError_t launch_pair2(const Plan& pl, cudaStream_t stream, int dev, bool pdl, const CUtensorMap& ta,
                          const CUtensorMap& tb, const CUtensorMap& te, const PairParams& kp) {
-    auto kern = spmm24_pair2_kernel<kPair2Stages>;
-    cudaError_t e = prepare(kern, Pair2C::SMEM_ALLOC, dev, 13);
+    const bool general = !epilogue_plain_fp16(kp.epi);
+    auto kern = general ? spmm24_pair2_kernel<kPair2Stages, true> : spmm24_pair2_kernel<kPair2Stages, false>;
+    cudaError_t e = prepare(kern, Pair2C::SMEM_ALLOC, dev, general ? 14 : 13);
     if (e != cudaSuccess) return e;
     return launch_kernel(kern, dim3(2u, (unsigned)pl.n_tiles, (unsigned)pl.m_tiles), Pair2C::SMEM_ALLOC, stream, 2u,
                          pdl, ta, tb, te, kp, kPairThreads);
@@ -522,7 +524,8 @@ cudaError_t launch_impl(cudaStream_t stream, const void* A, const void* B, const
     int dev = 0;
     e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    Plan pl = make_plan(M, N, K, split_k, sm_count(dev), plain);
+    const bool pair2_ok = !epi.residual && !epi.packed && epi.gather_n == 0;
+    Plan pl = make_plan(M, N, K, split_k, sm_count(dev), plain, true, kMaxSplit, pair2_ok);
 
     uint32_t* ws_counters = nullptr;
     float* ws_partials = nullptr;
@@ -666,7 +669,7 @@ cudaError_t launch_fp8_impl(cudaStream_t stream, const void* A, const void* B, c
     // (a cheaper cluster reduction and more SM slots left to the next
     // launch's early CTAs), and 11008-row layers pick 3 either way.  Wide N
     // takes the CTA pair as for 16-bit operands (its stage is 256 K: K % 256).
-    Plan pl = make_plan(M, N, Kh, split_k, sm_count(dev), false, Kh % 128 == 0, 5);
+    Plan pl = make_plan(M, N, Kh, split_k, sm_count(dev), false, Kh % 128 == 0, 5, false);
     const bool pair = pl.path == Path::kPair;
 
     CUtensorMap ta, tb, te;

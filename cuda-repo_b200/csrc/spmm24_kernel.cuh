@@ -863,7 +863,8 @@ spmm24_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
 // two TMEM accumulators (columns 0 and 256).  Every stage moves 66 KB per
 // CTA for 15.7 MFLOP (dense-equivalent) instead of 50 KB for 8.4 MFLOP,
 // so the same shared-memory bytes in flight feed the tensor core 1.4x
-// longer.  Plain fp16 row-major output; no K split.
+// longer.  Row-major output; EPI adds alpha, bias, activation and bf16
+// (no residual, no packed output, no gather); no K split.
 template <int STAGES>
 struct Pair2Cfg {
     static constexpr int HALF_N = 120;                   // columns of B / C per CTA (15 strips)
@@ -891,7 +892,7 @@ struct Pair2Cfg {
     static_assert(SMEM_ALLOC <= 232448, "shared memory overflow");
 };
 
-template <int STAGES>
+template <int STAGES, bool EPI>
 __global__ void __launch_bounds__(kPairThreads, 1)
 spmm24_pair2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmE, const PairParams p) {
@@ -984,7 +985,7 @@ spmm24_pair2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         __syncwarp();
     } else if (warp == 1 && leader) {
         // ---------------------------------- MMA issuer (leader CTA only)
-        const uint32_t idesc = pair_idesc<C_::TILE_N>();
+        const uint32_t idesc = pair_idesc<C_::TILE_N>() | ((EPI && p.epi.bf16) ? kIdescBf16 : 0u);
         const uint32_t smem_base = ptx::smem_u32(smem);
         uint32_t accumulate = 0;
         for (int it = 0; it < st_count; ++it) {
@@ -1024,8 +1025,8 @@ spmm24_pair2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     }
     {
         // ------------------------------- epilogue (every warp, both CTAs)
-        // TMEM -> fp16 -> staged rows (two halves of 128 rows, bank-shifted)
-        // -> coalesced 16-byte stores.
+        // TMEM -> (EPI: alpha, bias, activation) -> 16-bit -> staged rows
+        // (two halves of 128 rows, bank-shifted) -> coalesced 16-byte stores.
         if (!ptx::mbar_wait_bounded(acc_full, 0, kWaitLimitNs)) atomicOr(&g_spmm24_status, kStatusEpilogueTimeout);
         if (threadIdx.x == 64) SPMM24_STAMP(4);
         ptx::tc_fence_after();
@@ -1045,12 +1046,25 @@ spmm24_pair2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                                             (uint32_t)(c * 16),
                                         v);
                 ptx::tmem_wait_ld();
-                __align__(16) __half hv[16];
-#pragma unroll
-                for (int e = 0; e < 16; ++e) hv[e] = __float2half_rn(__uint_as_float(v[e]));
                 uint4* dst = reinterpret_cast<uint4*>(cst + (size_t)(h * kTileM + row) * C_::C_PITCH + c * 16);
-                dst[0] = reinterpret_cast<const uint4*>(hv)[0];
-                dst[1] = reinterpret_cast<const uint4*>(hv)[1];
+                if constexpr (EPI) {
+                    float y[16];
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) y[e] = __uint_as_float(v[e]);
+                    const int gm = m_tile * C_::TILE_M + h * 2 * kTileM + (int)rank * kTileM + row;
+                    if (gm < p.M) epilogue_pre<16>(y, p.epi, gm);
+                    uint32_t w[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) w[e] = pack2(y[2 * e], y[2 * e + 1], p.epi.bf16);
+                    dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+                    dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+                } else {
+                    __align__(16) __half hv[16];
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) hv[e] = __float2half_rn(__uint_as_float(v[e]));
+                    dst[0] = reinterpret_cast<const uint4*>(hv)[0];
+                    dst[1] = reinterpret_cast<const uint4*>(hv)[1];
+                }
             }
         }
         ptx::tc_fence_before();

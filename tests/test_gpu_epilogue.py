@@ -247,3 +247,20 @@ def test_device_packer_bf16(cuda_device):
     spmm24.prune_2of4_device(t, M, K, bf16=True)
     torch.cuda.synchronize(cuda_device)
     assert np.array_equal(t.cpu().numpy().view(np.uint16), host_pruned)
+
+
+@pytest.mark.parametrize("shape", [(1024, 480, 512), (592, 500, 384), (2048, 1024, 1024)], ids=lambda s: "x".join(map(str, s)))
+@pytest.mark.parametrize("bf16", [False, True])
+def test_two_m_half_pair_epilogue(cuda_device, monkeypatch, shape, bf16):
+    """The 512 x 240 pair kernel with alpha, bias and an activation, fp16 and
+    bf16; calls with a residual or a packed output take the 256 x 256 pair
+    kernel instead (same results)."""
+    import spmm24
+
+    monkeypatch.setenv("SPMM24_PAIR2", "1")
+    M, N, K = shape
+    assert spmm24.select_config(M, N, K)["tile_m"] == 512
+    _run(cuda_device, M, N, K, bf16=bf16, bias=True, alpha=0.5, act=2, seed=M + 7 * N)
+    _run(cuda_device, M, N, K, bf16=bf16, act=3, seed=M + 5 * N)
+    _run(cuda_device, M, N, K, bf16=bf16, residual=True, bias=True, act=1, seed=M + 3 * N)
+    _run(cuda_device, M, N, K, bf16=bf16, packed=True, seed=M + N)
