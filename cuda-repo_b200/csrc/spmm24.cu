@@ -114,6 +114,7 @@ using PairC = PairCfg<kPairStages>;
 // Two M halves per pair (512 x 240 tiles, 3-stage ring of 66 KB stages).
 constexpr int kPair2Stages = 3;
 using Pair2C = Pair2Cfg<kPair2Stages>;
+using Pair2C8 = Pair2Cfg<kPair2Stages, true>;
 using PairC8 = PairCfg<kPairStages, true>;
 using SV16 = StreamKVariant<16, 8>;
 using SV32 = StreamKVariant<32, 8>;
@@ -154,6 +155,29 @@ int cluster_smem(int tn) {
         case 128: return CV128::C_::SMEM_ALLOC;
         default: return CV256::C_::SMEM_ALLOC;
     }
+}
+
+// Two M halves per pair share each B tile: 512 x tile_n tiles, 1.6x the
+// time of a 256 x 256 tile for 1.875x its area (measured, 4096^3, tile_n
+// 240).  Switches a pair plan with one pair per tile to that kernel when
+// its waves of pairs cost less: e.g. 4096 x 4096 x 4096 (2 waves against
+// 4: -19%), 11008 x 512 x 4096 (1 against 2), not 4096 x 512 x 4096 (1
+// wave either way).
+void maybe_pair2(Plan& p, int M, int N, int sms, int tile_n, int stages, int smem) {
+    const int env = env_int("SPMM24_PAIR2", -1);  // tuning override: 0 = never, 1 = whenever legal
+    if (env == 0) return;
+    const long long slots = std::max(1, sms / 2);
+    const long long m2 = (M + 4 * kTileM - 1) / (4 * kTileM), n2 = (N + tile_n - 1) / tile_n;
+    const long long base_waves = ((long long)p.m_tiles * p.n_tiles + slots - 1) / slots;
+    const long long p2_waves = (m2 * n2 + slots - 1) / slots;
+    if (env != 1 && 16 * p2_waves >= 10 * base_waves) return;
+    p.pair2 = true;
+    p.tile_n = tile_n;
+    p.stages = stages;
+    p.smem = smem;
+    p.m_tiles = (int)m2;
+    p.n_tiles = (int)n2;
+    p.grid = 2 * p.m_tiles * p.n_tiles;
 }
 
 // plain: the plain fp16 launch (the only one the stream-K option serves).
@@ -222,26 +246,8 @@ Plan make_plan(int M, int N, int K, int split_k, int sms, bool plain = true, boo
         if (p.stages_total < 2) ps = 1;
         p.split = ps;
         p.grid = 2 * ps * (int)ptiles;
-        // Two M halves per pair share each B tile (plain fp16 output only):
-        // 512 x 240 tiles, 1.6x the time of a 256 x 256 tile for 1.875x its
-        // area (measured, 4096^3).  Taken when its waves of pairs cost less:
-        // e.g. 4096 x 4096 x 4096 (2 waves against 4: -19%), 11008 x 512 x
-        // 4096 (1 against 2), not 4096 x 512 x 4096 (1 wave either way).
-        const int pair2_env = env_int("SPMM24_PAIR2", -1);  // tuning override: 0 = never, 1 = whenever legal
-        const long long slots = std::max(1, sms / 2);
-        const long long p2tiles = (long long)((M + Pair2C::TILE_M - 1) / Pair2C::TILE_M) *
-                                  ((N + Pair2C::TILE_N - 1) / Pair2C::TILE_N);
-        const long long base_waves = (ptiles + slots - 1) / slots, p2_waves = (p2tiles + slots - 1) / slots;
-        const bool pair2_wins = 16 * p2_waves < 10 * base_waves;
-        if (pair2_ok && ps == 1 && split_k <= 1 && pair2_env != 0 && (pair2_env == 1 || pair2_wins)) {
-            p.pair2 = true;
-            p.tile_n = Pair2C::TILE_N;
-            p.stages = kPair2Stages;
-            p.smem = Pair2C::SMEM_ALLOC;
-            p.m_tiles = (M + Pair2C::TILE_M - 1) / Pair2C::TILE_M;
-            p.n_tiles = (N + Pair2C::TILE_N - 1) / Pair2C::TILE_N;
-            p.grid = 2 * p.m_tiles * p.n_tiles;
-        }
+        if (pair2_ok && ps == 1 && split_k <= 1)
+            maybe_pair2(p, M, N, sms, Pair2C::TILE_N, kPair2Stages, Pair2C::SMEM_ALLOC);
         return p;
     }
     p.path = Path::kCluster;
@@ -671,6 +677,8 @@ cudaError_t launch_fp8_impl(cudaStream_t stream, const void* A, const void* B, c
     // takes the CTA pair as for 16-bit operands (its stage is 256 K: K % 256).
     Plan pl = make_plan(M, N, Kh, split_k, sm_count(dev), false, Kh % 128 == 0, 5, false);
     const bool pair = pl.path == Path::kPair;
+    if (pair && pl.split == 1 && split_k <= 1 && !epi.residual && !epi.packed)
+        maybe_pair2(pl, M, N, sm_count(dev), Pair2C8::TILE_N, kPair2Stages, Pair2C8::SMEM_ALLOC);
 
     CUtensorMap ta, tb, te;
     {
@@ -684,7 +692,7 @@ cudaError_t launch_fp8_impl(cudaStream_t stream, const void* A, const void* B, c
     {
         cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)N};
         cuuint64_t str[1] = {(cuuint64_t)K};
-        cuuint32_t box[2] = {128, (cuuint32_t)(pair ? PairC8::HALF_N : pl.tile_n)};
+        cuuint32_t box[2] = {128, (cuuint32_t)(!pair ? pl.tile_n : pl.pair2 ? Pair2C8::HALF_N : PairC8::HALF_N)};
         if (!encode(&tb, 2, B, dims, str, box, CU_TENSOR_MAP_DATA_TYPE_UINT8, CU_TENSOR_MAP_SWIZZLE_128B))
             return invalid("TMA descriptor for B could not be encoded");
     }
@@ -714,6 +722,13 @@ cudaError_t launch_fp8_impl(cudaStream_t stream, const void* A, const void* B, c
         kp.weights_static = (flags & SPMM24_STATIC_WEIGHTS) ? 1 : 0;
         kp.split = pl.split;
         kp.mma_fmt = mma_fmt;
+        if (pl.pair2) {
+            auto kern = spmm24_pair2_kernel<kPair2Stages, true, true>;
+            e = prepare(kern, Pair2C8::SMEM_ALLOC, dev, kFp8Slot + 13);
+            if (e != cudaSuccess) return e;
+            return launch_kernel(kern, dim3(2u, (unsigned)pl.n_tiles, (unsigned)pl.m_tiles), Pair2C8::SMEM_ALLOC,
+                                 stream, 2u, pdl, ta, tb, te, kp, kPairThreads);
+        }
         return pl.split == 2 ? launch_pair_fp8<true>(pl, stream, dev, pdl, ta, tb, te, kp)
                              : launch_pair_fp8<false>(pl, stream, dev, pdl, ta, tb, te, kp);
     }

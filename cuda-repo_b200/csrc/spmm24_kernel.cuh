@@ -864,17 +864,22 @@ spmm24_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
 // CTA for 15.7 MFLOP (dense-equivalent) instead of 50 KB for 8.4 MFLOP,
 // so the same shared-memory bytes in flight feed the tensor core 1.4x
 // longer.  Row-major output; EPI adds alpha, bias, activation and bf16
-// (no residual, no packed output, no gather); no K split.
-template <int STAGES>
+// (no residual, no packed output, no gather); no K split.  FP8: 512 x 224
+// tiles (two 128-byte-swizzled B halves of 112 rows per stage, two 128-K
+// metadata groups per half: the wider metadata ring leaves room for two
+// 224-column accumulators in TMEM); always EPI.
+template <int STAGES, bool FP8 = false>
 struct Pair2Cfg {
-    static constexpr int HALF_N = 120;                   // columns of B / C per CTA (15 strips)
+    static constexpr bool kFp8 = FP8;
+    static constexpr int HALF_N = FP8 ? 112 : 120;       // columns of B / C per CTA
     static constexpr int TILE_N = 2 * HALF_N;            // columns per pair
     static constexpr int TILE_M = 4 * kTileM;            // rows per pair
-    static constexpr int A_HALF = 8 * 8 * 256;           // 128 rows x 128 logical K
+    static constexpr int A_HALF = 8 * 8 * 256;           // 128 rows x 128 logical K (fp8: 256)
     static constexpr int A_BYTES = 2 * A_HALF;
-    static constexpr int B_BYTES = (HALF_N / 8) * 2048;  // 15 strips x 128 K
-    static constexpr int E_HALF = 16 * 128;
+    static constexpr int B_BYTES = (HALF_N / 8) * 2048;  // HALF_N columns x 128 K (fp8: 256 K)
+    static constexpr int E_HALF = (FP8 ? 2 : 1) * 16 * 128;
     static constexpr int E_BYTES = 2 * E_HALF;
+    static constexpr int META_STRIDE = FP8 ? 8 : 4;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + E_BYTES;
     static constexpr int RING_BYTES = STAGES * STAGE_BYTES;
     static constexpr int BAR_OFFSET = RING_BYTES;
@@ -887,16 +892,20 @@ struct Pair2Cfg {
     static constexpr int META1_COL = ACC1_COL + TILE_N;
     static constexpr int TMEM_COLS = 512;
     static constexpr int C_PITCH = TILE_N + 8;  // halves per staged output row (bank-shifted)
-    static_assert(META0_COL + 4 * STAGES <= ACC1_COL && META1_COL + 4 * STAGES <= TMEM_COLS, "TMEM overflow");
+    static_assert(META0_COL + META_STRIDE * STAGES <= ACC1_COL && META1_COL + META_STRIDE * STAGES <= TMEM_COLS,
+                  "TMEM overflow");
     static_assert(2 * kTileM * C_PITCH * 2 <= RING_BYTES, "output staging does not fit");
     static_assert(SMEM_ALLOC <= 232448, "shared memory overflow");
+    static_assert(!FP8 || ((B_BYTES / 2) % 1024 == 0 && STAGE_BYTES % 1024 == 0),
+                  "fp8 B halves must start on 1024-byte boundaries (128-byte swizzle atoms)");
 };
 
-template <int STAGES, bool EPI>
+template <int STAGES, bool EPI, bool FP8 = false>
 __global__ void __launch_bounds__(kPairThreads, 1)
 spmm24_pair2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmE, const PairParams p) {
-    using C_ = Pair2Cfg<STAGES>;
+    static_assert(EPI || !FP8, "the fp8 form always runs the epilogue (alpha)");
+    using C_ = Pair2Cfg<STAGES, FP8>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + C_::BAR_OFFSET);  // used in the leader only
@@ -953,8 +962,22 @@ spmm24_pair2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     auto load_weights = [&](uint8_t* st, uint32_t bar, int g) {
         ptx::tma_load_3d_pair(st, &tmA, bar, 0, band_h0, 8 * g, pol);
         ptx::tma_load_3d_pair(st + C_::A_HALF, &tmA, bar, 0, band_h1, 8 * g, pol);
-        ptx::tma_load_2d_pair(st + C_::A_BYTES + C_::B_BYTES, &tmE, bar, 128 * g, band_h0, pol);
-        ptx::tma_load_2d_pair(st + C_::A_BYTES + C_::B_BYTES + C_::E_HALF, &tmE, bar, 128 * g, band_h1, pol);
+        uint8_t* se = st + C_::A_BYTES + C_::B_BYTES;
+        if constexpr (FP8) {  // box (256 B, 8 bands, 2 groups) per half
+            ptx::tma_load_3d_pair(se, &tmE, bar, 0, band_h0, 2 * g, pol);
+            ptx::tma_load_3d_pair(se + C_::E_HALF, &tmE, bar, 0, band_h1, 2 * g, pol);
+        } else {
+            ptx::tma_load_2d_pair(se, &tmE, bar, 128 * g, band_h0, pol);
+            ptx::tma_load_2d_pair(se + C_::E_HALF, &tmE, bar, 128 * g, band_h1, pol);
+        }
+    };
+    auto load_acts = [&](uint8_t* st, uint32_t bar, int g) {
+        if constexpr (FP8) {
+            ptx::tma_load_2d_pair(st + C_::A_BYTES, &tmB, bar, 256 * g, 8 * strip0, pol);
+            ptx::tma_load_2d_pair(st + C_::A_BYTES + C_::B_BYTES / 2, &tmB, bar, 256 * g + 128, 8 * strip0, pol);
+        } else {
+            ptx::tma_load_4d_pair(st + C_::A_BYTES, &tmB, bar, 0, 2 * g, 0, strip0, pol);
+        }
     };
     if (warp == 0) {
         // ------------------------------------------------- TMA producer
@@ -965,9 +988,7 @@ spmm24_pair2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             }
             ptx::grid_dep_wait();
             SPMM24_STAMP(1);
-            for (int it = 0; it < pre; ++it)
-                ptx::tma_load_4d_pair(smem + it * C_::STAGE_BYTES + C_::A_BYTES, &tmB, full0 + 8u * it, 0, 2 * it, 0,
-                                      strip0, pol);
+            for (int it = 0; it < pre; ++it) load_acts(smem + it * C_::STAGE_BYTES, full0 + 8u * it, it);
             for (int it = pre; it < st_count; ++it) {
                 const int s = it % STAGES;
                 const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
@@ -979,13 +1000,14 @@ spmm24_pair2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                 const uint32_t bar = full0 + 8u * s;
                 if (leader) ptx::mbar_arrive_expect_tx(&full[s], 2 * C_::STAGE_BYTES);
                 load_weights(st, bar, it);
-                ptx::tma_load_4d_pair(st + C_::A_BYTES, &tmB, bar, 0, 2 * it, 0, strip0, pol);
+                load_acts(st, bar, it);
             }
         }
         __syncwarp();
     } else if (warp == 1 && leader) {
         // ---------------------------------- MMA issuer (leader CTA only)
-        const uint32_t idesc = pair_idesc<C_::TILE_N>() | ((EPI && p.epi.bf16) ? kIdescBf16 : 0u);
+        const uint32_t idesc = FP8 ? pair_idesc_fp8<C_::TILE_N>() | p.mma_fmt
+                                   : pair_idesc<C_::TILE_N>() | ((EPI && p.epi.bf16) ? kIdescBf16 : 0u);
         const uint32_t smem_base = ptx::smem_u32(smem);
         uint32_t accumulate = 0;
         for (int it = 0; it < st_count; ++it) {
@@ -1002,19 +1024,36 @@ spmm24_pair2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                 const uint32_t st = smem_base + s * C_::STAGE_BYTES;
                 const uint32_t stB = st + C_::A_BYTES;
                 const uint32_t stE = stB + C_::B_BYTES;
-                const uint32_t meta0 = tmem_base + C_::META0_COL + 4 * s;
-                const uint32_t meta1 = tmem_base + C_::META1_COL + 4 * s;
-                ptx::tmem_cp_128x128b_pair(meta0, smem_desc(stE, 0, 128));
-                ptx::tmem_cp_128x128b_pair(meta1, smem_desc(stE + C_::E_HALF, 0, 128));
+                const uint32_t meta0 = tmem_base + C_::META0_COL + C_::META_STRIDE * s;
+                const uint32_t meta1 = tmem_base + C_::META1_COL + C_::META_STRIDE * s;
+                if constexpr (FP8) {
+                    ptx::tmem_cp_128x128b_pair(meta0, smem_desc(stE, 0, 128));
+                    ptx::tmem_cp_128x128b_pair(meta0 + 4, smem_desc(stE + 2048, 0, 128));
+                    ptx::tmem_cp_128x128b_pair(meta1, smem_desc(stE + C_::E_HALF, 0, 128));
+                    ptx::tmem_cp_128x128b_pair(meta1 + 4, smem_desc(stE + C_::E_HALF + 2048, 0, 128));
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const uint64_t bdesc = smem_desc(stB + j * 512, 128, 2048);
-                    const uint32_t id = idesc | (uint32_t)(j & 1);
-                    ptx::mma_sp_f16_pair(tmem_base, smem_desc(st + j * 2048, 4 * 2048, 128), bdesc, meta0 + (j & 2),
-                                         id, accumulate);
-                    ptx::mma_sp_f16_pair(tmem_base + C_::ACC1_COL, smem_desc(st + C_::A_HALF + j * 2048, 4 * 2048, 128),
-                                         bdesc, meta1 + (j & 2), id, accumulate);
-                    accumulate = 1;
+                    for (int j = 0; j < 4; ++j) {
+                        const uint64_t bdesc = smem_desc_sw128(stB + (j >> 1) * (C_::B_BYTES / 2) + (j & 1) * 64);
+                        ptx::mma_sp_f8_pair(tmem_base, smem_desc(st + j * 4096, 2048, 128), bdesc, meta0 + 2 * j, idesc,
+                                            accumulate);
+                        ptx::mma_sp_f8_pair(tmem_base + C_::ACC1_COL, smem_desc(st + C_::A_HALF + j * 4096, 2048, 128),
+                                            bdesc, meta1 + 2 * j, idesc, accumulate);
+                        accumulate = 1;
+                    }
+                } else {
+                    ptx::tmem_cp_128x128b_pair(meta0, smem_desc(stE, 0, 128));
+                    ptx::tmem_cp_128x128b_pair(meta1, smem_desc(stE + C_::E_HALF, 0, 128));
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const uint64_t bdesc = smem_desc(stB + j * 512, 128, 2048);
+                        const uint32_t id = idesc | (uint32_t)(j & 1);
+                        ptx::mma_sp_f16_pair(tmem_base, smem_desc(st + j * 2048, 4 * 2048, 128), bdesc,
+                                             meta0 + (j & 2), id, accumulate);
+                        ptx::mma_sp_f16_pair(tmem_base + C_::ACC1_COL,
+                                             smem_desc(st + C_::A_HALF + j * 2048, 4 * 2048, 128), bdesc,
+                                             meta1 + (j & 2), id, accumulate);
+                        accumulate = 1;
+                    }
                 }
                 ptx::tc_commit_pair_mc(&empty[s], (uint16_t)0x3);  // frees ring slot s in both CTAs
             }
@@ -1033,8 +1072,8 @@ spmm24_pair2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         __syncwarp();
         const int quad = warp & 3;
         const int row = quad * 32 + lane;
-        constexpr int NCH16 = C_::TILE_N / 16;          // 15 chunks of 16 columns per row
-        const int c_begin = (warp >> 2) ? (NCH16 + 1) / 2 : 0;  // warps 0-3: chunks 0-7, warps 4-7: 8-14
+        constexpr int NCH16 = C_::TILE_N / 16;          // chunks of 16 columns per row (15; fp8 14)
+        const int c_begin = (warp >> 2) ? (NCH16 + 1) / 2 : 0;  // warps 0-3 take the first half
         const int c_end = (warp >> 2) ? NCH16 : (NCH16 + 1) / 2;
         __half* cst = reinterpret_cast<__half*>(smem);
 #pragma unroll 1
@@ -1070,8 +1109,8 @@ spmm24_pair2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         ptx::tc_fence_before();
         ptx::named_barrier(kBarEpi, kPairThreads);
         ptx::grid_dep_wait();  // C may be in use by the previous grid
-        constexpr int LPR = C_::TILE_N / 8;  // 30 threads per row
-        constexpr int RPP = kPairThreads / LPR;  // 8 rows per pass (240 threads)
+        constexpr int LPR = C_::TILE_N / 8;      // threads per row (30; fp8 28)
+        constexpr int RPP = kPairThreads / LPR;  // rows per pass (8; fp8 9)
         const int etid = threadIdx.x;
         if (etid < LPR * RPP) {
             const int chunk = etid % LPR;

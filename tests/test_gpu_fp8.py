@@ -328,3 +328,17 @@ def test_fp8_random_case(cuda_device, case):
     M, N, K, split, fa, fb, bf16, act, res, packed, bias, alpha = case
     _run(cuda_device, M, N, K, fmt_a=fa, fmt_b=fb, split=split, bf16=bf16, act=act, residual=res, packed=packed,
          bias=bias, alpha=alpha, seed=M * 5 + N * 3 + K)
+
+
+@pytest.mark.parametrize("shape", [(512, 224, 256), (1024, 448, 1024), (592, 500, 768), (2048, 2048, 2048)],
+                         ids=lambda s: "x".join(map(str, s)))
+def test_fp8_two_m_half_pair(cuda_device, monkeypatch, shape):
+    """The fp8 pair kernel with two M halves (512 x 224 tiles): E4M3 and
+    E5M2, exact integer inputs, the epilogue, and calls with a residual
+    (which keep the 256 x 256 pair kernel)."""
+    monkeypatch.setenv("SPMM24_PAIR2", "1")
+    M, N, K = shape
+    _run(cuda_device, M, N, K, seed=M + N + K)
+    _run(cuda_device, M, N, K, integer=True, fmt_a=1, fmt_b=0, seed=M + 2 * N)
+    _run(cuda_device, M, N, K, bf16=True, bias=True, act=2, alpha=0.02, fmt_b=1, seed=M + 3 * N)
+    _run(cuda_device, M, N, K, residual=True, act=1, seed=M + 4 * N)
