@@ -19,6 +19,7 @@
 
 #include <cstdint>
 
+#include "ptx_sm100.cuh"
 #include "spmm24/SpMM_API.h"
 #include "spmm24_host.h"
 
@@ -158,6 +159,8 @@ __global__ void __launch_bounds__(kPackThreads) pack_a_kernel(const uint16_t* __
     const int q0 = blockIdx.x * kTileBlocks;
     const int nq = min(kTileBlocks, nbc - q0);  // a multiple of 4 (K % 64 == 0)
     const uint16_t* base = dense + (size_t)band0 * 16 * K + (size_t)q0 * 16;
+    ptx::grid_dep_wait();  // launched with programmatic serialization: the previous grid may write the input
+    if (threadIdx.x == 0) ptx::grid_dep_launch();
     if (nq == kTileBlocks && nb == kPackBands) {  // full tile: 32 chunks of 16 bytes per row
         uint4 v[kLoadsPerThread];
 #pragma unroll
@@ -309,6 +312,8 @@ __global__ void __launch_bounds__(kPackThreads) pack_a_fp8_kernel(const uint8_t*
     const int q0 = blockIdx.x * kTileBlocks;
     const int nq = min(kTileBlocks, nbc - q0);  // a multiple of 4 (K % 128 == 0)
     const uint8_t* base = dense + (size_t)band0 * 16 * K + (size_t)q0 * 32;
+    ptx::grid_dep_wait();  // launched with programmatic serialization: the previous grid may write the input
+    if (threadIdx.x == 0) ptx::grid_dep_launch();
     uint4 v[kLoadsPerThread];
     if (nq == kTileBlocks && nb == kPackBands) {  // full tile: 32 chunks of 16 bytes per row
 #pragma unroll
@@ -405,6 +410,25 @@ __global__ void __launch_bounds__(kPackThreads) pack_b_kernel(const uint16_t* __
 
 bool misaligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) != 0; }
 
+// Launches a packer kernel with programmatic stream serialization: its CTAs
+// may be scheduled while the previous kernel in the stream finishes (each
+// waits for that grid before reading), which hides the launch gap between
+// back-to-back packer calls.
+template <class... KArgs, class... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, cudaStream_t stream, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kPackThreads, 1, 1);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
 }  // namespace
 }  // namespace spmm24
 
@@ -421,9 +445,8 @@ extern "C" cudaError_t spmm24_pack_a_device(cudaStream_t stream, const void* den
     dim3 grid((unsigned)((nbc + kTileBlocks - 1) / kTileBlocks), (unsigned)((M / 16 + kPackBands - 1) / kPackBands));
     if (grid.y > 65535) return record_invalid("M too large");
     if (prune < SPMM24_PRUNE_NONE || prune > SPMM24_PRUNE_BF16) return record_invalid("unknown prune mode");
-    pack_a_kernel<<<grid, kPackThreads, 0, stream>>>(static_cast<const uint16_t*>(dense_a), M, K, prune,
-                                                     static_cast<uint16_t*>(values_out), meta_out, bad_blocks);
-    return cudaGetLastError();
+    return launch_pdl(pack_a_kernel, grid, stream, static_cast<const uint16_t*>(dense_a), M, K, prune,
+                      static_cast<uint16_t*>(values_out), meta_out, bad_blocks);
 }
 
 extern "C" cudaError_t spmm24_pack_a_fp8_device(cudaStream_t stream, const void* dense_a, int M, int K, int prune,
@@ -440,10 +463,8 @@ extern "C" cudaError_t spmm24_pack_a_fp8_device(cudaStream_t stream, const void*
     dim3 grid((unsigned)((nbc + kTileBlocks - 1) / kTileBlocks), (unsigned)((M / 16 + kPackBands - 1) / kPackBands));
     if (grid.y > 65535) return record_invalid("M too large");
     const uint32_t top = prune == 1 ? 0x7eu : prune == 2 ? 0x7cu : 0u;
-    pack_a_fp8_kernel<<<grid, kPackThreads, 0, stream>>>(static_cast<const uint8_t*>(dense_a), M, K, top,
-                                                         static_cast<uint8_t*>(values_out),
-                                                         static_cast<uint8_t*>(meta_out), bad_blocks);
-    return cudaGetLastError();
+    return launch_pdl(pack_a_fp8_kernel, grid, stream, static_cast<const uint8_t*>(dense_a), M, K, top,
+                      static_cast<uint8_t*>(values_out), static_cast<uint8_t*>(meta_out), bad_blocks);
 }
 
 namespace spmm24 {
