@@ -267,7 +267,8 @@ def run_ours(args, rank, world, local_rank):
         coff += cs
         calls.append({"M": r1 - r0, "N": N, "K": K, "A": A, "E": E, "B": B, "C": C, "M_full": M,
                       "boff": boff - bs, "coff": coff - cs,
-                      "split": spmm24.select_config(max(16, r1 - r0), N, K // 2 if fp8 else K, 0)["split_k"]})
+                      "split": (spmm24.select_config_fp8 if fp8 else spmm24.select_config)(max(16, r1 - r0), N, K,
+                                                                                          0)["split_k"]})
     weight_bytes = sum(c["A"].numel() * c["A"].element_size() + c["E"].numel() * c["E"].element_size() for c in calls)
     stream = torch.cuda.current_stream(dev)
     h_stream = int(stream.cuda_stream)
@@ -1121,7 +1122,7 @@ def run_single(args):
             raise SystemExit(f"launch failed {rc}")
     torch.cuda.synchronize(dev)
     print(json.dumps({"single": [M, N, K], "dtype": args.dtype,
-                      "config": spmm24.select_config(M, N, K // 2 if fp8 else K, split),
+                      "config": spmm24.select_config_fp8(M, N, K, split) if fp8 else spmm24.select_config(M, N, K, split),
                       "status": spmm24.device_status(0)}))
 
 

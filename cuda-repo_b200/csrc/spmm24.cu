@@ -649,6 +649,39 @@ cudaError_t launch_impl(cudaStream_t stream, const void* A, const void* B, const
 // The fp8 SpMM runs the cluster kernel with a stage of 256 logical K; its A
 // values occupy the bytes of a 16-bit A with K/2, so the plan and the A
 // descriptor are those of K/2.
+//
+// Automatic splits stop at 5: measured on the decode chain (M = 4096, K =
+// 4096 and 11008, N <= 32), five K slices beat eight by 4-8% per call (a
+// cheaper cluster reduction and more SM slots left to the next launch's
+// early CTAs), and 11008-row layers pick 3 either way.  Wide N takes the CTA
+// pair as for 16-bit operands (its stage is 256 K: K % 256), and the
+// two-M-half pair (512 x 224) when its waves cost less and the epilogue has
+// no residual and no packed output (pair2_ok).
+template <class V>
+int fp8_smem() {
+    return ClusterCfg<V::kTileN, V::kStages, true>::SMEM_ALLOC;
+}
+
+Plan plan_fp8(int M, int N, int K, int split_k, int sms, bool pair2_ok) {
+    const int Kh = K / 2;
+    Plan pl = make_plan(M, N, Kh, split_k, sms, false, Kh % 128 == 0, 5, false);
+    if (pl.path == Path::kPair) {
+        pl.smem = PairC8::SMEM_ALLOC;
+        if (pl.split == 1 && split_k <= 1 && pair2_ok)
+            maybe_pair2(pl, M, N, sms, Pair2C8::TILE_N, kPair2Stages, Pair2C8::SMEM_ALLOC);
+    } else if (pl.shallow) {
+        pl.smem = pl.tile_n == 16 ? fp8_smem<CV16s>() : fp8_smem<CV32s>();
+    } else {
+        switch (pl.tile_n) {
+            case 16: pl.smem = fp8_smem<CV16>(); break;
+            case 32: pl.smem = fp8_smem<CV32>(); break;
+            case 64: pl.smem = fp8_smem<CV64>(); break;
+            case 128: pl.smem = fp8_smem<CV128>(); break;
+            default: pl.smem = fp8_smem<CV256>(); break;
+        }
+    }
+    return pl;
+}
 cudaError_t launch_fp8_impl(cudaStream_t stream, const void* A, const void* B, const void* E, void* C, int M, int N,
                             int K, int split_k, unsigned flags, const spmm24_epilogue* user_epi) {
     g_last_error[0] = '\0';
@@ -670,15 +703,8 @@ cudaError_t launch_fp8_impl(cudaStream_t stream, const void* A, const void* B, c
     e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     const int Kh = K / 2;  // the 16-bit-equivalent K of the A bytes
-    // Automatic splits stop at 5: measured on the decode chain (M = 4096,
-    // K = 4096 and 11008, N <= 32), five K slices beat eight by 4-8% per call
-    // (a cheaper cluster reduction and more SM slots left to the next
-    // launch's early CTAs), and 11008-row layers pick 3 either way.  Wide N
-    // takes the CTA pair as for 16-bit operands (its stage is 256 K: K % 256).
-    Plan pl = make_plan(M, N, Kh, split_k, sm_count(dev), false, Kh % 128 == 0, 5, false);
+    Plan pl = plan_fp8(M, N, K, split_k, sm_count(dev), !epi.residual && !epi.packed);
     const bool pair = pl.path == Path::kPair;
-    if (pair && pl.split == 1 && split_k <= 1 && !epi.residual && !epi.packed)
-        maybe_pair2(pl, M, N, sm_count(dev), Pair2C8::TILE_N, kPair2Stages, Pair2C8::SMEM_ALLOC);
 
     CUtensorMap ta, tb, te;
     {
@@ -1062,24 +1088,46 @@ extern "C" cudaError_t spmm24_ipc_close(void* dev_ptr) {
 
 extern "C" size_t spmm24_workspace_bytes(int, int, int, int) { return 0; }
 
-extern "C" int spmm24_select_config(int M, int N, int K, int split_k, spmm24_config* out) {
-    if (!out || M <= 0 || N <= 0 || K <= 0 || M % 16 || K % 64 || split_k < 0) return -1;
+namespace spmm24 {
+namespace {
+int current_sms() {
     int dev = 0;
-    int sms = (cudaGetDevice(&dev) == cudaSuccess) ? spmm24::sm_count(dev) : 148;
+    int sms = (cudaGetDevice(&dev) == cudaSuccess) ? sm_count(dev) : 148;
     if (sms <= 0) sms = 148;
     cudaGetLastError();
-    const spmm24::Plan pl = spmm24::make_plan(M, N, K, split_k, sms);
+    return sms;
+}
+void fill_config(const Plan& pl, int stage_k, spmm24_config* out);
+}  // namespace
+}  // namespace spmm24
+
+extern "C" int spmm24_select_config(int M, int N, int K, int split_k, spmm24_config* out) {
+    if (!out || M <= 0 || N <= 0 || K <= 0 || M % 16 || K % 64 || split_k < 0) return -1;
+    spmm24::fill_config(spmm24::make_plan(M, N, K, split_k, spmm24::current_sms()), 128, out);
+    return 0;
+}
+
+extern "C" int spmm24_select_config_fp8(int M, int N, int K, int split_k, spmm24_config* out) {
+    if (!out || M <= 0 || N <= 0 || K <= 0 || M % 16 || K % 128 || split_k < 0) return -1;
+    spmm24::fill_config(spmm24::plan_fp8(M, N, K, split_k, spmm24::current_sms(), true), 256, out);
+    return 0;
+}
+
+namespace spmm24 {
+namespace {
+void fill_config(const Plan& pl, int stage_k, spmm24_config* out) {
     out->tile_m = pl.path == spmm24::Path::kPair ? (pl.pair2 ? 4 : 2) * spmm24::kTileM : spmm24::kTileM;
     out->tile_n = pl.tile_n;
-    out->stage_k = 128;
+    out->stage_k = stage_k;
     out->stages = pl.stages;
     out->split_k = pl.path == spmm24::Path::kStreamK ? 0 : pl.split;
     out->grid_ctas = pl.grid;
     out->smem_bytes = pl.smem;
     out->stream_k = pl.path == spmm24::Path::kStreamK ? 1 : 0;
     out->cta_pair = pl.path == spmm24::Path::kPair ? 1 : 0;
-    return 0;
 }
+}  // namespace
+}  // namespace spmm24
 
 extern "C" cudaError_t spmm24_device_status(int device, uint32_t* status_out) {
     if (!status_out) return cudaErrorInvalidValue;

@@ -121,6 +121,8 @@ _lib.spmm24_pack_a_fp8_device.restype = ctypes.c_int
 _lib.spmm24_workspace_bytes.argtypes = [ctypes.c_int] * 4
 _lib.spmm24_workspace_bytes.restype = ctypes.c_size_t
 _lib.spmm24_select_config.argtypes = [ctypes.c_int] * 4 + [ctypes.POINTER(SpmmConfig)]
+_lib.spmm24_select_config_fp8.argtypes = [ctypes.c_int] * 4 + [ctypes.POINTER(SpmmConfig)]
+_lib.spmm24_select_config_fp8.restype = ctypes.c_int
 _lib.spmm24_select_config.restype = ctypes.c_int
 _lib.spmm24_device_status.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_uint32)]
 _lib.spmm24_device_status.restype = ctypes.c_int
@@ -236,6 +238,14 @@ def select_config(M: int, N: int, K: int, split_k: int = 0) -> dict:
     cfg = SpmmConfig()
     if _lib.spmm24_select_config(M, N, K, split_k, ctypes.byref(cfg)) != 0:
         raise ValueError("unsupported shape")
+    return {n: getattr(cfg, n) for n, _ in SpmmConfig._fields_}
+
+
+def select_config_fp8(M: int, N: int, K: int, split_k: int = 0) -> dict:
+    """spmm24_select_config_fp8: the configuration spmm24_launch_fp8 uses."""
+    cfg = SpmmConfig()
+    if _lib.spmm24_select_config_fp8(M, N, K, split_k, ctypes.byref(cfg)) != 0:
+        raise ValueError("unsupported shape (K % 128)")
     return {n: getattr(cfg, n) for n, _ in SpmmConfig._fields_}
 
 

@@ -339,6 +339,10 @@ typedef struct spmm24_config {
     int cta_pair;    /* 1: 256 x 256 tiles on CTA pairs (cta_group::2 MMAs) */
 } spmm24_config;
 int spmm24_select_config(int M, int N, int K, int split_k, spmm24_config* out);
+/* The same for spmm24_launch_fp8 (stage_k 256: a stage carries 256 logical
+ * K of fp8 operands; K % 128 == 0), for an epilogue without a residual or a
+ * packed output. */
+int spmm24_select_config_fp8(int M, int N, int K, int split_k, spmm24_config* out);
 
 /* Row range of shard `index` of `parts` when an M x K layer is split along
  * M across devices (no reduction needed: each shard is a contiguous slice

@@ -182,7 +182,7 @@ def test_fp8_pair_matches_oracle(cuda_device, shape):
     import spmm24
 
     M, N, K = shape
-    assert spmm24.select_config(M, N, K // 2)["cta_pair"] == 1
+    assert spmm24.select_config_fp8(M, N, K)["cta_pair"] == 1
     _run(cuda_device, M, N, K, seed=M + 3 * N + K)
 
 
