@@ -864,14 +864,17 @@ spmm24_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
 // CTA for 15.7 MFLOP (dense-equivalent) instead of 50 KB for 8.4 MFLOP,
 // so the same shared-memory bytes in flight feed the tensor core 1.4x
 // longer.  Row-major output; EPI adds alpha, bias, activation and bf16
-// (no residual, no packed output, no gather); no K split.  FP8: 512 x 224
-// tiles (two 128-byte-swizzled B halves of 112 rows per stage, two 128-K
-// metadata groups per half: the wider metadata ring leaves room for two
-// 224-column accumulators in TMEM); always EPI.
+// (no residual, no packed output, no gather); no K split.  FP8: two
+// 128-byte-swizzled B halves of 120 rows per stage and two 128-K metadata
+// groups per M half; the metadata ring in TMEM has two slots instead of
+// one per stage (the copy into a slot is issued after the MMAs that read
+// it two stages earlier, and tcgen05 operations of one thread execute in
+// issue order), which leaves room for the two 240-column accumulators;
+// always EPI.
 template <int STAGES, bool FP8 = false>
 struct Pair2Cfg {
     static constexpr bool kFp8 = FP8;
-    static constexpr int HALF_N = FP8 ? 112 : 120;       // columns of B / C per CTA
+    static constexpr int HALF_N = 120;                   // columns of B / C per CTA
     static constexpr int TILE_N = 2 * HALF_N;            // columns per pair
     static constexpr int TILE_M = 4 * kTileM;            // rows per pair
     static constexpr int A_HALF = 8 * 8 * 256;           // 128 rows x 128 logical K (fp8: 256)
@@ -879,7 +882,8 @@ struct Pair2Cfg {
     static constexpr int B_BYTES = (HALF_N / 8) * 2048;  // HALF_N columns x 128 K (fp8: 256 K)
     static constexpr int E_HALF = (FP8 ? 2 : 1) * 16 * 128;
     static constexpr int E_BYTES = 2 * E_HALF;
-    static constexpr int META_STRIDE = FP8 ? 8 : 4;
+    static constexpr int META_STRIDE = FP8 ? 8 : 4;      // TMEM columns per metadata slot
+    static constexpr int META_SLOTS = FP8 ? 2 : STAGES;  // metadata ring slots per M half
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + E_BYTES;
     static constexpr int RING_BYTES = STAGES * STAGE_BYTES;
     static constexpr int BAR_OFFSET = RING_BYTES;
@@ -892,7 +896,7 @@ struct Pair2Cfg {
     static constexpr int META1_COL = ACC1_COL + TILE_N;
     static constexpr int TMEM_COLS = 512;
     static constexpr int C_PITCH = TILE_N + 8;  // halves per staged output row (bank-shifted)
-    static_assert(META0_COL + META_STRIDE * STAGES <= ACC1_COL && META1_COL + META_STRIDE * STAGES <= TMEM_COLS,
+    static_assert(META0_COL + META_STRIDE * META_SLOTS <= ACC1_COL && META1_COL + META_STRIDE * META_SLOTS <= TMEM_COLS,
                   "TMEM overflow");
     static_assert(2 * kTileM * C_PITCH * 2 <= RING_BYTES, "output staging does not fit");
     static_assert(SMEM_ALLOC <= 232448, "shared memory overflow");
@@ -1024,8 +1028,9 @@ spmm24_pair2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                 const uint32_t st = smem_base + s * C_::STAGE_BYTES;
                 const uint32_t stB = st + C_::A_BYTES;
                 const uint32_t stE = stB + C_::B_BYTES;
-                const uint32_t meta0 = tmem_base + C_::META0_COL + C_::META_STRIDE * s;
-                const uint32_t meta1 = tmem_base + C_::META1_COL + C_::META_STRIDE * s;
+                const uint32_t slot = (uint32_t)(it % C_::META_SLOTS);
+                const uint32_t meta0 = tmem_base + C_::META0_COL + C_::META_STRIDE * slot;
+                const uint32_t meta1 = tmem_base + C_::META1_COL + C_::META_STRIDE * slot;
                 if constexpr (FP8) {
                     ptx::tmem_cp_128x128b_pair(meta0, smem_desc(stE, 0, 128));
                     ptx::tmem_cp_128x128b_pair(meta0 + 4, smem_desc(stE + 2048, 0, 128));

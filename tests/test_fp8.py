@@ -151,17 +151,18 @@ def test_fp8_symbols_exported():
 
 
 def test_select_config_fp8():
-    """The fp8 plan: 256-K stages, automatic splits capped at 5, the fp8
-    two-M-half pair tile (512 x 224) when its waves cost less."""
+    """The fp8 plan: 256-K stages, automatic splits capped at 5, the
+    two-M-half pair tile (512 x 240) when its waves cost less."""
     import spmm24
 
     c = spmm24.select_config_fp8(4096, 16, 4096)
     assert (c["stage_k"], c["tile_n"], c["split_k"], c["grid_ctas"]) == (256, 16, 5, 160)
     assert spmm24.select_config_fp8(11008, 16, 4096)["split_k"] == 3
     c = spmm24.select_config_fp8(11008, 4096, 4096)
-    assert (c["cta_pair"], c["tile_m"], c["tile_n"], c["grid_ctas"]) == (1, 512, 224, 2 * 22 * 19)
+    assert (c["cta_pair"], c["tile_m"], c["tile_n"], c["grid_ctas"]) == (1, 512, 240, 2 * 22 * 18)
     c = spmm24.select_config_fp8(4096, 4096, 4096)
-    assert (c["cta_pair"], c["tile_m"], c["tile_n"]) == (1, 256, 256)
+    assert (c["cta_pair"], c["tile_m"], c["tile_n"]) == (1, 512, 240)
+    assert spmm24.select_config_fp8(4096, 512, 4096)["tile_m"] == 256
     assert spmm24.select_config_fp8(512, 16, 4096, 3)["split_k"] == 3
     with pytest.raises(ValueError):
         spmm24.select_config_fp8(512, 16, 192)

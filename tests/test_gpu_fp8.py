@@ -330,10 +330,12 @@ def test_fp8_random_case(cuda_device, case):
          bias=bias, alpha=alpha, seed=M * 5 + N * 3 + K)
 
 
-@pytest.mark.parametrize("shape", [(512, 224, 256), (1024, 448, 1024), (592, 500, 768), (2048, 2048, 2048)],
+@pytest.mark.parametrize("shape", [(512, 240, 256), (1024, 480, 1024), (592, 500, 768), (2048, 2048, 2048),
+                                   (1024, 720, 2560)],
                          ids=lambda s: "x".join(map(str, s)))
 def test_fp8_two_m_half_pair(cuda_device, monkeypatch, shape):
-    """The fp8 pair kernel with two M halves (512 x 224 tiles): E4M3 and
+    """The fp8 pair kernel with two M halves (512 x 240 tiles, a two-slot
+    metadata ring in TMEM; K = 2560 runs ten stages through it): E4M3 and
     E5M2, exact integer inputs, the epilogue, and calls with a residual
     (which keep the 256 x 256 pair kernel)."""
     monkeypatch.setenv("SPMM24_PAIR2", "1")
