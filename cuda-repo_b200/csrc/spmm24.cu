@@ -246,9 +246,25 @@ Plan make_plan(int M, int N, int K, int split_k, int sms, bool plain = true, boo
         if (p.stages_total < 2) ps = 1;
         p.split = ps;
         p.grid = 2 * ps * (int)ptiles;
-        if (pair2_ok && ps == 1 && split_k <= 1)
-            maybe_pair2(p, M, N, sms, Pair2C::TILE_N, kPair2Stages, Pair2C::SMEM_ALLOC);
-        return p;
+        // One pair tile across N (N <= 256) and pairs for less than three
+        // quarters of the SMs: 128-wide cluster tiles with a K split fill more
+        // of the GPU.  Measured (chains of one shape): 1024 x 256 x 8192
+        // 23.5 -> 12.9 us, 3584 x 256 x 8192 24.9 -> 19.6 us, 1024 x 256 x
+        // 28672 51.9 -> 27.9 us (the per-GPU shards of M-sharded 70B layers);
+        // 8192 x 256 x 8192 stays on the pair (29.8 against 32.2 us).
+        const bool few = N <= 256 && split_k == 0 && (long long)p.grid < (3LL * sms) / 4;
+        if (!(few && pair_env != 1 && env_int("SPMM24_PAIR2", -1) != 1)) {
+            if (pair2_ok && ps == 1 && split_k <= 1)
+                maybe_pair2(p, M, N, sms, Pair2C::TILE_N, kPair2Stages, Pair2C::SMEM_ALLOC);
+            return p;
+        }
+        p = Plan{};
+        p.tile_n = tn;
+        p.m_tiles = (M + kTileM - 1) / kTileM;
+        p.n_tiles = (N + tn - 1) / tn;
+        p.stages_total = (K / 64 + 1) / 2;
+        p.shallow = tn <= 32 && stages_env != 8;
+        max_split = std::min(max_split, 4);  // measured: 4 beats 8 for 128 x 128 tiles (cl4 12.9 us, cl8 19.5 us)
     }
     p.path = Path::kCluster;
     if (p.shallow) {

@@ -178,6 +178,11 @@ def test_select_config_picks_tiles_and_splits():
     assert spmm24.select_config(11008, 512, 4096)["tile_m"] == 512    # 1 wave against 2
     assert spmm24.select_config(4096, 512, 4096)["tile_m"] == 256     # 1 wave either way
     assert spmm24.select_config(2048, 2048, 2048)["tile_m"] == 256
+    # one pair tile across N and pairs for < 3/4 of the SMs: split-K clusters (split <= 4)
+    c = spmm24.select_config(1024, 256, 8192)
+    assert (c["cta_pair"], c["tile_n"], c["split_k"]) == (0, 128, 4)
+    assert spmm24.select_config(3584, 256, 8192)["split_k"] == 2
+    assert spmm24.select_config(8192, 256, 8192)["cta_pair"] == 1     # 128 pair CTAs: stays
     assert spmm24.select_config(4096, 512, 4160)["cta_pair"] == 0  # K % 128 != 0
     assert spmm24.select_config(4096, 512, 4096, 2)["cta_pair"] == 0  # explicit split-K
     # explicit split honoured, clamped to the number of 128-K stages

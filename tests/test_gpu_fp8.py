@@ -178,15 +178,17 @@ PAIR_SHAPES = [
 
 
 @pytest.mark.parametrize("shape", PAIR_SHAPES, ids=lambda s: "x".join(map(str, s)))
-def test_fp8_pair_matches_oracle(cuda_device, shape):
+def test_fp8_pair_matches_oracle(cuda_device, monkeypatch, shape):
     import spmm24
 
+    monkeypatch.setenv("SPMM24_PAIR", "1")  # also the few-tile shapes the picker gives to split-K clusters
     M, N, K = shape
     assert spmm24.select_config_fp8(M, N, K)["cta_pair"] == 1
     _run(cuda_device, M, N, K, seed=M + 3 * N + K)
 
 
-def test_fp8_pair_integer_exact_and_formats(cuda_device):
+def test_fp8_pair_integer_exact_and_formats(cuda_device, monkeypatch):
+    monkeypatch.setenv("SPMM24_PAIR", "1")
     _run(cuda_device, 512, 256, 1024, integer=True, seed=51)
     _run(cuda_device, 256, 512, 512, integer=True, fmt_a=1, fmt_b=0, seed=52)
     _run(cuda_device, 512, 264, 768, fmt_a=0, fmt_b=1, seed=53)
@@ -196,12 +198,14 @@ def test_fp8_pair_integer_exact_and_formats(cuda_device):
 def test_fp8_pair_k_split(cuda_device, monkeypatch):
     """Two pairs per tile, each half of K, partial exchanged on chip."""
     monkeypatch.setenv("SPMM24_PAIR_SPLIT", "2")
+    monkeypatch.setenv("SPMM24_PAIR", "1")
     _run(cuda_device, 512, 512, 4096, seed=61)
     _run(cuda_device, 256, 256, 2816, seed=62)  # odd number of 256-K stages
     _run(cuda_device, 512, 256, 2048, bias=True, act=3, alpha=0.5, seed=63)
 
 
-def test_fp8_pair_epilogue(cuda_device):
+def test_fp8_pair_epilogue(cuda_device, monkeypatch):
+    monkeypatch.setenv("SPMM24_PAIR", "1")
     _run(cuda_device, 512, 256, 1024, bf16=True, bias=True, residual=True, alpha=0.25, act=2, seed=71)
     _run(cuda_device, 256, 264, 512, residual=True, packed=True, act=1, seed=72)
 

@@ -170,6 +170,7 @@ def test_cta_pair_kernel(cuda_device, monkeypatch, shape, split):
 
     monkeypatch.setenv("SPMM24_PAIR_SPLIT", str(split))
     monkeypatch.setenv("SPMM24_PAIR2", "0")
+    monkeypatch.setenv("SPMM24_PAIR", "1")  # also the few-tile shapes the picker gives to split-K clusters
     M, N, K = shape
     cfg = spmm24.select_config(M, N, K)
     assert cfg["cta_pair"] == 1 and cfg["tile_n"] == 256 and cfg["split_k"] == (split if K >= 256 else 1)
@@ -195,6 +196,19 @@ def test_cta_pair_two_m_halves(cuda_device, monkeypatch, shape):
     cfg = spmm24.select_config(M, N, K)
     assert cfg["cta_pair"] == 1 and cfg["tile_m"] == 512 and cfg["tile_n"] == 240
     check(make_problem(M, N, K, seed=5 * M + N), 0, cuda_device)
+
+
+@pytest.mark.parametrize("shape", [(1024, 256, 8192), (3584, 256, 2048), (256, 200, 1024), (512, 136, 4096)],
+                         ids=lambda s: "x".join(map(str, s)))
+def test_few_tile_wide_n_takes_split_k_clusters(cuda_device, shape):
+    """N <= 256 with pairs for less than three quarters of the SMs: the
+    picker takes 128-wide cluster tiles with a K split (at most 4)."""
+    import spmm24
+
+    M, N, K = shape
+    cfg = spmm24.select_config(M, N, K)
+    assert cfg["cta_pair"] == 0 and cfg["tile_n"] == 128 and 1 <= cfg["split_k"] <= 4
+    check(make_problem(M, N, K, seed=M + 11 * N), 0, cuda_device)
 
 
 def test_cta_pair_forced_small_n(cuda_device, monkeypatch):
