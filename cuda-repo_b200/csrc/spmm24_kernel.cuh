@@ -4,7 +4,7 @@
 // and the separate split-K pass SplitK_Reduction (src/reduce_Kernel.cuh:27).
 // Formats and the tcgen05 mapping are described in spmm24_common.cuh.
 //
-// Three kernels share the stage layout and the MMA issue:
+// Four kernels share the stage layout and the MMA issue:
 //
 //   spmm24_cluster_kernel  one 128 x N_TILE tile per CTA; a split-K request
 //       of S becomes a thread-block cluster of S CTAs along K whose fp32
@@ -19,6 +19,12 @@
 //       sends its partial accumulator to pair 0 through distributed shared
 //       memory.
 //
+//   spmm24_pair2_kernel  a CTA pair computing a 512 x 240 tile: each CTA
+//       holds two 128-row halves of A and 120 columns of B, and the leader
+//       issues two M=256 MMAs per K step that share the B tile -- 1.87x the
+//       FLOPs per stage for 1.33x the bytes of the 256 x 256 pair, chosen for
+//       wide N when its waves of pairs cost less.
+//
 //   spmm24_streamk_kernel  a persistent grid (one CTA per SM) in which every
 //       CTA takes an equal share of the (tile, 128-K stage) units, walked
 //       tile-major.  A tile shared by several CTAs is finished by the CTA
@@ -32,7 +38,8 @@
 // The cluster and pair kernels come in two instantiations: the plain fp16
 // row-major SpMM, and EPI (alpha, bias, activation, residual, bf16, packed
 // output, fused all-gather), kept apart because the epilogue of every tile
-// is on the critical path.
+// is on the critical path.  All but stream-K also come in an FP8 form (OCP
+// E4M3 / E5M2 operands, tcgen05.mma.sp kind::f8f6f4, stages of 256 K).
 //
 // Roles (192 threads; the pair kernel 256):
 //   warp 0     TMA producer (lane 0)
