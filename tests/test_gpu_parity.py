@@ -270,6 +270,39 @@ def test_prefill_shape_row_sample(cuda_device):
     assert within_tolerance(stats), stats
 
 
+@pytest.mark.parametrize("M,N,K", [(28672, 16, 8192), (8192, 256, 28672), (28672, 4096, 8192)])
+def test_llama70b_full_size_row_sample(cuda_device, M, N, K):
+    """BASELINE config 4's largest layers at full size (the cluster kernel
+    with split-K, the CTA pair with its K split, the two-M-half pair),
+    checked on a seeded sample of rows."""
+    p = make_problem(M, N, K, seed=8, a_scale=0.01, b_dist="normal")
+    got = run_gpu(p, 0, cuda_device).reshape(M, N)
+    rows = np.sort(np.random.default_rng(2).choice(M, 96, replace=False))
+    stats = compare(got[rows].reshape(-1), oracle_c(p, rows))
+    assert within_tolerance(stats), stats
+
+
+def test_long_k_integer_exact(cuda_device):
+    """K = 65536 (512 stages of 128 K, split across a cluster) with A = +-1
+    on a random 2:4 mask and B in {-1, 0, 1}: every partial sum is an exact
+    integer in fp32, so C must equal the rounded exact product bit for bit."""
+    M, N, K = 256, 16, 65536
+    rng = np.random.default_rng(9)
+    a = np.where(rng.random(M * K) < 0.5, 0x3C00, 0xBC00).astype(np.uint16)  # +-1.0
+    a = O.random_mask_2of4(a, M, K, 99)
+    b = np.array([0xBC00, 0x0000, 0x3C00], dtype=np.uint16)[rng.integers(0, 3, K * N)]
+    p = pack_problem(M, N, K, a, b)
+    got = run_gpu(p, 0, cuda_device)
+    ref = O.f32_to_f16_bits(oracle_c(p).reshape(-1))
+    assert np.array_equal(got.reshape(-1), ref)
+
+
+def test_many_row_tiles(cuda_device):
+    """M = 65536 (512 row tiles on the grid's third dimension), short K."""
+    p = make_problem(65536, 16, 256, seed=10)
+    check(p, 0, cuda_device)
+
+
 def test_random_mask_square(cuda_device):
     """BASELINE config 5 inputs (U(-1,1) with a uniformly random 2:4 mask)."""
     p = make_problem(1024, 1024, 1024, seed=5, a_dist="uniform", mask="random")
