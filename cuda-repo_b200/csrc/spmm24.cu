@@ -946,6 +946,10 @@ struct BarrierArgs {
 __global__ void spmm24_gather_barrier_kernel(BarrierArgs a) {
     const int t = threadIdx.x;
     ptx::grid_dep_wait();
+    // The next kernel in the stream may be scheduled now (its weight
+    // prefetch then overlaps this wait); it still waits for this grid to
+    // finish before reading anything the gather wrote.
+    if (t == 0) ptx::grid_dep_launch();
     __threadfence_system();
     if (t < a.n) ptx::st_release_sys(a.flags[t] + a.rank, a.epoch);
     if (t < a.n) {
