@@ -149,7 +149,7 @@ __device__ __forceinline__ bool prune_compress_group(uint32_t x, uint32_t y, uin
 constexpr int kPackBands = 4;
 constexpr int kLoadsPerThread = kPackBands * 16 * (kTileCols / 8) / kPackThreads;
 
-__global__ void __launch_bounds__(kPackThreads) pack_a_kernel(const uint16_t* __restrict__ dense, int M, int K,
+__global__ void __launch_bounds__(kPackThreads, 6) pack_a_kernel(const uint16_t* __restrict__ dense, int M, int K,
                                                               int prune, uint16_t* __restrict__ vals,
                                                               uint16_t* __restrict__ meta, int* bad_blocks) {
     __shared__ __align__(16) uint16_t tile[kPackBands * 16 * kTilePitch];
@@ -196,11 +196,37 @@ __global__ void __launch_bounds__(kPackThreads) pack_a_kernel(const uint16_t* __
         bool ok = true;
         if (prune) {
             const uint32_t inf = prune == 2 ? 0x7f80u : 0x7c00u;
+            // Row fast path: no NaN in the row's 16 values and both kept
+            // magnitudes of every group non-zero -- one test per row instead
+            // of two branches per group; otherwise the per-group path.
+            const uint32_t add = (0x7fffu - inf) * 0x10001u;
+            uint32_t nan_bits = 0, top2[4], sec2[4];
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-                uint32_t idx;
-                ok &= prune_compress_group(wx[k], wy[k], inf, &w[k], &idx);
-                md |= idx << (4 * k);
+                const uint32_t ax = wx[k] & 0x7fff7fffu, ay = wy[k] & 0x7fff7fffu;
+                nan_bits |= (ax + add) | (ay + add);
+                const uint32_t a0 = ((ax << 2) & 0x3fffcu) | 3u, a1 = ((ax >> 14) & 0x3fffcu) | 2u;
+                const uint32_t a2 = ((ay << 2) & 0x3fffcu) | 1u, a3 = (ay >> 14) & 0x3fffcu;
+                const uint32_t hi01 = max(a0, a1), lo01 = min(a0, a1), hi23 = max(a2, a3), lo23 = min(a2, a3);
+                top2[k] = max(hi01, hi23);
+                sec2[k] = max(min(hi01, hi23), max(lo01, lo23));
+            }
+            const uint32_t min_sec = min(min(sec2[0], sec2[1]), min(sec2[2], sec2[3]));
+            if ((nan_bits & 0x80008000u) == 0u && min_sec >= 4u) {
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const uint32_t k0 = ~top2[k] & 3u, k1 = ~sec2[k] & 3u;  // 3 - (key & 3)
+                    const uint32_t ia = min(k0, k1), ib = max(k0, k1);
+                    w[k] = __byte_perm(wx[k], wy[k], ia * 0x22u + ib * 0x2200u + 0x1010u);
+                    md |= (ia | (ib << 2)) << (4 * k);
+                }
+            } else {
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    uint32_t idx;
+                    ok &= prune_compress_group(wx[k], wy[k], inf, &w[k], &idx);
+                    md |= idx << (4 * k);
+                }
             }
         } else {
 #pragma unroll
@@ -347,11 +373,41 @@ __global__ void __launch_bounds__(kPackThreads) pack_a_fp8_kernel(const uint8_t*
         const uint32_t w[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
         uint32_t pr[8], md = 0;
         bool ok = true;
+        // Row fast path (prune on, no NaN in the row's 32 bytes, both kept
+        // magnitudes of every group non-zero); otherwise per group.
+        bool fast = prune_top != 0;
+        uint32_t top8[8], sec8[8];
+        if (fast) {
+            const uint32_t add = (0x7fu - prune_top) * 0x01010101u;
+            uint32_t nan_bits = 0, min_sec = 0xffffffffu;
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            uint32_t idx;
-            ok &= pack_group8(w[k], prune_top, &pr[k], &idx);
-            md |= idx << (4 * k);
+            for (int k = 0; k < 8; ++k) {
+                const uint32_t a = w[k] & 0x7f7f7f7fu;
+                nan_bits |= a + add;
+                const uint32_t a0 = ((a << 2) & 0x1fcu) | 3u, a1 = ((a >> 6) & 0x1fcu) | 2u;
+                const uint32_t a2 = ((a >> 14) & 0x1fcu) | 1u, a3 = (a >> 22) & 0x1fcu;
+                const uint32_t hi01 = max(a0, a1), lo01 = min(a0, a1), hi23 = max(a2, a3), lo23 = min(a2, a3);
+                top8[k] = max(hi01, hi23);
+                sec8[k] = max(min(hi01, hi23), max(lo01, lo23));
+                min_sec = min(min_sec, sec8[k]);
+            }
+            fast = (nan_bits & 0x80808080u) == 0u && min_sec >= 4u;
+        }
+        if (fast) {
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const uint32_t k0 = ~top8[k] & 3u, k1 = ~sec8[k] & 3u;  // 3 - (key & 3)
+                const uint32_t ia = min(k0, k1), ib = max(k0, k1);
+                pr[k] = __byte_perm(w[k], 0, ia | (ib << 4) | 0x4400u);
+                md |= (ia | (ib << 2)) << (4 * k);
+            }
+        } else {
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                uint32_t idx;
+                ok &= pack_group8(w[k], prune_top, &pr[k], &idx);
+                md |= idx << (4 * k);
+            }
         }
         bad += ok ? 0 : 1;
         const int band = band0 + b;
