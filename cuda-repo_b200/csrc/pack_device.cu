@@ -149,6 +149,66 @@ __device__ __forceinline__ bool prune_compress_group(uint32_t x, uint32_t y, uin
 constexpr int kPackBands = 4;
 constexpr int kLoadsPerThread = kPackBands * 16 * (kTileCols / 8) / kPackThreads;
 
+// One row of a 16 x 16 block (row r of block qg of band `band`), staged in
+// shared memory: optional prune, compress, the values and the reordered
+// metadata word.  Returns false when a group keeps more than two values.
+__device__ __forceinline__ bool pack_row16(const uint16_t* row, int prune, uint16_t* __restrict__ vals,
+                                           uint16_t* __restrict__ meta, int band, int qg, int r, int nbc, int K) {
+    const uint4 lo = *reinterpret_cast<const uint4*>(row);
+    const uint4 hi = *reinterpret_cast<const uint4*>(row + 8);
+    uint32_t wx[4] = {lo.x, lo.z, hi.x, hi.z}, wy[4] = {lo.y, lo.w, hi.y, hi.w};
+    uint32_t w[4], md = 0;
+    bool ok = true;
+    if (prune) {
+        const uint32_t inf = prune == 2 ? 0x7f80u : 0x7c00u;
+        // Row fast path: no NaN in the row's 16 values and both kept
+        // magnitudes of every group non-zero -- one test per row instead
+        // of two branches per group; otherwise the per-group path.
+        const uint32_t add = (0x7fffu - inf) * 0x10001u;
+        uint32_t nan_bits = 0, top2[4], sec2[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint32_t ax = wx[k] & 0x7fff7fffu, ay = wy[k] & 0x7fff7fffu;
+            nan_bits |= (ax + add) | (ay + add);
+            const uint32_t a0 = ((ax << 2) & 0x3fffcu) | 3u, a1 = ((ax >> 14) & 0x3fffcu) | 2u;
+            const uint32_t a2 = ((ay << 2) & 0x3fffcu) | 1u, a3 = (ay >> 14) & 0x3fffcu;
+            const uint32_t hi01 = max(a0, a1), lo01 = min(a0, a1), hi23 = max(a2, a3), lo23 = min(a2, a3);
+            top2[k] = max(hi01, hi23);
+            sec2[k] = max(min(hi01, hi23), max(lo01, lo23));
+        }
+        const uint32_t min_sec = min(min(sec2[0], sec2[1]), min(sec2[2], sec2[3]));
+        if ((nan_bits & 0x80008000u) == 0u && min_sec >= 4u) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const uint32_t k0 = ~top2[k] & 3u, k1 = ~sec2[k] & 3u;  // 3 - (key & 3)
+                const uint32_t ia = min(k0, k1), ib = max(k0, k1);
+                w[k] = __byte_perm(wx[k], wy[k], ia * 0x22u + ib * 0x2200u + 0x1010u);
+                md |= (ia | (ib << 2)) << (4 * k);
+            }
+        } else {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                uint32_t idx;
+                ok &= prune_compress_group(wx[k], wy[k], inf, &w[k], &idx);
+                md |= idx << (4 * k);
+            }
+        }
+    } else {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            uint32_t idx;
+            ok &= compress_group(wx[k], wy[k], &w[k], &idx);
+            md |= idx << (4 * k);
+        }
+    }
+    *reinterpret_cast<uint4*>(vals + (((size_t)band * nbc + qg) * 16 + r) * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+    // Reordered metadata (test/utils.h:179-180): per band and 64-K group,
+    // word i*8 + j holds (row (j%2)*8 + i, block j/2 of the group).
+    const size_t grp = (size_t)band * (K / 64) + qg / 4;
+    meta[grp * 64 + (r % 8) * 8 + 2 * (qg % 4) + r / 8] = (uint16_t)md;
+    return ok;
+}
+
 __global__ void __launch_bounds__(kPackThreads, 6) pack_a_kernel(const uint16_t* __restrict__ dense, int M, int K,
                                                               int prune, uint16_t* __restrict__ vals,
                                                               uint16_t* __restrict__ meta, int* bad_blocks) {
@@ -187,63 +247,8 @@ __global__ void __launch_bounds__(kPackThreads, 6) pack_a_kernel(const uint16_t*
     if (q >= nq) return;
     const int qg = q0 + q;
     int bad = 0;
-    for (int b = 0; b < nb; ++b) {
-        const uint16_t* row = tile + (b * 16 + r) * kTilePitch + q * 16;
-        const uint4 lo = *reinterpret_cast<const uint4*>(row);
-        const uint4 hi = *reinterpret_cast<const uint4*>(row + 8);
-        uint32_t wx[4] = {lo.x, lo.z, hi.x, hi.z}, wy[4] = {lo.y, lo.w, hi.y, hi.w};
-        uint32_t w[4], md = 0;
-        bool ok = true;
-        if (prune) {
-            const uint32_t inf = prune == 2 ? 0x7f80u : 0x7c00u;
-            // Row fast path: no NaN in the row's 16 values and both kept
-            // magnitudes of every group non-zero -- one test per row instead
-            // of two branches per group; otherwise the per-group path.
-            const uint32_t add = (0x7fffu - inf) * 0x10001u;
-            uint32_t nan_bits = 0, top2[4], sec2[4];
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const uint32_t ax = wx[k] & 0x7fff7fffu, ay = wy[k] & 0x7fff7fffu;
-                nan_bits |= (ax + add) | (ay + add);
-                const uint32_t a0 = ((ax << 2) & 0x3fffcu) | 3u, a1 = ((ax >> 14) & 0x3fffcu) | 2u;
-                const uint32_t a2 = ((ay << 2) & 0x3fffcu) | 1u, a3 = (ay >> 14) & 0x3fffcu;
-                const uint32_t hi01 = max(a0, a1), lo01 = min(a0, a1), hi23 = max(a2, a3), lo23 = min(a2, a3);
-                top2[k] = max(hi01, hi23);
-                sec2[k] = max(min(hi01, hi23), max(lo01, lo23));
-            }
-            const uint32_t min_sec = min(min(sec2[0], sec2[1]), min(sec2[2], sec2[3]));
-            if ((nan_bits & 0x80008000u) == 0u && min_sec >= 4u) {
-#pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    const uint32_t k0 = ~top2[k] & 3u, k1 = ~sec2[k] & 3u;  // 3 - (key & 3)
-                    const uint32_t ia = min(k0, k1), ib = max(k0, k1);
-                    w[k] = __byte_perm(wx[k], wy[k], ia * 0x22u + ib * 0x2200u + 0x1010u);
-                    md |= (ia | (ib << 2)) << (4 * k);
-                }
-            } else {
-#pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    uint32_t idx;
-                    ok &= prune_compress_group(wx[k], wy[k], inf, &w[k], &idx);
-                    md |= idx << (4 * k);
-                }
-            }
-        } else {
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                uint32_t idx;
-                ok &= compress_group(wx[k], wy[k], &w[k], &idx);
-                md |= idx << (4 * k);
-            }
-        }
-        bad += ok ? 0 : 1;
-        const int band = band0 + b;
-        *reinterpret_cast<uint4*>(vals + (((size_t)band * nbc + qg) * 16 + r) * 8) = make_uint4(w[0], w[1], w[2], w[3]);
-        // Reordered metadata (test/utils.h:179-180): per band and 64-K group,
-        // word i*8 + j holds (row (j%2)*8 + i, block j/2 of the group).
-        const size_t grp = (size_t)band * (K / 64) + qg / 4;
-        meta[grp * 64 + (r % 8) * 8 + 2 * (qg % 4) + r / 8] = (uint16_t)md;
-    }
+    for (int b = 0; b < nb; ++b)
+        bad += pack_row16(tile + (b * 16 + r) * kTilePitch + q * 16, prune, vals, meta, band0 + b, qg, r, nbc, K) ? 0 : 1;
     if (bad && bad_blocks) atomicAdd(bad_blocks, bad);
 }
 
