@@ -330,14 +330,16 @@ __device__ __forceinline__ bool epilogue_is_plain(const Epilogue& e) {
 }
 
 // alpha, bias and activation on n values of row gm (no residual).
+// bias_pre: the row's bias already loaded (e.g. prefetched into shared
+// memory while the main loop ran), or null to read e.bias[gm].
 template <int n>
-__device__ __forceinline__ void epilogue_pre(float* y, const Epilogue& e, int gm) {
+__device__ __forceinline__ void epilogue_pre(float* y, const Epilogue& e, int gm, const float* bias_pre = nullptr) {
     if (e.alpha != 1.f) {
 #pragma unroll
         for (int i = 0; i < n; ++i) y[i] *= e.alpha;
     }
     if (e.bias) {
-        const float b = elem_to_f32(e.bias[gm], e.bf16);
+        const float b = bias_pre ? *bias_pre : elem_to_f32(e.bias[gm], e.bf16);
 #pragma unroll
         for (int i = 0; i < n; ++i) y[i] += b;
     }
@@ -366,12 +368,12 @@ __device__ __forceinline__ void round8(const float* y, int lim, int bf16, uint32
 // read as whole 16-byte strip rows.  Each optional stage sits behind one
 // uniform branch, so an unused stage costs nothing.
 __device__ __forceinline__ void epilogue8(const float* v, const Epilogue& e, int gm, int gn, int M, int N,
-                                          bool vec_rowmajor, uint32_t* w) {
+                                          bool vec_rowmajor, uint32_t* w, const float* bias_pre = nullptr) {
     const int lim = min(8, N - gn);
     float y[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) y[i] = v[i];
-    epilogue_pre<8>(y, e, gm);
+    epilogue_pre<8>(y, e, gm, bias_pre);
     if (e.residual) {
         const size_t base = c_offset(e, gm, gn, M, N);
         if (e.packed || vec_rowmajor) {
@@ -390,11 +392,11 @@ __device__ __forceinline__ void epilogue8(const float* v, const Epilogue& e, int
 // C is always written as whole 16-byte strip rows.  `plain`: the caller's
 // epilogue_is_plain(e), evaluated once per kernel.
 __device__ __forceinline__ void epilogue_store8(uint16_t* C, const float* v, const Epilogue& e, int gm, int gn, int M,
-                                                int N, bool vec_rowmajor, bool plain) {
+                                                int N, bool vec_rowmajor, bool plain, const float* bias_pre = nullptr) {
     const int lim = min(8, N - gn);
     uint32_t w[4];
     if (plain) round8(v, lim, e.bf16, w);
-    else epilogue8(v, e, gm, gn, M, N, vec_rowmajor, w);
+    else epilogue8(v, e, gm, gn, M, N, vec_rowmajor, w, bias_pre);
     if (e.packed) {
         *reinterpret_cast<uint4*>(C + c_offset(e, gm, gn, M, N)) = make_uint4(w[0], w[1], w[2], w[3]);
     } else if (vec_rowmajor) {

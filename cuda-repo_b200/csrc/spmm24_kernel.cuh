@@ -117,7 +117,8 @@ struct ClusterCfg : Cfg<N_TILE, STAGES, 1, FP8> {
     static constexpr int BAR_OFFSET = RECV_OFFSET + RECV_BYTES;
     static constexpr int NUM_BARS = 2 * STAGES + 2;  // full, empty, acc_full, recv
     static constexpr int HOLDER_OFFSET = BAR_OFFSET + NUM_BARS * 8;
-    static constexpr int SMEM_BYTES = HOLDER_OFFSET + 16;
+    static constexpr int BIAS_OFFSET = HOLDER_OFFSET + 16;  // the owner rows' bias, prefetched (EPI)
+    static constexpr int SMEM_BYTES = BIAS_OFFSET + kTileM * 4;
     static constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;  // slack to align the base to 1024 B
     // CTAs that fit on one SM (228 KB, 1 KB reserved per CTA), at most 4.
     static constexpr int CTAS_PER_SM = 233472 / (SMEM_ALLOC + 1024) < 4 ? 233472 / (SMEM_ALLOC + 1024) : 4;
@@ -226,6 +227,18 @@ spmm24_cluster_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_cons
         ptx::named_barrier(kBarTmem, kThreads - 32);
         ptx::tc_fence_after();
         tmem_base = *tmem_holder;
+    }
+    // The epilogue warps are idle until the accumulator is ready: with a bias,
+    // they wait for the previous grid now and bring this CTA's owner rows'
+    // bias into shared memory, off the critical path at the end.
+    float* bias_s = reinterpret_cast<float*>(smem + C_::BIAS_OFFSET);
+    if constexpr (EPI) {
+        if (warp >= 2 && p.epi.bias) {
+            ptx::grid_dep_wait();
+            const int m_first = blockIdx.z * kTileM + my_start;
+            for (int t = threadIdx.x - 64; t < my_end - my_start; t += kEpiThreads)
+                bias_s[t] = m_first + t < p.M ? elem_to_f32(p.epi.bias[m_first + t], p.epi.bf16) : 0.f;
+        }
     }
 
     if (warp == 1) {
@@ -340,7 +353,8 @@ spmm24_cluster_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_cons
             const int gn = n0 + ch * 8;
             if (gm >= p.M || gn >= p.N) continue;
             if constexpr (EPI) {
-                epilogue_store8(p.C, acc, p.epi, gm, gn, p.M, p.N, vec_ok, epilogue_is_plain(p.epi));
+                epilogue_store8(p.C, acc, p.epi, gm, gn, p.M, p.N, vec_ok, epilogue_is_plain(p.epi),
+                                p.epi.bias ? bias_s + lr : nullptr);
             } else {
                 if constexpr (FP8) {
 #pragma unroll
