@@ -367,8 +367,11 @@ __device__ __forceinline__ void round8(const float* y, int lim, int bf16, uint32
 // residual (N % 8 == 0 and 16-byte aligned); a packed residual is always
 // read as whole 16-byte strip rows.  Each optional stage sits behind one
 // uniform branch, so an unused stage costs nothing.
+// res_pre: the 8 residual values already loaded (16-byte layouts only), or
+// null to read them from e.residual.
 __device__ __forceinline__ void epilogue8(const float* v, const Epilogue& e, int gm, int gn, int M, int N,
-                                          bool vec_rowmajor, uint32_t* w, const float* bias_pre = nullptr) {
+                                          bool vec_rowmajor, uint32_t* w, const float* bias_pre = nullptr,
+                                          const uint4* res_pre = nullptr) {
     const int lim = min(8, N - gn);
     float y[8];
 #pragma unroll
@@ -377,7 +380,7 @@ __device__ __forceinline__ void epilogue8(const float* v, const Epilogue& e, int
     if (e.residual) {
         const size_t base = c_offset(e, gm, gn, M, N);
         if (e.packed || vec_rowmajor) {
-            const uint4 q = *reinterpret_cast<const uint4*>(e.residual + base);
+            const uint4 q = res_pre ? *res_pre : *reinterpret_cast<const uint4*>(e.residual + base);
             const uint32_t x[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
             for (int i = 0; i < 8; ++i) y[i] += elem_to_f32((uint16_t)(x[i >> 1] >> (16 * (i & 1))), e.bf16);
@@ -392,11 +395,12 @@ __device__ __forceinline__ void epilogue8(const float* v, const Epilogue& e, int
 // C is always written as whole 16-byte strip rows.  `plain`: the caller's
 // epilogue_is_plain(e), evaluated once per kernel.
 __device__ __forceinline__ void epilogue_store8(uint16_t* C, const float* v, const Epilogue& e, int gm, int gn, int M,
-                                                int N, bool vec_rowmajor, bool plain, const float* bias_pre = nullptr) {
+                                                int N, bool vec_rowmajor, bool plain, const float* bias_pre = nullptr,
+                                                const uint4* res_pre = nullptr) {
     const int lim = min(8, N - gn);
     uint32_t w[4];
     if (plain) round8(v, lim, e.bf16, w);
-    else epilogue8(v, e, gm, gn, M, N, vec_rowmajor, w, bias_pre);
+    else epilogue8(v, e, gm, gn, M, N, vec_rowmajor, w, bias_pre, res_pre);
     if (e.packed) {
         *reinterpret_cast<uint4*>(C + c_offset(e, gm, gn, M, N)) = make_uint4(w[0], w[1], w[2], w[3]);
     } else if (vec_rowmajor) {

@@ -118,7 +118,10 @@ struct ClusterCfg : Cfg<N_TILE, STAGES, 1, FP8> {
     static constexpr int NUM_BARS = 2 * STAGES + 2;  // full, empty, acc_full, recv
     static constexpr int HOLDER_OFFSET = BAR_OFFSET + NUM_BARS * 8;
     static constexpr int BIAS_OFFSET = HOLDER_OFFSET + 16;  // the owner rows' bias, prefetched (EPI)
-    static constexpr int SMEM_BYTES = BIAS_OFFSET + kTileM * 4;
+    // Narrow tiles: the owner rows' residual, prefetched (EPI, 16-byte layouts).
+    static constexpr int RES_OFFSET = BIAS_OFFSET + kTileM * 4;
+    static constexpr int RES_BYTES = N_TILE <= 32 ? kTileM * N_TILE * 2 : 0;
+    static constexpr int SMEM_BYTES = RES_OFFSET + RES_BYTES;
     static constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;  // slack to align the base to 1024 B
     // CTAs that fit on one SM (228 KB, 1 KB reserved per CTA), at most 4.
     static constexpr int CTAS_PER_SM = 233472 / (SMEM_ALLOC + 1024) < 4 ? 233472 / (SMEM_ALLOC + 1024) : 4;
@@ -228,16 +231,32 @@ spmm24_cluster_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_cons
         ptx::tc_fence_after();
         tmem_base = *tmem_holder;
     }
-    // The epilogue warps are idle until the accumulator is ready: with a bias,
-    // they wait for the previous grid now and bring this CTA's owner rows'
-    // bias into shared memory, off the critical path at the end.
+    // The epilogue warps are idle until the accumulator is ready: with a bias
+    // (or, for narrow tiles, a residual in a 16-byte layout), they wait for the
+    // previous grid now and bring this CTA's owner rows of it into shared
+    // memory, off the critical path at the end.
     float* bias_s = reinterpret_cast<float*>(smem + C_::BIAS_OFFSET);
+    uint4* res_s = reinterpret_cast<uint4*>(smem + C_::RES_OFFSET);  // [owner row][16-byte chunk]
+    const bool res_pre = EPI && C_::RES_BYTES > 0 && p.epi.residual && !p.epi.gather_n &&
+                         (p.epi.packed || ((p.N % 8 == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15u) == 0)));
     if constexpr (EPI) {
-        if (warp >= 2 && p.epi.bias) {
+        if (warp >= 2 && (p.epi.bias || res_pre)) {
             ptx::grid_dep_wait();
-            const int m_first = blockIdx.z * kTileM + my_start;
-            for (int t = threadIdx.x - 64; t < my_end - my_start; t += kEpiThreads)
-                bias_s[t] = m_first + t < p.M ? elem_to_f32(p.epi.bias[m_first + t], p.epi.bf16) : 0.f;
+            const int m_first = m_tile * kTileM + my_start;
+            const int nrows = my_end - my_start;
+            if (p.epi.bias)
+                for (int t = threadIdx.x - 64; t < nrows; t += kEpiThreads)
+                    bias_s[t] = m_first + t < p.M ? elem_to_f32(p.epi.bias[m_first + t], p.epi.bf16) : 0.f;
+            if constexpr (C_::RES_BYTES > 0) {
+                if (res_pre) {
+                    constexpr int CH = N_TILE / 8;
+                    for (int t = threadIdx.x - 64; t < nrows * CH; t += kEpiThreads) {
+                        const int gm = m_first + t / CH, gn = n_tile * N_TILE + (t % CH) * 8;
+                        if (gm < p.M && gn < p.N)
+                            res_s[t] = *reinterpret_cast<const uint4*>(p.epi.residual + c_offset(p.epi, gm, gn, p.M, p.N));
+                    }
+                }
+            }
         }
     }
 
@@ -354,7 +373,7 @@ spmm24_cluster_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_cons
             if (gm >= p.M || gn >= p.N) continue;
             if constexpr (EPI) {
                 epilogue_store8(p.C, acc, p.epi, gm, gn, p.M, p.N, vec_ok, epilogue_is_plain(p.epi),
-                                p.epi.bias ? bias_s + lr : nullptr);
+                                p.epi.bias ? bias_s + lr : nullptr, res_pre ? res_s + lr * CHUNKS + ch : nullptr);
             } else {
                 if constexpr (FP8) {
 #pragma unroll
