@@ -293,6 +293,48 @@ __device__ __forceinline__ uint32_t prune_keep_sequential8(uint32_t a, uint32_t 
     return (1u << k0) | (1u << k1);
 }
 
+// 16-bit-lane max / min (native instructions on sm_90 and later).
+__device__ __forceinline__ uint32_t vmax_u16x2(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("max.u16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+__device__ __forceinline__ uint32_t vmin_u16x2(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("min.u16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+
+// Top-2 of two groups at once (w0 in the low 16-bit lanes, w1 in the high
+// ones): key = magnitude << 8 | (3 - position), the scalar keys' order (ties
+// to the lower position) in 16 bits.  Returns the top and second keys; ORs
+// each byte + (0x7f - prune_top) into *nan_bits (bit 7 set: a NaN).
+__device__ __forceinline__ void top2_pair8(uint32_t w0, uint32_t w1, uint32_t add, uint32_t* nan_bits, uint32_t* top,
+                                           uint32_t* sec) {
+    const uint32_t a0 = w0 & 0x7f7f7f7fu, a1 = w1 & 0x7f7f7f7fu;
+    *nan_bits |= (a0 + add) | (a1 + add);
+    const uint32_t even = __byte_perm(a0, a1, 0x6420u), odd = __byte_perm(a0, a1, 0x7531u);
+    constexpr uint32_t kTags = 0x00010203u;  // byte j: 3 - j
+    const uint32_t k0 = __byte_perm(even, kTags, 0x2404u), k1 = __byte_perm(odd, kTags, 0x2505u);
+    const uint32_t k2 = __byte_perm(even, kTags, 0x3616u), k3 = __byte_perm(odd, kTags, 0x3717u);
+    const uint32_t hi01 = vmax_u16x2(k0, k1), lo01 = vmin_u16x2(k0, k1);
+    const uint32_t hi23 = vmax_u16x2(k2, k3), lo23 = vmin_u16x2(k2, k3);
+    *top = vmax_u16x2(hi01, hi23);
+    *sec = vmax_u16x2(vmin_u16x2(hi01, hi23), vmax_u16x2(lo01, lo23));
+}
+
+// From two groups' top and second keys: the four kept bytes (each group's
+// lower position first; w0's in the low half) and the two metadata nibbles
+// i0 | i1 << 2 (w0's at bit 0, w1's at bit 16).
+__device__ __forceinline__ uint32_t emit_pair8(uint32_t w0, uint32_t w1, uint32_t top, uint32_t sec, uint32_t* nibs) {
+    const uint32_t t = top & 0x00030003u, s = sec & 0x00030003u;
+    const uint32_t hi = vmax_u16x2(t, s), lo = vmin_u16x2(t, s);  // tags of the lower and the higher position
+    // per lane (i0 | i1 << 4), +4 on the high lane's positions (bytes of w1)
+    const uint32_t sel = __byte_perm(0x00770033u - (hi | (lo << 4)), 0, 0x4420u);
+    *nibs = 0x000f000fu - (hi | (lo << 2));
+    return __byte_perm(w0, w1, sel);
+}
+
 // Prune + compress of one group: the two kept bytes (lower position first)
 // in the low 16 bits of *pair, positions i0 | i1 << 2 in *idx; false when
 // the group keeps more than two values.  prune_top: 0 = no prune.
@@ -381,31 +423,26 @@ __global__ void __launch_bounds__(kPackThreads) pack_a_fp8_kernel(const uint8_t*
         // Row fast path (prune on, no NaN in the row's 32 bytes, both kept
         // magnitudes of every group non-zero); otherwise per group.
         bool fast = prune_top != 0;
-        uint32_t top8[8], sec8[8];
+        uint32_t top4[4], sec4[4];
         if (fast) {
             const uint32_t add = (0x7fu - prune_top) * 0x01010101u;
             uint32_t nan_bits = 0, min_sec = 0xffffffffu;
 #pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                const uint32_t a = w[k] & 0x7f7f7f7fu;
-                nan_bits |= a + add;
-                const uint32_t a0 = ((a << 2) & 0x1fcu) | 3u, a1 = ((a >> 6) & 0x1fcu) | 2u;
-                const uint32_t a2 = ((a >> 14) & 0x1fcu) | 1u, a3 = (a >> 22) & 0x1fcu;
-                const uint32_t hi01 = max(a0, a1), lo01 = min(a0, a1), hi23 = max(a2, a3), lo23 = min(a2, a3);
-                top8[k] = max(hi01, hi23);
-                sec8[k] = max(min(hi01, hi23), max(lo01, lo23));
-                min_sec = min(min_sec, sec8[k]);
+            for (int k = 0; k < 4; ++k) {
+                top2_pair8(w[2 * k], w[2 * k + 1], add, &nan_bits, &top4[k], &sec4[k]);
+                min_sec = vmin_u16x2(min_sec, sec4[k]);
             }
-            fast = (nan_bits & 0x80808080u) == 0u && min_sec >= 4u;
+            // no NaN, and every group's second kept magnitude non-zero
+            fast = (nan_bits & 0x80808080u) == 0u && (min_sec & 0xff00u) != 0u && (min_sec & 0xff000000u) != 0u;
         }
+        uint4 out;
         if (fast) {
+            uint32_t nib[4], vw[4];
 #pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                const uint32_t k0 = ~top8[k] & 3u, k1 = ~sec8[k] & 3u;  // 3 - (key & 3)
-                const uint32_t ia = min(k0, k1), ib = max(k0, k1);
-                pr[k] = __byte_perm(w[k], 0, ia | (ib << 4) | 0x4400u);
-                md |= (ia | (ib << 2)) << (4 * k);
-            }
+            for (int k = 0; k < 4; ++k) vw[k] = emit_pair8(w[2 * k], w[2 * k + 1], top4[k], sec4[k], &nib[k]);
+            const uint32_t n03 = __byte_perm(nib[0], nib[1], 0x6420u), n47 = __byte_perm(nib[2], nib[3], 0x6420u);
+            md = __byte_perm(n03, n47, 0x6420u) | (__byte_perm(n03, n47, 0x7531u) << 4);
+            out = make_uint4(vw[0], vw[1], vw[2], vw[3]);
         } else {
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
@@ -413,11 +450,10 @@ __global__ void __launch_bounds__(kPackThreads) pack_a_fp8_kernel(const uint8_t*
                 ok &= pack_group8(w[k], prune_top, &pr[k], &idx);
                 md |= idx << (4 * k);
             }
+            out = make_uint4(pr[0] | (pr[1] << 16), pr[2] | (pr[3] << 16), pr[4] | (pr[5] << 16), pr[6] | (pr[7] << 16));
         }
         bad += ok ? 0 : 1;
         const int band = band0 + b;
-        const uint4 out = make_uint4(pr[0] | (pr[1] << 16), pr[2] | (pr[3] << 16), pr[4] | (pr[5] << 16),
-                                     pr[6] | (pr[7] << 16));
         *reinterpret_cast<uint4*>(vals + (((size_t)band * nbc + qg) * 16 + r) * 16) = out;
         // metadata row (band, 128-K group qg / 4, row r): this block's 32 bits
         *reinterpret_cast<uint32_t*>(meta + (((size_t)band * (K / 128) + qg / 4) * 16 + r) * 16 + (qg % 4) * 4) = md;
