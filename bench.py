@@ -56,6 +56,14 @@ WORKLOADS = {
 # config 2 (dense fp16 N(0, 0.02), magnitude-pruned and compressed in one
 # kernel per layer).
 PACK_LAYERS = [(4096, 4096), (11008, 4096), (4096, 11008)]
+# Activations K x N of BASELINE config 3 (prefill): what spmm24_pack_b_device
+# turns into the packed B of the next SpMM.
+PACKB_ACTS = [(K, N) for K in (4096, 11008) for N in (512, 2048, 4096)]
+
+
+def packb_bytes(K, N):
+    """Algorithmic bytes of one B packing: read 2KN, write the packed strips."""
+    return 2 * K * N + 2 * K * ((N + 7) // 8) * 8
 
 
 def pack_bytes(M, K, fp8=False):
@@ -248,7 +256,9 @@ def run_ours(args, rank, world, local_rank):
     # views of two contiguous buffers, so a step's inputs and results move
     # host<->device in one copy each.
     b_sizes = [acts[(K, N)][1].size for (M, N, K) in shapes]
-    c_sizes = [(rows[M][1] - rows[M][0]) * N for (M, N, K) in shapes]
+    packed_out = args.epilogue == "packed_b"
+    # packed_b: C is written as the next layer's packed B (ceil(N/8) strips of M x 8)
+    c_sizes = [(rows[M][1] - rows[M][0]) * (((N + 7) // 8) * 8 if packed_out else N) for (M, N, K) in shapes]
     bdt, bview = (torch.uint8, "uint8") if fp8 else (torch.int16, "int16")
     B_all = torch.empty(sum(b_sizes), dtype=bdt, device=dev)
     C_all = torch.empty(sum(c_sizes), dtype=torch.float16, device=dev)
@@ -262,7 +272,7 @@ def run_ours(args, rank, world, local_rank):
         E = to_dev(torch, meta, dev)
         r0, r1 = rows[M]
         B = B_all[boff:boff + bs]
-        C = C_all[coff:coff + cs].view(r1 - r0, N)
+        C = C_all[coff:coff + cs] if packed_out else C_all[coff:coff + cs].view(r1 - r0, N)
         boff += bs
         coff += cs
         calls.append({"M": r1 - r0, "N": N, "K": K, "A": A, "E": E, "B": B, "C": C, "M_full": M,
@@ -286,10 +296,11 @@ def run_ours(args, rank, world, local_rank):
         for c in calls:
             c["bias"] = (torch.randn(c["M"], device=dev) * 0.1).to(edt)
             c["res"] = torch.randn(c["M"], c["N"], device=dev).to(edt) if args.epilogue == "bias_residual" else None
-            c["epi"] = spmm24.Epilogue(c["bias"].data_ptr() if args.epilogue != "none" else None,
+            with_bias = args.epilogue in ("bias_silu", "bias_residual")
+            c["epi"] = spmm24.Epilogue(c["bias"].data_ptr() if with_bias else None,
                                        c["res"].data_ptr() if c["res"] is not None else None, alpha,
                                        spmm24.ACT_SILU if args.epilogue == "bias_silu" else spmm24.ACT_NONE,
-                                       spmm24.OUT_ROW_MAJOR)
+                                       spmm24.OUT_PACKED_B if packed_out else spmm24.OUT_ROW_MAJOR)
 
     def launch(c, hs=None):
         if fp8:
@@ -363,8 +374,9 @@ def run_ours(args, rank, world, local_rank):
     call_sets = [calls, []]
     for c in calls:
         bs_, cs_ = c["B"].numel(), c["C"].numel()
+        c1 = C_set[1][c["coff"]:c["coff"] + cs_]
         call_sets[1].append(dict(c, B=B_set[1][c["boff"]:c["boff"] + bs_],
-                                 C=C_set[1][c["coff"]:c["coff"] + cs_].view(c["M"], c["N"])))
+                                 C=c1 if packed_out else c1.view(c["M"], c["N"])))
     graphs = [None, None]
     try:
         for k in range(2):
@@ -997,7 +1009,190 @@ def run_pack(args, rank, world, local_rank):
         print(json.dumps(out), flush=True)
 
 
+def host_pack_b_baseline(acts_np, budget_s=10.0):
+    """The reference's toolPackMatrixB (built from its sources into
+    oracle/_ref), else the oracle's restatement, on K-row samples of each
+    activation; single threaded as the reference is.  Returns (GB/s, kind,
+    sample)."""
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import oracle as O
+
+    use_ref = O.ref_packer_available()
+    pack = O.ref_pack_b if use_ref else O.pack_b
+    probe = 64
+    t = time.perf_counter()
+    for (K, N), b in zip(PACKB_ACTS, acts_np):
+        pack(b[: probe * N], probe, N)
+    dt = time.perf_counter() - t
+    rows = int(max(64, min(4096, probe * budget_s / max(dt, 1e-3) / 1.2))) // 64 * 64
+    nbytes = 0
+    t = time.perf_counter()
+    for (K, N), b in zip(PACKB_ACTS, acts_np):
+        r = min(rows, K)
+        pack(b[: r * N], r, N)
+        nbytes += packb_bytes(r, N)
+    dt = time.perf_counter() - t
+    kind = "reference" if use_ref else "port"
+    return nbytes / dt / 1e9, kind, (f"first {rows} K rows of each of the {len(PACKB_ACTS)} activations through "
+                                     f"{'toolPackMatrixB (oracle/_ref)' if use_ref else 'orc_pack_b'}, "
+                                     f"1 thread, {dt:.1f} s")
+
+
+def run_pack_b(args, rank, world, local_rank):
+    """Times spmm24_pack_b_device (row-major K x N fp16 activations ->
+    the packed 8-column strips the SpMM reads) over the prefill activations,
+    resident in HBM (201 MB read and 201 MB written per step, more than L2)."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import spmm24
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    g = torch.Generator(device=dev).manual_seed(11 + rank)
+    acts = [torch.randn(K, N, generator=g, device=dev).half() for (K, N) in PACKB_ACTS]
+    outs = [torch.empty(((N + 7) // 8) * 8 * K, dtype=torch.int16, device=dev) for (K, N) in PACKB_ACTS]
+    stream = torch.cuda.current_stream(dev)
+    hs = int(stream.cuda_stream)
+    L = spmm24._lib
+
+    def step():
+        for i, (K, N) in enumerate(PACKB_ACTS):
+            rc = L.spmm24_pack_b_device(hs, acts[i].data_ptr(), K, N, outs[i].data_ptr())
+            if rc != 0:
+                raise RuntimeError(f"spmm24_pack_b_device failed: {rc} {L.spmm24_last_error().decode()}")
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        torch.cuda._sleep(int(2e7))
+        t0.record(stream)
+        for _ in range(args.steps):
+            step()
+        t1.record(stream)
+        torch.cuda.synchronize(dev)
+    elapsed_ms = t0.elapsed_time(t1)
+    clocks = clk.summary()
+    # the timed work is checked: the smallest activation equals the host packer bit for bit
+    K0, N0 = PACKB_ACTS[0]
+    host = spmm24.pack_b(acts[0].view(torch.int16).cpu().numpy().view(np.uint16).reshape(-1), K0, N0)
+    assert np.array_equal(outs[0].cpu().numpy().view(np.uint16), host)
+
+    per = {}
+    for i, (K, N) in enumerate(PACKB_ACTS):
+        ts = []
+        for _ in range(5):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            L.spmm24_pack_b_device(hs, acts[i].data_ptr(), K, N, outs[i].data_ptr())
+            b.record(stream)
+            torch.cuda.synchronize(dev)
+            ts.append(a.elapsed_time(b) * 1e3)
+        per[f"{K}x{N}"] = round(statistics.median(ts), 3)
+
+    # end to end: activations from pinned host memory, pack, packed B back
+    host_acts = [a.cpu().pin_memory() for a in acts]
+    host_outs = [torch.empty(o.shape, dtype=o.dtype).pin_memory() for o in outs]
+
+    def e2e_step():
+        for i in range(len(PACKB_ACTS)):
+            acts[i].copy_(host_acts[i], non_blocking=True)
+        step()
+        for i in range(len(PACKB_ACTS)):
+            host_outs[i].copy_(outs[i], non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([elapsed_ms, e2e_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed_ms, e2e_ms = float(t[0]), float(t[1])
+
+    step_bytes = sum(packb_bytes(K, N) for (K, N) in PACKB_ACTS)
+    value = step_bytes * args.steps * world / (elapsed_ms * 1e-3) / 1e9
+    achieved = step_bytes * args.steps / (elapsed_ms * 1e-3) / 1e9
+    peaks = load_peaks()
+    out = {
+        "metric": "GB/s of the on-device B packer (row-major activations -> packed 8-column strips) "
+                  "on the LLaMA-7B prefill activations",
+        "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(elapsed_ms / args.steps, 5), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "u16 (fp16 bit patterns; a permutation copy)",
+        "data": "synthetic (seeded torch RNG on the device; activations N(0,1) fp16)",
+        "config": {"workload": "packb: " + ", ".join(f"{K}x{N}" for (K, N) in PACKB_ACTS),
+                   "baseline_config": 3, "calls_per_step": len(PACKB_ACTS),
+                   "l2": f"inputs larger than L2: {sum(2 * K * N for (K, N) in PACKB_ACTS) / 1e6:.0f} MB "
+                         "of activations per step",
+                   "parallelism": f"replicas x{world}"},
+        "per_act_us": per,
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None,
+                     "peak_src": f"{peaks['src']} (hbm_gbs copy)",
+                     "note": "bytes = read 2KN + write 2K*ceil(N/8)*8 per activation"},
+        "e2e": {"value": round(step_bytes * args.steps * world / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                "h2d_bytes_per_step": sum(2 * K * N for (K, N) in PACKB_ACTS),
+                "d2h_bytes_per_step": sum(o.numel() * 2 for o in outs),
+                "ms_per_step": round(e2e_ms / args.steps, 4),
+                "path": "per step: H2D of the activations (pinned), spmm24_pack_b_device per activation, "
+                        "D2H of the packed B"},
+        "gpu_launches": len(PACKB_ACTS) * args.steps,
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        an = [a.view(torch.int16).cpu().numpy().view(np.uint16).reshape(-1) for a in acts]
+        gbs, kind, sample = host_pack_b_baseline(an, args.cpu_seconds)
+        out["cpu_baseline"] = {"value": round(gbs, 4), "unit": "GB/s", "cores": 1, "kind": kind, "sample": sample}
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+
+
 # -------------------------------------------------------- reference arm
+def run_reference_pack_b(args):
+    """--impl reference --workload packb: the reference's host
+    toolPackMatrixB on K-row samples of the same activations, one step = one
+    sample of each."""
+    import numpy as np
+    import torch
+
+    g = torch.Generator().manual_seed(11)
+    acts = [torch.randn(K, N, generator=g).half().numpy().view(np.uint16).reshape(-1) for (K, N) in PACKB_ACTS]
+    for _ in range(args.warmup):
+        host_pack_b_baseline(acts, 0.2)
+    vals = [host_pack_b_baseline(acts, 1.0) for _ in range(args.steps)]
+    gbs = statistics.median(v[0] for v in vals)
+    kind, sample = vals[-1][1], vals[-1][2]
+    print(json.dumps({
+        "impl": "reference",
+        "metric": "GB/s of the on-device B packer (row-major activations -> packed 8-column strips) "
+                  "on the LLaMA-7B prefill activations",
+        "value": round(gbs, 4), "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "u16 (fp16 bit patterns; a permutation copy)", "data": "synthetic",
+        "config": {"workload": "packb: " + ", ".join(f"{K}x{N}" for (K, N) in PACKB_ACTS), "baseline_config": 3},
+        "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": 1, "kind": kind, "sample": sample},
+        "e2e": {"value": round(gbs, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference packs B on the host only (toolPackMatrixB)",
+    }), flush=True)
+
+
 def run_reference_pack(args):
     """--impl reference --workload pack: the reference's host packer on row
     samples of the same layers, one step = one sample of each layer."""
@@ -1034,6 +1229,9 @@ def run_reference(args, rank, world):
         return
     if args.workload == "pack":
         run_reference_pack(args)
+        return
+    if args.workload == "packb":
+        run_reference_pack_b(args)
         return
     import numpy as np
     import torch
@@ -1132,7 +1330,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["pack"], default="decode")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["pack", "packb"], default="decode")
     ap.add_argument("--comparators", action="store_true")
     ap.add_argument("--allgather", action="store_true", help="70b workload: also time the NCCL all-gather of C")
     ap.add_argument("--gather", action="store_true",
@@ -1142,8 +1340,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--dtype", choices=["f16", "bf16", "fp8"], default="f16",
                     help="operand and output type (SPMM24_BF16; fp8: E4M3 operands through spmm24_launch_fp8, fp16 out)")
-    ap.add_argument("--epilogue", choices=["none", "bias_silu", "bias_residual"], default="none",
-                    help="fused epilogue through spmm24_launch_fused")
+    ap.add_argument("--epilogue", choices=["none", "bias_silu", "bias_residual", "packed_b"], default="none",
+                    help="fused epilogue through spmm24_launch_fused (packed_b: C written as the next layer's "
+                         "packed B, SPMM24_OUT_PACKED_B)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--single", default=None,
                     help="M,N,K[,split]: run one shape (warm-up + 3 launches) for profiler captures")
@@ -1161,6 +1360,9 @@ def main():
         return
     if args.workload == "pack":
         run_pack(args, rank, world, local_rank)
+        return
+    if args.workload == "packb":
+        run_pack_b(args, rank, world, local_rank)
         return
     run_ours(args, rank, world, local_rank)
 
