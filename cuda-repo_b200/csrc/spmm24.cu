@@ -183,7 +183,7 @@ void maybe_pair2(Plan& p, int M, int N, int sms, int tile_n, int stages, int sme
 // plain: the plain fp16 launch (the only one the stream-K option serves).
 // allow_pair: the CTA-pair path may be chosen.  max_split: the largest
 // automatic K split.  pair2_ok: the two-M-half pair kernel may be chosen
-// (16-bit operands, no residual, row-major output, no gather).
+// (no residual, no gather).
 Plan make_plan(int M, int N, int K, int split_k, int sms, bool plain = true, bool allow_pair = true,
                int max_split = kMaxSplit, bool pair2_ok = true) {
     Plan p{};
@@ -546,7 +546,7 @@ cudaError_t launch_impl(cudaStream_t stream, const void* A, const void* B, const
     int dev = 0;
     e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    const bool pair2_ok = !epi.residual && !epi.packed && epi.gather_n == 0;
+    const bool pair2_ok = !epi.residual && epi.gather_n == 0;
     Plan pl = make_plan(M, N, K, split_k, sm_count(dev), plain, true, kMaxSplit, pair2_ok);
 
     uint32_t* ws_counters = nullptr;
@@ -671,8 +671,8 @@ cudaError_t launch_impl(cudaStream_t stream, const void* A, const void* B, const
 // cheaper cluster reduction and more SM slots left to the next launch's
 // early CTAs), and 11008-row layers pick 3 either way.  Wide N takes the CTA
 // pair as for 16-bit operands (its stage is 256 K: K % 256), and the
-// two-M-half pair (512 x 224) when its waves cost less and the epilogue has
-// no residual and no packed output (pair2_ok).
+// two-M-half pair (512 x 240) when its waves cost less and the epilogue has
+// no residual (pair2_ok).
 template <class V>
 int fp8_smem() {
     return ClusterCfg<V::kTileN, V::kStages, true>::SMEM_ALLOC;
@@ -719,7 +719,7 @@ cudaError_t launch_fp8_impl(cudaStream_t stream, const void* A, const void* B, c
     e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     const int Kh = K / 2;  // the 16-bit-equivalent K of the A bytes
-    Plan pl = plan_fp8(M, N, K, split_k, sm_count(dev), !epi.residual && !epi.packed);
+    Plan pl = plan_fp8(M, N, K, split_k, sm_count(dev), !epi.residual);
     const bool pair = pl.path == Path::kPair;
 
     CUtensorMap ta, tb, te;

@@ -903,8 +903,8 @@ spmm24_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
 // two TMEM accumulators (columns 0 and 256).  Every stage moves 66 KB per
 // CTA for 15.7 MFLOP (dense-equivalent) instead of 50 KB for 8.4 MFLOP,
 // so the same shared-memory bytes in flight feed the tensor core 1.4x
-// longer.  Row-major output; EPI adds alpha, bias, activation and bf16
-// (no residual, no packed output, no gather); no K split.  FP8: two
+// longer.  Row-major output; EPI adds alpha, bias, activation, bf16 and
+// the packed-B output layout (no residual, no gather); no K split.  FP8: two
 // 128-byte-swizzled B halves of 120 rows per stage and two 128-K metadata
 // groups per M half; the metadata ring in TMEM has two slots instead of
 // one per stage (the copy into a slot is issued after the MMAs that read
@@ -1157,7 +1157,34 @@ spmm24_pair2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         constexpr int LPR = C_::TILE_N / 8;      // threads per row (30; fp8 28)
         constexpr int RPP = kPairThreads / LPR;  // rows per pass (8; fp8 9)
         const int etid = threadIdx.x;
-        if (etid < LPR * RPP) {
+        bool packed_out = false;
+        if constexpr (EPI) packed_out = p.epi.packed != 0;
+        if (packed_out) {
+            // C in the packed-B layout (8-column strips of M rows x 16
+            // bytes, C 16-byte aligned): consecutive threads take consecutive
+            // rows of one strip within an M half, so each warp writes 512
+            // contiguous bytes.  Columns at or past N are written as zero.
+            constexpr int CH = C_::TILE_N / 8;
+            for (int i = etid; i < 2 * kTileM * CH; i += kPairThreads) {
+                const int r = i % kTileM, rest = i / kTileM;
+                const int sc = rest % CH, h = rest / CH;
+                const int gm = m_tile * C_::TILE_M + h * 2 * kTileM + (int)rank * kTileM + r;
+                const int gn = n_tile * C_::TILE_N + sc * 8;
+                if (gm >= p.M || gn >= p.N) continue;
+                uint4 v = *reinterpret_cast<const uint4*>(cst + (size_t)(h * kTileM + r) * C_::C_PITCH + sc * 8);
+                const int lim = p.N - gn;
+                if (lim < 8) {
+                    uint32_t x[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        if (2 * q >= lim) x[q] = 0u;
+                        else if (2 * q + 1 >= lim) x[q] &= 0xffffu;
+                    }
+                    v = make_uint4(x[0], x[1], x[2], x[3]);
+                }
+                *reinterpret_cast<uint4*>(reinterpret_cast<__half*>(p.C) + (((size_t)(gn >> 3) * p.M + gm) << 3)) = v;
+            }
+        } else if (etid < LPR * RPP) {
             const int chunk = etid % LPR;
             const int gn = n_tile * C_::TILE_N + chunk * 8;
             const bool vec_ok = (p.N % 8 == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15u) == 0);

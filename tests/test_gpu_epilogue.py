@@ -84,7 +84,8 @@ def _run(cuda_device, M, N, K, *, bf16=False, bias=False, residual=False, alpha=
     res_bits = _round(rng.standard_normal((M, N)), bf16).reshape(M, N) if residual else None
     strips = (N + 7) // 8
     c_elems = strips * 8 * M if packed else M * N
-    c = torch.zeros(c_elems, dtype=torch.int16, device=cuda_device)
+    # every element of C (the pad columns of a packed C too) must be written
+    c = torch.full((c_elems,), -1, dtype=torch.int16, device=cuda_device)
     res_dev = None
     if residual:
         res_layout = _pack_rowmajor(res_bits, M, N) if packed else res_bits.reshape(-1)
@@ -253,7 +254,8 @@ def test_device_packer_bf16(cuda_device):
 @pytest.mark.parametrize("bf16", [False, True])
 def test_two_m_half_pair_epilogue(cuda_device, monkeypatch, shape, bf16):
     """The 512 x 240 pair kernel with alpha, bias and an activation, fp16 and
-    bf16; calls with a residual or a packed output take the 256 x 256 pair
+    bf16, row-major or packed-B output (N = 500: a partial last strip whose
+    pad columns must be zero); calls with a residual take the 256 x 256 pair
     kernel instead (same results)."""
     import spmm24
 
@@ -264,3 +266,4 @@ def test_two_m_half_pair_epilogue(cuda_device, monkeypatch, shape, bf16):
     _run(cuda_device, M, N, K, bf16=bf16, act=3, seed=M + 5 * N)
     _run(cuda_device, M, N, K, bf16=bf16, residual=True, bias=True, act=1, seed=M + 3 * N)
     _run(cuda_device, M, N, K, bf16=bf16, packed=True, seed=M + N)
+    _run(cuda_device, M, N, K, bf16=bf16, packed=True, bias=True, alpha=-0.5, act=1, seed=M + 9 * N)

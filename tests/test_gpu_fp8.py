@@ -66,7 +66,8 @@ def _run(dev, M, N, K, *, fmt_a=0, fmt_b=0, split=0, bf16=False, bias=False, res
     bias_bits = _round(rng.standard_normal(M), bf16) if bias else None
     res_bits = _round(rng.standard_normal((M, N)), bf16).reshape(M, N) if residual else None
     strips = (N + 7) // 8
-    c = torch.zeros(strips * 8 * M if packed else M * N, dtype=torch.int16, device=dev)
+    # every element of C (the pad columns of a packed C too) must be written
+    c = torch.full((strips * 8 * M if packed else M * N,), -1, dtype=torch.int16, device=dev)
     res_dev = None
     if residual:
         if packed:
@@ -340,11 +341,12 @@ def test_fp8_random_case(cuda_device, case):
 def test_fp8_two_m_half_pair(cuda_device, monkeypatch, shape):
     """The fp8 pair kernel with two M halves (512 x 240 tiles, a two-slot
     metadata ring in TMEM; K = 2560 runs ten stages through it): E4M3 and
-    E5M2, exact integer inputs, the epilogue, and calls with a residual
-    (which keep the 256 x 256 pair kernel)."""
+    E5M2, exact integer inputs, the epilogue, a packed-B output, and calls
+    with a residual (which keep the 256 x 256 pair kernel)."""
     monkeypatch.setenv("SPMM24_PAIR2", "1")
     M, N, K = shape
     _run(cuda_device, M, N, K, seed=M + N + K)
     _run(cuda_device, M, N, K, integer=True, fmt_a=1, fmt_b=0, seed=M + 2 * N)
     _run(cuda_device, M, N, K, bf16=True, bias=True, act=2, alpha=0.02, fmt_b=1, seed=M + 3 * N)
     _run(cuda_device, M, N, K, residual=True, act=1, seed=M + 4 * N)
+    _run(cuda_device, M, N, K, packed=True, bias=True, act=3, fmt_a=1, seed=M + 5 * N)
