@@ -479,6 +479,8 @@ __global__ void __launch_bounds__(kPackThreads) pack_b_kernel(const uint16_t* __
     const int k0 = blockIdx.y * kBTileRows;
     const int n0 = blockIdx.x * kBTileCols;
     const bool vec = (N % 8 == 0) && ((reinterpret_cast<uintptr_t>(b) & 15u) == 0);
+    ptx::grid_dep_wait();  // launched with programmatic serialization: the previous grid may write B or read out
+    if (threadIdx.x == 0) ptx::grid_dep_launch();
     for (int c = threadIdx.x; c < kBTileRows * (kBTileCols / 8); c += kPackThreads) {
         const int r = c / (kBTileCols / 8), x = c % (kBTileCols / 8);
         const int n = n0 + x * 8;
@@ -600,7 +602,6 @@ extern "C" cudaError_t spmm24_pack_b_device(cudaStream_t stream, const void* b_r
     if (reinterpret_cast<uintptr_t>(b_rowmajor) & 1u) return record_invalid("B must be 2-byte aligned");
     if (K / kBTileRows > 65535) return record_invalid("K too large");
     dim3 grid((unsigned)((N + kBTileCols - 1) / kBTileCols), (unsigned)(K / kBTileRows));
-    pack_b_kernel<<<grid, kPackThreads, 0, stream>>>(static_cast<const uint16_t*>(b_rowmajor), K, N,
-                                                     static_cast<uint16_t*>(b_packed_out));
-    return cudaGetLastError();
+    return launch_pdl(pack_b_kernel, grid, stream, static_cast<const uint16_t*>(b_rowmajor), K, N,
+                      static_cast<uint16_t*>(b_packed_out));
 }
