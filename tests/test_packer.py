@@ -59,6 +59,26 @@ def test_packer_matches_oracle(shape):
     assert np.array_equal(spmm24.reorder_metadata(raw, M, K), O.reorder_metadata(oraw, M, K))
 
 
+def test_weights_sharing_b_stack_along_m():
+    """Values and (reordered) metadata are band-major, so layers that share
+    their input B (Q/K/V, gate/up) run as one call on M1 + M2 rows by
+    concatenating their packed arrays: packing the stacked dense matrix gives
+    the same bytes.  fp16 and fp8."""
+    K, M1, M2 = 256, 48, 80
+    a1 = O.prune_magnitude_2of4(O.normal_f16(M1 * K, 21, 0.0, 1.0), M1, K)
+    a2 = O.prune_magnitude_2of4(O.normal_f16(M2 * K, 22, 0.0, 1.0), M2, K)
+    v1, e1 = spmm24.compress_reordered(a1, M1, K)
+    v2, e2 = spmm24.compress_reordered(a2, M2, K)
+    v, e = spmm24.compress_reordered(np.concatenate([a1, a2]), M1 + M2, K)
+    assert np.array_equal(v, np.concatenate([v1, v2])) and np.array_equal(e, np.concatenate([e1, e2]))
+    rng = np.random.default_rng(23)
+    f1 = spmm24.prune_2of4_fp8(O.f32_to_fp8(rng.standard_normal(M1 * K).astype(np.float32), 0), M1, K, 0)
+    f2 = spmm24.prune_2of4_fp8(O.f32_to_fp8(rng.standard_normal(M2 * K).astype(np.float32), 0), M2, K, 0)
+    (w1, m1), (w2, m2) = spmm24.compress_a_fp8(f1, M1, K), spmm24.compress_a_fp8(f2, M2, K)
+    w, m = spmm24.compress_a_fp8(np.concatenate([f1, f2]), M1 + M2, K)
+    assert np.array_equal(w, np.concatenate([w1, w2])) and np.array_equal(m, np.concatenate([m1, m2]))
+
+
 def test_prune_matches_oracle():
     M, K = 64, 256
     a = O.normal_f16(M * K, 77, 0.0, 1.0)
