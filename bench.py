@@ -206,6 +206,21 @@ def make_activations_fp8(torch, K, N, seed):
     return b, b
 
 
+def workload_config(args, world):
+    """The `config` object of the JSON line, identical in both arms."""
+    wl = WORKLOADS[args.workload]
+    shapes = wl["shapes"]
+    shard = bool(wl.get("shard"))
+    fp8 = args.dtype == "fp8"
+    wbytes = sum((M * K // 2 if fp8 else M * K) + M * K // 8 for (M, N, K) in shapes)
+    return {"workload": f"{args.workload}: " + ", ".join(f"{M}x{N}x{K}" for (M, N, K) in shapes),
+            "baseline_config": {"decode": 2, "prefill": 3, "70b": 4, "square": 5}[args.workload],
+            "spmm_per_step": len(shapes), "split_k": "auto (library picker)",
+            "l2": f"inputs larger than L2: {wbytes / 1e6:.0f} MB of distinct weights per step (whole job)",
+            "parallelism": (f"M-sharded x{world} (rows split by spmm24_shard_rows, no reduction)" if shard
+                            else f"replicas x{world} (each rank its own layers)")}
+
+
 def to_dev(torch, arr, dev):
     if arr.dtype.itemsize == 1:
         return torch.from_numpy(arr.view("uint8")).to(dev)
@@ -490,12 +505,7 @@ def run_ours(args, rank, world, local_rank):
                  f"{wl['a_std']}; B N(0,1) in E4M3, N x K)" if fp8 else
                  f"synthetic (seeded torch RNG; A N(0,{wl['a_std']}) magnitude-pruned 2:4, B N(0,1))" if wl["a_std"]
                  else "synthetic (U(-1,1), random 2:4 mask)"),
-        "config": {"workload": f"{args.workload}: " + ", ".join(f"{M}x{N}x{K}" for (M, N, K) in shapes),
-                   "baseline_config": {"decode": 2, "prefill": 3, "70b": 4, "square": 5}[args.workload],
-                   "spmm_per_step": len(calls), "split_k": "auto (library picker)",
-                   "l2": f"inputs larger than L2: {weight_bytes / 1e6:.0f} MB of distinct weights per step",
-                   "parallelism": (f"M-sharded x{world} (rows split by spmm24_shard_rows, no reduction)" if shard
-                                   else f"replicas x{world} (each rank its own layers)")},
+        "config": workload_config(args, world),
         "per_shape_us": {f"{c['M']}x{c['N']}x{c['K']}": round(u, 3) for c, u in zip(calls, per_call)},
         "per_shape_note": "median single-kernel duration with an event pair around each launch",
         "launch_flags": " | ".join(f for f, on in (("SPMM24_STATIC_WEIGHTS", args.static_weights), ("SPMM24_BF16", bf16),
@@ -1233,11 +1243,9 @@ def run_reference(args, rank, world):
     if args.workload == "packb":
         run_reference_pack_b(args)
         return
-    import numpy as np
-    import torch
-
-    import spmm24
-
+    # Inputs come from the oracle's own seeded generators and prune (the
+    # product library is not loaded in this arm); same distributions as the
+    # repo arm's.
     sys.path.insert(0, os.path.join(REPO, "oracle"))
     import oracle as O
 
@@ -1246,10 +1254,15 @@ def run_reference(args, rank, world):
     square = args.workload == "square"
     layers = {}
     for i, (M, K) in enumerate(sorted({(M, K) for (M, N, K) in shapes})):
-        layers[(M, K)] = make_layer(torch, spmm24, M, K, wl["a_std"], seed=i, mask_random=square)
+        if wl["a_std"] is None:
+            a = O.uniform_f16(M * K, seed=i)
+            a = O.random_mask_2of4(a, M, K, seed=100 + i) if square else a
+        else:
+            a = O.prune_magnitude_2of4(O.normal_f16(M * K, seed=i, std=wl["a_std"]), M, K)
+        layers[(M, K)] = (a,)
     acts = {}
     for j, (K, N) in enumerate(sorted({(K, N) for (M, N, K) in shapes})):
-        acts[(K, N)] = make_activations(torch, spmm24, K, N, seed=5000 + j, uniform=square)
+        acts[(K, N)] = ((O.uniform_f16 if square else O.normal_f16)(K * N, seed=5000 + j),)
     threads = host_threads()
 
     def step(rows):
@@ -1280,8 +1293,7 @@ def run_reference(args, rank, world):
         "value": round(value, 6), "unit": "TFLOPS", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(dt * 1e3 / args.steps, 3), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f16 in, f32 accumulate, f16 out", "data": "synthetic",
-        "config": {"workload": f"{args.workload}: " + ", ".join(f"{M}x{N}x{K}" for (M, N, K) in shapes),
-                   "baseline_config": {"decode": 2, "prefill": 3, "70b": 4, "square": 5}[args.workload]},
+        "config": workload_config(args, world),
         "cpu_baseline": {"value": round(value, 6), "unit": "TFLOPS", "cores": threads, "kind": "port",
                          "sample": sample},
         "e2e": {"value": round(value, 6), "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},

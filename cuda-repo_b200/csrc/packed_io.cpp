@@ -117,12 +117,17 @@ extern "C" int spmm24_load_packed_header(const char* path, spmm24_packed_header*
     return rc;
 }
 
-extern "C" int spmm24_load_packed(const char* path, void* values, void* meta) {
+extern "C" int spmm24_load_packed(const char* path, void* values, size_t values_capacity, void* meta,
+                                  size_t meta_capacity) {
     if (!path || !values || !meta) return SPMM24_PACKED_EARG;
     FILE* f = std::fopen(path, "rb");
     if (!f) return SPMM24_PACKED_EIO;
     spmm24_packed_header h;
     int rc = read_header(f, &h);
+    // The payload sizes come from the header read here, which may differ from
+    // an earlier spmm24_load_packed_header call if the file was replaced in
+    // between: nothing is read unless both buffers can hold it.
+    if (rc == 0 && (h.values_bytes > values_capacity || h.meta_bytes > meta_capacity)) rc = SPMM24_PACKED_ECAPACITY;
     if (rc == 0) {
         if (std::fread(values, 1, h.values_bytes, f) != h.values_bytes ||
             std::fread(meta, 1, h.meta_bytes, f) != h.meta_bytes)

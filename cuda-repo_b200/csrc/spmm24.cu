@@ -5,8 +5,9 @@
 // stage / split configuration from the shape (the compile-time N switch of
 // src/SpMM_API.cu:128-154 becomes a runtime picker), encodes the three TMA
 // tensor maps and launches one kernel.  The reference's second launch
-// (SplitK_Reduction) is gone: split-K partials are reduced on chip (cluster
-// path) or by the last contributing CTA (stream-K path).
+// (SplitK_Reduction) is gone: split-K partials are reduced on chip, inside a
+// thread-block cluster (the allocation-free entry point's stream-K kernel
+// reduces through its fixed scratch array instead).
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -54,24 +55,71 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
+// A tensor map is a pure function of its inputs (address, sizes, strides,
+// box, type, swizzle), so encoded maps are kept in a small per-thread cache:
+// a serving loop that calls the same layers again skips the driver's
+// encoder.  Direct-mapped, 64 entries, no locking (each host thread has its
+// own); a freed and re-allocated buffer at the same address with the same
+// shape encodes to the same map, so an entry never goes stale.
+struct MapKey {
+    const void* base;
+    cuuint64_t dims[5];
+    cuuint64_t strides[4];
+    cuuint32_t box[5];
+    int rank, type, swizzle;
+};
+struct MapEntry {
+    MapKey key;
+    CUtensorMap map;
+    bool valid;
+};
+constexpr int kMapCacheSlots = 64;
+thread_local MapEntry t_map_cache[kMapCacheSlots];
+
 // Operands are moved as raw 16-bit words (the fp8 B as bytes): no conversion
 // in TMA.
 bool encode(CUtensorMap* m, int rank, const void* base, const cuuint64_t* dims, const cuuint64_t* strides_bytes,
             const cuuint32_t* box, CUtensorMapDataType type = CU_TENSOR_MAP_DATA_TYPE_UINT16,
             CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_NONE) {
+    if (rank < 1 || rank > 5) return false;
+    MapKey k;
+    std::memset(&k, 0, sizeof(k));  // padding included: keys compare bytewise
+    k.base = base;
+    for (int i = 0; i < rank; ++i) {
+        k.dims[i] = dims[i];
+        k.box[i] = box[i];
+        if (i + 1 < rank) k.strides[i] = strides_bytes[i];
+    }
+    k.rank = rank;
+    k.type = (int)type;
+    k.swizzle = (int)swizzle;
+    uint64_t h = 1469598103934665603ull;  // FNV-1a over the key bytes
+    const unsigned char* kb = reinterpret_cast<const unsigned char*>(&k);
+    for (size_t i = 0; i < sizeof(k); ++i) h = (h ^ kb[i]) * 1099511628211ull;
+    MapEntry& slot = t_map_cache[(h ^ (h >> 29)) % kMapCacheSlots];
+    if (slot.valid && std::memcmp(&slot.key, &k, sizeof(k)) == 0) {
+        *m = slot.map;
+        return true;
+    }
     EncodeTiledFn fn = encode_fn();
     if (!fn) return false;
     cuuint32_t estr[5] = {1, 1, 1, 1, 1};
     CUresult r = fn(m, type, (cuuint32_t)rank, const_cast<void*>(base), dims, strides_bytes, box, estr,
                     CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    return r == CUDA_SUCCESS;
+    if (r != CUDA_SUCCESS) return false;
+    slot.key = k;
+    slot.map = *m;
+    slot.valid = true;
+    return true;
 }
 
-int env_int(const char* name, int dflt) {
-    const char* v = std::getenv(name);
-    return (v && *v) ? std::atoi(v) : dflt;
-}
+// Picker overrides set by spmm24_set_tuning (tests and tuning sweeps); the
+// library reads no environment variables.
+struct Tuning {
+    std::atomic<int> pair{-1}, pair2{-1}, pair_split{0}, tile_n{0}, deep_ring{0};
+};
+Tuning g_tune;
 
 constexpr int kMaxDevices = 64;
 constexpr int kMaxSplit = 8;
@@ -116,14 +164,13 @@ constexpr int kPair2Stages = 3;
 using Pair2C = Pair2Cfg<kPair2Stages>;
 using Pair2C8 = Pair2Cfg<kPair2Stages, true>;
 using PairC8 = PairCfg<kPairStages, true>;
+// Stream-K variants: the scratch-array kernel of spmm24_launch_noalloc.
 using SV16 = StreamKVariant<16, 8>;
 using SV32 = StreamKVariant<32, 8>;
 // Shallow rings (about 92 KB of shared memory): two CTAs fit on one SM, so
 // consecutive launches overlap on the same SM under programmatic launch.
 using CV16s = ClusterVariant<16, 4>;
 using CV32s = ClusterVariant<32, 3>;
-using SV16s = StreamKVariant<16, 4>;
-using SV32s = StreamKVariant<32, 4>;
 
 struct Plan {
     Path path;
@@ -164,7 +211,7 @@ int cluster_smem(int tn) {
 // 4: -19%), 11008 x 512 x 4096 (1 against 2), not 4096 x 512 x 4096 (1
 // wave either way).
 void maybe_pair2(Plan& p, int M, int N, int sms, int tile_n, int stages, int smem) {
-    const int env = env_int("SPMM24_PAIR2", -1);  // tuning override: 0 = never, 1 = whenever legal
+    const int env = g_tune.pair2.load(std::memory_order_relaxed);  // override: 0 = never, 1 = whenever legal
     if (env == 0) return;
     const long long slots = std::max(1, sms / 2);
     const long long m2 = (M + 4 * kTileM - 1) / (4 * kTileM), n2 = (N + tile_n - 1) / tile_n;
@@ -180,48 +227,30 @@ void maybe_pair2(Plan& p, int M, int N, int sms, int tile_n, int stages, int sme
     p.grid = 2 * p.m_tiles * p.n_tiles;
 }
 
-// plain: the plain fp16 launch (the only one the stream-K option serves).
 // allow_pair: the CTA-pair path may be chosen.  max_split: the largest
 // automatic K split.  pair2_ok: the two-M-half pair kernel may be chosen
 // (no residual, no gather).
-Plan make_plan(int M, int N, int K, int split_k, int sms, bool plain = true, bool allow_pair = true,
-               int max_split = kMaxSplit, bool pair2_ok = true) {
+Plan make_plan(int M, int N, int K, int split_k, int sms, bool allow_pair = true, int max_split = kMaxSplit,
+               bool pair2_ok = true) {
     Plan p{};
     int tn = N <= 16 ? 16 : N <= 32 ? 32 : N <= 64 ? 64 : 128;
-    const int forced = env_int("SPMM24_TILE_N", 0);  // tuning override (16/32/64/128/256)
+    const int forced = g_tune.tile_n.load(std::memory_order_relaxed);  // override (16/32/64/128/256)
     if (forced == 16 || forced == 32 || forced == 64 || forced == 128 || forced == 256) tn = forced;
     p.tile_n = tn;
     p.m_tiles = (M + kTileM - 1) / kTileM;
     p.n_tiles = (N + tn - 1) / tn;
     p.stages_total = (K / 64 + 1) / 2;
     const long long tiles = (long long)p.m_tiles * p.n_tiles;
-    const long long units = tiles * p.stages_total;
 
     // Narrow N (decode) streams weights: a 4-stage ring (about 92 KB) puts two
     // CTAs on each SM, so consecutive launches overlap on the same SM under
     // programmatic launch, and the K split fills both slots of every SM.
-    const int stages_env = env_int("SPMM24_STAGES", 0);  // tuning override: 4 or 8
-    p.shallow = tn <= 32 && stages_env != 8;
+    const bool deep = g_tune.deep_ring.load(std::memory_order_relaxed) == 1;  // override: the deepest ring
+    p.shallow = tn <= 32 && !deep;
 
-    // Stream-K (tuning option only; the cluster path measured faster on the
-    // decode shapes): one CTA per SM streaming an equal share of the stages.
-    if (plain && env_int("SPMM24_PATH", 0) == 2 && split_k == 0 && tn <= 32 && units >= 2) {
-        p.path = Path::kStreamK;
-        if (p.shallow) {
-            p.stages = tn == 16 ? SV16s::kStages : SV32s::kStages;
-            p.smem = tn == 16 ? SV16s::C_::SMEM_ALLOC : SV32s::C_::SMEM_ALLOC;
-        } else {
-            p.stages = tn == 16 ? SV16::kStages : SV32::kStages;
-            p.smem = tn == 16 ? SV16::C_::SMEM_ALLOC : SV32::C_::SMEM_ALLOC;
-        }
-        const int g = env_int("SPMM24_GRID", sms);
-        p.grid = (int)std::max<long long>(1, std::min<long long>(g, units));
-        p.split = 1;
-        return p;
-    }
     // Wide N with K % 128 == 0: a CTA pair per 256 x 256 tile (cta_group::2),
     // so each SM feeds the tensor core half of B.
-    const int pair_env = env_int("SPMM24_PAIR", -1);  // tuning override: 0 = never, 1 = whenever legal
+    const int pair_env = g_tune.pair.load(std::memory_order_relaxed);  // override: 0 = never, 1 = whenever legal
     const bool pair_ok = allow_pair && (K % 128 == 0) && (split_k <= 1);
     if (pair_ok && (pair_env == 1 || (pair_env != 0 && N > 128))) {
         p.path = Path::kPair;
@@ -237,7 +266,7 @@ Plan make_plan(int M, int N, int K, int split_k, int sms, bool plain = true, boo
         // time; shorter K or more tiles lose (clusters of 4 leave SMs of
         // every GPC idle, and the 128 KB exchange costs a few us per tile).
         const long long ptiles = (long long)p.m_tiles * p.n_tiles;
-        const int pair_split_env = env_int("SPMM24_PAIR_SPLIT", 0);  // tuning override: 1 or 2
+        const int pair_split_env = g_tune.pair_split.load(std::memory_order_relaxed);  // override: 1 or 2
         int ps = 1;
         if (pair_split_env == 1 || pair_split_env == 2)
             ps = pair_split_env;
@@ -253,7 +282,7 @@ Plan make_plan(int M, int N, int K, int split_k, int sms, bool plain = true, boo
         // 28672 51.9 -> 27.9 us (the per-GPU shards of M-sharded 70B layers);
         // 8192 x 256 x 8192 stays on the pair (29.8 against 32.2 us).
         const bool few = N <= 256 && split_k == 0 && (long long)p.grid < (3LL * sms) / 4;
-        if (!(few && pair_env != 1 && env_int("SPMM24_PAIR2", -1) != 1)) {
+        if (!(few && pair_env != 1 && g_tune.pair2.load(std::memory_order_relaxed) != 1)) {
             if (pair2_ok && ps == 1 && split_k <= 1)
                 maybe_pair2(p, M, N, sms, Pair2C::TILE_N, kPair2Stages, Pair2C::SMEM_ALLOC);
             return p;
@@ -263,7 +292,7 @@ Plan make_plan(int M, int N, int K, int split_k, int sms, bool plain = true, boo
         p.m_tiles = (M + kTileM - 1) / kTileM;
         p.n_tiles = (N + tn - 1) / tn;
         p.stages_total = (K / 64 + 1) / 2;
-        p.shallow = tn <= 32 && stages_env != 8;
+        p.shallow = tn <= 32 && !deep;
         max_split = std::min(max_split, 4);  // measured: 4 beats 8 for 128 x 128 tiles (cl4 12.9 us, cl8 19.5 us)
     }
     p.path = Path::kCluster;
@@ -291,54 +320,6 @@ Plan make_plan(int M, int N, int K, int split_k, int sms, bool plain = true, boo
     p.split = std::max(1, std::min(std::min(s, kMaxSplit), p.stages_total));
     p.grid = p.split * p.n_tiles * p.m_tiles;
     return p;
-}
-
-// ------------------------------------------------------------- workspace
-// Stream-K partial tiles and per-CTA flags, one buffer per (device, stream)
-// so that calls on different streams never share it.  Layout:
-// [flags: counter_cap u32][partials: partial_cap bytes].  The flags sit at
-// a fixed offset whatever the shape, are zeroed when the buffer is
-// (re)allocated, and every launch leaves the ones it used at zero again.
-struct Workspace {
-    void* ptr = nullptr;
-    size_t counter_cap = 0;  // number of u32 counters
-    size_t partial_cap = 0;  // bytes
-};
-std::mutex g_ws_mu;
-std::map<std::pair<int, uintptr_t>, Workspace>* g_ws = new std::map<std::pair<int, uintptr_t>, Workspace>();
-
-cudaError_t get_workspace(int dev, cudaStream_t stream, size_t counters, size_t partial_bytes, uint32_t** ctr,
-                          float** partials) {
-    std::lock_guard<std::mutex> lk(g_ws_mu);
-    Workspace& w = (*g_ws)[{dev, reinterpret_cast<uintptr_t>(stream)}];
-    if (w.ptr == nullptr || w.counter_cap < counters || w.partial_cap < partial_bytes) {
-        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
-        cudaError_t e = cudaStreamIsCapturing(stream, &cs);
-        if (e != cudaSuccess) return e;
-        if (cs != cudaStreamCaptureStatusNone) return cudaErrorStreamCaptureUnsupported;
-        size_t ncap = std::max<size_t>(std::max(counters, w.counter_cap), 16384);
-        size_t pcap = std::max<size_t>(std::max(partial_bytes, w.partial_cap), (size_t)4 << 20);
-        if (w.ptr) {
-            // The old buffer may still be in use by work queued on this stream.
-            if ((e = cudaStreamSynchronize(stream)) != cudaSuccess) return e;
-            cudaFree(w.ptr);
-            w = Workspace{};
-        }
-        const size_t cbytes = (ncap * sizeof(uint32_t) + 255) & ~(size_t)255;
-        void* p = nullptr;
-        if ((e = cudaMalloc(&p, cbytes + pcap)) != cudaSuccess) return e;
-        if ((e = cudaMemsetAsync(p, 0, cbytes, stream)) != cudaSuccess) {
-            cudaFree(p);
-            return e;
-        }
-        w.ptr = p;
-        w.counter_cap = ncap;
-        w.partial_cap = pcap;
-    }
-    const size_t cbytes = (w.counter_cap * sizeof(uint32_t) + 255) & ~(size_t)255;
-    *ctr = static_cast<uint32_t*>(w.ptr);
-    *partials = reinterpret_cast<float*>(static_cast<uint8_t*>(w.ptr) + cbytes);
-    return cudaSuccess;
 }
 
 std::atomic<uint64_t> g_attr_done[96];  // per kernel variant: one bit per device
@@ -503,8 +484,6 @@ cudaError_t make_epilogue(const spmm24_epilogue* user_epi, unsigned flags, const
     return cudaSuccess;
 }
 
-size_t streamk_partial_bytes(const Plan& pl) { return (size_t)pl.grid * kTileM * pl.tile_n * sizeof(float); }
-
 cudaError_t launch_impl(cudaStream_t stream, const void* A, const void* B, const uint16_t* E, void* C, int M, int N,
                         int K, int split_k, unsigned flags, const spmm24_epilogue* user_epi = nullptr,
                         const spmm24_gather* gather = nullptr) {
@@ -540,35 +519,11 @@ cudaError_t launch_impl(cudaStream_t stream, const void* A, const void* B, const
             epi.gather_mc = static_cast<uint16_t*>(gather->c_multicast);
         }
     }
-    const bool plain = epi.bias == nullptr && epi.residual == nullptr && epi.act == kActNone && epi.alpha == 1.f &&
-                       !epi.packed && !epi.bf16 && epi.gather_n == 0;
-
     int dev = 0;
     e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     const bool pair2_ok = !epi.residual && epi.gather_n == 0;
-    Plan pl = make_plan(M, N, K, split_k, sm_count(dev), plain, true, kMaxSplit, pair2_ok);
-
-    uint32_t* ws_counters = nullptr;
-    float* ws_partials = nullptr;
-    if (pl.path == Path::kStreamK) {
-        e = get_workspace(dev, stream, (size_t)pl.grid, streamk_partial_bytes(pl), &ws_counters, &ws_partials);
-        if (e == cudaErrorStreamCaptureUnsupported) {
-            // First use of this stream under graph capture: no allocation is
-            // allowed, so fall back to the workspace-free cluster path.
-            cudaGetLastError();
-            pl = make_plan(M, N, K, 0, sm_count(dev));
-            pl.path = Path::kCluster;
-            pl.shallow = false;
-            pl.stages = cluster_stages(pl.tile_n);
-            pl.smem = cluster_smem(pl.tile_n);
-            int s = std::max(1, std::min((int)(sm_count(dev) / ((long long)pl.m_tiles * pl.n_tiles)),
-                                         pl.stages_total / 2));
-            pl.split = std::max(1, std::min(std::min(s, kMaxSplit), pl.stages_total));
-        } else if (e != cudaSuccess) {
-            return e;
-        }
-    }
+    Plan pl = make_plan(M, N, K, split_k, sm_count(dev), true, kMaxSplit, pair2_ok);
 
     // A: (128 halves of one 16x8 block, bands, 16-K blocks); box 8 bands x 8 blocks.
     CUtensorMap ta, tb, te;
@@ -615,28 +570,6 @@ cudaError_t launch_impl(cudaStream_t stream, const void* A, const void* B, const
         if (pl.pair2) return launch_pair2(pl, stream, dev, pdl, ta, tb, te, kp);
         return launch_pair(pl, stream, dev, pdl, ta, tb, te, kp);
     }
-    if (pl.path == Path::kStreamK) {
-        StreamKParams kp;
-        kp.C = static_cast<__half*>(C);
-        kp.ws = ws_partials;
-        kp.flags = ws_counters;
-        kp.M = M;
-        kp.N = N;
-        kp.K = K;
-        kp.groups = K / 64;
-        kp.stages_per_tile = pl.stages_total;
-        kp.m_tiles = pl.m_tiles;
-        kp.n_tiles = pl.n_tiles;
-        kp.units = (long long)pl.m_tiles * pl.n_tiles * pl.stages_total;
-        kp.grid = pl.grid;
-        kp.weights_static = wstatic;
-        if (pl.shallow) {
-            if (pl.tile_n == 16) return launch_streamk<SV16s>(pl, stream, dev, pdl, ta, tb, te, kp, 7);
-            return launch_streamk<SV32s>(pl, stream, dev, pdl, ta, tb, te, kp, 8);
-        }
-        if (pl.tile_n == 16) return launch_streamk<SV16>(pl, stream, dev, pdl, ta, tb, te, kp, 5);
-        return launch_streamk<SV32>(pl, stream, dev, pdl, ta, tb, te, kp, 6);
-    }
     ClusterParams kp;
     kp.C = static_cast<uint16_t*>(C);
     kp.epi = epi;
@@ -680,7 +613,7 @@ int fp8_smem() {
 
 Plan plan_fp8(int M, int N, int K, int split_k, int sms, bool pair2_ok) {
     const int Kh = K / 2;
-    Plan pl = make_plan(M, N, Kh, split_k, sms, false, Kh % 128 == 0, 5, false);
+    Plan pl = make_plan(M, N, Kh, split_k, sms, Kh % 128 == 0, 5, false);
     if (pl.path == Path::kPair) {
         pl.smem = PairC8::SMEM_ALLOC;
         if (pl.split == 1 && split_k <= 1 && pair2_ok)
@@ -1120,6 +1053,25 @@ int current_sms() {
 void fill_config(const Plan& pl, int stage_k, spmm24_config* out);
 }  // namespace
 }  // namespace spmm24
+
+extern "C" cudaError_t spmm24_set_tuning(const spmm24_tuning* t) {
+    spmm24::clear_last_error();
+    spmm24_tuning v{-1, -1, 0, 0, 0};
+    if (t) {
+        v = *t;
+        const bool tn_ok = v.tile_n == 0 || v.tile_n == 16 || v.tile_n == 32 || v.tile_n == 64 || v.tile_n == 128 ||
+                           v.tile_n == 256;
+        if (v.pair < -1 || v.pair > 1 || v.pair2 < -1 || v.pair2 > 1 || v.pair_split < 0 || v.pair_split > 2 || !tn_ok ||
+            v.deep_ring < 0 || v.deep_ring > 1)
+            return spmm24::record_invalid("tuning: a field is out of range");
+    }
+    spmm24::g_tune.pair.store(v.pair);
+    spmm24::g_tune.pair2.store(v.pair2);
+    spmm24::g_tune.pair_split.store(v.pair_split);
+    spmm24::g_tune.tile_n.store(v.tile_n);
+    spmm24::g_tune.deep_ring.store(v.deep_ring);
+    return cudaSuccess;
+}
 
 extern "C" int spmm24_select_config(int M, int N, int K, int split_k, spmm24_config* out) {
     if (!out || M <= 0 || N <= 0 || K <= 0 || M % 16 || K % 64 || split_k < 0) return -1;

@@ -60,7 +60,7 @@ _lib.spmm24_save_packed.argtypes = [ctypes.c_char_p, ctypes.c_int, ctypes.c_int,
 _lib.spmm24_save_packed.restype = ctypes.c_int
 _lib.spmm24_load_packed_header.argtypes = [ctypes.c_char_p, ctypes.POINTER(PackedHeader)]
 _lib.spmm24_load_packed_header.restype = ctypes.c_int
-_lib.spmm24_load_packed.argtypes = [ctypes.c_char_p, _vp, _vp]
+_lib.spmm24_load_packed.argtypes = [ctypes.c_char_p, _vp, ctypes.c_size_t, _vp, ctypes.c_size_t]
 _lib.spmm24_load_packed.restype = ctypes.c_int
 
 
@@ -239,6 +239,29 @@ def select_config(M: int, N: int, K: int, split_k: int = 0) -> dict:
     if _lib.spmm24_select_config(M, N, K, split_k, ctypes.byref(cfg)) != 0:
         raise ValueError("unsupported shape")
     return {n: getattr(cfg, n) for n, _ in SpmmConfig._fields_}
+
+
+class Tuning(ctypes.Structure):
+    """spmm24_tuning (include/spmm24/SpMM_API.h)."""
+    _fields_ = [(n, ctypes.c_int) for n in ("pair", "pair2", "pair_split", "tile_n", "deep_ring")]
+
+
+_lib.spmm24_set_tuning.argtypes = [ctypes.POINTER(Tuning)]
+_lib.spmm24_set_tuning.restype = ctypes.c_int
+
+
+def set_tuning(pair: int = -1, pair2: int = -1, pair_split: int = 0, tile_n: int = 0, deep_ring: int = 0) -> None:
+    """spmm24_set_tuning: process-wide picker override (tests and tuning
+    sweeps); called with no arguments it restores the automatic choice."""
+    t = Tuning(pair, pair2, pair_split, tile_n, deep_ring)
+    rc = _lib.spmm24_set_tuning(ctypes.byref(t))
+    if rc != 0:
+        raise ValueError(f"spmm24_set_tuning: {_lib.spmm24_last_error().decode()}")
+
+
+def reset_tuning() -> None:
+    """Restores the automatic kernel choice."""
+    _lib.spmm24_set_tuning(None)
 
 
 def select_config_fp8(M: int, N: int, K: int, split_k: int = 0) -> dict:
@@ -503,7 +526,8 @@ def pack_a_fp8_device(dense, M: int, K: int, prune: int = 0, values=None, meta=N
 
 # ------------------------------------------------- packed-weight files
 PACKED_ERRORS = {-1: "bad argument or shape", -2: "I/O error or short file",
-                 -3: "not a packed-weight file (magic, version or size)", -4: "checksum mismatch"}
+                 -3: "not a packed-weight file (magic, version or size)", -4: "checksum mismatch",
+                 -5: "the file's payload is larger than the buffers given (file changed after its header was read)"}
 
 
 def save_packed(path: str, values: np.ndarray, meta: np.ndarray, M: int, K: int, bf16: bool = False) -> None:
@@ -527,7 +551,7 @@ def load_packed(path: str):
         raise ValueError("an fp8 packed-weight file: use load_packed_fp8")
     v = np.empty(h.values_bytes // 2, dtype=np.uint16)
     m = np.empty(h.meta_bytes // 2, dtype=np.uint16)
-    rc = _lib.spmm24_load_packed(os.fsencode(path), v.ctypes.data, m.ctypes.data)
+    rc = _lib.spmm24_load_packed(os.fsencode(path), v.ctypes.data, v.nbytes, m.ctypes.data, m.nbytes)
     if rc != 0:
         raise OSError(f"spmm24_load_packed: {PACKED_ERRORS.get(rc, rc)}")
     return v, m, int(h.M), int(h.K), bool(h.dtype == 1)
@@ -554,7 +578,7 @@ def load_packed_fp8(path: str):
         raise ValueError("a 16-bit packed-weight file: use load_packed")
     v = np.empty(h.values_bytes, dtype=np.uint8)
     m = np.empty(h.meta_bytes, dtype=np.uint8)
-    rc = _lib.spmm24_load_packed(os.fsencode(path), v.ctypes.data, m.ctypes.data)
+    rc = _lib.spmm24_load_packed(os.fsencode(path), v.ctypes.data, v.nbytes, m.ctypes.data, m.nbytes)
     if rc != 0:
         raise OSError(f"spmm24_load_packed: {PACKED_ERRORS.get(rc, rc)}")
     return v, m, int(h.M), int(h.K), int(h.dtype) - 2

@@ -49,10 +49,9 @@ extern "C" {
  *             reproducible for a fixed split_k on a fixed GPU.
  *   split_reduction  accepted for ABI compatibility and never touched, so it
  *             may be NULL.
- * Memory: this call allocates nothing.  (Only the stream-K tuning path,
- * selected with the environment variable SPMM24_PATH=2, keeps a workspace of
- * a few MB per device and stream, allocated on its first use; during CUDA
- * graph capture it falls back to the default path instead of allocating.)
+ * Memory: this call allocates nothing and keeps no workspace.  Encoded TMA
+ * descriptors are cached per host thread (64 entries), so repeated calls on
+ * the same buffers skip the driver's encoder.
  * The kernel is launched with programmatic stream serialization: it may
  * start its set-up while the previous kernel in the stream finishes, and
  * waits for that kernel before touching global memory.
@@ -181,7 +180,10 @@ cudaError_t spmm24_ipc_close(void* dev_ptr);
  *   spmm24_last_error().
  *   The first call on a device looks up the scratch array's device address
  *   (cudaGetSymbolAddress, with that device current); make that first call
- *   before any stream capture.
+ *   before any stream capture.  The address is kept for the life of the
+ *   process: do not call this entry point on a device after
+ *   cudaDeviceReset on it (the module is loaded again and the array may
+ *   move).
  *   All calls share the one scratch array and every call starts by clearing
  *   the flag words it uses: calls that overlap on the GPU (different
  *   streams, or different host threads) race and must be serialised by the
@@ -308,7 +310,8 @@ enum {
     SPMM24_PACKED_EARG = -1,     /* bad argument or shape (M % 16, K % 64) */
     SPMM24_PACKED_EIO = -2,      /* open / read / write failed, or short file */
     SPMM24_PACKED_EFORMAT = -3,  /* not a packed-weight file, unknown version, or trailing bytes */
-    SPMM24_PACKED_ECHECKSUM = -4 /* payload does not match its checksum */
+    SPMM24_PACKED_ECHECKSUM = -4, /* payload does not match its checksum */
+    SPMM24_PACKED_ECAPACITY = -5  /* the payload is larger than the buffers passed to spmm24_load_packed */
 };
 typedef struct spmm24_packed_header {
     uint32_t version, dtype, M, K;
@@ -316,11 +319,15 @@ typedef struct spmm24_packed_header {
 } spmm24_packed_header;
 int spmm24_save_packed(const char* path, int dtype, int M, int K, const void* values, const void* meta);
 int spmm24_load_packed_header(const char* path, spmm24_packed_header* out);
-/* values: values_bytes, meta: meta_bytes (from the header). */
-int spmm24_load_packed(const char* path, void* values, void* meta);
+/* Reads the payload into values (values_capacity bytes) and meta
+ * (meta_capacity bytes), normally sized from spmm24_load_packed_header.  The
+ * header is read again inside this call; if its payload sizes exceed either
+ * capacity (the file was replaced or grew after the header was read),
+ * nothing is read and SPMM24_PACKED_ECAPACITY is returned. */
+int spmm24_load_packed(const char* path, void* values, size_t values_capacity, void* meta, size_t meta_capacity);
 
-/* Workspace the caller must pass as split_reduction: always 0 bytes (any
- * workspace is owned by the library, see spmm24_launch).
+/* Workspace the caller must pass as split_reduction: always 0 bytes (the
+ * split-K reduction runs on chip; no launch path keeps a workspace).
  * Replaces the Split_K*M*N halves contract of test/kernelTest.cu:136. */
 size_t spmm24_workspace_bytes(int M, int N, int K, int split_k);
 
@@ -332,13 +339,29 @@ typedef struct spmm24_config {
     int tile_n;      /* columns per tile */
     int stage_k;     /* logical K per pipeline stage (128) */
     int stages;      /* pipeline depth */
-    int split_k;     /* CTAs per cluster along K (0 on the stream-K path) */
+    int split_k;     /* CTAs per cluster along K */
     int grid_ctas;   /* CTAs launched */
     int smem_bytes;  /* dynamic shared memory per CTA */
-    int stream_k;    /* 1: persistent stream-K kernel, 0: cluster kernel */
+    int stream_k;    /* always 0: spmm24_launch never picks the stream-K kernel (spmm24_launch_noalloc's) */
     int cta_pair;    /* 1: 256 x 256 tiles on CTA pairs (cta_group::2 MMAs) */
 } spmm24_config;
 int spmm24_select_config(int M, int N, int K, int split_k, spmm24_config* out);
+/* Process-wide override of the kernel picker (no counterpart in the
+ * reference, whose tile configuration is fixed at compile time,
+ * src/TileConfig.h:60-94, src/SpMM_API.cu:128-154).  For tests and tuning
+ * sweeps that must reach one specific kernel; production callers never
+ * need it, and the library reads no environment variables.  Applies to the
+ * launches that follow on every thread; NULL restores the automatic choice.
+ * Returns cudaErrorInvalidValue for an out-of-range field. */
+typedef struct spmm24_tuning {
+    int pair;       /* -1 auto; 0 never use the CTA-pair kernels; 1 whenever legal (K % 128 == 0, split_k <= 1) */
+    int pair2;      /* -1 auto; 0 never use the two-M-half pair kernel; 1 whenever the pair path allows it */
+    int pair_split; /* 0 auto; 1 or 2 K halves per pair tile */
+    int tile_n;     /* 0 auto; 16, 32, 64, 128 or 256: the cluster kernel's tile width */
+    int deep_ring;  /* 0 auto (a shallow ring, two CTAs per SM, for tile_n <= 32); 1 the deepest ring */
+} spmm24_tuning;
+cudaError_t spmm24_set_tuning(const spmm24_tuning* t);
+
 /* The same for spmm24_launch_fp8 (stage_k 256: a stage carries 256 logical
  * K of fp8 operands; K % 128 == 0), for an epilogue without a residual or a
  * packed output. */
@@ -382,7 +405,19 @@ const char* spmm24_version(void);
 /* C++ drop-ins with the reference's exact names and types. */
 
 /* src/SpMM_API.cu:61-70 (the stale 7-argument declaration of
- * build/SpMM_API.cuh:15-22 is replaced by the 9-argument definition). */
+ * build/SpMM_API.cuh:15-22 is replaced by the 9-argument definition).
+ * Same call as spmm24_launch, with two differences from the reference a
+ * migrating caller should know:
+ *   Split_Reduction is never read or written (the split-K partial sums are
+ *     reduced on chip), so it may be NULL; the reference used it as the
+ *     Split_K * M * N fp16 scratch of its second, reduction launch.
+ *   Split_K is a request, not a guarantee of the launch shape: 0 lets the
+ *     library choose, 1..8 asks for that many K slices (clamped to the number
+ *     of 128-wide K stages; above 8 means 8), and a wide-N shape on the
+ *     CTA-pair kernels runs unsplit.  The result differs only in fp32
+ *     summation order.
+ * Unsupported shapes return cudaErrorInvalidValue (the reference returned
+ * success without launching). */
 cudaError_t SpMM_N2M4_Launch(cudaStream_t stream, const half* Compressed_A, const half* B, const uint16_t* metadata,
                              half* C, const int M_Global, const int N_Global, const int K_Global,
                              half* Split_Reduction, const int Split_K);

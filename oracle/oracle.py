@@ -33,11 +33,18 @@ _u8p = ctypes.POINTER(ctypes.c_uint8)
 _f32p = ctypes.POINTER(ctypes.c_float)
 
 
+def reference_dir() -> str:
+    """The reference checkout: $SPMM24_REFERENCE_DIR, else a directory named
+    `reference` beside this repository (it need not exist)."""
+    return os.environ.get("SPMM24_REFERENCE_DIR") or os.path.join(os.path.dirname(os.path.dirname(_HERE)), "reference")
+
+
 def build() -> None:
     """Compile liboracle.so (and oracle/_ref when the reference tree exists)."""
     subprocess.check_call(["make", "-s", "-C", _HERE])
-    if os.path.isdir("/root/reference"):
-        subprocess.check_call(["make", "-s", "-C", _HERE, "ref"])
+    ref = reference_dir()
+    if os.path.isdir(ref):
+        subprocess.check_call(["make", "-s", "-C", _HERE, "ref", f"REFERENCE={ref}"])
 
 
 _lib = None

@@ -25,3 +25,12 @@ def cuda_device():
     if (major, minor) != (10, 0):
         pytest.skip(f"needs sm_100 (got sm_{major}{minor})")
     return torch.device("cuda:0")
+
+
+@pytest.fixture
+def tuning():
+    """spmm24.set_tuning for one test, reset to the automatic picker after it."""
+    import spmm24
+
+    yield spmm24.set_tuning
+    spmm24.reset_tuning()

@@ -195,3 +195,32 @@ def test_select_config_picks_tiles_and_splits():
         assert spmm24.select_config(1024, n, 1024, 1)["tile_n"] == t
     with pytest.raises(ValueError):
         spmm24.select_config(100, 16, 256)
+
+
+def test_tuning_overrides_and_no_environment(monkeypatch):
+    """spmm24_set_tuning steers the picker; out-of-range fields are refused;
+    reset restores the automatic choice; environment variables of the old
+    tuning knobs have no effect."""
+    try:
+        spmm24.set_tuning(pair=1)
+        assert spmm24.select_config(384, 40, 512)["cta_pair"] == 1
+        spmm24.set_tuning(pair=0, tile_n=256)
+        c = spmm24.select_config(256, 256, 1024)
+        assert c["cta_pair"] == 0 and c["tile_n"] == 256
+        spmm24.set_tuning(pair2=1)
+        assert spmm24.select_config(1024, 480, 512)["tile_m"] == 512
+        spmm24.set_tuning(pair=1, pair2=0, pair_split=2)
+        assert spmm24.select_config(1024, 512, 4096)["split_k"] == 2
+        spmm24.set_tuning(deep_ring=1)
+        assert spmm24.select_config(4096, 16, 4096)["stages"] == 8
+        for bad in ({"pair": 2}, {"pair2": -2}, {"pair_split": 3}, {"tile_n": 48}, {"deep_ring": 2}):
+            with pytest.raises(ValueError, match="out of range"):
+                spmm24.set_tuning(**bad)
+    finally:
+        spmm24.reset_tuning()
+    auto = spmm24.select_config(384, 40, 512)
+    assert auto["cta_pair"] == 0
+    for name, val in (("SPMM24_PAIR", "1"), ("SPMM24_TILE_N", "256"), ("SPMM24_STAGES", "8"), ("SPMM24_PATH", "2")):
+        monkeypatch.setenv(name, val)
+    assert spmm24.select_config(384, 40, 512) == auto
+    assert spmm24.select_config(4096, 16, 4096)["stages"] == 4

@@ -39,3 +39,27 @@ def test_unknown_epilogue_is_rejected():
     out = subprocess.run([sys.executable, os.path.join(REPO, "bench.py"), "--epilogue", "nope"], capture_output=True,
                          text=True, timeout=120, cwd=REPO)
     assert out.returncode != 0 and "packed_b" in out.stderr
+
+
+def test_reference_arm_decode_uses_only_the_oracle():
+    """The default workload's reference arm: one JSON line whose config equals
+    the repo arm's, computed without loading the product library."""
+    code = ("import sys, runpy; sys.argv = ['bench.py', '--impl', 'reference', '--steps', '1', '--warmup', '3'];"
+            "runpy.run_path('bench.py', run_name='__main__');"
+            "maps = open('/proc/self/maps').read();"
+            "assert 'libspmm24' not in maps, 'product library loaded';"
+            "assert 'spmm24' not in sys.modules")
+    out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=600, cwd=REPO)
+    assert out.returncode == 0, out.stderr[-2000:]
+    lines = [l for l in out.stdout.splitlines() if l.startswith("{")]
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    assert d["impl"] == "reference" and d["unit"] == "TFLOPS" and d["value"] > 0
+    sys.path.insert(0, REPO)
+    import argparse
+
+    import bench
+
+    ours = bench.workload_config(argparse.Namespace(workload="decode", dtype="f16"), 1)
+    assert d["config"] == ours
+    assert d["cpu_baseline"]["kind"] == "port" and d["e2e"]["value"] == d["value"]

@@ -252,14 +252,14 @@ def test_device_packer_bf16(cuda_device):
 
 @pytest.mark.parametrize("shape", [(1024, 480, 512), (592, 500, 384), (2048, 1024, 1024)], ids=lambda s: "x".join(map(str, s)))
 @pytest.mark.parametrize("bf16", [False, True])
-def test_two_m_half_pair_epilogue(cuda_device, monkeypatch, shape, bf16):
+def test_two_m_half_pair_epilogue(cuda_device, tuning, shape, bf16):
     """The 512 x 240 pair kernel with alpha, bias and an activation, fp16 and
     bf16, row-major or packed-B output (N = 500: a partial last strip whose
     pad columns must be zero); calls with a residual take the 256 x 256 pair
     kernel instead (same results)."""
     import spmm24
 
-    monkeypatch.setenv("SPMM24_PAIR2", "1")
+    tuning(pair2=1)
     M, N, K = shape
     assert spmm24.select_config(M, N, K)["tile_m"] == 512
     _run(cuda_device, M, N, K, bf16=bf16, bias=True, alpha=0.5, act=2, seed=M + 7 * N)

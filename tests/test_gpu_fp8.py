@@ -54,13 +54,11 @@ def _problem(M, N, K, fmt_a, fmt_b, seed, integer=False):
 
 
 def _run(dev, M, N, K, *, fmt_a=0, fmt_b=0, split=0, bf16=False, bias=False, residual=False, alpha=1.0, act=0,
-         packed=False, seed=0, integer=False, tile_env=None, monkeypatch=None):
+         packed=False, seed=0, integer=False):
     import torch
 
     import spmm24
 
-    if tile_env is not None:
-        monkeypatch.setenv("SPMM24_TILE_N", str(tile_env))
     vals, meta, b_bits, acc, S = _problem(M, N, K, fmt_a, fmt_b, seed, integer)
     rng = np.random.default_rng(seed + 7)
     bias_bits = _round(rng.standard_normal(M), bf16) if bias else None
@@ -161,11 +159,11 @@ def test_fp8_epilogue_bf16_out(cuda_device):
     _run(cuda_device, 256, 40, 512, residual=True, packed=True, act=1, seed=23)
 
 
-def test_fp8_wide_tile(cuda_device, monkeypatch):
+def test_fp8_wide_tile(cuda_device, tuning):
     """The cluster kernel's 256-column tile (a tuning override; wide N
     otherwise takes the CTA pair)."""
-    monkeypatch.setenv("SPMM24_PAIR", "0")
-    _run(cuda_device, 256, 256, 1024, seed=31, tile_env=256, monkeypatch=monkeypatch)
+    tuning(pair=0, tile_n=256)
+    _run(cuda_device, 256, 256, 1024, seed=31)
 
 
 # CTA-pair kernel (N > 128, K % 256 == 0): 256 x 256 tiles, M and N ragged.
@@ -179,34 +177,33 @@ PAIR_SHAPES = [
 
 
 @pytest.mark.parametrize("shape", PAIR_SHAPES, ids=lambda s: "x".join(map(str, s)))
-def test_fp8_pair_matches_oracle(cuda_device, monkeypatch, shape):
+def test_fp8_pair_matches_oracle(cuda_device, tuning, shape):
     import spmm24
 
-    monkeypatch.setenv("SPMM24_PAIR", "1")  # also the few-tile shapes the picker gives to split-K clusters
+    tuning(pair=1)  # also the few-tile shapes the picker gives to split-K clusters
     M, N, K = shape
     assert spmm24.select_config_fp8(M, N, K)["cta_pair"] == 1
     _run(cuda_device, M, N, K, seed=M + 3 * N + K)
 
 
-def test_fp8_pair_integer_exact_and_formats(cuda_device, monkeypatch):
-    monkeypatch.setenv("SPMM24_PAIR", "1")
+def test_fp8_pair_integer_exact_and_formats(cuda_device, tuning):
+    tuning(pair=1)
     _run(cuda_device, 512, 256, 1024, integer=True, seed=51)
     _run(cuda_device, 256, 512, 512, integer=True, fmt_a=1, fmt_b=0, seed=52)
     _run(cuda_device, 512, 264, 768, fmt_a=0, fmt_b=1, seed=53)
     _run(cuda_device, 256, 256, 1280, fmt_a=1, fmt_b=1, seed=54)
 
 
-def test_fp8_pair_k_split(cuda_device, monkeypatch):
+def test_fp8_pair_k_split(cuda_device, tuning):
     """Two pairs per tile, each half of K, partial exchanged on chip."""
-    monkeypatch.setenv("SPMM24_PAIR_SPLIT", "2")
-    monkeypatch.setenv("SPMM24_PAIR", "1")
+    tuning(pair=1, pair_split=2)
     _run(cuda_device, 512, 512, 4096, seed=61)
     _run(cuda_device, 256, 256, 2816, seed=62)  # odd number of 256-K stages
     _run(cuda_device, 512, 256, 2048, bias=True, act=3, alpha=0.5, seed=63)
 
 
-def test_fp8_pair_epilogue(cuda_device, monkeypatch):
-    monkeypatch.setenv("SPMM24_PAIR", "1")
+def test_fp8_pair_epilogue(cuda_device, tuning):
+    tuning(pair=1)
     _run(cuda_device, 512, 256, 1024, bf16=True, bias=True, residual=True, alpha=0.25, act=2, seed=71)
     _run(cuda_device, 256, 264, 512, residual=True, packed=True, act=1, seed=72)
 
@@ -338,12 +335,12 @@ def test_fp8_random_case(cuda_device, case):
 @pytest.mark.parametrize("shape", [(512, 240, 256), (1024, 480, 1024), (592, 500, 768), (2048, 2048, 2048),
                                    (1024, 720, 2560)],
                          ids=lambda s: "x".join(map(str, s)))
-def test_fp8_two_m_half_pair(cuda_device, monkeypatch, shape):
+def test_fp8_two_m_half_pair(cuda_device, tuning, shape):
     """The fp8 pair kernel with two M halves (512 x 240 tiles, a two-slot
     metadata ring in TMEM; K = 2560 runs ten stages through it): E4M3 and
     E5M2, exact integer inputs, the epilogue, a packed-B output, and calls
     with a residual (which keep the 256 x 256 pair kernel)."""
-    monkeypatch.setenv("SPMM24_PAIR2", "1")
+    tuning(pair2=1)
     M, N, K = shape
     _run(cuda_device, M, N, K, seed=M + N + K)
     _run(cuda_device, M, N, K, integer=True, fmt_a=1, fmt_b=0, seed=M + 2 * N)

@@ -77,36 +77,43 @@ def test_shapes_and_splits(cuda_device, shape, split_k):
     check(p, split_k, cuda_device)
 
 
-@pytest.mark.parametrize("grid", [1, 2, 3, 7, 33, 100, 148, 500])
-@pytest.mark.parametrize("shape", [(256, 16, 1024), (1152, 8, 704), (144, 12, 320), (4096, 32, 4096), (128, 1, 320)])
-def test_stream_k_grids(cuda_device, shape, grid, monkeypatch):
-    """The stream-K path (split_k = 0, narrow N) with forced grid sizes: tiles
-    split across one, two or many CTAs, single-unit tiles, ragged M and N,
-    odd 64-K group counts, and more CTAs requested than units exist."""
-    import spmm24
-
-    M, N, K = shape
-    monkeypatch.setenv("SPMM24_PATH", "2")
-    monkeypatch.setenv("SPMM24_GRID", str(grid))
-    monkeypatch.setenv("SPMM24_STAGES", "8" if grid % 2 else "4")
-    assert spmm24.select_config(M, N, K)["stream_k"] == 1
-    p = make_problem(M, N, K, seed=grid + M)
-    first = check(p, 0, cuda_device)
-    # counters reset themselves: a second launch on the same workspace agrees bitwise
-    assert np.array_equal(first, run_gpu(p, 0, cuda_device))
-
-
-@pytest.mark.parametrize("stages", ["4", "8"])
-@pytest.mark.parametrize("path", ["1", "2"])
-def test_flags_and_streams(cuda_device, monkeypatch, path, stages):
-    """Static-weight prefetch, launches without PDL, and two streams (each gets
-    its own stream-K workspace) all give the same bits, on both kernels."""
+@pytest.mark.parametrize("shape", [(128, 1, 320), (144, 12, 320), (256, 16, 1024), (1152, 8, 704), (4096, 32, 4096),
+                                   (16, 1, 64)])
+def test_stream_k_kernel_shapes(cuda_device, shape):
+    """The stream-K kernel (the allocation-free entry point's): grids of 3,
+    6, 16, 54 and 148 CTAs sharing tiles, single-unit tiles, ragged M and N,
+    odd 64-K group counts; a second call (its flags cleared again) agrees bit
+    for bit."""
     import torch
 
     import spmm24
 
-    monkeypatch.setenv("SPMM24_PATH", path)
-    monkeypatch.setenv("SPMM24_STAGES", stages)
+    M, N, K = shape
+    p = make_problem(M, N, K, seed=M + 7 * N)
+    A = _to_dev(torch, p.vals, cuda_device)
+    E = _to_dev(torch, p.meta, cuda_device)
+    B = _to_dev(torch, p.b_packed, cuda_device)
+    outs = []
+    for _ in range(2):
+        C = torch.full((M, N), float("nan"), dtype=torch.float16, device=cuda_device)
+        rc = spmm24._lib.spmm24_launch_noalloc(torch.cuda.current_stream(cuda_device).cuda_stream, A.data_ptr(),
+                                               B.data_ptr(), E.data_ptr(), C.data_ptr(), M, N, K)
+        assert rc == 0, spmm24._lib.spmm24_last_error().decode()
+        torch.cuda.synchronize(cuda_device)
+        outs.append(C.view(torch.int16).cpu().numpy().view(np.uint16))
+    assert within_tolerance(compare(outs[0], oracle_c(p)))
+    assert np.array_equal(outs[0], outs[1])
+
+
+@pytest.mark.parametrize("deep_ring", [0, 1])
+def test_flags_and_streams(cuda_device, tuning, deep_ring):
+    """Static-weight prefetch, launches without PDL, and a second stream all
+    give the same bits, with the shallow (two CTAs per SM) and the deep ring."""
+    import torch
+
+    import spmm24
+
+    tuning(deep_ring=deep_ring)
     p = make_problem(2048, 16, 2048, seed=12, a_scale=0.02, b_dist="normal")
     ref = check(p, 0, cuda_device)
     assert np.array_equal(ref, run_gpu(p, 0, cuda_device, flags=spmm24.STATIC_WEIGHTS))
@@ -162,15 +169,13 @@ def test_back_to_back_calls_pdl(cuda_device):
     (768, 520, 3200),    # odd stage count split unevenly, ragged N
 ])
 @pytest.mark.parametrize("split", [1, 2])
-def test_cta_pair_kernel(cuda_device, monkeypatch, shape, split):
+def test_cta_pair_kernel(cuda_device, tuning, shape, split):
     """The cta_group::2 pair kernel (256 x 256 tiles, K % 128 == 0), one pair
     per tile or two pairs along K reducing through distributed shared
     memory."""
     import spmm24
 
-    monkeypatch.setenv("SPMM24_PAIR_SPLIT", str(split))
-    monkeypatch.setenv("SPMM24_PAIR2", "0")
-    monkeypatch.setenv("SPMM24_PAIR", "1")  # also the few-tile shapes the picker gives to split-K clusters
+    tuning(pair=1, pair2=0, pair_split=split)  # pair=1: also the few-tile shapes the picker gives to split-K clusters
     M, N, K = shape
     cfg = spmm24.select_config(M, N, K)
     assert cfg["cta_pair"] == 1 and cfg["tile_n"] == 256 and cfg["split_k"] == (split if K >= 256 else 1)
@@ -186,12 +191,12 @@ def test_cta_pair_kernel(cuda_device, monkeypatch, shape, split):
     (2048, 2048, 1024),
     (1536, 4096, 640),   # odd stage count
 ])
-def test_cta_pair_two_m_halves(cuda_device, monkeypatch, shape):
+def test_cta_pair_two_m_halves(cuda_device, tuning, shape):
     """The pair kernel with two M halves per pair (512 x 240 tiles: two
     M=256 MMAs share each B tile, two TMEM accumulators)."""
     import spmm24
 
-    monkeypatch.setenv("SPMM24_PAIR2", "1")
+    tuning(pair2=1)
     M, N, K = shape
     cfg = spmm24.select_config(M, N, K)
     assert cfg["cta_pair"] == 1 and cfg["tile_m"] == 512 and cfg["tile_n"] == 240
@@ -211,11 +216,11 @@ def test_few_tile_wide_n_takes_split_k_clusters(cuda_device, shape):
     check(make_problem(M, N, K, seed=M + 11 * N), 0, cuda_device)
 
 
-def test_cta_pair_forced_small_n(cuda_device, monkeypatch):
+def test_cta_pair_forced_small_n(cuda_device, tuning):
     """The pair kernel forced on N below its tile (most of B is zero-filled)."""
     import spmm24
 
-    monkeypatch.setenv("SPMM24_PAIR", "1")
+    tuning(pair=1)
     assert spmm24.select_config(384, 40, 512)["cta_pair"] == 1
     check(make_problem(384, 40, 512, seed=9), 0, cuda_device)
 

@@ -82,3 +82,30 @@ def test_fp8_round_trip(tmp_path, fmt):
     p.write_bytes(bytes(raw))
     with pytest.raises(OSError, match="checksum"):
         spmm24.load_packed_fp8(str(p))
+
+
+def test_file_replaced_after_header_read(tmp_path):
+    """The buffers are sized from the header; if the file is replaced by a
+    larger one before the payload is read, spmm24_load_packed reads nothing
+    and reports the capacity error instead of writing past the buffers."""
+    import ctypes
+
+    v, m = _packed(64, 256, 2)
+    p = tmp_path / "w.spmm24"
+    spmm24.save_packed(str(p), v, m, 64, 256)
+    h = spmm24.PackedHeader()
+    assert spmm24._lib.spmm24_load_packed_header(bytes(p), ctypes.byref(h)) == 0
+    # guard bytes after each buffer: they must stay untouched
+    guard = 4096
+    vbuf = np.full(h.values_bytes + guard, 0xA5, dtype=np.uint8)
+    mbuf = np.full(h.meta_bytes + guard, 0x5A, dtype=np.uint8)
+    v2, m2 = _packed(128, 256, 3)                       # the replacement: twice the rows
+    spmm24.save_packed(str(p), v2, m2, 128, 256)
+    rc = spmm24._lib.spmm24_load_packed(bytes(p), vbuf.ctypes.data, h.values_bytes, mbuf.ctypes.data, h.meta_bytes)
+    assert rc == -5
+    assert np.all(vbuf == 0xA5) and np.all(mbuf == 0x5A)
+    # with capacities that fit the new file the load succeeds
+    vb = np.empty(128 * 256, dtype=np.uint8)
+    mb = np.empty(128 * 256 // 8, dtype=np.uint8)
+    assert spmm24._lib.spmm24_load_packed(bytes(p), vb.ctypes.data, vb.nbytes, mb.ctypes.data, mb.nbytes) == 0
+    assert np.array_equal(vb.view(np.uint16), v2) and np.array_equal(mb.view(np.uint16), m2)
