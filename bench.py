@@ -332,29 +332,54 @@ def run_ours(args, rank, world, local_rank):
         if rc != 0:
             raise RuntimeError(f"spmm24_launch failed: {rc} {spmm24._lib.spmm24_last_error().decode()}")
 
-    for _ in range(args.warmup):
-        for c in calls:
-            launch(c)
-    torch.cuda.synchronize(dev)
-    if world > 1:
-        dist.barrier()
+    # A step: every SpMM of the workload.  "grouped" issues them as one
+    # spmm24_launch_grouped (one persistent kernel for all the step's N <= 32
+    # layers); "chain" issues one spmm24_launch per SpMM.
+    grouped = args.launch == "grouped" and not fp8 and args.epilogue == "none" and all(c["N"] <= 32 for c in calls)
+    group_flags = flags & (spmm24.STATIC_WEIGHTS | spmm24.BF16)
 
-    # Timed region.  A sleep kernel queued first lets the host enqueue every
-    # timed launch before the GPU reaches them, so the device-side interval
-    # measures the kernels back to back (programmatic dependent launch lets
-    # each kernel's set-up overlap the previous kernel's tail).
-    nl = len(calls) * args.steps
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local_rank) as clk:
+    def group_array(cs):
+        return spmm24.problem_array([(c["A"], c["B"], c["E"], c["C"], c["M"], c["N"], c["K"]) for c in cs])
+
+    group_arrays = {}
+
+    def step_launch(cs, hs=None, use_group=grouped):
+        if use_group:
+            arr = group_arrays.setdefault(id(cs), group_array(cs))
+            rc = spmm24._lib.spmm24_launch_grouped(h_stream if hs is None else hs, arr, len(arr), group_flags)
+            if rc != 0:
+                raise RuntimeError(f"spmm24_launch_grouped failed: {rc} {spmm24._lib.spmm24_last_error().decode()}")
+        else:
+            for c in cs:
+                launch(c, hs)
+
+    def timed_steps(use_group):
+        """Device time (ms) of args.steps steps back to back.  A sleep kernel
+        queued first lets the host enqueue every timed launch before the GPU
+        reaches them, so the interval measures the kernels back to back
+        (programmatic dependent launch lets each kernel's set-up overlap the
+        previous kernel's tail)."""
+        for _ in range(args.warmup):
+            step_launch(calls, use_group=use_group)
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize(dev)
         torch.cuda._sleep(int(2e7))
         t0.record(stream)
         for _ in range(args.steps):
-            for c in calls:
-                launch(c)
+            step_launch(calls, use_group=use_group)
         t1.record(stream)
         torch.cuda.synchronize(dev)
-    elapsed_ms = t0.elapsed_time(t1)
+        return t0.elapsed_time(t1)
+
+    chain_ms = None
+    if grouped:
+        chain_ms = timed_steps(False)  # the same steps as one launch per SpMM, for comparison
+    nl = (1 if grouped else len(calls)) * args.steps
+    with ClockSampler(local_rank) as clk:
+        elapsed_ms = timed_steps(grouped)
     clocks = clk.summary()
 
     # Per-shape kernel times: an event pair around every launch (this breaks
@@ -398,8 +423,7 @@ def run_ours(args, rank, world, local_rank):
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g):
                 hs = int(torch.cuda.current_stream(dev).cuda_stream)
-                for c in call_sets[k]:
-                    launch(c, hs)
+                step_launch(call_sets[k], hs)
             graphs[k] = g
     except Exception:  # noqa: BLE001 -- fall back to eager launches
         graphs = [None, None]
@@ -422,8 +446,7 @@ def run_ours(args, rank, world, local_rank):
         if graphs[k] is not None:
             graphs[k].replay()
         else:
-            for c in call_sets[k]:
-                launch(c)
+            step_launch(call_sets[k])
         comp_done[k].record(stream)
         with torch.cuda.stream(down):
             down.wait_event(comp_done[k])
@@ -482,7 +505,9 @@ def run_ours(args, rank, world, local_rank):
         unit = "TFLOP/s"
     traffic = None
     tr = load_traffic(args.workload)
-    if tr:
+    if tr and grouped:
+        traffic = tr.get("grouped_step")  # one grouped launch = the whole step
+    elif tr:
         per = [tr.get(f"{c['M']}x{c['N']}x{c['K']}") for c in calls]
         if all(v is not None for v in per):
             traffic = float(sum(per) / len(per))
@@ -526,7 +551,17 @@ def run_ours(args, rank, world, local_rank):
                          "overlap the neighbouring steps' kernels")},
         "gpu_launches": nl,
         "clocks": clocks,
+        "launch": ("grouped: one spmm24_launch_grouped per step (one persistent kernel for all the step's SpMMs)"
+                   if grouped else "chain: one spmm24_launch per SpMM"),
     }
+    if chain_ms is not None:
+        # The same steps issued as one spmm24_launch per SpMM (programmatic
+        # dependent launch between them), timed in the same run.
+        out["chain"] = {"value": round(total_flops / (chain_ms * 1e-3) / 1e12, 4), "unit": "TFLOPS",
+                        "us_per_spmm": round(chain_ms * 1e3 / args.steps / len(calls), 3),
+                        "roofline_frac": round(bytes_total / (chain_ms * 1e-3) / 1e9 / peak, 4)
+                        if wl["bound"] == "hbm" else None,
+                        "gpu_launches": len(calls) * args.steps}
 
     if shard and args.allgather and world > 1:
         # NCCL all-gather of the C shards (contiguous row ranges) into the full
@@ -1344,6 +1379,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["pack", "packb"], default="decode")
     ap.add_argument("--comparators", action="store_true")
+    ap.add_argument("--launch", choices=["grouped", "chain"], default="grouped",
+                    help="a step as one spmm24_launch_grouped (N <= 32 workloads without an epilogue or fp8) "
+                         "or as one spmm24_launch per SpMM")
     ap.add_argument("--allgather", action="store_true", help="70b workload: also time the NCCL all-gather of C")
     ap.add_argument("--gather", action="store_true",
                     help="70b workload: time the fused SpMM + NVLink all-gather against SpMM + NCCL all-gather")

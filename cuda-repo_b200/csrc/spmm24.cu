@@ -11,6 +11,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cmath>
 #include <cstdio>
@@ -19,10 +20,12 @@
 #include <map>
 #include <mutex>
 #include <utility>
+#include <vector>
 
 #include "spmm24/SpMM_API.h"
 #include "spmm24_host.h"
 #include "spmm24_kernel.cuh"
+#include "spmm24_grouped.cuh"
 
 namespace spmm24 {
 
@@ -731,6 +734,137 @@ cudaError_t launch_fp8_impl(cudaStream_t stream, const void* A, const void* B, c
     }
 }
 
+// ------------------------------------------------------ grouped launch
+// Independent narrow-N problems in one persistent launch (spmm24_grouped.cuh).
+// The tiles (problem, 128-row block) are balanced over one CTA per SM with
+// the longest-processing-time rule: tiles sorted by cost (128-K stages, plus
+// one for the tile's epilogue) in decreasing order, each given to the CTA
+// with the least work so far.  The encoded launch (descriptors + schedule)
+// is kept per host thread and reused while the same problems are launched
+// again.
+struct GroupCache {
+    std::vector<spmm24_problem> key;
+    unsigned flags = 0;
+    int sms = 0;
+    int n_ctas = 0;
+    GroupParams params;
+};
+thread_local GroupCache* t_group_cache = nullptr;
+
+cudaError_t build_group(const spmm24_problem* probs, int count, unsigned flags, int sms, GroupParams& gp, int& n_ctas) {
+    std::memset(&gp, 0, sizeof(gp));
+    struct Tile {
+        int cost, prob, m_tile;
+    };
+    std::vector<Tile> tiles;
+    for (int i = 0; i < count; ++i) {
+        const spmm24_problem& q = probs[i];
+        const int groups = q.K / 64, st = (groups + 1) / 2;
+        GroupProblem& g = gp.prob[i];
+        g.C = static_cast<uint16_t*>(q.c);
+        g.M = q.M;
+        g.N = q.N;
+        g.K = q.K;
+        g.groups = groups;
+        g.stages_total = st;
+        const int mt = (q.M + kTileM - 1) / kTileM;
+        for (int m = 0; m < mt; ++m) tiles.push_back({st + 1, i, m});
+        cuuint64_t adims[3] = {128, (cuuint64_t)(q.M / 16), (cuuint64_t)(q.K / 16)};
+        cuuint64_t astr[2] = {(cuuint64_t)16 * q.K, 256};
+        cuuint32_t abox[3] = {128, 8, 8};
+        if (!encode(&gp.tmA[i], 3, q.compressed_a, adims, astr, abox))
+            return invalid("grouped: TMA descriptor for A could not be encoded");
+        cuuint64_t bdims[4] = {128, (cuuint64_t)(q.K / 64), 4, (cuuint64_t)((q.N + 7) / 8)};
+        cuuint64_t bstr[3] = {1024, 256, (cuuint64_t)16 * q.K};
+        cuuint32_t bbox[4] = {128, 2, 4, (cuuint32_t)(kGroupTileN / 8)};
+        if (!encode(&gp.tmB[i], 4, q.b_packed, bdims, bstr, bbox))
+            return invalid("grouped: TMA descriptor for B could not be encoded");
+        cuuint64_t edims[2] = {(cuuint64_t)q.K, (cuuint64_t)(q.M / 16)};
+        cuuint64_t estr[1] = {(cuuint64_t)2 * q.K};
+        cuuint32_t ebox[2] = {128, 8};
+        if (!encode(&gp.tmE[i], 2, q.metadata, edims, estr, ebox))
+            return invalid("grouped: TMA descriptor for metadata could not be encoded");
+    }
+    if (tiles.size() > (size_t)kGroupMaxTiles) return invalid("grouped: more than 2048 128-row tiles in one launch");
+    std::stable_sort(tiles.begin(), tiles.end(), [](const Tile& a, const Tile& b) { return a.cost > b.cost; });
+    n_ctas = (int)std::min<size_t>(std::min(sms, kGroupMaxCtas), tiles.size());
+    std::vector<long long> load(n_ctas, 0);
+    std::vector<std::vector<uint16_t>> lists(n_ctas);
+    for (const Tile& t : tiles) {
+        int best = 0;  // least loaded CTA, lowest index on ties (a linear scan: <= 160 CTAs)
+        for (int c = 1; c < n_ctas; ++c)
+            if (load[c] < load[best]) best = c;
+        load[best] += t.cost;
+        lists[best].push_back((uint16_t)((t.prob << 12) | t.m_tile));
+    }
+    int off = 0;
+    for (int c = 0; c < n_ctas; ++c) {
+        gp.sched_off[c] = (uint16_t)off;
+        for (uint16_t e : lists[c]) gp.sched[off++] = e;
+    }
+    gp.sched_off[n_ctas] = (uint16_t)off;
+    gp.n_problems = count;
+    gp.weights_static = (flags & SPMM24_STATIC_WEIGHTS) ? 1 : 0;
+    gp.bf16 = (flags & SPMM24_BF16) ? 1 : 0;
+    return cudaSuccess;
+}
+
+cudaError_t launch_grouped_impl(cudaStream_t stream, const spmm24_problem* probs, int count, unsigned flags) {
+    g_last_error[0] = '\0';
+    if (!probs) return invalid("grouped: null problem array");
+    if (count < 1 || count > kGroupMaxProblems) return invalid("grouped: count must be 1..16");
+    if (flags & ~(unsigned)(SPMM24_STATIC_WEIGHTS | SPMM24_NO_PDL | SPMM24_BF16)) return invalid("unknown flag");
+    long long tiles = 0;
+    for (int i = 0; i < count; ++i) {
+        const spmm24_problem& q = probs[i];
+        if (!q.compressed_a || !q.b_packed || !q.metadata || !q.c) return invalid("grouped: null pointer");
+        if (q.M <= 0 || q.N <= 0 || q.K <= 0) return invalid("grouped: M, N and K must be positive");
+        if (q.M % 16) return invalid("grouped: M must be a multiple of 16");
+        if (q.K % 64) return invalid("grouped: K must be a multiple of 64");
+        if (q.N > kGroupTileN) return invalid("grouped: N must be <= 32 (wider N: spmm24_launch)");
+        if (((uintptr_t)q.compressed_a | (uintptr_t)q.b_packed | (uintptr_t)q.metadata) & 15u)
+            return invalid("grouped: A, B and metadata must be 16-byte aligned");
+        if ((uintptr_t)q.c & 1u) return invalid("grouped: C must be 2-byte aligned");
+        if ((q.M + kTileM - 1) / kTileM > 4096) return invalid("grouped: M must be <= 524288");
+        tiles += (q.M + kTileM - 1) / kTileM;
+    }
+    if (tiles > kGroupMaxTiles) return invalid("grouped: more than 2048 128-row tiles in one launch");
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const int sms = sm_count(dev);
+    if (!t_group_cache) t_group_cache = new GroupCache();
+    GroupCache& gc = *t_group_cache;
+    const bool hit = gc.n_ctas > 0 && gc.flags == flags && gc.sms == sms && (int)gc.key.size() == count &&
+                     std::memcmp(gc.key.data(), probs, sizeof(spmm24_problem) * count) == 0;
+    if (!hit) {
+        gc.n_ctas = 0;
+        int n = 0;
+        if ((e = build_group(probs, count, flags, sms, gc.params, n)) != cudaSuccess) return e;
+        gc.key.assign(probs, probs + count);
+        gc.flags = flags;
+        gc.sms = sms;
+        gc.n_ctas = n;
+    }
+    using GC = GroupCfg<kGroupStages>;
+    auto kern = spmm24_grouped_kernel<kGroupStages>;
+    if ((e = prepare(kern, GC::SMEM_ALLOC, dev, 80)) != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)gc.n_ctas, 1, 1);
+    cfg.blockDim = dim3((unsigned)kThreads, 1, 1);
+    cfg.dynamicSmemBytes = GC::SMEM_ALLOC;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = (flags & SPMM24_NO_PDL) ? 0 : 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+#ifdef SPMM24_TRACE
+    gc.params.trace_base = g_trace_next.fetch_add((long long)gc.n_ctas);
+#endif
+    return cudaLaunchKernelEx(&cfg, kern, gc.params);
+}
+
 // ------------------------------------------------ allocation-free variant
 // Scratch for spmm24_launch_noalloc, owned by the library as a file-scope
 // device array instead of a cudaMalloc'ed buffer: 256 flag words followed by
@@ -937,6 +1071,11 @@ extern "C" cudaError_t spmm24_launch_ex(cudaStream_t stream, const void* compres
 extern "C" cudaError_t spmm24_launch_noalloc(cudaStream_t stream, const void* compressed_a, const void* b_packed,
                                              const uint16_t* metadata, void* c, int M, int N, int K) {
     return spmm24::launch_noalloc_impl(stream, compressed_a, b_packed, metadata, c, M, N, K);
+}
+
+extern "C" cudaError_t spmm24_launch_grouped(cudaStream_t stream, const spmm24_problem* problems, int count,
+                                            unsigned flags) {
+    return spmm24::launch_grouped_impl(stream, problems, count, flags);
 }
 
 extern "C" cudaError_t spmm24_launch_fused(cudaStream_t stream, const void* compressed_a, const void* b_packed,

@@ -1,0 +1,287 @@
+// spmm24_grouped.cuh -- one persistent launch for a group of independent
+// narrow-N (decode) 2:4 SpMMs.
+//
+// A decode step runs many SpMMs whose weights are each read once (the
+// LLaMA-7B projections at N <= 32 tokens).  Launched one by one, every call
+// pays a dependency release, a pipeline fill and a split-K epilogue at its
+// end, during which the weight stream stops.  Here one CTA per SM walks a
+// list of whole 128-row tiles, possibly of several problems, and its TMA
+// producer streams the next tile's weights into the same stage ring while
+// the previous tile's accumulator drains, so the stream does not stop
+// between tiles or problems.  There is no K split, hence no reduction: a
+// tile's full K goes into one TMEM accumulator, and two accumulators
+// alternate so the epilogue of tile j overlaps the main loop of tile j + 1.
+//
+// The host balances the tiles over the CTAs (longest processing time first,
+// cost = the tile's 128-K stages) and passes each CTA's list in the kernel
+// parameters, with one TMA descriptor triple per problem.
+//
+// Roles (192 threads): warp 0 TMA producer (lane 0), warp 1 TMEM allocator
+// and MMA issuer, warps 2-5 epilogue (TMEM -> registers -> C).  Every wait
+// is bounded (kWaitLimitNs); a wait that gives up records a status bit and
+// the role stops, the others give up in turn, TMEM is freed.
+#pragma once
+#include "spmm24_common.cuh"
+
+namespace spmm24 {
+
+constexpr int kGroupMaxProblems = 16;
+constexpr int kGroupMaxTiles = 2048;  // schedule entries (128-row tiles) per launch
+constexpr int kGroupMaxCtas = 160;
+constexpr int kGroupTileN = 32;       // N <= 32: columns of B past N are zero-filled by TMA, never fetched
+constexpr int kGroupStages = 8;
+
+struct GroupProblem {
+    uint16_t* C;       // row-major M x N, fp16 or bf16
+    int M, N, K;
+    int groups;        // K / 64
+    int stages_total;  // ceil(groups / 2): 128-K stages per tile
+};
+
+struct GroupParams {
+    CUtensorMap tmA[kGroupMaxProblems];
+    CUtensorMap tmB[kGroupMaxProblems];
+    CUtensorMap tmE[kGroupMaxProblems];
+    GroupProblem prob[kGroupMaxProblems];
+    int n_problems;
+    int weights_static;
+    int bf16;
+    // CTA c processes sched[sched_off[c] .. sched_off[c + 1]); an entry is
+    // (problem << 12) | m_tile.
+    uint16_t sched_off[kGroupMaxCtas + 1];
+    uint16_t sched[kGroupMaxTiles];
+    SPMM24_TRACE_FIELD
+};
+
+template <int STAGES>
+struct GroupCfg : Cfg<kGroupTileN, STAGES, 2> {
+    using B_ = Cfg<kGroupTileN, STAGES, 2>;
+    static constexpr int BAR_OFFSET = B_::RING_BYTES;
+    static constexpr int NUM_BARS = 2 * STAGES + 4;  // full, empty, acc_full[2], acc_empty[2]
+    static constexpr int HOLDER_OFFSET = BAR_OFFSET + NUM_BARS * 8;
+    static constexpr int SMEM_BYTES = HOLDER_OFFSET + 16;
+    static constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;  // slack to align the base to 1024 B
+    static_assert(SMEM_ALLOC <= 232448, "shared memory overflow");
+    static_assert(B_::STAGE_BYTES % 1024 == 0, "stages must stay 1024-byte aligned");
+};
+
+__device__ __forceinline__ void group_entry(const GroupParams& p, int t, int& pi, int& m_tile) {
+    const uint32_t e = p.sched[t];
+    pi = (int)(e >> 12);
+    m_tile = (int)(e & 0xFFFu);
+}
+
+// Rounds the first N (<= 32) of 32 fp32 values of one output row to C's type
+// and stores them at row gm of C (16-byte stores when N % 8 == 0 and C is
+// 16-byte aligned).  Fully unrolled with predicates, so v stays in registers.
+__device__ __forceinline__ void group_store_row(uint16_t* C, int gm, int N, const uint32_t (&v)[32], int bf16,
+                                                bool vec) {
+    uint16_t* out = C + (size_t)gm * N;
+    if (vec) {
+#pragma unroll
+        for (int c = 0; c < 32; c += 8) {
+            if (c < N) {
+                uint32_t w[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                    w[i] = pack2(__uint_as_float(v[c + 2 * i]), __uint_as_float(v[c + 2 * i + 1]), bf16);
+                *reinterpret_cast<uint4*>(out + c) = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+        }
+    } else {
+#pragma unroll
+        for (int c = 0; c < 32; ++c)
+            if (c < N) out[c] = f32_to_elem(__uint_as_float(v[c]), bf16);
+    }
+}
+
+template <int STAGES>
+__global__ void __launch_bounds__(kThreads, 1) spmm24_grouped_kernel(const __grid_constant__ GroupParams p) {
+    using C_ = GroupCfg<STAGES>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C_::BAR_OFFSET);
+    uint64_t* empty = full + STAGES;
+    uint64_t* acc_full = empty + STAGES;  // [2]
+    uint64_t* acc_empty = acc_full + 2;   // [2]
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + C_::HOLDER_OFFSET);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int t_begin = p.sched_off[blockIdx.x];
+    const int t_end = p.sched_off[blockIdx.x + 1];
+
+    if (threadIdx.x == 0) {
+        SPMM24_STAMP(0);
+        for (int s = 0; s < STAGES; ++s) {
+            ptx::mbar_init(&full[s], 1);
+            ptx::mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            ptx::mbar_init(&acc_full[b], 1);
+            ptx::mbar_init(&acc_empty[b], kEpiThreads / 32);  // one arrival per epilogue warp
+        }
+        ptx::fence_mbarrier_init();
+        for (int i = 0; i < p.n_problems; ++i) {
+            ptx::prefetch_tmap(&p.tmA[i]);
+            ptx::prefetch_tmap(&p.tmB[i]);
+            ptx::prefetch_tmap(&p.tmE[i]);
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) ptx::grid_dep_launch();
+
+    uint32_t tmem_base = 0;
+    if (warp == 0) {
+        // ---------------------------------------------------- TMA producer
+        // One walk over (tile, stage) of this CTA's list; the ring index `it`
+        // runs on across tiles, so the next tile's weights stream in while
+        // the current tile is still being multiplied.
+        if (lane == 0) {
+            const uint64_t pol_stream = ptx::policy_evict_first();  // A, E: read once
+            const uint64_t pol_keep = ptx::policy_evict_last();     // B: re-read by every tile of its problem
+            int pre = 0;
+            if (p.weights_static) {  // the first stages' weights before the previous grid ends
+                int t = t_begin, s_in = 0;
+                while (pre < STAGES && t < t_end) {
+                    int pi, m_tile;
+                    group_entry(p, t, pi, m_tile);
+                    ptx::mbar_arrive_expect_tx(&full[pre], C_::STAGE_BYTES);
+                    load_stage_weights<C_>(smem + pre * C_::STAGE_BYTES, &full[pre], &p.tmA[pi], &p.tmE[pi],
+                                           m_tile * (kTileM / 16), 2 * s_in, pol_stream);
+                    ++pre;
+                    if (++s_in == p.prob[pi].stages_total) {
+                        s_in = 0;
+                        ++t;
+                    }
+                }
+            }
+            ptx::grid_dep_wait();
+            SPMM24_STAMP(1);
+            int t = t_begin, s_in = 0;
+            for (int it = 0; t < t_end; ++it) {
+                int pi, m_tile;
+                group_entry(p, t, pi, m_tile);
+                const int s = it % STAGES;
+                uint8_t* st = smem + s * C_::STAGE_BYTES;
+                if (it >= pre) {
+                    const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
+                    if (!ptx::mbar_wait_bounded(&empty[s], ph ^ 1u, kWaitLimitNs)) {
+                        atomicOr(&g_spmm24_status, kStatusProducerTimeout);
+                        break;
+                    }
+                    ptx::mbar_arrive_expect_tx(&full[s], C_::STAGE_BYTES);
+                    load_stage_weights<C_>(st, &full[s], &p.tmA[pi], &p.tmE[pi], m_tile * (kTileM / 16), 2 * s_in,
+                                           pol_stream);
+                }
+                load_stage_acts<C_>(st, &full[s], &p.tmB[pi], 0, 2 * s_in, pol_keep);
+                if (++s_in == p.prob[pi].stages_total) {
+                    s_in = 0;
+                    ++t;
+                }
+            }
+        }
+        __syncwarp();
+    } else {
+        if (warp == 1) {
+            ptx::tmem_alloc(tmem_holder, C_::TMEM_COLS);
+            ptx::tmem_relinquish();
+        }
+        ptx::tc_fence_before();
+        ptx::named_barrier(kBarTmem, kThreads - 32);
+        ptx::tc_fence_after();
+        tmem_base = *tmem_holder;
+    }
+
+    if (warp == 1) {
+        // ------------------------------------------------------ MMA issuer
+        const uint32_t smem_base = ptx::smem_u32(smem);
+        const uint32_t fmt = p.bf16 ? kIdescBf16 : 0u;
+        int it = 0;
+        bool ok = true;
+        for (int j = 0; t_begin + j < t_end && ok; ++j) {
+            int pi, m_tile;
+            group_entry(p, t_begin + j, pi, m_tile);
+            const int nst = p.prob[pi].stages_total;
+            const int groups = p.prob[pi].groups;
+            const int b = j & 1;
+            if (j >= 2) {  // accumulator b still holds tile j - 2 until the epilogue has read it
+                if (!ptx::mbar_wait_bounded(&acc_empty[b], (uint32_t)((j >> 1) - 1) & 1u, kWaitLimitNs)) {
+                    if (lane == 0) atomicOr(&g_spmm24_status, kStatusMmaTimeout);
+                    break;
+                }
+                ptx::tc_fence_after();
+            }
+            uint32_t accumulate = 0;
+            for (int s_in = 0; s_in < nst; ++s_in, ++it) {
+                const int s = it % STAGES;
+                if (!ptx::mbar_wait_bounded(&full[s], (uint32_t)(it / STAGES) & 1u, kWaitLimitNs)) {
+                    if (lane == 0) atomicOr(&g_spmm24_status, kStatusMmaTimeout);
+                    ok = false;
+                    break;
+                }
+                ptx::tc_fence_after();
+                if (2 * s_in + 1 >= groups) patch_tail_metadata<C_>(smem + s * C_::STAGE_BYTES, lane);
+                if (lane == 0) {
+                    mma_stage<C_, kGroupTileN>(smem_base + s * C_::STAGE_BYTES, tmem_base + C_::META_COL + 4 * s,
+                                               tmem_base + (uint32_t)(b * kGroupTileN), accumulate, fmt);
+                    ptx::tc_commit(&empty[s]);
+                }
+                __syncwarp();
+            }
+            if (!ok) break;
+            if (lane == 0) ptx::tc_commit(&acc_full[b]);
+            __syncwarp();
+        }
+    } else if (warp >= 2) {
+        // ----------------------------------------------------------- epilogue
+        // Thread = output row (TMEM lane); the accumulator is released as
+        // soon as it is in registers, then the row is rounded and stored.
+        const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+        const int row = quad * 32 + lane;
+        bool waited = false;
+        for (int j = 0; t_begin + j < t_end; ++j) {
+            int pi, m_tile;
+            group_entry(p, t_begin + j, pi, m_tile);
+            const int b = j & 1;
+            if (!ptx::mbar_wait_bounded(&acc_full[b], (uint32_t)(j >> 1) & 1u, kWaitLimitNs)) {
+                atomicOr(&g_spmm24_status, kStatusEpilogueTimeout);
+                break;
+            }
+            ptx::tc_fence_after();
+            const int N = p.prob[pi].N;
+            uint32_t v0[16], v1[16];
+            const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(b * kGroupTileN);
+            ptx::tmem_ld_32x32b_x16(taddr, v0);
+            if (N > 16) ptx::tmem_ld_32x32b_x16(taddr + 16, v1);
+            ptx::tmem_wait_ld();
+            uint32_t v[32];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                v[i] = v0[i];
+                v[16 + i] = N > 16 ? v1[i] : 0u;
+            }
+            ptx::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) ptx::mbar_arrive(&acc_empty[b]);
+            if (!waited) {  // C may be read or written by the previous grid
+                ptx::grid_dep_wait();
+                waited = true;
+            }
+            const int gm = m_tile * kTileM + row;
+            uint16_t* C = p.prob[pi].C;
+            if (gm < p.prob[pi].M)
+                group_store_row(C, gm, N, v, p.bf16, (N % 8 == 0) && ((reinterpret_cast<uintptr_t>(C) & 15u) == 0));
+        }
+    }
+
+    if (threadIdx.x == 64) SPMM24_STAMP(5);
+    ptx::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        ptx::tc_fence_after();
+        ptx::tmem_dealloc(tmem_base, C_::TMEM_COLS);
+    }
+}
+
+}  // namespace spmm24

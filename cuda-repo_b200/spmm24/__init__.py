@@ -212,6 +212,34 @@ def launch_fp8(stream, values, b_nk, metadata, c, M: int, N: int, K: int, split_
                                   split_k, flags, ctypes.addressof(epi))
 
 
+class Problem(ctypes.Structure):
+    """spmm24_problem (include/spmm24/SpMM_API.h)."""
+    _fields_ = [("compressed_a", ctypes.c_void_p), ("b_packed", ctypes.c_void_p), ("metadata", ctypes.c_void_p),
+                ("c", ctypes.c_void_p), ("M", ctypes.c_int), ("N", ctypes.c_int), ("K", ctypes.c_int)]
+
+
+_lib.spmm24_launch_grouped.argtypes = [_vp, ctypes.POINTER(Problem), ctypes.c_int, ctypes.c_uint]
+_lib.spmm24_launch_grouped.restype = ctypes.c_int
+
+
+def problem_array(problems):
+    """A ctypes array of spmm24_problem from (compressed_a, b_packed, metadata,
+    c, M, N, K) tuples (tensors or int addresses)."""
+    arr = (Problem * len(problems))()
+    for i, (a, b, e, c, M, N, K) in enumerate(problems):
+        arr[i] = Problem(_ptr(a), _ptr(b), _ptr(e), _ptr(c), M, N, K)
+    return arr
+
+
+def launch_grouped(stream, problems, flags: int = 0) -> int:
+    """spmm24_launch_grouped: several independent N <= 32 SpMMs in one
+    persistent launch.  `problems`: a list of (compressed_a, b_packed,
+    metadata, c, M, N, K) tuples, or an array from problem_array().  Returns
+    the cudaError_t code."""
+    arr = problems if isinstance(problems, ctypes.Array) else problem_array(problems)
+    return _lib.spmm24_launch_grouped(_stream_handle(stream), arr, len(arr), flags)
+
+
 def SpMM_N2M4_Launch(stream, Compressed_A, B, metadata, C, M_Global: int, N_Global: int, K_Global: int,
                      Split_Reduction=None, Split_K: int = 1) -> int:
     """The reference's launcher signature (src/SpMM_API.cu:61-70)."""

@@ -81,6 +81,29 @@ enum {
 cudaError_t spmm24_launch_ex(cudaStream_t stream, const void* compressed_a, const void* b_packed,
                              const uint16_t* metadata, void* c, int M, int N, int K, int split_k, unsigned flags);
 
+/* Several independent narrow-N SpMMs in one launch (no counterpart in the
+ * reference, which launches one SpMM_N2M4_Launch per layer,
+ * test/kernelTest.cu:193).  Each problem has the formats and shape rules of
+ * spmm24_launch, with N <= 32 (decode: a few tokens per layer), and its
+ * own buffers; problems must not write each other's inputs.  One CTA per
+ * SM walks whole 128-row tiles of all problems, balanced by K, so the
+ * weight stream does not stop between problems (per-call launches stop it
+ * at the end of every call).  No K split: each output is summed in one
+ * fp32 accumulator in increasing K.  count: 1..16; at most 2048 tiles of
+ * 128 rows in all; flags: SPMM24_STATIC_WEIGHTS, SPMM24_NO_PDL,
+ * SPMM24_BF16.  Allocates nothing; the encoded launch is cached per host
+ * thread and reused when the same problem array is launched again.
+ * Returns cudaErrorInvalidValue (reason in spmm24_last_error) for a bad
+ * problem, count or flag. */
+typedef struct spmm24_problem {
+    const void* compressed_a;
+    const void* b_packed;
+    const uint16_t* metadata;
+    void* c;
+    int M, N, K;
+} spmm24_problem;
+cudaError_t spmm24_launch_grouped(cudaStream_t stream, const spmm24_problem* problems, int count, unsigned flags);
+
 /* Epilogue of spmm24_launch_fused (no counterpart in the reference, whose
  * epilogue only rounds to fp16, src/LoadAndStore.cuh:385-429).  Applied
  * after the split-K reduction, before the output is rounded:
