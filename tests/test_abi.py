@@ -224,3 +224,29 @@ def test_tuning_overrides_and_no_environment(monkeypatch):
         monkeypatch.setenv(name, val)
     assert spmm24.select_config(384, 40, 512) == auto
     assert spmm24.select_config(4096, 16, 4096)["stages"] == 4
+
+
+def test_grouped_argument_checks():
+    """spmm24_launch_grouped rejects bad groups before touching the device."""
+    ok = 1 << 20
+    good = (ok, ok, ok, ok, 256, 16, 512)
+    cases = [
+        ([], "count must be 1..16"),
+        ([good] * 17, "count must be 1..16"),
+        ([(ok, ok, ok, ok, 256, 33, 512)], "N must be <= 32"),
+        ([(ok, ok, ok, ok, 250, 16, 512)], "multiple of 16"),
+        ([(ok, ok, ok, ok, 256, 16, 500)], "multiple of 64"),
+        ([(ok + 8, ok, ok, ok, 256, 16, 512)], "16-byte aligned"),
+        ([(ok, ok, ok, ok + 1, 256, 16, 512)], "2-byte aligned"),
+        ([(0, ok, ok, ok, 256, 16, 512)], "null pointer"),
+        ([(ok, ok, ok, ok, 0, 16, 512)], "positive"),
+        ([(ok, ok, ok, ok, 131072, 8, 64)] * 3, "2048 128-row tiles"),
+    ]
+    for probs, msg in cases:
+        arr = spmm24.problem_array(probs) if probs else (spmm24.Problem * 1)()
+        rc = spmm24._lib.spmm24_launch_grouped(None, arr, len(probs), 0)
+        assert rc == spmm24.CUDA_ERROR_INVALID_VALUE, msg
+        assert msg in spmm24._lib.spmm24_last_error().decode(), (msg, spmm24._lib.spmm24_last_error())
+    rc = spmm24._lib.spmm24_launch_grouped(None, spmm24.problem_array([good]), 1, 64)
+    assert rc == spmm24.CUDA_ERROR_INVALID_VALUE and "flag" in spmm24._lib.spmm24_last_error().decode()
+    assert spmm24._lib.spmm24_launch_grouped(None, None, 1, 0) == spmm24.CUDA_ERROR_INVALID_VALUE
