@@ -14,7 +14,16 @@ bytes = M*K + M*K/8 + 2*K*N + 2*M*N per call, against the measured copy
 bandwidth in MEASURED_PEAKS.json).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--workload decode|prefill|square] [--comparators]
+                  [--workload decode|prefill|70b|square|pack|packb] [--launch grouped|chain]
+                  [--no-comparators] [--no-secondary]
+
+A step of the decode workload is one spmm24_launch_grouped (one persistent
+kernel for all 12 SpMMs); the same steps as one spmm24_launch per SpMM are
+timed beside it ("chain").  At N=1 the line also carries same-run
+comparators (cuSPARSELt 0.7.1 with algorithm search, dense cuBLAS fp16, the
+reference kernel built for sm_100a; isolated calls, L2 flushed) and a
+secondary block with BASELINE configs 3 (prefill) and 5 (squares up to
+16384^3) against the sparse tensor-core ceiling measured in the same run.
 
 --impl reference times the reference path's CPU implementation (the
 oracle's dense GEMM on the pruned A -- the reference has no CPU GEMM of its
@@ -596,8 +605,10 @@ def run_ours(args, rank, world, local_rank):
     if shard and args.gather and world > 1:
         out["gather"] = time_gather(torch, dist, spmm24, calls, stream, dev, rank, world, args, flags)
 
-    if args.comparators and rank == 0 and not bf16 and not fp8:
+    if args.comparators and rank == 0 and world == 1 and not bf16 and not fp8:
         out["comparators"] = run_comparators(torch, spmm24, calls, layers, acts, dev, args)
+    if args.secondary and rank == 0 and world == 1 and args.workload == "decode" and not bf16 and not fp8:
+        out["secondary"] = run_secondary(torch, spmm24, dev, args)
 
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(layers, acts, shapes, budget_s=args.cpu_seconds, bf16=bf16, fp8=fp8)
@@ -735,22 +746,46 @@ def time_gather(torch, dist, spmm24, calls, stream, dev, rank, world, args, flag
     return out
 
 
-def run_comparators(torch, spmm24, calls, layers, acts, dev, args):
-    """Same step through dense cuBLAS (torch.matmul fp16), cuSPARSELt
-    (torch._cslt_sparse_mm) and the reference kernel built for sm_100a
-    (oracle/_ref, only N in {8..128}).  Each is timed per call with CUDA
-    events after warm-up, with an L2 flush before each call."""
-    import numpy as np
+# ---------------------------------------------------------- comparators
+# Same-run comparators (the reference times cuSPARSELt and cuBLAS beside its
+# kernel: bench/main.cu:104, :136): dense cuBLAS fp16 (torch.matmul, fp32
+# accumulation), cuSPARSELt 0.7.1 through its own plan / search / matmul API
+# (comparators/cmp.cu) and the reference's kernel built for sm_100a
+# (oracle/_ref, N in {8..128} only).  Each call is timed alone with CUDA
+# events after an L2 flush (a 256 MB write), median of `iters`.
+def _cmp_lib():
+    import ctypes
 
-    res = {}
-    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    path = os.path.join(REPO, "comparators", "_build", "libspmm24_cmp.so")
+    if not os.path.exists(path):
+        return None
+    L = ctypes.CDLL(path)
+    vp = ctypes.c_void_p
+    L.cmp_cslt_create.argtypes = [ctypes.c_int] * 3 + [vp, vp, vp, vp, ctypes.c_int, ctypes.POINTER(vp)]
+    L.cmp_cslt_create.restype = ctypes.c_int
+    L.cmp_cslt_run.argtypes = [vp, vp]
+    L.cmp_cslt_run.restype = ctypes.c_int
+    L.cmp_cslt_alg_id.argtypes = [vp]
+    L.cmp_cslt_alg_id.restype = ctypes.c_int
+    L.cmp_cslt_destroy.argtypes = [vp]
+    L.cmp_last_error.restype = ctypes.c_char_p
+    L.cmp_sparse_mma_peak.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_float)]
+    L.cmp_sparse_mma_peak.restype = ctypes.c_double
+    return L
 
-    def time_fn(fn, iters=10):
-        for _ in range(3):
+
+class _Timer:
+    def __init__(self, torch, dev):
+        self.torch = torch
+        self.flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+
+    def __call__(self, fn, iters=10, warmup=3):
+        torch = self.torch
+        for _ in range(warmup):
             fn()
         ts = []
         for _ in range(iters):
-            flush.zero_()
+            self.flush.zero_()
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record()
             fn()
@@ -759,49 +794,146 @@ def run_comparators(torch, spmm24, calls, layers, acts, dev, args):
             ts.append(a.elapsed_time(b) * 1e3)
         return statistics.median(ts)
 
-    ours, dense, cslt = {}, {}, {}
+
+def compare_case(torch, spmm24, timer, cmp, ref, dev, M, N, K, A, E, Bp, Ad, Bd, iters=10):
+    """One shape through every implementation; device operands given: the
+    packed A / metadata / B of this library, and the pruned dense A (M x K)
+    and row-major B (K x N) for the others.  Returns microseconds per call."""
+    import ctypes
+
+    h = int(torch.cuda.current_stream().cuda_stream)
+    C = torch.empty((M, N), dtype=torch.float16, device=dev)
+    row = {"ours_us": timer(lambda: spmm24._lib.spmm24_launch(h, A.data_ptr(), Bp.data_ptr(), E.data_ptr(),
+                                                               C.data_ptr(), M, N, K, None, 0), iters)}
+    prev = torch.backends.cuda.matmul.allow_fp16_reduced_precision_reduction
+    torch.backends.cuda.matmul.allow_fp16_reduced_precision_reduction = False
+    try:
+        row["cublas_dense_fp16_us"] = timer(lambda: torch.matmul(Ad, Bd), iters)
+    finally:
+        torch.backends.cuda.matmul.allow_fp16_reduced_precision_reduction = prev
+    if cmp is not None:
+        # cuSPARSELt wants 16-byte rows of B and C: N padded to a multiple of 8 (at least 16)
+        Np = max(16, (N + 7) // 8 * 8)
+        Bq = Bd if Np == N else torch.nn.functional.pad(Bd, (0, Np - N))
+        Cq = torch.empty((M, Np), dtype=torch.float16, device=dev)
+        plan = ctypes.c_void_p()
+        rc = cmp.cmp_cslt_create(M, Np, K, Ad.data_ptr(), Bq.data_ptr(), Cq.data_ptr(), h, 1, ctypes.byref(plan))
+        if rc == 0:
+            row["cusparselt_us"] = timer(lambda: cmp.cmp_cslt_run(plan, h), iters)
+            row["cusparselt_alg_id"] = cmp.cmp_cslt_alg_id(plan)
+            if Np != N:
+                row["cusparselt_n_padded"] = Np
+            cmp.cmp_cslt_destroy(plan)
+        else:
+            row["cusparselt_error"] = cmp.cmp_last_error().decode()
+    if ref is not None and ref.ref_spmm_supported(M, N, K, 1):
+        row["reference_kernel_us"] = timer(lambda: ref.ref_spmm_launch(h, A.data_ptr(), Bp.data_ptr(), E.data_ptr(),
+                                                                       C.data_ptr(), M, N, K, None, 1), iters)
+    if row.get("cusparselt_us"):
+        row["x_vs_cusparselt"] = round(row["cusparselt_us"] / row["ours_us"], 3)
+    row["x_vs_cublas"] = round(row["cublas_dense_fp16_us"] / row["ours_us"], 3)
+    return {k: (round(v, 3) if isinstance(v, float) else v) for k, v in row.items()}
+
+
+def _reference_kernel():
+    try:
+        sys.path.insert(0, os.path.join(REPO, "oracle"))
+        import oracle as O
+
+        return O.ref_spmm() if O.ref_spmm_available() else None
+    except Exception:  # noqa: BLE001
+        return None
+
+
+def target_summary(rows):
+    """The north star's targets per shape: >= 1.0x cuSPARSELt, >= 1.5x dense cuBLAS."""
+    out = {}
+    for key, field, bar in (("cusparselt_1.0x", "x_vs_cusparselt", 1.0), ("cublas_1.5x", "x_vs_cublas", 1.5)):
+        have = {k: r[field] for k, r in rows.items() if r.get(field) is not None}
+        out[key] = {"met": sum(1 for v in have.values() if v >= bar), "of": len(have),
+                    "missed": {k: v for k, v in have.items() if v < bar}}
+    return out
+
+
+def run_comparators(torch, spmm24, calls, layers, acts, dev, args):
+    """The step's shapes, one isolated call each, against the comparators."""
+    timer = _Timer(torch, dev)
+    cmp = _cmp_lib()
+    ref = _reference_kernel()
+    rows = {}
     for c in calls:
         key = f"{c['M']}x{c['N']}x{c['K']}"
         a_np = layers[(c["M"], c["K"])][0]
         b_np = acts[(c["K"], c["N"])][0]
         Ad = torch.from_numpy(a_np.view("int16")).to(dev).view(torch.float16).reshape(c["M"], c["K"])
         Bd = torch.from_numpy(b_np.view("int16")).to(dev).view(torch.float16).reshape(c["K"], c["N"])
-        h = int(torch.cuda.current_stream().cuda_stream)
-        ours[key] = time_fn(lambda: spmm24._lib.spmm24_launch(h, c["A"].data_ptr(), c["B"].data_ptr(),
-                                                              c["E"].data_ptr(), c["C"].data_ptr(), c["M"], c["N"],
-                                                              c["K"], None, 0))
-        dense[key] = time_fn(lambda: torch.matmul(Ad, Bd))
-        try:
-            comp = torch._cslt_compress(Ad)
-            Np = max(c["N"], 16)
-            Bp = torch.zeros(c["K"], Np, dtype=torch.float16, device=dev)
-            Bp[:, :c["N"]] = Bd
-            cslt[key] = time_fn(lambda: torch._cslt_sparse_mm(comp, Bp))
-        except Exception as e:  # noqa: BLE001
-            cslt[key] = None
-            res["cusparselt_error"] = str(e)[:200]
+        rows[key] = compare_case(torch, spmm24, timer, cmp, ref, dev, c["M"], c["N"], c["K"], c["A"], c["E"],
+                                 c["B"], Ad, Bd)
         del Ad, Bd
-    res["us_ours"] = ours
-    res["us_cublas_dense_fp16"] = dense
-    res["us_cusparselt"] = cslt
-    try:
-        sys.path.insert(0, os.path.join(REPO, "oracle"))
-        import oracle as O
+    return {"per_shape": rows, "targets": target_summary(rows),
+            "method": "isolated calls, L2 flushed (256 MB write) before each, CUDA events, median of 10; cuSPARSELt "
+                      "0.7.1 plan + cusparseLtMatmulSearch (comparators/cmp.cu); cuBLAS = torch.matmul fp16 with "
+                      "fp32 reduction"}
 
-        if O.ref_spmm_available():
-            ref = O.ref_spmm()
-            rk = {}
-            for c in calls:
-                key = f"{c['M']}x{c['N']}x{c['K']}"
-                if ref.ref_spmm_supported(c["M"], c["N"], c["K"], 1):
-                    h = int(torch.cuda.current_stream().cuda_stream)
-                    rk[key] = time_fn(lambda: ref.ref_spmm_launch(h, c["A"].data_ptr(), c["B"].data_ptr(),
-                                                                  c["E"].data_ptr(), c["C"].data_ptr(), c["M"],
-                                                                  c["N"], c["K"], None, 1))
-            res["us_reference_kernel_sm100a_splitk1"] = rk
-    except Exception as e:  # noqa: BLE001
-        res["reference_kernel_error"] = str(e)[:200]
-    return res
+
+def run_secondary(torch, spmm24, dev, args):
+    """BASELINE configs 3 (LLaMA-7B prefill) and 5 (squares up to 16384^3):
+    per-shape isolated calls against the comparators, and the sparse
+    tensor-core ceiling measured in the same run.  Operands are generated and
+    packed on the device (spmm24_prune_2of4_device, spmm24_pack_a_device,
+    spmm24_pack_b_device)."""
+    import ctypes
+
+    timer = _Timer(torch, dev)
+    cmp = _cmp_lib()
+    ref = _reference_kernel()
+    out = {}
+    peak = None
+    if cmp is not None:
+        ms = ctypes.c_float()
+        v = cmp.cmp_sparse_mma_peak(20000, ctypes.byref(ms))
+        if v > 0:
+            peak = v
+            out["sparse_ceiling"] = {"tflops": round(v, 1), "ms": round(ms.value, 3),
+                                     "what": "one CTA per SM repeating the kernels' stage mix (tcgen05.cp + 4 x "
+                                             "tcgen05.mma.sp kind::f16 M=128 N=256 K=32) on operands resident in "
+                                             "shared memory (comparators/cmp.cu); dense-equivalent"}
+    dense_peak = 2.0 * load_peaks()["bf16_tflops"]
+    g = torch.Generator(device=dev).manual_seed(2024)
+    for name, shapes, square in (("prefill", WORKLOADS["prefill"]["shapes"], False),
+                                 ("square", [(s, s, s) for s in (1024, 2048, 4096, 8192, 16384)], True)):
+        rows = {}
+        fl = us = 0.0
+        for (M, N, K) in shapes:
+            if square:
+                a = (torch.rand(M, K, generator=g, device=dev) * 2 - 1).half()
+                keep = torch.rand(M * K // 4, 4, generator=g, device=dev).argsort(dim=1)[:, :2]
+                mask = torch.zeros(M * K // 4, 4, dtype=torch.bool, device=dev).scatter_(1, keep, True)
+                a = (a.view(-1, 4) * mask).view(M, K)
+                del keep, mask
+                b = (torch.rand(K, N, generator=g, device=dev) * 2 - 1).half()
+            else:
+                a = (torch.randn(M, K, generator=g, device=dev) * 0.02).half()
+                spmm24.prune_2of4_device(a, M, K)
+                b = torch.randn(K, N, generator=g, device=dev).half()
+            A, E, _ = spmm24.pack_a_device(a, M, K)
+            Bp = spmm24.pack_b_device(b, K, N)
+            iters = 5 if M * N * K >= 8192 ** 3 else 10
+            r = compare_case(torch, spmm24, timer, cmp, ref, dev, M, N, K, A, E, Bp, a, b, iters)
+            r["ours_tflops"] = round(flops(M, N, K) / (r["ours_us"] * 1e-6) / 1e12, 1)
+            rows[f"{M}x{N}x{K}"] = r
+            fl += flops(M, N, K)
+            us += r["ours_us"]
+            del a, b, A, E, Bp
+            torch.cuda.empty_cache()
+        tf = fl / (us * 1e-6) / 1e12
+        out[name] = {"baseline_config": 3 if name == "prefill" else 5, "tflops": round(tf, 1),
+                     "frac_of_2x_dense_bf16": round(tf / dense_peak, 4),
+                     "frac_of_sparse_ceiling": round(tf / peak, 4) if peak else None,
+                     "per_shape": rows, "targets": target_summary(rows)}
+    out["method"] = ("isolated calls, L2 flushed before each, CUDA events, median of 10 (5 at >= 8192^3); tflops = "
+                     "sum of 2MNK / sum of the medians")
+    return out
 
 
 def host_threads():
@@ -1378,7 +1510,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["pack", "packb"], default="decode")
-    ap.add_argument("--comparators", action="store_true")
+    ap.add_argument("--no-comparators", dest="comparators", action="store_false",
+                    help="skip the same-run comparators (cuSPARSELt, dense cuBLAS, the reference kernel)")
+    ap.add_argument("--no-secondary", dest="secondary", action="store_false",
+                    help="skip the prefill / square block (configs 3 and 5) of the default decode line")
     ap.add_argument("--launch", choices=["grouped", "chain"], default="grouped",
                     help="a step as one spmm24_launch_grouped (N <= 32 workloads without an epilogue or fp8) "
                          "or as one spmm24_launch per SpMM")

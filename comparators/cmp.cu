@@ -1,0 +1,230 @@
+// cmp.cu -- comparators timed beside libspmm24 by bench.py (not part of the
+// library): cuSPARSELt 0.7.1 driven through its own plan / search / matmul
+// API, and a probe of the sparse tensor core's issue rate with operands
+// resident in shared memory (the measured 2:4 ceiling prefill shapes are
+// reported against).
+//
+// The reference benchmarks cuSPARSELt beside its kernel
+// (SpeakOutLoudly/CUDA-Repo bench/backends/cuSparseLt_backend.cuh:4-127);
+// that backend calls cusparseLtMatmulAlgSelectionDestroy, which 0.7.1 no
+// longer has, so this is a fresh client of the 0.7.1 API: one plan per
+// shape, cusparseLtMatmulSearch to pick the fastest configuration, then
+// timed cusparseLtMatmul calls.
+#include <cuda_runtime.h>
+#include <cusparseLt.h>
+
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "spmm24_common.cuh"
+
+namespace {
+
+std::mutex g_mu;
+bool g_handle_ok = false;
+cusparseLtHandle_t g_handle;
+
+const cusparseLtHandle_t* handle() {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g_handle_ok) g_handle_ok = cusparseLtInit(&g_handle) == CUSPARSE_STATUS_SUCCESS;
+    return g_handle_ok ? &g_handle : nullptr;
+}
+
+struct CsltPlan {
+    cusparseLtMatDescriptor_t a, b, c;
+    cusparseLtMatmulDescriptor_t mm;
+    cusparseLtMatmulAlgSelection_t alg;
+    cusparseLtMatmulPlan_t plan;
+    void* a_comp = nullptr;
+    void* ws = nullptr;
+    const void* dB = nullptr;
+    void* dC = nullptr;
+    int alg_id = -1;
+    bool plan_ok = false;
+};
+
+char g_err[256] = "";
+
+int fail(CsltPlan* p, const char* what, int code) {
+    std::snprintf(g_err, sizeof(g_err), "%s failed (%d)", what, code);
+    if (p) {
+        if (p->plan_ok) cusparseLtMatmulPlanDestroy(&p->plan);
+        cudaFree(p->a_comp);
+        cudaFree(p->ws);
+        delete p;
+    }
+    return code ? code : -1;
+}
+
+}  // namespace
+
+// C (M x N, row-major fp16) = A (M x K row-major fp16, 2:4 along K) * B (K x N
+// row-major fp16), fp32 accumulation.  A is compressed by cuSPARSELt here;
+// with `search` the fastest algorithm configuration is chosen by
+// cusparseLtMatmulSearch on these buffers.  N must be a multiple of 8 (pad
+// narrower activations).
+extern "C" int cmp_cslt_create(int M, int N, int K, const void* dA, const void* dB, void* dC, void* stream,
+                               int search, void** out) {
+    const cusparseLtHandle_t* h = handle();
+    if (!h) return fail(nullptr, "cusparseLtInit", -1);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    CsltPlan* p = new CsltPlan();
+    int rc;
+    if ((rc = cusparseLtStructuredDescriptorInit(h, &p->a, M, K, K, 16, CUDA_R_16F, CUSPARSE_ORDER_ROW,
+                                                 CUSPARSELT_SPARSITY_50_PERCENT)))
+        return fail(p, "structured descriptor", rc);
+    if ((rc = cusparseLtDenseDescriptorInit(h, &p->b, K, N, N, 16, CUDA_R_16F, CUSPARSE_ORDER_ROW)))
+        return fail(p, "dense descriptor B", rc);
+    if ((rc = cusparseLtDenseDescriptorInit(h, &p->c, M, N, N, 16, CUDA_R_16F, CUSPARSE_ORDER_ROW)))
+        return fail(p, "dense descriptor C", rc);
+    if ((rc = cusparseLtMatmulDescriptorInit(h, &p->mm, CUSPARSE_OPERATION_NON_TRANSPOSE,
+                                             CUSPARSE_OPERATION_NON_TRANSPOSE, &p->a, &p->b, &p->c, &p->c,
+                                             CUSPARSE_COMPUTE_32F)))
+        return fail(p, "matmul descriptor", rc);
+    if ((rc = cusparseLtMatmulAlgSelectionInit(h, &p->alg, &p->mm, CUSPARSELT_MATMUL_ALG_DEFAULT)))
+        return fail(p, "algorithm selection", rc);
+    if ((rc = cusparseLtMatmulPlanInit(h, &p->plan, &p->mm, &p->alg))) return fail(p, "plan", rc);
+    p->plan_ok = true;
+    size_t comp = 0, comp_buf = 0;
+    if ((rc = cusparseLtSpMMACompressedSize(h, &p->plan, &comp, &comp_buf))) return fail(p, "compressed size", rc);
+    void* buf = nullptr;
+    if (cudaMalloc(&p->a_comp, comp) != cudaSuccess || (comp_buf && cudaMalloc(&buf, comp_buf) != cudaSuccess))
+        return fail(p, "cudaMalloc", -2);
+    rc = cusparseLtSpMMACompress(h, &p->plan, dA, p->a_comp, buf, s);
+    cudaStreamSynchronize(s);
+    cudaFree(buf);
+    if (rc) return fail(p, "compress", rc);
+    size_t ws = 0;
+    if ((rc = cusparseLtMatmulGetWorkspace(h, &p->plan, &ws))) return fail(p, "workspace size", rc);
+    if (ws && cudaMalloc(&p->ws, ws) != cudaSuccess) return fail(p, "cudaMalloc", -2);
+    p->dB = dB;
+    p->dC = dC;
+    const float alpha = 1.f, beta = 0.f;
+    if (search) {
+        if ((rc = cusparseLtMatmulSearch(h, &p->plan, &alpha, p->a_comp, dB, &beta, dC, dC, p->ws, &s, 1)))
+            return fail(p, "search", rc);
+        size_t ws2 = 0;  // the chosen configuration may need a larger workspace
+        if ((rc = cusparseLtMatmulGetWorkspace(h, &p->plan, &ws2))) return fail(p, "workspace size", rc);
+        if (ws2 > ws) {
+            cudaFree(p->ws);
+            p->ws = nullptr;
+            if (cudaMalloc(&p->ws, ws2) != cudaSuccess) return fail(p, "cudaMalloc", -2);
+        }
+    }
+    int id = -1;
+    cusparseLtMatmulAlgGetAttribute(h, &p->alg, CUSPARSELT_MATMUL_ALG_CONFIG_ID, &id, sizeof(id));
+    p->alg_id = id;
+    cudaStreamSynchronize(s);
+    *out = p;
+    return 0;
+}
+
+extern "C" int cmp_cslt_run(void* plan, void* stream) {
+    CsltPlan* p = static_cast<CsltPlan*>(plan);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const float alpha = 1.f, beta = 0.f;
+    return cusparseLtMatmul(handle(), &p->plan, &alpha, p->a_comp, p->dB, &beta, p->dC, p->dC, p->ws, &s, 1);
+}
+
+extern "C" int cmp_cslt_alg_id(void* plan) { return static_cast<CsltPlan*>(plan)->alg_id; }
+
+extern "C" void cmp_cslt_destroy(void* plan) {
+    CsltPlan* p = static_cast<CsltPlan*>(plan);
+    if (!p) return;
+    cusparseLtMatmulPlanDestroy(&p->plan);
+    cudaFree(p->a_comp);
+    cudaFree(p->ws);
+    delete p;
+}
+
+extern "C" const char* cmp_last_error(void) { return g_err; }
+
+// ------------------------------------------------------------------------
+// Sparse tensor-core ceiling: every CTA (one per SM) repeats the stage
+// instruction mix of the library's kernels -- one tcgen05.cp of metadata
+// and four tcgen05.mma.sp kind::f16 (M = 128, N = 256, K = 32 logical) --
+// on operands that stay in shared memory, so nothing but the tensor core's
+// issue rate bounds it.  Dense-equivalent work per stage: 4 * 2 * 128 *
+// 256 * 32 flops.
+namespace {
+using ProbeCfg = spmm24::Cfg<256, 1, 1>;
+constexpr int kProbeSmem = 120 * 1024;  // more than half an SM: one CTA per SM
+
+__global__ void __launch_bounds__(128, 1) cmp_mma_probe_kernel(int stages, uint32_t* status) {
+    using namespace spmm24;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    __shared__ uint64_t done;
+    __shared__ uint32_t holder;
+    // A and B: zeros (values do not change the issue rate); metadata: the
+    // valid pattern "positions 0 and 1" in every group.
+    for (int i = threadIdx.x; i < (ProbeCfg::A_BYTES + ProbeCfg::B_BYTES) / 16; i += blockDim.x)
+        reinterpret_cast<uint4*>(smem)[i] = make_uint4(0, 0, 0, 0);
+    for (int i = threadIdx.x; i < ProbeCfg::E_BYTES / 16; i += blockDim.x)
+        reinterpret_cast<uint4*>(smem + ProbeCfg::A_BYTES + ProbeCfg::B_BYTES)[i] =
+            make_uint4(0x44444444u, 0x44444444u, 0x44444444u, 0x44444444u);
+    ptx::fence_proxy_async_smem();
+    if (threadIdx.x == 0) {
+        ptx::mbar_init(&done, 1);
+        ptx::fence_mbarrier_init();
+    }
+    if (threadIdx.x < 32) {
+        ptx::tmem_alloc(&holder, ProbeCfg::TMEM_COLS);
+        ptx::tmem_relinquish();
+    }
+    ptx::tc_fence_before();
+    __syncthreads();
+    ptx::tc_fence_after();
+    const uint32_t tmem = holder;
+    if (threadIdx.x == 0) {
+        const uint32_t base = ptx::smem_u32(smem);
+        uint32_t acc = 0;
+        for (int s = 0; s < stages; ++s)
+            mma_stage<ProbeCfg, 256>(base, tmem + ProbeCfg::META_COL, tmem, acc, 0u);
+        ptx::tc_commit(&done);
+        if (!ptx::mbar_wait_bounded(&done, 0, kWaitLimitNs)) atomicOr(status, 1u);
+    }
+    ptx::tc_fence_before();
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        ptx::tc_fence_after();
+        ptx::tmem_dealloc(tmem, ProbeCfg::TMEM_COLS);
+    }
+}
+}  // namespace
+
+// Runs the probe on the current device with `stages` stages per CTA and
+// returns the dense-equivalent TFLOPS (negative on error); *ms_out gets the
+// kernel's duration.
+extern "C" double cmp_sparse_mma_peak(int stages, float* ms_out) {
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return -1;
+    if (cudaFuncSetAttribute(cmp_mma_probe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kProbeSmem) !=
+        cudaSuccess)
+        return -2;
+    uint32_t* status = nullptr;
+    if (cudaMalloc(&status, 4) != cudaSuccess) return -3;
+    cudaMemset(status, 0, 4);
+    cudaEvent_t e0, e1;
+    cudaEventCreate(&e0);
+    cudaEventCreate(&e1);
+    cmp_mma_probe_kernel<<<sms, 128, kProbeSmem>>>(stages / 8, status);  // warm-up
+    cudaEventRecord(e0);
+    cmp_mma_probe_kernel<<<sms, 128, kProbeSmem>>>(stages, status);
+    cudaEventRecord(e1);
+    cudaError_t e = cudaEventSynchronize(e1);
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, e0, e1);
+    uint32_t st = 0;
+    cudaMemcpy(&st, status, 4, cudaMemcpyDeviceToHost);
+    cudaFree(status);
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    if (e != cudaSuccess || st != 0) return -4;
+    if (ms_out) *ms_out = ms;
+    const double flops = (double)sms * stages * 4.0 * 2.0 * 128.0 * 256.0 * 32.0;
+    return flops / (ms * 1e-3) / 1e12;
+}
