@@ -769,7 +769,7 @@ def _cmp_lib():
     L.cmp_cslt_alg_id.restype = ctypes.c_int
     L.cmp_cslt_destroy.argtypes = [vp]
     L.cmp_last_error.restype = ctypes.c_char_p
-    L.cmp_sparse_mma_peak.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_float)]
+    L.cmp_sparse_mma_peak.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_float)]
     L.cmp_sparse_mma_peak.restype = ctypes.c_double
     return L
 
@@ -890,14 +890,26 @@ def run_secondary(torch, spmm24, dev, args):
     out = {}
     peak = None
     if cmp is not None:
-        ms = ctypes.c_float()
-        v = cmp.cmp_sparse_mma_peak(20000, ctypes.byref(ms))
-        if v > 0:
-            peak = v
-            out["sparse_ceiling"] = {"tflops": round(v, 1), "ms": round(ms.value, 3),
-                                     "what": "one CTA per SM repeating the kernels' stage mix (tcgen05.cp + 4 x "
-                                             "tcgen05.mma.sp kind::f16 M=128 N=256 K=32) on operands resident in "
-                                             "shared memory (comparators/cmp.cu); dense-equivalent"}
+        # Burst figures (about 1 ms per run, best of 3), like the dense bf16
+        # burst of MEASURED_PEAKS: the CTA-pair mix of the prefill kernels is
+        # the ceiling; the one-CTA mix of the cluster kernels is reported too.
+        ceil = {}
+        for key, pair in (("cta_pair_m256", 1), ("one_cta_m128", 0)):
+            best, best_ms = -1.0, 0.0
+            for _ in range(3):
+                ms = ctypes.c_float()
+                v = cmp.cmp_sparse_mma_peak(4000, pair, ctypes.byref(ms))
+                if v > best:
+                    best, best_ms = v, ms.value
+            if best > 0:
+                ceil[key] = {"tflops": round(best, 1), "ms": round(best_ms, 3)}
+        if ceil:
+            peak = ceil.get("cta_pair_m256", ceil.get("one_cta_m128"))["tflops"]
+            out["sparse_ceiling"] = dict(ceil, tflops=peak, what=(
+                "the kernels' stage mix on operands resident in shared memory, one CTA (or CTA pair) per SM, 4000 "
+                "stages, best of 3: tcgen05.cp + 4 x tcgen05.mma.sp kind::f16 K=32 (M=256 N=256 cta_group::2; "
+                "M=128 N=256 cta_group::1) -- comparators/cmp.cu; dense-equivalent; the pair figure is the "
+                "ceiling"))
     dense_peak = 2.0 * load_peaks()["bf16_tflops"]
     g = torch.Generator(device=dev).manual_seed(2024)
     for name, shapes, square in (("prefill", WORKLOADS["prefill"]["shapes"], False),

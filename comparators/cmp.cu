@@ -193,17 +193,95 @@ __global__ void __launch_bounds__(128, 1) cmp_mma_probe_kernel(int stages, uint3
         ptx::tmem_dealloc(tmem, ProbeCfg::TMEM_COLS);
     }
 }
+
+// The CTA-pair form (the prefill kernels' instruction mix): a cluster of two
+// CTAs, each holding 128 rows of A and 128 columns of B; the leader issues
+// per stage one tcgen05.cp.cta_group::2 and four tcgen05.mma.sp.cta_group::2
+// (M = 256, N = 256, K = 32).  Dense-equivalent work per stage and pair:
+// 4 * 2 * 256 * 256 * 32 flops.
+constexpr int kPairProbeA = 8 * 8 * 256, kPairProbeB = 16 * 2048, kPairProbeE = 16 * 128;
+
+__global__ void __launch_bounds__(128, 1) cmp_mma_probe_pair_kernel(int stages, uint32_t* status) {
+    using namespace spmm24;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    __shared__ uint64_t done;
+    __shared__ uint32_t holder;
+    for (int i = threadIdx.x; i < (kPairProbeA + kPairProbeB) / 16; i += blockDim.x)
+        reinterpret_cast<uint4*>(smem)[i] = make_uint4(0, 0, 0, 0);
+    for (int i = threadIdx.x; i < kPairProbeE / 16; i += blockDim.x)
+        reinterpret_cast<uint4*>(smem + kPairProbeA + kPairProbeB)[i] =
+            make_uint4(0x44444444u, 0x44444444u, 0x44444444u, 0x44444444u);
+    ptx::fence_proxy_async_smem();
+    const uint32_t rank = ptx::cluster_ctarank() & 1u;
+    if (threadIdx.x == 0) {
+        ptx::mbar_init(&done, 1);
+        ptx::fence_mbarrier_init();
+    }
+    if (threadIdx.x < 32) {
+        ptx::tmem_alloc_pair(&holder, 512);
+        ptx::tmem_relinquish_pair();
+    }
+    ptx::tc_fence_before();
+    ptx::cluster_sync();
+    ptx::tc_fence_after();
+    const uint32_t tmem = holder;
+    if (rank == 0 && threadIdx.x == 0) {
+        const uint32_t st = ptx::smem_u32(smem);
+        const uint32_t stB = st + kPairProbeA;
+        const uint32_t idesc = (1u << 2) | (1u << 4) | (1u << 16) | ((uint32_t)(256 >> 3) << 17) |
+                               ((uint32_t)(256 >> 4) << 24);
+        uint32_t acc = 0;
+        for (int s = 0; s < stages; ++s) {
+            ptx::tmem_cp_128x128b_pair(tmem + 256, smem_desc(stB + kPairProbeB, 0, 128));
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                ptx::mma_sp_f16_pair(tmem, smem_desc(st + j * 2048, 4 * 2048, 128), smem_desc(stB + j * 512, 128, 2048),
+                                     tmem + 256 + (j & 2), idesc | (uint32_t)(j & 1), acc);
+                acc = 1;
+            }
+        }
+        ptx::tc_commit_pair_mc(&done, (uint16_t)0x3);
+    }
+    if (threadIdx.x == 0 && !ptx::mbar_wait_bounded(&done, 0, kWaitLimitNs)) atomicOr(status, 1u);
+    ptx::tc_fence_before();
+    __syncthreads();
+    ptx::cluster_sync();
+    if (threadIdx.x < 32) {
+        ptx::tc_fence_after();
+        ptx::tmem_dealloc_pair(tmem, 512);
+    }
+}
+
+cudaError_t launch_probe(bool pair, int sms, int stages, uint32_t* status) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(pair ? sms / 2 * 2 : sms), 1, 1);
+    cfg.blockDim = dim3(128, 1, 1);
+    cfg.dynamicSmemBytes = kProbeSmem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = pair ? 2 : 1;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return pair ? cudaLaunchKernelEx(&cfg, cmp_mma_probe_pair_kernel, stages, status)
+                : cudaLaunchKernelEx(&cfg, cmp_mma_probe_kernel, stages, status);
+}
 }  // namespace
 
-// Runs the probe on the current device with `stages` stages per CTA and
-// returns the dense-equivalent TFLOPS (negative on error); *ms_out gets the
-// kernel's duration.
-extern "C" double cmp_sparse_mma_peak(int stages, float* ms_out) {
+// Runs a probe on the current device (pair = 0: one CTA per SM, M = 128
+// MMAs; pair = 1: CTA pairs, M = 256 cta_group::2 MMAs) with `stages` stages
+// per CTA or pair, and returns the dense-equivalent TFLOPS (negative on
+// error); *ms_out gets the kernel's duration.
+extern "C" double cmp_sparse_mma_peak(int stages, int pair, float* ms_out) {
     int dev = 0, sms = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return -1;
     if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return -1;
     if (cudaFuncSetAttribute(cmp_mma_probe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kProbeSmem) !=
-        cudaSuccess)
+            cudaSuccess ||
+        cudaFuncSetAttribute(cmp_mma_probe_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kProbeSmem) !=
+            cudaSuccess)
         return -2;
     uint32_t* status = nullptr;
     if (cudaMalloc(&status, 4) != cudaSuccess) return -3;
@@ -211,9 +289,9 @@ extern "C" double cmp_sparse_mma_peak(int stages, float* ms_out) {
     cudaEvent_t e0, e1;
     cudaEventCreate(&e0);
     cudaEventCreate(&e1);
-    cmp_mma_probe_kernel<<<sms, 128, kProbeSmem>>>(stages / 8, status);  // warm-up
+    launch_probe(pair != 0, sms, stages / 8, status);  // warm-up
     cudaEventRecord(e0);
-    cmp_mma_probe_kernel<<<sms, 128, kProbeSmem>>>(stages, status);
+    launch_probe(pair != 0, sms, stages, status);
     cudaEventRecord(e1);
     cudaError_t e = cudaEventSynchronize(e1);
     float ms = 0.f;
@@ -225,6 +303,6 @@ extern "C" double cmp_sparse_mma_peak(int stages, float* ms_out) {
     cudaEventDestroy(e1);
     if (e != cudaSuccess || st != 0) return -4;
     if (ms_out) *ms_out = ms;
-    const double flops = (double)sms * stages * 4.0 * 2.0 * 128.0 * 256.0 * 32.0;
+    const double flops = (double)(sms / 2 * 2) * stages * 4.0 * 2.0 * 128.0 * 256.0 * 32.0;  // per SM: M = 128 rows
     return flops / (ms * 1e-3) / 1e12;
 }

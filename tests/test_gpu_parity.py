@@ -93,11 +93,16 @@ def test_stream_k_kernel_shapes(cuda_device, shape):
     A = _to_dev(torch, p.vals, cuda_device)
     E = _to_dev(torch, p.meta, cuda_device)
     B = _to_dev(torch, p.b_packed, cuda_device)
+    import ctypes
+
+    fn = ctypes.CDLL(spmm24.library_path()).spmm24_launch_noalloc
+    fn.argtypes = [ctypes.c_void_p] * 5 + [ctypes.c_int] * 3
+    fn.restype = ctypes.c_int
     outs = []
     for _ in range(2):
         C = torch.full((M, N), float("nan"), dtype=torch.float16, device=cuda_device)
-        rc = spmm24._lib.spmm24_launch_noalloc(torch.cuda.current_stream(cuda_device).cuda_stream, A.data_ptr(),
-                                               B.data_ptr(), E.data_ptr(), C.data_ptr(), M, N, K)
+        rc = fn(torch.cuda.current_stream(cuda_device).cuda_stream, A.data_ptr(), B.data_ptr(), E.data_ptr(),
+                C.data_ptr(), M, N, K)
         assert rc == 0, spmm24._lib.spmm24_last_error().decode()
         torch.cuda.synchronize(cuda_device)
         outs.append(C.view(torch.int16).cpu().numpy().view(np.uint16))

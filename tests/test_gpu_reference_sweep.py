@@ -13,8 +13,15 @@ test/kernelTest.cu:193,197 binds), and is checked
     of rows (the tolerance of tests/problems.py);
   * against the reference's own kernel built for sm_100a (oracle/_ref), on
     the same packed inputs with the same Split_K, where that kernel supports
-    the shape (same tolerance; the reference rounds its split-K partials to
-    fp16, so the two differ by more than summation order);
+    the shape.  The reference rounds each split-K partial sum to fp16 before
+    its reduction pass (src/SpMM_Kernel.cuh:473-489, reduce_Kernel.cuh:
+    27-53), which can put it outside the fp16 tolerance of the exact result
+    (up to 0.19 relative on single elements at Split_K 3-7 in this sweep); so both
+    kernels are held to a per-element bound derived from that algorithm: the
+    oracle emulates it (fp32 partials over the reference's K ranges, each
+    rounded to fp16, summed in fp32, rounded), the reference kernel must match
+    the emulation, and this library must match the reference kernel, within
+    sum_s ulp(partial_s) + 2 ulp(C) per element;
   * bit for bit against spmm24_launch with the same split_k.
 
 Weights are N(0, 0.02) generated on the device, magnitude-pruned 2:4 by
@@ -84,6 +91,38 @@ def _rows(M, seed):
     return np.unique(np.concatenate([[0, M - 1], rng.choice(M, SAMPLE_ROWS - 2, replace=False)]))
 
 
+def _ulp16(x):
+    """fp16 unit in the last place at |x| (subnormal spacing below 2^-14)."""
+    ax = np.maximum(np.abs(x.astype(np.float64)), 2.0 ** -14)
+    return 2.0 ** (np.floor(np.log2(ax)) - 10)
+
+
+def _reference_emulation(a_rows, b, n_rows, N, K, split_k):
+    """The reference's split-K arithmetic on the given rows: partial sums over
+    its K ranges (64-wide K blocks, ceil(blocks / Split_K) per split, the last
+    split the remainder; src/SpMM_Kernel.cuh:324-334), each rounded to fp16,
+    summed in fp32 in split order and rounded (reduce_Kernel.cuh:27-53).
+    Returns (C as fp32 values of fp16, the per-element bound
+    sum_s ulp(partial_s) + 2 ulp(C))."""
+    kt = K // 64
+    avg = (kt - 1) // split_k + 1
+    A = a_rows.reshape(n_rows, K)
+    Bm = b.reshape(K, N)
+    acc = np.zeros((n_rows, N), dtype=np.float32)
+    bound = np.zeros((n_rows, N), dtype=np.float64)
+    for s in range(split_k):
+        k0, k1 = 64 * s * avg, 64 * min((s + 1) * avg, kt)
+        if k1 <= k0:
+            continue
+        part = O.dense_gemm_f32(np.ascontiguousarray(A[:, k0:k1]).reshape(-1),
+                                np.ascontiguousarray(Bm[k0:k1]).reshape(-1), n_rows, N, k1 - k0).reshape(n_rows, N)
+        p16 = part.astype(np.float16).astype(np.float32)
+        acc += p16
+        bound += _ulp16(part)
+    c = acc.astype(np.float16).astype(np.float32)
+    return c, bound + 2 * _ulp16(c)
+
+
 def _bits(t):
     import torch
 
@@ -124,8 +163,16 @@ def _run_case(dev, a, vals, meta, M, K, N, split_k, seed, check_reference=True):
             assert rc == 0
             torch.cuda.synchronize(dev)
             refk = _bits(c3)
-            assert within_tolerance(compare(refk[rows], ref_c)), ("reference kernel vs oracle", M, K, N, split_k)
-            assert within_tolerance(compare(got, refk.view(np.float16).astype(np.float32))), (M, K, N, split_k)
+            a_rows = _bits(a[torch.from_numpy(rows).to(dev)]).reshape(-1)
+            emu, bound = _reference_emulation(a_rows, _bits(b).reshape(-1), len(rows), N, K, split_k)
+            rk = refk[rows].view(np.float16).astype(np.float32)
+            ours = got[rows].view(np.float16).astype(np.float32)
+            assert np.all(np.abs(rk - emu) <= bound), ("reference kernel vs its emulation", M, K, N, split_k,
+                                                       float(np.max(np.abs(rk - emu) - bound)))
+            assert np.all(np.abs(ours - rk) <= bound), ("ours vs reference kernel", M, K, N, split_k,
+                                                        float(np.max(np.abs(ours - rk) - bound)))
+            if split_k == 1:  # no partial rounding: the plain fp16 tolerance holds for the reference too
+                assert within_tolerance(compare(refk[rows], ref_c)), ("reference kernel vs oracle", M, K, N)
     return got
 
 
