@@ -46,9 +46,11 @@ REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(REPO, "cuda-repo_b200"))
 
 WORKLOADS = {
-    # BASELINE config 2 (the headline): LLaMA-7B decode
+    # BASELINE config 2 (the headline): LLaMA-7B decode; on N > 1 GPUs every
+    # layer is split along M across the ranks and the outputs are all-gathered
+    # inside the step (strong scaling)
     "decode": {"shapes": [(M, N, K) for (M, K) in ((4096, 4096), (11008, 4096), (4096, 11008)) for N in (1, 8, 16, 32)],
-               "a_std": 0.02, "bound": "hbm"},
+               "a_std": 0.02, "bound": "hbm", "shard": True},
     # LLaMA-7B prefill
     "prefill": {"shapes": [(M, N, K) for (M, K) in ((4096, 4096), (11008, 4096), (4096, 11008)) for N in (512, 2048, 4096)],
                 "a_std": 0.02, "bound": "tensor"},
@@ -226,7 +228,11 @@ def workload_config(args, world):
             "baseline_config": {"decode": 2, "prefill": 3, "70b": 4, "square": 5}[args.workload],
             "spmm_per_step": len(shapes), "split_k": "auto (library picker)",
             "l2": f"inputs larger than L2: {wbytes / 1e6:.0f} MB of distinct weights per step (whole job)",
-            "parallelism": (f"M-sharded x{world} (rows split by spmm24_shard_rows, no reduction)" if shard
+            "parallelism": (("M-sharded" if world > 1 else "unsharded") +
+                            f" x{world} (rows split by spmm24_shard_rows, no reduction" +
+                            ("; outputs all-gathered into every rank's full C inside the step: the grouped kernel's "
+                             "epilogue stores over NVLink + spmm24_gather_barrier)"
+                             if world > 1 and args.workload == "decode" else ")") if shard
                             else f"replicas x{world} (each rank its own layers)")}
 
 
@@ -271,9 +277,11 @@ def run_ours(args, rank, world, local_rank):
     acts = {}
     for j, (K, N) in enumerate(sorted({(K, N) for (M, N, K) in shapes})):
         if fp8:
-            acts[(K, N)] = make_activations_fp8(torch, K, N, seed=5000 + 100 * rank + j)
+            acts[(K, N)] = make_activations_fp8(torch, K, N, seed=5000 + (0 if shard else 100 * rank) + j)
             continue
-        acts[(K, N)] = make_activations(torch, spmm24, K, N, seed=5000 + 100 * rank + j, uniform=square)
+        # sharded layers: every rank holds the same activations
+        acts[(K, N)] = make_activations(torch, spmm24, K, N, seed=5000 + (0 if shard else 100 * rank) + j,
+                                        uniform=square)
 
     # Device copies: every call of a step gets its own weights so that the
     # working set of a step exceeds L2.  Activations and outputs of a step are
@@ -346,21 +354,70 @@ def run_ours(args, rank, world, local_rank):
     # layers); "chain" issues one spmm24_launch per SpMM.
     grouped = args.launch == "grouped" and not fp8 and args.epilogue == "none" and all(c["N"] <= 32 for c in calls)
     group_flags = flags & (spmm24.STATIC_WEIGHTS | spmm24.BF16)
+    # M-sharded decode on N > 1 GPUs: every rank's output rows go straight into
+    # every rank's full C (the grouped kernel's epilogue stores over NVLink to
+    # the peers' buffers, opened with CUDA IPC), then one cross-GPU barrier;
+    # both inside the timed step.  Two full-C sets, for the e2e loop's two
+    # buffer sets.
+    gather_mode = grouped and shard and world > 1
+    full_sets, flag_ptrs, imported, epoch = [], None, [], [0]
+    if gather_mode:
+        full_elems = sum(c["M_full"] * c["N"] for c in calls)
+        full_sets = [torch.zeros(full_elems, dtype=torch.float16, device=dev) for _ in range(2)]
+        flag_buf = torch.zeros(world, dtype=torch.int32, device=dev)
+        torch.cuda.synchronize(dev)
+        mine = [spmm24.ipc_export(t) for t in full_sets] + [spmm24.ipc_export(flag_buf)]
+        handles = [None] * world
+        dist.all_gather_object(handles, mine)
+        bases = [[None] * world for _ in range(3)]
+        for r in range(world):
+            for i in range(3):
+                if r == rank:
+                    bases[i][r] = (full_sets[i] if i < 2 else flag_buf).data_ptr()
+                else:
+                    bases[i][r] = spmm24.ipc_import(handles[r][i])
+                    imported.append(bases[i][r])
+        flag_ptrs = bases[2]
+        dist.barrier()
 
-    def group_array(cs):
-        return spmm24.problem_array([(c["A"], c["B"], c["E"], c["C"], c["M"], c["N"], c["K"]) for c in cs])
+    def gathers_for(k):
+        """Gather descriptors of full-C set k, one per call."""
+        out_g, off = [], 0
+        for c in calls:
+            out_g.append(spmm24.make_gather([b + 2 * off for b in bases[k]], rows[c["M_full"]][0], c["M_full"]))
+            off += c["M_full"] * c["N"]
+        return out_g
+
+    def group_array(cs, k):
+        gs = gathers_for(k) if gather_mode else [None] * len(cs)
+        return spmm24.problem_array([(c["A"], c["B"], c["E"], c["C"], c["M"], c["N"], c["K"], g)
+                                     for c, g in zip(cs, gs)])
 
     group_arrays = {}
 
-    def step_launch(cs, hs=None, use_group=grouped):
+    def step_launch(cs, hs=None, use_group=grouped, k=0):
+        hs = h_stream if hs is None else hs
         if use_group:
-            arr = group_arrays.setdefault(id(cs), group_array(cs))
-            rc = spmm24._lib.spmm24_launch_grouped(h_stream if hs is None else hs, arr, len(arr), group_flags)
+            arr = group_arrays.setdefault((id(cs), k), group_array(cs, k))
+            rc = spmm24._lib.spmm24_launch_grouped(hs, arr, len(arr), group_flags)
             if rc != 0:
                 raise RuntimeError(f"spmm24_launch_grouped failed: {rc} {spmm24._lib.spmm24_last_error().decode()}")
+        elif gather_mode:  # the chain: one spmm24_launch_gather per SpMM
+            off = 0
+            for c in cs:
+                rc = spmm24.launch_gather(hs, c["A"], c["B"], c["E"], c["M"], c["N"], c["K"],
+                                          [b + 2 * off for b in bases[k]], rows[c["M_full"]][0], c["M_full"], 0,
+                                          flags)
+                off += c["M_full"] * c["N"]
+                if rc != 0:
+                    raise RuntimeError(f"spmm24_launch_gather: {rc} {spmm24._lib.spmm24_last_error().decode()}")
         else:
             for c in cs:
                 launch(c, hs)
+        if gather_mode:
+            epoch[0] += 1
+            if spmm24.gather_barrier(hs, flag_ptrs, rank, epoch[0]) != 0:
+                raise RuntimeError("spmm24_gather_barrier failed")
 
     def timed_steps(use_group):
         """Device time (ms) of args.steps steps back to back.  A sleep kernel
@@ -386,7 +443,7 @@ def run_ours(args, rank, world, local_rank):
     chain_ms = None
     if grouped:
         chain_ms = timed_steps(False)  # the same steps as one launch per SpMM, for comparison
-    nl = (1 if grouped else len(calls)) * args.steps
+    nl = ((1 if grouped else len(calls)) + (1 if gather_mode else 0)) * args.steps  # + the barrier kernel
     with ClockSampler(local_rank) as clk:
         elapsed_ms = timed_steps(grouped)
     clocks = clk.summary()
@@ -415,11 +472,15 @@ def run_ours(args, rank, world, local_rank):
     # sets alternate between steps, so step i's upload (its own stream)
     # overlaps step i-1's kernels and step i-1's download (another stream)
     # overlaps step i's; events order every reuse of a buffer.
-    host_out = [torch.empty(C_all.shape, dtype=torch.float16).pin_memory() for _ in range(2)]
+    # (gather mode: the result a rank downloads is its full C, every layer's
+    # rows from every rank)
+    out_sets = full_sets if gather_mode else None
+    host_out = [torch.empty((out_sets[0] if gather_mode else C_all).shape, dtype=torch.float16).pin_memory()
+                for _ in range(2)]
     h2d = host_in.numel() * host_in.element_size()
     d2h = host_out[0].numel() * 2
     B_set = [B_all, torch.empty_like(B_all)]
-    C_set = [C_all, torch.empty_like(C_all)]
+    C_set = out_sets if gather_mode else [C_all, torch.empty_like(C_all)]
     call_sets = [calls, []]
     for c in calls:
         bs_, cs_ = c["B"].numel(), c["C"].numel()
@@ -428,11 +489,12 @@ def run_ours(args, rank, world, local_rank):
                                  C=c1 if packed_out else c1.view(c["M"], c["N"])))
     graphs = [None, None]
     try:
-        for k in range(2):
+        # (gather mode launches eagerly: every step's barrier takes a new epoch)
+        for k in range(0 if gather_mode else 2):
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g):
                 hs = int(torch.cuda.current_stream(dev).cuda_stream)
-                step_launch(call_sets[k], hs)
+                step_launch(call_sets[k], hs, k=k)
             graphs[k] = g
     except Exception:  # noqa: BLE001 -- fall back to eager launches
         graphs = [None, None]
@@ -455,7 +517,7 @@ def run_ours(args, rank, world, local_rank):
         if graphs[k] is not None:
             graphs[k].replay()
         else:
-            step_launch(call_sets[k])
+            step_launch(call_sets[k], k=k)
         comp_done[k].record(stream)
         with torch.cuda.stream(down):
             down.wait_event(comp_done[k])
@@ -613,6 +675,15 @@ def run_ours(args, rank, world, local_rank):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(layers, acts, shapes, budget_s=args.cpu_seconds, bf16=bf16, fp8=fp8)
 
+    if gather_mode:
+        out["gather"] = {"status": spmm24.device_status(dev.index), "ranks": world,
+                         "gathered_bytes_per_step": 2 * sum(c["M_full"] * c["N"] for c in calls),
+                         "op": "each rank's output rows stored by the grouped kernel's epilogue into all ranks' "
+                               "full C (CUDA IPC peer pointers, NVLink), then one spmm24_gather_barrier per step"}
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        for p_ in imported:
+            spmm24.ipc_close(p_)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -1191,6 +1262,15 @@ def run_pack(args, rank, world, local_rank):
             dn = [d.view(torch.int16).cpu().numpy().view(np.uint16).reshape(-1) for d in dense]
         gbs, kind, sample = host_pack_baseline(dn, args.cpu_seconds, fp8=fp8)
         out["cpu_baseline"] = {"value": round(gbs, 4), "unit": "GB/s", "cores": 1, "kind": kind, "sample": sample}
+    if gather_mode:
+        out["gather"] = {"status": spmm24.device_status(dev.index), "ranks": world,
+                         "gathered_bytes_per_step": 2 * sum(c["M_full"] * c["N"] for c in calls),
+                         "op": "each rank's output rows stored by the grouped kernel's epilogue into all ranks' "
+                               "full C (CUDA IPC peer pointers, NVLink), then one spmm24_gather_barrier per step"}
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        for p_ in imported:
+            spmm24.ipc_close(p_)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -1346,6 +1426,15 @@ def run_pack_b(args, rank, world, local_rank):
         an = [a.view(torch.int16).cpu().numpy().view(np.uint16).reshape(-1) for a in acts]
         gbs, kind, sample = host_pack_b_baseline(an, args.cpu_seconds)
         out["cpu_baseline"] = {"value": round(gbs, 4), "unit": "GB/s", "cores": 1, "kind": kind, "sample": sample}
+    if gather_mode:
+        out["gather"] = {"status": spmm24.device_status(dev.index), "ranks": world,
+                         "gathered_bytes_per_step": 2 * sum(c["M_full"] * c["N"] for c in calls),
+                         "op": "each rank's output rows stored by the grouped kernel's epilogue into all ranks' "
+                               "full C (CUDA IPC peer pointers, NVLink), then one spmm24_gather_barrier per step"}
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        for p_ in imported:
+            spmm24.ipc_close(p_)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

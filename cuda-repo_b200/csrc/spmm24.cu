@@ -743,7 +743,7 @@ cudaError_t launch_fp8_impl(cudaStream_t stream, const void* A, const void* B, c
 // is kept per host thread and reused while the same problems are launched
 // again.
 struct GroupCache {
-    std::vector<spmm24_problem> key;
+    std::vector<unsigned char> key;  // the problems and their gather descriptors, byte for byte
     unsigned flags = 0;
     int sms = 0;
     int n_ctas = 0;
@@ -767,6 +767,12 @@ cudaError_t build_group(const spmm24_problem* probs, int count, unsigned flags, 
         g.K = q.K;
         g.groups = groups;
         g.stages_total = st;
+        if (q.gather) {
+            g.gather_n = q.gather->n_ranks;
+            g.gather_row0 = q.gather->row_offset;
+            for (int r = 0; r < q.gather->n_ranks; ++r) g.gather_dst[r] = static_cast<uint16_t*>(q.gather->c_full[r]);
+            g.gather_mc = static_cast<uint16_t*>(q.gather->c_multicast);
+        }
         const int mt = (q.M + kTileM - 1) / kTileM;
         for (int m = 0; m < mt; ++m) tiles.push_back({st + 1, i, m});
         cuuint64_t adims[3] = {128, (cuuint64_t)(q.M / 16), (cuuint64_t)(q.K / 16)};
@@ -817,7 +823,7 @@ cudaError_t launch_grouped_impl(cudaStream_t stream, const spmm24_problem* probs
     long long tiles = 0;
     for (int i = 0; i < count; ++i) {
         const spmm24_problem& q = probs[i];
-        if (!q.compressed_a || !q.b_packed || !q.metadata || !q.c) return invalid("grouped: null pointer");
+        if (!q.compressed_a || !q.b_packed || !q.metadata || (!q.c && !q.gather)) return invalid("grouped: null pointer");
         if (q.M <= 0 || q.N <= 0 || q.K <= 0) return invalid("grouped: M, N and K must be positive");
         if (q.M % 16) return invalid("grouped: M must be a multiple of 16");
         if (q.K % 64) return invalid("grouped: K must be a multiple of 64");
@@ -827,6 +833,17 @@ cudaError_t launch_grouped_impl(cudaStream_t stream, const spmm24_problem* probs
         if ((uintptr_t)q.c & 1u) return invalid("grouped: C must be 2-byte aligned");
         if ((q.M + kTileM - 1) / kTileM > 4096) return invalid("grouped: M must be <= 524288");
         tiles += (q.M + kTileM - 1) / kTileM;
+        if (const spmm24_gather* g = q.gather) {
+            if (g->n_ranks < 1 || g->n_ranks > SPMM24_MAX_GATHER_RANKS) return invalid("gather: n_ranks must be 1..8");
+            if (g->row_offset < 0 || g->m_full < q.M || g->row_offset > g->m_full - q.M)
+                return invalid("gather: the shard's rows must lie inside the full C");
+            for (int r = 0; r < g->n_ranks; ++r) {
+                if (!g->c_full[r]) return invalid("gather: null full-C pointer");
+                if ((uintptr_t)g->c_full[r] & 15u) return invalid("gather: full-C buffers must be 16-byte aligned");
+            }
+            if (g->c_multicast && ((uintptr_t)g->c_multicast & 15u))
+                return invalid("gather: the multicast C must be 16-byte aligned");
+        }
     }
     if (tiles > kGroupMaxTiles) return invalid("grouped: more than 2048 128-row tiles in one launch");
     int dev = 0;
@@ -835,13 +852,23 @@ cudaError_t launch_grouped_impl(cudaStream_t stream, const spmm24_problem* probs
     const int sms = sm_count(dev);
     if (!t_group_cache) t_group_cache = new GroupCache();
     GroupCache& gc = *t_group_cache;
-    const bool hit = gc.n_ctas > 0 && gc.flags == flags && gc.sms == sms && (int)gc.key.size() == count &&
-                     std::memcmp(gc.key.data(), probs, sizeof(spmm24_problem) * count) == 0;
+    // Cache key: every problem and the contents of its gather descriptor.
+    thread_local std::vector<unsigned char> key;
+    key.clear();
+    for (int i = 0; i < count; ++i) {
+        const unsigned char* b = reinterpret_cast<const unsigned char*>(&probs[i]);
+        key.insert(key.end(), b, b + sizeof(spmm24_problem));
+        spmm24_gather g{};
+        if (probs[i].gather) g = *probs[i].gather;
+        const unsigned char* gb = reinterpret_cast<const unsigned char*>(&g);
+        key.insert(key.end(), gb, gb + sizeof(g));
+    }
+    const bool hit = gc.n_ctas > 0 && gc.flags == flags && gc.sms == sms && gc.key == key;
     if (!hit) {
         gc.n_ctas = 0;
         int n = 0;
         if ((e = build_group(probs, count, flags, sms, gc.params, n)) != cudaSuccess) return e;
-        gc.key.assign(probs, probs + count);
+        gc.key = key;
         gc.flags = flags;
         gc.sms = sms;
         gc.n_ctas = n;

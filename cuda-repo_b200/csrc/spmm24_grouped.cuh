@@ -36,6 +36,13 @@ struct GroupProblem {
     int M, N, K;
     int groups;        // K / 64
     int stages_total;  // ceil(groups / 2): 128-K stages per tile
+    // Fused all-gather of an M-shard (gather_n > 0): output row gm goes to row
+    // gather_row0 + gm of every rank's full row-major C (peer pointers reached
+    // over NVLink), or once through the full C's multicast address.
+    int gather_n;
+    int gather_row0;
+    uint16_t* gather_dst[kMaxGatherRanks];
+    uint16_t* gather_mc;
 };
 
 struct GroupParams {
@@ -72,11 +79,11 @@ __device__ __forceinline__ void group_entry(const GroupParams& p, int t, int& pi
 }
 
 // Rounds the first N (<= 32) of 32 fp32 values of one output row to C's type
-// and stores them at row gm of C (16-byte stores when N % 8 == 0 and C is
-// 16-byte aligned).  Fully unrolled with predicates, so v stays in registers.
-__device__ __forceinline__ void group_store_row(uint16_t* C, int gm, int N, const uint32_t (&v)[32], int bf16,
+// and stores them at `out` (16-byte stores when N % 8 == 0 and the row is
+// 16-byte aligned; through the multicast address `mc` instead when given).
+// Fully unrolled with predicates, so v stays in registers.
+__device__ __forceinline__ void group_store_row(uint16_t* out, uint16_t* mc, int N, const uint32_t (&v)[32], int bf16,
                                                 bool vec) {
-    uint16_t* out = C + (size_t)gm * N;
     if (vec) {
 #pragma unroll
         for (int c = 0; c < 32; c += 8) {
@@ -85,7 +92,9 @@ __device__ __forceinline__ void group_store_row(uint16_t* C, int gm, int N, cons
 #pragma unroll
                 for (int i = 0; i < 4; ++i)
                     w[i] = pack2(__uint_as_float(v[c + 2 * i]), __uint_as_float(v[c + 2 * i + 1]), bf16);
-                *reinterpret_cast<uint4*>(out + c) = make_uint4(w[0], w[1], w[2], w[3]);
+                const uint4 q = make_uint4(w[0], w[1], w[2], w[3]);
+                if (mc) ptx::multimem_st_v4(mc + c, q);
+                else *reinterpret_cast<uint4*>(out + c) = q;
             }
         }
     } else {
@@ -269,9 +278,21 @@ __global__ void __launch_bounds__(kThreads, 1) spmm24_grouped_kernel(const __gri
                 waited = true;
             }
             const int gm = m_tile * kTileM + row;
-            uint16_t* C = p.prob[pi].C;
-            if (gm < p.prob[pi].M)
-                group_store_row(C, gm, N, v, p.bf16, (N % 8 == 0) && ((reinterpret_cast<uintptr_t>(C) & 15u) == 0));
+            const GroupProblem& q = p.prob[pi];
+            if (gm < q.M) {
+                if (q.gather_n) {  // destinations are 16-byte aligned (checked by the host)
+                    const size_t off = (size_t)(q.gather_row0 + gm) * N;
+                    if (q.gather_mc && N % 8 == 0) {
+                        group_store_row(nullptr, q.gather_mc + off, N, v, p.bf16, true);
+                    } else {
+                        for (int d = 0; d < q.gather_n; ++d)
+                            group_store_row(q.gather_dst[d] + off, nullptr, N, v, p.bf16, N % 8 == 0);
+                    }
+                } else {
+                    group_store_row(q.C + (size_t)gm * N, nullptr, N, v, p.bf16,
+                                    (N % 8 == 0) && ((reinterpret_cast<uintptr_t>(q.C) & 15u) == 0));
+                }
+            }
         }
     }
 

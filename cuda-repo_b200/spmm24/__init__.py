@@ -215,7 +215,8 @@ def launch_fp8(stream, values, b_nk, metadata, c, M: int, N: int, K: int, split_
 class Problem(ctypes.Structure):
     """spmm24_problem (include/spmm24/SpMM_API.h)."""
     _fields_ = [("compressed_a", ctypes.c_void_p), ("b_packed", ctypes.c_void_p), ("metadata", ctypes.c_void_p),
-                ("c", ctypes.c_void_p), ("M", ctypes.c_int), ("N", ctypes.c_int), ("K", ctypes.c_int)]
+                ("c", ctypes.c_void_p), ("M", ctypes.c_int), ("N", ctypes.c_int), ("K", ctypes.c_int),
+                ("gather", ctypes.c_void_p)]
 
 
 _lib.spmm24_launch_grouped.argtypes = [_vp, ctypes.POINTER(Problem), ctypes.c_int, ctypes.c_uint]
@@ -224,11 +225,33 @@ _lib.spmm24_launch_grouped.restype = ctypes.c_int
 
 def problem_array(problems):
     """A ctypes array of spmm24_problem from (compressed_a, b_packed, metadata,
-    c, M, N, K) tuples (tensors or int addresses)."""
+    c, M, N, K[, gather]) tuples (tensors or int addresses; gather: a Gather
+    structure, kept alive by the returned array)."""
     arr = (Problem * len(problems))()
-    for i, (a, b, e, c, M, N, K) in enumerate(problems):
-        arr[i] = Problem(_ptr(a), _ptr(b), _ptr(e), _ptr(c), M, N, K)
+    keep = []
+    for i, t in enumerate(problems):
+        a, b, e, c, M, N, K = t[:7]
+        g = t[7] if len(t) > 7 else None
+        if g is not None:
+            keep.append(g)
+        arr[i] = Problem(_ptr(a), _ptr(b), _ptr(e), _ptr(c), M, N, K,
+                         ctypes.addressof(g) if g is not None else None)
+    arr._gathers = keep
     return arr
+
+
+def make_gather(c_full_ptrs, row_offset: int, m_full: int, c_multicast=None) -> "Gather":
+    """A spmm24_gather descriptor: rank r's full C at c_full_ptrs[r]."""
+    if len(c_full_ptrs) > 8:
+        raise ValueError("at most 8 ranks (SPMM24_MAX_GATHER_RANKS)")
+    g = Gather()
+    for r, p in enumerate(c_full_ptrs):
+        g.c_full[r] = _ptr(p)
+    g.n_ranks = len(c_full_ptrs)
+    g.row_offset = row_offset
+    g.m_full = m_full
+    g.c_multicast = _ptr(c_multicast)
+    return g
 
 
 def launch_grouped(stream, problems, flags: int = 0) -> int:

@@ -94,13 +94,20 @@ cudaError_t spmm24_launch_ex(cudaStream_t stream, const void* compressed_a, cons
  * SPMM24_BF16.  Allocates nothing; the encoded launch is cached per host
  * thread and reused when the same problem array is launched again.
  * Returns cudaErrorInvalidValue (reason in spmm24_last_error) for a bad
- * problem, count or flag. */
+ * problem, count or flag.
+ * gather (optional): the problem is one M-shard of a layer split across the
+ * GPUs of a node, and its output rows go straight into row
+ * gather->row_offset + m of every rank's full C (as for
+ * spmm24_launch_gather; c may then be NULL); complete on the peers after
+ * spmm24_gather_barrier on every rank.  spmm24_gather is declared below. */
+struct spmm24_gather;
 typedef struct spmm24_problem {
     const void* compressed_a;
     const void* b_packed;
     const uint16_t* metadata;
     void* c;
     int M, N, K;
+    const struct spmm24_gather* gather;
 } spmm24_problem;
 cudaError_t spmm24_launch_grouped(cudaStream_t stream, const spmm24_problem* problems, int count, unsigned flags);
 

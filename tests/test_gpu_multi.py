@@ -176,3 +176,92 @@ def test_fused_allgather_multicast_two_gpus(tmp_path):
     if results == {"unsupported"}:
         pytest.skip("no NVLink multicast between GPU 0 and GPU 1")
     assert results == {"ok"}
+
+
+def _worker_grouped(rank, world, port, shapes):
+    """Several M-sharded layers in one spmm24_launch_grouped whose epilogue
+    gathers every layer's rows into every rank's full C, then one barrier."""
+    import sys
+    from datetime import timedelta
+
+    sys.path.insert(0, os.path.join(REPO, "cuda-repo_b200"))
+    import torch
+    import torch.distributed as dist
+
+    import spmm24
+
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=60))
+    layers, expects, fulls = [], [], []
+    for (M, N, K) in shapes:
+        rng = np.random.default_rng(M + N + K)   # same weights and activations on every rank
+        a = (rng.standard_normal((M, K)) * 0.05).astype(np.float16).view(np.uint16)
+        vals, meta = spmm24.compress_reordered(spmm24.prune_2of4(a, M, K), M, K)
+        b = rng.standard_normal((K, N)).astype(np.float16).view(np.uint16)
+        bp = torch.from_numpy(spmm24.pack_b(b, K, N).view(np.int16)).to(dev)
+        A = torch.from_numpy(vals.view(np.int16)).to(dev)
+        E = torch.from_numpy(meta.view(np.int16)).to(dev)
+        layers.append((M, N, K, A, E, bp))
+        expects.append(torch.empty((M, N), dtype=torch.float16, device=dev))
+        fulls.append(torch.full((M, N), float("nan"), dtype=torch.float16, device=dev))
+    # expected: every rank's shards of every layer, one grouped launch on this GPU
+    local = []
+    for (M, N, K, A, E, bp), ex in zip(layers, expects):
+        for r in range(world):
+            r0, r1 = spmm24.shard_rows(M, world, r, 128)
+            Av, Ev = spmm24.shard_views(A, E, M, K, r0, r1)
+            local.append((Av, bp, Ev, ex[r0:r1], r1 - r0, N, K))
+    assert spmm24.launch_grouped(None, local) == 0, spmm24._lib.spmm24_last_error().decode()
+    flags = torch.zeros(world, dtype=torch.int32, device=dev)
+    torch.cuda.synchronize(dev)
+    handles = [None] * world
+    dist.all_gather_object(handles, [spmm24.ipc_export(f) for f in fulls] + [spmm24.ipc_export(flags)])
+    ptrs = [[None] * world for _ in range(len(fulls) + 1)]
+    opened = []
+    for r in range(world):
+        for i in range(len(fulls) + 1):
+            if r == rank:
+                ptrs[i][r] = (fulls[i] if i < len(fulls) else flags).data_ptr()
+            else:
+                ptrs[i][r] = spmm24.ipc_import(handles[r][i])
+                opened.append(ptrs[i][r])
+    dist.barrier()
+    probs = []
+    for i, (M, N, K, A, E, bp) in enumerate(layers):
+        r0, r1 = spmm24.shard_rows(M, world, rank, 128)
+        Av, Ev = spmm24.shard_views(A, E, M, K, r0, r1)
+        probs.append((Av, bp, Ev, None, r1 - r0, N, K, spmm24.make_gather(ptrs[i], r0, M)))
+    s = torch.cuda.current_stream(dev)
+    for epoch in (1, 2):  # twice: the second launch reuses the cached launch and the barrier's next epoch
+        for f in fulls:
+            f.fill_(float("nan"))
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        assert spmm24.launch_grouped(s, probs, spmm24.STATIC_WEIGHTS) == 0, spmm24._lib.spmm24_last_error().decode()
+        assert spmm24.gather_barrier(s, ptrs[-1], rank, epoch) == 0
+        torch.cuda.synchronize(dev)
+        assert spmm24.device_status(rank) == 0
+        for i, (f, ex) in enumerate(zip(fulls, expects)):
+            assert torch.equal(f, ex), (rank, epoch, shapes[i])
+        dist.barrier()
+    for p in opened:
+        spmm24.ipc_close(p)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_grouped_allgather_two_gpus():
+    """spmm24_launch_grouped with a gather descriptor per layer: each rank's
+    full C of every layer equals, bit for bit, all shards computed locally by
+    one grouped launch (ragged shards, N = 1 .. 32)."""
+    import torch
+    import torch.multiprocessing as mp
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    if not torch.cuda.can_device_access_peer(0, 1):
+        pytest.skip("no peer access between GPU 0 and GPU 1")
+    shapes = [(1024, 16, 1024), (2048, 8, 512), (512, 1, 256), (768, 24, 704), (640, 32, 512), (4096, 32, 4096)]
+    mp.spawn(_worker_grouped, args=(2, _free_port(), shapes), nprocs=2, join=True)
