@@ -21,7 +21,7 @@ test/kernelTest.cu:193,197 binds), and is checked
     oracle emulates it (fp32 partials over the reference's K ranges, each
     rounded to fp16, summed in fp32, rounded), the reference kernel must match
     the emulation, and this library must match the reference kernel, within
-    sum_s ulp(partial_s) + 2 ulp(C) per element;
+    sum_s ulp(partial_s) + 2 ulp(C) + 2^-15 sum_k |a_k b_k| per element;
   * bit for bit against spmm24_launch with the same split_k.
 
 Weights are N(0, 0.02) generated on the device, magnitude-pruned 2:4 by
@@ -103,7 +103,9 @@ def _reference_emulation(a_rows, b, n_rows, N, K, split_k):
     split the remainder; src/SpMM_Kernel.cuh:324-334), each rounded to fp16,
     summed in fp32 in split order and rounded (reduce_Kernel.cuh:27-53).
     Returns (C as fp32 values of fp16, the per-element bound
-    sum_s ulp(partial_s) + 2 ulp(C))."""
+    sum_s ulp(partial_s) + 2 ulp(C) + 2^-15 sum_k |a_k b_k|; the last term
+    covers fp32 accumulation in another order -- the tensor cores' against
+    the oracle's sequential sum -- where the result cancels)."""
     kt = K // 64
     avg = (kt - 1) // split_k + 1
     A = a_rows.reshape(n_rows, K)
@@ -120,7 +122,9 @@ def _reference_emulation(a_rows, b, n_rows, N, K, split_k):
         acc += p16
         bound += _ulp16(part)
     c = acc.astype(np.float16).astype(np.float32)
-    return c, bound + 2 * _ulp16(c)
+    mag = O.dense_gemm_f32(np.ascontiguousarray(a_rows & 0x7FFF), np.ascontiguousarray(b & 0x7FFF), n_rows, N,
+                           K).reshape(n_rows, N)
+    return c, bound + 2 * _ulp16(c) + 2.0 ** -15 * mag
 
 
 def _bits(t):
