@@ -464,6 +464,61 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize(dev)
     per_launch_us = [a.elapsed_time(b) * 1e3 for a, b in ev]
     per_call = [statistics.median(per_launch_us[ci::len(calls)]) for ci in range(len(calls))]
+    # The same single shapes through the grouped kernel (a group of one).
+    per_call_grouped = None
+    if grouped and not gather_mode:
+        singles = [spmm24.problem_array([(c["A"], c["B"], c["E"], c["C"], c["M"], c["N"], c["K"])]) for c in calls]
+        evg = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(reps * len(calls))]
+        torch.cuda.synchronize(dev)
+        torch.cuda._sleep(int(2e7))
+        i = 0
+        for _ in range(reps):
+            for arr in singles:
+                evg[i][0].record(stream)
+                spmm24._lib.spmm24_launch_grouped(h_stream, arr, 1, group_flags)
+                evg[i][1].record(stream)
+                i += 1
+        torch.cuda.synchronize(dev)
+        us_g = [a.elapsed_time(b) * 1e3 for a, b in evg]
+        per_call_grouped = [statistics.median(us_g[ci::len(calls)]) for ci in range(len(calls))]
+
+    # Host time per call: eager launches (no graph), each call's own host
+    # work (argument checks, plan, cached TMA descriptors, cudaLaunchKernelEx)
+    # less the same ctypes call rejected at its first check (unknown flag),
+    # with a sleep kernel ahead so the GPU never drains the launch queue.
+    def host_us(fn, bad_fn, n=200):
+        torch.cuda.synchronize(dev)
+        torch.cuda._sleep(int(1e8))
+        t = time.perf_counter()
+        for _ in range(n):
+            fn()
+        full = time.perf_counter() - t
+        t = time.perf_counter()
+        for _ in range(n):
+            bad_fn()
+        base = time.perf_counter() - t
+        torch.cuda.synchronize(dev)
+        return round(max(0.0, full - base) / n * 1e6, 3), round(full / n * 1e6, 3)
+
+    c0 = calls[0]
+    host = {}
+    if not fp8:
+        lx = spmm24._lib.spmm24_launch_ex
+        args0 = (c0["A"].data_ptr(), c0["B"].data_ptr(), c0["E"].data_ptr(), c0["C"].data_ptr(), c0["M"], c0["N"],
+                 c0["K"], 0)
+        net, tot = host_us(lambda: lx(h_stream, *args0, flags), lambda: lx(h_stream, *args0, 1 << 20))
+        host["spmm24_launch_ex_us"] = net
+        host["spmm24_launch_ex_us_with_ctypes"] = tot
+        if grouped and not gather_mode:
+            arr_all = group_array(calls, 0)
+            lg = spmm24._lib.spmm24_launch_grouped
+            net, tot = host_us(lambda: lg(h_stream, arr_all, len(arr_all), group_flags),
+                               lambda: lg(h_stream, arr_all, len(arr_all), 1 << 20))
+            host["spmm24_launch_grouped_12_us"] = net
+            host["spmm24_launch_grouped_12_us_with_ctypes"] = tot
+        host["note"] = ("host time per eager call, minus the same ctypes call rejected at its first argument check; "
+                        "the kernels' device time per call is in per_shape_us")
 
     # End to end through the public C ABI with host buffers, as a serving
     # loop runs it: every step uploads all of its packed activations from
@@ -603,7 +658,11 @@ def run_ours(args, rank, world, local_rank):
                  else "synthetic (U(-1,1), random 2:4 mask)"),
         "config": workload_config(args, world),
         "per_shape_us": {f"{c['M']}x{c['N']}x{c['K']}": round(u, 3) for c, u in zip(calls, per_call)},
-        "per_shape_note": "median single-kernel duration with an event pair around each launch",
+        "per_shape_note": "median single-kernel duration of one spmm24_launch per shape, an event pair around "
+                          "each launch (per_shape_grouped_us: the same shape as a grouped launch of one problem)",
+        "per_shape_grouped_us": ({f"{c['M']}x{c['N']}x{c['K']}": round(u, 3) for c, u in zip(calls, per_call_grouped)}
+                                 if per_call_grouped else None),
+        "host_per_call": host,
         "launch_flags": " | ".join(f for f, on in (("SPMM24_STATIC_WEIGHTS", args.static_weights), ("SPMM24_BF16", bf16),
                                                    ("spmm24_launch_fp8", fp8)) if on) or "none",
         "epilogue": args.epilogue,
