@@ -463,6 +463,11 @@ cudaError_t launch_pair(const Plan& pl, cudaStream_t stream, int dev, bool pdl, 
                          : launch_pair_v<false>(pl, stream, dev, pdl, ta, tb, te, kp, 11);
 }
 
+// True when an epilogue only rounds (the plain instantiations serve it).
+bool epilogue_is_plain_host(const Epilogue& e) {
+    return e.bias == nullptr && e.residual == nullptr && e.act == kActNone && e.alpha == 1.f && !e.packed;
+}
+
 // Validates a caller's epilogue and turns it into the kernels' form
 // (SPMM24_BF16 in flags: 16-bit outputs are bf16).
 cudaError_t make_epilogue(const spmm24_epilogue* user_epi, unsigned flags, const void* C, Epilogue* out) {
@@ -737,49 +742,43 @@ cudaError_t launch_fp8_impl(cudaStream_t stream, const void* A, const void* B, c
 // ------------------------------------------------------ grouped launch
 // Independent narrow-N problems in one persistent launch (spmm24_grouped.cuh).
 // The tiles (problem, 128-row block) are balanced over one CTA per SM with
-// the longest-processing-time rule: tiles sorted by cost (128-K stages, plus
-// one for the tile's epilogue) in decreasing order, each given to the CTA
-// with the least work so far.  The encoded launch (descriptors + schedule)
-// is kept per host thread and reused while the same problems are launched
-// again.
+// the longest-processing-time rule: tiles sorted by cost (K stages, plus one
+// for the tile's epilogue) in decreasing order, each given to the CTA with
+// the least work so far.  The encoded launch (descriptors, epilogues,
+// schedule) is kept per host thread and reused while the same problems are
+// launched again.
 struct GroupCache {
-    std::vector<unsigned char> key;  // the problems and their gather descriptors, byte for byte
+    std::vector<unsigned char> key;  // the problems, their gathers and epilogues, byte for byte
     unsigned flags = 0;
     int sms = 0;
     int n_ctas = 0;
+    bool epi = false;  // some problem has a non-plain epilogue
     GroupParams params;
 };
 thread_local GroupCache* t_group_cache = nullptr;
 
-cudaError_t build_group(const spmm24_problem* probs, int count, unsigned flags, int sms, GroupParams& gp, int& n_ctas) {
-    std::memset(&gp, 0, sizeof(gp));
-    struct Tile {
-        int cost, prob, m_tile;
-    };
-    std::vector<Tile> tiles;
-    for (int i = 0; i < count; ++i) {
-        const spmm24_problem& q = probs[i];
-        const int groups = q.K / 64, st = (groups + 1) / 2;
-        GroupProblem& g = gp.prob[i];
-        g.C = static_cast<uint16_t*>(q.c);
-        g.M = q.M;
-        g.N = q.N;
-        g.K = q.K;
-        g.groups = groups;
-        g.stages_total = st;
-        if (q.gather) {
-            g.gather_n = q.gather->n_ranks;
-            g.gather_row0 = q.gather->row_offset;
-            for (int r = 0; r < q.gather->n_ranks; ++r) g.gather_dst[r] = static_cast<uint16_t*>(q.gather->c_full[r]);
-            g.gather_mc = static_cast<uint16_t*>(q.gather->c_multicast);
-        }
-        const int mt = (q.M + kTileM - 1) / kTileM;
-        for (int m = 0; m < mt; ++m) tiles.push_back({st + 1, i, m});
-        cuuint64_t adims[3] = {128, (cuuint64_t)(q.M / 16), (cuuint64_t)(q.K / 16)};
-        cuuint64_t astr[2] = {(cuuint64_t)16 * q.K, 256};
-        cuuint32_t abox[3] = {128, 8, 8};
-        if (!encode(&gp.tmA[i], 3, q.compressed_a, adims, astr, abox))
-            return invalid("grouped: TMA descriptor for A could not be encoded");
+// Tensor maps of one problem: the 16-bit formats of spmm24_launch, or (fp8)
+// those of spmm24_launch_fp8; B boxes are kGroupTileN columns / rows wide.
+cudaError_t encode_group_maps(const spmm24_problem& q, bool fp8, GroupParams& gp, int i) {
+    const int Ka = fp8 ? q.K / 2 : q.K;  // the A bytes of an fp8 K are those of a 16-bit K / 2
+    cuuint64_t adims[3] = {128, (cuuint64_t)(q.M / 16), (cuuint64_t)(Ka / 16)};
+    cuuint64_t astr[2] = {(cuuint64_t)16 * Ka, 256};
+    cuuint32_t abox[3] = {128, 8, 8};
+    if (!encode(&gp.tmA[i], 3, q.compressed_a, adims, astr, abox))
+        return invalid("grouped: TMA descriptor for A could not be encoded");
+    if (fp8) {
+        cuuint64_t bdims[2] = {(cuuint64_t)q.K, (cuuint64_t)q.N};
+        cuuint64_t bstr[1] = {(cuuint64_t)q.K};
+        cuuint32_t bbox[2] = {128, (cuuint32_t)kGroupTileN};
+        if (!encode(&gp.tmB[i], 2, q.b_packed, bdims, bstr, bbox, CU_TENSOR_MAP_DATA_TYPE_UINT8,
+                    CU_TENSOR_MAP_SWIZZLE_128B))
+            return invalid("grouped: TMA descriptor for B could not be encoded");
+        cuuint64_t edims[3] = {128, (cuuint64_t)(q.M / 16), (cuuint64_t)(q.K / 128)};
+        cuuint64_t estr[2] = {(cuuint64_t)(q.K / 128) * 256, 256};
+        cuuint32_t ebox[3] = {128, 8, 2};
+        if (!encode(&gp.tmE[i], 3, q.metadata, edims, estr, ebox))
+            return invalid("grouped: TMA descriptor for metadata could not be encoded");
+    } else {
         cuuint64_t bdims[4] = {128, (cuuint64_t)(q.K / 64), 4, (cuuint64_t)((q.N + 7) / 8)};
         cuuint64_t bstr[3] = {1024, 256, (cuuint64_t)16 * q.K};
         cuuint32_t bbox[4] = {128, 2, 4, (cuuint32_t)(kGroupTileN / 8)};
@@ -791,7 +790,42 @@ cudaError_t build_group(const spmm24_problem* probs, int count, unsigned flags, 
         if (!encode(&gp.tmE[i], 2, q.metadata, edims, estr, ebox))
             return invalid("grouped: TMA descriptor for metadata could not be encoded");
     }
-    if (tiles.size() > (size_t)kGroupMaxTiles) return invalid("grouped: more than 2048 128-row tiles in one launch");
+    return cudaSuccess;
+}
+
+cudaError_t build_group(const spmm24_problem* probs, int count, unsigned flags, bool fp8, int sms, GroupParams& gp,
+                        int& n_ctas, bool& any_epi) {
+    std::memset(&gp, 0, sizeof(gp));
+    struct Tile {
+        int cost, prob, m_tile;
+    };
+    std::vector<Tile> tiles;
+    any_epi = false;
+    for (int i = 0; i < count; ++i) {
+        const spmm24_problem& q = probs[i];
+        const int groups = fp8 ? q.K / 128 : q.K / 64, st = (groups + 1) / 2;
+        GroupProblem& g = gp.prob[i];
+        g.C = static_cast<uint16_t*>(q.c);
+        g.M = q.M;
+        g.N = q.N;
+        g.K = q.K;
+        g.groups = groups;
+        g.stages_total = st;
+        cudaError_t e = make_epilogue(q.epilogue, flags, q.c, &g.epi);
+        if (e != cudaSuccess) return e;
+        if (!epilogue_is_plain_host(g.epi)) any_epi = true;
+        if (q.gather) {
+            if (g.epi.packed) return invalid("gather: the full C is row-major");
+            g.epi.gather_n = q.gather->n_ranks;
+            g.epi.gather_row0 = q.gather->row_offset;
+            for (int r = 0; r < q.gather->n_ranks; ++r)
+                g.epi.gather_dst[r] = static_cast<uint16_t*>(q.gather->c_full[r]);
+            g.epi.gather_mc = static_cast<uint16_t*>(q.gather->c_multicast);
+        }
+        const int mt = (q.M + kTileM - 1) / kTileM;
+        for (int m = 0; m < mt; ++m) tiles.push_back({st + 1, i, m});
+        if ((e = encode_group_maps(q, fp8, gp, i)) != cudaSuccess) return e;
+    }
     std::stable_sort(tiles.begin(), tiles.end(), [](const Tile& a, const Tile& b) { return a.cost > b.cost; });
     n_ctas = (int)std::min<size_t>(std::min(sms, kGroupMaxCtas), tiles.size());
     std::vector<long long> load(n_ctas, 0);
@@ -812,21 +846,45 @@ cudaError_t build_group(const spmm24_problem* probs, int count, unsigned flags, 
     gp.n_problems = count;
     gp.weights_static = (flags & SPMM24_STATIC_WEIGHTS) ? 1 : 0;
     gp.bf16 = (flags & SPMM24_BF16) ? 1 : 0;
+    gp.mma_fmt = ((flags & SPMM24_FP8_A_E5M2) ? kIdescFp8AE5M2 : 0u) | ((flags & SPMM24_FP8_B_E5M2) ? kIdescFp8BE5M2 : 0u);
     return cudaSuccess;
 }
 
-cudaError_t launch_grouped_impl(cudaStream_t stream, const spmm24_problem* probs, int count, unsigned flags) {
+template <bool EPI, bool FP8>
+cudaError_t launch_group_kernel(cudaStream_t stream, int dev, const GroupCache& gc, unsigned flags) {
+    using GC = GroupCfg<kGroupStages, FP8>;
+    auto kern = spmm24_grouped_kernel<kGroupStages, EPI, FP8>;
+    cudaError_t e = prepare(kern, GC::SMEM_ALLOC, dev, 80 + (EPI ? 1 : 0) + (FP8 ? 2 : 0));
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)gc.n_ctas, 1, 1);
+    cfg.blockDim = dim3((unsigned)kThreads, 1, 1);
+    cfg.dynamicSmemBytes = GC::SMEM_ALLOC;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = (flags & SPMM24_NO_PDL) ? 0 : 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, gc.params);
+}
+
+cudaError_t launch_grouped_impl(cudaStream_t stream, const spmm24_problem* probs, int count, unsigned flags,
+                                bool fp8) {
     g_last_error[0] = '\0';
     if (!probs) return invalid("grouped: null problem array");
     if (count < 1 || count > kGroupMaxProblems) return invalid("grouped: count must be 1..16");
-    if (flags & ~(unsigned)(SPMM24_STATIC_WEIGHTS | SPMM24_NO_PDL | SPMM24_BF16)) return invalid("unknown flag");
+    const unsigned allowed = SPMM24_STATIC_WEIGHTS | SPMM24_NO_PDL | SPMM24_BF16 |
+                             (fp8 ? (unsigned)(SPMM24_FP8_A_E5M2 | SPMM24_FP8_B_E5M2) : 0u);
+    if (flags & ~allowed) return invalid("unknown flag");
     long long tiles = 0;
     for (int i = 0; i < count; ++i) {
         const spmm24_problem& q = probs[i];
         if (!q.compressed_a || !q.b_packed || !q.metadata || (!q.c && !q.gather)) return invalid("grouped: null pointer");
         if (q.M <= 0 || q.N <= 0 || q.K <= 0) return invalid("grouped: M, N and K must be positive");
         if (q.M % 16) return invalid("grouped: M must be a multiple of 16");
-        if (q.K % 64) return invalid("grouped: K must be a multiple of 64");
+        if (fp8 ? (q.K % 128) : (q.K % 64)) return invalid(fp8 ? "grouped fp8: K must be a multiple of 128"
+                                                               : "grouped: K must be a multiple of 64");
         if (q.N > kGroupTileN) return invalid("grouped: N must be <= 32 (wider N: spmm24_launch)");
         if (((uintptr_t)q.compressed_a | (uintptr_t)q.b_packed | (uintptr_t)q.metadata) & 15u)
             return invalid("grouped: A, B and metadata must be 16-byte aligned");
@@ -852,44 +910,41 @@ cudaError_t launch_grouped_impl(cudaStream_t stream, const spmm24_problem* probs
     const int sms = sm_count(dev);
     if (!t_group_cache) t_group_cache = new GroupCache();
     GroupCache& gc = *t_group_cache;
-    // Cache key: every problem and the contents of its gather descriptor.
+    // Cache key: every problem and the contents of its gather and epilogue.
     thread_local std::vector<unsigned char> key;
     key.clear();
+    auto put = [](std::vector<unsigned char>& k, const void* p, size_t n) {
+        const unsigned char* b = static_cast<const unsigned char*>(p);
+        k.insert(k.end(), b, b + n);
+    };
+    key.push_back(fp8 ? 1 : 0);
     for (int i = 0; i < count; ++i) {
-        const unsigned char* b = reinterpret_cast<const unsigned char*>(&probs[i]);
-        key.insert(key.end(), b, b + sizeof(spmm24_problem));
+        put(key, &probs[i], sizeof(spmm24_problem));
         spmm24_gather g{};
         if (probs[i].gather) g = *probs[i].gather;
-        const unsigned char* gb = reinterpret_cast<const unsigned char*>(&g);
-        key.insert(key.end(), gb, gb + sizeof(g));
+        put(key, &g, sizeof(g));
+        spmm24_epilogue ep{};
+        if (probs[i].epilogue) ep = *probs[i].epilogue;
+        put(key, &ep, sizeof(ep));
     }
     const bool hit = gc.n_ctas > 0 && gc.flags == flags && gc.sms == sms && gc.key == key;
     if (!hit) {
         gc.n_ctas = 0;
         int n = 0;
-        if ((e = build_group(probs, count, flags, sms, gc.params, n)) != cudaSuccess) return e;
+        bool any_epi = false;
+        if ((e = build_group(probs, count, flags, fp8, sms, gc.params, n, any_epi)) != cudaSuccess) return e;
         gc.key = key;
         gc.flags = flags;
         gc.sms = sms;
         gc.n_ctas = n;
+        gc.epi = any_epi;
     }
-    using GC = GroupCfg<kGroupStages>;
-    auto kern = spmm24_grouped_kernel<kGroupStages>;
-    if ((e = prepare(kern, GC::SMEM_ALLOC, dev, 80)) != cudaSuccess) return e;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)gc.n_ctas, 1, 1);
-    cfg.blockDim = dim3((unsigned)kThreads, 1, 1);
-    cfg.dynamicSmemBytes = GC::SMEM_ALLOC;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = (flags & SPMM24_NO_PDL) ? 0 : 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
 #ifdef SPMM24_TRACE
     gc.params.trace_base = g_trace_next.fetch_add((long long)gc.n_ctas);
 #endif
-    return cudaLaunchKernelEx(&cfg, kern, gc.params);
+    if (fp8) return launch_group_kernel<true, true>(stream, dev, gc, flags);
+    if (gc.epi) return launch_group_kernel<true, false>(stream, dev, gc, flags);
+    return launch_group_kernel<false, false>(stream, dev, gc, flags);
 }
 
 // ------------------------------------------------ allocation-free variant
@@ -1102,7 +1157,12 @@ extern "C" cudaError_t spmm24_launch_noalloc(cudaStream_t stream, const void* co
 
 extern "C" cudaError_t spmm24_launch_grouped(cudaStream_t stream, const spmm24_problem* problems, int count,
                                             unsigned flags) {
-    return spmm24::launch_grouped_impl(stream, problems, count, flags);
+    return spmm24::launch_grouped_impl(stream, problems, count, flags, false);
+}
+
+extern "C" cudaError_t spmm24_launch_grouped_fp8(cudaStream_t stream, const spmm24_problem* problems, int count,
+                                                unsigned flags) {
+    return spmm24::launch_grouped_impl(stream, problems, count, flags, true);
 }
 
 extern "C" cudaError_t spmm24_launch_fused(cudaStream_t stream, const void* compressed_a, const void* b_packed,

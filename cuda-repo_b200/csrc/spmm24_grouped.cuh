@@ -16,6 +16,12 @@
 // cost = the tile's 128-K stages) and passes each CTA's list in the kernel
 // parameters, with one TMA descriptor triple per problem.
 //
+// Instantiations: the plain 16-bit SpMM (C = A * B rounded, fp16 or bf16,
+// with an optional fused all-gather); EPI, each problem with its own
+// epilogue (alpha, bias, activation, residual, packed-B output); FP8, the
+// fp8 operand formats of spmm24_launch_fp8 (kind::f8f6f4, stages of 256 K)
+// with the general epilogue (alpha carries the dequantisation scale).
+//
 // Roles (192 threads): warp 0 TMA producer (lane 0), warp 1 TMEM allocator
 // and MMA issuer, warps 2-5 epilogue (TMEM -> registers -> C).  Every wait
 // is bounded (kWaitLimitNs); a wait that gives up records a status bit and
@@ -32,17 +38,15 @@ constexpr int kGroupTileN = 32;       // N <= 32: columns of B past N are zero-f
 constexpr int kGroupStages = 8;
 
 struct GroupProblem {
-    uint16_t* C;       // row-major M x N, fp16 or bf16
+    uint16_t* C;       // M x N, fp16 or bf16, row-major (or packed-B with epi.packed)
     int M, N, K;
-    int groups;        // K / 64
-    int stages_total;  // ceil(groups / 2): 128-K stages per tile
-    // Fused all-gather of an M-shard (gather_n > 0): output row gm goes to row
-    // gather_row0 + gm of every rank's full row-major C (peer pointers reached
-    // over NVLink), or once through the full C's multicast address.
-    int gather_n;
-    int gather_row0;
-    uint16_t* gather_dst[kMaxGatherRanks];
-    uint16_t* gather_mc;
+    int groups;        // K / 64 (fp8: K / 128, the metadata groups)
+    int stages_total;  // ceil(groups / 2): stages per tile
+    // The problem's epilogue (EPI and FP8 instantiations) and its fused
+    // all-gather (every instantiation; epi.gather_n > 0): output row gm goes
+    // to row gather_row0 + gm of every rank's full row-major C, or once
+    // through the full C's multicast address.
+    Epilogue epi;
 };
 
 struct GroupParams {
@@ -53,6 +57,7 @@ struct GroupParams {
     int n_problems;
     int weights_static;
     int bf16;
+    uint32_t mma_fmt;  // fp8: operand-format bits of the instruction descriptor
     // CTA c processes sched[sched_off[c] .. sched_off[c + 1]); an entry is
     // (problem << 12) | m_tile.
     uint16_t sched_off[kGroupMaxCtas + 1];
@@ -60,9 +65,9 @@ struct GroupParams {
     SPMM24_TRACE_FIELD
 };
 
-template <int STAGES>
-struct GroupCfg : Cfg<kGroupTileN, STAGES, 2> {
-    using B_ = Cfg<kGroupTileN, STAGES, 2>;
+template <int STAGES, bool FP8 = false>
+struct GroupCfg : Cfg<kGroupTileN, STAGES, 2, FP8> {
+    using B_ = Cfg<kGroupTileN, STAGES, 2, FP8>;
     static constexpr int BAR_OFFSET = B_::RING_BYTES;
     static constexpr int NUM_BARS = 2 * STAGES + 4;  // full, empty, acc_full[2], acc_empty[2]
     static constexpr int HOLDER_OFFSET = BAR_OFFSET + NUM_BARS * 8;
@@ -104,9 +109,10 @@ __device__ __forceinline__ void group_store_row(uint16_t* out, uint16_t* mc, int
     }
 }
 
-template <int STAGES>
+template <int STAGES, bool EPI = false, bool FP8 = false>
 __global__ void __launch_bounds__(kThreads, 1) spmm24_grouped_kernel(const __grid_constant__ GroupParams p) {
-    using C_ = GroupCfg<STAGES>;
+    static_assert(EPI || !FP8, "the fp8 grouped kernel always runs the general epilogue");
+    using C_ = GroupCfg<STAGES, FP8>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + C_::BAR_OFFSET);
@@ -205,7 +211,7 @@ __global__ void __launch_bounds__(kThreads, 1) spmm24_grouped_kernel(const __gri
     if (warp == 1) {
         // ------------------------------------------------------ MMA issuer
         const uint32_t smem_base = ptx::smem_u32(smem);
-        const uint32_t fmt = p.bf16 ? kIdescBf16 : 0u;
+        const uint32_t fmt = FP8 ? p.mma_fmt : p.bf16 ? kIdescBf16 : 0u;
         int it = 0;
         bool ok = true;
         for (int j = 0; t_begin + j < t_end && ok; ++j) {
@@ -232,8 +238,14 @@ __global__ void __launch_bounds__(kThreads, 1) spmm24_grouped_kernel(const __gri
                 ptx::tc_fence_after();
                 if (2 * s_in + 1 >= groups) patch_tail_metadata<C_>(smem + s * C_::STAGE_BYTES, lane);
                 if (lane == 0) {
-                    mma_stage<C_, kGroupTileN>(smem_base + s * C_::STAGE_BYTES, tmem_base + C_::META_COL + 4 * s,
-                                               tmem_base + (uint32_t)(b * kGroupTileN), accumulate, fmt);
+                    const uint32_t meta_col = tmem_base + C_::META_COL + C_::META_STRIDE * s;
+                    const uint32_t d_tmem = tmem_base + (uint32_t)(b * kGroupTileN);
+                    if constexpr (FP8)
+                        mma_stage_fp8<C_, kGroupTileN>(smem_base + s * C_::STAGE_BYTES, meta_col, d_tmem, accumulate,
+                                                       fmt);
+                    else
+                        mma_stage<C_, kGroupTileN>(smem_base + s * C_::STAGE_BYTES, meta_col, d_tmem, accumulate,
+                                                   fmt);
                     ptx::tc_commit(&empty[s]);
                 }
                 __syncwarp();
@@ -280,13 +292,28 @@ __global__ void __launch_bounds__(kThreads, 1) spmm24_grouped_kernel(const __gri
             const int gm = m_tile * kTileM + row;
             const GroupProblem& q = p.prob[pi];
             if (gm < q.M) {
-                if (q.gather_n) {  // destinations are 16-byte aligned (checked by the host)
-                    const size_t off = (size_t)(q.gather_row0 + gm) * N;
-                    if (q.gather_mc && N % 8 == 0) {
-                        group_store_row(nullptr, q.gather_mc + off, N, v, p.bf16, true);
+                if constexpr (EPI) {
+                    // alpha, bias, activation, residual, rounding and the store
+                    // (row-major, packed-B or gathered), 8 columns at a time
+                    const bool vec = (N % 8 == 0) && ((reinterpret_cast<uintptr_t>(q.C) & 15u) == 0) &&
+                                     ((reinterpret_cast<uintptr_t>(q.epi.residual) & 15u) == 0);
+                    const bool plain = epilogue_is_plain(q.epi);
+#pragma unroll
+                    for (int c = 0; c < 32; c += 8) {
+                        if (c < N) {
+                            float y[8];
+#pragma unroll
+                            for (int e = 0; e < 8; ++e) y[e] = __uint_as_float(v[c + e]);
+                            epilogue_store8(q.C, y, q.epi, gm, c, q.M, N, vec, plain);
+                        }
+                    }
+                } else if (q.epi.gather_n) {  // destinations are 16-byte aligned (checked by the host)
+                    const size_t off = (size_t)(q.epi.gather_row0 + gm) * N;
+                    if (q.epi.gather_mc && N % 8 == 0) {
+                        group_store_row(nullptr, q.epi.gather_mc + off, N, v, p.bf16, true);
                     } else {
-                        for (int d = 0; d < q.gather_n; ++d)
-                            group_store_row(q.gather_dst[d] + off, nullptr, N, v, p.bf16, N % 8 == 0);
+                        for (int d = 0; d < q.epi.gather_n; ++d)
+                            group_store_row(q.epi.gather_dst[d] + off, nullptr, N, v, p.bf16, N % 8 == 0);
                     }
                 } else {
                     group_store_row(q.C + (size_t)gm * N, nullptr, N, v, p.bf16,

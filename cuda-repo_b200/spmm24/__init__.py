@@ -216,27 +216,31 @@ class Problem(ctypes.Structure):
     """spmm24_problem (include/spmm24/SpMM_API.h)."""
     _fields_ = [("compressed_a", ctypes.c_void_p), ("b_packed", ctypes.c_void_p), ("metadata", ctypes.c_void_p),
                 ("c", ctypes.c_void_p), ("M", ctypes.c_int), ("N", ctypes.c_int), ("K", ctypes.c_int),
-                ("gather", ctypes.c_void_p)]
+                ("gather", ctypes.c_void_p), ("epilogue", ctypes.c_void_p)]
 
 
 _lib.spmm24_launch_grouped.argtypes = [_vp, ctypes.POINTER(Problem), ctypes.c_int, ctypes.c_uint]
 _lib.spmm24_launch_grouped.restype = ctypes.c_int
+_lib.spmm24_launch_grouped_fp8.argtypes = [_vp, ctypes.POINTER(Problem), ctypes.c_int, ctypes.c_uint]
+_lib.spmm24_launch_grouped_fp8.restype = ctypes.c_int
 
 
 def problem_array(problems):
     """A ctypes array of spmm24_problem from (compressed_a, b_packed, metadata,
-    c, M, N, K[, gather]) tuples (tensors or int addresses; gather: a Gather
-    structure, kept alive by the returned array)."""
+    c, M, N, K[, gather[, epilogue]]) tuples (tensors or int addresses;
+    gather: a Gather structure, epilogue: an Epilogue structure, either may
+    be None; both kept alive by the returned array)."""
     arr = (Problem * len(problems))()
     keep = []
     for i, t in enumerate(problems):
         a, b, e, c, M, N, K = t[:7]
         g = t[7] if len(t) > 7 else None
-        if g is not None:
-            keep.append(g)
+        ep = t[8] if len(t) > 8 else None
+        keep += [x for x in (g, ep) if x is not None]
         arr[i] = Problem(_ptr(a), _ptr(b), _ptr(e), _ptr(c), M, N, K,
-                         ctypes.addressof(g) if g is not None else None)
-    arr._gathers = keep
+                         ctypes.addressof(g) if g is not None else None,
+                         ctypes.addressof(ep) if ep is not None else None)
+    arr._keep = keep
     return arr
 
 
@@ -254,13 +258,14 @@ def make_gather(c_full_ptrs, row_offset: int, m_full: int, c_multicast=None) -> 
     return g
 
 
-def launch_grouped(stream, problems, flags: int = 0) -> int:
-    """spmm24_launch_grouped: several independent N <= 32 SpMMs in one
-    persistent launch.  `problems`: a list of (compressed_a, b_packed,
-    metadata, c, M, N, K) tuples, or an array from problem_array().  Returns
-    the cudaError_t code."""
+def launch_grouped(stream, problems, flags: int = 0, fp8: bool = False) -> int:
+    """spmm24_launch_grouped (fp8: spmm24_launch_grouped_fp8): several
+    independent N <= 32 SpMMs in one persistent launch.  `problems`: a list
+    of problem_array() tuples, or such an array.  Returns the cudaError_t
+    code."""
     arr = problems if isinstance(problems, ctypes.Array) else problem_array(problems)
-    return _lib.spmm24_launch_grouped(_stream_handle(stream), arr, len(arr), flags)
+    fn = _lib.spmm24_launch_grouped_fp8 if fp8 else _lib.spmm24_launch_grouped
+    return fn(_stream_handle(stream), arr, len(arr), flags)
 
 
 def SpMM_N2M4_Launch(stream, Compressed_A, B, metadata, C, M_Global: int, N_Global: int, K_Global: int,

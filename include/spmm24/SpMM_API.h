@@ -99,8 +99,13 @@ cudaError_t spmm24_launch_ex(cudaStream_t stream, const void* compressed_a, cons
  * GPUs of a node, and its output rows go straight into row
  * gather->row_offset + m of every rank's full C (as for
  * spmm24_launch_gather; c may then be NULL); complete on the peers after
- * spmm24_gather_barrier on every rank.  spmm24_gather is declared below. */
+ * spmm24_gather_barrier on every rank.
+ * epilogue (optional): the problem's own fused epilogue, as for
+ * spmm24_launch_fused (alpha, bias, activation, residual, packed-B output;
+ * not packed with a gather).  spmm24_gather and spmm24_epilogue are
+ * declared below. */
 struct spmm24_gather;
+struct spmm24_epilogue;
 typedef struct spmm24_problem {
     const void* compressed_a;
     const void* b_packed;
@@ -108,8 +113,17 @@ typedef struct spmm24_problem {
     void* c;
     int M, N, K;
     const struct spmm24_gather* gather;
+    const struct spmm24_epilogue* epilogue;
 } spmm24_problem;
 cudaError_t spmm24_launch_grouped(cudaStream_t stream, const spmm24_problem* problems, int count, unsigned flags);
+/* The same for fp8 operands in spmm24_launch_fp8's formats (values,
+ * N x K row-major B, fp8 metadata; K % 128 == 0): compressed_a, b_packed
+ * and metadata point at those, C is fp16 (bf16 with SPMM24_BF16), and each
+ * problem's epilogue alpha carries its dequantisation scale (no epilogue:
+ * alpha 1).  flags additionally take SPMM24_FP8_A_E5M2 / SPMM24_FP8_B_E5M2
+ * (for every problem of the launch). */
+cudaError_t spmm24_launch_grouped_fp8(cudaStream_t stream, const spmm24_problem* problems, int count,
+                                      unsigned flags);
 
 /* Epilogue of spmm24_launch_fused (no counterpart in the reference, whose
  * epilogue only rounds to fp16, src/LoadAndStore.cuh:385-429).  Applied

@@ -195,3 +195,108 @@ def test_grouped_cuda_graph(cuda_device):
     torch.cuda.synchronize(cuda_device)
     for p, b in zip(probs, bufs):
         assert within_tolerance(compare(_bits(b["C"]), oracle_c(p)))
+
+
+def test_grouped_epilogues_match_fused_launches(cuda_device):
+    """Each problem of a group with its own epilogue (bias + SiLU, alpha +
+    GELU, a residual, a packed-B output, none): bit for bit the results of
+    spmm24_launch_fused with split_k = 1 (the same accumulator, the same
+    epilogue code), in fp16 and bf16."""
+    import torch
+
+    import spmm24
+
+    dev = cuda_device
+    cases = [((512, 16, 1024), dict(bias=True, act=spmm24.ACT_SILU)),
+             ((256, 32, 512), dict(alpha=0.5, act=spmm24.ACT_GELU)),
+             ((384, 24, 704), dict(residual=True, bias=True, act=spmm24.ACT_RELU)),
+             ((256, 12, 256), dict(packed=True, alpha=-0.25)),
+             ((144, 8, 320), dict()),
+             ((1024, 1, 512), dict(bias=True))]
+    for bf16 in (False, True):
+        dt = torch.bfloat16 if bf16 else torch.float16
+        flags = spmm24.BF16 if bf16 else 0
+        probs, refs, outs, keep = [], [], [], []
+        for i, ((M, N, K), kw) in enumerate(cases):
+            p = make_problem(M, N, K, seed=17 * i + M, a_scale=0.05, b_dist="normal")
+            b = _upload(torch, p, dev)
+            strips = (N + 7) // 8
+            size = strips * 8 * M if kw.get("packed") else M * N
+            bias = torch.randn(M, device=dev).to(dt) if kw.get("bias") else None
+            res = torch.randn(size, device=dev).to(dt) if kw.get("residual") else None
+            epi = spmm24.Epilogue(bias.data_ptr() if bias is not None else None,
+                                  res.data_ptr() if res is not None else None, kw.get("alpha", 1.0),
+                                  kw.get("act", spmm24.ACT_NONE),
+                                  spmm24.OUT_PACKED_B if kw.get("packed") else spmm24.OUT_ROW_MAJOR)
+            c_g = torch.full((size,), -1, dtype=torch.int16, device=dev)
+            c_r = torch.full((size,), -1, dtype=torch.int16, device=dev)
+            rc = spmm24.launch_fused(None, b["A"], b["B"], b["E"], c_r, M, N, K, 1, flags, bias=bias, residual=res,
+                                     alpha=kw.get("alpha", 1.0), activation=kw.get("act", spmm24.ACT_NONE),
+                                     out_layout=spmm24.OUT_PACKED_B if kw.get("packed") else spmm24.OUT_ROW_MAJOR)
+            assert rc == 0, spmm24._lib.spmm24_last_error().decode()
+            probs.append((b["A"], b["B"], b["E"], c_g, M, N, K, None, epi))
+            refs.append(c_r)
+            outs.append(c_g)
+            keep += [b, bias, res]
+        assert spmm24.launch_grouped(None, probs, flags) == 0, spmm24._lib.spmm24_last_error().decode()
+        torch.cuda.synchronize(dev)
+        for (shape, kw), r, g in zip(cases, refs, outs):
+            assert torch.equal(r, g), (bf16, shape, kw)
+        assert spmm24.device_status(0) == 0
+
+
+def test_grouped_fp8_matches_fp8_launches(cuda_device):
+    """spmm24_launch_grouped_fp8: E4M3 and E5M2 operands, alpha per problem,
+    bias / activation / residual / packed output: bit for bit the results of
+    spmm24_launch_fp8 with split_k = 1; one problem also against the oracle
+    (fp8 decode, fp32 GEMM; bound of tests/test_gpu_fp8.py)."""
+    import torch
+
+    import oracle as O
+    import spmm24
+    from test_gpu_fp8 import _problem
+
+    dev = cuda_device
+    cases = [((512, 16, 1024), dict(alpha=0.02)),
+             ((256, 32, 512), dict(alpha=0.5, bias=True, act=spmm24.ACT_SILU)),
+             ((384, 24, 1152), dict(residual=True, alpha=1.0)),
+             ((256, 8, 256), dict(packed=True, alpha=2.0)),
+             ((1024, 1, 2048), dict(alpha=0.125))]
+    for fmt_a, fmt_b in ((0, 0), (1, 0), (0, 1)):
+        flags = (spmm24.FP8_A_E5M2 if fmt_a else 0) | (spmm24.FP8_B_E5M2 if fmt_b else 0)
+        probs, refs, outs, keep, accs = [], [], [], [], []
+        for i, ((M, N, K), kw) in enumerate(cases):
+            vals, meta, b_bits, acc, S = _problem(M, N, K, fmt_a, fmt_b, seed=31 * i + M + fmt_a + 2 * fmt_b)
+            A = torch.from_numpy(np.ascontiguousarray(vals)).to(dev)
+            E = torch.from_numpy(np.ascontiguousarray(meta)).to(dev)
+            B = torch.from_numpy(np.ascontiguousarray(b_bits)).to(dev)
+            strips = (N + 7) // 8
+            size = strips * 8 * M if kw.get("packed") else M * N
+            bias = torch.randn(M, device=dev).half() if kw.get("bias") else None
+            res = torch.randn(size, device=dev).half() if kw.get("residual") else None
+            act = kw.get("act", spmm24.ACT_NONE)
+            layout = spmm24.OUT_PACKED_B if kw.get("packed") else spmm24.OUT_ROW_MAJOR
+            epi = spmm24.Epilogue(bias.data_ptr() if bias is not None else None,
+                                  res.data_ptr() if res is not None else None, kw["alpha"], act, layout)
+            c_g = torch.full((size,), -1, dtype=torch.int16, device=dev)
+            c_r = torch.full((size,), -1, dtype=torch.int16, device=dev)
+            rc = spmm24.launch_fp8(None, A, B, E, c_r, M, N, K, 1, flags, bias=bias, residual=res,
+                                   alpha=kw["alpha"], activation=act, out_layout=layout)
+            assert rc == 0, spmm24._lib.spmm24_last_error().decode()
+            probs.append((A, B, E, c_g, M, N, K, None, epi))
+            refs.append(c_r)
+            outs.append(c_g)
+            keep += [A, B, E, bias, res]
+            accs.append((acc, S))
+        assert spmm24.launch_grouped(None, probs, flags, fp8=True) == 0, spmm24._lib.spmm24_last_error().decode()
+        torch.cuda.synchronize(dev)
+        for (shape, kw), r, g in zip(cases, refs, outs):
+            assert torch.equal(r, g), (fmt_a, fmt_b, shape, kw)
+        # the first problem against the oracle: alpha * acc rounded to fp16
+        (M, N, K), kw = cases[0]
+        acc, S = accs[0]
+        got = outs[0].cpu().numpy().view(np.uint16).view(np.float16).astype(np.float64).reshape(M, N)
+        ref = (kw["alpha"] * acc).astype(np.float32).astype(np.float16).astype(np.float64)
+        tol = 2.0 ** -10 * np.abs(ref) + 1.2 * kw["alpha"] * 2.0 ** -12 * S + 1e-6
+        assert np.all(np.abs(got - ref) <= tol)
+        assert spmm24.device_status(0) == 0
