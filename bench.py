@@ -352,14 +352,15 @@ def run_ours(args, rank, world, local_rank):
     # A step: every SpMM of the workload.  "grouped" issues them as one
     # spmm24_launch_grouped (one persistent kernel for all the step's N <= 32
     # layers); "chain" issues one spmm24_launch per SpMM.
-    grouped = args.launch == "grouped" and not fp8 and args.epilogue == "none" and all(c["N"] <= 32 for c in calls)
+    grouped = args.launch == "grouped" and all(c["N"] <= 32 for c in calls)
     group_flags = flags & (spmm24.STATIC_WEIGHTS | spmm24.BF16)
+    group_fn = spmm24._lib.spmm24_launch_grouped_fp8 if fp8 else spmm24._lib.spmm24_launch_grouped
     # M-sharded decode on N > 1 GPUs: every rank's output rows go straight into
     # every rank's full C (the grouped kernel's epilogue stores over NVLink to
     # the peers' buffers, opened with CUDA IPC), then one cross-GPU barrier;
     # both inside the timed step.  Two full-C sets, for the e2e loop's two
     # buffer sets.
-    gather_mode = grouped and shard and world > 1
+    gather_mode = grouped and shard and world > 1 and not (fp8 or bf16) and args.epilogue == "none"
     full_sets, flag_ptrs, imported, epoch = [], None, [], [0]
     if gather_mode:
         full_elems = sum(c["M_full"] * c["N"] for c in calls)
@@ -390,7 +391,7 @@ def run_ours(args, rank, world, local_rank):
 
     def group_array(cs, k):
         gs = gathers_for(k) if gather_mode else [None] * len(cs)
-        return spmm24.problem_array([(c["A"], c["B"], c["E"], c["C"], c["M"], c["N"], c["K"], g)
+        return spmm24.problem_array([(c["A"], c["B"], c["E"], c["C"], c["M"], c["N"], c["K"], g, c.get("epi"))
                                      for c, g in zip(cs, gs)])
 
     group_arrays = {}
@@ -399,7 +400,7 @@ def run_ours(args, rank, world, local_rank):
         hs = h_stream if hs is None else hs
         if use_group:
             arr = group_arrays.setdefault((id(cs), k), group_array(cs, k))
-            rc = spmm24._lib.spmm24_launch_grouped(hs, arr, len(arr), group_flags)
+            rc = group_fn(hs, arr, len(arr), group_flags)
             if rc != 0:
                 raise RuntimeError(f"spmm24_launch_grouped failed: {rc} {spmm24._lib.spmm24_last_error().decode()}")
         elif gather_mode:  # the chain: one spmm24_launch_gather per SpMM
@@ -467,7 +468,8 @@ def run_ours(args, rank, world, local_rank):
     # The same single shapes through the grouped kernel (a group of one).
     per_call_grouped = None
     if grouped and not gather_mode:
-        singles = [spmm24.problem_array([(c["A"], c["B"], c["E"], c["C"], c["M"], c["N"], c["K"])]) for c in calls]
+        singles = [spmm24.problem_array([(c["A"], c["B"], c["E"], c["C"], c["M"], c["N"], c["K"], None, c.get("epi"))])
+                   for c in calls]
         evg = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                for _ in range(reps * len(calls))]
         torch.cuda.synchronize(dev)
@@ -476,7 +478,7 @@ def run_ours(args, rank, world, local_rank):
         for _ in range(reps):
             for arr in singles:
                 evg[i][0].record(stream)
-                spmm24._lib.spmm24_launch_grouped(h_stream, arr, 1, group_flags)
+                group_fn(h_stream, arr, 1, group_flags)
                 evg[i][1].record(stream)
                 i += 1
         torch.cuda.synchronize(dev)
@@ -512,7 +514,7 @@ def run_ours(args, rank, world, local_rank):
         host["spmm24_launch_ex_us_with_ctypes"] = tot
         if grouped and not gather_mode:
             arr_all = group_array(calls, 0)
-            lg = spmm24._lib.spmm24_launch_grouped
+            lg = group_fn
             net, tot = host_us(lambda: lg(h_stream, arr_all, len(arr_all), group_flags),
                                lambda: lg(h_stream, arr_all, len(arr_all), 1 << 20))
             host["spmm24_launch_grouped_12_us"] = net
