@@ -120,7 +120,7 @@ bool encode(CUtensorMap* m, int rank, const void* base, const cuuint64_t* dims, 
 // Picker overrides set by spmm24_set_tuning (tests and tuning sweeps); the
 // library reads no environment variables.
 struct Tuning {
-    std::atomic<int> pair{-1}, pair2{-1}, pair_split{0}, tile_n{0}, deep_ring{0};
+    std::atomic<int> pair{-1}, pair2{-1}, pair_split{0}, tile_n{0}, deep_ring{0}, group_split{0};
 };
 Tuning g_tune;
 
@@ -752,7 +752,9 @@ struct GroupCache {
     unsigned flags = 0;
     int sms = 0;
     int n_ctas = 0;
-    bool epi = false;  // some problem has a non-plain epilogue
+    bool epi = false;    // some problem has a non-plain epilogue
+    bool split = false;  // tiles split over CTA pairs (n_ctas then counts pairs)
+    int tuned = 0;       // the group_split tuning the schedule was built under
     GroupParams params;
 };
 thread_local GroupCache* t_group_cache = nullptr;
@@ -794,7 +796,7 @@ cudaError_t encode_group_maps(const spmm24_problem& q, bool fp8, GroupParams& gp
 }
 
 cudaError_t build_group(const spmm24_problem* probs, int count, unsigned flags, bool fp8, int sms, GroupParams& gp,
-                        int& n_ctas, bool& any_epi) {
+                        int& n_ctas, bool& any_epi, bool& split) {
     std::memset(&gp, 0, sizeof(gp));
     struct Tile {
         int cost, prob, m_tile;
@@ -826,21 +828,45 @@ cudaError_t build_group(const spmm24_problem* probs, int count, unsigned flags, 
         for (int m = 0; m < mt; ++m) tiles.push_back({st + 1, i, m});
         if ((e = encode_group_maps(q, fp8, gp, i)) != cudaSuccess) return e;
     }
-    std::stable_sort(tiles.begin(), tiles.end(), [](const Tile& a, const Tile& b) { return a.cost > b.cost; });
-    n_ctas = (int)std::min<size_t>(std::min(sms, kGroupMaxCtas), tiles.size());
-    std::vector<long long> load(n_ctas, 0);
-    std::vector<std::vector<uint16_t>> lists(n_ctas);
-    for (const Tile& t : tiles) {
-        int best = 0;  // least loaded CTA, lowest index on ties (a linear scan: <= 160 CTAs)
-        for (int c = 1; c < n_ctas; ++c)
-            if (load[c] < load[best]) best = c;
-        load[best] += t.cost;
-        lists[best].push_back((uint16_t)((t.prob << 12) | t.m_tile));
-    }
+    // Two schedules: whole tiles on one CTA per SM, or (K split) tiles on CTA
+    // pairs with half the stages each; the split is taken when it shortens
+    // the busiest unit's work by more than a tenth (its ring is one or two
+    // stages shallower and each tile pays a partial-sum exchange), or when
+    // the caller's tuning asks for it.
+    struct Sched {
+        int units = 0;
+        long long makespan = 0;
+        std::vector<std::vector<uint16_t>> lists;
+    };
+    auto lpt = [&](int max_units, bool halve) {
+        Sched sc;
+        std::vector<Tile> ts = tiles;
+        // cost = stages + 1 (the epilogue); halved: ceil(stages / 2) + 1
+        for (Tile& t : ts) t.cost = halve ? t.cost / 2 + 1 : t.cost;
+        std::stable_sort(ts.begin(), ts.end(), [](const Tile& a, const Tile& b) { return a.cost > b.cost; });
+        sc.units = (int)std::min<size_t>((size_t)max_units, ts.size());
+        std::vector<long long> load(sc.units, 0);
+        sc.lists.assign(sc.units, {});
+        for (const Tile& t : ts) {
+            int best = 0;  // least loaded unit, lowest index on ties (a linear scan: <= 160 units)
+            for (int c = 1; c < sc.units; ++c)
+                if (load[c] < load[best]) best = c;
+            load[best] += t.cost;
+            sc.lists[best].push_back((uint16_t)((t.prob << 12) | t.m_tile));
+        }
+        for (long long l : load) sc.makespan = std::max(sc.makespan, l);
+        return sc;
+    };
+    const int cap = std::min(sms, kGroupMaxCtas);
+    Sched whole = lpt(cap, false), halves = lpt(cap / 2, true);
+    const int forced = g_tune.group_split.load(std::memory_order_relaxed);
+    split = forced == 2 || (forced == 0 && cap >= 2 && 10 * halves.makespan < 9 * whole.makespan);
+    Sched& sc = split ? halves : whole;
+    n_ctas = sc.units;  // CTAs, or CTA pairs with the split
     int off = 0;
     for (int c = 0; c < n_ctas; ++c) {
         gp.sched_off[c] = (uint16_t)off;
-        for (uint16_t e : lists[c]) gp.sched[off++] = e;
+        for (uint16_t e : sc.lists[c]) gp.sched[off++] = e;
     }
     gp.sched_off[n_ctas] = (uint16_t)off;
     gp.n_problems = count;
@@ -850,22 +876,31 @@ cudaError_t build_group(const spmm24_problem* probs, int count, unsigned flags, 
     return cudaSuccess;
 }
 
-template <bool EPI, bool FP8>
+template <bool EPI, bool FP8, int SPLIT>
 cudaError_t launch_group_kernel(cudaStream_t stream, int dev, const GroupCache& gc, unsigned flags) {
-    using GC = GroupCfg<kGroupStages, FP8>;
-    auto kern = spmm24_grouped_kernel<kGroupStages, EPI, FP8>;
-    cudaError_t e = prepare(kern, GC::SMEM_ALLOC, dev, 80 + (EPI ? 1 : 0) + (FP8 ? 2 : 0));
+    constexpr int ST = SPLIT > 1 ? (FP8 ? kGroupSplitStagesFp8 : kGroupSplitStages) : kGroupStages;
+    using GC = GroupCfg<ST, FP8, SPLIT>;
+    auto kern = spmm24_grouped_kernel<ST, EPI, FP8, SPLIT>;
+    cudaError_t e = prepare(kern, GC::SMEM_ALLOC, dev, 80 + (EPI ? 1 : 0) + (FP8 ? 2 : 0) + (SPLIT > 1 ? 4 : 0));
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)gc.n_ctas, 1, 1);
+    cfg.gridDim = dim3((unsigned)(gc.n_ctas * SPLIT), 1, 1);
     cfg.blockDim = dim3((unsigned)kThreads, 1, 1);
     cfg.dynamicSmemBytes = GC::SMEM_ALLOC;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = (flags & SPMM24_NO_PDL) ? 0 : 1;
+    int n = 1;
+    if (SPLIT > 1) {
+        attr[1].id = cudaLaunchAttributeClusterDimension;
+        attr[1].val.clusterDim.x = SPLIT;
+        attr[1].val.clusterDim.y = 1;
+        attr[1].val.clusterDim.z = 1;
+        n = 2;
+    }
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = n;
     return cudaLaunchKernelEx(&cfg, kern, gc.params);
 }
 
@@ -927,24 +962,32 @@ cudaError_t launch_grouped_impl(cudaStream_t stream, const spmm24_problem* probs
         if (probs[i].epilogue) ep = *probs[i].epilogue;
         put(key, &ep, sizeof(ep));
     }
-    const bool hit = gc.n_ctas > 0 && gc.flags == flags && gc.sms == sms && gc.key == key;
+    const int tuned = g_tune.group_split.load(std::memory_order_relaxed);
+    const bool hit = gc.n_ctas > 0 && gc.flags == flags && gc.sms == sms && gc.tuned == tuned && gc.key == key;
     if (!hit) {
         gc.n_ctas = 0;
         int n = 0;
-        bool any_epi = false;
-        if ((e = build_group(probs, count, flags, fp8, sms, gc.params, n, any_epi)) != cudaSuccess) return e;
+        bool any_epi = false, split = false;
+        if ((e = build_group(probs, count, flags, fp8, sms, gc.params, n, any_epi, split)) != cudaSuccess) return e;
         gc.key = key;
         gc.flags = flags;
         gc.sms = sms;
         gc.n_ctas = n;
         gc.epi = any_epi;
+        gc.split = split;
+        gc.tuned = tuned;
     }
 #ifdef SPMM24_TRACE
     gc.params.trace_base = g_trace_next.fetch_add((long long)gc.n_ctas);
 #endif
-    if (fp8) return launch_group_kernel<true, true>(stream, dev, gc, flags);
-    if (gc.epi) return launch_group_kernel<true, false>(stream, dev, gc, flags);
-    return launch_group_kernel<false, false>(stream, dev, gc, flags);
+    if (gc.split) {
+        if (fp8) return launch_group_kernel<true, true, 2>(stream, dev, gc, flags);
+        if (gc.epi) return launch_group_kernel<true, false, 2>(stream, dev, gc, flags);
+        return launch_group_kernel<false, false, 2>(stream, dev, gc, flags);
+    }
+    if (fp8) return launch_group_kernel<true, true, 1>(stream, dev, gc, flags);
+    if (gc.epi) return launch_group_kernel<true, false, 1>(stream, dev, gc, flags);
+    return launch_group_kernel<false, false, 1>(stream, dev, gc, flags);
 }
 
 // ------------------------------------------------ allocation-free variant
@@ -1282,13 +1325,13 @@ void fill_config(const Plan& pl, int stage_k, spmm24_config* out);
 
 extern "C" cudaError_t spmm24_set_tuning(const spmm24_tuning* t) {
     spmm24::clear_last_error();
-    spmm24_tuning v{-1, -1, 0, 0, 0};
+    spmm24_tuning v{-1, -1, 0, 0, 0, 0};
     if (t) {
         v = *t;
         const bool tn_ok = v.tile_n == 0 || v.tile_n == 16 || v.tile_n == 32 || v.tile_n == 64 || v.tile_n == 128 ||
                            v.tile_n == 256;
         if (v.pair < -1 || v.pair > 1 || v.pair2 < -1 || v.pair2 > 1 || v.pair_split < 0 || v.pair_split > 2 || !tn_ok ||
-            v.deep_ring < 0 || v.deep_ring > 1)
+            v.deep_ring < 0 || v.deep_ring > 1 || v.group_split < 0 || v.group_split > 2)
             return spmm24::record_invalid("tuning: a field is out of range");
     }
     spmm24::g_tune.pair.store(v.pair);
@@ -1296,6 +1339,7 @@ extern "C" cudaError_t spmm24_set_tuning(const spmm24_tuning* t) {
     spmm24::g_tune.pair_split.store(v.pair_split);
     spmm24::g_tune.tile_n.store(v.tile_n);
     spmm24::g_tune.deep_ring.store(v.deep_ring);
+    spmm24::g_tune.group_split.store(v.group_split);
     return cudaSuccess;
 }
 

@@ -36,6 +36,15 @@ constexpr int kGroupMaxTiles = 2048;  // schedule entries (128-row tiles) per la
 constexpr int kGroupMaxCtas = 160;
 constexpr int kGroupTileN = 32;       // N <= 32: columns of B past N are zero-filled by TMA, never fetched
 constexpr int kGroupStages = 8;
+// K split in two (SPLIT = 2, for groups with fewer tiles than SMs): a
+// cluster of two CTAs takes each tile, one half of its K stages each; the
+// second CTA pushes its fp32 partial (128 x 32) into a receive slot of the
+// first through distributed shared memory, which adds it before the
+// epilogue.  Two slots alternate, like the accumulators; the ring gives up
+// one (fp8: two) stage for them.
+constexpr int kGroupSplitStages = 7;
+constexpr int kGroupSplitStagesFp8 = 6;
+constexpr int kGroupRecvPitch = kGroupTileN + 4;  // floats per received row (16-byte reads free of bank conflicts)
 
 struct GroupProblem {
     uint16_t* C;       // M x N, fp16 or bf16, row-major (or packed-B with epi.packed)
@@ -58,18 +67,23 @@ struct GroupParams {
     int weights_static;
     int bf16;
     uint32_t mma_fmt;  // fp8: operand-format bits of the instruction descriptor
-    // CTA c processes sched[sched_off[c] .. sched_off[c + 1]); an entry is
-    // (problem << 12) | m_tile.
+    // CTA c (SPLIT = 2: cluster c) processes sched[sched_off[c] ..
+    // sched_off[c + 1]); an entry is (problem << 12) | m_tile.
     uint16_t sched_off[kGroupMaxCtas + 1];
     uint16_t sched[kGroupMaxTiles];
     SPMM24_TRACE_FIELD
 };
 
-template <int STAGES, bool FP8 = false>
+template <int STAGES, bool FP8 = false, int SPLIT = 1>
 struct GroupCfg : Cfg<kGroupTileN, STAGES, 2, FP8> {
     using B_ = Cfg<kGroupTileN, STAGES, 2, FP8>;
-    static constexpr int BAR_OFFSET = B_::RING_BYTES;
-    static constexpr int NUM_BARS = 2 * STAGES + 4;  // full, empty, acc_full[2], acc_empty[2]
+    static constexpr int RECV_OFFSET = B_::RING_BYTES;
+    static constexpr int RECV_SLOT_BYTES = kTileM * kGroupRecvPitch * 4;
+    static constexpr int RECV_BYTES = SPLIT > 1 ? 2 * RECV_SLOT_BYTES : 0;
+    static constexpr uint32_t PARTIAL_BYTES = (uint32_t)kTileM * kGroupTileN * 4;  // pushed per tile
+    static constexpr int BAR_OFFSET = RECV_OFFSET + RECV_BYTES;
+    // full, empty, acc_full[2], acc_empty[2], recv_full[2], slot_free[2], slot_read[2]
+    static constexpr int NUM_BARS = 2 * STAGES + 10;
     static constexpr int HOLDER_OFFSET = BAR_OFFSET + NUM_BARS * 8;
     static constexpr int SMEM_BYTES = HOLDER_OFFSET + 16;
     static constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;  // slack to align the base to 1024 B
@@ -109,22 +123,43 @@ __device__ __forceinline__ void group_store_row(uint16_t* out, uint16_t* mc, int
     }
 }
 
-template <int STAGES, bool EPI = false, bool FP8 = false>
+// This CTA's share [lo, hi) of a tile's `n` stages: all of them, or (K split)
+// the first ceil(n / 2) for cluster rank 0 and the rest for rank 1.
+template <int SPLIT>
+__device__ __forceinline__ void group_share(int n, int rank, int& lo, int& hi) {
+    if (SPLIT == 1) {
+        lo = 0;
+        hi = n;
+    } else {
+        const int h = (n + 1) / 2;
+        lo = rank ? h : 0;
+        hi = rank ? n : h;
+    }
+}
+
+template <int STAGES, bool EPI = false, bool FP8 = false, int SPLIT = 1>
 __global__ void __launch_bounds__(kThreads, 1) spmm24_grouped_kernel(const __grid_constant__ GroupParams p) {
     static_assert(EPI || !FP8, "the fp8 grouped kernel always runs the general epilogue");
-    using C_ = GroupCfg<STAGES, FP8>;
+    static_assert(SPLIT == 1 || SPLIT == 2, "K split in one or two");
+    using C_ = GroupCfg<STAGES, FP8, SPLIT>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + C_::BAR_OFFSET);
     uint64_t* empty = full + STAGES;
     uint64_t* acc_full = empty + STAGES;  // [2]
     uint64_t* acc_empty = acc_full + 2;   // [2]
+    uint64_t* recv_full = acc_empty + 2;  // [2] rank 0 of a split: the partner's partial of slot b has arrived
+    uint64_t* slot_free = recv_full + 2;  // [2] rank 1 of a split: rank 0 has read slot b
+    uint64_t* slot_read = slot_free + 2;  // [2] rank 0 of a split: each epilogue warp has read its rows of slot b
+    float* recv = reinterpret_cast<float*>(smem + C_::RECV_OFFSET);  // [2][128][kGroupRecvPitch]
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + C_::HOLDER_OFFSET);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int t_begin = p.sched_off[blockIdx.x];
-    const int t_end = p.sched_off[blockIdx.x + 1];
+    const int rank = SPLIT > 1 ? (int)(ptx::cluster_ctarank() & 1u) : 0;
+    const int unit = SPLIT > 1 ? (int)blockIdx.x / 2 : (int)blockIdx.x;
+    const int t_begin = p.sched_off[unit];
+    const int t_end = p.sched_off[unit + 1];
 
     if (threadIdx.x == 0) {
         SPMM24_STAMP(0);
@@ -135,7 +170,15 @@ __global__ void __launch_bounds__(kThreads, 1) spmm24_grouped_kernel(const __gri
         for (int b = 0; b < 2; ++b) {
             ptx::mbar_init(&acc_full[b], 1);
             ptx::mbar_init(&acc_empty[b], kEpiThreads / 32);  // one arrival per epilogue warp
+            ptx::mbar_init(&recv_full[b], 1);
+            ptx::mbar_init(&slot_free[b], 1);
+            ptx::mbar_init(&slot_read[b], kEpiThreads / 32);
         }
+        // Rank 0 of a split arms the receive barriers of its first two tiles
+        // now, before the partner can push (the cluster barrier below); the
+        // next arm of slot b follows the read of slot b.
+        if (SPLIT > 1 && rank == 0)
+            for (int b = 0; b < 2 && t_begin + b < t_end; ++b) ptx::mbar_arrive_expect_tx(&recv_full[b], C_::PARTIAL_BYTES);
         ptx::fence_mbarrier_init();
         for (int i = 0; i < p.n_problems; ++i) {
             ptx::prefetch_tmap(&p.tmA[i]);
@@ -144,6 +187,7 @@ __global__ void __launch_bounds__(kThreads, 1) spmm24_grouped_kernel(const __gri
         }
     }
     __syncthreads();
+    if (SPLIT > 1) ptx::cluster_sync();  // both CTAs' barriers are initialised (and armed)
     if (threadIdx.x == 0) ptx::grid_dep_launch();
 
     uint32_t tmem_base = 0;
@@ -155,9 +199,23 @@ __global__ void __launch_bounds__(kThreads, 1) spmm24_grouped_kernel(const __gri
         if (lane == 0) {
             const uint64_t pol_stream = ptx::policy_evict_first();  // A, E: read once
             const uint64_t pol_keep = ptx::policy_evict_last();     // B: re-read by every tile of its problem
+            // Walk position: tile t, stage s_in of this CTA's share [lo, hi).
+            auto first_of = [&](int t, int& s_in, int& hi) {
+                for (; t < t_end; ++t) {
+                    int pi, m_tile, lo;
+                    group_entry(p, t, pi, m_tile);
+                    group_share<SPLIT>(p.prob[pi].stages_total, rank, lo, hi);
+                    if (lo < hi) {
+                        s_in = lo;
+                        return t;
+                    }
+                }
+                return t;
+            };
             int pre = 0;
             if (p.weights_static) {  // the first stages' weights before the previous grid ends
-                int t = t_begin, s_in = 0;
+                int hi = 0, s_in = 0;
+                int t = first_of(t_begin, s_in, hi);
                 while (pre < STAGES && t < t_end) {
                     int pi, m_tile;
                     group_entry(p, t, pi, m_tile);
@@ -165,15 +223,13 @@ __global__ void __launch_bounds__(kThreads, 1) spmm24_grouped_kernel(const __gri
                     load_stage_weights<C_>(smem + pre * C_::STAGE_BYTES, &full[pre], &p.tmA[pi], &p.tmE[pi],
                                            m_tile * (kTileM / 16), 2 * s_in, pol_stream);
                     ++pre;
-                    if (++s_in == p.prob[pi].stages_total) {
-                        s_in = 0;
-                        ++t;
-                    }
+                    if (++s_in == hi) t = first_of(t + 1, s_in, hi);
                 }
             }
             ptx::grid_dep_wait();
             SPMM24_STAMP(1);
-            int t = t_begin, s_in = 0;
+            int hi = 0, s_in = 0;
+            int t = first_of(t_begin, s_in, hi);
             for (int it = 0; t < t_end; ++it) {
                 int pi, m_tile;
                 group_entry(p, t, pi, m_tile);
@@ -190,10 +246,7 @@ __global__ void __launch_bounds__(kThreads, 1) spmm24_grouped_kernel(const __gri
                                            pol_stream);
                 }
                 load_stage_acts<C_>(st, &full[s], &p.tmB[pi], 0, 2 * s_in, pol_keep);
-                if (++s_in == p.prob[pi].stages_total) {
-                    s_in = 0;
-                    ++t;
-                }
+                if (++s_in == hi) t = first_of(t + 1, s_in, hi);
             }
         }
         __syncwarp();
@@ -217,7 +270,8 @@ __global__ void __launch_bounds__(kThreads, 1) spmm24_grouped_kernel(const __gri
         for (int j = 0; t_begin + j < t_end && ok; ++j) {
             int pi, m_tile;
             group_entry(p, t_begin + j, pi, m_tile);
-            const int nst = p.prob[pi].stages_total;
+            int lo, hi;
+            group_share<SPLIT>(p.prob[pi].stages_total, rank, lo, hi);
             const int groups = p.prob[pi].groups;
             const int b = j & 1;
             if (j >= 2) {  // accumulator b still holds tile j - 2 until the epilogue has read it
@@ -228,7 +282,7 @@ __global__ void __launch_bounds__(kThreads, 1) spmm24_grouped_kernel(const __gri
                 ptx::tc_fence_after();
             }
             uint32_t accumulate = 0;
-            for (int s_in = 0; s_in < nst; ++s_in, ++it) {
+            for (int s_in = lo; s_in < hi; ++s_in, ++it) {
                 const int s = it % STAGES;
                 if (!ptx::mbar_wait_bounded(&full[s], (uint32_t)(it / STAGES) & 1u, kWaitLimitNs)) {
                     if (lane == 0) atomicOr(&g_spmm24_status, kStatusMmaTimeout);
@@ -271,20 +325,71 @@ __global__ void __launch_bounds__(kThreads, 1) spmm24_grouped_kernel(const __gri
             }
             ptx::tc_fence_after();
             const int N = p.prob[pi].N;
-            uint32_t v0[16], v1[16];
-            const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(b * kGroupTileN);
-            ptx::tmem_ld_32x32b_x16(taddr, v0);
-            if (N > 16) ptx::tmem_ld_32x32b_x16(taddr + 16, v1);
-            ptx::tmem_wait_ld();
+            int lo, hi;
+            group_share<SPLIT>(p.prob[pi].stages_total, rank, lo, hi);
             uint32_t v[32];
+            if (lo < hi) {
+                uint32_t v0[16], v1[16];
+                const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(b * kGroupTileN);
+                ptx::tmem_ld_32x32b_x16(taddr, v0);
+                if (N > 16) ptx::tmem_ld_32x32b_x16(taddr + 16, v1);
+                ptx::tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                v[i] = v0[i];
-                v[16 + i] = N > 16 ? v1[i] : 0u;
+                for (int i = 0; i < 16; ++i) {
+                    v[i] = v0[i];
+                    v[16 + i] = N > 16 ? v1[i] : 0u;
+                }
+            } else {  // a one-stage tile leaves rank 1 of a split without a share
+#pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] = 0u;
             }
             ptx::tc_fence_before();
             __syncwarp();
             if (lane == 0) ptx::mbar_arrive(&acc_empty[b]);
+            if constexpr (SPLIT > 1) {
+                float* slot = recv + (size_t)b * kTileM * kGroupRecvPitch;
+                if (rank == 1) {
+                    // push this row's partial into rank 0's slot b, once rank 0
+                    // has read what the slot held two tiles ago
+                    if (j >= 2 && !ptx::mbar_wait_bounded(&slot_free[b], (uint32_t)((j >> 1) - 1) & 1u, kWaitLimitNs)) {
+                        atomicOr(&g_spmm24_status, kStatusEpilogueTimeout);
+                        break;
+                    }
+                    const uint32_t dst = ptx::mapa_shared(ptx::smem_u32(slot + row * kGroupRecvPitch), 0u);
+                    const uint32_t bar = ptx::mapa_shared(ptx::smem_u32(&recv_full[b]), 0u);
+#pragma unroll
+                    for (int q = 0; q < kGroupTileN / 4; ++q)
+                        ptx::st_async_v4(dst + 16u * q, __uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
+                                         __uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3]), bar);
+                    continue;  // rank 0 finishes the tile
+                }
+                // rank 0: add the partner's partial (fixed order: own half of K first)
+                if (!ptx::mbar_wait_bounded(&recv_full[b], (uint32_t)(j >> 1) & 1u, kWaitLimitNs)) {
+                    atomicOr(&g_spmm24_status, kStatusEpilogueTimeout);
+                    break;
+                }
+                const float* r = slot + row * kGroupRecvPitch;
+#pragma unroll
+                for (int q = 0; q < kGroupTileN / 4; ++q) {
+                    const float4 x = *reinterpret_cast<const float4*>(r + 4 * q);
+                    v[4 * q] = __float_as_uint(__uint_as_float(v[4 * q]) + x.x);
+                    v[4 * q + 1] = __float_as_uint(__uint_as_float(v[4 * q + 1]) + x.y);
+                    v[4 * q + 2] = __float_as_uint(__uint_as_float(v[4 * q + 2]) + x.z);
+                    v[4 * q + 3] = __float_as_uint(__uint_as_float(v[4 * q + 3]) + x.w);
+                }
+                __syncwarp();
+                if (lane == 0) ptx::mbar_arrive(&slot_read[b]);  // this warp's rows of slot b are read
+                if (threadIdx.x == 64 && t_begin + j + 2 < t_end) {
+                    // once every warp has read slot b: arm it for its next tile
+                    // and tell the partner it may push into it
+                    if (ptx::mbar_wait_bounded(&slot_read[b], (uint32_t)(j >> 1) & 1u, kWaitLimitNs)) {
+                        ptx::mbar_arrive_expect_tx(&recv_full[b], C_::PARTIAL_BYTES);
+                        ptx::mbar_arrive_cluster(ptx::mapa_shared(ptx::smem_u32(&slot_free[b]), 1u));
+                    } else {
+                        atomicOr(&g_spmm24_status, kStatusEpilogueTimeout);
+                    }
+                }
+            }
             if (!waited) {  // C may be read or written by the previous grid
                 ptx::grid_dep_wait();
                 waited = true;
@@ -326,6 +431,7 @@ __global__ void __launch_bounds__(kThreads, 1) spmm24_grouped_kernel(const __gri
     if (threadIdx.x == 64) SPMM24_STAMP(5);
     ptx::tc_fence_before();
     __syncthreads();
+    if (SPLIT > 1) ptx::cluster_sync();  // no CTA leaves while its partner may still reach its shared memory
     if (warp == 1) {
         ptx::tc_fence_after();
         ptx::tmem_dealloc(tmem_base, C_::TMEM_COLS);

@@ -299,17 +299,18 @@ def select_config(M: int, N: int, K: int, split_k: int = 0) -> dict:
 
 class Tuning(ctypes.Structure):
     """spmm24_tuning (include/spmm24/SpMM_API.h)."""
-    _fields_ = [(n, ctypes.c_int) for n in ("pair", "pair2", "pair_split", "tile_n", "deep_ring")]
+    _fields_ = [(n, ctypes.c_int) for n in ("pair", "pair2", "pair_split", "tile_n", "deep_ring", "group_split")]
 
 
 _lib.spmm24_set_tuning.argtypes = [ctypes.POINTER(Tuning)]
 _lib.spmm24_set_tuning.restype = ctypes.c_int
 
 
-def set_tuning(pair: int = -1, pair2: int = -1, pair_split: int = 0, tile_n: int = 0, deep_ring: int = 0) -> None:
+def set_tuning(pair: int = -1, pair2: int = -1, pair_split: int = 0, tile_n: int = 0, deep_ring: int = 0,
+               group_split: int = 0) -> None:
     """spmm24_set_tuning: process-wide picker override (tests and tuning
     sweeps); called with no arguments it restores the automatic choice."""
-    t = Tuning(pair, pair2, pair_split, tile_n, deep_ring)
+    t = Tuning(pair, pair2, pair_split, tile_n, deep_ring, group_split)
     rc = _lib.spmm24_set_tuning(ctypes.byref(t))
     if rc != 0:
         raise ValueError(f"spmm24_set_tuning: {_lib.spmm24_last_error().decode()}")

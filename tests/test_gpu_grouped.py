@@ -39,13 +39,14 @@ def _grouped(dev, probs, flags=0, stream=None):
     return bufs, [_bits(b["C"]) for b in bufs]
 
 
-def _single(dev, p, bufs):
+def _single(dev, p, bufs, split_k=1):
     import torch
 
     import spmm24
 
     C = torch.full((p.M, p.N), float("nan"), dtype=torch.float16, device=dev)
-    assert spmm24.launch(torch.cuda.current_stream(dev), bufs["A"], bufs["B"], bufs["E"], C, p.M, p.N, p.K, None, 1) == 0
+    assert spmm24.launch(torch.cuda.current_stream(dev), bufs["A"], bufs["B"], bufs["E"], C, p.M, p.N, p.K, None,
+                         split_k) == 0
     torch.cuda.synchronize(dev)
     return _bits(C)
 
@@ -61,22 +62,29 @@ SHAPES = [
 ]
 
 
-def test_grouped_mixed_shapes(cuda_device):
+@pytest.mark.parametrize("group_split", [1, 2])
+def test_grouped_mixed_shapes(cuda_device, tuning, group_split):
+    """Whole tiles (group_split 1) or each tile's K over a CTA pair (2):
+    against the oracle, and bit for bit against spmm24_launch with split_k =
+    group_split (the same halves added in the same order)."""
+    tuning(group_split=group_split)
     probs = [make_problem(M, N, K, seed=3 * M + N + K, a_scale=0.05, b_dist="normal") for (M, N, K) in SHAPES]
     bufs, outs = _grouped(cuda_device, probs)
     for p, b, got in zip(probs, bufs, outs):
         stats = compare(got, oracle_c(p))
         assert within_tolerance(stats), ((p.M, p.N, p.K), stats)
-        assert np.array_equal(got, _single(cuda_device, p, b)), (p.M, p.N, p.K)
+        assert np.array_equal(got, _single(cuda_device, p, b, group_split)), (p.M, p.N, p.K)
 
 
-def test_grouped_many_tiles_per_cta(cuda_device):
-    """More tiles than SMs (600 here): every CTA walks several tiles of
-    several problems and both TMEM accumulators alternate; a second launch
-    of the same problem array reuses the cached launch and gives the same
-    bits."""
+@pytest.mark.parametrize("group_split", [0, 2])
+def test_grouped_many_tiles_per_cta(cuda_device, tuning, group_split):
+    """More tiles than SMs (630 here): every CTA (or CTA pair) walks several
+    tiles of several problems and both TMEM accumulators (and both receive
+    slots) alternate; a second launch of the same problem array reuses the
+    cached launch and gives the same bits."""
     import spmm24
 
+    tuning(group_split=group_split)
     shapes = [(65536, 8, 256), (4096, 16, 1024), (11008, 32, 512)]
     probs = [make_problem(M, N, K, seed=M + N, a_scale=0.05, b_dist="normal") for (M, N, K) in shapes]
     bufs, outs = _grouped(cuda_device, probs, flags=spmm24.STATIC_WEIGHTS)
@@ -197,15 +205,17 @@ def test_grouped_cuda_graph(cuda_device):
         assert within_tolerance(compare(_bits(b["C"]), oracle_c(p)))
 
 
-def test_grouped_epilogues_match_fused_launches(cuda_device):
+@pytest.mark.parametrize("group_split", [1, 2])
+def test_grouped_epilogues_match_fused_launches(cuda_device, tuning, group_split):
     """Each problem of a group with its own epilogue (bias + SiLU, alpha +
     GELU, a residual, a packed-B output, none): bit for bit the results of
-    spmm24_launch_fused with split_k = 1 (the same accumulator, the same
-    epilogue code), in fp16 and bf16."""
+    spmm24_launch_fused with split_k = group_split (the same accumulator,
+    the same epilogue code), in fp16 and bf16."""
     import torch
 
     import spmm24
 
+    tuning(group_split=group_split)
     dev = cuda_device
     cases = [((512, 16, 1024), dict(bias=True, act=spmm24.ACT_SILU)),
              ((256, 32, 512), dict(alpha=0.5, act=spmm24.ACT_GELU)),
@@ -230,7 +240,8 @@ def test_grouped_epilogues_match_fused_launches(cuda_device):
                                   spmm24.OUT_PACKED_B if kw.get("packed") else spmm24.OUT_ROW_MAJOR)
             c_g = torch.full((size,), -1, dtype=torch.int16, device=dev)
             c_r = torch.full((size,), -1, dtype=torch.int16, device=dev)
-            rc = spmm24.launch_fused(None, b["A"], b["B"], b["E"], c_r, M, N, K, 1, flags, bias=bias, residual=res,
+            rc = spmm24.launch_fused(None, b["A"], b["B"], b["E"], c_r, M, N, K, group_split, flags, bias=bias,
+                                     residual=res,
                                      alpha=kw.get("alpha", 1.0), activation=kw.get("act", spmm24.ACT_NONE),
                                      out_layout=spmm24.OUT_PACKED_B if kw.get("packed") else spmm24.OUT_ROW_MAJOR)
             assert rc == 0, spmm24._lib.spmm24_last_error().decode()
@@ -245,17 +256,19 @@ def test_grouped_epilogues_match_fused_launches(cuda_device):
         assert spmm24.device_status(0) == 0
 
 
-def test_grouped_fp8_matches_fp8_launches(cuda_device):
+@pytest.mark.parametrize("group_split", [1, 2])
+def test_grouped_fp8_matches_fp8_launches(cuda_device, tuning, group_split):
     """spmm24_launch_grouped_fp8: E4M3 and E5M2 operands, alpha per problem,
     bias / activation / residual / packed output: bit for bit the results of
-    spmm24_launch_fp8 with split_k = 1; one problem also against the oracle
-    (fp8 decode, fp32 GEMM; bound of tests/test_gpu_fp8.py)."""
+    spmm24_launch_fp8 with split_k = group_split; one problem also against
+    the oracle (fp8 decode, fp32 GEMM; bound of tests/test_gpu_fp8.py)."""
     import torch
 
     import oracle as O
     import spmm24
     from test_gpu_fp8 import _problem
 
+    tuning(group_split=group_split)
     dev = cuda_device
     cases = [((512, 16, 1024), dict(alpha=0.02)),
              ((256, 32, 512), dict(alpha=0.5, bias=True, act=spmm24.ACT_SILU)),
@@ -280,7 +293,7 @@ def test_grouped_fp8_matches_fp8_launches(cuda_device):
                                   res.data_ptr() if res is not None else None, kw["alpha"], act, layout)
             c_g = torch.full((size,), -1, dtype=torch.int16, device=dev)
             c_r = torch.full((size,), -1, dtype=torch.int16, device=dev)
-            rc = spmm24.launch_fp8(None, A, B, E, c_r, M, N, K, 1, flags, bias=bias, residual=res,
+            rc = spmm24.launch_fp8(None, A, B, E, c_r, M, N, K, group_split, flags, bias=bias, residual=res,
                                    alpha=kw["alpha"], activation=act, out_layout=layout)
             assert rc == 0, spmm24._lib.spmm24_last_error().decode()
             probs.append((A, B, E, c_g, M, N, K, None, epi))
