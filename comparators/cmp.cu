@@ -306,3 +306,90 @@ extern "C" double cmp_sparse_mma_peak(int stages, int pair, float* ms_out) {
     const double flops = (double)(sms / 2 * 2) * stages * 4.0 * 2.0 * 128.0 * 256.0 * 32.0;  // per SM: M = 128 rows
     return flops / (ms * 1e-3) / 1e12;
 }
+
+// ------------------------------------------------------------------------
+// Stage issue-rate probe for narrow tiles: one CTA per SM repeats the decode
+// kernels' stage (one tcgen05.cp of metadata, four tcgen05.mma.sp kind::f16
+// M = 128, K = 32, N = N_TILE <= 128) on operands resident in shared memory, into
+// one accumulator, or alternating between two accumulators stage by stage
+// (two independent chains of MMAs).  Reports microseconds per stage: the
+// rate at which one CTA can consume stages when memory is not the limit.
+namespace {
+template <int N_TILE>
+__global__ void __launch_bounds__(128, 1) cmp_stage_probe_kernel(int stages, int two_acc, uint32_t* status) {
+    using namespace spmm24;
+    using PC = Cfg<N_TILE, 1, 2>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    __shared__ uint64_t done;
+    __shared__ uint32_t holder;
+    for (int i = threadIdx.x; i < (PC::A_BYTES + PC::B_BYTES) / 16; i += blockDim.x)
+        reinterpret_cast<uint4*>(smem)[i] = make_uint4(0, 0, 0, 0);
+    for (int i = threadIdx.x; i < PC::E_BYTES / 16; i += blockDim.x)
+        reinterpret_cast<uint4*>(smem + PC::A_BYTES + PC::B_BYTES)[i] =
+            make_uint4(0x44444444u, 0x44444444u, 0x44444444u, 0x44444444u);
+    ptx::fence_proxy_async_smem();
+    if (threadIdx.x == 0) {
+        ptx::mbar_init(&done, 1);
+        ptx::fence_mbarrier_init();
+    }
+    if (threadIdx.x < 32) {
+        ptx::tmem_alloc(&holder, PC::TMEM_COLS);
+        ptx::tmem_relinquish();
+    }
+    ptx::tc_fence_before();
+    __syncthreads();
+    ptx::tc_fence_after();
+    const uint32_t tmem = holder;
+    if (threadIdx.x == 0) {
+        const uint32_t base = ptx::smem_u32(smem);
+        uint32_t acc[2] = {0, 0};
+        for (int s = 0; s < stages; ++s) {
+            const int b = two_acc ? (s & 1) : 0;
+            mma_stage<PC, N_TILE>(base, tmem + PC::META_COL + 0, tmem + (uint32_t)(b * N_TILE), acc[b], 0u);
+        }
+        ptx::tc_commit(&done);
+        if (!ptx::mbar_wait_bounded(&done, 0, kWaitLimitNs)) atomicOr(status, 1u);
+    }
+    ptx::tc_fence_before();
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        ptx::tc_fence_after();
+        ptx::tmem_dealloc(tmem, PC::TMEM_COLS);
+    }
+}
+}  // namespace
+
+// Microseconds per stage (negative on error) of the probe above with tile
+// width n_tile (16, 32 or 128) and one or two accumulators.
+extern "C" double cmp_stage_probe_us(int n_tile, int two_acc, int stages) {
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return -1;
+    void (*kern)(int, int, uint32_t*) = n_tile == 16    ? cmp_stage_probe_kernel<16>
+                                        : n_tile == 32  ? cmp_stage_probe_kernel<32>
+                                        : n_tile == 128 ? cmp_stage_probe_kernel<128>
+                                                        : nullptr;
+    if (!kern) return -1;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kProbeSmem) != cudaSuccess) return -2;
+    uint32_t* status = nullptr;
+    if (cudaMalloc(&status, 4) != cudaSuccess) return -3;
+    cudaMemset(status, 0, 4);
+    cudaEvent_t e0, e1;
+    cudaEventCreate(&e0);
+    cudaEventCreate(&e1);
+    kern<<<sms, 128, kProbeSmem>>>(stages / 8, two_acc, status);
+    cudaEventRecord(e0);
+    kern<<<sms, 128, kProbeSmem>>>(stages, two_acc, status);
+    cudaEventRecord(e1);
+    cudaError_t e = cudaEventSynchronize(e1);
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, e0, e1);
+    uint32_t st = 0;
+    cudaMemcpy(&st, status, 4, cudaMemcpyDeviceToHost);
+    cudaFree(status);
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    if (e != cudaSuccess || st != 0) return -4;
+    return (double)ms * 1e3 / stages;
+}
