@@ -361,7 +361,7 @@ def run_ours(args, rank, world, local_rank):
     # both inside the timed step.  Two full-C sets, for the e2e loop's two
     # buffer sets.
     gather_mode = grouped and shard and world > 1 and not (fp8 or bf16) and args.epilogue == "none"
-    full_sets, flag_ptrs, imported, epoch = [], None, [], [0]
+    full_sets, flag_ptrs, imported = [], None, []
     if gather_mode:
         full_elems = sum(c["M_full"] * c["N"] for c in calls)
         full_sets = [torch.zeros(full_elems, dtype=torch.float16, device=dev) for _ in range(2)]
@@ -415,9 +415,8 @@ def run_ours(args, rank, world, local_rank):
         else:
             for c in cs:
                 launch(c, hs)
-        if gather_mode:
-            epoch[0] += 1
-            if spmm24.gather_barrier(hs, flag_ptrs, rank, epoch[0]) != 0:
+        if gather_mode:  # epoch 0: the barrier counts on the device, so the step can live in a CUDA graph
+            if spmm24.gather_barrier(hs, flag_ptrs, rank, 0) != 0:
                 raise RuntimeError("spmm24_gather_barrier failed")
 
     def timed_steps(use_group):
@@ -546,8 +545,7 @@ def run_ours(args, rank, world, local_rank):
                                  C=c1 if packed_out else c1.view(c["M"], c["N"])))
     graphs = [None, None]
     try:
-        # (gather mode launches eagerly: every step's barrier takes a new epoch)
-        for k in range(0 if gather_mode else 2):
+        for k in range(2):
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g):
                 hs = int(torch.cuda.current_stream(dev).cuda_stream)

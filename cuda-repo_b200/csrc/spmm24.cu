@@ -1136,18 +1136,25 @@ struct BarrierArgs {
 };
 
 __global__ void spmm24_gather_barrier_kernel(BarrierArgs a) {
+    __shared__ uint32_t epoch_s;
     const int t = threadIdx.x;
     ptx::grid_dep_wait();
     // The next kernel in the stream may be scheduled now (its weight
     // prefetch then overlaps this wait); it still waits for this grid to
     // finish before reading anything the gather wrote.
     if (t == 0) ptx::grid_dep_launch();
+    // Epoch 0: one past this rank's last published epoch (slot `rank` of its
+    // own array, written only by its own earlier barriers), read before any
+    // thread publishes the new one.
+    if (t == 0) epoch_s = a.epoch ? a.epoch : ptx::ld_acquire_sys(a.flags[a.rank] + a.rank) + 1u;
+    __syncthreads();
+    const uint32_t epoch = epoch_s;
     __threadfence_system();
-    if (t < a.n) ptx::st_release_sys(a.flags[t] + a.rank, a.epoch);
+    if (t < a.n) ptx::st_release_sys(a.flags[t] + a.rank, epoch);
     if (t < a.n) {
         const uint32_t* f = a.flags[a.rank] + t;
         const uint64_t t0 = ptx::globaltimer();
-        while ((int)(ptx::ld_acquire_sys(f) - a.epoch) < 0) {
+        while ((int)(ptx::ld_acquire_sys(f) - epoch) < 0) {
             ptx::nanosleep_ns(100);
             if (ptx::globaltimer() - t0 > a.limit_ns) {
                 atomicOr(&g_spmm24_status, kStatusBarrierTimeout);

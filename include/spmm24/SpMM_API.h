@@ -196,7 +196,11 @@ cudaError_t spmm24_launch_gather(cudaStream_t stream, const void* compressed_a, 
  * (flag_arrays[r]: n_ranks u32 of rank r, peers' opened with
  * spmm24_ipc_import, zero-initialised once), then waits until all n_ranks
  * slots of its own array have reached `epoch` (use a counter that grows by
- * one per call).  The wait is bounded by limit_us; a barrier that gives up
+ * one per call).  epoch = 0 takes one past this rank's last published epoch
+ * from its own flag array on the device, so the call needs no host-side
+ * counter and can be captured in a CUDA graph and replayed; use either
+ * form, or both, as long as every rank passes the same sequence of epochs.
+ * The wait is bounded by limit_us; a barrier that gives up
  * sets bit 8 of the device status word (spmm24_device_status) instead of
  * hanging. */
 cudaError_t spmm24_gather_barrier(cudaStream_t stream, uint32_t* const* flag_arrays, int n_ranks, int rank,

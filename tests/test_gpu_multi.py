@@ -234,18 +234,39 @@ def _worker_grouped(rank, world, port, shapes):
         Av, Ev = spmm24.shard_views(A, E, M, K, r0, r1)
         probs.append((Av, bp, Ev, None, r1 - r0, N, K, spmm24.make_gather(ptrs[i], r0, M)))
     s = torch.cuda.current_stream(dev)
-    for epoch in (1, 2):  # twice: the second launch reuses the cached launch and the barrier's next epoch
+    arr = spmm24.problem_array(probs)
+    # an explicit epoch, then the barrier's automatic one (0: the next after
+    # the last), then the same step captured in a CUDA graph, replayed twice
+    for epoch in (1, 0):
         for f in fulls:
             f.fill_(float("nan"))
         torch.cuda.synchronize(dev)
         dist.barrier()
-        assert spmm24.launch_grouped(s, probs, spmm24.STATIC_WEIGHTS) == 0, spmm24._lib.spmm24_last_error().decode()
+        assert spmm24.launch_grouped(s, arr, spmm24.STATIC_WEIGHTS) == 0, spmm24._lib.spmm24_last_error().decode()
         assert spmm24.gather_barrier(s, ptrs[-1], rank, epoch) == 0
         torch.cuda.synchronize(dev)
         assert spmm24.device_status(rank) == 0
         for i, (f, ex) in enumerate(zip(fulls, expects)):
             assert torch.equal(f, ex), (rank, epoch, shapes[i])
         dist.barrier()
+    gs = torch.cuda.Stream(dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(gs):
+        with torch.cuda.graph(graph, stream=gs):
+            assert spmm24.launch_grouped(gs, arr, spmm24.STATIC_WEIGHTS) == 0
+            assert spmm24.gather_barrier(gs, ptrs[-1], rank, 0) == 0
+    for rep in range(2):
+        for f in fulls:
+            f.fill_(float("nan"))
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        graph.replay()
+        torch.cuda.synchronize(dev)
+        assert spmm24.device_status(rank) == 0
+        for i, (f, ex) in enumerate(zip(fulls, expects)):
+            assert torch.equal(f, ex), (rank, "graph", rep, shapes[i])
+        dist.barrier()
+    del graph
     for p in opened:
         spmm24.ipc_close(p)
     dist.barrier()
