@@ -231,7 +231,7 @@ def workload_config(args, world):
             "parallelism": (("M-sharded" if world > 1 else "unsharded") +
                             f" x{world} (rows split by spmm24_shard_rows, no reduction" +
                             ("; outputs all-gathered into every rank's full C inside the step: the grouped kernel's "
-                             "epilogue stores over NVLink + spmm24_gather_barrier)"
+                             "epilogue stores over NVLink, its last CTA runs the cross-GPU barrier)"
                              if world > 1 and args.workload == "decode" else ")") if shard
                             else f"replicas x{world} (each rank its own layers)")}
 
@@ -244,6 +244,8 @@ def to_dev(torch, arr, dev):
 
 # ------------------------------------------------------------- our arm
 def run_ours(args, rank, world, local_rank):
+    import ctypes
+
     import numpy as np
     import torch
     import torch.distributed as dist
@@ -365,7 +367,7 @@ def run_ours(args, rank, world, local_rank):
     if gather_mode:
         full_elems = sum(c["M_full"] * c["N"] for c in calls)
         full_sets = [torch.zeros(full_elems, dtype=torch.float16, device=dev) for _ in range(2)]
-        flag_buf = torch.zeros(world, dtype=torch.int32, device=dev)
+        flag_buf = torch.zeros(world + 1, dtype=torch.int32, device=dev)  # + the fused barrier's CTA counter
         torch.cuda.synchronize(dev)
         mine = [spmm24.ipc_export(t) for t in full_sets] + [spmm24.ipc_export(flag_buf)]
         handles = [None] * world
@@ -379,6 +381,7 @@ def run_ours(args, rank, world, local_rank):
                     bases[i][r] = spmm24.ipc_import(handles[r][i])
                     imported.append(bases[i][r])
         flag_ptrs = bases[2]
+        group_bar = spmm24.group_barrier(flag_ptrs, rank)
         dist.barrier()
 
     def gathers_for(k):
@@ -398,6 +401,12 @@ def run_ours(args, rank, world, local_rank):
 
     def step_launch(cs, hs=None, use_group=grouped, k=0):
         hs = h_stream if hs is None else hs
+        if use_group and gather_mode:  # one kernel: the SpMMs, the gathered stores, the cross-GPU barrier
+            arr = group_arrays.setdefault((id(cs), k), group_array(cs, k))
+            rc = spmm24._lib.spmm24_launch_grouped_gather(hs, arr, len(arr), group_flags, ctypes.byref(group_bar))
+            if rc != 0:
+                raise RuntimeError(f"spmm24_launch_grouped_gather: {rc} {spmm24._lib.spmm24_last_error().decode()}")
+            return
         if use_group:
             arr = group_arrays.setdefault((id(cs), k), group_array(cs, k))
             rc = group_fn(hs, arr, len(arr), group_flags)
@@ -443,7 +452,7 @@ def run_ours(args, rank, world, local_rank):
     chain_ms = None
     if grouped:
         chain_ms = timed_steps(False)  # the same steps as one launch per SpMM, for comparison
-    nl = ((1 if grouped else len(calls)) + (1 if gather_mode else 0)) * args.steps  # + the barrier kernel
+    nl = (1 if grouped else len(calls) + (1 if gather_mode else 0)) * args.steps  # chain: + the barrier kernel
     with ClockSampler(local_rank) as clk:
         elapsed_ms = timed_steps(grouped)
     clocks = clk.summary()
@@ -737,8 +746,9 @@ def run_ours(args, rank, world, local_rank):
     if gather_mode:
         out["gather"] = {"status": spmm24.device_status(dev.index), "ranks": world,
                          "gathered_bytes_per_step": 2 * sum(c["M_full"] * c["N"] for c in calls),
-                         "op": "each rank's output rows stored by the grouped kernel's epilogue into all ranks' "
-                               "full C (CUDA IPC peer pointers, NVLink), then one spmm24_gather_barrier per step"}
+                         "op": "one spmm24_launch_grouped_gather per step: each rank's output rows stored by the "
+                               "grouped kernel's epilogue into all ranks' full C (CUDA IPC peer pointers, NVLink), "
+                               "the cross-GPU barrier run by the grid's last CTA"}
         torch.cuda.synchronize(dev)
         dist.barrier()
         for p_ in imported:
@@ -1324,8 +1334,9 @@ def run_pack(args, rank, world, local_rank):
     if gather_mode:
         out["gather"] = {"status": spmm24.device_status(dev.index), "ranks": world,
                          "gathered_bytes_per_step": 2 * sum(c["M_full"] * c["N"] for c in calls),
-                         "op": "each rank's output rows stored by the grouped kernel's epilogue into all ranks' "
-                               "full C (CUDA IPC peer pointers, NVLink), then one spmm24_gather_barrier per step"}
+                         "op": "one spmm24_launch_grouped_gather per step: each rank's output rows stored by the "
+                               "grouped kernel's epilogue into all ranks' full C (CUDA IPC peer pointers, NVLink), "
+                               "the cross-GPU barrier run by the grid's last CTA"}
         torch.cuda.synchronize(dev)
         dist.barrier()
         for p_ in imported:
@@ -1488,8 +1499,9 @@ def run_pack_b(args, rank, world, local_rank):
     if gather_mode:
         out["gather"] = {"status": spmm24.device_status(dev.index), "ranks": world,
                          "gathered_bytes_per_step": 2 * sum(c["M_full"] * c["N"] for c in calls),
-                         "op": "each rank's output rows stored by the grouped kernel's epilogue into all ranks' "
-                               "full C (CUDA IPC peer pointers, NVLink), then one spmm24_gather_barrier per step"}
+                         "op": "one spmm24_launch_grouped_gather per step: each rank's output rows stored by the "
+                               "grouped kernel's epilogue into all ranks' full C (CUDA IPC peer pointers, NVLink), "
+                               "the cross-GPU barrier run by the grid's last CTA"}
         torch.cuda.synchronize(dev)
         dist.barrier()
         for p_ in imported:

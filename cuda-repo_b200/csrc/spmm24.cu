@@ -905,9 +905,17 @@ cudaError_t launch_group_kernel(cudaStream_t stream, int dev, const GroupCache& 
 }
 
 cudaError_t launch_grouped_impl(cudaStream_t stream, const spmm24_problem* probs, int count, unsigned flags,
-                                bool fp8) {
+                                bool fp8, const spmm24_group_barrier* bar = nullptr) {
     g_last_error[0] = '\0';
     if (!probs) return invalid("grouped: null problem array");
+    if (bar) {
+        if (bar->n_ranks < 1 || bar->n_ranks > SPMM24_MAX_GATHER_RANKS || bar->rank < 0 || bar->rank >= bar->n_ranks)
+            return invalid("barrier: bad rank or rank count");
+        if (bar->limit_us == 0 || bar->limit_us > 60000000u) return invalid("barrier: limit_us must be 1..60e6");
+        for (int r = 0; r < bar->n_ranks; ++r)
+            if (!bar->flag_arrays[r] || ((uintptr_t)bar->flag_arrays[r] & 3u))
+                return invalid("barrier: bad flag array");
+    }
     if (count < 1 || count > kGroupMaxProblems) return invalid("grouped: count must be 1..16");
     const unsigned allowed = SPMM24_STATIC_WEIGHTS | SPMM24_NO_PDL | SPMM24_BF16 |
                              (fp8 ? (unsigned)(SPMM24_FP8_A_E5M2 | SPMM24_FP8_B_E5M2) : 0u);
@@ -953,6 +961,9 @@ cudaError_t launch_grouped_impl(cudaStream_t stream, const spmm24_problem* probs
         k.insert(k.end(), b, b + n);
     };
     key.push_back(fp8 ? 1 : 0);
+    spmm24_group_barrier bk{};
+    if (bar) bk = *bar;
+    put(key, &bk, sizeof(bk));
     for (int i = 0; i < count; ++i) {
         put(key, &probs[i], sizeof(spmm24_problem));
         spmm24_gather g{};
@@ -976,6 +987,12 @@ cudaError_t launch_grouped_impl(cudaStream_t stream, const spmm24_problem* probs
         gc.epi = any_epi;
         gc.split = split;
         gc.tuned = tuned;
+        if (bar) {
+            for (int r = 0; r < bar->n_ranks; ++r) gc.params.bar_flags[r] = bar->flag_arrays[r];
+            gc.params.bar_n = bar->n_ranks;
+            gc.params.bar_rank = bar->rank;
+            gc.params.bar_limit_ns = (unsigned long long)bar->limit_us * 1000ull;
+        }
     }
 #ifdef SPMM24_TRACE
     gc.params.trace_base = g_trace_next.fetch_add((long long)gc.n_ctas);
@@ -1213,6 +1230,12 @@ extern "C" cudaError_t spmm24_launch_grouped(cudaStream_t stream, const spmm24_p
 extern "C" cudaError_t spmm24_launch_grouped_fp8(cudaStream_t stream, const spmm24_problem* problems, int count,
                                                 unsigned flags) {
     return spmm24::launch_grouped_impl(stream, problems, count, flags, true);
+}
+
+extern "C" cudaError_t spmm24_launch_grouped_gather(cudaStream_t stream, const spmm24_problem* problems, int count,
+                                                   unsigned flags, const spmm24_group_barrier* barrier) {
+    if (!barrier) return spmm24::record_invalid("barrier: null descriptor");
+    return spmm24::launch_grouped_impl(stream, problems, count, flags, false, barrier);
 }
 
 extern "C" cudaError_t spmm24_launch_fused(cudaStream_t stream, const void* compressed_a, const void* b_packed,

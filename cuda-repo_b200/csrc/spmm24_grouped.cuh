@@ -67,6 +67,14 @@ struct GroupParams {
     int weights_static;
     int bf16;
     uint32_t mma_fmt;  // fp8: operand-format bits of the instruction descriptor
+    // Cross-GPU barrier at the end of the launch (bar_n > 0): when every CTA
+    // of this grid has stored its rows, the last one publishes this rank's
+    // next epoch into slot bar_rank of every rank's flag array and waits,
+    // bounded, until every slot of its own array has reached it.  Word bar_n
+    // of the own array counts finished CTAs (wraps to zero every launch).
+    uint32_t* bar_flags[kMaxGatherRanks];
+    int bar_n, bar_rank;
+    unsigned long long bar_limit_ns;
     // CTA c (SPLIT = 2: cluster c) processes sched[sched_off[c] ..
     // sched_off[c + 1]); an entry is (problem << 12) | m_tile.
     uint16_t sched_off[kGroupMaxCtas + 1];
@@ -430,7 +438,29 @@ __global__ void __launch_bounds__(kThreads, 1) spmm24_grouped_kernel(const __gri
 
     if (threadIdx.x == 64) SPMM24_STAMP(5);
     ptx::tc_fence_before();
+    if (p.bar_n) __threadfence_system();  // this thread's stores (peer rows included) before the CTA's count
     __syncthreads();
+    if (p.bar_n && threadIdx.x == 0) {
+        // the last CTA of the grid to get here runs the cross-GPU barrier
+        uint32_t* own = p.bar_flags[p.bar_rank];
+        const uint32_t done = atomicInc(own + p.bar_n, gridDim.x - 1u);
+        if (done == gridDim.x - 1u) {
+            __threadfence_system();
+            const uint32_t epoch = ptx::ld_acquire_sys(own + p.bar_rank) + 1u;
+            for (int r = 0; r < p.bar_n; ++r) ptx::st_release_sys(p.bar_flags[r] + p.bar_rank, epoch);
+            const uint64_t t0 = ptx::globaltimer();
+            for (int r = 0; r < p.bar_n; ++r) {
+                while ((int)(ptx::ld_acquire_sys(own + r) - epoch) < 0) {
+                    ptx::nanosleep_ns(100);
+                    if (ptx::globaltimer() - t0 > p.bar_limit_ns) {
+                        atomicOr(&g_spmm24_status, kStatusBarrierTimeout);
+                        r = p.bar_n;
+                        break;
+                    }
+                }
+            }
+        }
+    }
     if (SPLIT > 1) ptx::cluster_sync();  // no CTA leaves while its partner may still reach its shared memory
     if (warp == 1) {
         ptx::tc_fence_after();

@@ -258,6 +258,37 @@ def make_gather(c_full_ptrs, row_offset: int, m_full: int, c_multicast=None) -> 
     return g
 
 
+class GroupBarrier(ctypes.Structure):
+    """spmm24_group_barrier (include/spmm24/SpMM_API.h)."""
+    _fields_ = [("flag_arrays", ctypes.c_void_p * 8), ("n_ranks", ctypes.c_int), ("rank", ctypes.c_int),
+                ("limit_us", ctypes.c_uint)]
+
+
+_lib.spmm24_launch_grouped_gather.argtypes = [_vp, ctypes.POINTER(Problem), ctypes.c_int, ctypes.c_uint,
+                                              ctypes.POINTER(GroupBarrier)]
+_lib.spmm24_launch_grouped_gather.restype = ctypes.c_int
+
+
+def group_barrier(flag_ptrs, rank: int, limit_us: int = 2_000_000) -> GroupBarrier:
+    """A spmm24_group_barrier over the ranks' flag arrays (n_ranks + 1 u32 each)."""
+    if len(flag_ptrs) > 8:
+        raise ValueError("at most 8 ranks (SPMM24_MAX_GATHER_RANKS)")
+    b = GroupBarrier()
+    for r, p in enumerate(flag_ptrs):
+        b.flag_arrays[r] = _ptr(p)
+    b.n_ranks = len(flag_ptrs)
+    b.rank = rank
+    b.limit_us = limit_us
+    return b
+
+
+def launch_grouped_gather(stream, problems, barrier: GroupBarrier, flags: int = 0) -> int:
+    """spmm24_launch_grouped_gather: a grouped launch whose problems gather,
+    with the cross-GPU barrier at the end of the same kernel."""
+    arr = problems if isinstance(problems, ctypes.Array) else problem_array(problems)
+    return _lib.spmm24_launch_grouped_gather(_stream_handle(stream), arr, len(arr), flags, ctypes.byref(barrier))
+
+
 def launch_grouped(stream, problems, flags: int = 0, fp8: bool = False) -> int:
     """spmm24_launch_grouped (fp8: spmm24_launch_grouped_fp8): several
     independent N <= 32 SpMMs in one persistent launch.  `problems`: a list

@@ -206,6 +206,28 @@ cudaError_t spmm24_launch_gather(cudaStream_t stream, const void* compressed_a, 
 cudaError_t spmm24_gather_barrier(cudaStream_t stream, uint32_t* const* flag_arrays, int n_ranks, int rank,
                                   uint32_t epoch, unsigned limit_us);
 
+/* spmm24_launch_grouped with the cross-GPU barrier folded into the end of
+ * the same kernel, for a step whose problems all carry gather descriptors
+ * (no counterpart in the reference): when the launch has completed on
+ * every rank, every rank's full C holds every rank's rows, with no
+ * separate barrier launch.  flag_arrays[r]: rank r's array of n_ranks + 1
+ * u32 (this process's own one, the peers' opened with spmm24_ipc_import),
+ * zeroed once; slots 0..n_ranks-1 are spmm24_gather_barrier's, counted on
+ * the device as with its epoch 0 (the two can be mixed on one array), and
+ * word n_ranks counts this grid's finished CTAs (back to zero after every
+ * launch).  The last CTA to finish publishes the epoch and waits, bounded
+ * by limit_us; a barrier that gives up sets bit 8 of the device status
+ * word.  Same problems, formats and flags as spmm24_launch_grouped (16-bit
+ * operands). */
+typedef struct spmm24_group_barrier {
+    uint32_t* flag_arrays[SPMM24_MAX_GATHER_RANKS];
+    int n_ranks;
+    int rank;
+    unsigned limit_us;
+} spmm24_group_barrier;
+cudaError_t spmm24_launch_grouped_gather(cudaStream_t stream, const spmm24_problem* problems, int count,
+                                         unsigned flags, const spmm24_group_barrier* barrier);
+
 /* CUDA IPC for the peer buffers: spmm24_ipc_export describes a device
  * pointer (any address inside an allocation, e.g. a tensor of a caching
  * allocator) for another process of the node; spmm24_ipc_import maps it

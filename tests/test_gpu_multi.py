@@ -214,7 +214,7 @@ def _worker_grouped(rank, world, port, shapes):
             Av, Ev = spmm24.shard_views(A, E, M, K, r0, r1)
             local.append((Av, bp, Ev, ex[r0:r1], r1 - r0, N, K))
     assert spmm24.launch_grouped(None, local) == 0, spmm24._lib.spmm24_last_error().decode()
-    flags = torch.zeros(world, dtype=torch.int32, device=dev)
+    flags = torch.zeros(world + 1, dtype=torch.int32, device=dev)  # + the fused barrier's CTA counter
     torch.cuda.synchronize(dev)
     handles = [None] * world
     dist.all_gather_object(handles, [spmm24.ipc_export(f) for f in fulls] + [spmm24.ipc_export(flags)])
@@ -292,6 +292,37 @@ def _worker_grouped(rank, world, port, shapes):
         dist.barrier()
     finally:
         spmm24.reset_tuning()
+    # the barrier folded into the grouped kernel (spmm24_launch_grouped_gather),
+    # on the same flag arrays, eagerly twice and then replayed from a graph
+    bar = spmm24.group_barrier(ptrs[-1], rank)
+    for rep in range(2):
+        for f in fulls:
+            f.fill_(float("nan"))
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        assert spmm24.launch_grouped_gather(s, arr, bar, spmm24.STATIC_WEIGHTS) == 0, \
+            spmm24._lib.spmm24_last_error().decode()
+        torch.cuda.synchronize(dev)
+        assert spmm24.device_status(rank) == 0
+        for i, (f, ex) in enumerate(zip(fulls, expects)):
+            assert torch.equal(f, ex), (rank, "fused barrier", rep, shapes[i])
+        dist.barrier()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(gs):
+        with torch.cuda.graph(graph, stream=gs):
+            assert spmm24.launch_grouped_gather(gs, arr, bar, spmm24.STATIC_WEIGHTS) == 0
+    for rep in range(2):
+        for f in fulls:
+            f.fill_(float("nan"))
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        graph.replay()
+        torch.cuda.synchronize(dev)
+        assert spmm24.device_status(rank) == 0
+        for i, (f, ex) in enumerate(zip(fulls, expects)):
+            assert torch.equal(f, ex), (rank, "fused barrier graph", rep, shapes[i])
+        dist.barrier()
+    del graph
     for p in opened:
         spmm24.ipc_close(p)
     dist.barrier()
