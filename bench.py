@@ -745,6 +745,8 @@ def run_ours(args, rank, world, local_rank):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(layers, acts, shapes, budget_s=args.cpu_seconds, bf16=bf16, fp8=fp8)
 
+    if args.config4 and args.workload == "decode" and not (fp8 or bf16) and args.epilogue == "none":
+        out["config4"] = run_config4(torch, dist, spmm24, dev, rank, world, args)
     if gather_mode:
         out["gather"] = {"status": spmm24.device_status(dev.index), "ranks": world,
                          "gathered_bytes_per_step": 2 * sum(c["M_full"] * c["N"] for c in calls),
@@ -760,6 +762,120 @@ def run_ours(args, rank, world, local_rank):
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(out), flush=True)
+
+
+def run_config4(torch, dist, spmm24, dev, rank, world, args):
+    """BASELINE config 4 beside the decode line: the LLaMA-70B layers (M, K)
+    in {(8192, 8192), (28672, 8192), (8192, 28672)} x N in {16, 256, 4096},
+    each split along M across the ranks (spmm24_shard_rows, 128-row units),
+    A N(0, 0.01) pruned 2:4 and B N(0, 1) generated and packed on the device.
+    Timed twice, max over ranks: the shards alone (spmm24_launch per layer),
+    and with the full C of every layer gathered on every rank inside the
+    step (spmm24_launch_gather per layer -- the epilogue's stores over NVLink
+    -- and one spmm24_gather_barrier per step).  The gather's NVLink bound:
+    each rank receives (world - 1) / world of the full C, at the measured
+    770 GB/s per direction of a peer copy on this pool."""
+    layers_mk = [(8192, 8192), (28672, 8192), (8192, 28672)]
+    ns = (16, 256, 4096)
+    g = torch.Generator(device=dev)
+    stream = torch.cuda.current_stream(dev)
+    calls = []
+    for li, (M, K) in enumerate(layers_mk):
+        r0, r1 = spmm24.shard_rows(M, world, rank, 128)
+        g.manual_seed(7000 + 100 * rank + li)
+        a = (torch.randn(r1 - r0, K, generator=g, device=dev) * 0.01).half()
+        spmm24.prune_2of4_device(a, r1 - r0, K)
+        A, E, _ = spmm24.pack_a_device(a, r1 - r0, K)
+        del a
+        for N in ns:
+            g.manual_seed(9000 + N + K)  # the same activations on every rank
+            Bp = spmm24.pack_b_device(torch.randn(K, N, generator=g, device=dev).half(), K, N)
+            calls.append({"M": r1 - r0, "M_full": M, "r0": r0, "N": N, "K": K, "A": A, "E": E, "B": Bp,
+                          "C": torch.empty((r1 - r0, N), dtype=torch.float16, device=dev)})
+    full_elems = sum(c["M_full"] * c["N"] for c in calls)
+    full = torch.zeros(full_elems, dtype=torch.float16, device=dev)
+    flag_buf = torch.zeros(world + 1, dtype=torch.int32, device=dev)
+    torch.cuda.synchronize(dev)
+    imported = []
+    if world > 1:
+        handles = [None] * world
+        dist.all_gather_object(handles, (spmm24.ipc_export(full), spmm24.ipc_export(flag_buf)))
+        bases, flags_r = [], []
+        for r in range(world):
+            if r == rank:
+                bases.append(full.data_ptr())
+                flags_r.append(flag_buf.data_ptr())
+            else:
+                bases.append(spmm24.ipc_import(handles[r][0]))
+                flags_r.append(spmm24.ipc_import(handles[r][1]))
+                imported += [bases[-1], flags_r[-1]]
+        dist.barrier()
+    else:
+        bases, flags_r = [full.data_ptr()], [flag_buf.data_ptr()]
+    h = int(stream.cuda_stream)
+    fl = spmm24.STATIC_WEIGHTS
+
+    def shards():
+        for c in calls:
+            rc = spmm24._lib.spmm24_launch_ex(h, c["A"].data_ptr(), c["B"].data_ptr(), c["E"].data_ptr(),
+                                              c["C"].data_ptr(), c["M"], c["N"], c["K"], 0, fl)
+            if rc != 0:
+                raise RuntimeError(f"spmm24_launch_ex: {rc}")
+
+    def gathered():
+        off = 0
+        for c in calls:
+            rc = spmm24.launch_gather(h, c["A"], c["B"], c["E"], c["M"], c["N"], c["K"],
+                                      [b + 2 * off for b in bases], c["r0"], c["M_full"], 0, fl)
+            off += c["M_full"] * c["N"]
+            if rc != 0:
+                raise RuntimeError(f"spmm24_launch_gather: {rc} {spmm24._lib.spmm24_last_error().decode()}")
+        if spmm24.gather_barrier(h, flags_r, rank, 0) != 0:
+            raise RuntimeError("spmm24_gather_barrier failed")
+
+    steps = max(3, min(args.steps, 10))
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda._sleep(int(2e7))
+        e0.record(stream)
+        for _ in range(steps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        t = torch.tensor([e0.elapsed_time(e1) * 1e3 / steps], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t[0])
+
+    us_shards = timed(shards)
+    us_gather = timed(gathered)
+    status = spmm24.device_status(dev.index)
+    if world > 1:
+        dist.barrier()
+        for p in imported:
+            spmm24.ipc_close(p)
+        dist.barrier()
+    flop = sum(flops(M, N, K) for (M, K) in layers_mk for N in ns)
+    recv = 2 * full_elems * (world - 1) / world
+    bound_us = recv / 770e9 * 1e6
+    return {"baseline_config": 4, "workload": ", ".join(f"{M}x{N}x{K}" for (M, K) in layers_mk for N in ns),
+            "parallelism": f"M-sharded x{world}", "steps": steps,
+            "us_per_step_shards": round(us_shards, 2), "tflops_shards": round(flop / (us_shards * 1e-6) / 1e12, 1),
+            "us_per_step_gathered": round(us_gather, 2),
+            "tflops_gathered": round(flop / (us_gather * 1e-6) / 1e12, 1),
+            "gather_share": round(max(0.0, us_gather - us_shards) / us_gather, 4),
+            "gathered_bytes_per_step": 2 * full_elems,
+            "nvlink_receive_bound_us": round(bound_us, 2) if world > 1 else None,
+            "frac_of_nvlink_bound": round(bound_us / us_gather, 4) if world > 1 else None,
+            "status": status,
+            "op": "shards: spmm24_launch_ex per layer; gathered: spmm24_launch_gather per layer (peer stores over "
+                  "NVLink into every rank's full C) + one spmm24_gather_barrier per step; device time, max over ranks"}
 
 
 def time_gather(torch, dist, spmm24, calls, stream, dev, rank, world, args, flags):
@@ -1333,16 +1449,6 @@ def run_pack(args, rank, world, local_rank):
             dn = [d.view(torch.int16).cpu().numpy().view(np.uint16).reshape(-1) for d in dense]
         gbs, kind, sample = host_pack_baseline(dn, args.cpu_seconds, fp8=fp8)
         out["cpu_baseline"] = {"value": round(gbs, 4), "unit": "GB/s", "cores": 1, "kind": kind, "sample": sample}
-    if gather_mode:
-        out["gather"] = {"status": spmm24.device_status(dev.index), "ranks": world,
-                         "gathered_bytes_per_step": 2 * sum(c["M_full"] * c["N"] for c in calls),
-                         "op": "one spmm24_launch_grouped_gather per step: each rank's output rows stored by the "
-                               "grouped kernel's epilogue into all ranks' full C (CUDA IPC peer pointers, NVLink), "
-                               "the cross-GPU barrier run by the grid's last CTA"}
-        torch.cuda.synchronize(dev)
-        dist.barrier()
-        for p_ in imported:
-            spmm24.ipc_close(p_)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -1498,16 +1604,6 @@ def run_pack_b(args, rank, world, local_rank):
         an = [a.view(torch.int16).cpu().numpy().view(np.uint16).reshape(-1) for a in acts]
         gbs, kind, sample = host_pack_b_baseline(an, args.cpu_seconds)
         out["cpu_baseline"] = {"value": round(gbs, 4), "unit": "GB/s", "cores": 1, "kind": kind, "sample": sample}
-    if gather_mode:
-        out["gather"] = {"status": spmm24.device_status(dev.index), "ranks": world,
-                         "gathered_bytes_per_step": 2 * sum(c["M_full"] * c["N"] for c in calls),
-                         "op": "one spmm24_launch_grouped_gather per step: each rank's output rows stored by the "
-                               "grouped kernel's epilogue into all ranks' full C (CUDA IPC peer pointers, NVLink), "
-                               "the cross-GPU barrier run by the grid's last CTA"}
-        torch.cuda.synchronize(dev)
-        dist.barrier()
-        for p_ in imported:
-            spmm24.ipc_close(p_)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -1686,6 +1782,8 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["pack", "packb"], default="decode")
     ap.add_argument("--no-comparators", dest="comparators", action="store_false",
                     help="skip the same-run comparators (cuSPARSELt, dense cuBLAS, the reference kernel)")
+    ap.add_argument("--no-config4", dest="config4", action="store_false",
+                    help="skip the M-sharded LLaMA-70B block (config 4) of the default decode line")
     ap.add_argument("--no-secondary", dest="secondary", action="store_false",
                     help="skip the prefill / square block (configs 3 and 5) of the default decode line")
     ap.add_argument("--launch", choices=["grouped", "chain"], default="grouped",
