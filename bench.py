@@ -864,6 +864,11 @@ def run_config4(torch, dist, spmm24, dev, rank, world, args):
     flop = sum(flops(M, N, K) for (M, K) in layers_mk for N in ns)
     recv = 2 * full_elems * (world - 1) / world
     bound_us = recv / 770e9 * 1e6
+    # the fused step's roofline: the slower of this rank's share of the flops
+    # at the 2:4 tensor ceiling (2 x the measured dense bf16 burst) and the
+    # bytes it must receive over NVLink
+    compute_us = flop / world / (2.0 * load_peaks()["bf16_tflops"] * 1e12) * 1e6
+    step_bound_us = max(compute_us, bound_us if world > 1 else 0.0)
     return {"baseline_config": 4, "workload": ", ".join(f"{M}x{N}x{K}" for (M, K) in layers_mk for N in ns),
             "parallelism": f"M-sharded x{world}", "steps": steps,
             "us_per_step_shards": round(us_shards, 2), "tflops_shards": round(flop / (us_shards * 1e-6) / 1e12, 1),
@@ -872,7 +877,8 @@ def run_config4(torch, dist, spmm24, dev, rank, world, args):
             "gather_share": round(max(0.0, us_gather - us_shards) / us_gather, 4),
             "gathered_bytes_per_step": 2 * full_elems,
             "nvlink_receive_bound_us": round(bound_us, 2) if world > 1 else None,
-            "frac_of_nvlink_bound": round(bound_us / us_gather, 4) if world > 1 else None,
+            "compute_bound_us": round(compute_us, 2),
+            "frac_of_step_bound": round(step_bound_us / us_gather, 4),
             "status": status,
             "op": "shards: spmm24_launch_ex per layer; gathered: spmm24_launch_gather per layer (peer stores over "
                   "NVLink into every rank's full C) + one spmm24_gather_barrier per step; device time, max over ranks"}
