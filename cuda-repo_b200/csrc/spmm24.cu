@@ -232,7 +232,7 @@ void maybe_pair2(Plan& p, int M, int N, int sms, int tile_n, int stages, int sme
 
 // allow_pair: the CTA-pair path may be chosen.  max_split: the largest
 // automatic K split.  pair2_ok: the two-M-half pair kernel may be chosen
-// (no residual, no gather).
+// (no residual).
 Plan make_plan(int M, int N, int K, int split_k, int sms, bool allow_pair = true, int max_split = kMaxSplit,
                bool pair2_ok = true) {
     Plan p{};
@@ -530,7 +530,7 @@ cudaError_t launch_impl(cudaStream_t stream, const void* A, const void* B, const
     int dev = 0;
     e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    const bool pair2_ok = !epi.residual && epi.gather_n == 0;
+    const bool pair2_ok = !epi.residual;
     Plan pl = make_plan(M, N, K, split_k, sm_count(dev), true, kMaxSplit, pair2_ok);
 
     // A: (128 halves of one 16x8 block, bands, 16-K blocks); box 8 bands x 8 blocks.

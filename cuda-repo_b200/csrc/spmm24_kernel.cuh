@@ -724,6 +724,22 @@ spmm24_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                 const int gm = gm0 + r;
                 if (gm >= p.M || gn >= p.N) continue;
                 const __half* src = cst + (size_t)r * C_::C_PITCH + chunk * 8;
+                if constexpr (EPI) {
+                    if (p.epi.gather_n) {  // every rank's full C (or its multicast address)
+                        if (vec_ok) {
+                            store_row16(p.C, p.epi, gm, gn, p.N, *reinterpret_cast<const uint4*>(src));
+                        } else {
+                            const int lim = min(8, p.N - gn);
+                            uint32_t w[4];
+#pragma unroll
+                            for (int q = 0; q < 4; ++q)
+                                w[q] = (uint32_t)__half_as_ushort(src[2 * q]) |
+                                       ((uint32_t)__half_as_ushort(src[2 * q + 1]) << 16);
+                            store_row_elems(p.C, p.epi, gm, gn, p.N, w, lim);
+                        }
+                        continue;
+                    }
+                }
                 __half* out = reinterpret_cast<__half*>(p.C) + (size_t)gm * p.N + gn;
                 if (vec_ok) {
                     *reinterpret_cast<uint4*>(out) = *reinterpret_cast<const uint4*>(src);
@@ -904,7 +920,8 @@ spmm24_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
 // CTA for 15.7 MFLOP (dense-equivalent) instead of 50 KB for 8.4 MFLOP,
 // so the same shared-memory bytes in flight feed the tensor core 1.4x
 // longer.  Row-major output; EPI adds alpha, bias, activation, bf16 and
-// the packed-B output layout (no residual, no gather); no K split.  FP8: two
+// the packed-B output layout, the fused all-gather's row stores (no
+// residual); no K split.  FP8: two
 // 128-byte-swizzled B halves of 120 rows per stage and two 128-K metadata
 // groups per M half; the metadata ring in TMEM has two slots instead of
 // one per stage (the copy into a slot is issued after the MMAs that read
@@ -1192,6 +1209,22 @@ spmm24_pair2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                 const int gm = m_tile * C_::TILE_M + (r / kTileM) * 2 * kTileM + (int)rank * kTileM + r % kTileM;
                 if (gm >= p.M || gn >= p.N) continue;
                 const __half* src = cst + (size_t)r * C_::C_PITCH + chunk * 8;
+                if constexpr (EPI) {
+                    if (p.epi.gather_n) {  // every rank's full C (or its multicast address)
+                        if (vec_ok) {
+                            store_row16(p.C, p.epi, gm, gn, p.N, *reinterpret_cast<const uint4*>(src));
+                        } else {
+                            const int lim = min(8, p.N - gn);
+                            uint32_t w[4];
+#pragma unroll
+                            for (int q = 0; q < 4; ++q)
+                                w[q] = (uint32_t)__half_as_ushort(src[2 * q]) |
+                                       ((uint32_t)__half_as_ushort(src[2 * q + 1]) << 16);
+                            store_row_elems(p.C, p.epi, gm, gn, p.N, w, lim);
+                        }
+                        continue;
+                    }
+                }
                 __half* out = reinterpret_cast<__half*>(p.C) + (size_t)gm * p.N + gn;
                 if (vec_ok) {
                     *reinterpret_cast<uint4*>(out) = *reinterpret_cast<const uint4*>(src);
