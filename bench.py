@@ -861,6 +861,47 @@ def run_config4(torch, dist, spmm24, dev, rank, world, args):
         for p in imported:
             spmm24.ipc_close(p)
         dist.barrier()
+    # The same gather with every output chunk stored once through the full
+    # C's NVLink multicast address (a symmetric-memory buffer bound to every
+    # rank; multimem.st, replicated by the switch): a rank sends its shard
+    # once instead of once per peer.
+    us_mc = None
+    if world > 1:
+        try:
+            import torch.distributed._symmetric_memory as symm_mem
+
+            grp = dist.group.WORLD
+            mfull = symm_mem.empty((full_elems,), dtype=torch.float16, device=dev)
+            mh = symm_mem.rendezvous(mfull, grp)
+            mflags = symm_mem.empty((world + 1,), dtype=torch.int32, device=dev)
+            mflags.zero_()
+            fh = symm_mem.rendezvous(mflags, grp)
+            torch.cuda.synchronize(dev)
+            dist.barrier()
+            if mh.multicast_ptr:
+                moff = mfull.data_ptr() - mh.buffer_ptrs[rank]
+                mbases = [mh.buffer_ptrs[r] + moff for r in range(world)]
+                mcast = mh.multicast_ptr + moff
+                foff = mflags.data_ptr() - fh.buffer_ptrs[rank]
+                mflag_ptrs = [fh.buffer_ptrs[r] + foff for r in range(world)]
+
+                def gathered_mc():
+                    off = 0
+                    for c in calls:
+                        rc = spmm24.launch_gather(h, c["A"], c["B"], c["E"], c["M"], c["N"], c["K"],
+                                                  [b + 2 * off for b in mbases], c["r0"], c["M_full"], 0, fl,
+                                                  c_multicast=mcast + 2 * off)
+                        off += c["M_full"] * c["N"]
+                        if rc != 0:
+                            raise RuntimeError(f"spmm24_launch_gather: {rc} {spmm24._lib.spmm24_last_error().decode()}")
+                    if spmm24.gather_barrier(h, mflag_ptrs, rank, 0) != 0:
+                        raise RuntimeError("spmm24_gather_barrier failed")
+
+                us_mc = timed(gathered_mc)
+                status |= spmm24.device_status(dev.index)
+            dist.barrier()
+        except Exception as e:  # noqa: BLE001 -- report, keep the other numbers
+            us_mc = f"unavailable: {str(e)[:120]}"
     flop = sum(flops(M, N, K) for (M, K) in layers_mk for N in ns)
     recv = 2 * full_elems * (world - 1) / world
     bound_us = recv / 770e9 * 1e6
@@ -875,6 +916,8 @@ def run_config4(torch, dist, spmm24, dev, rank, world, args):
             "us_per_step_gathered": round(us_gather, 2),
             "tflops_gathered": round(flop / (us_gather * 1e-6) / 1e12, 1),
             "gather_share": round(max(0.0, us_gather - us_shards) / us_gather, 4),
+            "us_per_step_gathered_multicast": round(us_mc, 2) if isinstance(us_mc, float) else us_mc,
+            "tflops_gathered_multicast": round(flop / (us_mc * 1e-6) / 1e12, 1) if isinstance(us_mc, float) else None,
             "gathered_bytes_per_step": 2 * full_elems,
             "nvlink_receive_bound_us": round(bound_us, 2) if world > 1 else None,
             "compute_bound_us": round(compute_us, 2),
