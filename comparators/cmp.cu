@@ -393,3 +393,172 @@ extern "C" double cmp_stage_probe_us(int n_tile, int two_acc, int stages) {
     if (e != cudaSuccess || st != 0) return -4;
     return (double)ms * 1e3 / stages;
 }
+
+// ------------------------------------------------------------------------
+// TMA load-rate probe: one CTA per SM streams 16 KB boxes through rings of
+// four slots, one ring per issuing warp (the consumer only re-arms the slot; no MMA), from a buffer small
+// enough to stay in L2 (src_bytes = 4 MB) or large enough to come from HBM
+// (src_bytes >= 1 GB), for box geometries that move the same 16 KB:
+//   0  the compressed-A box of the SpMM kernels: 3-D {128 halves, 8 bands
+//      16*K bytes apart, 8 blocks 256 B apart} (64 rows of 256 B, hopping
+//      between bands)
+//   1  2-D {128 halves, 64 rows} over contiguous rows (64 rows of 256 B)
+//   2  2-D {256 halves, 32 rows} contiguous (32 rows of 512 B)
+//   3  2-D {64 halves, 128 rows} contiguous (128 rows of 128 B)
+//   4  as 3 with the 128-byte swizzle (the usual GEMM operand box)
+//   5  the same 16 KB chunks by plain 16-byte loads, 256 threads, no TMA
+// on `ctas` CTAs (0: one per SM).  Reports GB/s per CTA, one CTA per SM.
+namespace {
+using TmapEncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+constexpr int kTmaMaxSlots = 12;
+constexpr int kTmaBox = 16384;
+
+// `producers` warps (1..3) issue; warp w's lane 0 owns slots 4w..4w+3 and
+// the boxes it = w, w + producers, ...; all index arithmetic is incremental.
+__global__ void __launch_bounds__(96, 1) cmp_tma_probe_kernel(const __grid_constant__ CUtensorMap tm, int variant,
+                                                             int iters, int n_boxes, int producers, uint32_t* status) {
+    using namespace spmm24;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    __shared__ uint64_t full[kTmaMaxSlots];
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < 4 * producers; ++s) ptx::mbar_init(&full[s], 1);
+        ptx::fence_mbarrier_init();
+        ptx::prefetch_tmap(&tm);
+    }
+    __syncthreads();
+    const int w = threadIdx.x / 32;
+    if ((threadIdx.x & 31) != 0 || w >= producers) return;
+    const uint64_t pol = ptx::policy_evict_first();
+    const int bg = n_boxes / 32;  // variant 0: band groups (x 32 block groups)
+    const int mine = (iters - w + producers - 1) / producers;
+    int box = (int)(((long long)blockIdx.x * 7919 + w) % n_boxes);
+    auto issue = [&](int j) {
+        uint64_t* bar = &full[4 * w + (j & 3)];
+        uint8_t* dst = smem + (4 * w + (j & 3)) * kTmaBox;
+        ptx::mbar_arrive_expect_tx(bar, kTmaBox);
+        switch (variant) {
+            case 0: ptx::tma_load_3d(dst, &tm, bar, 0, (box % bg) * 8, (box / bg) * 8, pol); break;
+            case 1: ptx::tma_load_2d(dst, &tm, bar, 0, box * 64, pol); break;
+            case 2: ptx::tma_load_2d(dst, &tm, bar, 0, box * 32, pol); break;
+            default: ptx::tma_load_2d(dst, &tm, bar, 0, box * 128, pol); break;
+        }
+        box += producers;
+        if (box >= n_boxes) box -= n_boxes;
+    };
+    for (int j = 0; j < 4 && j < mine; ++j) issue(j);
+    for (int j = 0; j < mine; ++j) {
+        if (!ptx::mbar_wait_bounded(&full[4 * w + (j & 3)], (uint32_t)(j >> 2) & 1u, kWaitLimitNs)) {
+            atomicOr(status, 1u);
+            // let the copies still in flight land (each wait bounded) before the warp exits
+            for (int k = j + 1; k < j + 4 && k < mine; ++k)
+                ptx::mbar_wait_bounded(&full[4 * w + (k & 3)], (uint32_t)(k >> 2) & 1u, kWaitLimitNs);
+            return;
+        }
+        if (j + 4 < mine) issue(j + 4);
+    }
+}
+
+// Variant 5: the same 16 KB chunks read with plain 16-byte loads by 256
+// threads (four chunks in flight per CTA), no TMA.
+__global__ void __launch_bounds__(256, 1) cmp_ldg_probe_kernel(const uint4* __restrict__ src, int n_chunks, int iters,
+                                                              uint32_t* sink) {
+    uint32_t acc = 0;
+    for (int it = 0; it < iters; it += 4) {
+        uint4 v[4][4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int chunk = (blockIdx.x * 7919 + it + u) % n_chunks;
+            const uint4* c = src + (size_t)chunk * (kTmaBox / 16);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) v[u][j] = __ldcs(c + threadIdx.x + 256 * j);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) acc ^= v[u][j].x ^ v[u][j].y ^ v[u][j].z ^ v[u][j].w;
+    }
+    if (acc == 0x9e3779b9u) sink[0] = acc;  // keeps the loads; the source is zero so never taken
+}
+}  // namespace
+
+extern "C" double cmp_tma_probe_gbs_per_sm(int variant, long long src_bytes, int iters, int producers, int ctas) {
+    if (producers < 1 || 4 * producers > kTmaMaxSlots || variant < 0 || variant > 5) return -1;
+    static TmapEncodeFn enc = nullptr;
+    if (!enc) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return -1;
+        enc = reinterpret_cast<TmapEncodeFn>(p);
+    }
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    void* buf = nullptr;
+    if (cudaMalloc(&buf, (size_t)src_bytes) != cudaSuccess) return -2;
+    cudaMemset(buf, 0, (size_t)src_bytes);
+    CUtensorMap tm;
+    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    CUresult r = CUDA_SUCCESS;
+    int n_boxes = 0;
+    if (variant == 5) {
+        n_boxes = (int)(src_bytes / kTmaBox);
+    } else if (variant == 0) {
+        // A of K = 4096 (16*K = 64 KB between bands): bands = src / 64 KB, boxes of 8 bands x 8 blocks
+        const long long K = 4096, bands = src_bytes / (16 * K) / 8 * 8;
+        cuuint64_t dims[3] = {128, (cuuint64_t)bands, (cuuint64_t)(K / 16)};
+        cuuint64_t str[2] = {(cuuint64_t)(16 * K), 256};
+        cuuint32_t box[3] = {128, 8, 8};
+        r = enc(&tm, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, buf, dims, str, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        n_boxes = (int)((bands / 8) * 32);  // band groups x (K/16)/8 = 32 block groups
+    } else {
+        const int inner = variant == 2 ? 256 : variant == 1 ? 128 : 64;  // halves
+        const long long row_bytes = 2LL * inner, rows = src_bytes / row_bytes;
+        const int box_rows = kTmaBox / (int)row_bytes;
+        cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
+        cuuint64_t str[1] = {(cuuint64_t)row_bytes};
+        cuuint32_t box[2] = {(cuuint32_t)inner, (cuuint32_t)box_rows};
+        r = enc(&tm, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, buf, dims, str, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                variant == 4 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        n_boxes = (int)(rows / box_rows);
+    }
+    if (r != CUDA_SUCCESS || n_boxes < 1) {
+        cudaFree(buf);
+        return -3;
+    }
+    const int smem = 4 * producers * kTmaBox + 1024;
+    cudaFuncSetAttribute(cmp_tma_probe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    uint32_t* status = nullptr;
+    cudaMalloc(&status, 4);
+    cudaMemset(status, 0, 4);
+    cudaEvent_t e0, e1;
+    cudaEventCreate(&e0);
+    cudaEventCreate(&e1);
+    const int grid = ctas > 0 && ctas < sms ? ctas : sms;
+    for (int rep = 0; rep < 2; ++rep) {  // the first launch warms up
+        const int n = rep ? iters : iters / 8 / 4 * 4;
+        if (rep) cudaEventRecord(e0);
+        if (variant == 5)
+            cmp_ldg_probe_kernel<<<grid, 256>>>(static_cast<const uint4*>(buf), n_boxes, n, status);
+        else
+            cmp_tma_probe_kernel<<<grid, 96, smem>>>(tm, variant, n, n_boxes, producers, status);
+    }
+    cudaEventRecord(e1);
+    cudaError_t e = cudaEventSynchronize(e1);
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, e0, e1);
+    uint32_t st = 0;
+    cudaMemcpy(&st, status, 4, cudaMemcpyDeviceToHost);
+    cudaFree(status);
+    cudaFree(buf);
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    if (e != cudaSuccess || st) return -4;
+    return (double)iters * kTmaBox / (ms * 1e-3) / 1e9;  // per CTA (one CTA per SM)
+}

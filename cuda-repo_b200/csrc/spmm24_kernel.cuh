@@ -553,32 +553,43 @@ spmm24_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
     const uint64_t pol = ptx::policy_evict_last();  // A is re-read by every N tile, B by every M tile
     const uint32_t full0 = ptx::mapa_shared(ptx::smem_u32(&full[0]), lead_rank);
     const int pre = p.weights_static ? min(STAGES, st_count) : 0;
-    if (warp == 0) {
-        // ------------------------------------------------- TMA producer
+    // Two producers, one thread each, issue a stage's loads side by side
+    // (one issuing thread keeps only about 60-90 GB/s of boxes in flight per
+    // SM, below the 180 GB/s a stage needs to keep pace with the MMAs): warp
+    // 0 arms the leader's barrier and loads A and the metadata, warp 2 loads
+    // B.  Both wait on the same empty barrier and complete on the same full
+    // barrier.
+    if (warp == 0 || warp == 2) {
+        // ------------------------------------------------- TMA producers
+        const bool acts = warp == 2;
         if (lane == 0) {
-            for (int it = 0; it < pre; ++it) {
-                const int g = st_begin + it;
-                uint8_t* st = smem + it * C_::STAGE_BYTES;
-                if (leader) ptx::mbar_arrive_expect_tx(&full[it], 2 * C_::STAGE_BYTES);
-                pair_load_weights<C_>(st, &tmA, &tmE, full0 + 8u * it, band0, g, pol);
-            }
+            auto issue = [&](int it, int s) {
+                uint8_t* st = smem + s * C_::STAGE_BYTES;
+                const uint32_t bar = full0 + 8u * s;
+                if (acts)
+                    pair_load_acts<C_>(st, &tmB, bar, strip0, st_begin + it, pol);
+                else
+                    pair_load_weights<C_>(st, &tmA, &tmE, bar, band0, st_begin + it, pol);
+            };
+            if (!acts)
+                for (int it = 0; it < pre; ++it) {
+                    if (leader) ptx::mbar_arrive_expect_tx(&full[it], 2 * C_::STAGE_BYTES);
+                    issue(it, it);
+                }
             ptx::grid_dep_wait();
-            SPMM24_STAMP(1);
-            for (int it = 0; it < pre; ++it)
-                pair_load_acts<C_>(smem + it * C_::STAGE_BYTES, &tmB, full0 + 8u * it, strip0, st_begin + it, pol);
+            if (acts) {
+                SPMM24_STAMP(1);
+                for (int it = 0; it < pre; ++it) issue(it, it);
+            }
             for (int it = pre; it < st_count; ++it) {
                 const int s = it % STAGES;
-                const int g = st_begin + it;
                 const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
                 if (!ptx::mbar_wait_bounded(&empty[s], ph ^ 1u, kWaitLimitNs)) {
                     atomicOr(&g_spmm24_status, kStatusProducerTimeout);
                     break;
                 }
-                uint8_t* st = smem + s * C_::STAGE_BYTES;
-                const uint32_t bar = full0 + 8u * s;
-                if (leader) ptx::mbar_arrive_expect_tx(&full[s], 2 * C_::STAGE_BYTES);
-                pair_load_weights<C_>(st, &tmA, &tmE, bar, band0, g, pol);
-                pair_load_acts<C_>(st, &tmB, bar, strip0, g, pol);
+                if (!acts && leader) ptx::mbar_arrive_expect_tx(&full[s], 2 * C_::STAGE_BYTES);
+                issue(it, s);
             }
         }
         __syncwarp();
@@ -1020,17 +1031,15 @@ spmm24_pair2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     const uint64_t pol = ptx::policy_evict_last();
     const uint32_t full0 = ptx::mapa_shared(ptx::smem_u32(&full[0]), 0u);
     const int pre = p.weights_static ? min(STAGES, st_count) : 0;
-    auto load_weights = [&](uint8_t* st, uint32_t bar, int g) {
-        ptx::tma_load_3d_pair(st, &tmA, bar, 0, band_h0, 8 * g, pol);
-        ptx::tma_load_3d_pair(st + C_::A_HALF, &tmA, bar, 0, band_h1, 8 * g, pol);
-        uint8_t* se = st + C_::A_BYTES + C_::B_BYTES;
-        if constexpr (FP8) {  // box (256 B, 8 bands, 2 groups) per half
-            ptx::tma_load_3d_pair(se, &tmE, bar, 0, band_h0, 2 * g, pol);
-            ptx::tma_load_3d_pair(se + C_::E_HALF, &tmE, bar, 0, band_h1, 2 * g, pol);
-        } else {
-            ptx::tma_load_2d_pair(se, &tmE, bar, 128 * g, band_h0, pol);
-            ptx::tma_load_2d_pair(se + C_::E_HALF, &tmE, bar, 128 * g, band_h1, pol);
-        }
+    // One M half's A and metadata (h = 0, 1).
+    auto load_weights = [&](uint8_t* st, uint32_t bar, int g, int h) {
+        const int band = h ? band_h1 : band_h0;
+        ptx::tma_load_3d_pair(st + h * C_::A_HALF, &tmA, bar, 0, band, 8 * g, pol);
+        uint8_t* se = st + C_::A_BYTES + C_::B_BYTES + h * C_::E_HALF;
+        if constexpr (FP8)  // box (256 B, 8 bands, 2 groups)
+            ptx::tma_load_3d_pair(se, &tmE, bar, 0, band, 2 * g, pol);
+        else
+            ptx::tma_load_2d_pair(se, &tmE, bar, 128 * g, band, pol);
     };
     auto load_acts = [&](uint8_t* st, uint32_t bar, int g) {
         if constexpr (FP8) {
@@ -1040,16 +1049,34 @@ spmm24_pair2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             ptx::tma_load_4d_pair(st + C_::A_BYTES, &tmB, bar, 0, 2 * g, 0, strip0, pol);
         }
     };
-    if (warp == 0) {
-        // ------------------------------------------------- TMA producer
+    // Three producers, one thread each, issue a stage's loads side by side
+    // (one issuing thread keeps only about 60-90 GB/s of boxes in flight per
+    // SM, below the 127 GB/s a stage needs to keep pace with the MMAs):
+    // warp 0 arms the leader's barrier and loads M half 0's A and metadata,
+    // warp 2 M half 1's, warp 3 B.  All three wait on the same empty barrier
+    // and complete on the same full barrier.
+    const int role = warp == 0 ? 0 : warp == 2 ? 1 : warp == 3 ? 2 : -1;
+    if (role >= 0) {
+        // ------------------------------------------------- TMA producers
         if (lane == 0) {
-            for (int it = 0; it < pre; ++it) {
-                if (leader) ptx::mbar_arrive_expect_tx(&full[it], 2 * C_::STAGE_BYTES);
-                load_weights(smem + it * C_::STAGE_BYTES, full0 + 8u * it, it);
-            }
+            auto issue = [&](int it, int s) {
+                uint8_t* st = smem + s * C_::STAGE_BYTES;
+                const uint32_t bar = full0 + 8u * s;
+                if (role == 2)
+                    load_acts(st, bar, it);
+                else
+                    load_weights(st, bar, it, role);
+            };
+            if (role < 2)
+                for (int it = 0; it < pre; ++it) {
+                    if (role == 0 && leader) ptx::mbar_arrive_expect_tx(&full[it], 2 * C_::STAGE_BYTES);
+                    issue(it, it);
+                }
             ptx::grid_dep_wait();
-            SPMM24_STAMP(1);
-            for (int it = 0; it < pre; ++it) load_acts(smem + it * C_::STAGE_BYTES, full0 + 8u * it, it);
+            if (role == 2) {
+                SPMM24_STAMP(1);
+                for (int it = 0; it < pre; ++it) issue(it, it);
+            }
             for (int it = pre; it < st_count; ++it) {
                 const int s = it % STAGES;
                 const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
@@ -1057,11 +1084,8 @@ spmm24_pair2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                     atomicOr(&g_spmm24_status, kStatusProducerTimeout);
                     break;
                 }
-                uint8_t* st = smem + s * C_::STAGE_BYTES;
-                const uint32_t bar = full0 + 8u * s;
-                if (leader) ptx::mbar_arrive_expect_tx(&full[s], 2 * C_::STAGE_BYTES);
-                load_weights(st, bar, it);
-                load_acts(st, bar, it);
+                if (role == 0 && leader) ptx::mbar_arrive_expect_tx(&full[s], 2 * C_::STAGE_BYTES);
+                issue(it, s);
             }
         }
         __syncwarp();
