@@ -537,15 +537,20 @@ def run_ours(args, rank, world, local_rank):
     # sets alternate between steps, so step i's upload (its own stream)
     # overlaps step i-1's kernels and step i-1's download (another stream)
     # overlaps step i's; events order every reuse of a buffer.
-    # (gather mode: the result a rank downloads is its full C, every layer's
-    # rows from every rank)
+    # Gather mode: every rank holds the whole C of the step, and rank r
+    # downloads the r-th 1/N of it (one copy; together the ranks bring the
+    # whole C to the host once).
     out_sets = full_sets if gather_mode else None
-    host_out = [torch.empty((out_sets[0] if gather_mode else C_all).shape, dtype=torch.float16).pin_memory()
-                for _ in range(2)]
-    h2d = host_in.numel() * host_in.element_size()
-    d2h = host_out[0].numel() * 2
     B_set = [B_all, torch.empty_like(B_all)]
     C_set = out_sets if gather_mode else [C_all, torch.empty_like(C_all)]
+    if gather_mode:
+        ochunk = -(-C_set[0].numel() // world)
+        out_src = [C_set[k][rank * ochunk:(rank + 1) * ochunk] for k in range(2)]
+    else:
+        out_src = C_set
+    host_out = [torch.empty(out_src[0].shape, dtype=torch.float16).pin_memory() for _ in range(2)]
+    h2d = host_in.numel() * host_in.element_size()
+    d2h = host_out[0].numel() * 2
     call_sets = [calls, []]
     for c in calls:
         bs_, cs_ = c["B"].numel(), c["C"].numel()
@@ -585,7 +590,7 @@ def run_ours(args, rank, world, local_rank):
         comp_done[k].record(stream)
         with torch.cuda.stream(down):
             down.wait_event(comp_done[k])
-            host_out[k].copy_(C_set[k], non_blocking=True)
+            host_out[k].copy_(out_src[k], non_blocking=True)
             d2h_done[k].record(down)
         used[k] = True
 
@@ -686,8 +691,11 @@ def run_ours(args, rank, world, local_rank):
                 "ms_per_step": round(e2e_ms / args.steps, 5),
                 "path": ("per step: one H2D of all packed activations (pinned), the step's spmm24 calls" +
                          (" replayed as a CUDA graph" if graph is not None else "") +
-                         ", one D2H of all results (pinned); two buffer sets alternate so uploads and downloads "
-                         "overlap the neighbouring steps' kernels")},
+                         (", one D2H of the rank's 1/N share of the gathered C (pinned; the ranks together bring "
+                          "the whole C to the host once); h2d/d2h bytes are per rank" if gather_mode else
+                          ", one D2H of all results (pinned)") +
+                         "; two buffer sets alternate so uploads and downloads overlap the neighbouring steps' "
+                         "kernels")},
         "gpu_launches": nl,
         "clocks": clocks,
         "launch": ("grouped: one spmm24_launch_grouped per step (one persistent kernel for all the step's SpMMs)"
