@@ -753,7 +753,7 @@ struct GroupCache {
     int sms = 0;
     int n_ctas = 0;
     bool epi = false;    // some problem has a non-plain epilogue
-    bool split = false;  // tiles split over CTA pairs (n_ctas then counts pairs)
+    int split = 1;       // CTAs per tile along K: 1, 2 or 4 (n_ctas then counts clusters)
     int tuned = 0;       // the group_split tuning the schedule was built under
     GroupParams params;
 };
@@ -795,8 +795,8 @@ cudaError_t encode_group_maps(const spmm24_problem& q, bool fp8, GroupParams& gp
     return cudaSuccess;
 }
 
-cudaError_t build_group(const spmm24_problem* probs, int count, unsigned flags, bool fp8, int sms, GroupParams& gp,
-                        int& n_ctas, bool& any_epi, bool& split) {
+cudaError_t build_group(const spmm24_problem* probs, int count, unsigned flags, bool fp8, int sms, int max_clusters4,
+                        GroupParams& gp, int& n_ctas, bool& any_epi, int& split) {
     std::memset(&gp, 0, sizeof(gp));
     struct Tile {
         int cost, prob, m_tile;
@@ -828,23 +828,27 @@ cudaError_t build_group(const spmm24_problem* probs, int count, unsigned flags, 
         for (int m = 0; m < mt; ++m) tiles.push_back({st + 1, i, m});
         if ((e = encode_group_maps(q, fp8, gp, i)) != cudaSuccess) return e;
     }
-    // Two schedules: whole tiles on one CTA per SM, or (K split) tiles on CTA
-    // pairs with half the stages each; the split is taken when it shortens
-    // the busiest unit's work by more than a tenth (its ring is one or two
-    // stages shallower and each tile pays a partial-sum exchange), or when
-    // the caller's tuning asks for it.
+    // Three schedules: whole tiles on one CTA per SM, or (K split) tiles on
+    // clusters of 2 or 4 CTAs with a half or a quarter of the stages each; a
+    // split is taken when it shortens the busiest unit's work by more than a
+    // tenth against the best schedule with less split (its ring is shallower
+    // and each tile pays a partial-sum exchange), or when the caller's
+    // tuning asks for it.  Few tiles of unequal K (a sharded decode step)
+    // balance over the SMs only in quarters.
     struct Sched {
         int units = 0;
         long long makespan = 0;
         std::vector<std::vector<uint16_t>> lists;
     };
-    auto lpt = [&](int max_units, bool halve) {
+    auto lpt = [&](int max_units, int parts) {
         Sched sc;
         std::vector<Tile> ts = tiles;
-        // cost = stages + 1 (the epilogue); halved: ceil(stages / 2) + 1
-        for (Tile& t : ts) t.cost = halve ? t.cost / 2 + 1 : t.cost;
+        // cost = stages + 1 (the epilogue); split in `parts`: ceil(stages / parts)
+        // + 1, + 1 more for the four-way exchange
+        for (Tile& t : ts)
+            if (parts > 1) t.cost = (t.cost - 1 + parts - 1) / parts + (parts > 2 ? 2 : 1);
         std::stable_sort(ts.begin(), ts.end(), [](const Tile& a, const Tile& b) { return a.cost > b.cost; });
-        sc.units = (int)std::min<size_t>((size_t)max_units, ts.size());
+        sc.units = (int)std::min<size_t>((size_t)std::max(1, max_units), ts.size());
         std::vector<long long> load(sc.units, 0);
         sc.lists.assign(sc.units, {});
         for (const Tile& t : ts) {
@@ -858,10 +862,22 @@ cudaError_t build_group(const spmm24_problem* probs, int count, unsigned flags, 
         return sc;
     };
     const int cap = std::min(sms, kGroupMaxCtas);
-    Sched whole = lpt(cap, false), halves = lpt(cap / 2, true);
+    Sched whole = lpt(cap, 1), halves = lpt(cap / 2, 2);
+    const int c4 = std::min(cap / 4, max_clusters4);
+    Sched quarters = lpt(c4, 4);
     const int forced = g_tune.group_split.load(std::memory_order_relaxed);
-    split = forced == 2 || (forced == 0 && cap >= 2 && 10 * halves.makespan < 9 * whole.makespan);
-    Sched& sc = split ? halves : whole;
+    if (forced == 1 || forced == 2 || forced == 4) {
+        split = forced;
+    } else {
+        split = 1;
+        long long best = whole.makespan;
+        if (cap >= 2 && 10 * halves.makespan < 9 * best) {
+            split = 2;
+            best = halves.makespan;
+        }
+        if (c4 >= 1 && 10 * quarters.makespan < 9 * best) split = 4;
+    }
+    Sched& sc = split == 4 ? quarters : split == 2 ? halves : whole;
     n_ctas = sc.units;  // CTAs, or CTA pairs with the split
     int off = 0;
     for (int c = 0; c < n_ctas; ++c) {
@@ -876,12 +892,57 @@ cudaError_t build_group(const spmm24_problem* probs, int count, unsigned flags, 
     return cudaSuccess;
 }
 
+template <bool FP8, int SPLIT>
+constexpr int group_stages() {
+    return SPLIT == 4 ? kGroupSplit4Stages : SPLIT == 2 ? (FP8 ? kGroupSplitStagesFp8 : kGroupSplitStages) : kGroupStages;
+}
+
+template <bool EPI, bool FP8, int SPLIT>
+cudaError_t prepare_group_kernel(int dev) {
+    constexpr int ST = group_stages<FP8, SPLIT>();
+    return prepare(spmm24_grouped_kernel<ST, EPI, FP8, SPLIT>, GroupCfg<ST, FP8, SPLIT>::SMEM_ALLOC, dev,
+                   80 + (EPI ? 1 : 0) + (FP8 ? 2 : 0) + (SPLIT == 2 ? 4 : SPLIT == 4 ? 8 : 0));
+}
+
+// Clusters of four grouped CTAs that fit on the device at once (a GPC whose
+// SM count is not a multiple of four leaves SMs idle), cached per device;
+// 0 if the query fails (no four-way split then).
+int group_max_clusters4(int dev, bool fp8) {
+    static std::atomic<int> cache[2][64];
+    std::atomic<int>& slot = cache[fp8 ? 1 : 0][dev & 63];
+    int v = slot.load(std::memory_order_relaxed);
+    if (v) return v - 1;
+    constexpr int ST16 = group_stages<false, 4>(), ST8 = group_stages<true, 4>();
+    cudaError_t e = fp8 ? prepare_group_kernel<true, true, 4>(dev) : prepare_group_kernel<false, false, 4>(dev);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(4 * 64, 1, 1);
+    cfg.blockDim = dim3((unsigned)kThreads, 1, 1);
+    cfg.dynamicSmemBytes = fp8 ? GroupCfg<ST8, true, 4>::SMEM_ALLOC : GroupCfg<ST16, false, 4>::SMEM_ALLOC;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 4;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (e == cudaSuccess)
+        e = fp8 ? cudaOccupancyMaxActiveClusters(&n, spmm24_grouped_kernel<ST8, true, true, 4>, &cfg)
+                : cudaOccupancyMaxActiveClusters(&n, spmm24_grouped_kernel<ST16, false, false, 4>, &cfg);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        n = 0;
+    }
+    slot.store(n + 1, std::memory_order_relaxed);
+    return n;
+}
+
 template <bool EPI, bool FP8, int SPLIT>
 cudaError_t launch_group_kernel(cudaStream_t stream, int dev, const GroupCache& gc, unsigned flags) {
-    constexpr int ST = SPLIT > 1 ? (FP8 ? kGroupSplitStagesFp8 : kGroupSplitStages) : kGroupStages;
+    constexpr int ST = group_stages<FP8, SPLIT>();
     using GC = GroupCfg<ST, FP8, SPLIT>;
     auto kern = spmm24_grouped_kernel<ST, EPI, FP8, SPLIT>;
-    cudaError_t e = prepare(kern, GC::SMEM_ALLOC, dev, 80 + (EPI ? 1 : 0) + (FP8 ? 2 : 0) + (SPLIT > 1 ? 4 : 0));
+    cudaError_t e = prepare_group_kernel<EPI, FP8, SPLIT>(dev);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(gc.n_ctas * SPLIT), 1, 1);
@@ -977,9 +1038,11 @@ cudaError_t launch_grouped_impl(cudaStream_t stream, const spmm24_problem* probs
     const bool hit = gc.n_ctas > 0 && gc.flags == flags && gc.sms == sms && gc.tuned == tuned && gc.key == key;
     if (!hit) {
         gc.n_ctas = 0;
-        int n = 0;
-        bool any_epi = false, split = false;
-        if ((e = build_group(probs, count, flags, fp8, sms, gc.params, n, any_epi, split)) != cudaSuccess) return e;
+        int n = 0, split = 1;
+        bool any_epi = false;
+        if ((e = build_group(probs, count, flags, fp8, sms, group_max_clusters4(dev, fp8), gc.params, n, any_epi,
+                             split)) != cudaSuccess)
+            return e;
         gc.key = key;
         gc.flags = flags;
         gc.sms = sms;
@@ -997,7 +1060,12 @@ cudaError_t launch_grouped_impl(cudaStream_t stream, const spmm24_problem* probs
 #ifdef SPMM24_TRACE
     gc.params.trace_base = g_trace_next.fetch_add((long long)gc.n_ctas);
 #endif
-    if (gc.split) {
+    if (gc.split == 4) {
+        if (fp8) return launch_group_kernel<true, true, 4>(stream, dev, gc, flags);
+        if (gc.epi) return launch_group_kernel<true, false, 4>(stream, dev, gc, flags);
+        return launch_group_kernel<false, false, 4>(stream, dev, gc, flags);
+    }
+    if (gc.split == 2) {
         if (fp8) return launch_group_kernel<true, true, 2>(stream, dev, gc, flags);
         if (gc.epi) return launch_group_kernel<true, false, 2>(stream, dev, gc, flags);
         return launch_group_kernel<false, false, 2>(stream, dev, gc, flags);
@@ -1361,7 +1429,7 @@ extern "C" cudaError_t spmm24_set_tuning(const spmm24_tuning* t) {
         const bool tn_ok = v.tile_n == 0 || v.tile_n == 16 || v.tile_n == 32 || v.tile_n == 64 || v.tile_n == 128 ||
                            v.tile_n == 256;
         if (v.pair < -1 || v.pair > 1 || v.pair2 < -1 || v.pair2 > 1 || v.pair_split < 0 || v.pair_split > 2 || !tn_ok ||
-            v.deep_ring < 0 || v.deep_ring > 1 || v.group_split < 0 || v.group_split > 2)
+            v.deep_ring < 0 || v.deep_ring > 1 || v.group_split < 0 || v.group_split > 4 || v.group_split == 3)
             return spmm24::record_invalid("tuning: a field is out of range");
     }
     spmm24::g_tune.pair.store(v.pair);

@@ -36,14 +36,16 @@ constexpr int kGroupMaxTiles = 2048;  // schedule entries (128-row tiles) per la
 constexpr int kGroupMaxCtas = 160;
 constexpr int kGroupTileN = 32;       // N <= 32: columns of B past N are zero-filled by TMA, never fetched
 constexpr int kGroupStages = 8;
-// K split in two (SPLIT = 2, for groups with fewer tiles than SMs): a
-// cluster of two CTAs takes each tile, one half of its K stages each; the
-// second CTA pushes its fp32 partial (128 x 32) into a receive slot of the
-// first through distributed shared memory, which adds it before the
-// epilogue.  Two slots alternate, like the accumulators; the ring gives up
-// one (fp8: two) stage for them.
+// K split (SPLIT = 2 or 4, for groups with fewer tiles than SMs): a cluster
+// of SPLIT CTAs takes each tile, one share of its K stages each; CTAs 1 ..
+// SPLIT-1 push their fp32 partials (128 x 32) into receive slots of CTA 0
+// through distributed shared memory, which adds them, in rank order, before
+// the epilogue.  Each pushing CTA has two slots that alternate, like the
+// accumulators; the ring gives up stages for them (SPLIT = 2: one, fp8 two;
+// SPLIT = 4: four, fp8 four).
 constexpr int kGroupSplitStages = 7;
 constexpr int kGroupSplitStagesFp8 = 6;
+constexpr int kGroupSplit4Stages = 4;
 constexpr int kGroupRecvPitch = kGroupTileN + 4;  // floats per received row (16-byte reads free of bank conflicts)
 
 struct GroupProblem {
@@ -75,7 +77,7 @@ struct GroupParams {
     uint32_t* bar_flags[kMaxGatherRanks];
     int bar_n, bar_rank;
     unsigned long long bar_limit_ns;
-    // CTA c (SPLIT = 2: cluster c) processes sched[sched_off[c] ..
+    // CTA c (SPLIT > 1: cluster c) processes sched[sched_off[c] ..
     // sched_off[c + 1]); an entry is (problem << 12) | m_tile.
     uint16_t sched_off[kGroupMaxCtas + 1];
     uint16_t sched[kGroupMaxTiles];
@@ -87,11 +89,11 @@ struct GroupCfg : Cfg<kGroupTileN, STAGES, 2, FP8> {
     using B_ = Cfg<kGroupTileN, STAGES, 2, FP8>;
     static constexpr int RECV_OFFSET = B_::RING_BYTES;
     static constexpr int RECV_SLOT_BYTES = kTileM * kGroupRecvPitch * 4;
-    static constexpr int RECV_BYTES = SPLIT > 1 ? 2 * RECV_SLOT_BYTES : 0;
+    static constexpr int RECV_BYTES = (SPLIT - 1) * 2 * RECV_SLOT_BYTES;  // two slots per pushing CTA
     static constexpr uint32_t PARTIAL_BYTES = (uint32_t)kTileM * kGroupTileN * 4;  // pushed per tile
     static constexpr int BAR_OFFSET = RECV_OFFSET + RECV_BYTES;
-    // full, empty, acc_full[2], acc_empty[2], recv_full[2], slot_free[2], slot_read[2]
-    static constexpr int NUM_BARS = 2 * STAGES + 10;
+    // full, empty, acc_full[2], acc_empty[2], recv_full[2 (SPLIT - 1)], slot_free[2], slot_read[2]
+    static constexpr int NUM_BARS = 2 * STAGES + 8 + 2 * (SPLIT > 1 ? SPLIT - 1 : 1);
     static constexpr int HOLDER_OFFSET = BAR_OFFSET + NUM_BARS * 8;
     static constexpr int SMEM_BYTES = HOLDER_OFFSET + 16;
     static constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;  // slack to align the base to 1024 B
@@ -132,23 +134,19 @@ __device__ __forceinline__ void group_store_row(uint16_t* out, uint16_t* mc, int
 }
 
 // This CTA's share [lo, hi) of a tile's `n` stages: all of them, or (K split)
-// the first ceil(n / 2) for cluster rank 0 and the rest for rank 1.
+// n / SPLIT each, the first n % SPLIT ranks one more (the partition of the
+// cluster kernel's split-K, so both add the same partial sums).
 template <int SPLIT>
 __device__ __forceinline__ void group_share(int n, int rank, int& lo, int& hi) {
-    if (SPLIT == 1) {
-        lo = 0;
-        hi = n;
-    } else {
-        const int h = (n + 1) / 2;
-        lo = rank ? h : 0;
-        hi = rank ? n : h;
-    }
+    const int base = n / SPLIT, rem = n % SPLIT;
+    lo = rank * base + min(rank, rem);
+    hi = lo + base + (rank < rem ? 1 : 0);
 }
 
 template <int STAGES, bool EPI = false, bool FP8 = false, int SPLIT = 1>
 __global__ void __launch_bounds__(kThreads, 1) spmm24_grouped_kernel(const __grid_constant__ GroupParams p) {
     static_assert(EPI || !FP8, "the fp8 grouped kernel always runs the general epilogue");
-    static_assert(SPLIT == 1 || SPLIT == 2, "K split in one or two");
+    static_assert(SPLIT == 1 || SPLIT == 2 || SPLIT == 4, "K split in one, two or four");
     using C_ = GroupCfg<STAGES, FP8, SPLIT>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -156,16 +154,17 @@ __global__ void __launch_bounds__(kThreads, 1) spmm24_grouped_kernel(const __gri
     uint64_t* empty = full + STAGES;
     uint64_t* acc_full = empty + STAGES;  // [2]
     uint64_t* acc_empty = acc_full + 2;   // [2]
-    uint64_t* recv_full = acc_empty + 2;  // [2] rank 0 of a split: the partner's partial of slot b has arrived
-    uint64_t* slot_free = recv_full + 2;  // [2] rank 1 of a split: rank 0 has read slot b
-    uint64_t* slot_read = slot_free + 2;  // [2] rank 0 of a split: each epilogue warp has read its rows of slot b
-    float* recv = reinterpret_cast<float*>(smem + C_::RECV_OFFSET);  // [2][128][kGroupRecvPitch]
+    // rank 0 of a split: recv_full[2 q + b], the partial of rank q + 1 in its slot b has arrived
+    uint64_t* recv_full = acc_empty + 2;
+    uint64_t* slot_free = recv_full + 2 * (SPLIT > 1 ? SPLIT - 1 : 1);  // [2] ranks > 0: rank 0 has read slot b
+    uint64_t* slot_read = slot_free + 2;  // [2] rank 0: each epilogue warp has read its rows of every slot b
+    float* recv = reinterpret_cast<float*>(smem + C_::RECV_OFFSET);  // [SPLIT - 1][2][128][kGroupRecvPitch]
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + C_::HOLDER_OFFSET);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int rank = SPLIT > 1 ? (int)(ptx::cluster_ctarank() & 1u) : 0;
-    const int unit = SPLIT > 1 ? (int)blockIdx.x / 2 : (int)blockIdx.x;
+    const int rank = SPLIT > 1 ? (int)(ptx::cluster_ctarank() % (uint32_t)SPLIT) : 0;
+    const int unit = (int)blockIdx.x / SPLIT;
     const int t_begin = p.sched_off[unit];
     const int t_end = p.sched_off[unit + 1];
 
@@ -178,15 +177,17 @@ __global__ void __launch_bounds__(kThreads, 1) spmm24_grouped_kernel(const __gri
         for (int b = 0; b < 2; ++b) {
             ptx::mbar_init(&acc_full[b], 1);
             ptx::mbar_init(&acc_empty[b], kEpiThreads / 32);  // one arrival per epilogue warp
-            ptx::mbar_init(&recv_full[b], 1);
             ptx::mbar_init(&slot_free[b], 1);
             ptx::mbar_init(&slot_read[b], kEpiThreads / 32);
         }
+        for (int i = 0; i < 2 * (SPLIT > 1 ? SPLIT - 1 : 1); ++i) ptx::mbar_init(&recv_full[i], 1);
         // Rank 0 of a split arms the receive barriers of its first two tiles
-        // now, before the partner can push (the cluster barrier below); the
+        // now, before the partners can push (the cluster barrier below); the
         // next arm of slot b follows the read of slot b.
         if (SPLIT > 1 && rank == 0)
-            for (int b = 0; b < 2 && t_begin + b < t_end; ++b) ptx::mbar_arrive_expect_tx(&recv_full[b], C_::PARTIAL_BYTES);
+            for (int q = 0; q < SPLIT - 1; ++q)
+                for (int b = 0; b < 2 && t_begin + b < t_end; ++b)
+                    ptx::mbar_arrive_expect_tx(&recv_full[2 * q + b], C_::PARTIAL_BYTES);
         ptx::fence_mbarrier_init();
         for (int i = 0; i < p.n_problems; ++i) {
             ptx::prefetch_tmap(&p.tmA[i]);
@@ -195,7 +196,7 @@ __global__ void __launch_bounds__(kThreads, 1) spmm24_grouped_kernel(const __gri
         }
     }
     __syncthreads();
-    if (SPLIT > 1) ptx::cluster_sync();  // both CTAs' barriers are initialised (and armed)
+    if (SPLIT > 1) ptx::cluster_sync();  // every CTA's barriers are initialised (and armed)
     if (threadIdx.x == 0) ptx::grid_dep_launch();
 
     uint32_t tmem_base = 0;
@@ -347,7 +348,7 @@ __global__ void __launch_bounds__(kThreads, 1) spmm24_grouped_kernel(const __gri
                     v[i] = v0[i];
                     v[16 + i] = N > 16 ? v1[i] : 0u;
                 }
-            } else {  // a one-stage tile leaves rank 1 of a split without a share
+            } else {  // a tile of fewer stages than SPLIT leaves the last ranks without a share
 #pragma unroll
                 for (int i = 0; i < 32; ++i) v[i] = 0u;
             }
@@ -355,44 +356,54 @@ __global__ void __launch_bounds__(kThreads, 1) spmm24_grouped_kernel(const __gri
             __syncwarp();
             if (lane == 0) ptx::mbar_arrive(&acc_empty[b]);
             if constexpr (SPLIT > 1) {
-                float* slot = recv + (size_t)b * kTileM * kGroupRecvPitch;
-                if (rank == 1) {
-                    // push this row's partial into rank 0's slot b, once rank 0
-                    // has read what the slot held two tiles ago
+                if (rank > 0) {
+                    // push this row's partial into rank 0's slot (rank - 1, b),
+                    // once rank 0 has read what the slot held two tiles ago
                     if (j >= 2 && !ptx::mbar_wait_bounded(&slot_free[b], (uint32_t)((j >> 1) - 1) & 1u, kWaitLimitNs)) {
                         atomicOr(&g_spmm24_status, kStatusEpilogueTimeout);
                         break;
                     }
+                    const int q = 2 * (rank - 1) + b;
+                    float* slot = recv + (size_t)q * kTileM * kGroupRecvPitch;
                     const uint32_t dst = ptx::mapa_shared(ptx::smem_u32(slot + row * kGroupRecvPitch), 0u);
-                    const uint32_t bar = ptx::mapa_shared(ptx::smem_u32(&recv_full[b]), 0u);
+                    const uint32_t bar = ptx::mapa_shared(ptx::smem_u32(&recv_full[q]), 0u);
 #pragma unroll
-                    for (int q = 0; q < kGroupTileN / 4; ++q)
-                        ptx::st_async_v4(dst + 16u * q, __uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
-                                         __uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3]), bar);
+                    for (int c = 0; c < kGroupTileN / 4; ++c)
+                        ptx::st_async_v4(dst + 16u * c, __uint_as_float(v[4 * c]), __uint_as_float(v[4 * c + 1]),
+                                         __uint_as_float(v[4 * c + 2]), __uint_as_float(v[4 * c + 3]), bar);
                     continue;  // rank 0 finishes the tile
                 }
-                // rank 0: add the partner's partial (fixed order: own half of K first)
-                if (!ptx::mbar_wait_bounded(&recv_full[b], (uint32_t)(j >> 1) & 1u, kWaitLimitNs)) {
-                    atomicOr(&g_spmm24_status, kStatusEpilogueTimeout);
-                    break;
-                }
-                const float* r = slot + row * kGroupRecvPitch;
+                // rank 0: add the partners' partials (fixed order: own share of K
+                // first, then ranks 1, 2, ...)
+                bool got = true;
+                for (int r = 1; r < SPLIT && got; ++r) {
+                    const int q = 2 * (r - 1) + b;
+                    if (!ptx::mbar_wait_bounded(&recv_full[q], (uint32_t)(j >> 1) & 1u, kWaitLimitNs)) {
+                        atomicOr(&g_spmm24_status, kStatusEpilogueTimeout);
+                        got = false;
+                        break;
+                    }
+                    const float* rr = recv + ((size_t)q * kTileM + row) * kGroupRecvPitch;
 #pragma unroll
-                for (int q = 0; q < kGroupTileN / 4; ++q) {
-                    const float4 x = *reinterpret_cast<const float4*>(r + 4 * q);
-                    v[4 * q] = __float_as_uint(__uint_as_float(v[4 * q]) + x.x);
-                    v[4 * q + 1] = __float_as_uint(__uint_as_float(v[4 * q + 1]) + x.y);
-                    v[4 * q + 2] = __float_as_uint(__uint_as_float(v[4 * q + 2]) + x.z);
-                    v[4 * q + 3] = __float_as_uint(__uint_as_float(v[4 * q + 3]) + x.w);
+                    for (int c = 0; c < kGroupTileN / 4; ++c) {
+                        const float4 x = *reinterpret_cast<const float4*>(rr + 4 * c);
+                        v[4 * c] = __float_as_uint(__uint_as_float(v[4 * c]) + x.x);
+                        v[4 * c + 1] = __float_as_uint(__uint_as_float(v[4 * c + 1]) + x.y);
+                        v[4 * c + 2] = __float_as_uint(__uint_as_float(v[4 * c + 2]) + x.z);
+                        v[4 * c + 3] = __float_as_uint(__uint_as_float(v[4 * c + 3]) + x.w);
+                    }
                 }
+                if (!got) break;
                 __syncwarp();
-                if (lane == 0) ptx::mbar_arrive(&slot_read[b]);  // this warp's rows of slot b are read
+                if (lane == 0) ptx::mbar_arrive(&slot_read[b]);  // this warp's rows of every slot b are read
                 if (threadIdx.x == 64 && t_begin + j + 2 < t_end) {
                     // once every warp has read slot b: arm it for its next tile
-                    // and tell the partner it may push into it
+                    // and tell the partners they may push into it
                     if (ptx::mbar_wait_bounded(&slot_read[b], (uint32_t)(j >> 1) & 1u, kWaitLimitNs)) {
-                        ptx::mbar_arrive_expect_tx(&recv_full[b], C_::PARTIAL_BYTES);
-                        ptx::mbar_arrive_cluster(ptx::mapa_shared(ptx::smem_u32(&slot_free[b]), 1u));
+                        for (int r = 1; r < SPLIT; ++r) {
+                            ptx::mbar_arrive_expect_tx(&recv_full[2 * (r - 1) + b], C_::PARTIAL_BYTES);
+                            ptx::mbar_arrive_cluster(ptx::mapa_shared(ptx::smem_u32(&slot_free[b]), (uint32_t)r));
+                        }
                     } else {
                         atomicOr(&g_spmm24_status, kStatusEpilogueTimeout);
                     }
@@ -461,7 +472,7 @@ __global__ void __launch_bounds__(kThreads, 1) spmm24_grouped_kernel(const __gri
             }
         }
     }
-    if (SPLIT > 1) ptx::cluster_sync();  // no CTA leaves while its partner may still reach its shared memory
+    if (SPLIT > 1) ptx::cluster_sync();  // no CTA leaves while a partner may still reach its shared memory
     if (warp == 1) {
         ptx::tc_fence_after();
         ptx::tmem_dealloc(tmem_base, C_::TMEM_COLS);

@@ -91,9 +91,9 @@ cudaError_t spmm24_launch_ex(cudaStream_t stream, const void* compressed_a, cons
  * at the end of every call).  Each output is summed in one fp32
  * accumulator in increasing K (the result of spmm24_launch with
  * split_k = 1), except when the group has too few tiles to occupy the SMs:
- * then a pair of CTAs shares each tile, each summing one half of its K
- * stages, and the two halves are added in a fixed order (the result of
- * spmm24_launch with split_k = 2).  count: 1..16; at most 2048 tiles of
+ * then a cluster of 2 (or 4) CTAs shares each tile, each summing one share
+ * of its K stages, and the shares are added in a fixed order (the result of
+ * spmm24_launch with split_k = 2, or 4).  count: 1..16; at most 2048 tiles of
  * 128 rows in all; flags: SPMM24_STATIC_WEIGHTS, SPMM24_NO_PDL,
  * SPMM24_BF16.  Allocates nothing; the encoded launch is cached per host
  * thread and reused when the same problem array is launched again.
@@ -433,7 +433,7 @@ typedef struct spmm24_tuning {
     int pair_split; /* 0 auto; 1 or 2 K halves per pair tile */
     int tile_n;     /* 0 auto; 16, 32, 64, 128 or 256: the cluster kernel's tile width */
     int deep_ring;  /* 0 auto (a shallow ring, two CTAs per SM, for tile_n <= 32); 1 the deepest ring */
-    int group_split; /* grouped launches: 0 auto; 1 whole K per tile; 2 each tile's K split over a CTA pair */
+    int group_split; /* grouped launches: 0 auto; 1 whole K per tile; 2 or 4: each tile's K split over a cluster of 2 or 4 CTAs */
 } spmm24_tuning;
 cudaError_t spmm24_set_tuning(const spmm24_tuning* t);
 

@@ -213,7 +213,8 @@ def test_tuning_overrides_and_no_environment(monkeypatch):
         assert spmm24.select_config(1024, 512, 4096)["split_k"] == 2
         spmm24.set_tuning(deep_ring=1)
         assert spmm24.select_config(4096, 16, 4096)["stages"] == 8
-        for bad in ({"pair": 2}, {"pair2": -2}, {"pair_split": 3}, {"tile_n": 48}, {"deep_ring": 2}, {"group_split": 3}):
+        for bad in ({"pair": 2}, {"pair2": -2}, {"pair_split": 3}, {"tile_n": 48}, {"deep_ring": 2},
+                    {"group_split": 3}, {"group_split": 5}):
             with pytest.raises(ValueError, match="out of range"):
                 spmm24.set_tuning(**bad)
     finally:

@@ -62,11 +62,12 @@ SHAPES = [
 ]
 
 
-@pytest.mark.parametrize("group_split", [1, 2])
+@pytest.mark.parametrize("group_split", [1, 2, 4])
 def test_grouped_mixed_shapes(cuda_device, tuning, group_split):
-    """Whole tiles (group_split 1) or each tile's K over a CTA pair (2):
-    against the oracle, and bit for bit against spmm24_launch with split_k =
-    group_split (the same halves added in the same order)."""
+    """Whole tiles (group_split 1) or each tile's K over a cluster of 2 or 4
+    CTAs: against the oracle, and bit for bit against spmm24_launch with
+    split_k = group_split (the same K shares added in the same order; tiles
+    of fewer stages than CTAs leave the last CTAs without a share)."""
     tuning(group_split=group_split)
     probs = [make_problem(M, N, K, seed=3 * M + N + K, a_scale=0.05, b_dist="normal") for (M, N, K) in SHAPES]
     bufs, outs = _grouped(cuda_device, probs)
@@ -76,12 +77,12 @@ def test_grouped_mixed_shapes(cuda_device, tuning, group_split):
         assert np.array_equal(got, _single(cuda_device, p, b, group_split)), (p.M, p.N, p.K)
 
 
-@pytest.mark.parametrize("group_split", [0, 2])
+@pytest.mark.parametrize("group_split", [0, 2, 4])
 def test_grouped_many_tiles_per_cta(cuda_device, tuning, group_split):
-    """More tiles than SMs (630 here): every CTA (or CTA pair) walks several
+    """More tiles than SMs (630 here): every CTA (or cluster) walks several
     tiles of several problems and both TMEM accumulators (and both receive
-    slots) alternate; a second launch of the same problem array reuses the
-    cached launch and gives the same bits."""
+    slots of every pushing CTA) alternate; a second launch of the same
+    problem array reuses the cached launch and gives the same bits."""
     import spmm24
 
     tuning(group_split=group_split)
@@ -205,7 +206,7 @@ def test_grouped_cuda_graph(cuda_device):
         assert within_tolerance(compare(_bits(b["C"]), oracle_c(p)))
 
 
-@pytest.mark.parametrize("group_split", [1, 2])
+@pytest.mark.parametrize("group_split", [1, 2, 4])
 def test_grouped_epilogues_match_fused_launches(cuda_device, tuning, group_split):
     """Each problem of a group with its own epilogue (bias + SiLU, alpha +
     GELU, a residual, a packed-B output, none): bit for bit the results of
@@ -256,7 +257,7 @@ def test_grouped_epilogues_match_fused_launches(cuda_device, tuning, group_split
         assert spmm24.device_status(0) == 0
 
 
-@pytest.mark.parametrize("group_split", [1, 2])
+@pytest.mark.parametrize("group_split", [1, 2, 4])
 def test_grouped_fp8_matches_fp8_launches(cuda_device, tuning, group_split):
     """spmm24_launch_grouped_fp8: E4M3 and E5M2 operands, alpha per problem,
     bias / activation / residual / packed output: bit for bit the results of
