@@ -206,7 +206,10 @@ def _worker_grouped(rank, world, port, shapes):
         layers.append((M, N, K, A, E, bp))
         expects.append(torch.empty((M, N), dtype=torch.float16, device=dev))
         fulls.append(torch.full((M, N), float("nan"), dtype=torch.float16, device=dev))
-    # expected: every rank's shards of every layer, one grouped launch on this GPU
+    # expected: every rank's shards of every layer, one grouped launch on this
+    # GPU, with whole tiles (as the gathered launches below, whose fewer tiles
+    # would otherwise get another K split from the picker and other sums)
+    spmm24.set_tuning(group_split=1)
     local = []
     for (M, N, K, A, E, bp), ex in zip(layers, expects):
         for r in range(world):
@@ -267,31 +270,34 @@ def _worker_grouped(rank, world, port, shapes):
             assert torch.equal(f, ex), (rank, "graph", rep, shapes[i])
         dist.barrier()
     del graph
-    # the same with each tile's K split over a CTA pair (the mode a rank with
-    # fewer tiles than SMs gets: 4 and 8 GPUs on the decode step)
-    spmm24.set_tuning(group_split=2)
-    try:
-        arr2 = spmm24.problem_array(probs)
-        for f in fulls:
-            f.fill_(float("nan"))
-        torch.cuda.synchronize(dev)
-        dist.barrier()
-        assert spmm24.launch_grouped(s, arr2, spmm24.STATIC_WEIGHTS) == 0, spmm24._lib.spmm24_last_error().decode()
-        assert spmm24.gather_barrier(s, ptrs[-1], rank, 0) == 0
-        torch.cuda.synchronize(dev)
-        assert spmm24.device_status(rank) == 0
-        # expected with the split: every shard again, K in two halves
-        for (M, N, K, A, E, bp), ex, f in zip(layers, expects, fulls):
-            ex2 = torch.empty_like(ex)
-            for r in range(world):
-                r0, r1 = spmm24.shard_rows(M, world, r, 128)
-                Av, Ev = spmm24.shard_views(A, E, M, K, r0, r1)
-                assert spmm24.launch(None, Av, bp, Ev, ex2[r0:r1], r1 - r0, N, K, None, 2) == 0
+    # the same with each tile's K split over a cluster of 2 or 4 CTAs (the
+    # modes a rank with fewer tiles than SMs gets: 4 and 8 GPUs on the decode
+    # step)
+    for gsplit in (2, 4):
+        spmm24.set_tuning(group_split=gsplit)
+        try:
+            arr2 = spmm24.problem_array(probs)
+            for f in fulls:
+                f.fill_(float("nan"))
             torch.cuda.synchronize(dev)
-            assert torch.equal(f, ex2), (rank, "split", M, N, K)
-        dist.barrier()
-    finally:
-        spmm24.reset_tuning()
+            dist.barrier()
+            assert spmm24.launch_grouped(s, arr2, spmm24.STATIC_WEIGHTS) == 0, \
+                spmm24._lib.spmm24_last_error().decode()
+            assert spmm24.gather_barrier(s, ptrs[-1], rank, 0) == 0
+            torch.cuda.synchronize(dev)
+            assert spmm24.device_status(rank) == 0
+            # expected with the split: every shard again, K in gsplit shares
+            for (M, N, K, A, E, bp), ex, f in zip(layers, expects, fulls):
+                ex2 = torch.empty_like(ex)
+                for r in range(world):
+                    r0, r1 = spmm24.shard_rows(M, world, r, 128)
+                    Av, Ev = spmm24.shard_views(A, E, M, K, r0, r1)
+                    assert spmm24.launch(None, Av, bp, Ev, ex2[r0:r1], r1 - r0, N, K, None, gsplit) == 0
+                torch.cuda.synchronize(dev)
+                assert torch.equal(f, ex2), (rank, "split", gsplit, M, N, K)
+            dist.barrier()
+        finally:
+            spmm24.set_tuning(group_split=1)
     # the barrier folded into the grouped kernel (spmm24_launch_grouped_gather),
     # on the same flag arrays, eagerly twice and then replayed from a graph
     bar = spmm24.group_barrier(ptrs[-1], rank)
@@ -323,6 +329,7 @@ def _worker_grouped(rank, world, port, shapes):
             assert torch.equal(f, ex), (rank, "fused barrier graph", rep, shapes[i])
         dist.barrier()
     del graph
+    spmm24.reset_tuning()
     for p in opened:
         spmm24.ipc_close(p)
     dist.barrier()
