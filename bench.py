@@ -364,21 +364,40 @@ def run_ours(args, rank, world, local_rank):
     # buffer sets.
     gather_mode = grouped and shard and world > 1 and not (fp8 or bf16) and args.epilogue == "none"
     full_sets, flag_ptrs, imported = [], None, []
+    mc_bases, symm_keep = [None, None], []
     if gather_mode:
         full_elems = sum(c["M_full"] * c["N"] for c in calls)
-        full_sets = [torch.zeros(full_elems, dtype=torch.float16, device=dev) for _ in range(2)]
         flag_buf = torch.zeros(world + 1, dtype=torch.int32, device=dev)  # + the fused barrier's CTA counter
+        bases = [[None] * world for _ in range(3)]
+        if args.gather_mc:
+            # --gather-mc: the full-C sets in symmetric memory, so that rows
+            # whose N is a multiple of 8 are stored once through the NVLink
+            # multicast address (multimem.st, replicated by the switch)
+            import torch.distributed._symmetric_memory as symm_mem
+
+            for k in range(2):
+                t = symm_mem.empty((full_elems,), dtype=torch.float16, device=dev)
+                t.zero_()
+                hd = symm_mem.rendezvous(t, dist.group.WORLD)
+                moff = t.data_ptr() - hd.buffer_ptrs[rank]
+                bases[k] = [hd.buffer_ptrs[r] + moff for r in range(world)]
+                mc_bases[k] = hd.multicast_ptr + moff if hd.multicast_ptr else None
+                full_sets.append(t)
+                symm_keep.append(hd)
+        else:
+            full_sets = [torch.zeros(full_elems, dtype=torch.float16, device=dev) for _ in range(2)]
         torch.cuda.synchronize(dev)
-        mine = [spmm24.ipc_export(t) for t in full_sets] + [spmm24.ipc_export(flag_buf)]
+        ipc_bufs = ([] if args.gather_mc else full_sets) + [flag_buf]
+        mine = [spmm24.ipc_export(t) for t in ipc_bufs]
         handles = [None] * world
         dist.all_gather_object(handles, mine)
-        bases = [[None] * world for _ in range(3)]
+        slots = [2] if args.gather_mc else [0, 1, 2]
         for r in range(world):
-            for i in range(3):
+            for j, i in enumerate(slots):
                 if r == rank:
                     bases[i][r] = (full_sets[i] if i < 2 else flag_buf).data_ptr()
                 else:
-                    bases[i][r] = spmm24.ipc_import(handles[r][i])
+                    bases[i][r] = spmm24.ipc_import(handles[r][j])
                     imported.append(bases[i][r])
         flag_ptrs = bases[2]
         group_bar = spmm24.group_barrier(flag_ptrs, rank)
@@ -388,7 +407,8 @@ def run_ours(args, rank, world, local_rank):
         """Gather descriptors of full-C set k, one per call."""
         out_g, off = [], 0
         for c in calls:
-            out_g.append(spmm24.make_gather([b + 2 * off for b in bases[k]], rows[c["M_full"]][0], c["M_full"]))
+            out_g.append(spmm24.make_gather([b + 2 * off for b in bases[k]], rows[c["M_full"]][0], c["M_full"],
+                                            c_multicast=(mc_bases[k] + 2 * off) if mc_bases[k] else None))
             off += c["M_full"] * c["N"]
         return out_g
 
@@ -758,9 +778,12 @@ def run_ours(args, rank, world, local_rank):
     if gather_mode:
         out["gather"] = {"status": spmm24.device_status(dev.index), "ranks": world,
                          "gathered_bytes_per_step": 2 * sum(c["M_full"] * c["N"] for c in calls),
+                         "multicast": bool(mc_bases[0]),
                          "op": "one spmm24_launch_grouped_gather per step: each rank's output rows stored by the "
-                               "grouped kernel's epilogue into all ranks' full C (CUDA IPC peer pointers, NVLink), "
-                               "the cross-GPU barrier run by the grid's last CTA"}
+                               "grouped kernel's epilogue into all ranks' full C (" +
+                               ("through the NVLink multicast address where N % 8 == 0, else peer stores"
+                                if mc_bases[0] else "CUDA IPC peer pointers, NVLink") +
+                               "), the cross-GPU barrier run by the grid's last CTA"}
         torch.cuda.synchronize(dev)
         dist.barrier()
         for p_ in imported:
@@ -1847,6 +1870,9 @@ def main():
                     help="a step as one spmm24_launch_grouped (N <= 32 workloads without an epilogue or fp8) "
                          "or as one spmm24_launch per SpMM")
     ap.add_argument("--allgather", action="store_true", help="70b workload: also time the NCCL all-gather of C")
+    ap.add_argument("--gather-mc", dest="gather_mc", action="store_true",
+                    help="sharded decode on N > 1 GPUs: store the gathered rows through the full C's NVLink "
+                         "multicast address (symmetric memory) instead of once per peer")
     ap.add_argument("--gather", action="store_true",
                     help="70b workload: time the fused SpMM + NVLink all-gather against SpMM + NCCL all-gather")
     ap.add_argument("--no-static-weights", dest="static_weights", action="store_false",
