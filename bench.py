@@ -15,7 +15,7 @@ bandwidth in MEASURED_PEAKS.json).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                   [--workload decode|prefill|70b|square|pack|packb] [--launch grouped|chain]
-                  [--no-comparators] [--no-secondary]
+                  [--no-comparators] [--no-secondary] [--no-config4] [--no-extras] [--gather-mc]
 
 A step of the decode workload is one spmm24_launch_grouped (one persistent
 kernel for all 12 SpMMs); the same steps as one spmm24_launch per SpMM are
@@ -23,13 +23,18 @@ timed beside it ("chain").  At N=1 the line also carries same-run
 comparators (cuSPARSELt 0.7.1 with algorithm search, dense cuBLAS fp16, the
 reference kernel built for sm_100a; isolated calls, L2 flushed) and a
 secondary block with BASELINE configs 3 (prefill) and 5 (squares up to
-16384^3) against the sparse tensor-core ceiling measured in the same run.
+16384^3) against the sparse tensor-core ceiling measured in the same run,
+the M-sharded LLaMA-70B block (config 4), and an extras block (fp8 decode,
+a fused epilogue, the device packers; each a child run of this script).
 
 --impl reference times the reference path's CPU implementation (the
 oracle's dense GEMM on the pruned A -- the reference has no CPU GEMM of its
 own) on the host cores, on a bounded row sample of the same workload.
-Under torchrun every rank runs its own copy of the workload on its own GPU
-(weak scaling, no collective on the data path); rank 0 prints one JSON line.
+Under torchrun (N > 1) the decode layers are split along M across the ranks
+(strong scaling): each step is one grouped launch per rank whose epilogue
+stores every output row into every rank's full C over NVLink and whose last
+CTA runs the cross-GPU barrier; time is the max over ranks; rank 0 prints
+one JSON line.
 """
 from __future__ import annotations
 
@@ -772,6 +777,9 @@ def run_ours(args, rank, world, local_rank):
 
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(layers, acts, shapes, budget_s=args.cpu_seconds, bf16=bf16, fp8=fp8)
+    if rank == 0 and world == 1 and args.extras and args.workload == "decode" and not (fp8 or bf16) \
+            and args.epilogue == "none":
+        out["extras"] = run_extras(args)
 
     if args.config4 and args.workload == "decode" and not (fp8 or bf16) and args.epilogue == "none":
         out["config4"] = run_config4(torch, dist, spmm24, dev, rank, world, args)
@@ -793,6 +801,45 @@ def run_ours(args, rank, world, local_rank):
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(out), flush=True)
+
+
+def run_extras(args):
+    """The rest of the hot path's measured rows in the default line, each as
+    its own bench.py run (a child process on the same GPU, short steps): the
+    fp8 decode step, the decode step with a fused bias + SiLU epilogue, the
+    device A packer (prune + compress + reorder) and the packed-B producer.
+    Each entry keeps the child's value, unit, roofline fraction and e2e; a
+    child that fails is reported, not fatal."""
+    runs = {
+        "decode_fp8": ["--dtype", "fp8"],
+        "decode_bias_silu": ["--epilogue", "bias_silu"],
+        "pack_a_device": ["--workload", "pack"],
+        "pack_b_device": ["--workload", "packb"],
+    }
+    out = {}
+    env = {k: v for k, v in os.environ.items() if k not in ("RANK", "WORLD_SIZE", "LOCAL_RANK")}
+    for name, extra in runs.items():
+        cmd = [sys.executable, os.path.abspath(__file__), "--steps", "10", "--warmup", "3", "--no-comparators",
+               "--no-secondary", "--no-config4", "--no-cpu-baseline", "--no-extras"] + extra
+        t0 = time.time()
+        try:
+            r = subprocess.run(cmd, capture_output=True, text=True, timeout=300, env=env)
+            line = [x for x in r.stdout.splitlines() if x.startswith("{")]
+            if r.returncode != 0 or not line:
+                out[name] = {"error": f"exit {r.returncode}: {r.stderr.strip()[-200:]}"}
+                continue
+            d = json.loads(line[-1])
+            rf = d.get("roofline") or {}
+            out[name] = {"value": d.get("value"), "unit": d.get("unit"), "dtype": d.get("dtype"),
+                         "roofline_frac": rf.get("frac"), "roofline_peak": rf.get("peak"),
+                         "e2e": (d.get("e2e") or {}).get("value"), "workload": (d.get("config") or {}).get("workload"),
+                         "gpu_launches": d.get("gpu_launches"), "clocks": d.get("clocks"),
+                         "wall_s": round(time.time() - t0, 1)}
+        except Exception as e:  # noqa: BLE001 -- report, keep the main line
+            out[name] = {"error": str(e)[:200]}
+    out["how"] = ("bench.py " + "--steps 10 --warmup 3 --no-comparators --no-secondary --no-config4 "
+                  "--no-cpu-baseline plus: " + "; ".join(f"{k}: {' '.join(v)}" for k, v in runs.items()))
+    return out
 
 
 def run_config4(torch, dist, spmm24, dev, rank, world, args):
@@ -1878,6 +1925,9 @@ def main():
     ap.add_argument("--no-static-weights", dest="static_weights", action="store_false",
                     help="launch without SPMM24_STATIC_WEIGHTS (no kernel in the step writes the weights)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", dest="extras", action="store_false",
+                    help="skip the extras block of the default decode line (fp8 decode, fused epilogue, device "
+                         "packers, each as a child run)")
     ap.add_argument("--dtype", choices=["f16", "bf16", "fp8"], default="f16",
                     help="operand and output type (SPMM24_BF16; fp8: E4M3 operands through spmm24_launch_fp8, fp16 out)")
     ap.add_argument("--epilogue", choices=["none", "bias_silu", "bias_residual", "packed_b"], default="none",
