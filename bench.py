@@ -467,6 +467,10 @@ def run_ours(args, rank, world, local_rank):
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize(dev)
         torch.cuda._sleep(int(2e7))
+        if gather_mode:
+            # one untimed step: its cross-GPU barrier lines the ranks up on the
+            # device, so no rank's interval holds another's late start
+            step_launch(calls, use_group=use_group)
         t0.record(stream)
         for _ in range(args.steps):
             step_launch(calls, use_group=use_group)
@@ -624,6 +628,8 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
+    if gather_mode:
+        e2e_step(-1)  # untimed: its cross-GPU barrier lines the ranks up on the device
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     up.wait_event(e0)
@@ -913,7 +919,9 @@ def run_config4(torch, dist, spmm24, dev, rank, world, args):
 
     steps = max(3, min(args.steps, 10))
 
-    def timed(fn):
+    def timed(fn, sync=False):
+        """sync: fn ends in a cross-GPU barrier; one untimed call after the
+        sleep lines the ranks up on the device before the interval opens."""
         for _ in range(args.warmup):
             fn()
         torch.cuda.synchronize(dev)
@@ -921,6 +929,8 @@ def run_config4(torch, dist, spmm24, dev, rank, world, args):
             dist.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda._sleep(int(2e7))
+        if sync and world > 1:
+            fn()
         e0.record(stream)
         for _ in range(steps):
             fn()
@@ -932,7 +942,7 @@ def run_config4(torch, dist, spmm24, dev, rank, world, args):
         return float(t[0])
 
     us_shards = timed(shards)
-    us_gather = timed(gathered)
+    us_gather = timed(gathered, sync=True)
     status = spmm24.device_status(dev.index)
     if world > 1:
         dist.barrier()
@@ -975,7 +985,7 @@ def run_config4(torch, dist, spmm24, dev, rank, world, args):
                     if spmm24.gather_barrier(h, mflag_ptrs, rank, 0) != 0:
                         raise RuntimeError("spmm24_gather_barrier failed")
 
-                us_mc = timed(gathered_mc)
+                us_mc = timed(gathered_mc, sync=True)
                 status |= spmm24.device_status(dev.index)
             dist.barrier()
         except Exception as e:  # noqa: BLE001 -- report, keep the other numbers
@@ -1061,6 +1071,7 @@ def time_gather(torch, dist, spmm24, calls, stream, dev, rank, world, args, flag
             fn()
         torch.cuda.synchronize(dev)
         dist.barrier()
+        fn()  # untimed: both forms end in a cross-GPU exchange, which lines the ranks up on the device
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for _ in range(args.steps):

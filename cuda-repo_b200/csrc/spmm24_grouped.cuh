@@ -451,23 +451,33 @@ __global__ void __launch_bounds__(kThreads, 1) spmm24_grouped_kernel(const __gri
     ptx::tc_fence_before();
     if (p.bar_n) __threadfence_system();  // this thread's stores (peer rows included) before the CTA's count
     __syncthreads();
-    if (p.bar_n && threadIdx.x == 0) {
-        // the last CTA of the grid to get here runs the cross-GPU barrier
+    if (p.bar_n) {
+        // The last CTA of the grid to get here runs the cross-GPU barrier:
+        // thread 0 finds out and reads the epoch; then thread r publishes it
+        // into rank r's flag array and waits, bounded, for rank r's epoch in
+        // this rank's array -- one thread per rank, so the remote stores and
+        // the waits overlap instead of running one rank after another.
+        __shared__ uint32_t bar_epoch, bar_last;
         uint32_t* own = p.bar_flags[p.bar_rank];
-        const uint32_t done = atomicInc(own + p.bar_n, gridDim.x - 1u);
-        if (done == gridDim.x - 1u) {
-            __threadfence_system();
-            const uint32_t epoch = ptx::ld_acquire_sys(own + p.bar_rank) + 1u;
-            for (int r = 0; r < p.bar_n; ++r) ptx::st_release_sys(p.bar_flags[r] + p.bar_rank, epoch);
+        if (threadIdx.x == 0) {
+            const uint32_t done = atomicInc(own + p.bar_n, gridDim.x - 1u);
+            bar_last = done == gridDim.x - 1u ? 1u : 0u;
+            if (bar_last) {
+                __threadfence_system();
+                bar_epoch = ptx::ld_acquire_sys(own + p.bar_rank) + 1u;
+            }
+        }
+        __syncthreads();
+        if (bar_last && threadIdx.x < p.bar_n) {
+            const int r = threadIdx.x;
+            const uint32_t epoch = bar_epoch;
+            ptx::st_release_sys(p.bar_flags[r] + p.bar_rank, epoch);
             const uint64_t t0 = ptx::globaltimer();
-            for (int r = 0; r < p.bar_n; ++r) {
-                while ((int)(ptx::ld_acquire_sys(own + r) - epoch) < 0) {
-                    ptx::nanosleep_ns(100);
-                    if (ptx::globaltimer() - t0 > p.bar_limit_ns) {
-                        atomicOr(&g_spmm24_status, kStatusBarrierTimeout);
-                        r = p.bar_n;
-                        break;
-                    }
+            while ((int)(ptx::ld_acquire_sys(own + r) - epoch) < 0) {
+                ptx::nanosleep_ns(100);
+                if (ptx::globaltimer() - t0 > p.bar_limit_ns) {
+                    atomicOr(&g_spmm24_status, kStatusBarrierTimeout);
+                    break;
                 }
             }
         }
