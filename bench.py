@@ -1911,6 +1911,45 @@ def run_single(args):
                       "status": spmm24.device_status(0)}))
 
 
+def run_single_group(args):
+    """The decode step's 12 layers with M / DIV rows each (a rank's share of
+    the step split over DIV GPUs) as one grouped launch, `warmup` launches
+    then 3 more, with group_split SPLIT (0: the picker's choice): the case
+    profiler captures of the grouped kernel use (ncu -k regex:spmm24_grouped
+    -s <warmup> -c 1)."""
+    import torch
+
+    import spmm24
+
+    parts = [int(x) for x in args.single_group.split(",")]
+    div = parts[0]
+    split = parts[1] if len(parts) > 1 else 0
+    dev = torch.device("cuda", 0)
+    probs, keep = [], []
+    for i, (M, K) in enumerate(((4096, 4096), (11008, 4096), (4096, 11008))):
+        m = spmm24.shard_rows(M, div, 0, 128)[1]
+        for j, N in enumerate((1, 8, 16, 32)):
+            # every problem its own weights, as in the bench step (no problem finds another's in L2)
+            _, vals, meta = make_layer(torch, spmm24, m, K, 0.02, seed=1 + 4 * i + j)
+            A, E = to_dev(torch, vals, dev), to_dev(torch, meta, dev)
+            _, bp = make_activations(torch, spmm24, K, N, seed=10 * i + j)
+            B = to_dev(torch, bp, dev)
+            C = torch.empty((m, N), dtype=torch.float16, device=dev)
+            probs.append((A, B, E, C, m, N, K))
+            keep += [A, E, B, C]
+    arr = spmm24.problem_array(probs)
+    spmm24.set_tuning(group_split=split)
+    s = torch.cuda.current_stream(dev)
+    for _ in range(args.warmup + 3):
+        rc = spmm24.launch_grouped(s, arr, spmm24.STATIC_WEIGHTS)
+        if rc != 0:
+            raise SystemExit(f"spmm24_launch_grouped failed {rc}: {spmm24._lib.spmm24_last_error().decode()}")
+    torch.cuda.synchronize(dev)
+    spmm24.reset_tuning()
+    print(json.dumps({"single_group": {"rows_divisor": div, "group_split": split, "problems": len(probs)},
+                      "status": spmm24.device_status(0)}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1947,6 +1986,9 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--single", default=None,
                     help="M,N,K[,split]: run one shape (warm-up + 3 launches) for profiler captures")
+    ap.add_argument("--single-group", dest="single_group", default=None,
+                    help="DIV[,SPLIT]: the decode step's layers with M / DIV rows as one grouped launch (warm-up + "
+                         "3 launches, group_split SPLIT) for profiler captures")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -1958,6 +2000,9 @@ def main():
         return
     if args.single:
         run_single(args)
+        return
+    if args.single_group:
+        run_single_group(args)
         return
     if args.workload == "pack":
         run_pack(args, rank, world, local_rank)
