@@ -795,13 +795,70 @@ cudaError_t encode_group_maps(const spmm24_problem& q, bool fp8, GroupParams& gp
     return cudaSuccess;
 }
 
+// One 128-row tile of a grouped launch: its cost (K stages + 1 for the
+// epilogue), problem and row tile.
+struct GroupTile {
+    int cost, prob, m_tile;
+};
+struct GroupSchedule {
+    int split = 1;  // CTAs per tile along K: 1, 2 or 4
+    int units = 0;  // CTAs, or clusters with a split
+    long long makespan = 0;
+    std::vector<std::vector<uint16_t>> lists;  // per unit: (problem << 12) | m_tile
+};
+
+// Three schedules by the longest-processing-time rule: whole tiles on one
+// CTA per SM, or (K split) tiles on clusters of 2 or 4 CTAs with a half or a
+// quarter of the stages each; a split is taken when it shortens the busiest
+// unit's work by more than a tenth against the best schedule with less split
+// (its ring is shallower and each tile pays a partial-sum exchange), or when
+// `forced` (the group_split tuning: 1, 2 or 4) asks for it.  Few tiles of
+// unequal K (a sharded decode step) balance over the SMs only in quarters.
+// Host-only (no CUDA call): spmm24_group_schedule exposes it to tests.
+GroupSchedule schedule_group(const std::vector<GroupTile>& tiles, int sms, int max_clusters4, int forced) {
+    auto lpt = [&](int max_units, int parts) {
+        GroupSchedule sc;
+        sc.split = parts;
+        std::vector<GroupTile> ts = tiles;
+        // cost = stages + 1 (the epilogue); split in `parts`: ceil(stages / parts)
+        // + 1, + 1 more for the four-way exchange
+        for (GroupTile& t : ts)
+            if (parts > 1) t.cost = (t.cost - 1 + parts - 1) / parts + (parts > 2 ? 2 : 1);
+        std::stable_sort(ts.begin(), ts.end(), [](const GroupTile& a, const GroupTile& b) { return a.cost > b.cost; });
+        sc.units = (int)std::min<size_t>((size_t)std::max(1, max_units), ts.size());
+        std::vector<long long> load(sc.units, 0);
+        sc.lists.assign(sc.units, {});
+        for (const GroupTile& t : ts) {
+            int best = 0;  // least loaded unit, lowest index on ties (a linear scan: <= 160 units)
+            for (int c = 1; c < sc.units; ++c)
+                if (load[c] < load[best]) best = c;
+            load[best] += t.cost;
+            sc.lists[best].push_back((uint16_t)((t.prob << 12) | t.m_tile));
+        }
+        for (long long l : load) sc.makespan = std::max(sc.makespan, l);
+        return sc;
+    };
+    const int cap = std::min(sms, kGroupMaxCtas);
+    const int c4 = std::min(cap / 4, max_clusters4);
+    if (forced == 1) return lpt(cap, 1);
+    if (forced == 2) return lpt(cap / 2, 2);
+    if (forced == 4) return lpt(c4, 4);
+    GroupSchedule best = lpt(cap, 1);
+    if (cap >= 2) {
+        GroupSchedule halves = lpt(cap / 2, 2);
+        if (10 * halves.makespan < 9 * best.makespan) best = std::move(halves);
+    }
+    if (c4 >= 1) {
+        GroupSchedule quarters = lpt(c4, 4);
+        if (10 * quarters.makespan < 9 * best.makespan) best = std::move(quarters);
+    }
+    return best;
+}
+
 cudaError_t build_group(const spmm24_problem* probs, int count, unsigned flags, bool fp8, int sms, int max_clusters4,
                         GroupParams& gp, int& n_ctas, bool& any_epi, int& split) {
     std::memset(&gp, 0, sizeof(gp));
-    struct Tile {
-        int cost, prob, m_tile;
-    };
-    std::vector<Tile> tiles;
+    std::vector<GroupTile> tiles;
     any_epi = false;
     for (int i = 0; i < count; ++i) {
         const spmm24_problem& q = probs[i];
@@ -828,57 +885,9 @@ cudaError_t build_group(const spmm24_problem* probs, int count, unsigned flags, 
         for (int m = 0; m < mt; ++m) tiles.push_back({st + 1, i, m});
         if ((e = encode_group_maps(q, fp8, gp, i)) != cudaSuccess) return e;
     }
-    // Three schedules: whole tiles on one CTA per SM, or (K split) tiles on
-    // clusters of 2 or 4 CTAs with a half or a quarter of the stages each; a
-    // split is taken when it shortens the busiest unit's work by more than a
-    // tenth against the best schedule with less split (its ring is shallower
-    // and each tile pays a partial-sum exchange), or when the caller's
-    // tuning asks for it.  Few tiles of unequal K (a sharded decode step)
-    // balance over the SMs only in quarters.
-    struct Sched {
-        int units = 0;
-        long long makespan = 0;
-        std::vector<std::vector<uint16_t>> lists;
-    };
-    auto lpt = [&](int max_units, int parts) {
-        Sched sc;
-        std::vector<Tile> ts = tiles;
-        // cost = stages + 1 (the epilogue); split in `parts`: ceil(stages / parts)
-        // + 1, + 1 more for the four-way exchange
-        for (Tile& t : ts)
-            if (parts > 1) t.cost = (t.cost - 1 + parts - 1) / parts + (parts > 2 ? 2 : 1);
-        std::stable_sort(ts.begin(), ts.end(), [](const Tile& a, const Tile& b) { return a.cost > b.cost; });
-        sc.units = (int)std::min<size_t>((size_t)std::max(1, max_units), ts.size());
-        std::vector<long long> load(sc.units, 0);
-        sc.lists.assign(sc.units, {});
-        for (const Tile& t : ts) {
-            int best = 0;  // least loaded unit, lowest index on ties (a linear scan: <= 160 units)
-            for (int c = 1; c < sc.units; ++c)
-                if (load[c] < load[best]) best = c;
-            load[best] += t.cost;
-            sc.lists[best].push_back((uint16_t)((t.prob << 12) | t.m_tile));
-        }
-        for (long long l : load) sc.makespan = std::max(sc.makespan, l);
-        return sc;
-    };
-    const int cap = std::min(sms, kGroupMaxCtas);
-    Sched whole = lpt(cap, 1), halves = lpt(cap / 2, 2);
-    const int c4 = std::min(cap / 4, max_clusters4);
-    Sched quarters = lpt(c4, 4);
-    const int forced = g_tune.group_split.load(std::memory_order_relaxed);
-    if (forced == 1 || forced == 2 || forced == 4) {
-        split = forced;
-    } else {
-        split = 1;
-        long long best = whole.makespan;
-        if (cap >= 2 && 10 * halves.makespan < 9 * best) {
-            split = 2;
-            best = halves.makespan;
-        }
-        if (c4 >= 1 && 10 * quarters.makespan < 9 * best) split = 4;
-    }
-    Sched& sc = split == 4 ? quarters : split == 2 ? halves : whole;
-    n_ctas = sc.units;  // CTAs, or CTA pairs with the split
+    GroupSchedule sc = schedule_group(tiles, sms, max_clusters4, g_tune.group_split.load(std::memory_order_relaxed));
+    split = sc.split;
+    n_ctas = sc.units;  // CTAs, or clusters with a split
     int off = 0;
     for (int c = 0; c < n_ctas; ++c) {
         gp.sched_off[c] = (uint16_t)off;
@@ -1420,6 +1429,25 @@ int current_sms() {
 void fill_config(const Plan& pl, int stage_k, spmm24_config* out);
 }  // namespace
 }  // namespace spmm24
+
+extern "C" int spmm24_group_schedule(const int* M, const int* K, int count, int fp8, int sms, int max_clusters4,
+                                     int* split, int* units, long long* makespan) {
+    if (!M || !K || count < 1 || count > spmm24::kGroupMaxProblems || sms < 1 || max_clusters4 < 0) return -1;
+    std::vector<spmm24::GroupTile> tiles;
+    for (int i = 0; i < count; ++i) {
+        if (M[i] <= 0 || M[i] % 16 || K[i] <= 0 || (fp8 ? K[i] % 128 : K[i] % 64)) return -1;
+        const int groups = fp8 ? K[i] / 128 : K[i] / 64, st = (groups + 1) / 2;
+        const int mt = (M[i] + spmm24::kTileM - 1) / spmm24::kTileM;
+        if ((long long)tiles.size() + mt > spmm24::kGroupMaxTiles) return -1;
+        for (int m = 0; m < mt; ++m) tiles.push_back({st + 1, i, m});
+    }
+    const spmm24::GroupSchedule sc =
+        spmm24::schedule_group(tiles, sms, max_clusters4, spmm24::g_tune.group_split.load(std::memory_order_relaxed));
+    if (split) *split = sc.split;
+    if (units) *units = sc.units;
+    if (makespan) *makespan = sc.makespan;
+    return 0;
+}
 
 extern "C" cudaError_t spmm24_set_tuning(const spmm24_tuning* t) {
     spmm24::clear_last_error();

@@ -352,6 +352,28 @@ def reset_tuning() -> None:
     _lib.spmm24_set_tuning(None)
 
 
+_IntArr = ctypes.POINTER(ctypes.c_int)
+_lib.spmm24_group_schedule.argtypes = [_IntArr, _IntArr, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                       _IntArr, _IntArr, ctypes.POINTER(ctypes.c_longlong)]
+_lib.spmm24_group_schedule.restype = ctypes.c_int
+
+
+def group_schedule(Ms, Ks, fp8: bool = False, sms: int = 148, max_clusters4: int = 33) -> dict:
+    """spmm24_group_schedule: the K split, unit count and makespan (in
+    stages) a grouped launch of problems with these M and K would use, from
+    the host alone (no GPU)."""
+    n = len(Ms)
+    if len(Ks) != n:
+        raise ValueError("Ms and Ks must have the same length")
+    m = (ctypes.c_int * n)(*Ms)
+    k = (ctypes.c_int * n)(*Ks)
+    split, units, mk = ctypes.c_int(), ctypes.c_int(), ctypes.c_longlong()
+    if _lib.spmm24_group_schedule(m, k, n, int(fp8), sms, max_clusters4, ctypes.byref(split), ctypes.byref(units),
+                                  ctypes.byref(mk)) != 0:
+        raise ValueError("bad grouped problems")
+    return {"split": split.value, "units": units.value, "makespan": mk.value}
+
+
 def select_config_fp8(M: int, N: int, K: int, split_k: int = 0) -> dict:
     """spmm24_select_config_fp8: the configuration spmm24_launch_fp8 uses."""
     cfg = SpmmConfig()

@@ -436,6 +436,17 @@ typedef struct spmm24_tuning {
     int group_split; /* grouped launches: 0 auto; 1 whole K per tile; 2 or 4: each tile's K split over a cluster of 2 or 4 CTAs */
 } spmm24_tuning;
 cudaError_t spmm24_set_tuning(const spmm24_tuning* t);
+/* The schedule spmm24_launch_grouped would build for `count` problems of
+ * M[i] rows and K[i] (fp8: K % 128 == 0, else K % 64 == 0) on a device of
+ * `sms` SMs where `max_clusters4` clusters of four CTAs fit at once,
+ * computed on the host without a GPU (N does not enter it): *split = CTAs
+ * per 128-row tile along K (1, 2 or 4), *units = CTAs (or clusters) the
+ * launch would use, *makespan = the busiest unit's cost in stages (a tile
+ * costs its stages + 1; split: its share + 1, + 1 more for four).  Follows
+ * spmm24_set_tuning's group_split.  For tests and tuning; any output may
+ * be NULL.  Returns 0, or -1 for bad arguments. */
+int spmm24_group_schedule(const int* M, const int* K, int count, int fp8, int sms, int max_clusters4, int* split,
+                          int* units, long long* makespan);
 
 /* The same for spmm24_launch_fp8 (stage_k 256: a stage carries 256 logical
  * K of fp8 operands; K % 128 == 0), for an epilogue without a residual or a
