@@ -162,6 +162,10 @@ using CV256 = ClusterVariant<256, 2>;
 // Pair tiles: 256 x 256 with a 4-stage ring (one CTA per SM).
 constexpr int kPairStages = 4;
 using PairC = PairCfg<kPairStages>;
+// Narrow pair tiles: 256 x 128 with a 6-stage ring of 34 KB stages, for
+// shapes with less than half a wave of 256 x 256 tiles (fp16 / bf16 only).
+constexpr int kPairNarrowStages = 6;
+using PairNC = PairCfg<kPairNarrowStages, false, 64>;
 // Two M halves per pair (512 x 240 tiles, 3-stage ring of 66 KB stages).
 constexpr int kPair2Stages = 3;
 using Pair2C = Pair2Cfg<kPair2Stages>;
@@ -178,6 +182,7 @@ using CV32s = ClusterVariant<32, 3>;
 struct Plan {
     Path path;
     bool pair2;        // pair path with two M halves per pair (512 x 240 tiles)
+    bool narrow;       // pair path with 256 x 128 tiles
     bool shallow;      // 4-stage ring, two CTAs per SM (narrow N only)
     int tile_n;
     int stages;
@@ -234,7 +239,7 @@ void maybe_pair2(Plan& p, int M, int N, int sms, int tile_n, int stages, int sme
 // automatic K split.  pair2_ok: the two-M-half pair kernel may be chosen
 // (no residual).
 Plan make_plan(int M, int N, int K, int split_k, int sms, bool allow_pair = true, int max_split = kMaxSplit,
-               bool pair2_ok = true) {
+               bool pair2_ok = true, bool narrow_ok = true) {
     Plan p{};
     int tn = N <= 16 ? 16 : N <= 32 ? 32 : N <= 64 ? 64 : 128;
     const int forced = g_tune.tile_n.load(std::memory_order_relaxed);  // override (16/32/64/128/256)
@@ -278,6 +283,27 @@ Plan make_plan(int M, int N, int K, int split_k, int sms, bool allow_pair = true
         if (p.stages_total < 2) ps = 1;
         p.split = ps;
         p.grid = 2 * ps * (int)ptiles;
+        // Less than half a wave of 256 x 256 tiles and no K split (N > 256;
+        // narrower N takes the cluster tiles below): 256 x 128 tiles on
+        // twice as many pairs, when they still fit in one wave.  Measured
+        // back to back: 4096 x 512 x 4096 17.35 -> 16.74 us, 2048 x 512 x
+        // 2048 10.81 -> 9.98, 1024^3 7.81 -> 7.03 (isolated with L2 flushed:
+        // equal or faster).  Tuning: tile_n 128 forces it, 256 keeps the wide
+        // tile, a forced pair2 takes precedence.
+        const bool pair2_forced = g_tune.pair2.load(std::memory_order_relaxed) == 1;
+        if (narrow_ok && ps == 1 && forced != 256 && !pair2_forced &&
+            (forced == 128 || (N > 256 && 2 * ptiles <= sms / 2))) {
+            const long long ntiles = (long long)p.m_tiles * ((N + 127) / 128);
+            if (forced == 128 || 2 * ntiles <= sms) {
+                p.narrow = true;
+                p.tile_n = PairNC::TILE_N;
+                p.stages = kPairNarrowStages;
+                p.smem = PairNC::SMEM_ALLOC;
+                p.n_tiles = (N + p.tile_n - 1) / p.tile_n;
+                p.grid = 2 * p.m_tiles * p.n_tiles;
+                return p;
+            }
+        }
         // One pair tile across N (N <= 256) and pairs for less than three
         // quarters of the SMs: 128-wide cluster tiles with a K split fill more
         // of the GPU.  Measured (chains of one shape): 1024 x 256 x 8192
@@ -457,8 +483,20 @@ cudaError_t launch_pair2(const Plan& pl, cudaStream_t stream, int dev, bool pdl,
                          pdl, ta, tb, te, kp, kPairThreads);
 }
 
+cudaError_t launch_pair_narrow(const Plan& pl, cudaStream_t stream, int dev, bool pdl, const CUtensorMap& ta,
+                               const CUtensorMap& tb, const CUtensorMap& te, const PairParams& kp) {
+    const bool general = !epilogue_plain_fp16(kp.epi);
+    auto kern = general ? spmm24_pair_kernel<kPairNarrowStages, true, false, false, 64>
+                        : spmm24_pair_kernel<kPairNarrowStages, false, false, false, 64>;
+    cudaError_t e = prepare(kern, PairNC::SMEM_ALLOC, dev, 15 + (general ? kEpiSlot : 0));
+    if (e != cudaSuccess) return e;
+    return launch_kernel(kern, dim3(2u, (unsigned)pl.n_tiles, (unsigned)pl.m_tiles), PairNC::SMEM_ALLOC, stream, 2u,
+                         pdl, ta, tb, te, kp, kPairThreads);
+}
+
 cudaError_t launch_pair(const Plan& pl, cudaStream_t stream, int dev, bool pdl, const CUtensorMap& ta,
                         const CUtensorMap& tb, const CUtensorMap& te, const PairParams& kp) {
+    if (pl.narrow) return launch_pair_narrow(pl, stream, dev, pdl, ta, tb, te, kp);
     return pl.split == 2 ? launch_pair_v<true>(pl, stream, dev, pdl, ta, tb, te, kp, 12)
                          : launch_pair_v<false>(pl, stream, dev, pdl, ta, tb, te, kp, 11);
 }
@@ -546,7 +584,10 @@ cudaError_t launch_impl(cudaStream_t stream, const void* A, const void* B, const
     {
         cuuint64_t dims[4] = {128, (cuuint64_t)(K / 64), 4, (cuuint64_t)((N + 7) / 8)};
         cuuint64_t str[3] = {1024, 256, (cuuint64_t)16 * K};
-        const int cta_n = pl.path != Path::kPair ? pl.tile_n : pl.pair2 ? Pair2C::HALF_N : PairC::HALF_N;  // columns one CTA loads
+        const int cta_n = pl.path != Path::kPair ? pl.tile_n
+                          : pl.pair2             ? Pair2C::HALF_N
+                          : pl.narrow            ? PairNC::HALF_N
+                                                 : PairC::HALF_N;  // columns one CTA loads
         cuuint32_t box[4] = {128, 2, 4, (cuuint32_t)(cta_n / 8)};
         if (!encode(&tb, 4, B, dims, str, box)) return invalid("TMA descriptor for B could not be encoded");
     }
@@ -621,7 +662,7 @@ int fp8_smem() {
 
 Plan plan_fp8(int M, int N, int K, int split_k, int sms, bool pair2_ok) {
     const int Kh = K / 2;
-    Plan pl = make_plan(M, N, Kh, split_k, sms, Kh % 128 == 0, 5, false);
+    Plan pl = make_plan(M, N, Kh, split_k, sms, Kh % 128 == 0, 5, false, false);
     if (pl.path == Path::kPair) {
         pl.smem = PairC8::SMEM_ALLOC;
         if (pl.split == 1 && split_k <= 1 && pair2_ok)

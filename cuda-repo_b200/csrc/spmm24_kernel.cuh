@@ -395,17 +395,21 @@ spmm24_cluster_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_cons
 }
 
 // -------------------------------------------------------------------------
-// A CTA pair computes a 256 x 256 tile; each CTA holds 128 rows of A and 128
-// columns of B.  With a K split, a cluster of two pairs computes the tile:
+// A CTA pair computes a 256 x 256 tile (256 x 128 with HALF_N = 64); each
+// CTA holds 128 rows of A and HALF_N columns of B.  With a K split, a
+// cluster of two pairs computes the tile:
 // pair 1 sends its fp32 partial accumulator to pair 0 through distributed
 // shared memory, and pair 0 adds it before the epilogue.
 // FP8: a stage covers 256 logical K of fp8 operands in the same A and B bytes
 // (B: two 128-byte-swizzled halves of HALF_N rows x 128 K) and two 128-K
 // metadata groups.
-template <int STAGES, bool FP8 = false>
+// HALF_N_: 128 (256 x 256 tiles), or 64 (256 x 128 tiles, for shapes with
+// less than half a wave of the wide ones).
+template <int STAGES, bool FP8 = false, int HALF_N_ = 128>
 struct PairCfg {
+    static_assert(HALF_N_ == 64 || HALF_N_ == 128, "pair tiles are 256 or 128 columns wide");
     static constexpr bool kFp8 = FP8;
-    static constexpr int HALF_N = 128;                   // columns of B / C per CTA
+    static constexpr int HALF_N = HALF_N_;               // columns of B / C per CTA
     static constexpr int TILE_N = 2 * HALF_N;            // columns per pair
     static constexpr int TILE_M = 2 * kTileM;            // rows per pair
     static constexpr int A_BYTES = 8 * 8 * 256;          // this CTA's 128 rows x 128 logical K
@@ -479,12 +483,12 @@ __host__ __device__ constexpr uint32_t pair_idesc_fp8() {
 // cluster of two pairs, each taking half of the 128-K stages (p.split == 2;
 // not with a residual, whose staging the partner partial would overlap).
 // FP8: fp8 operand formats and kind::f8f6f4 MMAs (always with EPI).
-template <int STAGES, bool EPI, bool KSPLIT, bool FP8 = false>
+template <int STAGES, bool EPI, bool KSPLIT, bool FP8 = false, int HALF_N = 128>
 __global__ void __launch_bounds__(kPairThreads, 1)
 spmm24_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmE, const PairParams p) {
     static_assert(EPI || !FP8, "the fp8 kernel always runs the general epilogue");
-    using C_ = PairCfg<STAGES, FP8>;
+    using C_ = PairCfg<STAGES, FP8, HALF_N>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + C_::BAR_OFFSET);  // used in the leader only

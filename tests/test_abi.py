@@ -164,9 +164,15 @@ def test_select_config_picks_tiles_and_splits():
     c = spmm24.select_config(4096, 128, 4096)
     assert c["tile_n"] == 128 and c["stages"] == 4 and c["cta_pair"] == 0
     # wide N with K % 128 == 0: 256 x 256 tiles on CTA pairs
-    c = spmm24.select_config(4096, 512, 4096)
+    c = spmm24.select_config(2048, 2048, 2048)
     assert c["cta_pair"] == 1 and c["tile_m"] == 256 and c["tile_n"] == 256 and c["split_k"] == 1
-    assert c["grid_ctas"] == 64
+    assert c["grid_ctas"] == 128
+    # less than half a wave of those (32 tiles) and no K split: 256 x 128 tiles
+    c = spmm24.select_config(4096, 512, 4096)
+    assert c["cta_pair"] == 1 and c["tile_m"] == 256 and c["tile_n"] == 128 and c["split_k"] == 1
+    assert c["grid_ctas"] == 128 and c["stages"] == 6
+    assert spmm24.select_config(4096, 1024, 4096)["tile_n"] == 256  # 64 narrow tiles would not fit one wave
+    assert spmm24.select_config(4096, 256, 4096)["cta_pair"] == 0  # N <= 256: split-K cluster tiles
     # 32 pair tiles (0.4 waves) and 86 stages: two pairs per tile, each with half of K
     c = spmm24.select_config(4096, 512, 11008)
     assert c["cta_pair"] == 1 and c["split_k"] == 2 and c["grid_ctas"] == 128

@@ -1,7 +1,7 @@
 """The fused all-gather's store path on one GPU: spmm24_launch_gather with a
 single rank writes the shard's rows into its own full C at the row offset,
-through every kernel's gather epilogue (cluster split-K, 256 x 256 pair,
-512 x 240 pair, ragged N with element stores), equal bit for bit to the plain
+through every kernel's gather epilogue (cluster split-K, 256 x 256 and
+256 x 128 pair, 512 x 240 pair, ragged N with element stores), equal bit for bit to the plain
 launch with the same kernel; rows outside the shard stay untouched.  The
 same for the grouped kernel's gather (spmm24_launch_grouped_gather, with
 its fused barrier of one rank).  The cross-GPU forms run in
@@ -21,7 +21,8 @@ def _dev(torch, arr, dev):
 @pytest.mark.parametrize("shape,tune", [
     ((1024, 16, 1024), {}),                      # cluster kernel, split-K
     ((512, 40, 512), {}),                        # mid N, ragged N (element stores)
-    ((1024, 512, 1024), dict(pair=1, pair2=0)),  # 256 x 256 pair kernel
+    ((1024, 512, 1024), dict(pair=1, pair2=0, tile_n=256)),  # 256 x 256 pair kernel
+    ((1024, 384, 1024), dict(pair=1, tile_n=128)),  # 256 x 128 pair kernel
     ((1024, 480, 512), dict(pair2=1)),           # 512 x 240 pair kernel
     ((592, 500, 384), dict(pair2=1)),            # ragged M and N on the 512 x 240 tile
 ], ids=lambda v: "x".join(map(str, v)) if isinstance(v, tuple) else str(v))

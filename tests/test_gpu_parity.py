@@ -180,12 +180,65 @@ def test_cta_pair_kernel(cuda_device, tuning, shape, split):
     memory."""
     import spmm24
 
-    tuning(pair=1, pair2=0, pair_split=split)  # pair=1: also the few-tile shapes the picker gives to split-K clusters
+    # pair=1: also the few-tile shapes the picker gives to split-K clusters;
+    # tile_n=256: also the sub-wave shapes it gives to 256 x 128 pair tiles
+    tuning(pair=1, pair2=0, pair_split=split, tile_n=256)
     M, N, K = shape
     cfg = spmm24.select_config(M, N, K)
     assert cfg["cta_pair"] == 1 and cfg["tile_n"] == 256 and cfg["split_k"] == (split if K >= 256 else 1)
     p = make_problem(M, N, K, seed=3 * M + N)
     check(p, 0, cuda_device)
+
+
+@pytest.mark.parametrize("shape", [
+    (256, 128, 128),     # one pair, one stage
+    (512, 384, 512),
+    (272, 200, 384),     # ragged M (one band past a pair tile) and ragged N
+    (768, 1000, 256),    # N not a multiple of 8: scalar stores
+    (1024, 512, 4096),   # the sub-wave case the picker gives this tile
+    (768, 520, 3200),    # odd stage count, ragged N
+])
+def test_cta_pair_narrow_tiles(cuda_device, tuning, shape):
+    """The pair kernel with 256 x 128 tiles (64 columns of B per CTA, a
+    6-stage ring)."""
+    import spmm24
+
+    tuning(pair=1, tile_n=128)
+    M, N, K = shape
+    cfg = spmm24.select_config(M, N, K)
+    assert cfg["cta_pair"] == 1 and cfg["tile_m"] == 256 and cfg["tile_n"] == 128 and cfg["stages"] == 6
+    check(make_problem(M, N, K, seed=7 * M + N), 0, cuda_device)
+
+
+def test_cta_pair_narrow_epilogues(cuda_device, tuning):
+    """The 256 x 128 pair tile through the general epilogue: bias + SiLU,
+    a residual, bf16 and a packed-B output, each bit for bit the wide pair
+    tile's result (the same MMAs in the same K order, the same epilogue)."""
+    import torch
+
+    import spmm24
+
+    dev = cuda_device
+    M, N, K = 512, 384, 1024
+    p = make_problem(M, N, K, seed=77, a_scale=0.05, b_dist="normal")
+    A = torch.from_numpy(p.vals.view(np.int16)).to(dev)
+    E = torch.from_numpy(p.meta.view(np.int16)).to(dev)
+    B = torch.from_numpy(p.b_packed.view(np.int16)).to(dev)
+    bias = (torch.randn(M, device=dev) * 0.1).half()
+    res = torch.randn(M, N, device=dev).half()
+    cases = [dict(bias=bias, activation=spmm24.ACT_SILU), dict(residual=res, alpha=0.5),
+             dict(out_layout=spmm24.OUT_PACKED_B, bias=bias)]
+    for kw in cases:
+        outs = []
+        for tn in (128, 256):
+            tuning(pair=1, pair2=0, tile_n=tn)
+            C = torch.full((M * N,), -1, dtype=torch.int16, device=dev)
+            assert spmm24.launch_fused(None, A, B, E, C, M, N, K, 1, 0, **kw) == 0, \
+                spmm24._lib.spmm24_last_error().decode()
+            torch.cuda.synchronize(dev)
+            outs.append(C)
+        assert torch.equal(outs[0], outs[1]), kw
+    assert spmm24.device_status(0) == 0
 
 
 @pytest.mark.parametrize("shape", [
