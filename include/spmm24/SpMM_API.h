@@ -409,7 +409,7 @@ size_t spmm24_workspace_bytes(int M, int N, int K, int split_k);
  * Replaces the compile-time N switch of src/SpMM_API.cu:128-154 and
  * N2M4TilingConfig (src/TileConfig.h:60-94).  Returns 0 or -1. */
 typedef struct spmm24_config {
-    int tile_m;      /* rows per tile (128; 256 for a CTA pair) */
+    int tile_m;      /* rows per tile (128; 256 or 512 for a CTA pair) */
     int tile_n;      /* columns per tile */
     int stage_k;     /* logical K per pipeline stage (128) */
     int stages;      /* pipeline depth */
@@ -417,7 +417,7 @@ typedef struct spmm24_config {
     int grid_ctas;   /* CTAs launched */
     int smem_bytes;  /* dynamic shared memory per CTA */
     int stream_k;    /* always 0: spmm24_launch never picks the stream-K kernel (spmm24_launch_noalloc's) */
-    int cta_pair;    /* 1: 256 x 256 tiles on CTA pairs (cta_group::2 MMAs) */
+    int cta_pair;    /* 1: CTA-pair tiles (cta_group::2 MMAs): 256 x 256, 256 x 128 or 512 x 240 */
 } spmm24_config;
 int spmm24_select_config(int M, int N, int K, int split_k, spmm24_config* out);
 /* Process-wide override of the kernel picker (no counterpart in the
