@@ -431,7 +431,8 @@ typedef struct spmm24_tuning {
     int pair;       /* -1 auto; 0 never use the CTA-pair kernels; 1 whenever legal (K % 128 == 0, split_k <= 1) */
     int pair2;      /* -1 auto; 0 never use the two-M-half pair kernel; 1 whenever the pair path allows it */
     int pair_split; /* 0 auto; 1 or 2 K halves per pair tile */
-    int tile_n;     /* 0 auto; 16, 32, 64, 128 or 256: the cluster kernel's tile width */
+    int tile_n;     /* 0 auto; 16, 32, 64, 128 or 256: the cluster kernel's tile width; on the pair
+                       path 128 forces 256 x 128 tiles and 256 the 256 x 256 ones */
     int deep_ring;  /* 0 auto (a shallow ring, two CTAs per SM, for tile_n <= 32); 1 the deepest ring */
     int group_split; /* grouped launches: 0 auto; 1 whole K per tile; 2 or 4: each tile's K split over a cluster of 2 or 4 CTAs */
 } spmm24_tuning;
