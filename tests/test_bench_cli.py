@@ -63,3 +63,14 @@ def test_reference_arm_decode_uses_only_the_oracle():
     ours = bench.workload_config(argparse.Namespace(workload="decode", dtype="f16"), 1)
     assert d["config"] == ours
     assert d["cpu_baseline"]["kind"] == "port" and d["e2e"]["value"] == d["value"]
+
+
+def test_help_lists_the_default_line_switches():
+    """The switches that shape the default line and the profiler cases are
+    accepted (argument parsing only; the GPU arms run on the GPU box)."""
+    out = subprocess.run([sys.executable, os.path.join(REPO, "bench.py"), "--help"], capture_output=True, text=True,
+                         timeout=120, cwd=REPO)
+    assert out.returncode == 0, out.stderr[-2000:]
+    for flag in ("--no-comparators", "--no-secondary", "--no-config4", "--no-extras", "--gather-mc", "--single",
+                 "--single-group", "--workload", "--dtype", "--epilogue", "--impl"):
+        assert flag in out.stdout, flag
